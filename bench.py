@@ -1,0 +1,390 @@
+#!/usr/bin/env python3
+"""Benchmark of the BFP8 GEMV / lm_head decode hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload stack|gemv|lm_bf16|lm_bfp8]
+
+Default workload (the BASELINE metric's configuration): the full per-token
+linear stack of Qwen3.5-0.8B at batch 1 -- 150 BFP8 GEMVs, 504,791,040 bytes
+of weights, each GEMV on its own fp32 N(0,1) activation re-quantized inside
+the kernel -- as ONE grouped kernel launch per token.  A step is one token.
+Weights are random N(0, 0.02), packed on the device, and the timed steps
+rotate through enough byte-identical copies (> 4 GB) that no step finds its
+weights in the 126 MB L2.
+
+One JSON line on rank 0.  `value` is algorithmic GB/s of the stack
+(weights + fp32 activations in + fp32 outputs out, summed over ranks) with
+everything resident in HBM; `e2e` is the same metric with every token's
+activations copied in from pinned host memory and its outputs copied back
+inside the timed region.  With --gpus N under torchrun every rank runs its
+own token stream on its own GPU (independent decode replicas, weak scaling,
+no collective on the data path).
+
+--impl reference times the reference's own C bfp8_gemv (compiled from its
+source for this host, scalar float path since the host has no NEON) on the
+same workload with every host thread, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "qwen35-ax7020-edge-llm_b200")
+for _p in (REPO, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "BFP8 GEMV HBM GB/s (% of B200 peak); 0.8B-shape linear-stack ms/token, batch 1"
+L2_DEFEAT_BYTES = 4.3e9
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=["stack", "gemv", "lm_bf16", "lm_bfp8"], default="stack")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample", action="store_true", help=argparse.SUPPRESS)
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def committed_traffic(kernel_key):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
+    summary (profiles/traffic.json), or None."""
+    try:
+        with open(os.path.join(REPO, "profiles", "traffic.json")) as f:
+            t = json.load(f)
+        return t.get(kernel_key)
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------------ workloads
+def stack_shapes(workload):
+    from qwen_b200 import model
+
+    if workload == "stack":
+        return model.qwen35_08b_stack(), "qwen35-0.8b linear stack (150 BFP8 GEMVs), batch 1"
+    if workload == "gemv":
+        return [model.Linear("mlp.up_proj", 3584, 1024)], "single BFP8 GEMV 3584x1024, batch 1"
+    raise ValueError(workload)
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples of one GPU during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.path = tempfile.mktemp(suffix=".csv")
+        self.proc = None
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(gpu_id), "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def gpu_identifier(torch, dev):
+    try:
+        return "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        return dev.index or 0
+
+
+def timed(torch, fn, steps, warmup, barrier):
+    """Run warmup untimed steps, then time exactly `steps` steps with CUDA
+    events on the current stream, barrier + synchronize on both sides."""
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(steps):
+        fn(warmup + i)
+    e.record()
+    torch.cuda.synchronize()
+    barrier()
+    return s.elapsed_time(e) / 1e3
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    from qwen_b200 import model, ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    hbm_peak, peak_kind = peaks()
+    line = {"metric": METRIC, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int16xint8->fp32",
+            "data": "synthetic: weights N(0,0.02) packed BFP8 on device (seeded), activations N(0,1)"}
+
+    if args.workload in ("stack", "gemv"):
+        shapes, desc = stack_shapes(args.workload)
+        nb = model.stack_bytes(shapes)
+        wbytes = nb["weights"]
+        copies = max(2, math.ceil(L2_DEFEAT_BYTES / wbytes))
+        ds = model.DeviceStack(shapes, copies=copies, device=dev, seed=1234 + rank)
+        plans = [ops.LinearStack(ds.views(c)) for c in range(copies)]
+        launches_per_step = 1
+
+        def step(i):
+            plans[i % copies].run()
+
+        # ------------------------------------------------ device-resident timing
+        clk = ClockSampler(gpu_identifier(torch, dev))
+        secs = timed(torch, step, args.steps, args.warmup, barrier)
+        clocks = clk.stop()
+        t = torch.tensor([secs], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        secs = float(t.item())
+        per_step = secs / args.steps
+        value = world * nb["total"] / per_step / 1e9
+        kernel_gbs = nb["total"] / per_step / 1e9
+
+        # ------------------------------------------------ end to end, host buffers
+        hx = torch.empty(ds.x_flat.numel(), dtype=torch.float32, pin_memory=True)
+        hx.copy_(ds.x_flat.cpu())
+        hy = torch.empty(ds.y_flat.numel(), dtype=torch.float32, pin_memory=True)
+
+        def e2e_step(i):
+            ds.x_flat.copy_(hx, non_blocking=True)
+            plans[i % copies].run()
+            hy.copy_(ds.y_flat, non_blocking=True)
+
+        esecs = timed(torch, e2e_step, args.steps, args.warmup, barrier)
+        te = torch.tensor([esecs], device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        esecs = float(te.item())
+        e2e = {"value": round(world * nb["total"] / (esecs / args.steps) / 1e9, 2), "unit": "GB/s",
+               "ms_per_step": round(esecs / args.steps * 1e3, 4),
+               "h2d_bytes_per_step": hx.numel() * 4, "d2h_bytes_per_step": hy.numel() * 4}
+
+        line.update({
+            "value": round(value, 2), "ms_per_step": round(per_step * 1e3, 4),
+            "config": {"workload": desc, "gemvs_per_step": len(shapes), "weight_bytes": wbytes,
+                       "algorithmic_bytes_per_step": nb["total"], "macs_per_step": nb["macs"],
+                       "l2": f"rotates {copies} weight copies ({copies * wbytes / 1e9:.2f} GB) > 126 MB L2",
+                       "launch": "one grouped persistent kernel per step", "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 2), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(kernel_gbs / hbm_peak, 4), "peak_kind": peak_kind,
+                         "traffic": committed_traffic(args.workload),
+                         "kernel": "gemv_exact_kernel (grouped)"},
+            "e2e": e2e,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+        })
+        for p in plans:
+            p.close()
+    else:
+        line.update(run_lm_head(args, torch, ops, dev, barrier, world, hbm_peak, peak_kind))
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.workload)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_lm_head(args, torch, ops, dev, barrier, world, hbm_peak, peak_kind):
+    """Secondary lines: the 65536 x 1024 lm_head (bf16 table or BFP8 matrix)
+    fused with argmax and top-40."""
+    V, H, k = 65536, 1024, 40
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    w = torch.randn((V, H), generator=g, device=dev) * 0.02
+    if args.workload == "lm_bf16":
+        tab = w.to(torch.bfloat16).view(torch.int16)
+        per = V * H * 2
+        copies = max(2, math.ceil(L2_DEFEAT_BYTES / per))
+        tabs = [tab] + [tab.clone() for _ in range(copies - 1)]
+        h = torch.randn(H, generator=g, device=dev)
+
+        def step(i):
+            ops.lm_head_bf16(h, tabs[i % copies], k)
+        desc = "bf16 lm_head 65536x1024 + argmax + top-40"
+    else:
+        mant, exps = ops.pack_bfp8(w)
+        per = V * H + V * H // 64
+        copies = max(2, math.ceil(L2_DEFEAT_BYTES / per))
+        mats = [(mant, exps)] + [(mant.clone(), exps.clone()) for _ in range(copies - 1)]
+        h = torch.randn(H, generator=g, device=dev)
+
+        def step(i):
+            m, e = mats[i % copies]
+            ops.lm_head_bfp8(h, m, e, k)
+        desc = "BFP8 lm_head 65536x1024 + argmax + top-40"
+    del w
+    secs = timed(torch, step, args.steps, args.warmup, barrier)
+    per_step = secs / args.steps
+    nbytes = per + 4 * H
+    gbs = nbytes / per_step / 1e9
+    return {"value": round(world * gbs, 2), "ms_per_step": round(per_step * 1e3, 4),
+            "config": {"workload": desc, "algorithmic_bytes_per_step": nbytes,
+                       "l2": f"rotates {copies} copies"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind,
+                         "traffic": committed_traffic(args.workload)},
+            "gpu_launches": args.steps}
+
+
+# ------------------------------------------------------------------ reference arm
+def reference_stack_runner(workload, seed=7):
+    """The reference's own bfp8_gemv (oracle/_ref/libref_kernels.so, built
+    from 04-板载脚本与工具/qwen_kernels_opt.c) over the workload's GEMVs."""
+    import ctypes
+
+    import numpy as np
+
+    lib = ctypes.CDLL(os.path.join(REPO, "oracle", "_ref", "libref_kernels.so"))
+    P, I = ctypes.c_void_p, ctypes.c_int
+    lib.bfp8_gemv.argtypes = [P, P, P, P, I, I]
+    lib.bfp8_gemv.restype = None
+    lib.init_kernels()
+    shapes, desc = stack_shapes(workload)
+    rng = np.random.default_rng(seed)
+    ents = []
+    for t in shapes:
+        mant = rng.integers(-128, 128, (t.M, t.K), dtype=np.int8)
+        exps = rng.integers(118, 131, (t.M, t.K // 64), dtype=np.uint8)
+        x = rng.standard_normal(t.K, dtype=np.float32)
+        y = np.empty(t.M, np.float32)
+        ents.append((y, x, mant, exps, t.M, t.K))
+
+    def token():
+        for y, x, m, e, M, K in ents:
+            lib.bfp8_gemv(y.ctypes.data, x.ctypes.data, m.ctypes.data, e.ctypes.data, M, K)
+    return token, shapes, desc
+
+
+def cpu_baseline(workload):
+    """Bounded sample of the reference C on this host's cores, in a child
+    process so OpenMP starts with every host thread."""
+    if workload not in ("stack", "gemv"):
+        return None
+    env = dict(os.environ, OMP_NUM_THREADS=str(os.cpu_count()))
+    try:
+        out = subprocess.run([sys.executable, os.path.abspath(__file__), "--impl", "reference", "--cpu-sample",
+                              "--workload", workload], env=env, capture_output=True, text=True, timeout=300)
+        return json.loads(out.stdout.strip().splitlines()[-1])
+    except Exception as e:  # a baseline failure must not hide the GPU number
+        return {"error": str(e)[:200]}
+
+
+def run_reference(args):
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    from qwen_b200 import model
+
+    token, shapes, desc = reference_stack_runner(args.workload)
+    nb = model.stack_bytes(shapes)
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count()))
+    if args.cpu_sample:
+        # bounded sample: whole tokens for ~10 s (at least 2)
+        token()
+        n, t0 = 0, time.perf_counter()
+        while n < 2 or (time.perf_counter() - t0 < 10.0 and n < 1000):
+            token()
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        print(json.dumps({"value": round(nb["total"] / dt / 1e9, 4), "unit": "GB/s", "ms_per_step": round(dt * 1e3, 3),
+                          "cores": cores, "kind": "reference",
+                          "sample": f"{n} whole tokens of the workload ({desc}) after 1 warm-up token; "
+                                    "reference C bfp8_gemv scalar build, OpenMP"}))
+        return
+    for _ in range(args.warmup):
+        token()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        token()
+    dt = (time.perf_counter() - t0) / args.steps
+    v = nb["total"] / dt / 1e9
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (reference scalar path)",
+        "data": "synthetic: random int8 mantissas, exponents 118..130, activations N(0,1)",
+        "config": {"workload": desc, "algorithmic_bytes_per_step": nb["total"]},
+        "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "reference",
+                         "sample": f"{args.steps} whole tokens after {args.warmup} warm-up tokens"},
+        "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count()))
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

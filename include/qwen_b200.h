@@ -1,0 +1,169 @@
+/*
+ * qwen_b200.h -- C ABI of libqwen_kernels_b200.so, the B200 (sm_100a)
+ * implementation of the BFP8 GEMV / lm_head decode hot path of
+ * ideal1128/qwen35-ax7020-edge-llm.
+ *
+ * Two groups of entry points:
+ *
+ *  1. Drop-in replacements of the reference C kernels.  Same names, argument
+ *     meaning and return conventions as the reference libraries the Python
+ *     engine binds through ctypes; every pointer is a HOST pointer.  Weight
+ *     and embedding pointers are translated to device copies: ranges
+ *     registered with qwen_b200_register_weights() map by offset, any other
+ *     pointer is uploaded on first use and cached by (address, size) -- a
+ *     caller that rewrites a weight buffer in place must call
+ *     qwen_b200_forget_weights() first.  Activations and outputs are copied
+ *     in and out on every call, and the call returns after the result is on
+ *     the host.
+ *
+ *  2. Device entry points (suffix _dev).  Every pointer is a device pointer
+ *     on the current device, `stream` is a cudaStream_t (NULL = legacy
+ *     default stream), nothing is synchronised.  They return 0 on success or
+ *     a negative QB_E* code; qwen_b200_last_error() describes the last
+ *     failure of the calling thread.
+ *
+ * Weight layout (both groups): block-64 BFP8 SoA as written by the reference
+ * packer (05-主机侧源码/bfp8_packer.py:53-86): mantissas int8 [M][K]
+ * row-major, then exponents uint8 [M][K/64]; a weight's value is
+ * m * 2^(e-134).  K must be a positive multiple of 64.
+ *
+ * Numerics: every entry point reproduces the reference's NEON build
+ * bit-for-bit (activation quantization 04-板载脚本与工具/qwen_kernels_opt.c:
+ * 182-205, GEMV float order :213-308, lm_head order :401-488,
+ * top-k order qwen_sampling.c:117-155,283-353), for any K.
+ */
+#ifndef QWEN_B200_H
+#define QWEN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QB_API __attribute__((visibility("default")))
+#else
+#define QB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QB_OK 0
+#define QB_EINVAL (-1)   /* bad argument (shape, null pointer, k out of range) */
+#define QB_ECUDA (-2)    /* CUDA runtime error */
+#define QB_ENOMEM (-3)   /* device allocation failed */
+#define QB_ENODEV (-4)   /* no usable CUDA device */
+
+/* ------------------------------------------------ 1. reference drop-ins */
+
+/* Replaces init_kernels() (04-板载脚本与工具/qwen_kernels_opt.c:128-135;
+ * called from qwen_real_engine.py:667-668).  Idempotent: selects the device
+ * (QWEN_B200_DEVICE, default 0), creates the stream and scratch.  Every other
+ * entry point calls it on first use. */
+QB_API void init_kernels(void);
+
+/* Replaces bfp8_gemv() (qwen_kernels_opt.c:207-326; callers
+ * qwen_kernels_opt.c:946-1001, qwen_real_engine.py:1073-1087,1108-1165,
+ * 1226-1232).  y[M] = BFP8 GEMV of x[K]; y is fully overwritten.  Unlike the
+ * reference it keeps no static activation cache, so it is reentrant across
+ * threads and never returns a stale quantization.  On error y is left
+ * unchanged and qwen_b200_last_error() says why (the reference has no error
+ * channel). */
+QB_API void bfp8_gemv(float* y, const float* x, const int8_t* mantissas, const uint8_t* exps, int M, int K);
+
+/* Replaces lm_head_argmax() (qwen_kernels_opt.c:401-506; callers
+ * qwen_kernels_opt.c:1046, qwen_real_engine.py:1301).  Returns the id with
+ * the largest score h . bf16(embed[id]); ties -> lowest id; 0 if no score
+ * exceeds -1e30.  Returns -1 on error. */
+QB_API int lm_head_argmax(const float* h, const uint16_t* embed_table, int vocab_size, int hidden_dim);
+
+/* Replaces lm_head_topk() (04-板载脚本与工具/qwen_sampling.c:283-353; caller
+ * chat_v3.py:151-155,180-181).  Writes the min(k, vocab) best (id, score)
+ * pairs sorted by score descending, ties by ascending id, and returns their
+ * number; 0 on invalid arguments.  This build serves k <= 1024. */
+QB_API int lm_head_topk(const float* h, const uint16_t* embed_table, int vocab_size, int hidden_dim, int k,
+                 int* out_ids, float* out_scores);
+
+/* Replaces sample_from_topk() (qwen_sampling.c:411-529; caller
+ * chat_v3.py:156-160,184-187).  Host-side temperature / top-k / top-p
+ * sampling with the reference's xorshift32 stream; same results as the
+ * reference for the same arguments and rng_state. */
+QB_API int sample_from_topk(const int* ids, const float* scores, int n, float temperature, int top_k,
+                     float top_p, unsigned int* rng_state);
+
+/* Replace the stage profiler (qwen_kernels_opt.c:71-91; read by
+ * qwen_real_engine.py:1008-1047 when QWEN_PROFILE=1).  Slots accumulate
+ * host wall milliseconds per entry point. */
+QB_API void qwen_prof_enable(int on);
+QB_API void qwen_prof_reset(void);
+QB_API int qwen_prof_count(void);
+QB_API double qwen_prof_get(int i);
+QB_API const char* qwen_prof_name(int i);
+
+/* ------------------------------------------------ weight registry */
+
+/* Upload [host_base, host_base + nbytes) once (e.g. the whole mmap'd weight
+ * file or the embedding file); later drop-in calls whose pointers fall inside
+ * it use the device copy.  Returns 0 or a QB_E* code.  No reference
+ * counterpart: the reference reads the mmap directly. */
+QB_API int qwen_b200_register_weights(const void* host_base, size_t nbytes);
+/* Drop every registration or cached upload that contains `host_ptr`. */
+QB_API int qwen_b200_forget_weights(const void* host_ptr);
+/* Drop everything. */
+QB_API void qwen_b200_reset_weights(void);
+
+/* ------------------------------------------------ 2. device entry points */
+
+/* y[M] = exact BFP8 GEMV of fp32 x[K] (quantized in-kernel by the reference
+ * rule).  Device form of bfp8_gemv(). */
+QB_API int qwen_b200_gemv_dev(float* y, const float* x, const int8_t* mant, const uint8_t* exps, int M, int K,
+                       void* stream);
+
+/* Same from an already quantized activation: xq int16 [K], xs fp32 [K/64]. */
+QB_API int qwen_b200_gemv_q_dev(float* y, const int16_t* xq, const float* xs, const int8_t* mant,
+                         const uint8_t* exps, int M, int K, void* stream);
+
+/* Block-64 activation quantizer (quant_x_blocks, qwen_kernels_opt.c:182-205)
+ * over B rows: x [B][K] -> xq int16 [B][K], xs [B][K/64]. */
+QB_API int qwen_b200_quant_dev(const float* x, int B, int K, int16_t* xq, float* xs, void* stream);
+
+/* Grouped launch of n independent GEMVs (e.g. the per-token linear stack).
+ * Arrays are HOST arrays of DEVICE pointers.  Returns a plan handle (>= 1)
+ * or a QB_E* code; the plan is reusable and safe to launch inside CUDA
+ * graph capture.  Every mant pointer must be 16-byte aligned, every exps
+ * pointer 8-byte aligned, every x 8-byte aligned, and every K a multiple of
+ * 512. */
+QB_API int qwen_b200_stack_create(int n, const int8_t* const* mant, const uint8_t* const* exps,
+                           const float* const* x, float* const* y, const int* M, const int* K);
+QB_API int qwen_b200_stack_run(int plan, void* stream);
+QB_API int qwen_b200_stack_destroy(int plan);
+
+/* bf16 lm_head over E [vocab][hidden] (tied embedding).  Always writes the
+ * greedy id to out_id[0]; for k > 0 also the top-k into out_ids/out_scores
+ * and its length into out_n[0].  k <= 1024.  Device form of
+ * lm_head_argmax() / lm_head_topk().  Calls on one device share a scratch
+ * area: do not run two lm_head calls concurrently on different streams. */
+QB_API int qwen_b200_lm_head_bf16_dev(const float* h, const uint16_t* E, int vocab, int hidden, int k,
+                               int* out_id, int* out_ids, float* out_scores, int* out_n, void* stream);
+
+/* BFP8 lm_head (vocab x hidden BFP8 matrix): exact bfp8_gemv scores fused
+ * with the same argmax / top-k rules; the scores never reach global memory.
+ * No reference routine (the reference lm_head is bf16); same scratch rule. */
+QB_API int qwen_b200_lm_head_bfp8_dev(const float* h, const int8_t* mant, const uint8_t* exps, int vocab,
+                               int hidden, int k, int* out_id, int* out_ids, float* out_scores,
+                               int* out_n, void* stream);
+
+/* Block-64 BFP8 packer on the device: w fp32 [M][K] -> mant int8 [M][K],
+ * exps uint8 [M][K/64], by the reference packer's rule
+ * (05-主机侧源码/bfp8_packer.py:53-86) with ceil(log2(peak)) taken exactly
+ * from the float's bits. */
+QB_API int qwen_b200_pack_bfp8_dev(const float* w, int M, int K, int8_t* mant, uint8_t* exps, void* stream);
+
+/* Description of the calling thread's last failure ("" if none). */
+QB_API const char* qwen_b200_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWEN_B200_H */

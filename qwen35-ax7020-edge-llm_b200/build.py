@@ -1,0 +1,98 @@
+"""Build the native parts of the package.
+
+    python qwen35-ax7020-edge-llm_b200/build.py
+
+produces, in-tree:
+  qwen_b200/libqwen_kernels_b200.so   CUDA kernels + C ABI (nvcc, sm_100a)
+  qwen_b200/_C*.so                    PyTorch operator library (torch.ops.qwen_b200)
+"""
+from __future__ import annotations
+
+import glob
+import os
+import shutil
+import subprocess
+import sys
+
+PKG_ROOT = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(PKG_ROOT)
+CSRC = os.path.join(PKG_ROOT, "csrc")
+OUT_DIR = os.path.join(PKG_ROOT, "qwen_b200")
+INCLUDE = os.path.join(REPO, "include")
+LIB_NAME = "libqwen_kernels_b200.so"
+
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+CU_SOURCES = ["bfp8_gemv.cu", "lm_head.cu", "pack.cu", "capi.cu"]
+
+
+def _nvcc() -> str:
+    cand = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(cand):
+        raise RuntimeError("nvcc not found")
+    return cand
+
+
+def _stale(target: str, deps: list[str]) -> bool:
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def build_core(force: bool = False, verbose: bool = False) -> str:
+    target = os.path.join(OUT_DIR, LIB_NAME)
+    deps = [os.path.join(CSRC, f) for f in os.listdir(CSRC)] + [os.path.join(INCLUDE, "qwen_b200.h")]
+    if not force and not _stale(target, deps):
+        return target
+    cmd = [_nvcc(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
+           "-Xcompiler", "-fvisibility=hidden", "-shared", f"-I{INCLUDE}", f"-I{CSRC}",
+           "-o", target + ".tmp", *[os.path.join(CSRC, f) for f in CU_SOURCES]]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+    subprocess.run(cmd, check=True)
+    os.replace(target + ".tmp", target)
+    return target
+
+
+def build_torch_ext(force: bool = False) -> str | None:
+    """Compile the torch.ops.qwen_b200 operator library (C++ only; it calls
+    the C ABI of the core library)."""
+    src = os.path.join(CSRC, "torch_ops.cpp")
+    if not os.path.exists(src):
+        return None
+    existing = glob.glob(os.path.join(OUT_DIR, "_C*.so"))
+    core = os.path.join(OUT_DIR, LIB_NAME)
+    if existing and not force and not _stale(existing[0], [src, core, os.path.join(INCLUDE, "qwen_b200.h")]):
+        return existing[0]
+    import torch.utils.cpp_extension as ce
+    from torch.utils.cpp_extension import _get_build_directory  # noqa: F401  (import check)
+
+    build_dir = os.path.join(PKG_ROOT, "_build", "torch_ext")
+    os.makedirs(build_dir, exist_ok=True)
+    ce.load(
+        name="_C",
+        sources=[src],
+        extra_include_paths=[INCLUDE, CSRC],
+        extra_cflags=["-O2", "-std=c++17"],
+        extra_ldflags=[f"-L{OUT_DIR}", "-lqwen_kernels_b200", "-Wl,-rpath,$ORIGIN"],
+        build_directory=build_dir,
+        is_python_module=False,
+        with_cuda=True,
+        verbose=False,
+    )
+    built = glob.glob(os.path.join(build_dir, "_C*.so"))
+    if not built:
+        raise RuntimeError("torch extension build produced no library")
+    dst = os.path.join(OUT_DIR, os.path.basename(built[0]))
+    shutil.copy2(built[0], dst)
+    return dst
+
+
+def build_all(force: bool = False, verbose: bool = False) -> None:
+    build_core(force=force, verbose=verbose)
+    build_torch_ext(force=force)
+
+
+if __name__ == "__main__":
+    build_all(force="--force" in sys.argv, verbose="-v" in sys.argv)
+    print("built", os.path.join(OUT_DIR, LIB_NAME))

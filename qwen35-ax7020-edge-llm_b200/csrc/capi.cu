@@ -1,0 +1,554 @@
+// capi.cu -- C ABI of libqwen_kernels_b200.so (declared in include/qwen_b200.h).
+//
+// The drop-in entry points keep the reference's signatures and host-pointer
+// conventions (04-板载脚本与工具/qwen_kernels_opt.c, qwen_sampling.c) and run
+// the work on the device; the _dev entry points take device pointers and a
+// stream and are what the PyTorch operators and the benchmarks call.
+#include "bfp8_gemv.cuh"
+#include "common.cuh"
+#include "lm_head.cuh"
+#include "topk.cuh"
+
+#include "qwen_b200.h"
+
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* what, cudaError_t e = cudaSuccess) {
+    char buf[256];
+    if (e != cudaSuccess)
+        snprintf(buf, sizeof buf, "%s: %s", what, cudaGetErrorString(e));
+    else
+        snprintf(buf, sizeof buf, "%s", what);
+    g_err = buf;
+    return code;
+}
+
+// ---------------------------------------------------------------- profiler
+enum { PF_GEMV = 0, PF_ARGMAX, PF_TOPK, PF_SAMPLE, PF_UPLOAD, PF_N };
+const char* kProfNames[PF_N] = {"bfp8_gemv", "lm_head_argmax", "lm_head_topk", "sample_from_topk",
+                                "weight_upload"};
+int g_prof_on = 0;
+double g_prof_ms[PF_N];
+
+struct ProfScope {
+    int slot;
+    std::chrono::steady_clock::time_point t0;
+    explicit ProfScope(int s) : slot(s), t0(std::chrono::steady_clock::now()) {}
+    ~ProfScope() {
+        if (g_prof_on)
+            g_prof_ms[slot] +=
+                std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    }
+};
+
+// ---------------------------------------------------------------- device context
+struct Ctx {
+    bool ready = false;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    qb::LmScratch* scratch = nullptr;
+    // pinned host staging + device buffers for the drop-in calls
+    void* h_in = nullptr;
+    size_t h_in_cap = 0;
+    void* h_out = nullptr;
+    size_t h_out_cap = 0;
+    void* d_in = nullptr;
+    size_t d_in_cap = 0;
+    void* d_out = nullptr;
+    size_t d_out_cap = 0;
+    int* d_res = nullptr;   // [0] id, [1] n
+    float* d_scores = nullptr;
+    size_t d_scores_cap = 0;
+};
+Ctx g_ctx;
+std::mutex g_mu;   // serialises the drop-in entry points
+
+int ensure_ctx() {
+    if (g_ctx.ready) return QB_OK;
+    int ndev = 0;
+    cudaError_t e = cudaGetDeviceCount(&ndev);
+    if (e != cudaSuccess || ndev <= 0) return fail(QB_ENODEV, "no CUDA device", e);
+    int dev = 0;
+    if (const char* s = getenv("QWEN_B200_DEVICE")) dev = atoi(s);
+    if (dev < 0 || dev >= ndev) dev = 0;
+    if ((e = cudaSetDevice(dev)) != cudaSuccess) return fail(QB_ECUDA, "cudaSetDevice", e);
+    if ((e = cudaStreamCreateWithFlags(&g_ctx.stream, cudaStreamNonBlocking)) != cudaSuccess)
+        return fail(QB_ECUDA, "cudaStreamCreate", e);
+    if ((e = cudaMalloc(&g_ctx.scratch, sizeof(qb::LmScratch))) != cudaSuccess)
+        return fail(QB_ENOMEM, "scratch alloc", e);
+    if ((e = cudaMemset(g_ctx.scratch, 0, sizeof(qb::LmScratch))) != cudaSuccess)
+        return fail(QB_ECUDA, "scratch clear", e);
+    if ((e = cudaMalloc(&g_ctx.d_res, 4 * sizeof(int))) != cudaSuccess)
+        return fail(QB_ENOMEM, "result alloc", e);
+    g_ctx.device = dev;
+    g_ctx.ready = true;
+    return QB_OK;
+}
+
+int grow_pinned(void** p, size_t* cap, size_t need) {
+    if (*cap >= need) return QB_OK;
+    if (*p) cudaFreeHost(*p);
+    *p = nullptr;
+    *cap = 0;
+    cudaError_t e = cudaMallocHost(p, need);
+    if (e != cudaSuccess) return fail(QB_ENOMEM, "pinned alloc", e);
+    *cap = need;
+    return QB_OK;
+}
+int grow_dev(void** p, size_t* cap, size_t need) {
+    if (*cap >= need) return QB_OK;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    cudaError_t e = cudaMalloc(p, need);
+    if (e != cudaSuccess) return fail(QB_ENOMEM, "device alloc", e);
+    *cap = need;
+    return QB_OK;
+}
+
+// ---------------------------------------------------------------- weight registry
+struct Range {
+    const unsigned char* host;
+    size_t bytes;
+    unsigned char* dev;
+};
+std::vector<Range> g_ranges;
+
+const void* lookup(const void* p, size_t bytes) {
+    const unsigned char* h = static_cast<const unsigned char*>(p);
+    for (const Range& r : g_ranges)
+        if (h >= r.host && h + bytes <= r.host + r.bytes) return r.dev + (h - r.host);
+    return nullptr;
+}
+
+int upload_range(const void* host, size_t bytes) {
+    ProfScope ps(PF_UPLOAD);
+    unsigned char* d = nullptr;
+    cudaError_t e = cudaMalloc(&d, bytes ? bytes : 1);
+    if (e != cudaSuccess) return fail(QB_ENOMEM, "weight upload alloc", e);
+    e = cudaMemcpy(d, host, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(d);
+        return fail(QB_ECUDA, "weight upload copy", e);
+    }
+    g_ranges.push_back({static_cast<const unsigned char*>(host), bytes, d});
+    return QB_OK;
+}
+
+// Device address of [p, p + bytes), uploading it on first sight.
+const void* device_of(const void* p, size_t bytes, int* rc) {
+    if (const void* d = lookup(p, bytes)) return d;
+    *rc = upload_range(p, bytes);
+    return *rc == QB_OK ? lookup(p, bytes) : nullptr;
+}
+
+// ---------------------------------------------------------------- stack plans
+struct StackPlan {
+    qb::GemvPlan plan;
+    qb::GemvDesc* dev_descs = nullptr;
+    bool live = false;
+};
+std::vector<StackPlan> g_plans;
+
+int check_gemv_args(const void* y, const void* x, const void* mant, const void* exps, int M, int K) {
+    if (!y || !x || !mant || !exps) return fail(QB_EINVAL, "null pointer");
+    if (M < 0 || K <= 0 || K % 64) return fail(QB_EINVAL, "M must be >= 0 and K a positive multiple of 64");
+    return QB_OK;
+}
+
+// ---------------------------------------------------------------- sampler
+// xorshift32 (Marsaglia 13/17/5) with the zero state remapped to 0x9E3779B9,
+// the generator the reference sampler uses (qwen_sampling.c:360-373).
+unsigned int xs32_next(unsigned int* st) {
+    unsigned int x = *st;
+    if (x == 0u) x = 0x9E3779B9u;
+    x ^= x << 13;
+    x ^= x >> 17;
+    x ^= x << 5;
+    *st = x;
+    return x;
+}
+
+struct Cand {
+    int id;
+    float score;
+};
+
+}  // namespace
+
+extern "C" {
+
+void init_kernels(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    ensure_ctx();
+}
+
+const char* qwen_b200_last_error(void) { return g_err.c_str(); }
+
+void qwen_prof_enable(int on) { g_prof_on = on; }
+void qwen_prof_reset(void) {
+    for (double& v : g_prof_ms) v = 0.0;
+}
+int qwen_prof_count(void) { return PF_N; }
+double qwen_prof_get(int i) { return (i >= 0 && i < PF_N) ? g_prof_ms[i] : 0.0; }
+const char* qwen_prof_name(int i) { return (i >= 0 && i < PF_N) ? kProfNames[i] : "?"; }
+
+int qwen_b200_register_weights(const void* host_base, size_t nbytes) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!host_base || !nbytes) return fail(QB_EINVAL, "empty range");
+    int rc = ensure_ctx();
+    if (rc) return rc;
+    if (lookup(host_base, nbytes)) return QB_OK;
+    return upload_range(host_base, nbytes);
+}
+
+int qwen_b200_forget_weights(const void* host_ptr) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const unsigned char* h = static_cast<const unsigned char*>(host_ptr);
+    for (size_t i = 0; i < g_ranges.size();) {
+        if (h >= g_ranges[i].host && h < g_ranges[i].host + g_ranges[i].bytes) {
+            cudaFree(g_ranges[i].dev);
+            g_ranges.erase(g_ranges.begin() + i);
+        } else {
+            i++;
+        }
+    }
+    return QB_OK;
+}
+
+void qwen_b200_reset_weights(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (Range& r : g_ranges) cudaFree(r.dev);
+    g_ranges.clear();
+}
+
+// ------------------------------------------------------------ drop-ins
+void bfp8_gemv(float* y, const float* x, const int8_t* mant, const uint8_t* exps, int M, int K) {
+    ProfScope ps(PF_GEMV);
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (check_gemv_args(y, x, mant, exps, M, K) || M == 0) return;
+    if (ensure_ctx()) return;
+    const size_t wbytes = (size_t)M * K, ebytes = (size_t)M * (K / 64);
+    int rc = QB_OK;
+    const void* dm;
+    const void* de;
+    if (exps == reinterpret_cast<const uint8_t*>(mant) + wbytes) {
+        dm = device_of(mant, wbytes + ebytes, &rc);
+        de = dm ? static_cast<const unsigned char*>(dm) + wbytes : nullptr;
+    } else {
+        dm = device_of(mant, wbytes, &rc);
+        de = dm ? device_of(exps, ebytes, &rc) : nullptr;
+    }
+    if (!dm || !de) return;
+    if (grow_pinned(&g_ctx.h_in, &g_ctx.h_in_cap, 4 * (size_t)K) ||
+        grow_pinned(&g_ctx.h_out, &g_ctx.h_out_cap, 4 * (size_t)M) ||
+        grow_dev(&g_ctx.d_in, &g_ctx.d_in_cap, 4 * (size_t)K) ||
+        grow_dev(&g_ctx.d_out, &g_ctx.d_out_cap, 4 * (size_t)M))
+        return;
+    cudaStream_t s = g_ctx.stream;
+    memcpy(g_ctx.h_in, x, 4 * (size_t)K);
+    cudaMemcpyAsync(g_ctx.d_in, g_ctx.h_in, 4 * (size_t)K, cudaMemcpyHostToDevice, s);
+    qb::GemvDesc d{};
+    d.mant = static_cast<const int8_t*>(dm);
+    d.exps = static_cast<const uint8_t*>(de);
+    d.x = static_cast<const float*>(g_ctx.d_in);
+    d.y = static_cast<float*>(g_ctx.d_out);
+    d.M = M;
+    d.K = K;
+    cudaError_t e = qb::launch_gemv(d, s);
+    if (e != cudaSuccess) {
+        fail(QB_ECUDA, "bfp8_gemv launch", e);
+        return;
+    }
+    cudaMemcpyAsync(g_ctx.h_out, g_ctx.d_out, 4 * (size_t)M, cudaMemcpyDeviceToHost, s);
+    e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        fail(QB_ECUDA, "bfp8_gemv", e);
+        return;
+    }
+    memcpy(y, g_ctx.h_out, 4 * (size_t)M);
+}
+
+static int lm_bf16_host(const float* h, const uint16_t* E, int vocab, int hidden, int k, int with_tail,
+                        int* out_ids, float* out_scores, int* id_out) {
+    if (ensure_ctx()) return QB_ENODEV;
+    int rc = QB_OK;
+    const void* dE = device_of(E, (size_t)vocab * hidden * 2, &rc);
+    if (!dE) return rc;
+    const size_t kk = (size_t)(k < vocab ? k : vocab);
+    const size_t in_b = 4 * (size_t)hidden;
+    const size_t out_b = kk * 8 + 16;
+    if ((rc = grow_pinned(&g_ctx.h_in, &g_ctx.h_in_cap, in_b)) ||
+        (rc = grow_pinned(&g_ctx.h_out, &g_ctx.h_out_cap, out_b)) ||
+        (rc = grow_dev(&g_ctx.d_in, &g_ctx.d_in_cap, in_b + 16)) ||
+        (rc = grow_dev(&g_ctx.d_out, &g_ctx.d_out_cap, out_b)))
+        return rc;
+    float* score_buf = nullptr;
+    if (hidden % 8 || reinterpret_cast<uintptr_t>(dE) % 16) {
+        if ((rc = grow_dev(reinterpret_cast<void**>(&g_ctx.d_scores), &g_ctx.d_scores_cap, 4 * (size_t)vocab)))
+            return rc;
+        score_buf = g_ctx.d_scores;
+    }
+    cudaStream_t s = g_ctx.stream;
+    memcpy(g_ctx.h_in, h, in_b);
+    cudaMemcpyAsync(g_ctx.d_in, g_ctx.h_in, in_b, cudaMemcpyHostToDevice, s);
+    int* d_ids = static_cast<int*>(g_ctx.d_out);
+    float* d_sc = reinterpret_cast<float*>(d_ids + kk);
+    cudaError_t e = qb::launch_lm_head_bf16(static_cast<const float*>(g_ctx.d_in), static_cast<const uint16_t*>(dE),
+                                            vocab, hidden, (int)kk, with_tail, g_ctx.scratch, score_buf,
+                                            g_ctx.d_res, d_ids, d_sc, g_ctx.d_res + 1, s);
+    if (e != cudaSuccess) return fail(QB_ECUDA, "lm_head launch", e);
+    int res[2] = {0, 0};
+    cudaMemcpyAsync(g_ctx.h_out, d_ids, kk * 8, cudaMemcpyDeviceToHost, s);
+    cudaMemcpyAsync(res, g_ctx.d_res, 2 * sizeof(int), cudaMemcpyDeviceToHost, s);
+    e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return fail(QB_ECUDA, "lm_head", e);
+    *id_out = res[0];
+    if (kk > 0) {
+        const int n = res[1];
+        memcpy(out_ids, g_ctx.h_out, (size_t)n * 4);
+        memcpy(out_scores, static_cast<char*>(g_ctx.h_out) + kk * 4, (size_t)n * 4);
+        return n;
+    }
+    return 0;
+}
+
+int lm_head_argmax(const float* h, const uint16_t* embed_table, int vocab_size, int hidden_dim) {
+    ProfScope ps(PF_ARGMAX);
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!h || !embed_table || vocab_size <= 0 || hidden_dim <= 0) {
+        fail(QB_EINVAL, "lm_head_argmax: bad arguments");
+        return -1;
+    }
+    int id = 0;
+    int rc = lm_bf16_host(h, embed_table, vocab_size, hidden_dim, 0, 0, nullptr, nullptr, &id);
+    return rc < 0 ? -1 : id;
+}
+
+int lm_head_topk(const float* h, const uint16_t* embed_table, int vocab_size, int hidden_dim, int k,
+                 int* out_ids, float* out_scores) {
+    ProfScope ps(PF_TOPK);
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!h || !embed_table || !out_ids || !out_scores) return 0;
+    if (vocab_size <= 0 || hidden_dim <= 0 || k <= 0) return 0;
+    if ((k < vocab_size ? k : vocab_size) > qb::kTopkMax) {
+        fail(QB_EINVAL, "lm_head_topk: k above 1024 is not served by this build");
+        return 0;
+    }
+    int id = 0;
+    int n = lm_bf16_host(h, embed_table, vocab_size, hidden_dim, k, 1, out_ids, out_scores, &id);
+    return n < 0 ? 0 : n;
+}
+
+int sample_from_topk(const int* ids, const float* scores, int n, float temperature, int top_k, float top_p,
+                     unsigned int* rng_state) {
+    ProfScope ps(PF_SAMPLE);
+    // Same procedure and operation order as qwen_sampling.c:411-529.
+    if (!ids || !scores || n <= 0) return -1;
+    if (!rng_state) return ids[0];
+    std::vector<Cand> sorted_copy;
+    bool is_sorted = true;
+    for (int i = 1; i < n; i++)
+        if (scores[i] > scores[i - 1]) {
+            is_sorted = false;
+            break;
+        }
+    if (!is_sorted) {
+        sorted_copy.resize(n);
+        for (int i = 0; i < n; i++) sorted_copy[i] = {ids[i], scores[i]};
+        qsort(sorted_copy.data(), (size_t)n, sizeof(Cand), [](const void* a, const void* b) -> int {
+            const Cand* pa = static_cast<const Cand*>(a);
+            const Cand* pb = static_cast<const Cand*>(b);
+            if (pa->score > pb->score) return -1;
+            if (pa->score < pb->score) return 1;
+            if (pa->id < pb->id) return -1;
+            if (pa->id > pb->id) return 1;
+            return 0;
+        });
+    }
+    auto ID = [&](int i) { return is_sorted ? ids[i] : sorted_copy[i].id; };
+    auto SC = [&](int i) { return is_sorted ? scores[i] : sorted_copy[i].score; };
+
+    if (!(temperature >= 1e-6f)) return ID(0);
+    int m = n;
+    if (top_k > 0 && top_k < m) m = top_k;
+    float maxf = SC(0);
+    for (int i = 1; i < m; i++)
+        if (SC(i) > maxf) maxf = SC(i);
+    const float inv_t = 1.0f / temperature;
+    double sum_all = 0.0;
+    for (int i = 0; i < m; i++) sum_all += (double)expf((SC(i) - maxf) * inv_t);
+    if (!(sum_all > 0.0)) return ID(0);
+    float p_thresh = top_p;
+    if (!(p_thresh > 0.0f)) p_thresh = 0.0f;
+    if (p_thresh > 1.0f) p_thresh = 1.0f;
+    int keep = m;
+    double cum = 0.0;
+    for (int i = 0; i < m; i++) {
+        cum += (double)expf((SC(i) - maxf) * inv_t) / sum_all;
+        if (cum > (double)p_thresh) {
+            keep = i + 1;
+            break;
+        }
+    }
+    if (keep < 1) keep = 1;
+    double sum_keep = 0.0;
+    for (int i = 0; i < keep; i++) sum_keep += (double)expf((SC(i) - maxf) * inv_t);
+    if (!(sum_keep > 0.0)) return ID(0);
+    const double u = (double)((float)(xs32_next(rng_state) >> 8) * (1.0f / 16777216.0f));
+    const double r = u * sum_keep;
+    cum = 0.0;
+    int chosen = keep - 1;
+    for (int i = 0; i < keep; i++) {
+        cum += (double)expf((SC(i) - maxf) * inv_t);
+        if (r < cum) {
+            chosen = i;
+            break;
+        }
+    }
+    return ID(chosen);
+}
+
+// ------------------------------------------------------------ device entry points
+int qwen_b200_gemv_dev(float* y, const float* x, const int8_t* mant, const uint8_t* exps, int M, int K,
+                       void* stream) {
+    if (int rc = check_gemv_args(y, x, mant, exps, M, K)) return rc;
+    qb::GemvDesc d{};
+    d.mant = mant;
+    d.exps = exps;
+    d.x = x;
+    d.y = y;
+    d.M = M;
+    d.K = K;
+    cudaError_t e = qb::launch_gemv(d, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_gemv_dev", e);
+}
+
+int qwen_b200_gemv_q_dev(float* y, const int16_t* xq, const float* xs, const int8_t* mant,
+                         const uint8_t* exps, int M, int K, void* stream) {
+    if (int rc = check_gemv_args(y, xq, mant, exps, M, K)) return rc;
+    if (!xs) return fail(QB_EINVAL, "null xs");
+    qb::GemvDesc d{};
+    d.mant = mant;
+    d.exps = exps;
+    d.xq = xq;
+    d.xs = xs;
+    d.y = y;
+    d.M = M;
+    d.K = K;
+    cudaError_t e = qb::launch_gemv(d, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_gemv_q_dev", e);
+}
+
+int qwen_b200_quant_dev(const float* x, int B, int K, int16_t* xq, float* xs, void* stream) {
+    if (!x || !xq || !xs || B < 0 || K <= 0 || K % 64) return fail(QB_EINVAL, "qwen_b200_quant_dev: bad arguments");
+    cudaError_t e = qb::launch_quant_block64(x, B, K, xq, xs, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_quant_dev", e);
+}
+
+int qwen_b200_stack_create(int n, const int8_t* const* mant, const uint8_t* const* exps, const float* const* x,
+                           float* const* y, const int* M, const int* K) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (n <= 0 || !mant || !exps || !x || !y || !M || !K) return fail(QB_EINVAL, "stack: bad arguments");
+    std::vector<qb::GemvDesc> v;
+    for (int i = 0; i < n; i++) {
+        if (M[i] < 0 || K[i] <= 0 || K[i] % 64 || !mant[i] || !exps[i] || !x[i] || !y[i])
+            return fail(QB_EINVAL, "stack: bad descriptor");
+        if (M[i] == 0) continue;
+        qb::GemvDesc d{};
+        d.mant = mant[i];
+        d.exps = exps[i];
+        d.x = x[i];
+        d.y = y[i];
+        d.M = M[i];
+        d.K = K[i];
+        v.push_back(d);
+    }
+    StackPlan sp;
+    if (!qb::gemv_plan(v.data(), (int)v.size(), 32, &sp.plan))
+        return fail(QB_EINVAL, "stack: every K must be a multiple of 512 with 16/8/8-byte aligned mant/exps/x");
+    cudaError_t e = cudaMalloc(&sp.dev_descs, sizeof(qb::GemvDesc) * (v.size() ? v.size() : 1));
+    if (e != cudaSuccess) return fail(QB_ENOMEM, "stack alloc", e);
+    e = cudaMemcpy(sp.dev_descs, v.data(), sizeof(qb::GemvDesc) * v.size(), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return fail(QB_ECUDA, "stack upload", e);
+    sp.live = true;
+    g_plans.push_back(sp);
+    return (int)g_plans.size();
+}
+
+int qwen_b200_stack_run(int plan, void* stream) {
+    if (plan < 1 || plan > (int)g_plans.size() || !g_plans[plan - 1].live) return fail(QB_EINVAL, "stack: bad handle");
+    const StackPlan& sp = g_plans[plan - 1];
+    cudaError_t e = qb::launch_gemv_list(sp.dev_descs, sp.plan, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_stack_run", e);
+}
+
+int qwen_b200_stack_destroy(int plan) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (plan < 1 || plan > (int)g_plans.size() || !g_plans[plan - 1].live) return fail(QB_EINVAL, "stack: bad handle");
+    cudaFree(g_plans[plan - 1].dev_descs);
+    g_plans[plan - 1].live = false;
+    g_plans[plan - 1].dev_descs = nullptr;
+    return QB_OK;
+}
+
+static int scratch_for_current_device(qb::LmScratch** out) {
+    // one zeroed scratch per device, created on first use
+    static std::mutex mu;
+    static std::vector<qb::LmScratch*> per_dev;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(QB_ECUDA, "cudaGetDevice", e);
+    std::lock_guard<std::mutex> lk(mu);
+    if ((int)per_dev.size() <= dev) per_dev.resize(dev + 1, nullptr);
+    if (!per_dev[dev]) {
+        qb::LmScratch* p = nullptr;
+        if ((e = cudaMalloc(&p, sizeof(qb::LmScratch))) != cudaSuccess) return fail(QB_ENOMEM, "scratch alloc", e);
+        if ((e = cudaMemset(p, 0, sizeof(qb::LmScratch))) != cudaSuccess) return fail(QB_ECUDA, "scratch clear", e);
+        per_dev[dev] = p;
+    }
+    *out = per_dev[dev];
+    return QB_OK;
+}
+
+int qwen_b200_lm_head_bf16_dev(const float* h, const uint16_t* E, int vocab, int hidden, int k, int* out_id,
+                               int* out_ids, float* out_scores, int* out_n, void* stream) {
+    if (!h || !E || !out_id || vocab <= 0 || hidden <= 0 || k < 0) return fail(QB_EINVAL, "lm_head_bf16: bad arguments");
+    if (k > 0 && (!out_ids || !out_scores || !out_n)) return fail(QB_EINVAL, "lm_head_bf16: null outputs");
+    if ((k < vocab ? k : vocab) > qb::kTopkMax) return fail(QB_EINVAL, "lm_head_bf16: k above 1024");
+    if (hidden % 8 || reinterpret_cast<uintptr_t>(E) % 16 || reinterpret_cast<uintptr_t>(h) % 8)
+        return fail(QB_EINVAL, "lm_head_bf16_dev: hidden must be a multiple of 8, E 16-byte and h 8-byte aligned");
+    qb::LmScratch* sc = nullptr;
+    if (int rc = scratch_for_current_device(&sc)) return rc;
+    cudaError_t e = qb::launch_lm_head_bf16(h, E, vocab, hidden, k, 1, sc, nullptr, out_id, out_ids, out_scores,
+                                            out_n, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_lm_head_bf16_dev", e);
+}
+
+int qwen_b200_lm_head_bfp8_dev(const float* h, const int8_t* mant, const uint8_t* exps, int vocab, int hidden,
+                               int k, int* out_id, int* out_ids, float* out_scores, int* out_n, void* stream) {
+    if (!h || !mant || !exps || !out_id || vocab <= 0 || hidden <= 0 || k < 0)
+        return fail(QB_EINVAL, "lm_head_bfp8: bad arguments");
+    if (k > 0 && (!out_ids || !out_scores || !out_n)) return fail(QB_EINVAL, "lm_head_bfp8: null outputs");
+    if ((k < vocab ? k : vocab) > qb::kTopkMax) return fail(QB_EINVAL, "lm_head_bfp8: k above 1024");
+    qb::LmScratch* sc = nullptr;
+    if (int rc = scratch_for_current_device(&sc)) return rc;
+    cudaError_t e = qb::launch_bfp8_lm_head(h, mant, exps, vocab, hidden, k, sc, out_id, out_ids, out_scores, out_n,
+                                            static_cast<cudaStream_t>(stream));
+    if (e == cudaErrorInvalidValue)
+        return fail(QB_EINVAL, "lm_head_bfp8: hidden must be a multiple of 512 with 16/8/8-byte aligned mant/exps/h");
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_lm_head_bfp8_dev", e);
+}
+
+}  // extern "C"

@@ -1,0 +1,89 @@
+// common.cuh -- shared device helpers for the BFP8 GEMV / lm_head kernels.
+//
+// Floating point: the reference's vector path runs on ARMv7 Advanced SIMD,
+// which always flushes subnormal inputs and results to a same-signed zero and
+// never fuses multiply-add (VMLA rounds the product).  The *_ftz helpers below
+// are single PTX instructions with exactly those semantics; the *_rn helpers
+// are the IEEE (subnormal-preserving) forms used where the reference runs on
+// scalar VFP.  Every call is an explicit instruction, so nvcc cannot contract
+// a multiply and an add into an FMA.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace qb {
+
+constexpr int kWarp = 32;
+
+__device__ __forceinline__ float mul_ftz(float a, float b) {
+    float d;
+    asm("mul.rn.ftz.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
+__device__ __forceinline__ float add_ftz(float a, float b) {
+    float d;
+    asm("add.rn.ftz.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
+__device__ __forceinline__ float mul_rn(float a, float b) {
+    float d;
+    asm("mul.rn.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
+__device__ __forceinline__ float add_rn(float a, float b) {
+    float d;
+    asm("add.rn.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
+__device__ __forceinline__ float i2f_rn(int v) {
+    float d;
+    asm("cvt.rn.f32.s32 %0, %1;" : "=f"(d) : "r"(v));
+    return d;
+}
+
+// 2^(e-134) as the vector unit sees it: exact power of two for e >= 8, a
+// flushed zero for the subnormal range e < 8.
+__device__ __forceinline__ float exp_scale_ftz(uint32_t e) {
+    return e >= 8u ? __uint_as_float((e - 7u) << 23) : 0.0f;
+}
+// 2^(e-134) with IEEE subnormals (scalar VFP): 2^(e-134) = 2^(e+15) * 2^-149.
+__device__ __forceinline__ float exp_scale_ieee(uint32_t e) {
+    return e >= 8u ? __uint_as_float((e - 7u) << 23) : __uint_as_float(1u << (e + 15u));
+}
+
+// Monotone map of a float score to an unsigned key (-0 and +0 share a key).
+__device__ __forceinline__ uint32_t ord_score(float s) {
+    uint32_t u = __float_as_uint(s);
+    if (u == 0x80000000u) u = 0u;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float unord_score(uint32_t k) {
+    uint32_t u = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
+    return __uint_as_float(u);
+}
+// 64-bit candidate key: higher score first, then lower id first.
+__device__ __forceinline__ unsigned long long cand_key(float s, int id) {
+    return ((unsigned long long)ord_score(s) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)id);
+}
+__device__ __forceinline__ int key_id(unsigned long long k) {
+    return (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+}
+__device__ __forceinline__ float key_score(unsigned long long k) {
+    return unord_score((uint32_t)(k >> 32));
+}
+
+// ------------------------------------------------------------ cp.async
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)), "l"(src));
+}
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(smem_u32(dst)), "l"(src));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+}  // namespace qb

@@ -1,0 +1,284 @@
+// lm_head.cu -- bf16 tied-embedding lm_head scan with fused argmax / top-k.
+//
+// Semantics (reference 04-板载脚本与工具/qwen_kernels_opt.c:401-488 and
+// qwen_sampling.c:160-353): score_t = sum_i h_i * bf16(E[t][i]) evaluated as
+// the NEON loop does -- eight fp32 chains c = i mod 8, each
+// acc_c = acc_c + E*h with a rounded (flushed) product, then
+// s = ((c0+c4) + (c2+c6)) + ((c1+c5) + (c3+c7)) -- so every score is
+// bit-identical to the reference build.  Greedy pick: best must exceed -1e30,
+// strict '>' in ascending id (ties -> lowest id).  Top-k: scores above
+// -FLT_MAX, sorted descending, ties by ascending id.  The 65536 scores never
+// leave the SM: each CTA keeps its candidates in shared memory.
+//
+// Kernel shape: a unit is 64 table rows; thread t owns row t/4 and the two
+// chains 2*(t%4), 2*(t%4)+1 for the whole unit, so every chain is summed in
+// one thread in element order.  Rows stream through a P-stage cp.async ring
+// in 16 KB slices (64 rows x 256 bytes) laid out as 128-byte rows with the
+// 16-byte chunk index XORed by (row & 7) (the TMA SWIZZLE_128B pattern); the
+// 32-bit reads of a warp (8 rows x one chunk) are conflict free.
+#include "bfp8_gemv.cuh"
+#include "common.cuh"
+#include "lm_head.cuh"
+#include "topk.cuh"
+
+#include <algorithm>
+
+namespace qb {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kRows = 64;                 // rows per unit
+constexpr int kSegBytes = 256;            // bytes of one row per slice
+constexpr int kChunks = kSegBytes / 16;   // 16-byte chunks of one row per slice
+constexpr int kStage = kRows * kSegBytes; // 16 KB
+constexpr int kP = 6;
+
+struct LmArgs {
+    const float* h;
+    const uint16_t* E;
+    int vocab, hidden;
+    int units, slices;  // per unit
+    LmScratch* sc;
+    int kk;
+    int* out_id;
+    int* out_ids;
+    float* out_scores;
+    int* out_n;
+};
+
+__device__ __forceinline__ void issue(const LmArgs& A, int u, int s, unsigned char* st) {
+    const int r0 = u * kRows;
+    const int rv = min(kRows, A.vocab - r0);
+    const int chunks_total = A.hidden >> 3;          // 16-byte chunks per row
+    const int vc = min(kChunks, chunks_total - s * kChunks);
+    const unsigned char* src = reinterpret_cast<const unsigned char*>(A.E) +
+                               ((size_t)r0 * A.hidden + (size_t)s * (kSegBytes / 2)) * 2;
+    const size_t rowb = (size_t)A.hidden * 2;
+    if (vc == kChunks) {
+#pragma unroll 4
+        for (int idx = threadIdx.x; idx < rv * kChunks; idx += kThreads) {
+            int r = idx / kChunks, q = idx % kChunks;
+            cp_async16(st + (q >> 3) * (kRows * 128) + r * 128 + (((q & 7) ^ (r & 7)) << 4),
+                       src + (size_t)r * rowb + q * 16);
+        }
+    } else {
+        for (int idx = threadIdx.x; idx < rv * vc; idx += kThreads) {
+            int r = idx / vc, q = idx - r * vc;
+            cp_async16(st + (q >> 3) * (kRows * 128) + r * 128 + (((q & 7) ^ (r & 7)) << 4),
+                       src + (size_t)r * rowb + q * 16);
+        }
+    }
+}
+
+template <bool TOPK>
+__global__ void __launch_bounds__(kThreads, 1) lm_bf16_kernel(const __grid_constant__ LmArgs A) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    unsigned char* stages = smem;
+    float* hs = reinterpret_cast<float*>(smem + kP * kStage);
+    unsigned long long* cand = reinterpret_cast<unsigned long long*>(hs + A.hidden);
+    __shared__ int s_cand_count;
+    __shared__ unsigned long long s_red[kThreads / 32];
+
+    const int tid = threadIdx.x;
+    const int r = tid >> 2, p = tid & 3;
+    if (tid == 0) s_cand_count = 0;
+
+    // contiguous unit range of this CTA
+    const int u_begin = (int)(((long long)A.units * blockIdx.x) / gridDim.x);
+    const int u_end = (int)(((long long)A.units * (blockIdx.x + 1)) / gridDim.x);
+    const int total = (u_end - u_begin) * A.slices;
+
+    // prologue: first P-1 slices, then h (overlaps the copies)
+    int iu = u_begin, is = 0, issued = 0;
+#pragma unroll 1
+    for (int k = 0; k < kP - 1; k++) {
+        if (issued < total) {
+            issue(A, iu, is, stages + k * kStage);
+            if (++is == A.slices) { is = 0; iu++; }
+            issued++;
+        }
+        cp_async_commit();
+    }
+    for (int i = tid; i < A.hidden; i += kThreads) hs[i] = A.h[i];
+
+    unsigned long long best = 0ull;
+    float ca = 0.0f, cb = 0.0f;
+    int cu = u_begin, cs = 0;
+#pragma unroll 1
+    for (int it = 0; it < total; it++) {
+        cp_async_wait<kP - 2>();
+        __syncthreads();
+        if (issued < total) {
+            issue(A, iu, is, stages + ((it + kP - 1) % kP) * kStage);
+            if (++is == A.slices) { is = 0; iu++; }
+            issued++;
+        }
+        cp_async_commit();
+        if (TOPK && s_cand_count > kCandCap - 2 * kRows) cand_compact(cand, &s_cand_count, A.kk);
+
+        const unsigned char* st = stages + (it % kP) * kStage;
+        const int chunks_total = A.hidden >> 3;
+        const int vc = min(kChunks, chunks_total - cs * kChunks);
+        const unsigned char* rowp = st + r * 128 + 4 * p;
+        const float2* hp = reinterpret_cast<const float2*>(hs + cs * (kSegBytes / 2) + 2 * p);
+        const int sw = r & 7;
+        if (vc == kChunks) {
+#pragma unroll
+            for (int q = 0; q < kChunks; q++) {
+                uint32_t w = *reinterpret_cast<const uint32_t*>(rowp + (q >> 3) * (kRows * 128) +
+                                                                 (((q & 7) ^ sw) << 4));
+                float2 hv = hp[4 * q];
+                ca = add_ftz(ca, mul_ftz(__uint_as_float(w << 16), hv.x));
+                cb = add_ftz(cb, mul_ftz(__uint_as_float(w & 0xFFFF0000u), hv.y));
+            }
+        } else {
+            for (int q = 0; q < vc; q++) {
+                uint32_t w = *reinterpret_cast<const uint32_t*>(rowp + (q >> 3) * (kRows * 128) +
+                                                                 (((q & 7) ^ sw) << 4));
+                float2 hv = hp[4 * q];
+                ca = add_ftz(ca, mul_ftz(__uint_as_float(w << 16), hv.x));
+                cb = add_ftz(cb, mul_ftz(__uint_as_float(w & 0xFFFF0000u), hv.y));
+            }
+        }
+        if (cs == A.slices - 1) {
+            // thread p holds chains (2p, 2p+1); combine in the NEON order
+            float oa = __shfl_xor_sync(0xffffffffu, ca, 2);
+            float ob = __shfl_xor_sync(0xffffffffu, cb, 2);
+            float lo = add_ftz(ca, oa), hi = add_ftz(cb, ob);   // p=0: c0+c4, c1+c5; p=1: c2+c6, c3+c7
+            float lo2 = __shfl_xor_sync(0xffffffffu, lo, 1);
+            float hi2 = __shfl_xor_sync(0xffffffffu, hi, 1);
+            float s = add_ftz(add_ftz(lo, lo2), add_ftz(hi, hi2));
+            const int row = cu * kRows + r;
+            if (p == 0 && row < A.vocab) {
+                if (s > -1e30f) {
+                    unsigned long long key = cand_key(s, row);
+                    best = key > best ? key : best;
+                }
+                if (TOPK && s > -3.402823466e38f) {
+                    int pos = atomicAdd(&s_cand_count, 1);
+                    cand[pos] = cand_key(s, row);
+                }
+            }
+            ca = cb = 0.0f;
+            cs = 0;
+            cu++;
+        } else {
+            cs++;
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    unsigned long long* work = reinterpret_cast<unsigned long long*>(stages);
+    lm_finish(A.sc, cand, &s_cand_count, work, (kP * kStage) / 8, best, TOPK ? A.kk : 0, A.out_id,
+              A.out_ids, A.out_scores, A.out_n, s_red);
+}
+
+// Any hidden size / alignment: one thread per row, same score order; the
+// with_tail flag adds the elements past the last multiple of 8 on IEEE
+// scalar arithmetic (lm_head_topk) or drops them (lm_head_argmax).
+__global__ void __launch_bounds__(kThreads) lm_bf16_generic_kernel(const float* h, const uint16_t* E,
+                                                                  int vocab, int hidden, int with_tail,
+                                                                  float* scores) {
+    const int t = blockIdx.x * kThreads + threadIdx.x;
+    if (t >= vocab) return;
+    const uint16_t* row = E + (size_t)t * hidden;
+    float c[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int i = 0;
+    for (; i + 8 <= hidden; i += 8)
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            c[j] = add_ftz(c[j], mul_ftz(__uint_as_float((uint32_t)row[i + j] << 16), h[i + j]));
+    float s = add_ftz(add_ftz(add_ftz(c[0], c[4]), add_ftz(c[2], c[6])),
+                      add_ftz(add_ftz(c[1], c[5]), add_ftz(c[3], c[7])));
+    if (with_tail)
+        for (; i < hidden; i++) s = add_rn(s, mul_rn(h[i], __uint_as_float((uint32_t)row[i] << 16)));
+    scores[t] = s;
+}
+
+// Selection over a materialised score vector (generic-shape path only).
+__global__ void __launch_bounds__(kThreads, 1) select_kernel(const float* scores, int vocab,
+                                                             const __grid_constant__ LmArgs A) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    unsigned long long* cand = reinterpret_cast<unsigned long long*>(smem);
+    unsigned long long* work = cand + kCandCap;
+    __shared__ int s_cand_count;
+    __shared__ unsigned long long s_red[kThreads / 32];
+    if (threadIdx.x == 0) s_cand_count = 0;
+    __syncthreads();
+    const int lo = (int)(((long long)vocab * blockIdx.x) / gridDim.x);
+    const int hi = (int)(((long long)vocab * (blockIdx.x + 1)) / gridDim.x);
+    unsigned long long best = 0ull;
+    for (int base = lo; base < hi; base += kThreads) {
+        if (A.kk > 0 && s_cand_count > kCandCap - kThreads) cand_compact(cand, &s_cand_count, A.kk);
+        int t = base + threadIdx.x;
+        if (t < hi) {
+            float s = scores[t];
+            if (s > -1e30f) {
+                unsigned long long key = cand_key(s, t);
+                best = key > best ? key : best;
+            }
+            if (A.kk > 0 && s > -3.402823466e38f) {
+                int pos = atomicAdd(&s_cand_count, 1);
+                cand[pos] = cand_key(s, t);
+            }
+        }
+        __syncthreads();
+    }
+    lm_finish(A.sc, cand, &s_cand_count, work, kCandCap * 4, best, A.kk, A.out_id, A.out_ids,
+              A.out_scores, A.out_n, s_red);
+}
+
+}  // namespace
+
+cudaError_t launch_lm_head_bf16(const float* h, const uint16_t* E, int vocab, int hidden, int k,
+                                int with_tail, LmScratch* scratch, float* score_buf, int* out_id,
+                                int* out_ids, float* out_scores, int* out_n, cudaStream_t stream) {
+    if (vocab <= 0 || hidden <= 0 || k < 0 || k > kTopkMax) return cudaErrorInvalidValue;
+    LmArgs A{};
+    A.h = h;
+    A.E = E;
+    A.vocab = vocab;
+    A.hidden = hidden;
+    A.sc = scratch;
+    A.kk = std::min(k, vocab);
+    A.out_id = out_id;
+    A.out_ids = out_ids;
+    A.out_scores = out_scores;
+    A.out_n = out_n;
+    const bool fast = hidden % 8 == 0 && reinterpret_cast<uintptr_t>(E) % 16 == 0 &&
+                      reinterpret_cast<uintptr_t>(h) % 8 == 0;
+    if (fast) {
+        A.units = (vocab + kRows - 1) / kRows;
+        A.slices = ((hidden >> 3) + kChunks - 1) / kChunks;
+        const int grid = std::min(std::min(num_sms(), A.units), kMaxGrid);
+        const size_t smem = (size_t)kP * kStage + 4 * (size_t)hidden + ((4 * (size_t)hidden) % 16 ? 8 : 0) +
+                            (size_t)kCandCap * 8;
+        cudaError_t err;
+        if (A.kk > 0) {
+            err = cudaFuncSetAttribute(lm_bf16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+            if (err != cudaSuccess) return err;
+            lm_bf16_kernel<true><<<grid, kThreads, smem, stream>>>(A);
+        } else {
+            err = cudaFuncSetAttribute(lm_bf16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+            if (err != cudaSuccess) return err;
+            lm_bf16_kernel<false><<<grid, kThreads, smem, stream>>>(A);
+        }
+        return cudaGetLastError();
+    }
+    if (!score_buf) return cudaErrorInvalidValue;
+    lm_bf16_generic_kernel<<<(vocab + kThreads - 1) / kThreads, kThreads, 0, stream>>>(h, E, vocab, hidden,
+                                                                                     with_tail, score_buf);
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    const size_t smem = (size_t)kCandCap * 8 * 5;
+    err = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess) return err;
+    const int grid = std::max(1, std::min(std::min(num_sms(), (vocab + 1023) / 1024), kMaxGrid));
+    select_kernel<<<grid, kThreads, smem, stream>>>(score_buf, vocab, A);
+    return cudaGetLastError();
+}
+
+}  // namespace qb

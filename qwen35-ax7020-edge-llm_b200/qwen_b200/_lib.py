@@ -1,0 +1,71 @@
+"""ctypes binding of libqwen_kernels_b200.so (the C ABI in include/qwen_b200.h).
+
+The library is built in-tree by ``build.py``.  Importing this module never
+falls back to anything else: if the library is missing or fails to load, the
+import raises, so a run without the CUDA path fails loudly.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libqwen_kernels_b200.so")
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_F = ctypes.c_float
+
+# name -> (restype, argtypes); mirrors include/qwen_b200.h
+SIGNATURES = {
+    "init_kernels": (None, []),
+    "bfp8_gemv": (None, [_P, _P, _P, _P, _I, _I]),
+    "lm_head_argmax": (_I, [_P, _P, _I, _I]),
+    "lm_head_topk": (_I, [_P, _P, _I, _I, _I, _P, _P]),
+    "sample_from_topk": (_I, [_P, _P, _I, _F, _I, _F, _P]),
+    "qwen_prof_enable": (None, [_I]),
+    "qwen_prof_reset": (None, []),
+    "qwen_prof_count": (_I, []),
+    "qwen_prof_get": (ctypes.c_double, [_I]),
+    "qwen_prof_name": (ctypes.c_char_p, [_I]),
+    "qwen_b200_register_weights": (_I, [_P, ctypes.c_size_t]),
+    "qwen_b200_forget_weights": (_I, [_P]),
+    "qwen_b200_reset_weights": (None, []),
+    "qwen_b200_gemv_dev": (_I, [_P, _P, _P, _P, _I, _I, _P]),
+    "qwen_b200_gemv_q_dev": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
+    "qwen_b200_quant_dev": (_I, [_P, _I, _I, _P, _P, _P]),
+    "qwen_b200_stack_create": (_I, [_I, _P, _P, _P, _P, _P, _P]),
+    "qwen_b200_stack_run": (_I, [_I, _P]),
+    "qwen_b200_stack_destroy": (_I, [_I]),
+    "qwen_b200_lm_head_bf16_dev": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P, _P]),
+    "qwen_b200_lm_head_bfp8_dev": (_I, [_P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P]),
+    "qwen_b200_pack_bfp8_dev": (_I, [_P, _I, _I, _P, _P, _P]),
+    "qwen_b200_last_error": (ctypes.c_char_p, []),
+}
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the kernel library (raises OSError if it is absent)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise OSError(f"{LIB_PATH} is missing: run qwen35-ax7020-edge-llm_b200/build.py")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+class KernelError(RuntimeError):
+    pass
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = load().qwen_b200_last_error().decode(errors="replace")
+        raise KernelError(f"{what} failed ({rc}): {msg}")

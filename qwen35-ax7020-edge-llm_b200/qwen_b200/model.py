@@ -1,0 +1,185 @@
+"""Linear-stack shapes of the served model and synthetic BFP8 weight stacks.
+
+The per-token linear stack of Qwen3.5-0.8B as the reference engine runs it
+(04-板载脚本与工具/qwen_real_engine.py:848-999, 1060-1166; shapes from
+06-模型与权重/config.json and qwen35_weights_64k_manifest.json): 24 layers,
+layers 3, 7, 11, 15, 19, 23 full attention (q+gate 4096x1024, k 512x1024,
+v 512x1024, o 1024x2048), the other 18 Gated-DeltaNet (in_proj_qkv
+6144x1024, in_proj_z 2048x1024, out_proj 1024x2048), every layer an MLP
+(gate 3584x1024, up 3584x1024, down 1024x3584): 150 BFP8 tensors,
+504,791,040 bytes.
+"""
+from __future__ import annotations
+
+import json
+from dataclasses import dataclass
+
+HIDDEN = 1024
+FFN = 3584
+LAYERS = 24
+FULL_ATTN = (3, 7, 11, 15, 19, 23)
+VOCAB = 65536
+
+
+@dataclass(frozen=True)
+class Linear:
+    name: str
+    M: int
+    K: int
+
+    @property
+    def mant_bytes(self) -> int:
+        return self.M * self.K
+
+    @property
+    def exp_bytes(self) -> int:
+        return self.M * self.K // 64
+
+    @property
+    def soa_bytes(self) -> int:
+        e = self.exp_bytes
+        return self.mant_bytes + e + ((-e) % 8)
+
+
+def qwen35_08b_stack() -> list[Linear]:
+    """The 150 BFP8 GEMVs of one token, in the order the engine issues them."""
+    out = []
+    for l in range(LAYERS):
+        p = f"model.language_model.layers.{l}."
+        if l in FULL_ATTN:
+            out += [Linear(p + "self_attn.q_proj.weight", 4096, HIDDEN),
+                    Linear(p + "self_attn.k_proj.weight", 512, HIDDEN),
+                    Linear(p + "self_attn.v_proj.weight", 512, HIDDEN),
+                    Linear(p + "self_attn.o_proj.weight", HIDDEN, 2048)]
+        else:
+            out += [Linear(p + "linear_attn.in_proj_qkv.weight", 6144, HIDDEN),
+                    Linear(p + "linear_attn.in_proj_z.weight", 2048, HIDDEN),
+                    Linear(p + "linear_attn.out_proj.weight", HIDDEN, 2048)]
+        out += [Linear(p + "mlp.gate_proj.weight", FFN, HIDDEN),
+                Linear(p + "mlp.up_proj.weight", FFN, HIDDEN),
+                Linear(p + "mlp.down_proj.weight", HIDDEN, FFN)]
+    return out
+
+
+def scaled_stack(layers: int = 8, hidden: int = 8192, ffn: int = 28672) -> list[Linear]:
+    """The multi-GPU configuration: `layers` x (gate, up ffn x hidden, down hidden x ffn)."""
+    out = []
+    for l in range(layers):
+        p = f"layers.{l}.mlp."
+        out += [Linear(p + "gate_proj", ffn, hidden), Linear(p + "up_proj", ffn, hidden),
+                Linear(p + "down_proj", hidden, ffn)]
+    return out
+
+
+def stack_bytes(stack) -> dict:
+    """Algorithmic bytes of one pass: weights (mantissas + exponents) and the
+    fp32 activation in / output out of every GEMV."""
+    w = sum(t.mant_bytes + t.exp_bytes for t in stack)
+    io = sum(4 * t.K + 4 * t.M for t in stack)
+    macs = sum(t.M * t.K for t in stack)
+    return {"weights": w, "io": io, "total": w + io, "macs": macs}
+
+
+def align64(n: int) -> int:
+    return (n + 63) & ~63
+
+
+def layout(stack) -> tuple[dict, int]:
+    """Offsets of each tensor in one contiguous buffer, 64-byte aligned like the
+    reference weight file (05-主机侧源码/export_qwen35_weights_bfp8_64k.py:31,64-80)."""
+    off = 0
+    table = {}
+    for t in stack:
+        off = align64(off)
+        table[t.name] = (off, t)
+        off += t.soa_bytes
+    return table, align64(off)
+
+
+def manifest_for(stack, model_name="synthetic") -> dict:
+    """A manifest with the reference's keys for the BFP8 tensors of `stack`
+    (06-模型与权重/qwen35_weights_64k_manifest.json)."""
+    table, total = layout(stack)
+    tensors = {}
+    for name, (off, t) in table.items():
+        tensors[name] = {
+            "dtype": "bfp8_soa", "shape": [t.M, t.K], "type": "block64_bfp8",
+            "mantissa_bytes": t.mant_bytes, "exponent_bytes": t.exp_bytes + ((-t.exp_bytes) % 8),
+            "file_offset": off, "byte_size": t.soa_bytes,
+        }
+    return {"model_name": model_name, "tensors": tensors, "total_binary_bytes": total,
+            "total_tensors": len(tensors)}
+
+
+def read_manifest(path: str) -> dict:
+    with open(path, encoding="utf-8") as f:
+        return json.load(f)
+
+
+def bfp8_tensors(manifest: dict) -> list[tuple[str, int, int, int]]:
+    """(name, file_offset, M, K) of every BFP8 tensor of a reference manifest,
+    sliced the way the engine does (qwen_real_engine.py:834-846)."""
+    out = []
+    for name, info in manifest["tensors"].items():
+        if info.get("dtype") == "bfp8_soa":
+            M, K = info["shape"]
+            out.append((name, info["file_offset"], M, K))
+    return out
+
+
+class DeviceStack:
+    """One or more copies of a synthetic BFP8 stack resident on a CUDA device.
+
+    Weights are fp32 N(0, std) drawn with a seeded torch generator on the
+    device and packed by ``ops.pack_bfp8``; copy 0 is packed, further copies
+    are byte-identical clones at distinct addresses (so a benchmark that
+    rotates through them defeats the 126 MB L2).  Activations are fp32
+    N(0, 1), one per GEMV, outputs one fp32 vector per GEMV.
+    """
+
+    def __init__(self, stack, copies=1, device="cuda", seed=0, std=0.02):
+        import torch
+
+        from . import ops
+
+        self.stack = list(stack)
+        self.table, self.nbytes = layout(self.stack)
+        self.device = torch.device(device)
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed)
+        base = torch.empty(self.nbytes, dtype=torch.uint8, device=self.device)
+        for name, (off, t) in self.table.items():
+            w = torch.randn((t.M, t.K), generator=g, device=self.device, dtype=torch.float32) * std
+            mant = base[off:off + t.mant_bytes].view(torch.int8).view(t.M, t.K)
+            exps = base[off + t.mant_bytes: off + t.mant_bytes + t.exp_bytes].view(t.M, t.K // 64)
+            ops.pack_bfp8(w, mant, exps)
+            del w
+        self.buffers = [base] + [base.clone() for _ in range(copies - 1)]
+        # activations and outputs live in two flat buffers (one copy each way
+        # moves a whole token); each GEMV's slice starts on a 16-byte boundary
+        xo, yo = [], []
+        nx = ny = 0
+        for t in self.stack:
+            xo.append(nx)
+            yo.append(ny)
+            nx += (t.K + 3) & ~3
+            ny += (t.M + 3) & ~3
+        gx = torch.Generator(device=self.device)
+        gx.manual_seed(seed + 1)
+        self.x_flat = torch.randn(nx, generator=gx, device=self.device, dtype=torch.float32)
+        self.y_flat = torch.zeros(ny, dtype=torch.float32, device=self.device)
+        self.x = [self.x_flat[o:o + t.K] for o, t in zip(xo, self.stack)]
+        self.y = [self.y_flat[o:o + t.M] for o, t in zip(yo, self.stack)]
+
+    def views(self, copy=0):
+        """[(x, mant, exps, y)] of one copy, in stack order."""
+        import torch
+
+        buf = self.buffers[copy]
+        out = []
+        for i, t in enumerate(self.stack):
+            off, _ = self.table[t.name]
+            mant = buf[off:off + t.mant_bytes].view(torch.int8).view(t.M, t.K)
+            exps = buf[off + t.mant_bytes: off + t.mant_bytes + t.exp_bytes].view(t.M, t.K // 64)
+            out.append((self.x[i], mant, exps, self.y[i]))
+        return out

@@ -1,0 +1,185 @@
+"""Device-tensor API of the hot path (PyTorch tensors in, PyTorch tensors out).
+
+Every function runs on torch's current CUDA stream and raises
+``KernelError`` on failure.  The arithmetic is the reference NEON build's,
+bit-for-bit (see include/qwen_b200.h).
+
+Reference routines served (ideal1128/qwen35-ax7020-edge-llm):
+  quant_block64   04-板载脚本与工具/qwen_kernels_opt.c:182-205 (quant_x_blocks)
+  bfp8_gemv       04-板载脚本与工具/qwen_kernels_opt.c:207-326
+  lm_head_bf16    04-板载脚本与工具/qwen_kernels_opt.c:401-506 (lm_head_argmax)
+                  04-板载脚本与工具/qwen_sampling.c:283-353    (lm_head_topk)
+  lm_head_bfp8    bfp8_gemv scores + the same selection rules (no reference routine)
+  pack_bfp8       05-主机侧源码/bfp8_packer.py:53-86
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from ._lib import KernelError, check, load
+
+__all__ = [
+    "KernelError", "quant_block64", "bfp8_gemv", "bfp8_gemv_q", "lm_head_bf16", "lm_head_bfp8",
+    "pack_bfp8", "LinearStack", "LmResult",
+]
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor) -> int:
+    return t.data_ptr()
+
+
+def _need(t: torch.Tensor, dtype: torch.dtype, name: str) -> torch.Tensor:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    return t.contiguous()
+
+
+def quant_block64(x: torch.Tensor):
+    """x fp32 [..., K] -> (xq int16 [..., K], xs fp32 [..., K/64])."""
+    x = _need(x, torch.float32, "x")
+    K = x.shape[-1]
+    B = x.numel() // K if K else 0
+    xq = torch.empty(x.shape, dtype=torch.int16, device=x.device)
+    xs = torch.empty((*x.shape[:-1], K // 64), dtype=torch.float32, device=x.device)
+    check(load().qwen_b200_quant_dev(_ptr(x), B, K, _ptr(xq), _ptr(xs), _stream()), "quant_block64")
+    return xq, xs
+
+
+def bfp8_gemv(x: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor, out: torch.Tensor | None = None):
+    """y = BFP8 GEMV.  x fp32 [K] or [B, K]; mant int8 [M, K]; exps uint8 [M, K/64]."""
+    x = _need(x, torch.float32, "x")
+    mant = _need(mant, torch.int8, "mant")
+    exps = _need(exps, torch.uint8, "exps")
+    M, K = mant.shape
+    if x.shape[-1] != K or exps.numel() < M * (K // 64):
+        raise ValueError("shape mismatch")
+    rows = x.reshape(-1, K)
+    y = out if out is not None else torch.empty((*x.shape[:-1], M), dtype=torch.float32, device=x.device)
+    yr = y.view(-1, M)
+    L = load()
+    for i in range(rows.shape[0]):
+        check(L.qwen_b200_gemv_dev(_ptr(yr[i]), _ptr(rows[i]), _ptr(mant), _ptr(exps), M, K, _stream()),
+              "bfp8_gemv")
+    return y
+
+
+def bfp8_gemv_q(xq: torch.Tensor, xs: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor):
+    """y = BFP8 GEMV of an already quantized activation (xq int16 [K], xs fp32 [K/64])."""
+    xq = _need(xq, torch.int16, "xq")
+    xs = _need(xs, torch.float32, "xs")
+    mant = _need(mant, torch.int8, "mant")
+    exps = _need(exps, torch.uint8, "exps")
+    M, K = mant.shape
+    y = torch.empty(M, dtype=torch.float32, device=mant.device)
+    check(load().qwen_b200_gemv_q_dev(_ptr(y), _ptr(xq), _ptr(xs), _ptr(mant), _ptr(exps), M, K, _stream()),
+          "bfp8_gemv_q")
+    return y
+
+
+@dataclass
+class LmResult:
+    argmax: torch.Tensor      # int32 [1] (device)
+    ids: torch.Tensor         # int32 [k] (device), first n valid
+    scores: torch.Tensor      # fp32 [k] (device), first n valid
+    n: torch.Tensor           # int32 [1] (device)
+
+    def host(self):
+        """(argmax id, ids list, scores list) on the host."""
+        n = int(self.n.item())
+        return int(self.argmax.item()), self.ids[:n].cpu().tolist(), self.scores[:n].cpu().tolist()
+
+
+def _lm_outputs(device, k: int) -> LmResult:
+    kk = max(k, 1)
+    return LmResult(torch.zeros(1, dtype=torch.int32, device=device),
+                    torch.zeros(kk, dtype=torch.int32, device=device),
+                    torch.zeros(kk, dtype=torch.float32, device=device),
+                    torch.zeros(1, dtype=torch.int32, device=device))
+
+
+def lm_head_bf16(h: torch.Tensor, E: torch.Tensor, k: int = 0) -> LmResult:
+    """Tied-embedding lm_head over E bf16 bits [vocab, hidden] (uint16 or bfloat16)."""
+    h = _need(h, torch.float32, "h")
+    if E.dtype == torch.bfloat16:
+        E = E.view(torch.int16)
+    if E.dtype not in (torch.int16, torch.uint16):
+        raise TypeError("E must hold bf16 bit patterns (bfloat16/int16/uint16)")
+    E = E.contiguous()
+    V, H = E.shape
+    r = _lm_outputs(h.device, min(k, V))
+    check(load().qwen_b200_lm_head_bf16_dev(_ptr(h), _ptr(E), V, H, k, _ptr(r.argmax), _ptr(r.ids),
+                                            _ptr(r.scores), _ptr(r.n), _stream()), "lm_head_bf16")
+    return r
+
+
+def lm_head_bfp8(h: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor, k: int = 40) -> LmResult:
+    """BFP8 lm_head [vocab, hidden] with fused argmax and top-k."""
+    h = _need(h, torch.float32, "h")
+    mant = _need(mant, torch.int8, "mant")
+    exps = _need(exps, torch.uint8, "exps")
+    V, H = mant.shape
+    r = _lm_outputs(h.device, min(k, V))
+    check(load().qwen_b200_lm_head_bfp8_dev(_ptr(h), _ptr(mant), _ptr(exps), V, H, k, _ptr(r.argmax),
+                                            _ptr(r.ids), _ptr(r.scores), _ptr(r.n), _stream()),
+          "lm_head_bfp8")
+    return r
+
+
+def pack_bfp8(w: torch.Tensor, out_mant: torch.Tensor | None = None, out_exps: torch.Tensor | None = None):
+    """Pack fp32 [M, K] weights into (mant int8 [M, K], exps uint8 [M, K/64]) on the device."""
+    w = _need(w, torch.float32, "w")
+    M, K = w.shape
+    mant = out_mant if out_mant is not None else torch.empty((M, K), dtype=torch.int8, device=w.device)
+    exps = out_exps if out_exps is not None else torch.empty((M, K // 64), dtype=torch.uint8, device=w.device)
+    rc = load().qwen_b200_pack_bfp8_dev(_ptr(w), M, K, _ptr(mant), _ptr(exps), _stream())
+    check(rc, "pack_bfp8")
+    return mant, exps
+
+
+class LinearStack:
+    """A reusable grouped launch of independent BFP8 GEMVs (one kernel).
+
+    ``items`` is a list of (x fp32 [K], mant int8 [M, K], exps uint8 [M, K/64],
+    y fp32 [M]) device tensors; the tensors must stay alive and in place while
+    the stack is used.  ``run()`` enqueues every GEMV on the current stream and
+    is safe inside CUDA graph capture.
+    """
+
+    def __init__(self, items):
+        n = len(items)
+        P = ctypes.c_void_p * n
+        I = ctypes.c_int * n
+        self._keep = items
+        mant = P(*[_ptr(m) for (_, m, _, _) in items])
+        exps = P(*[_ptr(e) for (_, _, e, _) in items])
+        xs = P(*[_ptr(x) for (x, _, _, _) in items])
+        ys = P(*[_ptr(y) for (_, _, _, y) in items])
+        Ms = I(*[m.shape[0] for (_, m, _, _) in items])
+        Ks = I(*[m.shape[1] for (_, m, _, _) in items])
+        h = load().qwen_b200_stack_create(n, mant, exps, xs, ys, Ms, Ks)
+        if h <= 0:
+            check(h, "LinearStack")
+        self.handle = h
+
+    def run(self, stream: int | None = None) -> None:
+        check(load().qwen_b200_stack_run(self.handle, _stream() if stream is None else stream), "LinearStack.run")
+
+    def close(self) -> None:
+        if getattr(self, "handle", 0) > 0:
+            load().qwen_b200_stack_destroy(self.handle)
+            self.handle = 0
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,111 @@
+"""The reference drop-in entry points (host pointers, ctypes, as the engine
+calls them) on a GPU: bfp8_gemv, lm_head_argmax, lm_head_topk."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def bits(a):
+    a = np.ascontiguousarray(a, np.float32)
+    return np.where(np.isnan(a), np.uint32(0x7FC00000), a.view(np.uint32))
+
+
+@pytest.fixture(scope="module")
+def lib(cuda):
+    from qwen_b200 import _lib
+
+    L = _lib.load()
+    L.init_kernels()
+    return L
+
+
+def fake_weight_file(rng, shapes):
+    """A weight 'file' in host memory with 64-byte aligned SoA tensors, like
+    qwen35_weights_64k.bin, and the (offset, M, K) the engine slices out."""
+    from qwen_b200 import model
+
+    stack = [model.Linear(f"t{i}", M, K) for i, (M, K) in enumerate(shapes)]
+    table, total = model.layout(stack)
+    buf = np.zeros(total + 64, np.uint8)
+    base = (-buf.ctypes.data) % 64
+    buf = buf[base:base + total]
+    ents = []
+    for t in stack:
+        off, _ = table[t.name]
+        mant, exps = O.pack_bfp8(rng.normal(0, 0.02, (t.M, t.K)).astype(np.float32))
+        blob = np.frombuffer(O.soa_bytes(mant, exps), np.uint8)
+        buf[off:off + blob.size] = blob
+        ents.append((off, t.M, t.K, mant, exps))
+    return buf, ents
+
+
+def test_bfp8_gemv_dropin_engine_style(lib):
+    """Pointers into one mapped weight buffer, sliced the way
+    qwen_real_engine._gemv_ent does (mant at the offset, exps right after)."""
+    rng = np.random.default_rng(11)
+    buf, ents = fake_weight_file(rng, [(3584, 1024), (1024, 3584), (6144, 1024), (33, 512)])
+    assert lib.qwen_b200_register_weights(buf.ctypes.data, buf.nbytes) == 0
+    try:
+        for off, M, K, mant, exps in ents:
+            x = rng.normal(0, 1, K).astype(np.float32)
+            y = np.zeros(M, np.float32)
+            lib.bfp8_gemv(y.ctypes.data, x.ctypes.data, buf.ctypes.data + off, buf.ctypes.data + off + M * K, M, K)
+            assert np.array_equal(bits(y), bits(O.bfp8_gemv(x, mant, exps)))
+    finally:
+        lib.qwen_b200_forget_weights(buf.ctypes.data)
+
+
+def test_bfp8_gemv_dropin_unregistered_pointers(lib):
+    """Separate mantissa / exponent arrays never registered: uploaded on
+    first use, and the same x pointer with new contents is requantized (the
+    reference's pointer cache, qwen_kernels_opt.c:183, would not)."""
+    rng = np.random.default_rng(12)
+    M, K = 515, 2048
+    mant, exps = O.pack_bfp8(rng.normal(0, 0.02, (M, K)).astype(np.float32))
+    x = rng.normal(0, 1, K).astype(np.float32)
+    for _ in range(2):
+        y = np.zeros(M, np.float32)
+        lib.bfp8_gemv(y.ctypes.data, x.ctypes.data, mant.ctypes.data, exps.ctypes.data, M, K)
+        assert np.array_equal(bits(y), bits(O.bfp8_gemv(x, mant, exps)))
+        x[:] = rng.normal(0, 1, K)
+    lib.qwen_b200_forget_weights(mant.ctypes.data)
+    lib.qwen_b200_forget_weights(exps.ctypes.data)
+
+
+def test_lm_head_dropins_selftest_data(lib, golden):
+    g = O.XorShift32(0x13579BDF)
+    cases = {"c1": g.selftest_fill(1000, 64), "c2": g.selftest_fill(500, 67)}
+    for tag, (tab, h) in cases.items():
+        V, H = tab.shape
+        am = lib.lm_head_argmax(h.ctypes.data, tab.ctypes.data, V, H)
+        assert am == O.lm_head_argmax(h, tab)
+        for k in (1, 7, 20, V + 50):
+            kk = min(k, V)
+            ids = np.zeros(kk, np.int32)
+            sc = np.zeros(kk, np.float32)
+            n = lib.lm_head_topk(h.ctypes.data, tab.ctypes.data, V, H, k, ids.ctypes.data, sc.ctypes.data)
+            rids, rsc = O.lm_head_topk(h, tab, k)
+            assert n == len(rids)
+            assert np.array_equal(ids[:n], rids)
+            assert np.array_equal(bits(sc[:n]), bits(rsc))
+        lib.qwen_b200_forget_weights(tab.ctypes.data)
+    assert lib.lm_head_topk(None, None, 0, 0, 0, None, None) == 0
+
+
+def test_profiler_counts_dropin_calls(lib):
+    lib.qwen_prof_enable(1)
+    lib.qwen_prof_reset()
+    rng = np.random.default_rng(1)
+    mant, exps = O.pack_bfp8(rng.normal(0, 0.02, (64, 512)).astype(np.float32))
+    x = rng.normal(0, 1, 512).astype(np.float32)
+    y = np.zeros(64, np.float32)
+    lib.bfp8_gemv(y.ctypes.data, x.ctypes.data, mant.ctypes.data, exps.ctypes.data, 64, 512)
+    assert lib.qwen_prof_get(0) > 0.0
+    lib.qwen_prof_enable(0)
+    lib.qwen_b200_forget_weights(mant.ctypes.data)
+    lib.qwen_b200_forget_weights(exps.ctypes.data)

@@ -1,0 +1,204 @@
+"""GPU parity of the quantizer and the exact BFP8 GEMV against the CPU oracle.
+
+Bit-exact: int16 activations, block scales and every fp32 output (compared
+as bit patterns), over the model's shapes, odd row counts, odd block counts,
+extreme exponents and the grouped 150-GEMV stack.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def bits(a):
+    """fp32 bit patterns; every NaN maps to one pattern (each platform has
+    its own default NaN, so payloads are not compared)."""
+    a = np.ascontiguousarray(a, np.float32)
+    return np.where(np.isnan(a), np.uint32(0x7FC00000), a.view(np.uint32))
+
+
+def rand_weights(rng, M, K, std=0.02, exp_range=None):
+    w = rng.normal(0, std, (M, K)).astype(np.float32)
+    mant, exps = O.pack_bfp8(w)
+    if exp_range is not None:
+        exps = rng.integers(exp_range[0], exp_range[1] + 1, exps.shape).astype(np.uint8)
+        mant = rng.integers(-128, 128, mant.shape).astype(np.int8)
+    return mant, exps
+
+
+def to_dev(*arrs):
+    import torch
+
+    return [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in arrs]
+
+
+# ------------------------------------------------------------------ quantizer
+def test_quant_block64_bit_exact(cuda):
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(0)
+    for K in (64, 1024, 3584, 64 * 37):
+        x = rng.normal(0, 1, (3, K)).astype(np.float32)
+        x[0, :64] = 0.0                           # zero block
+        x[1, 64:128] = 1e-22                      # below the 1e-20 floor
+        if K >= 256:
+            x[2, 128:192] = rng.normal(0, 1e4, 64)   # large block
+            x[2, 192:256] = np.arange(64, dtype=np.float32) * 0.5 - 16   # rounding ties
+        xq, xs = ops.quant_block64(*to_dev(x))
+        for r in range(3):
+            q_ref, s_ref = O.quant_x(x[r])
+            assert np.array_equal(xq[r].cpu().numpy(), q_ref), (K, r)
+            assert np.array_equal(bits(xs[r].cpu().numpy()), bits(s_ref)), (K, r)
+
+
+# ------------------------------------------------------------------ single GEMV
+SHAPES = [(3584, 1024), (1024, 3584), (6144, 1024), (2048, 1024), (1024, 2048), (4096, 1024), (512, 1024),
+          (1, 1024), (2, 512), (3, 512), (31, 1024), (33, 2048), (3583, 1024), (129, 4096), (64, 8192)]
+
+
+@pytest.mark.parametrize("M,K", SHAPES)
+def test_gemv_exact_model_shapes(cuda, M, K):
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(M * 7919 + K)
+    mant, exps = rand_weights(rng, M, K)
+    x = rng.normal(0, 1, K).astype(np.float32)
+    y = ops.bfp8_gemv(*to_dev(x, mant, exps)).cpu().numpy()
+    assert np.array_equal(bits(y), bits(O.bfp8_gemv(x, mant, exps)))
+
+
+@pytest.mark.parametrize("M,K", [(5, 64), (17, 192), (40, 64 * 23), (7, 64 * 9)])
+def test_gemv_exact_generic_shapes(cuda, M, K):
+    """K not a multiple of 512 runs the generic kernel; same bits."""
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(K + M)
+    mant, exps = rand_weights(rng, M, K)
+    x = rng.normal(0, 1, K).astype(np.float32)
+    y = ops.bfp8_gemv(*to_dev(x, mant, exps)).cpu().numpy()
+    assert np.array_equal(bits(y), bits(O.bfp8_gemv(x, mant, exps)))
+
+
+@pytest.mark.parametrize("lo,hi", [(0, 12), (0, 255), (100, 140), (200, 255)])
+def test_gemv_exact_extreme_exponents(cuda, lo, hi):
+    """Subnormal block scales (e < 8, flushed on the vector path, kept on the
+    odd row's scalar path), huge scales (inf), random mantissas incl. -128."""
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(lo * 256 + hi)
+    for M, K in ((33, 1024), (64, 512)):
+        mant, exps = rand_weights(rng, M, K, exp_range=(lo, hi))
+        x = rng.normal(0, 1, K).astype(np.float32) * np.float32(10.0) ** rng.integers(-30, 30, K)
+        y = ops.bfp8_gemv(*to_dev(x.astype(np.float32), mant, exps)).cpu().numpy()
+        ref = O.bfp8_gemv(x.astype(np.float32), mant, exps)
+        assert np.array_equal(bits(y), bits(ref)), (M, K)
+
+
+def test_gemv_q_known_answer_constant_pattern(cuda):
+    """01-系统概述/FINAL_REPORT.md:222-226: all-0x01 weights, all-0x1111 x ->
+    every block sum 279616.  With unit block scales (e = 134, xs = 1) and one
+    block per row the GEMV returns that sum exactly."""
+    from qwen_b200 import ops
+
+    M, K = 3584, 1024
+    mant = np.ones((M, K), np.int8)
+    exps = np.full((M, K // 64), 134, np.uint8)
+    xq = np.full(K, 0x1111, np.int16)
+    xs = np.ones(K // 64, np.float32)
+    y = ops.bfp8_gemv_q(*to_dev(xq, xs, mant, exps)).cpu().numpy()
+    assert (y == 279616.0 * (K // 64)).all()
+    y1 = ops.bfp8_gemv_q(*to_dev(xq[:64], xs[:1], mant[:, :64].copy(), exps[:, :1].copy())).cpu().numpy()
+    assert (y1 == 279616.0).all()
+
+
+def test_gemv_q_tb_vectors(cuda, golden):
+    """tb_gemv_core.v stimulus (LCG cases :401-419) through the quantized-input
+    path: bit-exact against the oracle, and within the testbench tolerance
+    of its double-precision model where the row does not saturate."""
+    from qwen_b200 import ops
+
+    g = golden("tb_gemv.npz")
+    for i, (K, M, sd, dq, elo, ehi, xo, au, sat) in enumerate(g["cases"]):
+        xq, xs, w, e = g[f"{i}_xq"], g[f"{i}_xs"], g[f"{i}_w"], g[f"{i}_e"]
+        y = ops.bfp8_gemv_q(*to_dev(xq, xs, w, e)).cpu().numpy()
+        assert np.array_equal(bits(y), bits(O.bfp8_gemv_q(xq, xs, w, e))), i
+
+
+# ------------------------------------------------------------------ grouped stack
+def test_linear_stack_full_token_bit_exact(cuda):
+    """The 150 GEMVs of one Qwen3.5-0.8B token in one grouped launch."""
+    import torch
+
+    from qwen_b200 import model, ops
+
+    st = model.DeviceStack(model.qwen35_08b_stack(), copies=1, seed=5)
+    items = st.views(0)
+    stack = ops.LinearStack(items)
+    stack.run()
+    torch.cuda.synchronize()
+    for (x, mant, exps, y), t in zip(items, st.stack):
+        ref = O.bfp8_gemv(x.cpu().numpy(), mant.cpu().numpy(), exps.cpu().numpy())
+        assert np.array_equal(bits(y.cpu().numpy()), bits(ref)), t.name
+    stack.close()
+
+
+def test_linear_stack_in_cuda_graph(cuda):
+    import torch
+
+    from qwen_b200 import model, ops
+
+    shapes = [model.Linear(f"t{i}", M, K) for i, (M, K) in enumerate([(3584, 1024), (1024, 3584), (512, 1024),
+                                                                       (6144, 1024), (33, 2048)])]
+    st = model.DeviceStack(shapes, copies=1, seed=9)
+    items = st.views(0)
+    stack = ops.LinearStack(items)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        stack.run()       # warm up (attribute setup) outside capture
+    torch.cuda.synchronize()
+    for _, _, _, y in items:
+        y.zero_()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        stack.run()
+    for rep in range(2):
+        for x, _, _, y in items:
+            x.normal_()
+            y.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        for x, mant, exps, y in items:
+            ref = O.bfp8_gemv(x.cpu().numpy(), mant.cpu().numpy(), exps.cpu().numpy())
+            assert np.array_equal(bits(y.cpu().numpy()), bits(ref))
+    stack.close()
+
+
+def test_scaled_layer_shape(cuda):
+    """One gate and one down projection of the multi-GPU configuration
+    (28672 x 8192 and 8192 x 28672), bit-exact."""
+    import torch
+
+    from qwen_b200 import model, ops
+
+    st = model.DeviceStack(model.scaled_stack(layers=1)[1:], copies=1, seed=3)
+    for x, mant, exps, y in st.views(0):
+        ops.bfp8_gemv(x, mant, exps, out=y)
+        torch.cuda.synchronize()
+        ref = O.bfp8_gemv(x.cpu().numpy(), mant.cpu().numpy(), exps.cpu().numpy())
+        assert np.array_equal(bits(y.cpu().numpy()), bits(ref))
+
+
+def test_device_packer_matches_reference_rule(cuda, golden):
+    """On-device packer == reference packer on the committed fixtures (those
+    matrices have no block peak within an ulp above a power of two)."""
+    from qwen_b200 import ops
+
+    g = golden("packer.npz")
+    for name in ("normal", "edges", "wide"):
+        w = g[f"{name}_w"]
+        mant, exps = ops.pack_bfp8(*to_dev(w))
+        assert np.array_equal(mant.cpu().numpy(), g[f"{name}_mant"]), name
+        e = g[f"{name}_exps_padded"][: exps.numel()]
+        assert np.array_equal(exps.cpu().numpy().reshape(-1), e), name

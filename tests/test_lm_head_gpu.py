@@ -1,0 +1,97 @@
+"""GPU parity of the fused lm_head kernels (bf16 tied embedding, BFP8)
+against the oracle: greedy id exact, top-k ids exact and scores bit-exact,
+on the reference self-test data (qwen_sampling.c:917-1010) and edge cases."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def bits(a):
+    a = np.ascontiguousarray(a, np.float32)
+    return np.where(np.isnan(a), np.uint32(0x7FC00000), a.view(np.uint32))
+
+
+def dev(a):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def check_bf16(tab, h, k):
+    from qwen_b200 import ops
+
+    r = ops.lm_head_bf16(dev(h), dev(tab.view(np.int16)), k)
+    am, ids, sc = r.host()
+    s = O.lm_scores(h, tab, with_tail=True)
+    assert am == O.argmax(O.lm_scores(h, tab, with_tail=False))
+    if k > 0:
+        rids, rsc = O.topk(s, k)
+        assert ids == rids.tolist()
+        assert np.array_equal(bits(np.array(sc, np.float32)), bits(rsc))
+    return am, ids
+
+
+@pytest.fixture(scope="module")
+def selftest_tables():
+    g = O.XorShift32(0x13579BDF)
+    return {"c1": g.selftest_fill(1000, 64), "c2": g.selftest_fill(500, 67), "c3": g.selftest_fill(65536, 1024)}
+
+
+@pytest.mark.parametrize("k", [0, 1, 5, 20, 100, 1000, 1050])
+def test_bf16_selftest_case1(cuda, selftest_tables, k):
+    tab, h = selftest_tables["c1"]
+    check_bf16(tab, h, k)
+
+
+@pytest.mark.parametrize("k", [0, 1, 20, 40, 64])
+def test_bf16_selftest_realistic_shape(cuda, selftest_tables, golden, k):
+    tab, h = selftest_tables["c3"]
+    am, ids = check_bf16(tab, h, k)
+    g = golden("ref_lm.npz")
+    # the reference ranks its scalar-order scores; ours the NEON order -- the
+    # greedy token agrees on this data
+    assert am == int(g["c3_argmax"])
+
+
+def test_bf16_ties_nans_and_floor(cuda):
+    rng = np.random.default_rng(3)
+    V, H = 4096, 256
+    tab = (rng.normal(0, 1, (V, H)).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    tab[100] = tab[7]          # exact ties: lower id first
+    tab[3000] = tab[7]
+    tab[5] = 0x7FC0            # NaN row: never selected
+    tab[6] = 0xFF80            # -inf products
+    h = rng.normal(0, 1, H).astype(np.float32)
+    for k in (0, 1, 3, 64, 1024):
+        check_bf16(tab, h, k)
+    # every score below -1e30 -> greedy id 0; top-k still ranks them
+    big = np.full((64, 8), 0xFF7F, np.uint16)      # -3.39e38
+    hh = np.ones(8, np.float32) * 1e-6
+    check_bf16(big, hh, 5)
+
+
+def test_bf16_repeated_calls_reuse_scratch(cuda, selftest_tables):
+    tab, h = selftest_tables["c1"]
+    first = check_bf16(tab, h, 20)
+    for _ in range(3):
+        assert check_bf16(tab, h, 20) == first
+
+
+@pytest.mark.parametrize("V,H,k", [(65536, 1024, 40), (65536, 1024, 0), (4099, 512, 64), (1000, 1024, 1000)])
+def test_bfp8_lm_head(cuda, V, H, k):
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(V + H + k)
+    w = rng.normal(0, 0.02, (V, H)).astype(np.float32)
+    mant, exps = O.pack_bfp8(w)
+    h = rng.normal(0, 1, H).astype(np.float32)
+    r = ops.lm_head_bfp8(dev(h), dev(mant), dev(exps), k)
+    am, ids, sc = r.host()
+    ram, rids, rsc = O.bfp8_lm_head(h, mant, exps, k)
+    assert am == ram
+    if k > 0:
+        assert ids == rids.tolist()
+        assert np.array_equal(bits(np.array(sc, np.float32)), bits(rsc))

@@ -1,0 +1,195 @@
+"""Pin the CPU oracle to the reference's own outputs and known answers.
+
+Fixtures in tests/golden/ were produced by the reference's code (packer run
+as Python, C kernels compiled from source, testbench recipe) -- see
+tests/golden/make_golden.py.  These tests need no GPU.
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF_DIR = os.path.join(REPO, "oracle", "_ref")
+
+
+# ------------------------------------------------------------------ packer
+@pytest.mark.parametrize("name", ["normal", "edges", "wide"])
+def test_packer_matches_reference_packer(golden, name):
+    g = golden("packer.npz")
+    w = g[f"{name}_w"]
+    mant, exps = O.pack_bfp8(w)
+    assert np.array_equal(mant, g[f"{name}_mant"])
+    assert O.soa_bytes(mant, exps)[mant.size:] == g[f"{name}_exps_padded"].tobytes()
+
+
+def test_packer_selftest_snr():
+    """05-主机侧源码/bfp8_packer.py:89-107: SNR > 30 dB with an outlier."""
+    rng = np.random.default_rng(42)
+    v = rng.normal(0, 1, 64).astype(np.float32)
+    v[17] = 25.0
+    m, e = O.pack_bfp8(v[None, :])
+    rec = O.dequant(m, e)[0]
+    snr = 10 * np.log10(np.sum(v ** 2) / np.sum((v - rec) ** 2))
+    assert snr > 30.0
+
+
+def test_packer_soa_sizes():
+    m, e = O.pack_bfp8(np.random.default_rng(1).normal(0, 1, (128, 64)).astype(np.float32))
+    b = O.soa_bytes(m, e)
+    assert len(b) - m.size == 128 and (len(b) - m.size) % 8 == 0
+
+
+# ------------------------------------------------------------------ quantizer
+def test_quant_rule_by_hand():
+    x = np.zeros(128, np.float32)
+    x[:64] = np.linspace(-3, 5, 64, dtype=np.float32)
+    x[64:] = 1e-21                      # amax <= 1e-20 -> zero block
+    xq, xs = O.quant_x(x)
+    amax = np.float32(5.0)
+    q = np.float32(16384.0) / amax
+    assert xs[0] == amax / np.float32(16384.0)
+    assert np.array_equal(xq[:64], np.rint(x[:64] * q).astype(np.int16))
+    assert xs[1] == 0 and not xq[64:].any()
+    assert xq[63] == 16384
+
+
+def test_exp_scale_table():
+    s = O.exp_scale()
+    for e in (0, 7, 8, 127, 134, 255):
+        assert s[e] == np.ldexp(np.float32(1), e - 134)
+
+
+# ------------------------------------------------------------------ known answers
+def test_constant_pattern_block_sum():
+    """01-系统概述/FINAL_REPORT.md:222-226: all-0x01 weights x all-0x1111 x ->
+    every block sum 279616, on the 3584 x 1024 shape (57,344 blocks)."""
+    mant = np.ones((3584, 1024), np.int8)
+    xq = np.full(1024, 0x1111, np.int16)
+    d = O.block_dots(mant, xq)
+    assert d.size == 57344 and (d == 279616).all()
+    lanes = O.lane_dots(mant[:2], xq)
+    assert (lanes.sum(axis=2) == 279616).all() and (lanes == 69904).all()
+
+
+def test_tb_gemv_core_block_dots(golden):
+    """tb_gemv_core.v legacy cases (:401-402): raw int32 block dots bit-exact."""
+    g = golden("tb_gemv.npz")
+    for i, case in enumerate(g["cases"]):
+        d = O.block_dots(g[f"{i}_w"], g[f"{i}_xq"])
+        assert np.array_equal(d.astype(np.int64), g[f"{i}_dots"]), i
+
+
+def test_tb_gemv_core_rtl20_tolerance(golden):
+    """tb_gemv_core.v dequant cases (:404-419): the gemv_core word / 2^20 lies
+    within 2e-6 + 3e-4|y| of the double model; huge exponents sit on a rail
+    with the saturation flag set; tiny exponents flush to ~0."""
+    g = golden("tb_gemv.npz")
+    for i, (K, M, sd, dq, elo, ehi, xo, au, sat) in enumerate(g["cases"]):
+        if not dq:
+            continue
+        words, flags = O.bfp8_gemv_rtl20(g[f"{i}_xq"], g[f"{i}_xs"], g[f"{i}_w"], g[f"{i}_e"])
+        yref = g[f"{i}_yref"]
+        if sat:
+            assert all(w in (2**31 - 1, -2**31) for w in words), i
+            assert flags & 2
+        else:
+            err = np.abs(words / 2.0**20 - yref)
+            assert (err <= 2e-6 + 3e-4 * np.abs(yref)).all(), (i, err.max())
+            assert flags == 0
+
+
+def test_neon_order_close_to_double_model(golden):
+    """The NEON-order float result tracks the exact double sum of its terms."""
+    g = golden("tb_gemv.npz")
+    for i, (K, M, sd, dq, elo, ehi, xo, au, sat) in enumerate(g["cases"]):
+        if not dq or sat:
+            continue
+        y = O.bfp8_gemv_q(g[f"{i}_xq"], g[f"{i}_xs"], g[f"{i}_w"], g[f"{i}_e"])
+        yref = g[f"{i}_yref"]
+        d = g[f"{i}_dots"].astype(np.float64)
+        scale = (np.abs(d) * np.ldexp(1.0, g[f"{i}_e"].astype(np.int64) - 134) *
+                 g[f"{i}_xs"].astype(np.float64)).sum(axis=1)
+        assert (np.abs(y - yref) <= 1e-6 * scale + 1e-30).all(), i
+
+
+# ------------------------------------------------------------------ compiled reference
+def _ref():
+    k = os.path.join(REF_DIR, "libref_kernels.so")
+    s = os.path.join(REF_DIR, "libref_sampling.so")
+    if not (os.path.exists(k) and os.path.exists(s)):
+        pytest.skip("reference C not compiled (make -C oracle ref)")
+    return ctypes.CDLL(k), ctypes.CDLL(s)
+
+
+def test_scalar_gemv_matches_fixture(golden):
+    """Oracle's scalar form == reference bfp8_gemv compiled for x86 (its
+    scalar fallback, qwen_kernels_opt.c:311-325), bit for bit."""
+    g = golden("ref_gemv.npz")
+    for t in "abc":
+        y = O.bfp8_gemv_scalar(g[f"{t}_x"], g[f"{t}_mant"], g[f"{t}_exps"])
+        assert np.array_equal(y.view(np.uint32), g[f"{t}_y"].view(np.uint32)), t
+
+
+def test_neon_gemv_close_to_scalar_reference(golden):
+    """The int16 path differs from the float fallback only by activation
+    quantization (relative ~1e-4 of the row's magnitude)."""
+    g = golden("ref_gemv.npz")
+    for t in "abc":
+        y = O.bfp8_gemv(g[f"{t}_x"], g[f"{t}_mant"], g[f"{t}_exps"])
+        ref = g[f"{t}_y"]
+        w = O.dequant(g[f"{t}_mant"], g[f"{t}_exps"])
+        mag = np.abs(w) @ np.abs(g[f"{t}_x"])
+        assert (np.abs(y - ref) <= 2e-4 * mag).all(), t
+
+
+def _selftest_tables():
+    g = O.XorShift32(0x13579BDF)
+    return {"c1": g.selftest_fill(1000, 64), "c2": g.selftest_fill(500, 67), "c3": g.selftest_fill(65536, 1024)}
+
+
+@pytest.fixture(scope="module")
+def selftest_tables():
+    return _selftest_tables()
+
+
+def test_lm_selection_matches_reference_scalar_build(golden, selftest_tables):
+    """With the scalar score order the oracle's argmax / top-k reproduce the
+    compiled reference exactly (ids and scores), for every k of the
+    reference self-test including k > vocab."""
+    g = golden("ref_lm.npz")
+    for tag, (tab, h) in selftest_tables.items():
+        s = O.lm_scores_scalar(h, tab)
+        assert O.argmax(s) == int(g[f"{tag}_argmax"])
+        for key in g.files:
+            if key.startswith(tag + "_k") and key.endswith("_ids"):
+                k = int(key[len(tag) + 2:-4])
+                ids, sc = O.topk(s, k)
+                assert np.array_equal(ids, g[key]), key
+                assert np.array_equal(sc.view(np.uint32), g[key.replace("_ids", "_scores")].view(np.uint32))
+
+
+def test_lm_neon_order_agrees_with_reference_ranking(golden, selftest_tables):
+    """NEON-order scores (what the board and the GPU compute) against the
+    reference self-test criterion: same ranking up to swaps of scores closer
+    than the 1e-3 tolerance of check_topk_against_brute (qwen_sampling.c:585-631)."""
+    g = golden("ref_lm.npz")
+    for tag, (tab, h) in selftest_tables.items():
+        s = O.lm_scores(h, tab, with_tail=True)
+        ids, sc = O.topk(s, 64)
+        ref_ids = g[f"{tag}_k{1 if tag != 'c2' else 7}_ids"]
+        assert ids[0] == ref_ids[0] or abs(sc[0] - s[ref_ids[0]]) < 1e-3
+        sref = O.lm_scores_scalar(h, tab)
+        assert np.abs(s - sref).max() < 1e-3
+
+
+def test_oracle_topk_rules():
+    s = np.array([1.0, 3.0, 3.0, np.nan, -np.inf, 2.0, -3.4028235e38, 3.0], np.float32)
+    ids, sc = O.topk(s, 10)
+    assert ids.tolist() == [1, 2, 7, 5, 0]
+    assert O.argmax(s) == 1
+    assert O.argmax(np.full(5, -1e31, np.float32)) == 0
+    assert O.topk(s, 0)[0].size == 0
