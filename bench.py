@@ -33,7 +33,6 @@ import os
 import statistics
 import subprocess
 import sys
-import tempfile
 import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
@@ -54,6 +53,9 @@ def parse():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=["stack", "gemv", "lm_bf16", "lm_bfp8"], default="stack")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--copies", type=int, default=0,
+                    help="weight copies to rotate (default: enough for > 4 GB; fewer only for profiling)")
     ap.add_argument("--cpu-sample", action="store_true", help=argparse.SUPPRESS)
     return ap.parse_args()
 
@@ -90,53 +92,68 @@ def stack_shapes(workload):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle samples of one GPU during the timed region."""
+    """SM clock and throttle reasons of one GPU, polled through NVML from a
+    thread every ~2 ms while the timed region runs (read-only queries)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4}
 
-    def __init__(self, gpu_id):
-        self.path = tempfile.mktemp(suffix=".csv")
-        self.proc = None
+    def __init__(self, uuid, index):
+        import threading
+
+        self.samples, self.maxclk, self.err = [], None, None
+        self._stop = threading.Event()
         try:
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-i", str(gpu_id), "-lms", "200"], stdout=self.f,
-                                         stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = None
+            want = (uuid or "").lower().replace("gpu-", "")
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                hi = pynvml.nvmlDeviceGetHandleByIndex(i)
+                u = pynvml.nvmlDeviceGetUUID(hi)
+                u = (u.decode() if isinstance(u, bytes) else u).lower().replace("gpu-", "")
+                if want and u == want:
+                    h = hi
+            if h is None:
+                h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.maxclk = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self._nv, self._h = pynvml, h
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        except Exception as e:   # sampling must never break the benchmark
+            self.err = str(e)[:120]
+            self._t = None
+
+    def _run(self):
+        nv, h = self._nv, self._h
+        while not self._stop.is_set():
+            try:
+                clk = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((clk, rs))
+            except Exception:
+                pass
+            self._stop.wait(0.002)
 
     def stop(self):
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        self.f.close()
-        rows = []
-        for line in open(self.path):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
-        os.unlink(self.path)
-        if not rows:
-            return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        if self._t is None:
+            return {"error": self.err}
+        self._stop.set()
+        self._t.join(timeout=2)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.maxclk, "reasons": [], "samples": 0}
+        clks = [c for c, _ in self.samples]
+        reasons = sorted({n for _, r in self.samples for n, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(clks), "sm_max_mhz": self.maxclk, "reasons": reasons,
+                "samples": len(self.samples), "source": "nvml"}
 
 
-def gpu_identifier(torch, dev):
+def gpu_uuid(torch, dev):
     try:
-        return "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+        return str(torch.cuda.get_device_properties(dev).uuid)
     except Exception:
-        return dev.index or 0
+        return None
 
 
 def timed(torch, fn, steps, warmup, barrier):
@@ -186,7 +203,7 @@ def run_b200(args):
         shapes, desc = stack_shapes(args.workload)
         nb = model.stack_bytes(shapes)
         wbytes = nb["weights"]
-        copies = max(2, math.ceil(L2_DEFEAT_BYTES / wbytes))
+        copies = args.copies or max(2, math.ceil(L2_DEFEAT_BYTES / wbytes))
         ds = model.DeviceStack(shapes, copies=copies, device=dev, seed=1234 + rank)
         plans = [ops.LinearStack(ds.views(c)) for c in range(copies)]
         launches_per_step = 1
@@ -195,7 +212,7 @@ def run_b200(args):
             plans[i % copies].run()
 
         # ------------------------------------------------ device-resident timing
-        clk = ClockSampler(gpu_identifier(torch, dev))
+        clk = ClockSampler(gpu_uuid(torch, dev), dev.index or 0)
         secs = timed(torch, step, args.steps, args.warmup, barrier)
         clocks = clk.stop()
         t = torch.tensor([secs], device=dev)
@@ -207,24 +224,9 @@ def run_b200(args):
         kernel_gbs = nb["total"] / per_step / 1e9
 
         # ------------------------------------------------ end to end, host buffers
-        hx = torch.empty(ds.x_flat.numel(), dtype=torch.float32, pin_memory=True)
-        hx.copy_(ds.x_flat.cpu())
-        hy = torch.empty(ds.y_flat.numel(), dtype=torch.float32, pin_memory=True)
-
-        def e2e_step(i):
-            ds.x_flat.copy_(hx, non_blocking=True)
-            plans[i % copies].run()
-            hy.copy_(ds.y_flat, non_blocking=True)
-
-        esecs = timed(torch, e2e_step, args.steps, args.warmup, barrier)
-        te = torch.tensor([esecs], device=dev)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        esecs = float(te.item())
-        e2e = {"value": round(world * nb["total"] / (esecs / args.steps) / 1e9, 2), "unit": "GB/s",
-               "ms_per_step": round(esecs / args.steps * 1e3, 4),
-               "h2d_bytes_per_step": hx.numel() * 4, "d2h_bytes_per_step": hy.numel() * 4}
-
+        e2e = None
+        if not args.no_e2e:
+            e2e = end_to_end(torch, dist, ds, plans, copies, nb, args, barrier, world, dev)
         line.update({
             "value": round(value, 2), "ms_per_step": round(per_step * 1e3, 4),
             "config": {"workload": desc, "gemvs_per_step": len(shapes), "weight_bytes": wbytes,
@@ -250,6 +252,29 @@ def run_b200(args):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def end_to_end(torch, dist, ds, plans, copies, nb, args, barrier, world, dev):
+    """The same token through the public API with host buffers: the step's
+    activations copied in from pinned host memory, the stack run, its
+    outputs copied back, all on the timed stream."""
+    hx = torch.empty(ds.x_flat.numel(), dtype=torch.float32, pin_memory=True)
+    hx.copy_(ds.x_flat.cpu())
+    hy = torch.empty(ds.y_flat.numel(), dtype=torch.float32, pin_memory=True)
+
+    def e2e_step(i):
+        ds.x_flat.copy_(hx, non_blocking=True)
+        plans[i % copies].run()
+        hy.copy_(ds.y_flat, non_blocking=True)
+
+    esecs = timed(torch, e2e_step, args.steps, args.warmup, barrier)
+    te = torch.tensor([esecs], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    esecs = float(te.item())
+    return {"value": round(world * nb["total"] / (esecs / args.steps) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(esecs / args.steps * 1e3, 4),
+            "h2d_bytes_per_step": hx.numel() * 4, "d2h_bytes_per_step": hy.numel() * 4}
 
 
 def run_lm_head(args, torch, ops, dev, barrier, world, hbm_peak, peak_kind):

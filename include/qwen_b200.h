@@ -159,6 +159,11 @@ QB_API int qwen_b200_lm_head_bfp8_dev(const float* h, const int8_t* mant, const 
  * from the float's bits. */
 QB_API int qwen_b200_pack_bfp8_dev(const float* w, int M, int K, int8_t* mant, uint8_t* exps, void* stream);
 
+/* Error bits the kernels of the current device recorded (bounded waits that
+ * timed out: 1); 0 if none.  clear != 0 resets them.  No reference
+ * counterpart. */
+QB_API int qwen_b200_device_error(int clear);
+
 /* Description of the calling thread's last failure ("" if none). */
 QB_API const char* qwen_b200_last_error(void);
 

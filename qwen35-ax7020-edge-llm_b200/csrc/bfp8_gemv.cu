@@ -27,6 +27,7 @@
 // bank-conflict free.
 #include "bfp8_gemv.cuh"
 #include "common.cuh"
+#include "tma.cuh"
 #include "topk.cuh"
 
 #include <algorithm>
@@ -34,14 +35,15 @@
 namespace qb {
 
 constexpr int kThreads = 256;
-constexpr int kSliceBytes = 16384;
+constexpr int kStageMant = 16384;   // mantissa bytes per stage (TMA boxes)
+constexpr int kStages = 5;          // ring depth; two CTAs fit one SM for K <= 4096
 
 template <int RG>
 struct Geo {
     static constexpr int SB = 256 / RG;          // 64-byte blocks per slice row
     static constexpr int RS = 64 * SB;           // bytes per slice row
-    static constexpr int EXB = RG * SB;          // exponent bytes per stage
-    static constexpr int STAGE = kSliceBytes + EXB;
+    static constexpr int BOXES = RS / 128;       // TMA boxes (RG rows x 128 B) per slice
+    static constexpr int EXB = RG * SB;          // exponent bytes per stage (256)
 };
 
 struct GemvArgs {
@@ -51,6 +53,7 @@ struct GemvArgs {
     int total_units;
     long long total_cost;
     int kmax;
+    unsigned int* err;
     // lm_head epilogue
     LmScratch* sc;
     int kk;
@@ -60,19 +63,18 @@ struct GemvArgs {
     int* out_n;
 };
 
-__device__ __forceinline__ GemvDesc load_desc(const GemvArgs& A, int d) {
+__device__ __forceinline__ const GemvDesc& desc_ref(const GemvArgs& A, int d) {
     return A.list ? A.list[d] : A.single;
 }
 
 template <int RG>
 struct Cursor {
     int d, u, s, ns, M, K, nb, ub, ue;
-    const int8_t* mant;
     const uint8_t* exps;
     bool valid;
 
     __device__ void set_desc(const GemvArgs& A, int dd) {
-        GemvDesc D = load_desc(A, dd);
+        const GemvDesc& D = desc_ref(A, dd);
         d = dd;
         M = D.M;
         K = D.K;
@@ -80,7 +82,6 @@ struct Cursor {
         ns = (nb + Geo<RG>::SB - 1) / Geo<RG>::SB;
         ub = D.unit_begin;
         ue = D.unit_begin + (M + RG - 1) / RG;
-        mant = D.mant;
         exps = D.exps;
     }
     __device__ void advance(const GemvArgs& A, int u_end) {
@@ -104,10 +105,10 @@ __device__ int unit_at_cost(const GemvArgs& A, long long pos, int* d_out) {
     int lo = 0, hi = A.n - 1;
     while (lo < hi) {  // largest d with cost_begin <= pos
         int mid = (lo + hi + 1) >> 1;
-        if (load_desc(A, mid).cost_begin <= pos) lo = mid;
+        if (desc_ref(A, mid).cost_begin <= pos) lo = mid;
         else hi = mid - 1;
     }
-    GemvDesc D = load_desc(A, lo);
+    const GemvDesc& D = desc_ref(A, lo);
     int ns = ((D.K >> 6) + Geo<RG>::SB - 1) / Geo<RG>::SB;
     int units = (D.M + RG - 1) / RG;
     long long off = pos - D.cost_begin;
@@ -161,47 +162,38 @@ __device__ void stage_activation(const GemvDesc& D, uint32_t* xp, float* xss) {
     }
 }
 
+// Start one slice: thread 0 arms the stage barrier and issues the TMA boxes
+// of the mantissa tile; warp 1 copies the slice's exponent bytes (8-byte
+// pieces, cp.async, one commit group per slice issued by every thread).
 template <int RG>
-__device__ __forceinline__ void issue_slice(const Cursor<RG>& c, unsigned char* st) {
+__device__ __forceinline__ void issue_slice(const GemvArgs& A, const Cursor<RG>& c, unsigned char* mant_st,
+                                            unsigned char* exps_st, uint64_t* bar) {
     using G = Geo<RG>;
     const int r0 = (c.u - c.ub) * RG;
-    const int rv = min(RG, c.M - r0);
     const int b0 = c.s * G::SB;
-    const int vb = min(G::SB, c.nb - b0);
-    const int8_t* src = c.mant + (size_t)r0 * c.K + b0 * 64;
-    const uint8_t* esrc = c.exps + (size_t)r0 * c.nb + b0;
-    if (vb == G::SB) {
-        constexpr int CPR = G::SB * 4;
-#pragma unroll 4
-        for (int idx = threadIdx.x; idx < rv * CPR; idx += kThreads) {
-            int r = idx / CPR, q = idx % CPR;
-            cp_async16(st + (q >> 3) * (RG * 128) + r * 128 + (((q & 7) ^ (r & 7)) << 4),
-                       src + (size_t)r * c.K + q * 16);
-        }
-        constexpr int PPR = G::SB / 8;
-        for (int idx = threadIdx.x; idx < rv * PPR; idx += kThreads) {
-            int r = idx / PPR, p = idx % PPR;
-            cp_async8(st + kSliceBytes + r * G::SB + p * 8, esrc + (size_t)r * c.nb + p * 8);
-        }
-    } else {
-        const int cpr = vb * 4;
-        for (int idx = threadIdx.x; idx < rv * cpr; idx += kThreads) {
-            int r = idx / cpr, q = idx - r * cpr;
-            cp_async16(st + (q >> 3) * (RG * 128) + r * 128 + (((q & 7) ^ (r & 7)) << 4),
-                       src + (size_t)r * c.K + q * 16);
-        }
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(bar, kStageMant);
+        const void* tm = &desc_ref(A, c.d).tmap;
+#pragma unroll
+        for (int j = 0; j < G::BOXES; j++) tma_load_2d(mant_st + j * (RG * 128), tm, b0 * 64 + j * 128, r0, bar);
+    } else if ((threadIdx.x >> 5) == 1) {
+        const int lane = threadIdx.x & 31;
+        const int rv = min(RG, c.M - r0);
+        const int vb = min(G::SB, c.nb - b0);
         const int ppr = vb >> 3;
-        for (int idx = threadIdx.x; idx < rv * ppr; idx += kThreads) {
+        const uint8_t* esrc = c.exps + (size_t)r0 * c.nb + b0;
+        for (int idx = lane; idx < rv * ppr; idx += 32) {
             int r = idx / ppr, p = idx - r * ppr;
-            cp_async8(st + kSliceBytes + r * G::SB + p * 8, esrc + (size_t)r * c.nb + p * 8);
+            cp_async8(exps_st + r * G::SB + p * 8, esrc + (size_t)r * c.nb + p * 8);
         }
     }
 }
 
 // Block terms of one slice: thread (row r = lane % RG, block bs) -> tb[bs][r][0..3].
 template <int RG>
-__device__ __forceinline__ void compute_slice(const Cursor<RG>& c, const unsigned char* st,
-                                              float* tb, const uint32_t* xp, const float* xss) {
+__device__ __forceinline__ void compute_slice(const Cursor<RG>& c, const unsigned char* mant_st,
+                                              const unsigned char* exps_st, float* tb, const uint32_t* xp,
+                                              const float* xss) {
     using G = Geo<RG>;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r = lane % RG;
@@ -210,27 +202,29 @@ __device__ __forceinline__ void compute_slice(const Cursor<RG>& c, const unsigne
     const int vb = min(G::SB, c.nb - b0);
     if (bs >= vb) return;
     const int b = b0 + bs;
-    const unsigned char* rowp = st + (bs >> 1) * (RG * 128) + r * 128;
+    const unsigned char* rowp = mant_st + (bs >> 1) * (RG * 128) + r * 128;
     const int sw = r & 7;
     const int cbase = (bs & 1) * 4;
     const uint4* xb = reinterpret_cast<const uint4*>(xp) + b * 8;
-    int L0 = 0, L1 = 0, L2 = 0, L3 = 0;
+    // two accumulators per lane class: dependent dp2a chains of 4, not 8
+    int A0 = 0, A1 = 0, A2 = 0, A3 = 0, B0 = 0, B1 = 0, B2 = 0, B3 = 0;
 #pragma unroll
     for (int cc = 0; cc < 4; cc++) {
         uint4 w = *reinterpret_cast<const uint4*>(rowp + (((cbase + cc) ^ sw) << 4));
         uint4 xa = xb[2 * cc], xc = xb[2 * cc + 1];
         int p01 = (int)__byte_perm(w.x, w.y, 0x5140), p23 = (int)__byte_perm(w.x, w.y, 0x7362);
-        L0 = __dp2a_lo((int)xa.x, p01, L0);
-        L1 = __dp2a_hi((int)xa.y, p01, L1);
-        L2 = __dp2a_lo((int)xa.z, p23, L2);
-        L3 = __dp2a_hi((int)xa.w, p23, L3);
+        A0 = __dp2a_lo((int)xa.x, p01, A0);
+        A1 = __dp2a_hi((int)xa.y, p01, A1);
+        A2 = __dp2a_lo((int)xa.z, p23, A2);
+        A3 = __dp2a_hi((int)xa.w, p23, A3);
         int q01 = (int)__byte_perm(w.z, w.w, 0x5140), q23 = (int)__byte_perm(w.z, w.w, 0x7362);
-        L0 = __dp2a_lo((int)xc.x, q01, L0);
-        L1 = __dp2a_hi((int)xc.y, q01, L1);
-        L2 = __dp2a_lo((int)xc.z, q23, L2);
-        L3 = __dp2a_hi((int)xc.w, q23, L3);
+        B0 = __dp2a_lo((int)xc.x, q01, B0);
+        B1 = __dp2a_hi((int)xc.y, q01, B1);
+        B2 = __dp2a_lo((int)xc.z, q23, B2);
+        B3 = __dp2a_hi((int)xc.w, q23, B3);
     }
-    const uint32_t e = st[kSliceBytes + r * G::SB + bs];
+    const int L0 = A0 + B0, L1 = A1 + B1, L2 = A2 + B2, L3 = A3 + B3;
+    const uint32_t e = exps_st[r * G::SB + bs];
     const float xsb = xss[b];
     const int grow = (c.u - c.ub) * RG + r;
     float4 T;
@@ -271,19 +265,30 @@ struct LmState {
     int* cand_count;
 };
 
-// Sequential float chain of one slice (threads < 4*RG: row = t/4, class = t%4).
+// Sequential float chain of one slice, run by the 4*RG threads of the LAST
+// warps of the CTA (warps 0 and 1 also issue the TMA and exponent copies):
+// chain thread c = row*4 + class.  The slice's terms are loaded first (they
+// do not depend on the chain), then added in block order.
 template <int RG, bool LM>
 __device__ __forceinline__ void chain_slice(const GemvArgs& A, const SliceInfo& s, const float* tb,
                                             float& f, LmState& lm) {
-    const int ct = threadIdx.x;
-    if (ct >= 4 * RG) return;
+    constexpr int SB = Geo<RG>::SB;
+    const int ct = threadIdx.x - (kThreads - 4 * RG);
+    if (ct < 0) return;
     const int r = ct >> 2, j = ct & 3;
     const int grow = s.row0 + r;
     const bool odd = (s.M & 1) && grow == s.M - 1;
+    float t[SB];
+#pragma unroll
+    for (int bs = 0; bs < SB; bs++) t[bs] = (bs < s.vb) ? tb[bs * RG * 4 + ct] : 0.0f;
     if (odd) {
-        for (int bs = 0; bs < s.vb; bs++) f = add_rn(f, tb[bs * RG * 4 + ct]);
+#pragma unroll
+        for (int bs = 0; bs < SB; bs++)
+            if (bs < s.vb) f = add_rn(f, t[bs]);
     } else {
-        for (int bs = 0; bs < s.vb; bs++) f = add_ftz(f, tb[bs * RG * 4 + ct]);
+#pragma unroll
+        for (int bs = 0; bs < SB; bs++)
+            if (bs < s.vb) f = add_ftz(f, t[bs]);
     }
     if (s.last) {
         float a = add_ftz(f, __shfl_xor_sync(0xffffffffu, f, 2));
@@ -300,23 +305,44 @@ __device__ __forceinline__ void chain_slice(const GemvArgs& A, const SliceInfo& 
                     lm.cand[p] = cand_key(yv, grow);
                 }
             } else {
-                load_desc(A, s.d).y[grow] = yv;
+                desc_ref(A, s.d).y[grow] = yv;
             }
         }
         f = 0.0f;
     }
 }
 
-template <int RG, int P, bool LM>
-__global__ void __launch_bounds__(kThreads, 1) gemv_exact_kernel(const __grid_constant__ GemvArgs A) {
+struct SmemLayout {
+    size_t exps, bars, terms, xp, xss, cand, total;
+};
+__host__ __device__ inline SmemLayout smem_layout(int kmax, bool lm) {
+    SmemLayout L;
+    L.exps = (size_t)kStages * kStageMant;
+    L.bars = L.exps + (size_t)kStages * 256;
+    L.terms = (L.bars + kStages * 8 + 15) & ~size_t(15);
+    L.xp = L.terms + 2 * 1024 * sizeof(float);
+    L.xss = L.xp + 2 * (size_t)kmax;
+    L.cand = (L.xss + 4 * (size_t)(kmax / 64) + 15) & ~size_t(15);
+    L.total = L.cand + (lm ? (size_t)kCandCap * 8 : 0);
+    return L;
+}
+
+template <int RG, bool LM>
+__global__ void __launch_bounds__(kThreads, 2) gemv_exact_kernel(const __grid_constant__ GemvArgs A) {
     using G = Geo<RG>;
-    extern __shared__ __align__(128) unsigned char smem[];
-    unsigned char* stages = smem;
-    float* terms = reinterpret_cast<float*>(smem + P * G::STAGE);
-    uint32_t* xp = reinterpret_cast<uint32_t*>(terms + 2 * 1024);
-    float* xss = reinterpret_cast<float*>(xp + A.kmax / 2);
-    unsigned long long* cand = reinterpret_cast<unsigned long long*>(
-        (reinterpret_cast<uintptr_t>(xss + A.kmax / 64) + 15) & ~uintptr_t(15));
+    constexpr int P = kStages;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // TMA 128-byte swizzle needs 1024-byte aligned destinations
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                           ~uintptr_t(1023));
+    const SmemLayout Ly = smem_layout(A.kmax, LM);
+    unsigned char* mant_st = smem;
+    unsigned char* exps_st = smem + Ly.exps;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Ly.bars);
+    float* terms = reinterpret_cast<float*>(smem + Ly.terms);
+    uint32_t* xp = reinterpret_cast<uint32_t*>(smem + Ly.xp);
+    float* xss = reinterpret_cast<float*>(smem + Ly.xss);
+    unsigned long long* cand = reinterpret_cast<unsigned long long*>(smem + Ly.cand);
     __shared__ int s_cand_count;
     __shared__ unsigned long long s_red[kThreads / 32];
 
@@ -324,7 +350,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_exact_kernel(const __grid_co
     lm.best = 0ull;
     lm.cand = cand;
     lm.cand_count = &s_cand_count;
-    if (LM && threadIdx.x == 0) s_cand_count = 0;
+    if (threadIdx.x == 0) {
+        s_cand_count = 0;
+        for (int s = 0; s < P; s++) mbar_init(&bars[s], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
 
     const long long T = A.total_cost;
     int d0, d1;
@@ -335,13 +366,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_exact_kernel(const __grid_co
     ic.valid = u_begin < u_end;
     ic.u = u_begin;
     ic.s = 0;
-    if (ic.valid) ic.set_desc(A, d0);
+    if (ic.valid) {
+        ic.set_desc(A, d0);
+        if (threadIdx.x == 0) tma_prefetch_desc(&desc_ref(A, d0).tmap);
+    }
     Cursor<RG> cc = ic;
 
 #pragma unroll 1
     for (int p = 0; p < P - 1; p++) {
         if (ic.valid) {
-            issue_slice<RG>(ic, stages + p * G::STAGE);
+            issue_slice<RG>(A, ic, mant_st + p * kStageMant, exps_st + p * G::EXB, &bars[p]);
             ic.advance(A, u_end);
         }
         cp_async_commit();
@@ -354,21 +388,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_exact_kernel(const __grid_co
     int i = 0;
 #pragma unroll 1
     for (; cc.valid; i++) {
+        const int st = i % P;
+        mbar_wait(&bars[st], (uint32_t)(i / P) & 1u, A.err);
         cp_async_wait<P - 2>();
         __syncthreads();
         if (ic.valid) {
-            issue_slice<RG>(ic, stages + ((i + P - 1) % P) * G::STAGE);
+            const int ns = (i + P - 1) % P;
+            issue_slice<RG>(A, ic, mant_st + ns * kStageMant, exps_st + ns * G::EXB, &bars[ns]);
             ic.advance(A, u_end);
         }
         cp_async_commit();
         if (cc.d != loaded_d) {
-            stage_activation(load_desc(A, cc.d), xp, xss);
+            stage_activation(desc_ref(A, cc.d), xp, xss);
             __syncthreads();
             loaded_d = cc.d;
         }
         if (LM && s_cand_count > kCandCap - 2 * RG) cand_compact(cand, &s_cand_count, A.kk);
         if (have_prev) chain_slice<RG, LM>(A, prev, terms + ((i - 1) & 1) * 1024, f, lm);
-        compute_slice<RG>(cc, stages + (i % P) * G::STAGE, terms + (i & 1) * 1024, xp, xss);
+        compute_slice<RG>(cc, mant_st + st * kStageMant, exps_st + st * G::EXB, terms + (i & 1) * 1024, xp, xss);
         prev = slice_info<RG>(cc);
         have_prev = true;
         cc.advance(A, u_end);
@@ -378,8 +415,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_exact_kernel(const __grid_co
     if (have_prev) chain_slice<RG, LM>(A, prev, terms + ((i - 1) & 1) * 1024, f, lm);
     if (LM) {
         __syncthreads();
-        unsigned long long* work = reinterpret_cast<unsigned long long*>(stages);
-        const int work_cap = (P * G::STAGE) / 8;
+        unsigned long long* work = reinterpret_cast<unsigned long long*>(mant_st);
+        const int work_cap = (P * kStageMant) / 8;
         lm_finish(A.sc, cand, &s_cand_count, work, work_cap, lm.best, A.kk, A.out_id, A.out_ids,
                   A.out_scores, A.out_n, s_red);
     }
@@ -481,15 +518,6 @@ int num_sms() {
     return n;
 }
 
-template <int RG>
-static size_t exact_smem_bytes(int P, int kmax, bool lm) {
-    size_t b = (size_t)P * Geo<RG>::STAGE + 2 * 1024 * sizeof(float) + 2 * (size_t)kmax +
-               4 * (size_t)(kmax / 64);
-    b = (b + 15) & ~size_t(15);
-    if (lm) b += (size_t)kCandCap * 8;
-    return b;
-}
-
 static bool fast_shape_ok(const GemvDesc& d) {
     if (d.M <= 0 || d.K <= 0 || d.K % 512) return false;
     if (reinterpret_cast<uintptr_t>(d.mant) % 16 || reinterpret_cast<uintptr_t>(d.exps) % 8) return false;
@@ -504,6 +532,7 @@ bool gemv_plan(GemvDesc* descs, int n, int rows_per_unit, GemvPlan* plan) {
     for (int i = 0; i < n; i++) {
         GemvDesc& d = descs[i];
         if (!fast_shape_ok(d)) return false;
+        if (!encode_tmap_2d(&d.tmap, d.mant, 1, (uint64_t)d.M, (uint64_t)d.K, (uint32_t)rows_per_unit)) return false;
         d.unit_begin = units;
         d.cost_begin = cost;
         const int u = (d.M + rows_per_unit - 1) / rows_per_unit;
@@ -520,42 +549,50 @@ bool gemv_plan(GemvDesc* descs, int n, int rows_per_unit, GemvPlan* plan) {
     return true;
 }
 
-template <int RG, int P, bool LM>
-static cudaError_t launch_exact(const GemvArgs& A, int grid, cudaStream_t stream) {
-    const size_t smem = exact_smem_bytes<RG>(P, A.kmax, LM);
-    auto kern = gemv_exact_kernel<RG, P, LM>;
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (err != cudaSuccess) return err;
+template <int RG, bool LM>
+static cudaError_t launch_exact(const GemvArgs& A, int max_grid, cudaStream_t stream) {
+    const size_t smem = smem_layout(A.kmax, LM).total + 1024;
+    auto kern = gemv_exact_kernel<RG, LM>;
+    static size_t configured = 0;   // largest dynamic smem size set so far
+    if (smem > configured) {
+        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (err != cudaSuccess) return err;
+        configured = smem;
+    }
+    int occ = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem) != cudaSuccess || occ < 1)
+        occ = 1;
+    const int grid = std::max(1, std::min(max_grid, num_sms() * occ));
     kern<<<grid, kThreads, smem, stream>>>(A);
     return cudaGetLastError();
 }
 
 static int pick_rows_per_unit(int M) {
-    // favour enough units to cover every SM; 32-row units read the most
+    // enough units to give every CTA slot work; 32-row units read the most
     // bytes per shared-memory access
-    const int sms = num_sms();
-    if ((M + 31) / 32 >= sms) return 32;
-    if ((M + 15) / 16 >= sms) return 16;
+    const int slots = num_sms() * 2;
+    if ((M + 31) / 32 >= slots) return 32;
+    if ((M + 15) / 16 >= slots) return 16;
     return 8;
 }
 
-static cudaError_t dispatch_exact(GemvArgs& A, int rg, bool lm, int grid, cudaStream_t stream) {
-    constexpr int P = 6;
+static cudaError_t dispatch_exact(GemvArgs& A, int rg, bool lm, int max_grid, cudaStream_t stream) {
     if (lm) {
         switch (rg) {
-            case 32: return launch_exact<32, P, true>(A, grid, stream);
-            case 16: return launch_exact<16, P, true>(A, grid, stream);
-            default: return launch_exact<8, P, true>(A, grid, stream);
+            case 32: return launch_exact<32, true>(A, max_grid, stream);
+            case 16: return launch_exact<16, true>(A, max_grid, stream);
+            default: return launch_exact<8, true>(A, max_grid, stream);
         }
     }
     switch (rg) {
-        case 32: return launch_exact<32, P, false>(A, grid, stream);
-        case 16: return launch_exact<16, P, false>(A, grid, stream);
-        default: return launch_exact<8, P, false>(A, grid, stream);
+        case 32: return launch_exact<32, false>(A, max_grid, stream);
+        case 16: return launch_exact<16, false>(A, max_grid, stream);
+        default: return launch_exact<8, false>(A, max_grid, stream);
     }
 }
 
-cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, cudaStream_t stream) {
+cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, unsigned int* err,
+                             cudaStream_t stream) {
     if (plan.n <= 0 || plan.total_units <= 0) return cudaSuccess;
     GemvArgs A{};
     A.list = dev_descs;
@@ -563,26 +600,25 @@ cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, cu
     A.total_units = plan.total_units;
     A.total_cost = plan.total_cost;
     A.kmax = plan.kmax;
-    const int grid = std::min(num_sms(), plan.total_units);
-    return dispatch_exact(A, plan.rows_per_unit, false, grid, stream);
+    A.err = err;
+    return dispatch_exact(A, plan.rows_per_unit, false, plan.total_units, stream);
 }
 
-cudaError_t launch_gemv(const GemvDesc& d0, cudaStream_t stream) {
+cudaError_t launch_gemv(const GemvDesc& d0, unsigned int* err, cudaStream_t stream) {
     if (d0.M <= 0) return cudaSuccess;
     if (d0.K <= 0 || d0.K % 64) return cudaErrorInvalidValue;
     GemvDesc d = d0;
-    if (!fast_shape_ok(d)) {
+    const int rg = pick_rows_per_unit(d.M);
+    GemvPlan plan;
+    if (!fast_shape_ok(d) || !gemv_plan(&d, 1, rg, &plan)) {
         const size_t smem = (((size_t)2 * d.K + 15) & ~size_t(15)) + 4 * (size_t)(d.K / 64);
         if (smem > 200 * 1024) return cudaErrorInvalidValue;
-        cudaError_t err = cudaFuncSetAttribute(gemv_generic_kernel,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (err != cudaSuccess) return err;
+        cudaError_t e = cudaFuncSetAttribute(gemv_generic_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
         gemv_generic_kernel<<<(d.M + kThreads - 1) / kThreads, kThreads, smem, stream>>>(d);
         return cudaGetLastError();
     }
-    const int rg = pick_rows_per_unit(d.M);
-    GemvPlan plan;
-    gemv_plan(&d, 1, rg, &plan);
     GemvArgs A{};
     A.single = d;
     A.list = nullptr;
@@ -590,38 +626,37 @@ cudaError_t launch_gemv(const GemvDesc& d0, cudaStream_t stream) {
     A.total_units = plan.total_units;
     A.total_cost = plan.total_cost;
     A.kmax = plan.kmax;
-    const int grid = std::min(num_sms(), plan.total_units);
-    return dispatch_exact(A, rg, false, grid, stream);
+    A.err = err;
+    return dispatch_exact(A, rg, false, plan.total_units, stream);
 }
 
 cudaError_t launch_bfp8_lm_head(const float* h, const int8_t* mant, const uint8_t* exps, int vocab,
-                                int hidden, int k, LmScratch* scratch, int* out_id, int* out_ids,
-                                float* out_scores, int* out_n, cudaStream_t stream) {
+                                int hidden, int k, LmScratch* scratch, unsigned int* err, int* out_id,
+                                int* out_ids, float* out_scores, int* out_n, cudaStream_t stream) {
     GemvDesc d{};
     d.mant = mant;
     d.exps = exps;
     d.x = h;
     d.M = vocab;
     d.K = hidden;
-    if (vocab <= 0 || hidden <= 0 || k < 0 || k > kTopkMax) return cudaErrorInvalidValue;
-    if (!fast_shape_ok(d)) return cudaErrorInvalidValue;
+    if (vocab <= 0 || hidden <= 0 || k < 0 || std::min(k, vocab) > kTopkMax) return cudaErrorInvalidValue;
     const int rg = pick_rows_per_unit(vocab);
     GemvPlan plan;
-    gemv_plan(&d, 1, rg, &plan);
+    if (!fast_shape_ok(d) || !gemv_plan(&d, 1, rg, &plan)) return cudaErrorInvalidValue;
     GemvArgs A{};
     A.single = d;
     A.n = 1;
     A.total_units = plan.total_units;
     A.total_cost = plan.total_cost;
     A.kmax = plan.kmax;
+    A.err = err;
     A.sc = scratch;
     A.kk = std::min(k, vocab);
     A.out_id = out_id;
     A.out_ids = out_ids;
     A.out_scores = out_scores;
     A.out_n = out_n;
-    const int grid = std::min(std::min(num_sms(), plan.total_units), kMaxGrid);
-    return dispatch_exact(A, rg, true, grid, stream);
+    return dispatch_exact(A, rg, true, std::min(plan.total_units, kMaxGrid), stream);
 }
 
 cudaError_t launch_quant_block64(const float* x, int B, int K, int16_t* xq, float* xs,

@@ -1,6 +1,7 @@
 // bfp8_gemv.cuh -- host-visible declarations of the BFP8 GEMV launchers.
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace qb {
@@ -10,7 +11,8 @@ namespace qb {
 // (05-主机侧源码/bfp8_packer.py:53-86).  The activation is either fp32 `x`
 // (quantized inside the kernel by the reference block-64 rule) or, when
 // x == nullptr, an already quantized int16 `xq` [K] with scales `xs` [K/64].
-struct GemvDesc {
+struct alignas(64) GemvDesc {
+    CUtensorMap tmap;     // planner output: 2D map of `mant` (rows x K bytes, 128-byte boxes)
     const int8_t* mant;
     const uint8_t* exps;
     const float* x;
@@ -35,23 +37,26 @@ struct GemvPlan {
     long long total_cost;
 };
 
-// Fill unit_begin / cost_begin of `descs` (host array) for a grouped launch.
-// Descriptors with M == 0 must not be passed.  Returns false if a shape is
-// not supported by the grouped kernel (K % 512 != 0 or misaligned pointers).
+// Fill tmap / unit_begin / cost_begin of `descs` (host array) for a grouped
+// launch.  Descriptors with M == 0 must not be passed.  Returns false if a
+// shape is not served by the grouped kernel (K % 512 != 0, misaligned
+// pointers) or a tensor map cannot be encoded.
 bool gemv_plan(GemvDesc* descs, int n, int rows_per_unit, GemvPlan* plan);
 
 // Grouped exact GEMV over a planned, device-resident descriptor array.
-cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, cudaStream_t stream);
+// `err` (device word, may be null) collects kernel error bits.
+cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, unsigned int* err,
+                             cudaStream_t stream);
 
 // One exact GEMV (any M >= 1, K a positive multiple of 64, any alignment).
-cudaError_t launch_gemv(const GemvDesc& d, cudaStream_t stream);
+cudaError_t launch_gemv(const GemvDesc& d, unsigned int* err, cudaStream_t stream);
 
 // BFP8 lm_head: scores = bfp8_gemv(h), fused argmax (ties -> lowest id, best
 // must beat -1e30) and top-k (k <= 1024; score desc, ties ascending id).
 // Results land in device memory: out_id[0], out_ids/out_scores[0..n), *out_n.
 cudaError_t launch_bfp8_lm_head(const float* h, const int8_t* mant, const uint8_t* exps, int vocab,
-                                int hidden, int k, LmScratch* scratch, int* out_id, int* out_ids,
-                                float* out_scores, int* out_n, cudaStream_t stream);
+                                int hidden, int k, LmScratch* scratch, unsigned int* err, int* out_id,
+                                int* out_ids, float* out_scores, int* out_n, cudaStream_t stream);
 
 // Standalone block-64 quantizer: x [B][K] -> xq [B][K] (natural order), xs [B][K/64].
 cudaError_t launch_quant_block64(const float* x, int B, int K, int16_t* xq, float* xs,

@@ -185,6 +185,37 @@ struct Cand {
     float score;
 };
 
+// Per-device state of the _dev entry points: lm_head scratch and the
+// device error word the kernels report bounded-wait timeouts into.
+struct DevState {
+    qb::LmScratch* scratch = nullptr;
+    unsigned int* err = nullptr;
+};
+
+int dev_state(DevState** out) {
+    static std::mutex mu;
+    static std::vector<DevState> per_dev;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(QB_ECUDA, "cudaGetDevice", e);
+    std::lock_guard<std::mutex> lk(mu);
+    if ((int)per_dev.size() <= dev) per_dev.resize(dev + 1);
+    DevState& st = per_dev[dev];
+    if (!st.scratch) {
+        qb::LmScratch* p = nullptr;
+        if ((e = cudaMalloc(&p, sizeof(qb::LmScratch))) != cudaSuccess) return fail(QB_ENOMEM, "scratch alloc", e);
+        if ((e = cudaMemset(p, 0, sizeof(qb::LmScratch))) != cudaSuccess) return fail(QB_ECUDA, "scratch clear", e);
+        unsigned int* w = nullptr;
+        if ((e = cudaMalloc(&w, sizeof(unsigned int))) != cudaSuccess) return fail(QB_ENOMEM, "error word alloc", e);
+        if ((e = cudaMemset(w, 0, sizeof(unsigned int))) != cudaSuccess) return fail(QB_ECUDA, "error word clear", e);
+        st.scratch = p;
+        st.err = w;
+    }
+    *out = &st;
+    return QB_OK;
+}
+
+
 }  // namespace
 
 extern "C" {
@@ -266,7 +297,9 @@ void bfp8_gemv(float* y, const float* x, const int8_t* mant, const uint8_t* exps
     d.y = static_cast<float*>(g_ctx.d_out);
     d.M = M;
     d.K = K;
-    cudaError_t e = qb::launch_gemv(d, s);
+    DevState* dst = nullptr;
+    if (dev_state(&dst)) return;
+    cudaError_t e = qb::launch_gemv(d, dst->err, s);
     if (e != cudaSuccess) {
         fail(QB_ECUDA, "bfp8_gemv launch", e);
         return;
@@ -305,8 +338,10 @@ static int lm_bf16_host(const float* h, const uint16_t* E, int vocab, int hidden
     cudaMemcpyAsync(g_ctx.d_in, g_ctx.h_in, in_b, cudaMemcpyHostToDevice, s);
     int* d_ids = static_cast<int*>(g_ctx.d_out);
     float* d_sc = reinterpret_cast<float*>(d_ids + kk);
+    DevState* dst = nullptr;
+    if (int rc2 = dev_state(&dst)) return rc2;
     cudaError_t e = qb::launch_lm_head_bf16(static_cast<const float*>(g_ctx.d_in), static_cast<const uint16_t*>(dE),
-                                            vocab, hidden, (int)kk, with_tail, g_ctx.scratch, score_buf,
+                                            vocab, hidden, (int)kk, with_tail, g_ctx.scratch, dst->err, score_buf,
                                             g_ctx.d_res, d_ids, d_sc, g_ctx.d_res + 1, s);
     if (e != cudaSuccess) return fail(QB_ECUDA, "lm_head launch", e);
     int res[2] = {0, 0};
@@ -431,7 +466,9 @@ int qwen_b200_gemv_dev(float* y, const float* x, const int8_t* mant, const uint8
     d.y = y;
     d.M = M;
     d.K = K;
-    cudaError_t e = qb::launch_gemv(d, static_cast<cudaStream_t>(stream));
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    cudaError_t e = qb::launch_gemv(d, st->err, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_gemv_dev", e);
 }
 
@@ -447,7 +484,9 @@ int qwen_b200_gemv_q_dev(float* y, const int16_t* xq, const float* xs, const int
     d.y = y;
     d.M = M;
     d.K = K;
-    cudaError_t e = qb::launch_gemv(d, static_cast<cudaStream_t>(stream));
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    cudaError_t e = qb::launch_gemv(d, st->err, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_gemv_q_dev", e);
 }
 
@@ -490,7 +529,9 @@ int qwen_b200_stack_create(int n, const int8_t* const* mant, const uint8_t* cons
 int qwen_b200_stack_run(int plan, void* stream) {
     if (plan < 1 || plan > (int)g_plans.size() || !g_plans[plan - 1].live) return fail(QB_EINVAL, "stack: bad handle");
     const StackPlan& sp = g_plans[plan - 1];
-    cudaError_t e = qb::launch_gemv_list(sp.dev_descs, sp.plan, static_cast<cudaStream_t>(stream));
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    cudaError_t e = qb::launch_gemv_list(sp.dev_descs, sp.plan, st->err, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_stack_run", e);
 }
 
@@ -503,23 +544,14 @@ int qwen_b200_stack_destroy(int plan) {
     return QB_OK;
 }
 
-static int scratch_for_current_device(qb::LmScratch** out) {
-    // one zeroed scratch per device, created on first use
-    static std::mutex mu;
-    static std::vector<qb::LmScratch*> per_dev;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return fail(QB_ECUDA, "cudaGetDevice", e);
-    std::lock_guard<std::mutex> lk(mu);
-    if ((int)per_dev.size() <= dev) per_dev.resize(dev + 1, nullptr);
-    if (!per_dev[dev]) {
-        qb::LmScratch* p = nullptr;
-        if ((e = cudaMalloc(&p, sizeof(qb::LmScratch))) != cudaSuccess) return fail(QB_ENOMEM, "scratch alloc", e);
-        if ((e = cudaMemset(p, 0, sizeof(qb::LmScratch))) != cudaSuccess) return fail(QB_ECUDA, "scratch clear", e);
-        per_dev[dev] = p;
-    }
-    *out = per_dev[dev];
-    return QB_OK;
+int qwen_b200_device_error(int clear) {
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    unsigned int v = 0;
+    cudaError_t e = cudaMemcpy(&v, st->err, sizeof v, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return fail(QB_ECUDA, "device error read", e);
+    if (clear) cudaMemset(st->err, 0, sizeof v);
+    return (int)v;
 }
 
 int qwen_b200_lm_head_bf16_dev(const float* h, const uint16_t* E, int vocab, int hidden, int k, int* out_id,
@@ -529,10 +561,10 @@ int qwen_b200_lm_head_bf16_dev(const float* h, const uint16_t* E, int vocab, int
     if ((k < vocab ? k : vocab) > qb::kTopkMax) return fail(QB_EINVAL, "lm_head_bf16: k above 1024");
     if (hidden % 8 || reinterpret_cast<uintptr_t>(E) % 16 || reinterpret_cast<uintptr_t>(h) % 8)
         return fail(QB_EINVAL, "lm_head_bf16_dev: hidden must be a multiple of 8, E 16-byte and h 8-byte aligned");
-    qb::LmScratch* sc = nullptr;
-    if (int rc = scratch_for_current_device(&sc)) return rc;
-    cudaError_t e = qb::launch_lm_head_bf16(h, E, vocab, hidden, k, 1, sc, nullptr, out_id, out_ids, out_scores,
-                                            out_n, static_cast<cudaStream_t>(stream));
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    cudaError_t e = qb::launch_lm_head_bf16(h, E, vocab, hidden, k, 1, st->scratch, st->err, nullptr, out_id,
+                                            out_ids, out_scores, out_n, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_lm_head_bf16_dev", e);
 }
 
@@ -542,10 +574,10 @@ int qwen_b200_lm_head_bfp8_dev(const float* h, const int8_t* mant, const uint8_t
         return fail(QB_EINVAL, "lm_head_bfp8: bad arguments");
     if (k > 0 && (!out_ids || !out_scores || !out_n)) return fail(QB_EINVAL, "lm_head_bfp8: null outputs");
     if ((k < vocab ? k : vocab) > qb::kTopkMax) return fail(QB_EINVAL, "lm_head_bfp8: k above 1024");
-    qb::LmScratch* sc = nullptr;
-    if (int rc = scratch_for_current_device(&sc)) return rc;
-    cudaError_t e = qb::launch_bfp8_lm_head(h, mant, exps, vocab, hidden, k, sc, out_id, out_ids, out_scores, out_n,
-                                            static_cast<cudaStream_t>(stream));
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    cudaError_t e = qb::launch_bfp8_lm_head(h, mant, exps, vocab, hidden, k, st->scratch, st->err, out_id, out_ids,
+                                            out_scores, out_n, static_cast<cudaStream_t>(stream));
     if (e == cudaErrorInvalidValue)
         return fail(QB_EINVAL, "lm_head_bfp8: hidden must be a multiple of 512 with 16/8/8-byte aligned mant/exps/h");
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_lm_head_bfp8_dev", e);

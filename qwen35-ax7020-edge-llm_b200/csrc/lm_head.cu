@@ -12,13 +12,14 @@
 //
 // Kernel shape: a unit is 64 table rows; thread t owns row t/4 and the two
 // chains 2*(t%4), 2*(t%4)+1 for the whole unit, so every chain is summed in
-// one thread in element order.  Rows stream through a P-stage cp.async ring
-// in 16 KB slices (64 rows x 256 bytes) laid out as 128-byte rows with the
-// 16-byte chunk index XORed by (row & 7) (the TMA SWIZZLE_128B pattern); the
+// one thread in element order.  Rows stream through a P-stage ring of 16 KB
+// slices (64 rows x 256 bytes) loaded by TMA (two 64 x 128-byte boxes per
+// slice, SWIZZLE_128B: the 16-byte chunk index XORed by row & 7), so the
 // 32-bit reads of a warp (8 rows x one chunk) are conflict free.
 #include "bfp8_gemv.cuh"
 #include "common.cuh"
 #include "lm_head.cuh"
+#include "tma.cuh"
 #include "topk.cuh"
 
 #include <algorithm>
@@ -35,10 +36,12 @@ constexpr int kStage = kRows * kSegBytes; // 16 KB
 constexpr int kP = 6;
 
 struct LmArgs {
+    CUtensorMap tmap;   // E as rows x hidden uint16, 64 x 64-element boxes
     const float* h;
     const uint16_t* E;
     int vocab, hidden;
     int units, slices;  // per unit
+    unsigned int* err;
     LmScratch* sc;
     int kk;
     int* out_id;
@@ -47,42 +50,35 @@ struct LmArgs {
     int* out_n;
 };
 
-__device__ __forceinline__ void issue(const LmArgs& A, int u, int s, unsigned char* st) {
-    const int r0 = u * kRows;
-    const int rv = min(kRows, A.vocab - r0);
-    const int chunks_total = A.hidden >> 3;          // 16-byte chunks per row
-    const int vc = min(kChunks, chunks_total - s * kChunks);
-    const unsigned char* src = reinterpret_cast<const unsigned char*>(A.E) +
-                               ((size_t)r0 * A.hidden + (size_t)s * (kSegBytes / 2)) * 2;
-    const size_t rowb = (size_t)A.hidden * 2;
-    if (vc == kChunks) {
-#pragma unroll 4
-        for (int idx = threadIdx.x; idx < rv * kChunks; idx += kThreads) {
-            int r = idx / kChunks, q = idx % kChunks;
-            cp_async16(st + (q >> 3) * (kRows * 128) + r * 128 + (((q & 7) ^ (r & 7)) << 4),
-                       src + (size_t)r * rowb + q * 16);
-        }
-    } else {
-        for (int idx = threadIdx.x; idx < rv * vc; idx += kThreads) {
-            int r = idx / vc, q = idx - r * vc;
-            cp_async16(st + (q >> 3) * (kRows * 128) + r * 128 + (((q & 7) ^ (r & 7)) << 4),
-                       src + (size_t)r * rowb + q * 16);
-        }
+__device__ __forceinline__ void issue(const LmArgs& A, int u, int s, unsigned char* st, uint64_t* bar) {
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(bar, kStage);
+        tma_load_2d(st, &A.tmap, s * (kSegBytes / 2), u * kRows, bar);
+        tma_load_2d(st + kRows * 128, &A.tmap, s * (kSegBytes / 2) + 64, u * kRows, bar);
     }
 }
 
 template <bool TOPK>
 __global__ void __launch_bounds__(kThreads, 1) lm_bf16_kernel(const __grid_constant__ LmArgs A) {
-    extern __shared__ __align__(128) unsigned char smem[];
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                           ~uintptr_t(1023));
     unsigned char* stages = smem;
-    float* hs = reinterpret_cast<float*>(smem + kP * kStage);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kP * kStage);
+    float* hs = reinterpret_cast<float*>(smem + kP * kStage + 64);
     unsigned long long* cand = reinterpret_cast<unsigned long long*>(hs + A.hidden);
     __shared__ int s_cand_count;
     __shared__ unsigned long long s_red[kThreads / 32];
 
     const int tid = threadIdx.x;
     const int r = tid >> 2, p = tid & 3;
-    if (tid == 0) s_cand_count = 0;
+    if (tid == 0) {
+        s_cand_count = 0;
+        for (int k = 0; k < kP; k++) mbar_init(&bars[k], 1);
+        fence_barrier_init();
+        tma_prefetch_desc(&A.tmap);
+    }
+    __syncthreads();
 
     // contiguous unit range of this CTA
     const int u_begin = (int)(((long long)A.units * blockIdx.x) / gridDim.x);
@@ -94,11 +90,10 @@ __global__ void __launch_bounds__(kThreads, 1) lm_bf16_kernel(const __grid_const
 #pragma unroll 1
     for (int k = 0; k < kP - 1; k++) {
         if (issued < total) {
-            issue(A, iu, is, stages + k * kStage);
+            issue(A, iu, is, stages + k * kStage, &bars[k]);
             if (++is == A.slices) { is = 0; iu++; }
             issued++;
         }
-        cp_async_commit();
     }
     for (int i = tid; i < A.hidden; i += kThreads) hs[i] = A.h[i];
 
@@ -107,14 +102,14 @@ __global__ void __launch_bounds__(kThreads, 1) lm_bf16_kernel(const __grid_const
     int cu = u_begin, cs = 0;
 #pragma unroll 1
     for (int it = 0; it < total; it++) {
-        cp_async_wait<kP - 2>();
+        mbar_wait(&bars[it % kP], (uint32_t)(it / kP) & 1u, A.err);
         __syncthreads();
         if (issued < total) {
-            issue(A, iu, is, stages + ((it + kP - 1) % kP) * kStage);
+            const int ns = (it + kP - 1) % kP;
+            issue(A, iu, is, stages + ns * kStage, &bars[ns]);
             if (++is == A.slices) { is = 0; iu++; }
             issued++;
         }
-        cp_async_commit();
         if (TOPK && s_cand_count > kCandCap - 2 * kRows) cand_compact(cand, &s_cand_count, A.kk);
 
         const unsigned char* st = stages + (it % kP) * kStage;
@@ -167,7 +162,6 @@ __global__ void __launch_bounds__(kThreads, 1) lm_bf16_kernel(const __grid_const
             cs++;
         }
     }
-    cp_async_wait<0>();
     __syncthreads();
     unsigned long long* work = reinterpret_cast<unsigned long long*>(stages);
     lm_finish(A.sc, cand, &s_cand_count, work, (kP * kStage) / 8, best, TOPK ? A.kk : 0, A.out_id,
@@ -232,9 +226,9 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(const float* scores
 }  // namespace
 
 cudaError_t launch_lm_head_bf16(const float* h, const uint16_t* E, int vocab, int hidden, int k,
-                                int with_tail, LmScratch* scratch, float* score_buf, int* out_id,
-                                int* out_ids, float* out_scores, int* out_n, cudaStream_t stream) {
-    if (vocab <= 0 || hidden <= 0 || k < 0 || k > kTopkMax) return cudaErrorInvalidValue;
+                                int with_tail, LmScratch* scratch, unsigned int* err_word, float* score_buf,
+                                int* out_id, int* out_ids, float* out_scores, int* out_n, cudaStream_t stream) {
+    if (vocab <= 0 || hidden <= 0 || k < 0 || std::min(k, vocab) > kTopkMax) return cudaErrorInvalidValue;
     LmArgs A{};
     A.h = h;
     A.E = E;
@@ -246,14 +240,15 @@ cudaError_t launch_lm_head_bf16(const float* h, const uint16_t* E, int vocab, in
     A.out_ids = out_ids;
     A.out_scores = out_scores;
     A.out_n = out_n;
+    A.err = err_word;
     const bool fast = hidden % 8 == 0 && reinterpret_cast<uintptr_t>(E) % 16 == 0 &&
-                      reinterpret_cast<uintptr_t>(h) % 8 == 0;
+                      reinterpret_cast<uintptr_t>(h) % 8 == 0 &&
+                      encode_tmap_2d(&A.tmap, E, 2, (uint64_t)vocab, (uint64_t)hidden, (uint32_t)kRows);
     if (fast) {
         A.units = (vocab + kRows - 1) / kRows;
         A.slices = ((hidden >> 3) + kChunks - 1) / kChunks;
         const int grid = std::min(std::min(num_sms(), A.units), kMaxGrid);
-        const size_t smem = (size_t)kP * kStage + 4 * (size_t)hidden + ((4 * (size_t)hidden) % 16 ? 8 : 0) +
-                            (size_t)kCandCap * 8;
+        const size_t smem = 1024 + (size_t)kP * kStage + 64 + 4 * (size_t)hidden + (size_t)kCandCap * 8;
         cudaError_t err;
         if (A.kk > 0) {
             err = cudaFuncSetAttribute(lm_bf16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,

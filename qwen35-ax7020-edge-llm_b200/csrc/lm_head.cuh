@@ -13,7 +13,7 @@ struct LmScratch;
 // lm_head_argmax drops it); it only matters on the generic-shape path, which
 // also needs `score_buf` (vocab floats).  Results land in device memory.
 cudaError_t launch_lm_head_bf16(const float* h, const uint16_t* E, int vocab, int hidden, int k,
-                                int with_tail, LmScratch* scratch, float* score_buf, int* out_id,
-                                int* out_ids, float* out_scores, int* out_n, cudaStream_t stream);
+                                int with_tail, LmScratch* scratch, unsigned int* err, float* score_buf,
+                                int* out_id, int* out_ids, float* out_scores, int* out_n, cudaStream_t stream);
 
 }  // namespace qb

@@ -12,9 +12,9 @@
 //      buffer (compacting to the best kk when it fills),
 //   2. at its end the CTA sorts the buffer and writes its best kk keys to the
 //      scratch lists, then takes a ticket,
-//   3. the CTA with the last ticket radix-selects the kk-th largest key of
-//      the union, sorts the winners and writes ids / scores, then clears the
-//      ticket and the argmax word for the next launch.
+//   3. the CTA with the last ticket selects the kk largest keys of the
+//      union (see lm_finish), writes ids / scores, then clears the ticket and
+//      the argmax word for the next launch.
 #pragma once
 #include "common.cuh"
 
@@ -91,17 +91,35 @@ __device__ inline unsigned long long block_max_u64(unsigned long long v, unsigne
     return m;
 }
 
+// Scatter the keys of work[0..m) (distinct) by descending rank into
+// out[0..min(m, keep)), by counting, O(m^2 / threads).  Ends with a barrier.
+__device__ inline void rank_place(const unsigned long long* work, int m, int keep, unsigned long long* out) {
+    for (int i = threadIdx.x; i < m; i += blockDim.x) {
+        const unsigned long long k = work[i];
+        int r = 0;
+        for (int j = 0; j < m; j++) r += work[j] > k;
+        if (r < keep) out[r] = k;
+    }
+    __syncthreads();
+}
+
 // End-of-CTA work for the lm_head kernels.  `cand`/`cand_count` is the CTA's
-// shared buffer, `work` a shared scratch area of at least
-// max(kCandCap, union) keys that may alias the CTA's stage buffers,
-// `work_cap` its size in keys.  `best` is this thread's argmax key.
-// Writes out_id[0] (argmax) and, for kk > 0, out_ids/out_scores[0..n) and
-// *out_n.
+// shared buffer (kCandCap keys), `work` a shared scratch area of `work_cap`
+// keys that may alias the CTA's stage buffers.  `best` is this thread's
+// argmax key.  Writes out_id[0] (argmax) and, for kk > 0,
+// out_ids/out_scores[0..n) and *out_n.
+//
+// Final merge in the last CTA: with L_c the sorted list of CTA c, the
+// kk-th largest key K* of the union is at least T1 = max_c L_c[kk-1] and at
+// least T2 = the kk-th largest head L_c[0]; every key >= T = max(T1, T2)
+// is gathered (typically ~2kk of them) and ranked.  If too many qualify
+// the CTA falls back to a radix select of K* over the lists.
 __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int* cand_count,
                                  unsigned long long* work, int work_cap, unsigned long long best,
                                  int kk, int* out_id, int* out_ids, float* out_scores, int* out_n,
                                  unsigned long long* red) {
     const int tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
     unsigned long long bm = block_max_u64(best, red);
     if (tid == 0 && bm) atomicMax(&sc->argmax_key, bm);
 
@@ -126,103 +144,130 @@ __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int* c
         *out_id = k ? key_id(k) : 0;
     }
     if (kk > 0) {
-        // gather the union of the per-CTA lists into shared memory
+        __shared__ int s_m;
         __shared__ int s_total;
-        __shared__ unsigned int s_hist[256];
-        __shared__ unsigned long long s_prefix;
-        __shared__ int s_remaining;
-        __shared__ int s_nsel;
-        if (tid == 0) {
-            int t = 0;
-            for (int c = 0; c < (int)gridDim.x; c++) t += ((volatile int*)sc->counts)[c];
-            s_total = t;
+        const int G = gridDim.x;
+        const volatile int* counts = sc->counts;
+        const volatile unsigned long long* lists = sc->lists;
+        // thresholds: heads into cand[0..pow2(G)), kth keys reduced
+        const int gp = next_pow2(G);
+        unsigned long long t1 = 0ull;
+        int tot = 0;
+        for (int c = tid; c < gp; c += blockDim.x) {
+            int n = c < G ? counts[c] : 0;
+            cand[c] = n > 0 ? lists[(size_t)c * kk] : 0ull;
+            if (n == kk) {
+                unsigned long long v = lists[(size_t)c * kk + kk - 1];
+                t1 = v > t1 ? v : t1;
+            }
+            tot += n;
         }
+        for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+        if (tid == 0) s_total = 0;
         __syncthreads();
+        if (lane == 0) atomicAdd(&s_total, tot);
+        t1 = block_max_u64(t1, red);   // contains barriers
+        block_sort_desc(cand, gp);
+        const unsigned long long t2 = (kk <= G) ? cand[kk - 1] : 0ull;
+        const unsigned long long T = t1 > t2 ? t1 : t2;
         const int total = s_total;
-        const bool in_smem = total <= work_cap;
-        // keys live either in `work` (shared) or are read from the lists
-        if (in_smem) {
-            int base = 0;
-            for (int c = 0; c < (int)gridDim.x; c++) {
-                int n = ((volatile int*)sc->counts)[c];
-                const volatile unsigned long long* src = sc->lists + (size_t)c * kk;
-                for (int i = tid; i < n; i += blockDim.x) work[base + i] = src[i];
-                base += n;
+        const int want = total < kk ? total : kk;
+        // gather keys >= T (lists are sorted: each warp walks one list)
+        if (tid == 0) s_m = 0;
+        __syncthreads();
+        for (int c = warp; c < G; c += nwarps) {
+            const int n = counts[c];
+            for (int i = lane; i < n; i += 32) {
+                const unsigned long long key = lists[(size_t)c * kk + i];
+                const bool take = key >= T;
+                if (take) {
+                    int p = atomicAdd(&s_m, 1);
+                    if (p < work_cap) work[p] = key;
+                }
+                if (!__any_sync(__activemask(), take)) break;
             }
         }
         __syncthreads();
-        auto key_at = [&](int c, int i) -> unsigned long long {
-            return ((const volatile unsigned long long*)sc->lists)[(size_t)c * kk + i];
-        };
-        // radix select of the kk-th largest key (keys are distinct)
-        const int want = total < kk ? total : kk;
-        if (tid == 0) {
-            s_prefix = 0ull;
-            s_remaining = want;
-        }
-        __syncthreads();
-        if (want > 0 && want < total) {
+        const int m = s_m;
+        if (m <= work_cap) {
+            if (m <= 1024) {
+                rank_place(work, m, want, cand);
+            } else {
+                const int p2 = next_pow2(m);
+                for (int i = m + tid; i < p2; i += blockDim.x) work[i] = 0ull;
+                __syncthreads();
+                if (p2 <= work_cap) {
+                    block_sort_desc(work, p2);
+                    for (int i = tid; i < want; i += blockDim.x) cand[i] = work[i];
+                    __syncthreads();
+                } else {
+                    rank_place(work, m, want, cand);
+                }
+            }
+        } else {
+            // radix select of the want-th largest key over the lists, with
+            // warp-private histograms (work area reused)
+            unsigned int* hist = reinterpret_cast<unsigned int*>(work);   // [nwarps][256]
+            __shared__ unsigned long long s_prefix;
+            __shared__ int s_rem;
+            if (tid == 0) {
+                s_prefix = 0ull;
+                s_rem = want;
+            }
+            __syncthreads();
             for (int pass = 0; pass < 8; pass++) {
                 const int shift = 56 - 8 * pass;
-                for (int i = tid; i < 256; i += blockDim.x) s_hist[i] = 0u;
+                for (int i = tid; i < nwarps * 256; i += blockDim.x) hist[i] = 0u;
                 __syncthreads();
                 const unsigned long long pre = s_prefix;
-                auto count_key = [&](unsigned long long key) {
-                    bool match = pass == 0 ? true : ((key >> (shift + 8)) == pre);
-                    if (match) atomicAdd(&s_hist[(key >> shift) & 0xFFull], 1u);
-                };
-                if (in_smem) {
-                    for (int i = tid; i < total; i += blockDim.x) count_key(work[i]);
-                } else {
-                    for (int c = 0; c < (int)gridDim.x; c++) {
-                        int n = ((volatile int*)sc->counts)[c];
-                        for (int i = tid; i < n; i += blockDim.x) count_key(key_at(c, i));
+                for (int c = warp; c < G; c += nwarps) {
+                    const int n = counts[c];
+                    for (int i = lane; i < n; i += 32) {
+                        const unsigned long long key = lists[(size_t)c * kk + i];
+                        if (pass == 0 || (key >> (shift + 8)) == pre)
+                            atomicAdd(&hist[warp * 256 + ((key >> shift) & 0xFFull)], 1u);
                     }
                 }
                 __syncthreads();
                 if (tid == 0) {
-                    int rem = s_remaining;
+                    int rem = s_rem;
                     unsigned int cum = 0;
                     int d = 255;
                     for (; d > 0; d--) {
-                        if ((int)(cum + s_hist[d]) >= rem) break;
-                        cum += s_hist[d];
+                        unsigned int h = 0;
+                        for (int w = 0; w < nwarps; w++) h += hist[w * 256 + d];
+                        if ((int)(cum + h) >= rem) break;
+                        cum += h;
                     }
-                    s_remaining = rem - (int)cum;
+                    s_rem = rem - (int)cum;
                     s_prefix = (pre << 8) | (unsigned long long)d;
                 }
                 __syncthreads();
             }
-        }
-        const unsigned long long kstar = (want > 0 && want < total) ? s_prefix : 0ull;
-        // collect the winners (exactly `want` keys >= kstar) into cand[]
-        if (tid == 0) s_nsel = 0;
-        __syncthreads();
-        auto take = [&](unsigned long long key) {
-            if (key >= kstar && key != 0ull) {
-                int p = atomicAdd(&s_nsel, 1);
-                if (p < kTopkMax) cand[p] = key;
+            const unsigned long long kstar = s_prefix;
+            if (tid == 0) s_m = 0;
+            __syncthreads();
+            for (int c = warp; c < G; c += nwarps) {
+                const int n = counts[c];
+                for (int i = lane; i < n; i += 32) {
+                    const unsigned long long key = lists[(size_t)c * kk + i];
+                    if (key >= kstar) {
+                        int p = atomicAdd(&s_m, 1);
+                        if (p < kTopkMax) cand[p] = key;
+                    }
+                }
             }
-        };
-        if (in_smem) {
-            for (int i = tid; i < total; i += blockDim.x) take(work[i]);
-        } else {
-            for (int c = 0; c < (int)gridDim.x; c++) {
-                int n = ((volatile int*)sc->counts)[c];
-                for (int i = tid; i < n; i += blockDim.x) take(key_at(c, i));
-            }
+            __syncthreads();
+            const int p2 = next_pow2(want < 1 ? 1 : want);
+            for (int i = want + tid; i < p2; i += blockDim.x) cand[i] = 0ull;
+            __syncthreads();
+            block_sort_desc(cand, p2);
         }
-        __syncthreads();
-        int nsel = s_nsel < want ? s_nsel : want;
-        int p2 = next_pow2(nsel < 1 ? 1 : nsel);
-        for (int i = nsel + tid; i < p2; i += blockDim.x) cand[i] = 0ull;
-        __syncthreads();
-        block_sort_desc(cand, p2);
-        for (int i = tid; i < nsel; i += blockDim.x) {
+        for (int i = tid; i < want; i += blockDim.x) {
             out_ids[i] = key_id(cand[i]);
             out_scores[i] = key_score(cand[i]);
         }
-        if (tid == 0) *out_n = nsel;
+        if (tid == 0) *out_n = want;
     }
     if (tid == 0) {
         sc->argmax_key = 0ull;
