@@ -206,7 +206,7 @@ def run_b200(args):
         copies = args.copies or max(2, math.ceil(L2_DEFEAT_BYTES / wbytes))
         ds = model.DeviceStack(shapes, copies=copies, device=dev, seed=1234 + rank)
         plans = [ops.LinearStack(ds.views(c)) for c in range(copies)]
-        launches_per_step = 1
+        launches_per_step = 2   # act_prep + gemv_warp
 
         def step(i):
             plans[i % copies].run()
@@ -232,11 +232,11 @@ def run_b200(args):
             "config": {"workload": desc, "gemvs_per_step": len(shapes), "weight_bytes": wbytes,
                        "algorithmic_bytes_per_step": nb["total"], "macs_per_step": nb["macs"],
                        "l2": f"rotates {copies} weight copies ({copies * wbytes / 1e9:.2f} GB) > 126 MB L2",
-                       "launch": "one grouped persistent kernel per step", "parallelism": f"replicas x{world}"},
+                       "launch": "act_prep + one grouped warp-autonomous kernel (PDL) per step", "parallelism": f"replicas x{world}"},
             "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 2), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(kernel_gbs / hbm_peak, 4), "peak_kind": peak_kind,
                          "traffic": committed_traffic(args.workload),
-                         "kernel": "gemv_exact_kernel (grouped)"},
+                         "kernel": "gemv_warp_kernel (grouped)"},
             "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,

@@ -129,10 +129,11 @@ QB_API int qwen_b200_quant_dev(const float* x, int B, int K, int16_t* xq, float*
 
 /* Grouped launch of n independent GEMVs (e.g. the per-token linear stack).
  * Arrays are HOST arrays of DEVICE pointers.  Returns a plan handle (>= 1)
- * or a QB_E* code; the plan is reusable and safe to launch inside CUDA
- * graph capture.  Every mant pointer must be 16-byte aligned, every exps
- * pointer 8-byte aligned, every x 8-byte aligned, and every K a multiple of
- * 512. */
+ * or a QB_E* code; the plan owns its activation scratch and scheduler
+ * counters, is reusable and can be launched inside CUDA graph capture.
+ * 1 <= n <= 160; every mant pointer 16-byte aligned, every exps pointer
+ * 4-byte aligned, every x 8-byte aligned, every K a multiple of 512.  Runs
+ * of one plan must not overlap on the GPU (they share its scratch). */
 QB_API int qwen_b200_stack_create(int n, const int8_t* const* mant, const uint8_t* const* exps,
                            const float* const* x, float* const* y, const int* M, const int* K);
 QB_API int qwen_b200_stack_run(int plan, void* stream);

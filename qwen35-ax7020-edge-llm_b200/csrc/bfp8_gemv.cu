@@ -13,121 +13,65 @@
 //                             D the whole block dot and IEEE subnormals.
 // The result is bit-identical to the reference's NEON build.
 //
-// Kernel shape.  A work unit is RG consecutive rows of one GEMV; a CTA owns a
-// contiguous run of units (balanced by bytes across all GEMVs of a grouped
-// launch) and streams each unit through a P-stage cp.async ring in 16 KB
-// slices of RG rows x (16384/RG) bytes.  Inside a slice, lane = row and warp
-// = 64-byte block: a thread forms the four lane-class sums of one (row, block)
-// with __dp2a (int16 activation pairs (k, k+4) against weight bytes paired by
-// prmt), turns them into the four fp32 block terms and stores them; the
-// per-row float chains then run sequentially over blocks in 4*RG "chain"
-// threads (row, lane class), one slice behind.  Weight tiles are laid out in
-// shared memory as 128-byte rows with the 16-byte chunk index XORed by
-// (row & 7), the TMA SWIZZLE_128B pattern, so the per-row reads of a warp are
-// bank-conflict free.
+// Two kernels per launch:
+//  1. act_prep: every activation of the launch is quantized once into a
+//     paired int16 layout (block b, group g = elements 8g..8g+7, word j =
+//     the pair (xq[64b+8g+j], xq[64b+8g+4+j]), the operand order of __dp2a)
+//     plus its block scales.  It releases the dependent launch at once.
+//  2. gemv_warp (programmatic dependent launch): warp-autonomous streaming.
+//     A work unit is 32 consecutive rows of one GEMV; a warp owns a unit
+//     from its first byte to its output (lane = row), streaming it through a
+//     private 3-stage ring: per stage two TMA boxes of 32 rows x 128 bytes
+//     (SWIZZLE_128B, 4 blocks of every row) plus one bulk copy of those 4
+//     blocks' activation pairs and scales, all on one mbarrier, while each
+//     lane copies its row's four exponent bytes with cp.async.  Each lane
+//     forms the four lane-class sums of a block with __dp2a (int16 pairs
+//     against weight bytes paired by prmt) and keeps the four fp32 chains in
+//     registers, so the float order is the reference's with no cross-thread
+//     exchange and no CTA barrier.  Weight loads are issued before the kernel
+//     waits on act_prep.  Units are handed out by an atomic counter (largest
+//     K first) in grouped launches and round-robin for a single GEMV.
 #include "bfp8_gemv.cuh"
 #include "common.cuh"
 #include "tma.cuh"
 #include "topk.cuh"
 
 #include <algorithm>
+#include <numeric>
+#include <vector>
 
 namespace qb {
 
 constexpr int kThreads = 256;
-constexpr int kStageMant = 16384;   // mantissa bytes per stage (TMA boxes)
-constexpr int kStages = 5;          // ring depth; two CTAs fit one SM for K <= 4096
+constexpr int kWarps = kThreads / 32;
+constexpr int kRows = 32;            // rows per unit (lane = row)
+constexpr int kStage = 8192;         // bytes per stage: 32 rows x 256 bytes (4 blocks)
+constexpr int kBox = 4096;           // one TMA box: 32 rows x 128 bytes
+constexpr int kRing = 3;             // stages per warp
+constexpr int kXp = 528;             // activation bytes per stage: 4 blocks x 128 B pairs + 4 scales
+constexpr int kMaxSDesc = 160;       // GEMVs per grouped launch
 
-template <int RG>
-struct Geo {
-    static constexpr int SB = 256 / RG;          // 64-byte blocks per slice row
-    static constexpr int RS = 64 * SB;           // bytes per slice row
-    static constexpr int BOXES = RS / 128;       // TMA boxes (RG rows x 128 B) per slice
-    static constexpr int EXB = RG * SB;          // exponent bytes per stage (256)
-};
+size_t gemv_act_words(int K) { return (size_t)K / 2 + (size_t)K / 64; }
 
-struct GemvArgs {
+// ---------------------------------------------------------------- act_prep
+struct PrepArgs {
     GemvDesc single;
-    const GemvDesc* list;   // nullptr -> `single`
+    const GemvDesc* list;
     int n;
-    int total_units;
-    long long total_cost;
-    int kmax;
-    unsigned int* err;
-    // lm_head epilogue
-    LmScratch* sc;
-    int kk;
-    int* out_id;
-    int* out_ids;
-    float* out_scores;
-    int* out_n;
 };
 
-__device__ __forceinline__ const GemvDesc& desc_ref(const GemvArgs& A, int d) {
+__device__ __forceinline__ const GemvDesc& prep_desc(const PrepArgs& A, int d) {
     return A.list ? A.list[d] : A.single;
 }
 
-template <int RG>
-struct Cursor {
-    int d, u, s, ns, M, K, nb, ub, ue;
-    const uint8_t* exps;
-    bool valid;
-
-    __device__ void set_desc(const GemvArgs& A, int dd) {
-        const GemvDesc& D = desc_ref(A, dd);
-        d = dd;
-        M = D.M;
-        K = D.K;
-        nb = K >> 6;
-        ns = (nb + Geo<RG>::SB - 1) / Geo<RG>::SB;
-        ub = D.unit_begin;
-        ue = D.unit_begin + (M + RG - 1) / RG;
-        exps = D.exps;
-    }
-    __device__ void advance(const GemvArgs& A, int u_end) {
-        if (++s < ns) return;
-        s = 0;
-        if (++u >= u_end) {
-            valid = false;
-            return;
-        }
-        while (u >= ue) set_desc(A, d + 1);
-    }
-};
-
-// First unit whose cost start is >= pos (units ordered GEMV by GEMV).
-template <int RG>
-__device__ int unit_at_cost(const GemvArgs& A, long long pos, int* d_out) {
-    if (pos >= A.total_cost) {
-        *d_out = A.n;
-        return A.total_units;
-    }
-    int lo = 0, hi = A.n - 1;
-    while (lo < hi) {  // largest d with cost_begin <= pos
-        int mid = (lo + hi + 1) >> 1;
-        if (desc_ref(A, mid).cost_begin <= pos) lo = mid;
-        else hi = mid - 1;
-    }
-    const GemvDesc& D = desc_ref(A, lo);
-    int ns = ((D.K >> 6) + Geo<RG>::SB - 1) / Geo<RG>::SB;
-    int units = (D.M + RG - 1) / RG;
-    long long off = pos - D.cost_begin;
-    long long uo = (off + ns - 1) / ns;
-    if (uo >= units) {
-        *d_out = lo + 1;
-        return D.unit_begin + units;
-    }
-    *d_out = lo;
-    return D.unit_begin + (int)uo;
-}
-
-// Quantize (or load) one activation into the paired shared layout:
-// block b, group g (elements 8g..8g+7), word j holds the int16 pair
-// (xq[64b+8g+j], xq[64b+8g+4+j]) -- the operand order of __dp2a below.
-__device__ void stage_activation(const GemvDesc& D, uint32_t* xp, float* xss) {
+// grid (n, chunks): CTA (d, c) prepares blocks [64c, 64c + 64) of GEMV d.
+__global__ void __launch_bounds__(kThreads) act_prep_kernel(const __grid_constant__ PrepArgs A) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const GemvDesc& D = prep_desc(A, blockIdx.x);
     const int nb = D.K >> 6;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int b = warp; b < nb; b += kThreads / 32) {
+    const int b_end = min(nb, (int)(blockIdx.y + 1) * 64);
+    for (int b = blockIdx.y * 64 + warp; b < b_end; b += kWarps) {
         int q0, q1;
         float xs;
         if (D.x) {
@@ -156,107 +100,73 @@ __device__ void stage_activation(const GemvDesc& D, uint32_t* xp, float* xss) {
             int g = lane >> 2, p = 2 * (lane & 3);
             uint32_t w0 = (mine & 0xFFFFu) | (part << 16);
             uint32_t w1 = (mine >> 16) | (part & 0xFFFF0000u);
-            *reinterpret_cast<uint2*>(xp + b * 32 + g * 4 + p) = make_uint2(w0, w1);
+            *reinterpret_cast<uint2*>(D.xpairs + b * 32 + g * 4 + p) = make_uint2(w0, w1);
         }
-        if (lane == 0) xss[b] = xs;
+        if (lane == 0) D.xscale[b] = xs;
     }
 }
 
-// Start one slice: thread 0 arms the stage barrier and issues the TMA boxes
-// of the mantissa tile; warp 1 copies the slice's exponent bytes (8-byte
-// pieces, cp.async, one commit group per slice issued by every thread).
-template <int RG>
-__device__ __forceinline__ void issue_slice(const GemvArgs& A, const Cursor<RG>& c, unsigned char* mant_st,
-                                            unsigned char* exps_st, uint64_t* bar) {
-    using G = Geo<RG>;
-    const int r0 = (c.u - c.ub) * RG;
-    const int b0 = c.s * G::SB;
-    if (threadIdx.x == 0) {
-        mbar_arrive_expect_tx(bar, kStageMant);
-        const void* tm = &desc_ref(A, c.d).tmap;
-#pragma unroll
-        for (int j = 0; j < G::BOXES; j++) tma_load_2d(mant_st + j * (RG * 128), tm, b0 * 64 + j * 128, r0, bar);
-    } else if ((threadIdx.x >> 5) == 1) {
-        const int lane = threadIdx.x & 31;
-        const int rv = min(RG, c.M - r0);
-        const int vb = min(G::SB, c.nb - b0);
-        const int ppr = vb >> 3;
-        const uint8_t* esrc = c.exps + (size_t)r0 * c.nb + b0;
-        for (int idx = lane; idx < rv * ppr; idx += 32) {
-            int r = idx / ppr, p = idx - r * ppr;
-            cp_async8(exps_st + r * G::SB + p * 8, esrc + (size_t)r * c.nb + p * 8);
-        }
-    }
-}
-
-// Block terms of one slice: thread (row r = lane % RG, block bs) -> tb[bs][r][0..3].
-template <int RG>
-__device__ __forceinline__ void compute_slice(const Cursor<RG>& c, const unsigned char* mant_st,
-                                              const unsigned char* exps_st, float* tb, const uint32_t* xp,
-                                              const float* xss) {
-    using G = Geo<RG>;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int r = lane % RG;
-    const int bs = warp * (32 / RG) + lane / RG;
-    const int b0 = c.s * G::SB;
-    const int vb = min(G::SB, c.nb - b0);
-    if (bs >= vb) return;
-    const int b = b0 + bs;
-    const unsigned char* rowp = mant_st + (bs >> 1) * (RG * 128) + r * 128;
-    const int sw = r & 7;
-    const int cbase = (bs & 1) * 4;
-    const uint4* xb = reinterpret_cast<const uint4*>(xp) + b * 8;
-    // two accumulators per lane class: dependent dp2a chains of 4, not 8
-    int A0 = 0, A1 = 0, A2 = 0, A3 = 0, B0 = 0, B1 = 0, B2 = 0, B3 = 0;
-#pragma unroll
-    for (int cc = 0; cc < 4; cc++) {
-        uint4 w = *reinterpret_cast<const uint4*>(rowp + (((cbase + cc) ^ sw) << 4));
-        uint4 xa = xb[2 * cc], xc = xb[2 * cc + 1];
-        int p01 = (int)__byte_perm(w.x, w.y, 0x5140), p23 = (int)__byte_perm(w.x, w.y, 0x7362);
-        A0 = __dp2a_lo((int)xa.x, p01, A0);
-        A1 = __dp2a_hi((int)xa.y, p01, A1);
-        A2 = __dp2a_lo((int)xa.z, p23, A2);
-        A3 = __dp2a_hi((int)xa.w, p23, A3);
-        int q01 = (int)__byte_perm(w.z, w.w, 0x5140), q23 = (int)__byte_perm(w.z, w.w, 0x7362);
-        B0 = __dp2a_lo((int)xc.x, q01, B0);
-        B1 = __dp2a_hi((int)xc.y, q01, B1);
-        B2 = __dp2a_lo((int)xc.z, q23, B2);
-        B3 = __dp2a_hi((int)xc.w, q23, B3);
-    }
-    const int L0 = A0 + B0, L1 = A1 + B1, L2 = A2 + B2, L3 = A3 + B3;
-    const uint32_t e = exps_st[r * G::SB + bs];
-    const float xsb = xss[b];
-    const int grow = (c.u - c.ub) * RG + r;
-    float4 T;
-    if ((c.M & 1) && grow == c.M - 1) {
-        const float S = exp_scale_ieee(e);
-        T.x = mul_rn(mul_rn(i2f_rn(L0 + L1 + L2 + L3), S), xsb);
-        T.y = T.z = T.w = 0.0f;
-    } else {
-        const float S = exp_scale_ftz(e);
-        T.x = mul_ftz(mul_ftz(i2f_rn(L0), S), xsb);
-        T.y = mul_ftz(mul_ftz(i2f_rn(L1), S), xsb);
-        T.z = mul_ftz(mul_ftz(i2f_rn(L2), S), xsb);
-        T.w = mul_ftz(mul_ftz(i2f_rn(L3), S), xsb);
-    }
-    reinterpret_cast<float4*>(tb)[bs * RG + r] = T;
-}
-
-struct SliceInfo {
-    int vb, row0, M, rv, d;
-    bool last;
+// ---------------------------------------------------------------- gemv_warp
+struct WArgs {
+    GemvDesc single;
+    const GemvDesc* list;   // nullptr -> `single`
+    int n;
+    int total_units;
+    unsigned int* ctr;      // [0] next unit, [1] exhausted warps; nullptr -> round-robin
+    unsigned int* err;
+    // lm_head epilogue
+    LmScratch* sc;
+    int kk;
+    int* out_id;
+    int* out_ids;
+    float* out_scores;
+    int* out_n;
 };
 
-template <int RG>
-__device__ __forceinline__ SliceInfo slice_info(const Cursor<RG>& c) {
-    SliceInfo s;
-    s.vb = min(Geo<RG>::SB, c.nb - c.s * Geo<RG>::SB);
-    s.row0 = (c.u - c.ub) * RG;
-    s.M = c.M;
-    s.rv = min(RG, c.M - s.row0);
-    s.d = c.d;
-    s.last = (c.s == c.ns - 1);
-    return s;
+__device__ __forceinline__ const GemvDesc& wdesc(const WArgs& A, int d) {
+    return A.list ? A.list[d] : A.single;
+}
+
+// What a warp needs to know about a GEMV, copied to shared memory at start
+// so that mapping a claimed unit to its GEMV never touches global memory.
+struct SDesc {
+    int unit_begin, M, K, pad;
+    const uint8_t* exps;
+    const uint32_t* xp;
+    const float* xs;
+    const void* tmap;
+    float* y;
+};
+
+struct Unit {
+    bool valid;
+    int d, r0, M, K, nb, nst;
+    const uint8_t* exps;
+    const uint32_t* xp;
+    const float* xs;
+};
+
+__device__ __forceinline__ Unit load_unit(const SDesc* T, int n, int total_units, int u) {
+    Unit U;
+    U.valid = u < total_units;
+    if (!U.valid) return U;
+    int lo = 0, hi = n - 1;
+    while (lo < hi) {   // largest d with unit_begin <= u
+        const int mid = (lo + hi + 1) >> 1;
+        if (T[mid].unit_begin <= u) lo = mid;
+        else hi = mid - 1;
+    }
+    const SDesc& D = T[lo];
+    U.d = lo;
+    U.r0 = (u - D.unit_begin) * kRows;
+    U.M = D.M;
+    U.K = D.K;
+    U.nb = D.K >> 6;
+    U.nst = D.K >> 8;
+    U.exps = D.exps;
+    U.xp = D.xp;
+    U.xs = D.xs;
+    return U;
 }
 
 struct LmState {
@@ -265,160 +175,257 @@ struct LmState {
     int* cand_count;
 };
 
-// Sequential float chain of one slice, run by the 4*RG threads of the LAST
-// warps of the CTA (warps 0 and 1 also issue the TMA and exponent copies):
-// chain thread c = row*4 + class.  The slice's terms are loaded first (they
-// do not depend on the chain), then added in block order.
-template <int RG, bool LM>
-__device__ __forceinline__ void chain_slice(const GemvArgs& A, const SliceInfo& s, const float* tb,
-                                            float& f, LmState& lm) {
-    constexpr int SB = Geo<RG>::SB;
-    const int ct = threadIdx.x - (kThreads - 4 * RG);
-    if (ct < 0) return;
-    const int r = ct >> 2, j = ct & 3;
-    const int grow = s.row0 + r;
-    const bool odd = (s.M & 1) && grow == s.M - 1;
-    float t[SB];
-#pragma unroll
-    for (int bs = 0; bs < SB; bs++) t[bs] = (bs < s.vb) ? tb[bs * RG * 4 + ct] : 0.0f;
-    if (odd) {
-#pragma unroll
-        for (int bs = 0; bs < SB; bs++)
-            if (bs < s.vb) f = add_rn(f, t[bs]);
-    } else {
-#pragma unroll
-        for (int bs = 0; bs < SB; bs++)
-            if (bs < s.vb) f = add_ftz(f, t[bs]);
-    }
-    if (s.last) {
-        float a = add_ftz(f, __shfl_xor_sync(0xffffffffu, f, 2));
-        float yv = add_ftz(a, __shfl_xor_sync(0xffffffffu, a, 1));
-        if (odd) yv = f;
-        if (j == 0 && r < s.rv) {
-            if (LM) {
-                if (yv > -1e30f) {
-                    unsigned long long k = cand_key(yv, grow);
-                    lm.best = k > lm.best ? k : lm.best;
-                }
-                if (A.kk > 0 && yv > -3.402823466e38f) {
-                    int p = atomicAdd(lm.cand_count, 1);
-                    lm.cand[p] = cand_key(yv, grow);
-                }
-            } else {
-                desc_ref(A, s.d).y[grow] = yv;
-            }
+template <bool LM>
+__device__ __forceinline__ void unit_result(const WArgs& A, const SDesc* T, const Unit& U, int lane, float yv,
+                                            LmState& lm) {
+    const int row = U.r0 + lane;
+    if (row >= U.M) return;
+    if (LM) {
+        if (yv > -1e30f) {
+            const unsigned long long k = cand_key(yv, row);
+            lm.best = k > lm.best ? k : lm.best;
         }
-        f = 0.0f;
+        if (A.kk > 0 && yv > -3.402823466e38f) {
+            const int p = atomicAdd(lm.cand_count, 1);
+            if (p < kCandCap) lm.cand[p] = cand_key(yv, row);
+        }
+    } else {
+        T[U.d].y[row] = yv;
     }
 }
 
-struct SmemLayout {
-    size_t exps, bars, terms, xp, xss, cand, total;
-};
-__host__ __device__ inline SmemLayout smem_layout(int kmax, bool lm) {
-    SmemLayout L;
-    L.exps = (size_t)kStages * kStageMant;
-    L.bars = L.exps + (size_t)kStages * 256;
-    L.terms = (L.bars + kStages * 8 + 15) & ~size_t(15);
-    L.xp = L.terms + 2 * 1024 * sizeof(float);
-    L.xss = L.xp + 2 * (size_t)kmax;
-    L.cand = (L.xss + 4 * (size_t)(kmax / 64) + 15) & ~size_t(15);
-    L.total = L.cand + (lm ? (size_t)kCandCap * 8 : 0);
-    return L;
+// The 4 blocks of one stage for this lane's row: lane-class sums with
+// __dp2a, then the reference float steps into the four chains (or, for the
+// odd last row, the scalar form into fo).
+template <bool ODD>
+__device__ __forceinline__ void stage_blocks(const unsigned char* st, const uint4* xst, const float* xsst,
+                                             uint32_t ew, int sw, bool odd, float& f0, float& f1, float& f2,
+                                             float& f3, float& fo) {
+#pragma unroll
+    for (int jb = 0; jb < 4; jb++) {
+        const unsigned char* rowp = st + (jb >> 1) * kBox;
+        const int cb = (jb & 1) * 4;
+        const uint4* xb = xst + jb * 8;
+        int A0 = 0, A1 = 0, A2 = 0, A3 = 0, B0 = 0, B1 = 0, B2 = 0, B3 = 0;
+#pragma unroll
+        for (int cc = 0; cc < 4; cc++) {
+            const uint4 w = *reinterpret_cast<const uint4*>(rowp + (((cb + cc) ^ sw) << 4));
+            const uint4 xa = xb[2 * cc], xc = xb[2 * cc + 1];
+            const int p01 = (int)__byte_perm(w.x, w.y, 0x5140), p23 = (int)__byte_perm(w.x, w.y, 0x7362);
+            A0 = __dp2a_lo((int)xa.x, p01, A0);
+            A1 = __dp2a_hi((int)xa.y, p01, A1);
+            A2 = __dp2a_lo((int)xa.z, p23, A2);
+            A3 = __dp2a_hi((int)xa.w, p23, A3);
+            const int q01 = (int)__byte_perm(w.z, w.w, 0x5140), q23 = (int)__byte_perm(w.z, w.w, 0x7362);
+            B0 = __dp2a_lo((int)xc.x, q01, B0);
+            B1 = __dp2a_hi((int)xc.y, q01, B1);
+            B2 = __dp2a_lo((int)xc.z, q23, B2);
+            B3 = __dp2a_hi((int)xc.w, q23, B3);
+        }
+        const int L0 = A0 + B0, L1 = A1 + B1, L2 = A2 + B2, L3 = A3 + B3;
+        const uint32_t e = (ew >> (8 * jb)) & 0xFFu;
+        const float xsb = xsst[jb];
+        if (!ODD || !odd) {
+            const float S = exp_scale_ftz(e);
+            f0 = add_ftz(f0, mul_ftz(mul_ftz(i2f_rn(L0), S), xsb));
+            f1 = add_ftz(f1, mul_ftz(mul_ftz(i2f_rn(L1), S), xsb));
+            f2 = add_ftz(f2, mul_ftz(mul_ftz(i2f_rn(L2), S), xsb));
+            f3 = add_ftz(f3, mul_ftz(mul_ftz(i2f_rn(L3), S), xsb));
+        } else {
+            fo = add_rn(fo, mul_rn(mul_rn(i2f_rn(L0 + L1 + L2 + L3), exp_scale_ieee(e)), xsb));
+        }
+    }
 }
 
-template <int RG, bool LM>
-__global__ void __launch_bounds__(kThreads, 2) gemv_exact_kernel(const __grid_constant__ GemvArgs A) {
-    using G = Geo<RG>;
-    constexpr int P = kStages;
+template <bool LM>
+__global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_constant__ WArgs A) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    // TMA 128-byte swizzle needs 1024-byte aligned destinations
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                            ~uintptr_t(1023));
-    const SmemLayout Ly = smem_layout(A.kmax, LM);
-    unsigned char* mant_st = smem;
-    unsigned char* exps_st = smem + Ly.exps;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Ly.bars);
-    float* terms = reinterpret_cast<float*>(smem + Ly.terms);
-    uint32_t* xp = reinterpret_cast<uint32_t*>(smem + Ly.xp);
-    float* xss = reinterpret_cast<float*>(smem + Ly.xss);
-    unsigned long long* cand = reinterpret_cast<unsigned long long*>(smem + Ly.cand);
+    unsigned char* rings = smem;                                            // [warp][slot] 8 KB
+    unsigned char* xrings = smem + kWarps * kRing * kStage;                 // [warp][slot] 528 B
+    unsigned char* erings = xrings + kWarps * kRing * kXp;                  // [warp][slot][lane] 4 B
+    uint64_t* bars = reinterpret_cast<uint64_t*>(erings + kWarps * kRing * 128);   // [warp][slot]
+    SDesc* sdesc = reinterpret_cast<SDesc*>(bars + kWarps * kRing);                  // [n]
+    unsigned long long* cand = reinterpret_cast<unsigned long long*>(sdesc + A.n);
     __shared__ int s_cand_count;
-    __shared__ unsigned long long s_red[kThreads / 32];
+    __shared__ unsigned long long s_red[kWarps];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    unsigned char* ring = rings + warp * kRing * kStage;
+    unsigned char* xring = xrings + warp * kRing * kXp;
+    unsigned char* ering = erings + warp * kRing * 128;
+    uint64_t* bar = bars + warp * kRing;
+    if (threadIdx.x == 0) s_cand_count = 0;
+    if (lane == 0) {
+        for (int s = 0; s < kRing; s++) mbar_init(&bar[s], 1);
+        fence_barrier_init();
+    }
+    for (int d = threadIdx.x; d < A.n; d += kThreads) {
+        const GemvDesc& D = wdesc(A, d);
+        SDesc t;
+        t.unit_begin = D.unit_begin;
+        t.M = D.M;
+        t.K = D.K;
+        t.pad = 0;
+        t.exps = D.exps;
+        t.xp = D.xpairs;
+        t.xs = D.xscale;
+        t.tmap = &D.tmap;
+        t.y = D.y;
+        sdesc[d] = t;
+    }
+    __syncthreads();
+    const int nd = A.n, nu_total = A.total_units;
 
     LmState lm;
     lm.best = 0ull;
     lm.cand = cand;
     lm.cand_count = &s_cand_count;
-    if (threadIdx.x == 0) {
-        s_cand_count = 0;
-        for (int s = 0; s < P; s++) mbar_init(&bars[s], 1);
-        fence_barrier_init();
-    }
-    __syncthreads();
 
-    const long long T = A.total_cost;
-    int d0, d1;
-    const int u_begin = unit_at_cost<RG>(A, (T * blockIdx.x) / gridDim.x, &d0);
-    const int u_end = unit_at_cost<RG>(A, (T * (blockIdx.x + 1)) / gridDim.x, &d1);
+    const int W = gridDim.x * kWarps;
+    const int gw = blockIdx.x * kWarps + warp;
+    int rr_next = gw;   // round-robin schedule
+    bool exhausted = false;
+    auto claim = [&]() -> int {
+        if (exhausted) return nu_total;
+        int u;
+        if (A.ctr) {
+            unsigned int v = 0;
+            if (lane == 0) v = atomicAdd(&A.ctr[0], 1u);
+            u = (int)__shfl_sync(0xffffffffu, v, 0);
+            if (u >= nu_total) {
+                exhausted = true;
+                __threadfence();
+                if (lane == 0 && atomicAdd(&A.ctr[1], 1u) == (unsigned int)W - 1u) {
+                    // every warp has seen the end: leave the counters zero
+                    A.ctr[0] = 0u;
+                    A.ctr[1] = 0u;
+                }
+            }
+        } else {
+            u = rr_next;
+            rr_next += W;
+            if (u >= nu_total) exhausted = true;
+        }
+        return u < nu_total ? u : nu_total;
+    };
 
-    Cursor<RG> ic;
-    ic.valid = u_begin < u_end;
-    ic.u = u_begin;
-    ic.s = 0;
-    if (ic.valid) {
-        ic.set_desc(A, d0);
-        if (threadIdx.x == 0) tma_prefetch_desc(&desc_ref(A, d0).tmap);
-    }
-    Cursor<RG> cc = ic;
+    // producer: claimed units in a two-entry ring (it runs at most one unit
+    // ahead of the consumer); the claim after the producer's current unit is
+    // requested as soon as that unit starts, so the atomic's round trip
+    // overlaps the unit's streaming
+    int claimed0, claimed1;          // claim sequence entries 2j and 2j+1
+    int kp = 0;                      // index of the producer's unit in the claim sequence
+    claimed0 = claim();
+    claimed1 = nu_total;
+    int ahead = claim();
+    Unit pu = load_unit(sdesc, nd, nu_total, claimed0);
+    int ps = 0;
+    if (lane == 0 && pu.valid) tma_prefetch_desc(sdesc[pu.d].tmap);
 
-#pragma unroll 1
-    for (int p = 0; p < P - 1; p++) {
-        if (ic.valid) {
-            issue_slice<RG>(A, ic, mant_st + p * kStageMant, exps_st + p * G::EXB, &bars[p]);
-            ic.advance(A, u_end);
+    // One stage: both weight boxes and the stage's activation slice (pairs +
+    // scales of its 4 blocks) land on bar[slot].  The activation slice comes
+    // from act_prep, so the stages issued before griddepcontrol.wait defer
+    // their activation copies (the barrier already expects those bytes).
+    static_assert(kRing == 3, "two deferred activation copies are tracked");
+    const uint32_t* pend_xp0 = nullptr;
+    const uint32_t* pend_xp1 = nullptr;
+    const float* pend_xs0 = nullptr;
+    const float* pend_xs1 = nullptr;
+    auto issue = [&](int slot, bool xp_ready) {
+        if (pu.valid) {
+            if (lane == 0) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive_expect_tx(&bar[slot], kStage + kXp);
+                const void* tm = sdesc[pu.d].tmap;
+                tma_load_2d(ring + slot * kStage, tm, ps * 256, pu.r0, &bar[slot]);
+                tma_load_2d(ring + slot * kStage + kBox, tm, ps * 256 + 128, pu.r0, &bar[slot]);
+                if (xp_ready) {
+                    bulk_load(xring + slot * kXp, pu.xp + ps * 128, 512, &bar[slot]);
+                    bulk_load(xring + slot * kXp + 512, pu.xs + ps * 4, 16, &bar[slot]);
+                }
+            }
+            if (!xp_ready) {
+                if (slot == 0) {
+                    pend_xp0 = pu.xp + ps * 128;
+                    pend_xs0 = pu.xs + ps * 4;
+                } else {
+                    pend_xp1 = pu.xp + ps * 128;
+                    pend_xs1 = pu.xs + ps * 4;
+                }
+            }
+            if (pu.r0 + lane < pu.M)
+                cp_async4(ering + slot * 128 + lane * 4, pu.exps + (size_t)(pu.r0 + lane) * pu.nb + ps * 4);
+            if (++ps == pu.nst) {
+                ps = 0;
+                kp++;
+                const int nu = ahead;
+                if (kp & 1) claimed1 = nu;
+                else claimed0 = nu;
+                pu = load_unit(sdesc, nd, nu_total, nu);
+                ahead = claim();
+            }
         }
         cp_async_commit();
+    };
+
+    issue(0, false);
+    issue(1, false);
+
+    // the activations come from act_prep (programmatic dependent launch)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (lane == 0) {
+        if (pend_xp0) {
+            bulk_load(xring, pend_xp0, 512, &bar[0]);
+            bulk_load(xring + 512, pend_xs0, 16, &bar[0]);
+        }
+        if (pend_xp1) {
+            bulk_load(xring + kXp, pend_xp1, 512, &bar[1]);
+            bulk_load(xring + kXp + 512, pend_xs1, 16, &bar[1]);
+        }
     }
 
-    int loaded_d = -1;
-    float f = 0.0f;
-    SliceInfo prev;
-    bool have_prev = false;
+    int kc = 0;
+    Unit cu = load_unit(sdesc, nd, nu_total, claimed0);
+    int cs = 0;
+    float f0 = 0.f, f1 = 0.f, f2 = 0.f, f3 = 0.f, fo = 0.f;
+    const int sw = lane & 7;
     int i = 0;
 #pragma unroll 1
-    for (; cc.valid; i++) {
-        const int st = i % P;
-        mbar_wait(&bars[st], (uint32_t)(i / P) & 1u, A.err);
-        cp_async_wait<P - 2>();
-        __syncthreads();
-        if (ic.valid) {
-            const int ns = (i + P - 1) % P;
-            issue_slice<RG>(A, ic, mant_st + ns * kStageMant, exps_st + ns * G::EXB, &bars[ns]);
-            ic.advance(A, u_end);
+    while (cu.valid) {
+        const int slot = i % kRing;
+        mbar_wait(&bar[slot], (uint32_t)(i / kRing) & 1u, A.err);
+        cp_async_wait<kRing - 2>();
+        __syncwarp();
+        issue((i + kRing - 1) % kRing, true);
+
+        const bool odd_unit = (cu.M & 1) && (cu.r0 + kRows > cu.M - 1);   // the unit holds the odd last row
+        const bool odd = odd_unit && (cu.r0 + lane == cu.M - 1);
+        const uint32_t ew = *reinterpret_cast<const uint32_t*>(ering + slot * 128 + lane * 4);
+        const unsigned char* st = ring + slot * kStage + lane * 128;
+        const uint4* xst = reinterpret_cast<const uint4*>(xring + slot * kXp);
+        const float* xsst = reinterpret_cast<const float*>(xring + slot * kXp + 512);
+        if (!odd_unit)
+            stage_blocks<false>(st, xst, xsst, ew, sw, false, f0, f1, f2, f3, fo);
+        else
+            stage_blocks<true>(st, xst, xsst, ew, sw, odd, f0, f1, f2, f3, fo);
+        if (++cs == cu.nst) {
+            const float yv = odd ? fo : add_ftz(add_ftz(f0, f2), add_ftz(f1, f3));
+            unit_result<LM>(A, sdesc, cu, lane, yv, lm);
+            f0 = f1 = f2 = f3 = fo = 0.f;
+            cs = 0;
+            kc++;
+            cu = load_unit(sdesc, nd, nu_total, (kc & 1) ? claimed1 : claimed0);
         }
-        cp_async_commit();
-        if (cc.d != loaded_d) {
-            stage_activation(desc_ref(A, cc.d), xp, xss);
-            __syncthreads();
-            loaded_d = cc.d;
-        }
-        if (LM && s_cand_count > kCandCap - 2 * RG) cand_compact(cand, &s_cand_count, A.kk);
-        if (have_prev) chain_slice<RG, LM>(A, prev, terms + ((i - 1) & 1) * 1024, f, lm);
-        compute_slice<RG>(cc, mant_st + st * kStageMant, exps_st + st * G::EXB, terms + (i & 1) * 1024, xp, xss);
-        prev = slice_info<RG>(cc);
-        have_prev = true;
-        cc.advance(A, u_end);
+        i++;
     }
     cp_async_wait<0>();
-    __syncthreads();
-    if (have_prev) chain_slice<RG, LM>(A, prev, terms + ((i - 1) & 1) * 1024, f, lm);
     if (LM) {
         __syncthreads();
-        unsigned long long* work = reinterpret_cast<unsigned long long*>(mant_st);
-        const int work_cap = (P * kStageMant) / 8;
-        lm_finish(A.sc, cand, &s_cand_count, work, work_cap, lm.best, A.kk, A.out_id, A.out_ids,
-                  A.out_scores, A.out_n, s_red);
+        unsigned long long* work = reinterpret_cast<unsigned long long*>(rings);
+        lm_finish(A.sc, cand, &s_cand_count, work, (kWarps * kRing * kStage) / 8, lm.best, A.kk, A.out_id,
+                  A.out_ids, A.out_scores, A.out_n, s_red);
     }
 }
 
@@ -518,99 +525,102 @@ int num_sms() {
     return n;
 }
 
+static size_t warp_smem_bytes(bool lm, int n) {
+    return 1024 + (size_t)kWarps * kRing * (kStage + kXp + 128) + (size_t)kWarps * kRing * 8 +
+           (size_t)n * sizeof(SDesc) + (lm ? (size_t)kCandCap * 8 : 0);
+}
+
 static bool fast_shape_ok(const GemvDesc& d) {
     if (d.M <= 0 || d.K <= 0 || d.K % 512) return false;
-    if (reinterpret_cast<uintptr_t>(d.mant) % 16 || reinterpret_cast<uintptr_t>(d.exps) % 8) return false;
+    if (reinterpret_cast<uintptr_t>(d.mant) % 16 || reinterpret_cast<uintptr_t>(d.exps) % 4) return false;
     if (d.x ? (reinterpret_cast<uintptr_t>(d.x) % 8) : (reinterpret_cast<uintptr_t>(d.xq) % 4)) return false;
     return true;
 }
 
-bool gemv_plan(GemvDesc* descs, int n, int rows_per_unit, GemvPlan* plan) {
-    const int sb = 256 / rows_per_unit;
+bool gemv_plan(GemvDesc* descs, int n, uint32_t* act, GemvPlan* plan) {
+    if (n <= 0 || n > kMaxSDesc) return false;
+    // largest K first: the counter then hands out the biggest units first
+    std::vector<int> order(n);
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return descs[a].K > descs[b].K; });
+    std::vector<GemvDesc> sorted;
+    sorted.reserve(n);
+    for (int i : order) sorted.push_back(descs[i]);
     int units = 0, kmax = 0;
-    long long cost = 0;
+    size_t words = 0;
     for (int i = 0; i < n; i++) {
-        GemvDesc& d = descs[i];
+        GemvDesc& d = sorted[i];
         if (!fast_shape_ok(d)) return false;
-        if (!encode_tmap_2d(&d.tmap, d.mant, 1, (uint64_t)d.M, (uint64_t)d.K, (uint32_t)rows_per_unit)) return false;
+        if (!encode_tmap_2d(&d.tmap, d.mant, 1, (uint64_t)d.M, (uint64_t)d.K, (uint32_t)kRows)) return false;
         d.unit_begin = units;
-        d.cost_begin = cost;
-        const int u = (d.M + rows_per_unit - 1) / rows_per_unit;
-        const int ns = ((d.K >> 6) + sb - 1) / sb;
-        units += u;
-        cost += (long long)u * ns;
+        d.xpairs = act ? act + words : nullptr;
+        d.xscale = act ? reinterpret_cast<float*>(act + words + d.K / 2) : nullptr;
+        words += gemv_act_words(d.K);
+        words = (words + 3) & ~size_t(3);   // keep every pair block 16-byte aligned
+        units += (d.M + kRows - 1) / kRows;
         kmax = std::max(kmax, d.K);
     }
-    plan->rows_per_unit = rows_per_unit;
+    for (int i = 0; i < n; i++) descs[i] = sorted[i];
     plan->n = n;
     plan->total_units = units;
-    plan->total_cost = cost;
     plan->kmax = kmax;
+    plan->act_words = words;
     return true;
 }
 
-template <int RG, bool LM>
-static cudaError_t launch_exact(const GemvArgs& A, int max_grid, cudaStream_t stream) {
-    const size_t smem = smem_layout(A.kmax, LM).total + 1024;
-    auto kern = gemv_exact_kernel<RG, LM>;
-    static size_t configured = 0;   // largest dynamic smem size set so far
-    if (smem > configured) {
-        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (err != cudaSuccess) return err;
-        configured = smem;
-    }
-    int occ = 1;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem) != cudaSuccess || occ < 1)
-        occ = 1;
-    const int grid = std::max(1, std::min(max_grid, num_sms() * occ));
-    kern<<<grid, kThreads, smem, stream>>>(A);
+static cudaError_t launch_prep(const PrepArgs& P, int nchunks, cudaStream_t stream) {
+    dim3 grid(P.n, nchunks);
+    act_prep_kernel<<<grid, kThreads, 0, stream>>>(P);
     return cudaGetLastError();
 }
 
-static int pick_rows_per_unit(int M) {
-    // enough units to give every CTA slot work; 32-row units read the most
-    // bytes per shared-memory access
-    const int slots = num_sms() * 2;
-    if ((M + 31) / 32 >= slots) return 32;
-    if ((M + 15) / 16 >= slots) return 16;
-    return 8;
+template <bool LM>
+static cudaError_t launch_warp(const WArgs& A, int grid, cudaStream_t stream) {
+    const size_t smem = warp_smem_bytes(LM, A.n);
+    static size_t configured = 0;   // largest dynamic smem size set so far
+    if (smem > configured) {
+        cudaError_t err = cudaFuncSetAttribute(gemv_warp_kernel<LM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)smem);
+        if (err != cudaSuccess) return err;
+        configured = smem;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemv_warp_kernel<LM>, A);
 }
 
-static cudaError_t dispatch_exact(GemvArgs& A, int rg, bool lm, int max_grid, cudaStream_t stream) {
-    if (lm) {
-        switch (rg) {
-            case 32: return launch_exact<32, true>(A, max_grid, stream);
-            case 16: return launch_exact<16, true>(A, max_grid, stream);
-            default: return launch_exact<8, true>(A, max_grid, stream);
-        }
-    }
-    switch (rg) {
-        case 32: return launch_exact<32, false>(A, max_grid, stream);
-        case 16: return launch_exact<16, false>(A, max_grid, stream);
-        default: return launch_exact<8, false>(A, max_grid, stream);
-    }
-}
-
-cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, unsigned int* err,
-                             cudaStream_t stream) {
+cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, unsigned int* ctr,
+                             unsigned int* err, cudaStream_t stream) {
     if (plan.n <= 0 || plan.total_units <= 0) return cudaSuccess;
-    GemvArgs A{};
+    PrepArgs P{};
+    P.list = dev_descs;
+    P.n = plan.n;
+    cudaError_t e = launch_prep(P, (plan.kmax / 64 + 63) / 64, stream);
+    if (e != cudaSuccess) return e;
+    WArgs A{};
     A.list = dev_descs;
     A.n = plan.n;
     A.total_units = plan.total_units;
-    A.total_cost = plan.total_cost;
-    A.kmax = plan.kmax;
+    A.ctr = ctr;
     A.err = err;
-    return dispatch_exact(A, plan.rows_per_unit, false, plan.total_units, stream);
+    const int grid = std::min(num_sms(), (plan.total_units + kWarps - 1) / kWarps);
+    return launch_warp<false>(A, grid, stream);
 }
 
-cudaError_t launch_gemv(const GemvDesc& d0, unsigned int* err, cudaStream_t stream) {
+cudaError_t launch_gemv(const GemvDesc& d0, uint32_t* act, unsigned int* err, cudaStream_t stream) {
     if (d0.M <= 0) return cudaSuccess;
     if (d0.K <= 0 || d0.K % 64) return cudaErrorInvalidValue;
     GemvDesc d = d0;
-    const int rg = pick_rows_per_unit(d.M);
     GemvPlan plan;
-    if (!fast_shape_ok(d) || !gemv_plan(&d, 1, rg, &plan)) {
+    if (!fast_shape_ok(d) || !act || !gemv_plan(&d, 1, act, &plan)) {
         const size_t smem = (((size_t)2 * d.K + 15) & ~size_t(15)) + 4 * (size_t)(d.K / 64);
         if (smem > 200 * 1024) return cudaErrorInvalidValue;
         cudaError_t e = cudaFuncSetAttribute(gemv_generic_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -619,36 +629,49 @@ cudaError_t launch_gemv(const GemvDesc& d0, unsigned int* err, cudaStream_t stre
         gemv_generic_kernel<<<(d.M + kThreads - 1) / kThreads, kThreads, smem, stream>>>(d);
         return cudaGetLastError();
     }
-    GemvArgs A{};
+    PrepArgs P{};
+    P.single = d;
+    P.n = 1;
+    cudaError_t e = launch_prep(P, (d.K / 64 + 63) / 64, stream);
+    if (e != cudaSuccess) return e;
+    WArgs A{};
     A.single = d;
-    A.list = nullptr;
     A.n = 1;
     A.total_units = plan.total_units;
-    A.total_cost = plan.total_cost;
-    A.kmax = plan.kmax;
+    A.ctr = nullptr;
     A.err = err;
-    return dispatch_exact(A, rg, false, plan.total_units, stream);
+    const int grid = std::min(num_sms(), (plan.total_units + kWarps - 1) / kWarps);
+    return launch_warp<false>(A, grid, stream);
 }
 
 cudaError_t launch_bfp8_lm_head(const float* h, const int8_t* mant, const uint8_t* exps, int vocab,
-                                int hidden, int k, LmScratch* scratch, unsigned int* err, int* out_id,
-                                int* out_ids, float* out_scores, int* out_n, cudaStream_t stream) {
+                                int hidden, int k, LmScratch* scratch, uint32_t* act, unsigned int* err,
+                                int* out_id, int* out_ids, float* out_scores, int* out_n,
+                                cudaStream_t stream) {
     GemvDesc d{};
     d.mant = mant;
     d.exps = exps;
     d.x = h;
     d.M = vocab;
     d.K = hidden;
-    if (vocab <= 0 || hidden <= 0 || k < 0 || std::min(k, vocab) > kTopkMax) return cudaErrorInvalidValue;
-    const int rg = pick_rows_per_unit(vocab);
+    if (vocab <= 0 || hidden <= 0 || k < 0 || std::min(k, vocab) > kTopkMax || !act) return cudaErrorInvalidValue;
     GemvPlan plan;
-    if (!fast_shape_ok(d) || !gemv_plan(&d, 1, rg, &plan)) return cudaErrorInvalidValue;
-    GemvArgs A{};
+    if (!fast_shape_ok(d) || !gemv_plan(&d, 1, act, &plan)) return cudaErrorInvalidValue;
+    const int grid = std::min(std::min(num_sms(), (plan.total_units + kWarps - 1) / kWarps), kMaxGrid);
+    // round-robin units: every CTA scores at most this many rows
+    const long long rows_per_cta =
+        (long long)((plan.total_units + grid * kWarps - 1) / (grid * kWarps)) * kWarps * kRows;
+    if (rows_per_cta > kCandCap) return cudaErrorInvalidValue;
+    PrepArgs P{};
+    P.single = d;
+    P.n = 1;
+    cudaError_t e = launch_prep(P, (d.K / 64 + 63) / 64, stream);
+    if (e != cudaSuccess) return e;
+    WArgs A{};
     A.single = d;
     A.n = 1;
     A.total_units = plan.total_units;
-    A.total_cost = plan.total_cost;
-    A.kmax = plan.kmax;
+    A.ctr = nullptr;
     A.err = err;
     A.sc = scratch;
     A.kk = std::min(k, vocab);
@@ -656,7 +679,7 @@ cudaError_t launch_bfp8_lm_head(const float* h, const int8_t* mant, const uint8_
     A.out_ids = out_ids;
     A.out_scores = out_scores;
     A.out_n = out_n;
-    return dispatch_exact(A, rg, true, std::min(plan.total_units, kMaxGrid), stream);
+    return launch_warp<true>(A, grid, stream);
 }
 
 cudaError_t launch_quant_block64(const float* x, int B, int K, int16_t* xq, float* xs,

@@ -157,6 +157,8 @@ const void* device_of(const void* p, size_t bytes, int* rc) {
 struct StackPlan {
     qb::GemvPlan plan;
     qb::GemvDesc* dev_descs = nullptr;
+    uint32_t* act = nullptr;          // paired activations of every GEMV
+    unsigned int* ctr = nullptr;      // unit counter pair of the dynamic scheduler
     bool live = false;
 };
 std::vector<StackPlan> g_plans;
@@ -190,7 +192,9 @@ struct Cand {
 struct DevState {
     qb::LmScratch* scratch = nullptr;
     unsigned int* err = nullptr;
+    uint32_t* act = nullptr;       // paired-activation scratch of single-GEMV launches
 };
+constexpr size_t kActScratchWords = 128 * 1024;   // serves K <= 253952
 
 int dev_state(DevState** out) {
     static std::mutex mu;
@@ -208,8 +212,11 @@ int dev_state(DevState** out) {
         unsigned int* w = nullptr;
         if ((e = cudaMalloc(&w, sizeof(unsigned int))) != cudaSuccess) return fail(QB_ENOMEM, "error word alloc", e);
         if ((e = cudaMemset(w, 0, sizeof(unsigned int))) != cudaSuccess) return fail(QB_ECUDA, "error word clear", e);
+        uint32_t* a = nullptr;
+        if ((e = cudaMalloc(&a, kActScratchWords * 4)) != cudaSuccess) return fail(QB_ENOMEM, "act scratch alloc", e);
         st.scratch = p;
         st.err = w;
+        st.act = a;
     }
     *out = &st;
     return QB_OK;
@@ -299,7 +306,11 @@ void bfp8_gemv(float* y, const float* x, const int8_t* mant, const uint8_t* exps
     d.K = K;
     DevState* dst = nullptr;
     if (dev_state(&dst)) return;
-    cudaError_t e = qb::launch_gemv(d, dst->err, s);
+    if (qb::gemv_act_words(K) > kActScratchWords) {
+        fail(QB_EINVAL, "bfp8_gemv: K too large");
+        return;
+    }
+    cudaError_t e = qb::launch_gemv(d, dst->act, dst->err, s);
     if (e != cudaSuccess) {
         fail(QB_ECUDA, "bfp8_gemv launch", e);
         return;
@@ -468,7 +479,8 @@ int qwen_b200_gemv_dev(float* y, const float* x, const int8_t* mant, const uint8
     d.K = K;
     DevState* st = nullptr;
     if (int rc = dev_state(&st)) return rc;
-    cudaError_t e = qb::launch_gemv(d, st->err, static_cast<cudaStream_t>(stream));
+    if (qb::gemv_act_words(K) > kActScratchWords) return fail(QB_EINVAL, "K too large");
+    cudaError_t e = qb::launch_gemv(d, st->act, st->err, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_gemv_dev", e);
 }
 
@@ -486,7 +498,8 @@ int qwen_b200_gemv_q_dev(float* y, const int16_t* xq, const float* xs, const int
     d.K = K;
     DevState* st = nullptr;
     if (int rc = dev_state(&st)) return rc;
-    cudaError_t e = qb::launch_gemv(d, st->err, static_cast<cudaStream_t>(stream));
+    if (qb::gemv_act_words(K) > kActScratchWords) return fail(QB_EINVAL, "K too large");
+    cudaError_t e = qb::launch_gemv(d, st->act, st->err, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_gemv_q_dev", e);
 }
 
@@ -515,9 +528,15 @@ int qwen_b200_stack_create(int n, const int8_t* const* mant, const uint8_t* cons
         v.push_back(d);
     }
     StackPlan sp;
-    if (!qb::gemv_plan(v.data(), (int)v.size(), 32, &sp.plan))
-        return fail(QB_EINVAL, "stack: every K must be a multiple of 512 with 16/8/8-byte aligned mant/exps/x");
-    cudaError_t e = cudaMalloc(&sp.dev_descs, sizeof(qb::GemvDesc) * (v.size() ? v.size() : 1));
+    if (!qb::gemv_plan(v.data(), (int)v.size(), nullptr, &sp.plan))
+        return fail(QB_EINVAL, "stack: 1..160 GEMVs, every K a multiple of 512, mant/exps/x 16/4/8-byte aligned");
+    cudaError_t e = cudaMalloc(&sp.act, sp.plan.act_words * 4 + 16);
+    if (e != cudaSuccess) return fail(QB_ENOMEM, "stack act alloc", e);
+    if ((e = cudaMalloc(&sp.ctr, 2 * sizeof(unsigned int))) != cudaSuccess) return fail(QB_ENOMEM, "stack ctr alloc", e);
+    if ((e = cudaMemset(sp.ctr, 0, 2 * sizeof(unsigned int))) != cudaSuccess)
+        return fail(QB_ECUDA, "stack ctr clear", e);
+    qb::gemv_plan(v.data(), (int)v.size(), sp.act, &sp.plan);
+    e = cudaMalloc(&sp.dev_descs, sizeof(qb::GemvDesc) * (v.size() ? v.size() : 1));
     if (e != cudaSuccess) return fail(QB_ENOMEM, "stack alloc", e);
     e = cudaMemcpy(sp.dev_descs, v.data(), sizeof(qb::GemvDesc) * v.size(), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return fail(QB_ECUDA, "stack upload", e);
@@ -531,7 +550,7 @@ int qwen_b200_stack_run(int plan, void* stream) {
     const StackPlan& sp = g_plans[plan - 1];
     DevState* st = nullptr;
     if (int rc = dev_state(&st)) return rc;
-    cudaError_t e = qb::launch_gemv_list(sp.dev_descs, sp.plan, st->err, static_cast<cudaStream_t>(stream));
+    cudaError_t e = qb::launch_gemv_list(sp.dev_descs, sp.plan, sp.ctr, st->err, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_stack_run", e);
 }
 
@@ -539,6 +558,8 @@ int qwen_b200_stack_destroy(int plan) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (plan < 1 || plan > (int)g_plans.size() || !g_plans[plan - 1].live) return fail(QB_EINVAL, "stack: bad handle");
     cudaFree(g_plans[plan - 1].dev_descs);
+    cudaFree(g_plans[plan - 1].act);
+    cudaFree(g_plans[plan - 1].ctr);
     g_plans[plan - 1].live = false;
     g_plans[plan - 1].dev_descs = nullptr;
     return QB_OK;
@@ -576,10 +597,12 @@ int qwen_b200_lm_head_bfp8_dev(const float* h, const int8_t* mant, const uint8_t
     if ((k < vocab ? k : vocab) > qb::kTopkMax) return fail(QB_EINVAL, "lm_head_bfp8: k above 1024");
     DevState* st = nullptr;
     if (int rc = dev_state(&st)) return rc;
-    cudaError_t e = qb::launch_bfp8_lm_head(h, mant, exps, vocab, hidden, k, st->scratch, st->err, out_id, out_ids,
-                                            out_scores, out_n, static_cast<cudaStream_t>(stream));
+    if (qb::gemv_act_words(hidden) > kActScratchWords) return fail(QB_EINVAL, "lm_head_bfp8: hidden too large");
+    cudaError_t e = qb::launch_bfp8_lm_head(h, mant, exps, vocab, hidden, k, st->scratch, st->act, st->err, out_id,
+                                            out_ids, out_scores, out_n, static_cast<cudaStream_t>(stream));
     if (e == cudaErrorInvalidValue)
-        return fail(QB_EINVAL, "lm_head_bfp8: hidden must be a multiple of 512 with 16/8/8-byte aligned mant/exps/h");
+        return fail(QB_EINVAL, "lm_head_bfp8: hidden must be a multiple of 512, mant/exps/h 16/4/8-byte aligned, "
+                               "and at most 2048 vocab rows per SM");
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_lm_head_bfp8_dev", e);
 }
 

@@ -64,6 +64,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, 
         : "memory");
 }
 
+// 1D bulk copy global -> shared (16-byte aligned addresses, size a multiple
+// of 16), completing on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src), "r"(bytes),
+          "r"((uint32_t)__cvta_generic_to_shared(bar))
+        : "memory");
+}
+
 // ------------------------------------------------------------ host side
 // Encode a 2D row-major tensor map (rows x cols elements of elem_bytes) with
 // a box of box_rows x (128 / elem_bytes) elements and SWIZZLE_128B.
