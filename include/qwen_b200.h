@@ -127,6 +127,21 @@ QB_API int qwen_b200_gemv_q_dev(float* y, const int16_t* xq, const float* xs, co
  * over B rows: x [B][K] -> xq int16 [B][K], xs [B][K/64]. */
 QB_API int qwen_b200_quant_dev(const float* x, int B, int K, int16_t* xq, float* xs, void* stream);
 
+/* Same GEMV as qwen_b200_gemv_dev(), for callers that cannot let a library
+ * allocate device memory (a process whose allocator owns all of HBM, a
+ * path that cannot afford cudaMalloc's device-wide synchronisation, a host
+ * framework that only lends memory from its own pools).  Its scratch is a
+ * fixed 33 KB array inside the library's device image, present on every GPU
+ * that loads the library until the process exits; nothing is allocated or
+ * freed.  K <= 16384 (QB_EINVAL beyond).  The first call on a device looks
+ * up the array's device address; make that first call before any stream
+ * capture.  All calls on a device share the array: calls that overlap on
+ * the GPU (e.g. on two streams) race and must be serialised by the caller.
+ * Bounded-wait timeouts are not recorded for qwen_b200_device_error().  No
+ * counterpart in the reference. */
+QB_API int qwen_b200_gemv_noalloc_dev(float* y, const float* x, const int8_t* mant, const uint8_t* exps, int M,
+                                      int K, void* stream);
+
 /* Grouped launch of n independent GEMVs (e.g. the per-token linear stack).
  * Arrays are HOST arrays of DEVICE pointers.  Returns a plan handle (>= 1)
  * or a QB_E* code; the plan owns its activation scratch and scheduler

@@ -32,6 +32,7 @@ SIGNATURES = {
     "qwen_b200_forget_weights": (_I, [_P]),
     "qwen_b200_reset_weights": (None, []),
     "qwen_b200_gemv_dev": (_I, [_P, _P, _P, _P, _I, _I, _P]),
+    "qwen_b200_gemv_noalloc_dev": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "qwen_b200_gemv_q_dev": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
     "qwen_b200_quant_dev": (_I, [_P, _I, _I, _P, _P, _P]),
     "qwen_b200_stack_create": (_I, [_I, _P, _P, _P, _P, _P, _P]),
