@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["stack", "gemv", "lm_bf16", "lm_bfp8"], default="stack")
+    ap.add_argument("--workload", choices=["stack", "gemv", "lm_bf16", "lm_bfp8", "sharded"], default="stack")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--copies", type=int, default=0,
@@ -243,6 +243,8 @@ def run_b200(args):
         })
         for p in plans:
             p.close()
+    elif args.workload == "sharded":
+        line.update(run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, peak_kind))
     else:
         line.update(run_lm_head(args, torch, ops, dev, barrier, world, hbm_peak, peak_kind))
 
@@ -252,6 +254,39 @@ def run_b200(args):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, peak_kind):
+    """8 layers x (gate, up 28672x8192; down 8192x28672),
+    batch 1, output rows sharded over the ranks with an NCCL all-gather
+    after every projection.  Total work is fixed as N grows (strong scaling)."""
+    from qwen_b200 import sharded
+
+    layers = sharded.scaled_layers()
+    full_w = sum(t.M * t.K + t.M * t.K // 64 for L in layers for t in (L.gate, L.up, L.down))
+    copies = args.copies or max(1, math.ceil(L2_DEFEAT_BYTES / (full_w / world)))
+    st = sharded.ShardedDeviceStack(layers, world, rank, dev, copies=copies, seed=11, fast=True)
+    clk = ClockSampler(gpu_uuid(torch, dev), local)
+    secs = timed(torch, lambda i: st.step(i % copies), args.steps, args.warmup, barrier)
+    clocks = clk.stop()
+    t = torch.tensor([secs], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    per_step = float(t.item()) / args.steps
+    nbytes = st.bytes_per_step()
+    st.close()
+    per_rank_gbs = nbytes / world / per_step / 1e9
+    return {"value": round(nbytes / per_step / 1e9, 2), "ms_per_step": round(per_step * 1e3, 4), "scaling": "strong",
+            "config": {"workload": "scaled BFP8 stack: 8 x (gate/up 28672x8192, down 8192x28672), batch 1",
+                       "arithmetic": "fast (split-K, fma per block; within 1e-5 of the exact order)",
+                       "algorithmic_bytes_per_step": nbytes, "weight_bytes": full_w,
+                       "parallelism": f"output rows sharded x{world}, NCCL all-gather after each projection",
+                       "l2": f"rotates {copies} copies of this rank's {full_w / world / 1e9:.2f} GB"},
+            "roofline": {"bound": "hbm", "achieved": round(per_rank_gbs, 2), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(per_rank_gbs / hbm_peak, 4), "peak_kind": peak_kind, "traffic": None,
+                         "kernel": "gemv_warp_kernel per rank (per-rank GB/s incl. all-gathers)"},
+            "gpu_launches": args.steps * len(layers) * 4,   # 2 grouped launches x (act_prep + gemv_warp); NCCL not counted
+            "clocks": clocks}
 
 
 def end_to_end(torch, dist, ds, plans, copies, nb, args, barrier, world, dev):

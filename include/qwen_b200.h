@@ -123,6 +123,17 @@ QB_API int qwen_b200_gemv_dev(float* y, const float* x, const int8_t* mant, cons
 QB_API int qwen_b200_gemv_q_dev(float* y, const int16_t* xq, const float* xs, const int8_t* mant,
                          const uint8_t* exps, int M, int K, void* stream);
 
+/* Fast form of qwen_b200_gemv_dev(): per 64-block one exact int32 dot
+ * product (the same int16 activation), then acc = fma(float(dot),
+ * 2^(e-134)*xs, acc) over a K segment and the segments added in order, so a
+ * matrix with few rows can be split along K across the whole GPU.
+ * Deterministic; differs from the reference float order by at most
+ * 1e-5 * sum_b |float(dot_b) * 2^(e_b-134) * xs_b| per row.  Needs K a
+ * multiple of 512, mant 16-, exps 4-, x 8-byte aligned.  No reference
+ * routine (the reference has only the NEON order). */
+QB_API int qwen_b200_gemv_fast_dev(float* y, const float* x, const int8_t* mant, const uint8_t* exps, int M,
+                                   int K, void* stream);
+
 /* Block-64 activation quantizer (quant_x_blocks, qwen_kernels_opt.c:182-205)
  * over B rows: x [B][K] -> xq int16 [B][K], xs [B][K/64]. */
 QB_API int qwen_b200_quant_dev(const float* x, int B, int K, int16_t* xq, float* xs, void* stream);
@@ -151,6 +162,12 @@ QB_API int qwen_b200_gemv_noalloc_dev(float* y, const float* x, const int8_t* ma
  * of one plan must not overlap on the GPU (they share its scratch). */
 QB_API int qwen_b200_stack_create(int n, const int8_t* const* mant, const uint8_t* const* exps,
                            const float* const* x, float* const* y, const int* M, const int* K);
+/* Same with flags: QB_STACK_FAST selects the fast arithmetic of
+ * qwen_b200_gemv_fast_dev() and lets rows of deep matrices be split into K
+ * segments (for stacks with few rows per GPU, e.g. row-sharded ones). */
+#define QB_STACK_FAST 1
+QB_API int qwen_b200_stack_create_ex(int n, const int8_t* const* mant, const uint8_t* const* exps,
+                              const float* const* x, float* const* y, const int* M, const int* K, int flags);
 QB_API int qwen_b200_stack_run(int plan, void* stream);
 QB_API int qwen_b200_stack_destroy(int plan);
 

@@ -37,6 +37,7 @@
 #include "topk.cuh"
 
 #include <algorithm>
+#include <cmath>
 #include <numeric>
 #include <vector>
 
@@ -130,17 +131,20 @@ __device__ __forceinline__ const GemvDesc& wdesc(const WArgs& A, int d) {
 // What a warp needs to know about a GEMV, copied to shared memory at start
 // so that mapping a claimed unit to its GEMV never touches global memory.
 struct SDesc {
-    int unit_begin, M, K, pad;
+    int unit_begin, M, K, nseg;
+    int seg_stages, pad0, pad1, pad2;
     const uint8_t* exps;
     const uint32_t* xp;
     const float* xs;
     const void* tmap;
     float* y;
+    float* partial;
+    unsigned int* tickets;
 };
 
 struct Unit {
     bool valid;
-    int d, r0, M, K, nb, nst;
+    int d, r0, M, K, nb, g, s, st0, st1;   // row group g, K segment s = stages [st0, st1)
     const uint8_t* exps;
     const uint32_t* xp;
     const float* xs;
@@ -157,12 +161,16 @@ __device__ __forceinline__ Unit load_unit(const SDesc* T, int n, int total_units
         else hi = mid - 1;
     }
     const SDesc& D = T[lo];
+    const int local = u - D.unit_begin;
     U.d = lo;
-    U.r0 = (u - D.unit_begin) * kRows;
+    U.g = local / D.nseg;
+    U.s = local - U.g * D.nseg;
+    U.r0 = U.g * kRows;
     U.M = D.M;
     U.K = D.K;
     U.nb = D.K >> 6;
-    U.nst = D.K >> 8;
+    U.st0 = U.s * D.seg_stages;
+    U.st1 = min(D.K >> 8, U.st0 + D.seg_stages);
     U.exps = D.exps;
     U.xp = D.xp;
     U.xs = D.xs;
@@ -179,6 +187,26 @@ template <bool LM>
 __device__ __forceinline__ void unit_result(const WArgs& A, const SDesc* T, const Unit& U, int lane, float yv,
                                             LmState& lm) {
     const int row = U.r0 + lane;
+    const SDesc& D = T[U.d];
+    if (!LM && D.nseg > 1) {
+        // fast mode, split row group: publish this segment's sums; the warp
+        // that completes the group adds the segments in order
+        if (row < U.M) D.partial[(size_t)U.s * U.M + row] = yv;
+        __threadfence();
+        __syncwarp();
+        unsigned int t = 0;
+        if (lane == 0) t = atomicAdd(&D.tickets[U.g], 1u);
+        t = __shfl_sync(0xffffffffu, t, 0);
+        if (t != (unsigned int)D.nseg - 1u) return;
+        __threadfence();
+        if (row < U.M) {
+            float sum = 0.0f;
+            for (int s = 0; s < D.nseg; s++) sum = __fadd_rn(sum, __ldcg(D.partial + (size_t)s * U.M + row));
+            D.y[row] = sum;
+        }
+        if (lane == 0) D.tickets[U.g] = 0u;
+        return;
+    }
     if (row >= U.M) return;
     if (LM) {
         if (yv > -1e30f) {
@@ -197,7 +225,7 @@ __device__ __forceinline__ void unit_result(const WArgs& A, const SDesc* T, cons
 // The 4 blocks of one stage for this lane's row: lane-class sums with
 // __dp2a, then the reference float steps into the four chains (or, for the
 // odd last row, the scalar form into fo).
-template <bool ODD>
+template <bool ODD, bool FAST>
 __device__ __forceinline__ void stage_blocks(const unsigned char* st, const uint4* xst, const float* xsst,
                                              uint32_t ew, int sw, bool odd, float& f0, float& f1, float& f2,
                                              float& f3, float& fo) {
@@ -225,7 +253,10 @@ __device__ __forceinline__ void stage_blocks(const unsigned char* st, const uint
         const int L0 = A0 + B0, L1 = A1 + B1, L2 = A2 + B2, L3 = A3 + B3;
         const uint32_t e = (ew >> (8 * jb)) & 0xFFu;
         const float xsb = xsst[jb];
-        if (!ODD || !odd) {
+        if (FAST) {
+            // one int32 dot per block, one fused multiply-add per block
+            f0 = __fmaf_rn(i2f_rn((L0 + L1) + (L2 + L3)), __fmul_rn(exp_scale_ieee(e), xsb), f0);
+        } else if (!ODD || !odd) {
             const float S = exp_scale_ftz(e);
             f0 = add_ftz(f0, mul_ftz(mul_ftz(i2f_rn(L0), S), xsb));
             f1 = add_ftz(f1, mul_ftz(mul_ftz(i2f_rn(L1), S), xsb));
@@ -237,7 +268,7 @@ __device__ __forceinline__ void stage_blocks(const unsigned char* st, const uint
     }
 }
 
-template <bool LM>
+template <bool LM, bool FAST>
 __global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_constant__ WArgs A) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -267,7 +298,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_con
         t.unit_begin = D.unit_begin;
         t.M = D.M;
         t.K = D.K;
-        t.pad = 0;
+        t.nseg = D.nseg;
+        t.seg_stages = D.seg_stages;
+        t.pad0 = t.pad1 = t.pad2 = 0;
+        t.partial = D.partial;
+        t.tickets = D.tickets;
         t.exps = D.exps;
         t.xp = D.xpairs;
         t.xs = D.xscale;
@@ -321,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_con
     claimed1 = nu_total;
     int ahead = claim();
     Unit pu = load_unit(sdesc, nd, nu_total, claimed0);
-    int ps = 0;
+    int ps = pu.valid ? pu.st0 : 0;
     if (lane == 0 && pu.valid) tma_prefetch_desc(sdesc[pu.d].tmap);
 
     // One stage: both weight boxes and the stage's activation slice (pairs +
@@ -357,13 +392,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_con
             }
             if (pu.r0 + lane < pu.M)
                 cp_async4(ering + slot * 128 + lane * 4, pu.exps + (size_t)(pu.r0 + lane) * pu.nb + ps * 4);
-            if (++ps == pu.nst) {
-                ps = 0;
+            if (++ps == pu.st1) {
                 kp++;
                 const int nu = ahead;
                 if (kp & 1) claimed1 = nu;
                 else claimed0 = nu;
                 pu = load_unit(sdesc, nd, nu_total, nu);
+                ps = pu.valid ? pu.st0 : 0;
                 ahead = claim();
             }
         }
@@ -388,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_con
 
     int kc = 0;
     Unit cu = load_unit(sdesc, nd, nu_total, claimed0);
-    int cs = 0;
+    int cs = cu.valid ? cu.st0 : 0;
     float f0 = 0.f, f1 = 0.f, f2 = 0.f, f3 = 0.f, fo = 0.f;
     const int sw = lane & 7;
     int i = 0;
@@ -400,23 +435,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_con
         __syncwarp();
         issue((i + kRing - 1) % kRing, true);
 
-        const bool odd_unit = (cu.M & 1) && (cu.r0 + kRows > cu.M - 1);   // the unit holds the odd last row
+        const bool odd_unit = !FAST && (cu.M & 1) && (cu.r0 + kRows > cu.M - 1);   // holds the odd last row
         const bool odd = odd_unit && (cu.r0 + lane == cu.M - 1);
         const uint32_t ew = *reinterpret_cast<const uint32_t*>(ering + slot * 128 + lane * 4);
         const unsigned char* st = ring + slot * kStage + lane * 128;
         const uint4* xst = reinterpret_cast<const uint4*>(xring + slot * kXp);
         const float* xsst = reinterpret_cast<const float*>(xring + slot * kXp + 512);
-        if (!odd_unit)
-            stage_blocks<false>(st, xst, xsst, ew, sw, false, f0, f1, f2, f3, fo);
+        if (FAST)
+            stage_blocks<false, true>(st, xst, xsst, ew, sw, false, f0, f1, f2, f3, fo);
+        else if (!odd_unit)
+            stage_blocks<false, false>(st, xst, xsst, ew, sw, false, f0, f1, f2, f3, fo);
         else
-            stage_blocks<true>(st, xst, xsst, ew, sw, odd, f0, f1, f2, f3, fo);
-        if (++cs == cu.nst) {
-            const float yv = odd ? fo : add_ftz(add_ftz(f0, f2), add_ftz(f1, f3));
+            stage_blocks<true, false>(st, xst, xsst, ew, sw, odd, f0, f1, f2, f3, fo);
+        if (++cs == cu.st1) {
+            const float yv = FAST ? f0 : (odd ? fo : add_ftz(add_ftz(f0, f2), add_ftz(f1, f3)));
             unit_result<LM>(A, sdesc, cu, lane, yv, lm);
             f0 = f1 = f2 = f3 = fo = 0.f;
-            cs = 0;
             kc++;
             cu = load_unit(sdesc, nd, nu_total, (kc & 1) ? claimed1 : claimed0);
+            cs = cu.valid ? cu.st0 : 0;
         }
         i++;
     }
@@ -537,8 +574,10 @@ static bool fast_shape_ok(const GemvDesc& d) {
     return true;
 }
 
-bool gemv_plan(GemvDesc* descs, int n, uint32_t* act, GemvPlan* plan) {
+bool gemv_plan(GemvDesc* descs, int n, uint32_t* act, GemvPlan* plan, int mode, size_t act_cap_words,
+               unsigned int* tickets, size_t tickets_cap) {
     if (n <= 0 || n > kMaxSDesc) return false;
+    const bool fast = mode == kFast;
     // largest K first: the counter then hands out the biggest units first
     std::vector<int> order(n);
     std::iota(order.begin(), order.end(), 0);
@@ -546,8 +585,43 @@ bool gemv_plan(GemvDesc* descs, int n, uint32_t* act, GemvPlan* plan) {
     std::vector<GemvDesc> sorted;
     sorted.reserve(n);
     for (int i : order) sorted.push_back(descs[i]);
+    // fast mode: split row groups into K segments so that every GEMV gets
+    // about its byte share of 2 units per warp slot
+    const double slots = 2.0 * num_sms() * kWarps;
+    double total_bytes = 0;
+    for (const GemvDesc& d : sorted) total_bytes += (double)d.M * d.K;
+    size_t pair_words = 0, part_words = 0, ticket_words = 0;
+    for (GemvDesc& d : sorted) {
+        const int groups = (d.M + kRows - 1) / kRows, nst = d.K >> 8;
+        int nseg = 1;
+        if (fast) {
+            // segments of >= 2 stages: the per-warp claim ring assumes its
+            // producer never runs more than one unit ahead
+            nseg = (int)std::ceil(slots * ((double)d.M * d.K / total_bytes) / groups);
+            nseg = std::max(1, std::min(nseg, nst / 2));
+        }
+        d.seg_stages = (nst + nseg - 1) / nseg;
+        d.nseg = (nst + d.seg_stages - 1) / d.seg_stages;
+        pair_words += (gemv_act_words(d.K) + 3) & ~size_t(3);
+        if (d.nseg > 1) {
+            part_words += (size_t)d.nseg * d.M;
+            ticket_words += (size_t)groups;
+        }
+    }
+    if (tickets) {   // counters live in the caller's separate zeroed buffer
+        if (ticket_words > tickets_cap) part_words = ticket_words = (size_t)-1 / 4;
+        else ticket_words = 0;
+    }
+    if (act_cap_words && pair_words + part_words + ticket_words > act_cap_words) {
+        // not enough scratch for the segment sums: whole rows
+        part_words = ticket_words = 0;
+        for (GemvDesc& d : sorted) {
+            d.nseg = 1;
+            d.seg_stages = d.K >> 8;
+        }
+    }
     int units = 0, kmax = 0;
-    size_t words = 0;
+    size_t words = 0, pw = pair_words, tw = pair_words + part_words;
     for (int i = 0; i < n; i++) {
         GemvDesc& d = sorted[i];
         if (!fast_shape_ok(d)) return false;
@@ -555,16 +629,25 @@ bool gemv_plan(GemvDesc* descs, int n, uint32_t* act, GemvPlan* plan) {
         d.unit_begin = units;
         d.xpairs = act ? act + words : nullptr;
         d.xscale = act ? reinterpret_cast<float*>(act + words + d.K / 2) : nullptr;
-        words += gemv_act_words(d.K);
-        words = (words + 3) & ~size_t(3);   // keep every pair block 16-byte aligned
-        units += (d.M + kRows - 1) / kRows;
+        words += (gemv_act_words(d.K) + 3) & ~size_t(3);   // keep every pair block 16-byte aligned
+        const int groups = (d.M + kRows - 1) / kRows;
+        d.partial = nullptr;
+        d.tickets = nullptr;
+        if (d.nseg > 1) {
+            d.partial = act ? reinterpret_cast<float*>(act + pw) : nullptr;
+            d.tickets = tickets ? tickets + (tw - pair_words - part_words) : (act ? act + tw : nullptr);
+            pw += (size_t)d.nseg * d.M;
+            tw += (size_t)groups;
+        }
+        units += groups * d.nseg;
         kmax = std::max(kmax, d.K);
     }
     for (int i = 0; i < n; i++) descs[i] = sorted[i];
     plan->n = n;
     plan->total_units = units;
     plan->kmax = kmax;
-    plan->act_words = words;
+    plan->fast = fast;
+    plan->act_words = pair_words + part_words + ticket_words;
     return true;
 }
 
@@ -574,13 +657,13 @@ static cudaError_t launch_prep(const PrepArgs& P, int nchunks, cudaStream_t stre
     return cudaGetLastError();
 }
 
-template <bool LM>
+template <bool LM, bool FAST>
 static cudaError_t launch_warp(const WArgs& A, int grid, cudaStream_t stream) {
     const size_t smem = warp_smem_bytes(LM, A.n);
     static size_t configured = 0;   // largest dynamic smem size set so far
     if (smem > configured) {
-        cudaError_t err = cudaFuncSetAttribute(gemv_warp_kernel<LM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)smem);
+        cudaError_t err = cudaFuncSetAttribute(gemv_warp_kernel<LM, FAST>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (err != cudaSuccess) return err;
         configured = smem;
     }
@@ -594,7 +677,7 @@ static cudaError_t launch_warp(const WArgs& A, int grid, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemv_warp_kernel<LM>, A);
+    return cudaLaunchKernelEx(&cfg, gemv_warp_kernel<LM, FAST>, A);
 }
 
 cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, unsigned int* ctr,
@@ -612,7 +695,29 @@ cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, un
     A.ctr = ctr;
     A.err = err;
     const int grid = std::min(num_sms(), (plan.total_units + kWarps - 1) / kWarps);
-    return launch_warp<false>(A, grid, stream);
+    return plan.fast ? launch_warp<false, true>(A, grid, stream) : launch_warp<false, false>(A, grid, stream);
+}
+
+cudaError_t launch_gemv_fast(const GemvDesc& d0, uint32_t* act, size_t act_cap_words, unsigned int* tickets,
+                             size_t tickets_cap, unsigned int* err, cudaStream_t stream) {
+    if (d0.M <= 0) return cudaSuccess;
+    GemvDesc d = d0;
+    GemvPlan plan;
+    if (!act || !tickets || !gemv_plan(&d, 1, act, &plan, kFast, act_cap_words, tickets, tickets_cap))
+        return cudaErrorInvalidValue;
+    PrepArgs P{};
+    P.single = d;
+    P.n = 1;
+    cudaError_t e = launch_prep(P, (d.K / 64 + 63) / 64, stream);
+    if (e != cudaSuccess) return e;
+    WArgs A{};
+    A.single = d;
+    A.n = 1;
+    A.total_units = plan.total_units;
+    A.ctr = nullptr;
+    A.err = err;
+    const int grid = std::min(num_sms(), (plan.total_units + kWarps - 1) / kWarps);
+    return launch_warp<false, true>(A, grid, stream);
 }
 
 cudaError_t launch_gemv(const GemvDesc& d0, uint32_t* act, unsigned int* err, cudaStream_t stream) {
@@ -641,7 +746,7 @@ cudaError_t launch_gemv(const GemvDesc& d0, uint32_t* act, unsigned int* err, cu
     A.ctr = nullptr;
     A.err = err;
     const int grid = std::min(num_sms(), (plan.total_units + kWarps - 1) / kWarps);
-    return launch_warp<false>(A, grid, stream);
+    return launch_warp<false, false>(A, grid, stream);
 }
 
 cudaError_t launch_bfp8_lm_head(const float* h, const int8_t* mant, const uint8_t* exps, int vocab,
@@ -679,7 +784,7 @@ cudaError_t launch_bfp8_lm_head(const float* h, const int8_t* mant, const uint8_
     A.out_ids = out_ids;
     A.out_scores = out_scores;
     A.out_n = out_n;
-    return launch_warp<true>(A, grid, stream);
+    return launch_warp<true, false>(A, grid, stream);
 }
 
 cudaError_t launch_quant_block64(const float* x, int B, int K, int16_t* xq, float* xs,

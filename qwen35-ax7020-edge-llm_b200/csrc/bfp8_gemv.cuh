@@ -21,9 +21,13 @@ struct alignas(64) GemvDesc {
     float* y;
     uint32_t* xpairs;       // planner: where the paired int16 activation goes (K/2 words)
     float* xscale;          // planner: its block scales (K/64)
+    float* partial;         // planner (fast mode): nseg x M fp32 segment sums
+    unsigned int* tickets;  // planner (fast mode): one zero-initialised counter per 32-row group
     int M;
     int K;
-    int unit_begin;         // planner: first 32-row work unit of this GEMV
+    int unit_begin;         // planner: first work unit of this GEMV
+    int nseg;               // planner: K segments per row group (1 = whole rows)
+    int seg_stages;         // planner: 256-byte columns per segment
     int pad_;
 };
 
@@ -34,8 +38,18 @@ struct GemvPlan {
     int n;
     int total_units;
     int kmax;
-    size_t act_words;       // 32-bit words of activation scratch the plan needs
+    bool fast;
+    size_t act_words;       // 32-bit words of scratch the plan needs (zeroed once before first use)
 };
+
+// Arithmetic of a launch.
+//   exact: the reference NEON float order, bit for bit (one warp streams
+//          each 32-row group end to end).
+//   fast:  per block one int32 dot, acc = fma(float(dot), 2^(e-134)*xs, acc)
+//          within a K segment, segments summed in order; rows may be split
+//          into K segments so that short, deep matrices fill the GPU.
+//          Deterministic; |y - exact| <= 1e-5 * sum_b |term_b|.
+enum GemvMode { kExact = 0, kFast = 1 };
 
 // Activation scratch (32-bit words) one GEMV of depth K needs.
 size_t gemv_act_words(int K);
@@ -48,7 +62,11 @@ size_t gemv_act_words(int K);
 // passed; at most 160 descriptors.  Returns false if a shape is not served
 // by the fast kernel (K % 512 != 0 or misaligned pointers) or a tensor map
 // cannot be encoded.
-bool gemv_plan(GemvDesc* descs, int n, uint32_t* act, GemvPlan* plan);
+// Fast mode keeps one counter per split row group: in `act` after the
+// segment sums, or, when `tickets` is given, in that separate zeroed buffer
+// of tickets_cap words (for scratch that other launches also write).
+bool gemv_plan(GemvDesc* descs, int n, uint32_t* act, GemvPlan* plan, int mode = kExact,
+               size_t act_cap_words = 0, unsigned int* tickets = nullptr, size_t tickets_cap = 0);
 
 // Grouped exact GEMV over a planned, device-resident descriptor array.
 // `ctr` is a 2-word device counter pair owned by the plan (zero before the
@@ -60,6 +78,12 @@ cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, un
 // One exact GEMV (any M >= 1, K a positive multiple of 64, any alignment).
 // `act` is device scratch of gemv_act_words(K) words.
 cudaError_t launch_gemv(const GemvDesc& d, uint32_t* act, unsigned int* err, cudaStream_t stream);
+
+// Fast-mode single GEMV (K % 512 == 0, aligned pointers); `act` holds
+// act_cap_words words of scratch, `tickets` tickets_cap zeroed counters
+// (every launch leaves them zero).
+cudaError_t launch_gemv_fast(const GemvDesc& d, uint32_t* act, size_t act_cap_words, unsigned int* tickets,
+                             size_t tickets_cap, unsigned int* err, cudaStream_t stream);
 
 // BFP8 lm_head: scores = bfp8_gemv(h), fused argmax (ties -> lowest id, best
 // must beat -1e30) and top-k (k <= 1024; score desc, ties ascending id).

@@ -193,7 +193,9 @@ struct DevState {
     qb::LmScratch* scratch = nullptr;
     unsigned int* err = nullptr;
     uint32_t* act = nullptr;       // paired-activation scratch of single-GEMV launches
+    unsigned int* tickets = nullptr;   // zeroed split-K counters of fast single-GEMV launches
 };
+constexpr size_t kTicketWords = 16384;
 constexpr size_t kActScratchWords = 128 * 1024;   // serves K <= 253952
 
 int dev_state(DevState** out) {
@@ -214,9 +216,14 @@ int dev_state(DevState** out) {
         if ((e = cudaMemset(w, 0, sizeof(unsigned int))) != cudaSuccess) return fail(QB_ECUDA, "error word clear", e);
         uint32_t* a = nullptr;
         if ((e = cudaMalloc(&a, kActScratchWords * 4)) != cudaSuccess) return fail(QB_ENOMEM, "act scratch alloc", e);
+        if ((e = cudaMemset(a, 0, kActScratchWords * 4)) != cudaSuccess) return fail(QB_ECUDA, "act scratch clear", e);
+        unsigned int* tk = nullptr;
+        if ((e = cudaMalloc(&tk, kTicketWords * 4)) != cudaSuccess) return fail(QB_ENOMEM, "ticket alloc", e);
+        if ((e = cudaMemset(tk, 0, kTicketWords * 4)) != cudaSuccess) return fail(QB_ECUDA, "ticket clear", e);
         st.scratch = p;
         st.err = w;
         st.act = a;
+        st.tickets = tk;
     }
     *out = &st;
     return QB_OK;
@@ -503,14 +510,34 @@ int qwen_b200_gemv_q_dev(float* y, const int16_t* xq, const float* xs, const int
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_gemv_q_dev", e);
 }
 
+int qwen_b200_gemv_fast_dev(float* y, const float* x, const int8_t* mant, const uint8_t* exps, int M, int K,
+                            void* stream) {
+    if (int rc = check_gemv_args(y, x, mant, exps, M, K)) return rc;
+    if (M == 0) return QB_OK;
+    qb::GemvDesc d{};
+    d.mant = mant;
+    d.exps = exps;
+    d.x = x;
+    d.y = y;
+    d.M = M;
+    d.K = K;
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    cudaError_t e = qb::launch_gemv_fast(d, st->act, kActScratchWords, st->tickets, kTicketWords, st->err,
+                                         static_cast<cudaStream_t>(stream));
+    if (e == cudaErrorInvalidValue)
+        return fail(QB_EINVAL, "gemv_fast: K must be a multiple of 512, mant/exps/x 16/4/8-byte aligned");
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_gemv_fast_dev", e);
+}
+
 int qwen_b200_quant_dev(const float* x, int B, int K, int16_t* xq, float* xs, void* stream) {
     if (!x || !xq || !xs || B < 0 || K <= 0 || K % 64) return fail(QB_EINVAL, "qwen_b200_quant_dev: bad arguments");
     cudaError_t e = qb::launch_quant_block64(x, B, K, xq, xs, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_quant_dev", e);
 }
 
-int qwen_b200_stack_create(int n, const int8_t* const* mant, const uint8_t* const* exps, const float* const* x,
-                           float* const* y, const int* M, const int* K) {
+int qwen_b200_stack_create_ex(int n, const int8_t* const* mant, const uint8_t* const* exps, const float* const* x,
+                              float* const* y, const int* M, const int* K, int flags) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (n <= 0 || !mant || !exps || !x || !y || !M || !K) return fail(QB_EINVAL, "stack: bad arguments");
     std::vector<qb::GemvDesc> v;
@@ -528,14 +555,17 @@ int qwen_b200_stack_create(int n, const int8_t* const* mant, const uint8_t* cons
         v.push_back(d);
     }
     StackPlan sp;
-    if (!qb::gemv_plan(v.data(), (int)v.size(), nullptr, &sp.plan))
+    const int mode = (flags & QB_STACK_FAST) ? qb::kFast : qb::kExact;
+    if (!qb::gemv_plan(v.data(), (int)v.size(), nullptr, &sp.plan, mode))
         return fail(QB_EINVAL, "stack: 1..160 GEMVs, every K a multiple of 512, mant/exps/x 16/4/8-byte aligned");
     cudaError_t e = cudaMalloc(&sp.act, sp.plan.act_words * 4 + 16);
     if (e != cudaSuccess) return fail(QB_ENOMEM, "stack act alloc", e);
     if ((e = cudaMalloc(&sp.ctr, 2 * sizeof(unsigned int))) != cudaSuccess) return fail(QB_ENOMEM, "stack ctr alloc", e);
     if ((e = cudaMemset(sp.ctr, 0, 2 * sizeof(unsigned int))) != cudaSuccess)
         return fail(QB_ECUDA, "stack ctr clear", e);
-    qb::gemv_plan(v.data(), (int)v.size(), sp.act, &sp.plan);
+    if ((e = cudaMemset(sp.act, 0, sp.plan.act_words * 4 + 16)) != cudaSuccess)
+        return fail(QB_ECUDA, "stack act clear", e);
+    qb::gemv_plan(v.data(), (int)v.size(), sp.act, &sp.plan, mode);
     e = cudaMalloc(&sp.dev_descs, sizeof(qb::GemvDesc) * (v.size() ? v.size() : 1));
     if (e != cudaSuccess) return fail(QB_ENOMEM, "stack alloc", e);
     e = cudaMemcpy(sp.dev_descs, v.data(), sizeof(qb::GemvDesc) * v.size(), cudaMemcpyHostToDevice);
@@ -543,6 +573,11 @@ int qwen_b200_stack_create(int n, const int8_t* const* mant, const uint8_t* cons
     sp.live = true;
     g_plans.push_back(sp);
     return (int)g_plans.size();
+}
+
+int qwen_b200_stack_create(int n, const int8_t* const* mant, const uint8_t* const* exps, const float* const* x,
+                           float* const* y, const int* M, const int* K) {
+    return qwen_b200_stack_create_ex(n, mant, exps, x, y, M, K, 0);
 }
 
 int qwen_b200_stack_run(int plan, void* stream) {

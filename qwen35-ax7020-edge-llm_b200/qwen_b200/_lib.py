@@ -33,9 +33,11 @@ SIGNATURES = {
     "qwen_b200_reset_weights": (None, []),
     "qwen_b200_gemv_dev": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "qwen_b200_gemv_noalloc_dev": (_I, [_P, _P, _P, _P, _I, _I, _P]),
+    "qwen_b200_gemv_fast_dev": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "qwen_b200_gemv_q_dev": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
     "qwen_b200_quant_dev": (_I, [_P, _I, _I, _P, _P, _P]),
     "qwen_b200_stack_create": (_I, [_I, _P, _P, _P, _P, _P, _P]),
+    "qwen_b200_stack_create_ex": (_I, [_I, _P, _P, _P, _P, _P, _P, _I]),
     "qwen_b200_stack_run": (_I, [_I, _P]),
     "qwen_b200_stack_destroy": (_I, [_I]),
     "qwen_b200_lm_head_bf16_dev": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P, _P]),

@@ -22,7 +22,7 @@ import torch
 from ._lib import KernelError, check, load
 
 __all__ = [
-    "KernelError", "quant_block64", "bfp8_gemv", "bfp8_gemv_q", "lm_head_bf16", "lm_head_bfp8",
+    "KernelError", "quant_block64", "bfp8_gemv", "bfp8_gemv_fast", "bfp8_gemv_q", "lm_head_bf16", "lm_head_bfp8",
     "pack_bfp8", "LinearStack", "LmResult",
 ]
 
@@ -69,6 +69,18 @@ def bfp8_gemv(x: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor, out: torc
     for i in range(rows.shape[0]):
         check(L.qwen_b200_gemv_dev(_ptr(yr[i]), _ptr(rows[i]), _ptr(mant), _ptr(exps), M, K, _stream()),
               "bfp8_gemv")
+    return y
+
+
+def bfp8_gemv_fast(x: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor, out: torch.Tensor | None = None):
+    """Fast-mode GEMV (split-K, fused multiply-add per block); within
+    1e-5 * sum|terms| of bfp8_gemv.  x fp32 [K]; K a multiple of 512."""
+    x = _need(x, torch.float32, "x")
+    mant = _need(mant, torch.int8, "mant")
+    exps = _need(exps, torch.uint8, "exps")
+    M, K = mant.shape
+    y = out if out is not None else torch.empty(M, dtype=torch.float32, device=x.device)
+    check(load().qwen_b200_gemv_fast_dev(_ptr(y), _ptr(x), _ptr(mant), _ptr(exps), M, K, _stream()), "bfp8_gemv_fast")
     return y
 
 
@@ -154,7 +166,7 @@ class LinearStack:
     is safe inside CUDA graph capture.
     """
 
-    def __init__(self, items):
+    def __init__(self, items, fast: bool = False):
         n = len(items)
         P = ctypes.c_void_p * n
         I = ctypes.c_int * n
@@ -165,7 +177,7 @@ class LinearStack:
         ys = P(*[_ptr(y) for (_, _, _, y) in items])
         Ms = I(*[m.shape[0] for (_, m, _, _) in items])
         Ks = I(*[m.shape[1] for (_, m, _, _) in items])
-        h = load().qwen_b200_stack_create(n, mant, exps, xs, ys, Ms, Ks)
+        h = load().qwen_b200_stack_create_ex(n, mant, exps, xs, ys, Ms, Ks, 1 if fast else 0)
         if h <= 0:
             check(h, "LinearStack")
         self.handle = h

@@ -1,0 +1,204 @@
+"""Output-row-sharded BFP8 linear stack over several GPUs (one process per GPU).
+
+Every GEMV's rows are split into contiguous slices, one per rank, with slice
+boundaries on multiples of 64 rows.  Each rank streams only its slice of the
+weights (the exact kernel, so its rows are bit-identical to an unsharded
+run) and an all-gather over NCCL rebuilds the full output vector in every
+rank's own memory before the next GEMV reads it.  The data flow of one
+scaled MLP layer (gate / up ffn x hidden, down hidden x ffn): gate and up
+read the layer input; down reads the gathered gate output (the element-wise
+SwiGLU between them is glue outside this path); the next layer reads the
+gathered down output.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+from . import model
+
+
+def shard_rows(M: int, world: int, rank: int, align: int = 64) -> tuple[int, int]:
+    """Rows [r0, r1) of an M-row matrix owned by `rank`: contiguous slices
+    whose boundaries are multiples of `align` (the last rank takes the rest)."""
+    blocks = (M + align - 1) // align
+    b0 = blocks * rank // world
+    b1 = blocks * (rank + 1) // world
+    return min(M, b0 * align), min(M, b1 * align)
+
+
+@dataclass(frozen=True)
+class LayerPlan:
+    """The three GEMVs of one scaled MLP layer."""
+    gate: model.Linear
+    up: model.Linear
+    down: model.Linear
+
+
+def scaled_layers(layers=8, hidden=8192, ffn=28672) -> list[LayerPlan]:
+    s = model.scaled_stack(layers, hidden, ffn)
+    return [LayerPlan(s[3 * i], s[3 * i + 1], s[3 * i + 2]) for i in range(layers)]
+
+
+def run_layers(layers, x0, gemv, all_gather, world, rank):
+    """Reference data flow, independent of the device: `gemv(name, x_full,
+    r0, r1) -> y_shard` computes rows [r0, r1) of a GEMV, `all_gather(y_shard,
+    M) -> y_full` concatenates the rank slices.  Returns every gathered
+    output in order (gate, up, down per layer)."""
+    outs = []
+    x = x0
+    for L in layers:
+        g0, g1 = shard_rows(L.gate.M, world, rank)
+        u0, u1 = shard_rows(L.up.M, world, rank)
+        d0, d1 = shard_rows(L.down.M, world, rank)
+        gate = all_gather(gemv(L.gate.name, x, g0, g1), L.gate.M)
+        up = all_gather(gemv(L.up.name, x, u0, u1), L.up.M)
+        down = all_gather(gemv(L.down.name, gate, d0, d1), L.down.M)
+        outs += [gate, up, down]
+        x = down
+    return outs
+
+
+class ShardedDeviceStack:
+    """This rank's weight slices of a scaled stack on its GPU, plus the
+    gather buffers, driven by grouped launches and NCCL all-gathers.
+
+    `fast` selects the split-K arithmetic (see ops.bfp8_gemv_fast), which
+    keeps every GPU busy when each holds few rows.  Weights are fp32 N(0, 0.02) drawn per tensor from a seeded generator on
+    the device (the same full matrix on every rank), packed, and sliced; only
+    the slice is kept.  `copies` byte-identical copies of the slices rotate
+    across steps so that timing never finds them in L2.
+    """
+
+    def __init__(self, layers, world, rank, device, copies=1, seed=0, group=None, fast=False):
+        import torch
+
+        from . import ops
+
+        self.layers = list(layers)
+        self.world, self.rank, self.group = world, rank, group
+        self.fast = fast
+        self.device = torch.device(device)
+        self.shards = {}   # name -> (r0, r1)
+        slices = []        # (name, r0, r1, K)
+        for L in self.layers:
+            for t in (L.gate, L.up, L.down):
+                r0, r1 = shard_rows(t.M, world, rank)
+                self.shards[t.name] = (r0, r1)
+                slices.append((t, r0, r1))
+        # one buffer per copy holding every slice (SoA, 64-byte aligned)
+        offs, off = {}, 0
+        for t, r0, r1 in slices:
+            off = model.align64(off)
+            rows = r1 - r0
+            offs[t.name] = off
+            off += rows * t.K + model.align64(rows * t.K // 64)
+        self.nbytes = model.align64(off)
+        base = torch.empty(max(self.nbytes, 64), dtype=torch.uint8, device=self.device)
+        g = torch.Generator(device=self.device)
+        for i, (t, r0, r1) in enumerate(slices):
+            g.manual_seed(seed * 1000 + i)
+            w = torch.randn((t.M, t.K), generator=g, device=self.device, dtype=torch.float32) * 0.02
+            mant, exps = ops.pack_bfp8(w)
+            del w
+            rows = r1 - r0
+            o = offs[t.name]
+            base[o:o + rows * t.K].view(torch.int8).view(rows, t.K).copy_(mant[r0:r1])
+            base[o + rows * t.K:o + rows * t.K + rows * t.K // 64].view(rows, t.K // 64).copy_(exps[r0:r1])
+            del mant, exps
+        self.offs = offs
+        self.buffers = [base] + [base.clone() for _ in range(copies - 1)]
+        gx = torch.Generator(device=self.device)
+        gx.manual_seed(seed + 7)
+        L0 = self.layers[0]
+        self.x0 = torch.randn(L0.gate.K, generator=gx, device=self.device, dtype=torch.float32)
+        # gathered outputs (full vectors, every rank) and this rank's slices
+        self.full = {t.name: torch.zeros(t.M, dtype=torch.float32, device=self.device)
+                     for L in self.layers for t in (L.gate, L.up, L.down)}
+        self.part = {t.name: torch.zeros(self.padded_rows(t.M), dtype=torch.float32, device=self.device)
+                     for L in self.layers for t in (L.gate, L.up, L.down)}
+        self.gath = {t.name: torch.zeros(self.padded_rows(t.M) * world, dtype=torch.float32, device=self.device)
+                     for L in self.layers for t in (L.gate, L.up, L.down)}
+        self.plans = [self._plans(c) for c in range(copies)]
+
+    def padded_rows(self, M):
+        """Every rank contributes the same count to the all-gather: the
+        largest slice, rounded up to 64."""
+        return max(r1 - r0 for r0, r1 in (shard_rows(M, self.world, r) for r in range(self.world)))
+
+    def weight(self, copy, t):
+        import torch
+
+        r0, r1 = self.shards[t.name]
+        rows = r1 - r0
+        o = self.offs[t.name]
+        buf = self.buffers[copy]
+        mant = buf[o:o + rows * t.K].view(torch.int8).view(rows, t.K)
+        exps = buf[o + rows * t.K:o + rows * t.K + rows * t.K // 64].view(rows, t.K // 64)
+        return mant, exps
+
+    def _plans(self, copy):
+        """Per layer: one grouped launch for gate+up (same input), one for down."""
+        from . import ops
+
+        plans = []
+        x = self.x0
+
+        def out(t, rows):   # a single rank writes straight into the full vector
+            return self.full[t.name] if self.world == 1 else self.part[t.name][:rows]
+
+        for L in self.layers:
+            gu = []
+            for t in (L.gate, L.up):
+                mant, exps = self.weight(copy, t)
+                r0, r1 = self.shards[t.name]
+                if r1 > r0:
+                    gu.append((x, mant, exps, out(t, r1 - r0)))
+            mant, exps = self.weight(copy, L.down)
+            r0, r1 = self.shards[L.down.name]
+            dn = [(self.full[L.gate.name], mant, exps, out(L.down, r1 - r0))] if r1 > r0 else []
+            plans.append((ops.LinearStack(gu, fast=self.fast) if gu else None,
+                          ops.LinearStack(dn, fast=self.fast) if dn else None))
+            x = self.full[L.down.name]
+        return plans
+
+    def _gather(self, t):
+        import torch.distributed as dist
+
+        part, gath, full = self.part[t.name], self.gath[t.name], self.full[t.name]
+        if self.world == 1:
+            return
+        if part.numel() * self.world == t.M:   # equal slices: gather straight into place
+            dist.all_gather_into_tensor(full, part, group=self.group)
+            return
+        dist.all_gather_into_tensor(gath, part, group=self.group)
+        P = part.numel()
+        for r in range(self.world):
+            r0, r1 = shard_rows(t.M, self.world, r)
+            if r1 > r0:
+                full[r0:r1].copy_(gath[r * P: r * P + (r1 - r0)])
+
+    def step(self, copy=0):
+        """One token through every layer (grouped GEMV launches + gathers)."""
+        for L, (gu, dn) in zip(self.layers, self.plans[copy]):
+            if gu is not None:
+                gu.run()
+            self._gather(L.gate)
+            self._gather(L.up)
+            if dn is not None:
+                dn.run()
+            self._gather(L.down)
+
+    def bytes_per_step(self):
+        """Algorithmic bytes of one token over ALL ranks: the full weights
+        once, plus the fp32 activation in and output out of every GEMV."""
+        tot = 0
+        for L in self.layers:
+            for t in (L.gate, L.up, L.down):
+                tot += t.M * t.K + t.M * t.K // 64 + 4 * t.K + 4 * t.M
+        return tot
+
+    def close(self):
+        for gu, dn in (p for plans in self.plans for p in plans):
+            for s in (gu, dn):
+                if s is not None:
+                    s.close()

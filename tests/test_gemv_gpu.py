@@ -202,3 +202,47 @@ def test_device_packer_matches_reference_rule(cuda, golden):
         assert np.array_equal(mant.cpu().numpy(), g[f"{name}_mant"]), name
         e = g[f"{name}_exps_padded"][: exps.numel()]
         assert np.array_equal(exps.cpu().numpy().reshape(-1), e), name
+
+
+# ------------------------------------------------------------------ fast mode
+def term_magnitude(x, mant, exps):
+    """sum_b |float(dot_b) * 2^(e_b-134) * xs_b| per row (float64)."""
+    xq, xs = O.quant_x(x)
+    d = O.block_dots(mant, xq).astype(np.float64)
+    return (np.abs(d) * np.ldexp(1.0, exps.astype(np.int64) - 134) * xs.astype(np.float64)).sum(axis=1)
+
+
+@pytest.mark.parametrize("M,K", [(3584, 1024), (1024, 3584), (8192, 28672 // 4), (33, 2048), (1, 512)])
+def test_gemv_fast_within_tolerance_and_deterministic(cuda, M, K):
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(M + 3 * K)
+    mant, exps = rand_weights(rng, M, K)
+    x = rng.normal(0, 1, K).astype(np.float32)
+    dx, dm, de = to_dev(x, mant, exps)
+    y1 = ops.bfp8_gemv_fast(dx, dm, de).cpu().numpy()
+    y2 = ops.bfp8_gemv_fast(dx, dm, de).cpu().numpy()
+    assert np.array_equal(bits(y1), bits(y2))
+    ref = O.bfp8_gemv(x, mant, exps).astype(np.float64)
+    tol = 1e-5 * term_magnitude(x, mant, exps) + 1e-30
+    assert (np.abs(y1 - ref) <= tol).all()
+
+
+def test_linear_stack_fast_within_tolerance(cuda):
+    import torch
+
+    from qwen_b200 import model, ops
+
+    shapes = [model.Linear(f"t{i}", M, K) for i, (M, K) in enumerate([(8192, 7168), (2048, 1024), (512, 3584)])]
+    st = model.DeviceStack(shapes, copies=1, seed=12)
+    items = st.views(0)
+    stack = ops.LinearStack(items, fast=True)
+    for _ in range(2):   # the second run starts from the first run's tickets
+        stack.run()
+    torch.cuda.synchronize()
+    for x, mant, exps, y in items:
+        xn, mn, en = x.cpu().numpy(), mant.cpu().numpy(), exps.cpu().numpy()
+        ref = O.bfp8_gemv(xn, mn, en).astype(np.float64)
+        tol = 1e-5 * term_magnitude(xn, mn, en) + 1e-30
+        assert (np.abs(y.cpu().numpy() - ref) <= tol).all()
+    stack.close()
