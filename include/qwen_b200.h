@@ -171,6 +171,38 @@ QB_API int qwen_b200_stack_create_ex(int n, const int8_t* const* mant, const uin
 QB_API int qwen_b200_stack_run(int plan, void* stream);
 QB_API int qwen_b200_stack_destroy(int plan);
 
+/* ---- Batched decode on the tensor cores (B sequences share the weights).
+ * Activations are int16 block-64 values stored as two int8 planes,
+ * xq = 256*hi + lo (hi = xq >> 8 signed, lo = xq & 255 unsigned):
+ * planes [2][B][K] bytes (plane 0 = hi, plane 1 = lo), 16-byte aligned, and
+ * block scales xs_t [K/64][ldxs] fp32 (block-major, ldxs >= B, ldxs % 4 == 0).
+ * The reference decodes one sequence at a time; these entry points have no
+ * reference counterpart.  The block dots are exact; each output is the
+ * exact sum_b dot_b * 2^(e_b-134) * xs_b up to one f32 rounding per block,
+ * and agrees with bfp8_gemv() on that batch row to 1e-5 of the magnitude of
+ * the reference's own lane-class terms, sum_{b,j} |L_j * 2^(e_b-134) * xs_b|. */
+
+/* fp32 x [B][K] -> planes + xs_t with quant_x_blocks' arithmetic
+ * (qwen_kernels_opt.c:182-205): 256*hi + lo equals its xq bit for bit. */
+QB_API int qwen_b200_quant_planes_dev(const float* x, int B, int K, int8_t* planes, float* xs_t, int ldxs,
+                                      void* stream);
+
+/* y [B][M] = W (BFP8 [M][K], mant 16-byte aligned) x activations, on
+ * tcgen05 kind::i8 (exact int32 block dots, hi and lo accumulators).  If
+ * dots is not null the exact block dots are also written to it
+ * ([B][M][K/64] int32, a verification aid; slower). */
+QB_API int qwen_b200_gemm_tc_dev(float* y, const int8_t* planes, const float* xs_t, int ldxs, const int8_t* mant,
+                                 const uint8_t* exps, int M, int K, int B, int32_t* dots, void* stream);
+
+/* Grouped batched launch of n independent GEMMs with a common B and ldxs
+ * (e.g. the per-step linear stack of B sequences).  HOST arrays of DEVICE
+ * pointers; returns a plan handle (>= 1) or a QB_E* code.  1 <= n <= 4096. */
+QB_API int qwen_b200_tc_stack_create(int n, const int8_t* const* mant, const uint8_t* const* exps,
+                                     const int8_t* const* planes, const float* const* xs_t, float* const* y,
+                                     const int* M, const int* K, int B, int ldxs);
+QB_API int qwen_b200_tc_stack_run(int plan, void* stream);
+QB_API int qwen_b200_tc_stack_destroy(int plan);
+
 /* bf16 lm_head over E [vocab][hidden] (tied embedding).  Always writes the
  * greedy id to out_id[0]; for k > 0 also the top-k into out_ids/out_scores
  * and its length into out_n[0].  k <= 1024.  Device form of

@@ -1,0 +1,61 @@
+// bfp8_gemm_tc.cuh -- batched BFP8 GEMM on the tcgen05 tensor cores (sm_100a).
+//
+// Batched decode runs B sequences through the same weights, so each weight
+// row meets B activation rows: a dense int8 contraction.  The int16 block-64
+// activations (xq in [-16384, 16384], one f32 scale per 64-block) are stored
+// as two int8 planes, xq = 256*hi + lo with hi = xq >> 8 (signed, -64..64)
+// and lo = xq & 255 (unsigned), so the tensor cores compute both halves of
+// every block dot exactly in int32 (tcgen05.mma kind::i8, signed x signed and
+// signed x unsigned) and the epilogue recombines D = 256*Dhi + Dlo -- the same
+// integer the batch-1 kernel forms with dp2a.  Per block the epilogue adds
+// float(D) * 2^(e-134) * xs to an f32 accumulator (order: blocks ascending,
+// one fused multiply-add each), which agrees with the reference's NEON
+// combine to a few ulp of the sum of |terms|.
+//
+// Activation layout ("planar int16"): planes [2][B][K] bytes (plane 0 = hi,
+// plane 1 = lo) and block scales xs_t [K/64][ldxs] f32 (block-major, so one
+// TMA box brings a stage's scales for a tile of batch columns).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace qb {
+
+// One GEMM of a (grouped) launch: y[B][M] = W[M][K] (BFP8) x X[B][K] (planar int16).
+struct alignas(128) TcDesc {
+    CUtensorMap tm_w;       // mantissas [M][K] u8, box 128 rows x 128 B, SWIZZLE_128B
+    CUtensorMap tm_x;       // planes [2][B][K] u8, box 128 B x N rows x 2 planes, SWIZZLE_128B
+    CUtensorMap tm_s;       // scales [nb][ldxs] f32, box N columns x 2 blocks
+    const uint8_t* exps;    // [M][nb]
+    float* y;               // [B][M]
+    int32_t* dots;          // optional [B][M][nb]: exact block dots (verification)
+    int M, K, B, nb;
+    int unit_begin;         // first unit (row tile x column tile) of this GEMM
+    int n_nt;               // column tiles per row tile
+    int pad_[2];
+};
+
+// Column-tile width used for a batch of B rows (8, 16, 32, 64 or 128).
+int tc_tile_n(int B);
+
+// Fill `d` (host memory); false if a pointer, stride or size breaks the
+// kernel's alignment rules.
+bool tc_make_desc(TcDesc* d, float* y, const void* planes, const float* xs_t, int ldxs, const int8_t* mant,
+                  const uint8_t* exps, int M, int K, int B, int32_t* dots);
+
+// Units (tiles) of one descriptor after tc_make_desc.
+int tc_units(const TcDesc& d);
+
+// Launch: `dev_descs` (device array of n descriptors with unit_begin set,
+// largest K first) or, when it is null, the single descriptor `one`.  With
+// `dots` the kernel also writes every exact block dot to desc.dots.
+cudaError_t launch_gemm_tc(const TcDesc* dev_descs, const TcDesc* one, int n, int total_units, int B, bool dots,
+                           unsigned int* err, cudaStream_t stream);
+
+// fp32 [B][K] -> planes [2][B][K] + xs_t [K/64][ldxs], the reference
+// quantizer's arithmetic (bit-exact xq and scales).
+cudaError_t launch_quant_planes(const float* x, int B, int K, void* planes, float* xs_t, int ldxs,
+                                cudaStream_t stream);
+
+}  // namespace qb

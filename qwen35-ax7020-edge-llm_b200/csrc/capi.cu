@@ -4,6 +4,7 @@
 // conventions (04-板载脚本与工具/qwen_kernels_opt.c, qwen_sampling.c) and run
 // the work on the device; the _dev entry points take device pointers and a
 // stream and are what the PyTorch operators and the benchmarks call.
+#include "bfp8_gemm_tc.cuh"
 #include "bfp8_gemv.cuh"
 #include "common.cuh"
 #include "lm_head.cuh"
@@ -11,6 +12,7 @@
 
 #include "qwen_b200.h"
 
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstdio>
@@ -162,6 +164,14 @@ struct StackPlan {
     bool live = false;
 };
 std::vector<StackPlan> g_plans;
+
+// Grouped batched tensor-core plans.
+struct TcPlan {
+    qb::TcDesc* dev_descs = nullptr;
+    int n = 0, total_units = 0, B = 0;
+    bool live = false;
+};
+std::vector<TcPlan> g_tc_plans;
 
 int check_gemv_args(const void* y, const void* x, const void* mant, const void* exps, int M, int K) {
     if (!y || !x || !mant || !exps) return fail(QB_EINVAL, "null pointer");
@@ -639,6 +649,85 @@ int qwen_b200_lm_head_bfp8_dev(const float* h, const int8_t* mant, const uint8_t
         return fail(QB_EINVAL, "lm_head_bfp8: hidden must be a multiple of 512, mant/exps/h 16/4/8-byte aligned, "
                                "and at most 2048 vocab rows per SM");
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_lm_head_bfp8_dev", e);
+}
+
+int qwen_b200_quant_planes_dev(const float* x, int B, int K, int8_t* planes, float* xs_t, int ldxs, void* stream) {
+    if (!x || !planes || !xs_t || B <= 0 || K <= 0 || K % 64 || ldxs < B)
+        return fail(QB_EINVAL, "qwen_b200_quant_planes_dev: bad arguments");
+    if ((reinterpret_cast<uintptr_t>(x) & 7) || (reinterpret_cast<uintptr_t>(planes) & 1))
+        return fail(QB_EINVAL, "qwen_b200_quant_planes_dev: x must be 8-byte and planes 2-byte aligned");
+    cudaError_t e = qb::launch_quant_planes(x, B, K, planes, xs_t, ldxs, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_quant_planes_dev", e);
+}
+
+int qwen_b200_gemm_tc_dev(float* y, const int8_t* planes, const float* xs_t, int ldxs, const int8_t* mant,
+                          const uint8_t* exps, int M, int K, int B, int32_t* dots, void* stream) {
+    if (M == 0 || B == 0) return QB_OK;
+    qb::TcDesc d;
+    if (M < 0 || B < 0 || !qb::tc_make_desc(&d, y, planes, xs_t, ldxs, mant, exps, M, K, B, dots))
+        return fail(QB_EINVAL, "qwen_b200_gemm_tc_dev: K a positive multiple of 64, planes/xs_t/mant 16-byte "
+                               "aligned, ldxs >= B and a multiple of 4");
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    cudaError_t e = qb::launch_gemm_tc(nullptr, &d, 1, qb::tc_units(d), B, dots != nullptr, st->err,
+                                       static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_gemm_tc_dev", e);
+}
+
+int qwen_b200_tc_stack_create(int n, const int8_t* const* mant, const uint8_t* const* exps,
+                              const int8_t* const* planes, const float* const* xs_t, float* const* y, const int* M,
+                              const int* K, int B, int ldxs) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (n <= 0 || n > 4096 || !mant || !exps || !planes || !xs_t || !y || !M || !K || B <= 0)
+        return fail(QB_EINVAL, "tc_stack: bad arguments");
+    std::vector<qb::TcDesc> v;
+    for (int i = 0; i < n; i++) {
+        if (M[i] == 0) continue;
+        qb::TcDesc d;
+        if (M[i] < 0 || !qb::tc_make_desc(&d, y[i], planes[i], xs_t[i], ldxs, mant[i], exps[i], M[i], K[i], B,
+                                          nullptr))
+            return fail(QB_EINVAL, "tc_stack: bad descriptor (K a multiple of 64, 16-byte aligned planes/xs_t/"
+                                   "mant, ldxs >= B and a multiple of 4)");
+        v.push_back(d);
+    }
+    // deepest matrices first, so the round-robin tail is made of short units
+    std::stable_sort(v.begin(), v.end(), [](const qb::TcDesc& a, const qb::TcDesc& b) { return a.K > b.K; });
+    TcPlan tp;
+    for (auto& d : v) {
+        d.unit_begin = tp.total_units;
+        tp.total_units += qb::tc_units(d);
+    }
+    tp.n = (int)v.size();
+    tp.B = B;
+    cudaError_t e = cudaMalloc(&tp.dev_descs, sizeof(qb::TcDesc) * (v.empty() ? 1 : v.size()));
+    if (e != cudaSuccess) return fail(QB_ENOMEM, "tc_stack alloc", e);
+    if (!v.empty() &&
+        (e = cudaMemcpy(tp.dev_descs, v.data(), sizeof(qb::TcDesc) * v.size(), cudaMemcpyHostToDevice)) != cudaSuccess)
+        return fail(QB_ECUDA, "tc_stack upload", e);
+    tp.live = true;
+    g_tc_plans.push_back(tp);
+    return (int)g_tc_plans.size();
+}
+
+int qwen_b200_tc_stack_run(int plan, void* stream) {
+    if (plan < 1 || plan > (int)g_tc_plans.size() || !g_tc_plans[plan - 1].live)
+        return fail(QB_EINVAL, "tc_stack: bad handle");
+    const TcPlan& tp = g_tc_plans[plan - 1];
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    cudaError_t e = qb::launch_gemm_tc(tp.dev_descs, nullptr, tp.n, tp.total_units, tp.B, false, st->err,
+                                       static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_tc_stack_run", e);
+}
+
+int qwen_b200_tc_stack_destroy(int plan) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (plan < 1 || plan > (int)g_tc_plans.size() || !g_tc_plans[plan - 1].live)
+        return fail(QB_EINVAL, "tc_stack: bad handle");
+    cudaFree(g_tc_plans[plan - 1].dev_descs);
+    g_tc_plans[plan - 1].dev_descs = nullptr;
+    g_tc_plans[plan - 1].live = false;
+    return QB_OK;
 }
 
 }  // extern "C"

@@ -64,6 +64,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, 
         : "memory");
 }
 
+// 3D tile load at (x, y, z); x in elements of the innermost dimension.
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, int y, int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(tmap), "r"(x), "r"(y), "r"(z),
+          "r"((uint32_t)__cvta_generic_to_shared(bar))
+        : "memory");
+}
+
 // 1D bulk copy global -> shared (16-byte aligned addresses, size a multiple
 // of 16), completing on `bar`.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -80,5 +89,9 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 // Returns false if the driver entry point is unavailable or rejects it.
 bool encode_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols,
                     uint32_t box_rows);
+// General tiled tensor map: `rank` dimensions innermost first, byte strides
+// of dimensions 1..rank-1, box extents, element type and swizzle.
+bool encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
+                 const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
 
 }  // namespace qb

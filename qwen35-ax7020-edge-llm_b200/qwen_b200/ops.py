@@ -23,7 +23,7 @@ from ._lib import KernelError, check, load
 
 __all__ = [
     "KernelError", "quant_block64", "bfp8_gemv", "bfp8_gemv_fast", "bfp8_gemv_q", "lm_head_bf16", "lm_head_bfp8",
-    "pack_bfp8", "LinearStack", "LmResult",
+    "pack_bfp8", "LinearStack", "LmResult", "Planes", "quant_planes", "bfp8_gemm_tc", "BatchedStack",
 ]
 
 
@@ -95,6 +95,101 @@ def bfp8_gemv_q(xq: torch.Tensor, xs: torch.Tensor, mant: torch.Tensor, exps: to
     check(load().qwen_b200_gemv_q_dev(_ptr(y), _ptr(xq), _ptr(xs), _ptr(mant), _ptr(exps), M, K, _stream()),
           "bfp8_gemv_q")
     return y
+
+
+@dataclass
+class Planes:
+    """Batched int16 block-64 activations as two int8 planes (xq = 256*hi + lo):
+    ``planes`` int8 [2, B, K] (plane 0 = hi, plane 1 = lo as raw bytes) and
+    block scales ``xs_t`` fp32 [K/64, ldxs] (block-major, first B columns used)."""
+    planes: torch.Tensor
+    xs_t: torch.Tensor
+    B: int
+    K: int
+
+    @property
+    def ldxs(self) -> int:
+        return self.xs_t.shape[1]
+
+    def xq(self) -> torch.Tensor:
+        """The int16 activations [B, K] these planes encode."""
+        hi = self.planes[0].to(torch.int32)
+        lo = self.planes[1].view(torch.uint8).to(torch.int32)
+        return (hi * 256 + lo).to(torch.int16)
+
+    def xs(self) -> torch.Tensor:
+        """Block scales [B, K/64]."""
+        return self.xs_t[:, :self.B].t().contiguous()
+
+
+def planes_empty(B: int, K: int, device) -> Planes:
+    ldxs = (B + 3) // 4 * 4
+    return Planes(torch.empty((2, B, K), dtype=torch.int8, device=device),
+                  torch.zeros((K // 64, ldxs), dtype=torch.float32, device=device), B, K)
+
+
+def quant_planes(x: torch.Tensor, out: Planes | None = None) -> Planes:
+    """x fp32 [B, K] -> Planes, with the reference quantizer's arithmetic
+    (256*hi + lo equals quant_block64's xq bit for bit)."""
+    x = _need(x, torch.float32, "x")
+    B, K = x.shape
+    p = out if out is not None else planes_empty(B, K, x.device)
+    check(load().qwen_b200_quant_planes_dev(_ptr(x), B, K, _ptr(p.planes), _ptr(p.xs_t), p.ldxs, _stream()),
+          "quant_planes")
+    return p
+
+
+def bfp8_gemm_tc(p: Planes, mant: torch.Tensor, exps: torch.Tensor, out: torch.Tensor | None = None,
+                 dots: bool = False):
+    """y fp32 [B, M] = BFP8 W [M, K] x planar activations, on tcgen05 kind::i8.
+    With ``dots=True`` also returns the exact int32 block dots [B, M, K/64]."""
+    mant = _need(mant, torch.int8, "mant")
+    exps = _need(exps, torch.uint8, "exps")
+    M, K = mant.shape
+    if K != p.K or exps.numel() < M * (K // 64):
+        raise ValueError("shape mismatch")
+    y = out if out is not None else torch.empty((p.B, M), dtype=torch.float32, device=mant.device)
+    d = torch.empty((p.B, M, K // 64), dtype=torch.int32, device=mant.device) if dots else None
+    check(load().qwen_b200_gemm_tc_dev(_ptr(y), _ptr(p.planes), _ptr(p.xs_t), p.ldxs, _ptr(mant), _ptr(exps), M, K,
+                                       p.B, _ptr(d) if d is not None else None, _stream()), "bfp8_gemm_tc")
+    return (y, d) if dots else y
+
+
+class BatchedStack:
+    """A reusable grouped launch of independent batched BFP8 GEMMs (one
+    kernel): ``items`` is a list of (Planes, mant, exps, y fp32 [B, M]) with a
+    common B and ldxs."""
+
+    def __init__(self, items):
+        n = len(items)
+        P = ctypes.c_void_p * n
+        I = ctypes.c_int * n
+        self._keep = items
+        B = items[0][0].B
+        ldxs = items[0][0].ldxs
+        h = load().qwen_b200_tc_stack_create(
+            n, P(*[_ptr(m) for (_, m, _, _) in items]), P(*[_ptr(e) for (_, _, e, _) in items]),
+            P(*[_ptr(p.planes) for (p, _, _, _) in items]), P(*[_ptr(p.xs_t) for (p, _, _, _) in items]),
+            P(*[_ptr(y) for (_, _, _, y) in items]), I(*[m.shape[0] for (_, m, _, _) in items]),
+            I(*[m.shape[1] for (_, m, _, _) in items]), B, ldxs)
+        if h <= 0:
+            check(h, "BatchedStack")
+        self.handle = h
+
+    def run(self, stream: int | None = None) -> None:
+        check(load().qwen_b200_tc_stack_run(self.handle, _stream() if stream is None else stream),
+              "BatchedStack.run")
+
+    def close(self) -> None:
+        if getattr(self, "handle", 0) > 0:
+            load().qwen_b200_tc_stack_destroy(self.handle)
+            self.handle = 0
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 @dataclass

@@ -1,0 +1,167 @@
+"""GPU parity of the batched tensor-core path (tcgen05 kind::i8) against the
+CPU oracle.
+
+* quant_planes: 256*hi + lo equals the reference quantizer's xq bit for bit,
+  and the block scales match bit for bit.
+* every per-block int32 dot product the tensor cores form (hi and lo planes
+  recombined) equals the oracle's exact dot -- bit-exact;
+* every fp32 output is within the rounding bound of its own arithmetic of
+  the exact value sum_b dot_b * 2^(e_b-134) * xs_b (float64 from the exact
+  dots): (nb + 1) * 2^-24 * sum_b |term_b|, one rounding per block;
+* and within 1e-5 * sum_{b,j} |float(L_j) * 2^(e_b-134) * xs_b| of the
+  reference's NEON-order result, where L_j are the reference's four
+  lane-class partial dots: that sum scales the reference's own rounding
+  (its lane partials can be far larger than the block dot they add up to);
+* the grouped launch gives the same bits as single launches.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def bits(a):
+    a = np.ascontiguousarray(a, np.float32)
+    return np.where(np.isnan(a), np.uint32(0x7FC00000), a.view(np.uint32))
+
+
+def rand_weights(rng, M, K, std=0.02):
+    return O.pack_bfp8(rng.normal(0, std, (M, K)).astype(np.float32))
+
+
+class Rows:
+    """Oracle view of a batch: reference outputs (NEON order), exact block
+    dots, exact outputs and the two term magnitudes, per (row, output)."""
+
+    def __init__(self, x, mant, exps):
+        B = x.shape[0]
+        M, K = mant.shape
+        self.nb = K // 64
+        self.ref = np.zeros((B, M), np.float32)
+        self.dots = np.zeros((B, M, K // 64), np.int32)
+        self.exact = np.zeros((B, M), np.float64)
+        self.mag = np.zeros((B, M), np.float64)        # sum_b |dot_b * S * xs|
+        self.mag_lane = np.zeros((B, M), np.float64)   # sum_{b,j} |L_j * S * xs|
+        scale = np.ldexp(1.0, exps.astype(np.int64) - 134)
+        for b in range(B):
+            xq, xs = O.quant_x(x[b])
+            lanes = O.lane_dots(mant, xq).astype(np.float64)
+            d = O.block_dots(mant, xq)
+            sx = scale * xs.astype(np.float64)
+            self.dots[b] = d
+            self.ref[b] = O.bfp8_gemv(x[b], mant, exps)
+            self.exact[b] = (d.astype(np.float64) * sx).sum(axis=1)
+            self.mag[b] = (np.abs(d.astype(np.float64)) * sx).sum(axis=1)
+            self.mag_lane[b] = (np.abs(lanes).sum(axis=2) * sx).sum(axis=1)
+
+    def check(self, y, what):
+        y = y.astype(np.float64)
+        bound = (self.nb + 1) * 2.0 ** -24 * self.mag + 1e-30
+        e1 = np.abs(y - self.exact)
+        assert (e1 <= bound).all(), (what, "vs exact", float((e1 / bound).max()))
+        tol = 1e-5 * self.mag_lane + 1e-30
+        e2 = np.abs(y - self.ref.astype(np.float64))
+        assert (e2 <= tol).all(), (what, "vs reference", float((e2 / tol).max()))
+
+
+def test_quant_planes_bit_exact(cuda):
+    import torch
+
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(5)
+    for B, K in ((1, 64), (5, 1024), (8, 3584), (33, 64 * 37)):
+        x = rng.normal(0, 1, (B, K)).astype(np.float32)
+        x[0, :64] = 0.0
+        if B > 1:
+            x[1, 64:128] = 1e-22
+        if B > 2 and K >= 256:
+            x[2, 128:192] = rng.normal(0, 1e4, 64)
+            x[2, 192:256] = np.arange(64, dtype=np.float32) * 0.5 - 16
+        p = ops.quant_planes(torch.from_numpy(x).cuda())
+        xq = p.xq().cpu().numpy()
+        xs = p.xs().cpu().numpy()
+        for r in range(B):
+            q_ref, s_ref = O.quant_x(x[r])
+            assert np.array_equal(xq[r], q_ref), (B, K, r)
+            assert np.array_equal(bits(xs[r]), bits(s_ref)), (B, K, r)
+        hi = p.planes[0].cpu().numpy().astype(np.int32)
+        assert hi.min() >= -64 and hi.max() <= 64
+
+
+TC_SHAPES = [(128, 128, 8), (200, 1088, 5), (64, 512, 1), (1000, 1024, 16), (3584, 1024, 32), (512, 2048, 64),
+             (1024, 3584, 128), (520, 2048, 256), (300, 640, 100)]
+
+
+@pytest.mark.parametrize("M,K,B", TC_SHAPES)
+def test_gemm_tc_dots_exact_and_outputs_within_tolerance(cuda, M, K, B):
+    import torch
+
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(M * 7 + K + B)
+    mant, exps = rand_weights(rng, M, K)
+    x = rng.normal(0, 1, (B, K)).astype(np.float32)
+    x[0, 64:128] = 0.0   # a zero block
+    p = ops.quant_planes(torch.from_numpy(x).cuda())
+    dm = torch.from_numpy(mant).cuda()
+    de = torch.from_numpy(exps).cuda()
+    y, d = ops.bfp8_gemm_tc(p, dm, de, dots=True)
+    y2 = ops.bfp8_gemm_tc(p, dm, de)
+    torch.cuda.synchronize()
+    y, d, y2 = y.cpu().numpy(), d.cpu().numpy(), y2.cpu().numpy()
+    rows = Rows(x, mant, exps)
+    assert np.array_equal(d, rows.dots), (M, K, B)
+    assert np.array_equal(bits(y), bits(y2))              # the dots variant computes the same floats
+    rows.check(y, (M, K, B))
+
+
+def test_gemm_tc_extreme_weights_exact_dots(cuda):
+    """Full-range mantissas (-128..127 bytes, i.e. -127..127 plus -128) and
+    activations at the +-16384 rails: the hi/lo split still gives exact dots."""
+    import torch
+
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(99)
+    M, K, B = 256, 1024, 32
+    mant = rng.integers(-128, 128, (M, K)).astype(np.int8)
+    mant[0, :] = -128
+    mant[1, :] = 127
+    exps = rng.integers(100, 140, (M, K // 64)).astype(np.uint8)
+    x = rng.normal(0, 1, (B, K)).astype(np.float32)
+    x[0] = np.sign(rng.normal(0, 1, K)).astype(np.float32)        # every element at +-amax -> xq = +-16384
+    x[1] = -np.abs(x[1])
+    p = ops.quant_planes(torch.from_numpy(x).cuda())
+    _, d = ops.bfp8_gemm_tc(p, torch.from_numpy(mant).cuda(), torch.from_numpy(exps).cuda(), dots=True)
+    assert np.array_equal(d.cpu().numpy(), Rows(x, mant, exps).dots)
+
+
+def test_batched_stack_matches_single_launches(cuda):
+    import torch
+
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(17)
+    B = 32
+    shapes = [(3584, 1024), (1024, 3584), (512, 1024), (6144, 1024), (1024, 2048)]
+    items, singles = [], []
+    for M, K in shapes:
+        mant, exps = rand_weights(rng, M, K)
+        dm, de = torch.from_numpy(mant).cuda(), torch.from_numpy(exps).cuda()
+        p = ops.quant_planes(torch.from_numpy(rng.normal(0, 1, (B, K)).astype(np.float32)).cuda())
+        y = torch.full((B, M), float("nan"), device="cuda")
+        items.append((p, dm, de, y))
+        singles.append(ops.bfp8_gemm_tc(p, dm, de))
+    st = ops.BatchedStack(items)
+    st.run()
+    st.run()   # reusable
+    torch.cuda.synchronize()
+    for (p, _, _, y), ys in zip(items, singles):
+        assert np.array_equal(bits(y.cpu().numpy()), bits(ys.cpu().numpy()))
+    st.close()
+    from qwen_b200 import _lib
+
+    assert _lib.load().qwen_b200_device_error(1) == 0
