@@ -2,7 +2,7 @@
 """Benchmark of the BFP8 GEMV / lm_head decode hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload stack|gemv|lm_bf16|lm_bfp8]
+                    [--workload stack|gemv|lm_bf16|lm_bfp8|sharded|batched] [--batch B]
 
 Default workload (the BASELINE metric's configuration): the full per-token
 linear stack of Qwen3.5-0.8B at batch 1 -- 150 BFP8 GEMVs, 504,791,040 bytes
@@ -51,7 +51,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["stack", "gemv", "lm_bf16", "lm_bfp8", "sharded"], default="stack")
+    ap.add_argument("--workload", choices=["stack", "gemv", "lm_bf16", "lm_bfp8", "sharded", "batched"],
+                    default="stack")
+    ap.add_argument("--batch", type=int, default=256, help="sequences per step of --workload batched")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--copies", type=int, default=0,
@@ -245,15 +247,115 @@ def run_b200(args):
             p.close()
     elif args.workload == "sharded":
         line.update(run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, peak_kind))
+    elif args.workload == "batched":
+        line.update(run_batched(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kind))
     else:
         line.update(run_lm_head(args, torch, ops, dev, barrier, world, hbm_peak, peak_kind))
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args.workload)
+        line["cpu_baseline"] = cpu_baseline(args.workload, args.batch)
     if world > 1:
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def int8_peak_tops(torch, dev):
+    """Dense int8 tensor throughput of this GPU, measured live: cuBLASLt
+    through torch._int_mm on 8192^3 (2*N^3 ops), best of 10, CUDA events."""
+    n = 8192
+    a = torch.randint(-128, 127, (n, n), dtype=torch.int8, device=dev)
+    b = torch.randint(-128, 127, (n, n), dtype=torch.int8, device=dev).t()
+    for _ in range(3):
+        torch._int_mm(a, b)
+    best = float("inf")
+    for _ in range(10):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch._int_mm(a, b)
+        e.record()
+        torch.cuda.synchronize()
+        best = min(best, s.elapsed_time(e) / 1e3)
+    del a, b
+    return 2 * n ** 3 / best / 1e12
+
+
+def run_batched(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kind):
+    """B sequences x the 0.8B linear stack, one grouped
+    tcgen05 kind::i8 launch per step (150 GEMMs).  Activations enter as
+    planar int16 (hi/lo int8 planes + block scales, the quantizer's output);
+    outputs leave as fp32 [B][M].  Weight copies and activation sets rotate
+    together (> 4 GB), so no step finds its inputs in L2."""
+    from qwen_b200 import model, ops
+
+    B = args.batch
+    shapes = model.qwen35_08b_stack()
+    nb = model.batched_bytes(shapes, B)
+    copies = args.copies or max(2, math.ceil(L2_DEFEAT_BYTES / nb["weights"]))
+    ds = model.DeviceStack(shapes, copies=copies, device=dev, seed=1234 + rank)
+    db = model.DeviceBatch(shapes, B, sets=copies, device=dev, seed=77 + rank)
+    plans = [ops.BatchedStack(db.items(ds.views(c), c)) for c in range(copies)]
+    p_int8 = int8_peak_tops(torch, dev)
+
+    clk = ClockSampler(gpu_uuid(torch, dev), dev.index or 0)
+    secs = timed(torch, lambda i: plans[i % copies].run(), args.steps, args.warmup, barrier)
+    clocks = clk.stop()
+    t = torch.tensor([secs], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    per_step = float(t.item()) / args.steps
+    gbs = nb["total"] / per_step / 1e9
+    tops = nb["tensor_ops"] / per_step / 1e12
+    t_hbm = nb["total"] / (hbm_peak * 1e9)
+    t_tc = nb["tensor_ops"] / (p_int8 * 1e12)
+    if t_hbm >= t_tc:
+        roof = {"bound": "hbm", "achieved": round(gbs, 2), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind}
+    else:
+        roof = {"bound": "tensor", "achieved": round(tops, 2), "peak": round(p_int8, 1), "unit": "TOPS (int8)",
+                "frac": round(tops / p_int8, 4), "peak_kind": "measured live (cuBLASLt int8, torch._int_mm 8192^3)"}
+    roof.update({"traffic": committed_traffic(f"batched_b{B}"), "kernel": "gemm_tc_kernel (grouped)",
+                 "roofline_time_ms": round(max(t_hbm, t_tc) * 1e3, 4),
+                 "frac_of_roofline_time": round(max(t_hbm, t_tc) / per_step, 4),
+                 "hbm_frac": round(gbs / hbm_peak, 4), "tensor_frac": round(tops / p_int8, 4),
+                 "int8_peak_tops": round(p_int8, 1)})
+
+    e2e = None
+    if not args.no_e2e:
+        s0 = db.sets[0]
+        hp = torch.empty(s0["planes"].numel(), dtype=torch.int8, pin_memory=True)
+        hs = torch.empty(s0["scales"].numel(), dtype=torch.float32, pin_memory=True)
+        hy = torch.empty(s0["y"].numel(), dtype=torch.float32, pin_memory=True)
+        hp.copy_(s0["planes"].cpu())
+        hs.copy_(s0["scales"].cpu())
+
+        def e2e_step(i):
+            st = db.sets[i % copies]
+            st["planes"].copy_(hp, non_blocking=True)
+            st["scales"].copy_(hs, non_blocking=True)
+            plans[i % copies].run()
+            hy.copy_(st["y"], non_blocking=True)
+
+        esecs = timed(torch, e2e_step, args.steps, args.warmup, barrier)
+        te = torch.tensor([esecs], device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        eper = float(te.item()) / args.steps
+        e2e = {"value": round(world * nb["total"] / eper / 1e9, 2), "unit": "GB/s",
+               "ms_per_step": round(eper * 1e3, 4), "tokens_per_s": round(world * B / eper, 1),
+               "h2d_bytes_per_step": hp.numel() + hs.numel() * 4, "d2h_bytes_per_step": hy.numel() * 4}
+    for p in plans:
+        p.close()
+    return {"value": round(world * gbs, 2), "ms_per_step": round(per_step * 1e3, 4), "dtype": "int8xint8->int32 (hi/lo planes)->fp32",
+            "config": {"workload": f"batched decode: B={B} sequences x qwen35-0.8b linear stack (150 BFP8 GEMMs)",
+                       "batch": B, "gemms_per_step": len(shapes), "weight_bytes": nb["weights"],
+                       "algorithmic_bytes_per_step": nb["total"], "macs_per_step": nb["macs"] * B,
+                       "tensor_int8_ops_per_step": nb["tensor_ops"], "tokens_per_s": round(world * B / per_step, 1),
+                       "tops_issued_int8": round(tops, 2),
+                       "l2": f"rotates {copies} weight copies + activation sets "
+                             f"({copies * nb['weights'] / 1e9:.2f} GB weights) > 126 MB L2",
+                       "launch": "one grouped tcgen05 kernel per step", "parallelism": f"replicas x{world}"},
+            "roofline": roof, "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks}
 
 
 def run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, peak_kind):
@@ -367,7 +469,7 @@ def reference_stack_runner(workload, seed=7):
     lib.bfp8_gemv.argtypes = [P, P, P, P, I, I]
     lib.bfp8_gemv.restype = None
     lib.init_kernels()
-    shapes, desc = stack_shapes(workload)
+    shapes, desc = stack_shapes("stack" if workload == "batched" else workload)
     rng = np.random.default_rng(seed)
     ents = []
     for t in shapes:
@@ -383,15 +485,16 @@ def reference_stack_runner(workload, seed=7):
     return token, shapes, desc
 
 
-def cpu_baseline(workload):
+def cpu_baseline(workload, batch=1):
     """Bounded sample of the reference C on this host's cores, in a child
     process so OpenMP starts with every host thread."""
-    if workload not in ("stack", "gemv"):
+    if workload not in ("stack", "gemv", "batched"):
         return None
     env = dict(os.environ, OMP_NUM_THREADS=str(os.cpu_count()))
     try:
         out = subprocess.run([sys.executable, os.path.abspath(__file__), "--impl", "reference", "--cpu-sample",
-                              "--workload", workload], env=env, capture_output=True, text=True, timeout=300)
+                              "--workload", workload, "--batch", str(batch)], env=env, capture_output=True, text=True,
+                             timeout=300)
         return json.loads(out.stdout.strip().splitlines()[-1])
     except Exception as e:  # a baseline failure must not hide the GPU number
         return {"error": str(e)[:200]}
@@ -404,6 +507,11 @@ def run_reference(args):
 
     token, shapes, desc = reference_stack_runner(args.workload)
     nb = model.stack_bytes(shapes)
+    # the reference has no batched path: B sequences cost B one-sequence passes
+    seqs = args.batch if args.workload == "batched" else 1
+    if seqs > 1:
+        nb = model.batched_bytes(shapes, seqs)
+        desc = f"batched decode: B={seqs} sequences x {desc}, one sequence at a time"
     cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count()))
     if args.cpu_sample:
         # bounded sample: whole tokens for ~10 s (at least 2)
@@ -412,17 +520,19 @@ def run_reference(args):
         while n < 2 or (time.perf_counter() - t0 < 10.0 and n < 1000):
             token()
             n += 1
-        dt = (time.perf_counter() - t0) / n
+        dt = (time.perf_counter() - t0) / n * seqs
         print(json.dumps({"value": round(nb["total"] / dt / 1e9, 4), "unit": "GB/s", "ms_per_step": round(dt * 1e3, 3),
                           "cores": cores, "kind": "reference",
-                          "sample": f"{n} whole tokens of the workload ({desc}) after 1 warm-up token; "
-                                    "reference C bfp8_gemv scalar build, OpenMP"}))
+                          "sample": f"{n} whole one-sequence passes of the stack after 1 warm-up pass, scaled by "
+                                    f"{seqs} sequences per step ({desc}); reference C bfp8_gemv scalar build, "
+                                    "OpenMP"}))
         return
     for _ in range(args.warmup):
         token()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        token()
+        for _ in range(seqs):
+            token()
     dt = (time.perf_counter() - t0) / args.steps
     v = nb["total"] / dt / 1e9
     print(json.dumps({

@@ -172,8 +172,8 @@ QB_API int qwen_b200_stack_run(int plan, void* stream);
 QB_API int qwen_b200_stack_destroy(int plan);
 
 /* ---- Batched decode on the tensor cores (B sequences share the weights).
- * Activations are int16 block-64 values stored as two int8 planes,
- * xq = 256*hi + lo (hi = xq >> 8 signed, lo = xq & 255 unsigned):
+ * Activations are int16 block-64 values stored as two signed int8 planes,
+ * xq = 256*hi + lo (lo = low byte of xq as a signed int8, hi = (xq - lo)/256):
  * planes [2][B][K] bytes (plane 0 = hi, plane 1 = lo), 16-byte aligned, and
  * block scales xs_t [K/64][ldxs] fp32 (block-major, ldxs >= B, ldxs % 4 == 0).
  * The reference decodes one sequence at a time; these entry points have no
@@ -196,7 +196,8 @@ QB_API int qwen_b200_gemm_tc_dev(float* y, const int8_t* planes, const float* xs
 
 /* Grouped batched launch of n independent GEMMs with a common B and ldxs
  * (e.g. the per-step linear stack of B sequences).  HOST arrays of DEVICE
- * pointers; returns a plan handle (>= 1) or a QB_E* code.  1 <= n <= 4096. */
+ * pointers; returns a plan handle (>= 1) or a QB_E* code.  1 <= n <= 4096; a run
+ * is one launch per 160 GEMMs. */
 QB_API int qwen_b200_tc_stack_create(int n, const int8_t* const* mant, const uint8_t* const* exps,
                                      const int8_t* const* planes, const float* const* xs_t, float* const* y,
                                      const int* M, const int* K, int B, int ldxs);

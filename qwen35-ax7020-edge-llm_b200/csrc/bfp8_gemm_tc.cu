@@ -8,14 +8,20 @@
 //               (128 rows x 128 B), one activation box (both planes, N rows)
 //               and one scale box (N columns x 2 blocks) on one mbarrier;
 //   warp 1      allocates TMEM and issues the MMAs from one thread: per
-//               64-block two K=32 steps into a hi accumulator and two into
-//               a lo accumulator (N columns each), then tcgen05.commit;
+//               64-block two K=32 steps of one M=128, N=2*N_tile MMA whose
+//               B operand is the hi plane rows followed by the lo plane rows
+//               (both signed int8), so the accumulator holds the hi dots in
+//               columns [0, N) and the lo dots in [N, 2N); then
+//               tcgen05.commit;
 //   warps 2..9  epilogue: each thread owns one weight row (its TMEM lane)
 //               and N/2 batch columns; per block it reads Dhi/Dlo from
 //               TMEM, frees the slot, and accumulates
 //               float(256*Dhi + Dlo) * 2^(e-134) * xs in f32 registers.
 // TMEM holds kSlots accumulator pairs so the tensor cores run ahead of the
 // epilogue by up to kSlots blocks; shared memory holds kStages K stages.
+// The producer resolves each unit (descriptor, tile, exponent tile) once and
+// publishes it through a two-entry unit ring in shared memory, so the MMA and
+// epilogue warps never wait on descriptor loads at unit boundaries.
 // Every mbarrier wait is bounded (error word + early exit), and TMEM is
 // released only after a final commit shows no MMA in flight.
 #include "bfp8_gemm_tc.cuh"
@@ -33,6 +39,39 @@ constexpr int kEpiWarps = 8;
 constexpr int kTileRows = 128;
 constexpr int kStageK = 128;   // K bytes per pipeline stage (two 64-blocks)
 
+constexpr int kExpsMax = 56;   // block exponents per row staged in shared memory (K <= 3584)
+constexpr int kMaxTable = kTcMaxDescs;   // GEMMs per launch (their scalar fields are kept in shared memory)
+constexpr int kEBytes = kTileRows * kExpsMax;
+
+// TMEM accumulator presets.  Before the first K step of a block, the hi
+// accumulator holds the bits of 1.5*2^31 and the lo accumulator those of
+// 1.5*2^23; the MMAs add the int32 dots to those bit patterns.  Since
+// |Dhi| < 2^20 and |Dlo| < 2^21 the sums stay inside one binade, so read as
+// floats the accumulators are exactly 1.5*2^31 + 256*Dhi (ulp 256) and
+// 1.5*2^23 + Dlo (ulp 1).  Then (hi - kMagicSum) is exact and adding lo
+// gives float(256*Dhi + Dlo) = float(D) with a single rounding: two f32
+// additions per block dot instead of an int->float conversion.
+constexpr uint32_t kMagicHi = 0x4F400000u;
+constexpr uint32_t kMagicLo = 0x4B400000u;
+constexpr float kMagicSum = 3233808384.0f;   // 1.5*2^31 + 1.5*2^23 = 771 * 2^22
+
+// Scalar fields of one GEMM, copied to shared memory at kernel start so that
+// unit lookups never wait on global loads.
+struct DescRow {
+    int unit_begin, n_nt, nb, M, B, pad_;
+    const uint8_t* exps;
+    float* y;
+    int32_t* dots;
+};
+
+// One unit as the producer publishes it to the MMA and epilogue warps.
+struct UnitInfo {
+    const uint8_t* exps;   // exponent rows of the tile (shared-memory copy when ebulk)
+    float* y;
+    int32_t* dots;
+    int M, nb, B, rt, nt, ebulk;
+};
+
 template <int N>
 struct TcCfg {
     static constexpr int kStages = N >= 128 ? 4 : (N >= 64 ? 6 : 8);
@@ -45,9 +84,17 @@ struct TcCfg {
     static constexpr int kSBytes = kSBox < 128 ? 128 : kSBox;        // 128-byte aligned slots
     static constexpr int kTxBytes = kStageBytes + kSBox;
     static constexpr int kCols = N / 2;                              // columns per epilogue thread
-    static constexpr int kChunk = kCols < 16 ? kCols : 16;
-    static constexpr size_t kSmem =
-        1024 + (size_t)kStages * (kStageBytes + kSBytes) + (size_t)(2 * kStages + 2 * kSlots + 1) * 8 + 16;
+    // Small tiles: the epilogue takes kGroup blocks per round (one barrier
+    // wait, one TMEM load wait and one store wait for all of them).  Large
+    // tiles: one block per round, its columns in kChunk pieces whose TMEM
+    // loads overlap the previous piece's arithmetic.
+    static constexpr int kGroup = N <= 16 ? 4 : (N <= 32 ? 2 : 1);
+    static constexpr int kChunk = kGroup > 1 ? kCols : 8;
+    static constexpr int kPreset = kCols < 16 ? kCols : 16;
+    static constexpr int kGroupsInFlight = kSlots / kGroup;
+    static constexpr size_t kSmem = 1024 + (size_t)kStages * (kStageBytes + kSBytes) + 2 * (size_t)kEBytes +
+                                    2 * sizeof(UnitInfo) + (size_t)kMaxTable * sizeof(DescRow) +
+                                    (size_t)(2 * kStages + kGroupsInFlight + kSlots + 5) * 8 + 16;
 };
 
 struct TcLaunch {
@@ -67,12 +114,11 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// Instruction descriptor: int32 accumulator, A signed int8 K-major, B int8
-// (signed or unsigned) K-major, M = 128, N columns.
+// Instruction descriptor: int32 accumulator, A and B signed int8, both
+// K-major, M = 128, N columns.
 template <int N>
-__host__ __device__ constexpr uint32_t idesc_i8(bool b_signed) {
-    return (2u << 4) | (1u << 7) | ((b_signed ? 1u : 0u) << 10) | ((uint32_t)(N >> 3) << 17) |
-           ((uint32_t)(kTileRows >> 4) << 24);
+__host__ __device__ constexpr uint32_t idesc_i8() {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kTileRows >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
@@ -125,10 +171,47 @@ __device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, uint32_t (&v)[16]) {
         : "r"(taddr));
 }
 
-__device__ __forceinline__ const TcDesc* desc_for(const TcLaunch& p, int u, int& di) {
-    if (!p.descs) return &p.one;
-    while (di + 1 < p.n && u >= p.descs[di + 1].unit_begin) di++;
-    return p.descs + di;
+// Store one 32-bit value into C consecutive columns of the warp's 32 lanes.
+template <int C>
+__device__ __forceinline__ void tmem_st_rep(uint32_t taddr, uint32_t v);
+template <>
+__device__ __forceinline__ void tmem_st_rep<4>(uint32_t taddr, uint32_t v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %1, %1, %1};" ::"r"(taddr), "r"(v) : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_st_rep<8>(uint32_t taddr, uint32_t v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
+                 "r"(v)
+                 : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_st_rep<16>(uint32_t taddr, uint32_t v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
+        "%1};" ::"r"(taddr),
+        "r"(v)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// tcgen05.wait::ld, then tie the loaded registers to it so that no use of
+// them can be scheduled before the wait.
+template <int C>
+__device__ __forceinline__ void tmem_wait_ld_dep(uint32_t (&a)[C], uint32_t (&b)[C]) {
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < C; i++) asm volatile("" : "+r"(a[i]), "+r"(b[i]));
+}
+
+// Block exponents of a unit's 128-row tile reach shared memory in one bulk
+// copy when its rows are contiguous whole 16-byte multiples; otherwise the
+// epilogue reads them from global memory.
+
+// Index of the GEMM that owns unit u (units are numbered GEMM by GEMM, and
+// every role walks its units in increasing order, so the index only grows).
+__device__ __forceinline__ int desc_index(const DescRow* tab, int n, int u, int di) {
+    while (di + 1 < n && u >= tab[di + 1].unit_begin) di++;
+    return di;
 }
 
 // Warp-uniform bounded wait (every lane polls; the warp agrees on the result).
@@ -145,22 +228,44 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char* stages = base;
     unsigned char* sxs = base + (size_t)C::kStages * C::kStageBytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sxs + (size_t)C::kStages * C::kSBytes);
+    unsigned char* ebuf = sxs + (size_t)C::kStages * C::kSBytes;
+    UnitInfo* uring = reinterpret_cast<UnitInfo*>(ebuf + 2 * kEBytes);
+    DescRow* tab = reinterpret_cast<DescRow*>(uring + 2);
+    uint64_t* full = reinterpret_cast<uint64_t*>(tab + kMaxTable);
     uint64_t* empty = full + C::kStages;
-    uint64_t* tfull = empty + C::kStages;
-    uint64_t* tempty = tfull + C::kSlots;
-    uint64_t* done = tempty + C::kSlots;
+    uint64_t* tfull = empty + C::kStages;          // one per group of blocks in flight
+    uint64_t* tempty = tfull + C::kGroupsInFlight;  // one per TMEM slot
+    uint64_t* ufull = tempty + C::kSlots;   // unit ring entry published (and its exponent tile landed)
+    uint64_t* uempty = ufull + 2;           // unit ring entry consumed by the epilogue
+    uint64_t* done = uempty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = p.descs ? p.n : 1;
+    for (int k = threadIdx.x; k < n; k += blockDim.x) {
+        const TcDesc* d = p.descs ? p.descs + k : &p.one;
+        DescRow r;
+        r.unit_begin = d->unit_begin;
+        r.n_nt = d->n_nt;
+        r.nb = d->nb;
+        r.M = d->M;
+        r.B = d->B;
+        r.pad_ = 0;
+        r.exps = d->exps;
+        r.y = d->y;
+        r.dots = d->dots;
+        tab[k] = r;
+    }
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kStages; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1 + kEpiWarps);   // MMA commit + every epilogue warp (scales read)
+            mbar_init(&empty[s], kEpiWarps);   // every epilogue warp, after the stage's MMAs completed
         }
-        for (int t = 0; t < C::kSlots; t++) {
-            mbar_init(&tfull[t], 1);
-            mbar_init(&tempty[t], kEpiWarps);
+        for (int g = 0; g < C::kGroupsInFlight; g++) mbar_init(&tfull[g], 1);
+        for (int t = 0; t < C::kSlots; t++) mbar_init(&tempty[t], kEpiWarps);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&ufull[b], 1);
+            mbar_init(&uempty[b], kEpiWarps);
         }
         mbar_init(done, 1);
         fence_barrier_init();
@@ -170,6 +275,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const int q = warp & 3, chalf = (warp - 2) >> 2;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    if (warp >= 2) {   // preset every accumulator slot before the first MMA
+        for (int t = 0; t < C::kSlots; t++) {
+            const uint32_t tcol = tmem + lane_base + (uint32_t)(t * 2 * N + chalf * C::kCols);
+#pragma unroll
+            for (int c = 0; c < C::kCols; c += C::kPreset) {
+                tmem_st_rep<C::kPreset>(tcol + c, kMagicHi);
+                tmem_st_rep<C::kPreset>(tcol + N + c, kMagicLo);
+            }
+        }
+        tmem_wait_st();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
 
     if (warp == 0) {
         // ---------------------------------------------------- TMA producer
@@ -177,10 +298,42 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
             uint32_t gs = 0;
             int di = 0;
             bool bad = false;
-            for (int u = blockIdx.x; u < p.total_units && !bad; u += gridDim.x) {
-                const TcDesc* d = desc_for(p, u, di);
-                const int local = u - d->unit_begin, rt = local / d->n_nt, nt = local - rt * d->n_nt;
-                const int nst = (d->nb + 1) >> 1;
+            for (int u = blockIdx.x, i = 0; u < p.total_units && !bad; u += gridDim.x, i++) {
+                di = desc_index(tab, n, u, di);
+                const DescRow& r = tab[di];
+                const TcDesc* d = p.descs ? p.descs + di : &p.one;
+                if (u + (int)gridDim.x < p.total_units) {   // warm the TMA descriptor cache for the next unit
+                    const int dj = desc_index(tab, n, u + gridDim.x, di);
+                    const TcDesc* dn = p.descs ? p.descs + dj : &p.one;
+                    tma_prefetch_desc(&dn->tm_w);
+                    tma_prefetch_desc(&dn->tm_x);
+                    tma_prefetch_desc(&dn->tm_s);
+                }
+                const int local = u - r.unit_begin, rt = local / r.n_nt, nt = local - rt * r.n_nt;
+                const int nb = r.nb, nst = (nb + 1) >> 1;
+                const int eb = i & 1;
+                const int rows = min(kTileRows, r.M - rt * kTileRows);
+                const uint32_t ebytes = (uint32_t)rows * (uint32_t)nb;
+                const uint8_t* esrc = r.exps + (size_t)rt * kTileRows * nb;
+                const bool ebulk = nb <= kExpsMax && (ebytes & 15u) == 0 && (reinterpret_cast<uintptr_t>(esrc) & 15u) == 0;
+                UnitInfo info;
+                info.exps = ebulk ? ebuf + eb * kEBytes : esrc;
+                info.y = r.y;
+                info.dots = r.dots;
+                info.M = r.M;
+                info.nb = nb;
+                info.B = r.B;
+                info.rt = rt;
+                info.nt = nt;
+                info.ebulk = ebulk;
+                if (!mbar_wait(&uempty[eb], ((i >> 1) & 1) ^ 1, p.err)) break;
+                uring[eb] = info;   // published by the arrive below (release)
+                if (ebulk) {
+                    mbar_arrive_expect_tx(&ufull[eb], ebytes);
+                    bulk_load(ebuf + eb * kEBytes, esrc, ebytes, &ufull[eb]);
+                } else {
+                    mbar_arrive_expect_tx(&ufull[eb], 0);
+                }
                 for (int st = 0; st < nst; st++, gs++) {
                     const int s = gs % C::kStages;
                     if (!mbar_wait(&empty[s], ((gs / C::kStages) & 1) ^ 1, p.err)) {
@@ -201,13 +354,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     } else if (warp == 1) {
         // ---------------------------------------------------- MMA issuer
         if (lane == 0) {
-            constexpr uint32_t kIdHi = idesc_i8<N>(true), kIdLo = idesc_i8<N>(false);
-            uint32_t gs = 0, gb = 0;
-            int di = 0;
+            constexpr uint32_t kId = idesc_i8<2 * N>();
+            constexpr int G = C::kGroup;
+            uint32_t gs = 0, gb = 0, gg = 0;
             bool bad = false;
-            for (int u = blockIdx.x; u < p.total_units && !bad; u += gridDim.x) {
-                const TcDesc* d = desc_for(p, u, di);
-                const int nb = d->nb, nst = (nb + 1) >> 1;
+            for (int u = blockIdx.x, i = 0; u < p.total_units && !bad; u += gridDim.x, i++) {
+                if (!mbar_wait(&ufull[i & 1], (i >> 1) & 1, p.err)) break;
+                const int nb = uring[i & 1].nb, nst = (nb + 1) >> 1;
                 for (int st = 0; st < nst && !bad; st++, gs++) {
                     const int s = gs % C::kStages;
                     if (!mbar_wait(&full[s], (gs / C::kStages) & 1, p.err)) {
@@ -216,25 +369,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                     }
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(stages + (size_t)s * C::kStageBytes);
-                    const uint64_t da = desc_sw128(a0), dh = desc_sw128(a0 + C::kWBytes),
-                                   dl = desc_sw128(a0 + C::kWBytes + N * kStageK);
+                    const uint64_t da = desc_sw128(a0), dx = desc_sw128(a0 + C::kWBytes);
                     for (int h = 0; h < 2 && 2 * st + h < nb; h++, gb++) {
-                        const int t = gb % C::kSlots;
+                        const int t = gb % C::kSlots, j = 2 * st + h;
                         if (!mbar_wait(&tempty[t], ((gb / C::kSlots) & 1) ^ 1, p.err)) {
                             bad = true;
                             break;
                         }
                         tc_fence_after();
-                        const uint32_t dhi = tmem + (uint32_t)(t * 2 * N), dlo = dhi + N;
 #pragma unroll
-                        for (int kk = 0; kk < 2; kk++) {
+                        for (int kk = 0; kk < 2; kk++) {   // every step accumulates onto the preset
                             const uint64_t off = (uint64_t)((h * 64 + kk * 32) >> 4);
-                            mma_i8(dhi, da + off, dh + off, kIdHi, kk);
-                            mma_i8(dlo, da + off, dl + off, kIdLo, kk);
+                            mma_i8(tmem + (uint32_t)(t * 2 * N), da + off, dx + off, kId, 1u);
                         }
-                        mma_commit(&tfull[t]);
+                        if (j % G == G - 1 || j == nb - 1) {   // a group of blocks is complete
+                            mma_commit(&tfull[gg % C::kGroupsInFlight]);
+                            gg++;
+                        }
                     }
-                    mma_commit(&empty[s]);
                 }
             }
             // no MMA may still be writing TMEM when it is released
@@ -243,72 +395,134 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         }
     } else {
         // ---------------------------------------------------- epilogue
-        const int ew = warp - 2, q = warp & 3, chalf = ew >> 2;
-        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        uint32_t gs = 0, gb = 0;
-        int di = 0;
+        constexpr int G = C::kGroup;
+        uint32_t gs = 0, gb = 0, gg = 0;
         bool bad = false;
-        for (int u = blockIdx.x; u < p.total_units && !bad; u += gridDim.x) {
-            const TcDesc* d = desc_for(p, u, di);
-            const int M = d->M, nb = d->nb, B = d->B;
-            const int local = u - d->unit_begin, rt = local / d->n_nt, nt = local - rt * d->n_nt;
-            const int m = rt * kTileRows + q * 32 + lane;
+        const float2 neg_magic = make_float2(-kMagicSum, -kMagicSum);
+        for (int u = blockIdx.x, i = 0; u < p.total_units && !bad; u += gridDim.x, i++) {
+            const int eb = i & 1;
+            if (!warp_wait(&ufull[eb], (i >> 1) & 1, p.err)) break;
+            const UnitInfo info = uring[eb];
+            const int M = info.M, nb = info.nb, B = info.B, nt = info.nt;
+            const int r = q * 32 + lane, m = info.rt * kTileRows + r;
             const bool row_ok = m < M;
-            const uint8_t* erow = d->exps + (size_t)(row_ok ? m : 0) * nb;
-            int32_t* dots = d->dots;
-            float acc[C::kCols];
+            const uint8_t* erow = info.exps + (size_t)(row_ok ? r : 0) * nb;
+            const int col0 = chalf * C::kCols;
+            float2 acc[C::kCols / 2];
 #pragma unroll
-            for (int i = 0; i < C::kCols; i++) acc[i] = 0.0f;
-            uint32_t e_next = __ldg(erow);
-            for (int j = 0; j < nb; j++, gb++) {
-                const int h = j & 1;
+            for (int k = 0; k < C::kCols / 2; k++) acc[k] = make_float2(0.0f, 0.0f);
+
+            // acc += float(256*Dhi + Dlo) * 2^(e-134) * xs over kCh columns
+            // starting at column c of block j; hv/lv are the raw accumulators.
+            auto accumulate = [&](const uint32_t* hv, const uint32_t* lv, int c, int kCh, int j, uint32_t e) {
                 const int s = (gs + (j >> 1)) % C::kStages;
-                const uint32_t e = e_next;
-                if (j + 1 < nb) e_next = __ldg(erow + j + 1);
-                const int t = gb % C::kSlots;
-                if (!warp_wait(&tfull[t], (gb / C::kSlots) & 1, p.err)) {
-                    bad = true;
-                    break;
-                }
-                tc_fence_after();
                 const float sm = exp_scale_ieee(e);
-                const float* xsv =
-                    reinterpret_cast<const float*>(sxs + (size_t)s * C::kSBytes) + h * N + chalf * C::kCols;
-                const uint32_t tcol = tmem + lane_base + (uint32_t)(t * 2 * N + chalf * C::kCols);
+                const float2 sm2 = make_float2(sm, sm);
+                const float2* xsv =
+                    reinterpret_cast<const float2*>(sxs + (size_t)s * C::kSBytes) + ((j & 1) * N + col0 + c) / 2;
 #pragma unroll
-                for (int c = 0; c < C::kCols; c += C::kChunk) {
-                    uint32_t hv[C::kChunk], lv[C::kChunk];
-                    tmem_ld<C::kChunk>(tcol + c, hv);
-                    tmem_ld<C::kChunk>(tcol + N + c, lv);
-                    tmem_wait_ld();
-                    if (c + C::kChunk >= C::kCols) {   // slot drained: hand it back to the MMA warp
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&tempty[t]);
-                    }
+                for (int k = 0; k < kCh; k += 2) {
+                    const float2 th = make_float2(__uint_as_float(hv[k]), __uint_as_float(hv[k + 1]));
+                    const float2 tl = make_float2(__uint_as_float(lv[k]), __uint_as_float(lv[k + 1]));
+                    const float2 fd = __fadd2_rn(__fadd2_rn(th, neg_magic), tl);
+                    acc[(c + k) / 2] = __ffma2_rn(fd, __fmul2_rn(sm2, xsv[k / 2]), acc[(c + k) / 2]);
+                    if constexpr (DOTS) {
 #pragma unroll
-                    for (int i = 0; i < C::kChunk; i++) {
-                        const int D = (int)hv[i] * 256 + (int)lv[i];
-                        acc[c + i] = fmaf(i2f_rn(D), sm * xsv[c + i], acc[c + i]);
-                        if constexpr (DOTS) {
-                            const int b = nt * N + chalf * C::kCols + c + i;
-                            if (row_ok && b < B) dots[((size_t)b * M + m) * nb + j] = D;
+                        for (int w = 0; w < 2; w++) {
+                            const int D = (int)(hv[k + w] - kMagicHi) * 256 + (int)(lv[k + w] - kMagicLo);
+                            const int b = nt * N + col0 + c + k + w;
+                            if (row_ok && b < B) info.dots[((size_t)b * M + m) * nb + j] = D;
                         }
                     }
                 }
-                if (h == 1 || j == nb - 1) {   // this warp is done with the stage's scales
+            };
+            // this warp is done with a stage's scales after the stage's last block
+            auto release_stage = [&](int j) {
+                if ((j & 1) || j == nb - 1) {
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&empty[s]);
+                    if (lane == 0) mbar_arrive(&empty[(gs + (j >> 1)) % C::kStages]);
                 }
+            };
+
+            for (int j0 = 0; j0 < nb; j0 += G) {
+                const int ng = min(G, nb - j0);
+                uint32_t ev[G];
+#pragma unroll
+                for (int g = 0; g < G; g++) ev[g] = g < ng ? (uint32_t)erow[j0 + g] : 0u;
+                // the group's commit covers all of its MMAs (and every earlier one)
+                if (!warp_wait(&tfull[gg % C::kGroupsInFlight], (gg / C::kGroupsInFlight) & 1, p.err)) {
+                    bad = true;
+                    break;
+                }
+                gg++;
+                tc_fence_after();
+                if constexpr (G > 1) {
+                    uint32_t hv[G][C::kCols], lv[G][C::kCols];
+#pragma unroll
+                    for (int g = 0; g < G; g++)
+                        if (g < ng) {
+                            const uint32_t tcol = tmem + lane_base + (uint32_t)(((gb + g) % C::kSlots) * 2 * N + col0);
+                            tmem_ld<C::kCols>(tcol, hv[g]);
+                            tmem_ld<C::kCols>(tcol + N, lv[g]);
+                        }
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int g = 0; g < G; g++)
+#pragma unroll
+                        for (int k = 0; k < C::kCols; k++) asm volatile("" : "+r"(hv[g][k]), "+r"(lv[g][k]));
+#pragma unroll
+                    for (int g = 0; g < G; g++)
+                        if (g < ng) {   // preset the slots for their next blocks
+                            const uint32_t tcol = tmem + lane_base + (uint32_t)(((gb + g) % C::kSlots) * 2 * N + col0);
+                            tmem_st_rep<C::kCols>(tcol, kMagicHi);
+                            tmem_st_rep<C::kCols>(tcol + N, kMagicLo);
+                        }
+#pragma unroll
+                    for (int g = 0; g < G; g++)
+                        if (g < ng) {
+                            accumulate(hv[g], lv[g], 0, C::kCols, j0 + g, ev[g]);
+                            release_stage(j0 + g);
+                        }
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0)
+                        for (int g = 0; g < ng; g++) mbar_arrive(&tempty[(gb + g) % C::kSlots]);
+                } else {
+                    const uint32_t tcol = tmem + lane_base + (uint32_t)((gb % C::kSlots) * 2 * N + col0);
+                    uint32_t hv[2][C::kChunk], lv[2][C::kChunk];
+                    tmem_ld<C::kChunk>(tcol, hv[0]);
+                    tmem_ld<C::kChunk>(tcol + N, lv[0]);
+#pragma unroll
+                    for (int c = 0, ci = 0; c < C::kCols; c += C::kChunk, ci++) {
+                        tmem_wait_ld_dep<C::kChunk>(hv[ci & 1], lv[ci & 1]);
+                        tmem_st_rep<C::kChunk>(tcol + c, kMagicHi);   // preset for the slot's next block
+                        tmem_st_rep<C::kChunk>(tcol + N + c, kMagicLo);
+                        if (c + C::kChunk < C::kCols) {   // next piece loads while this one is summed
+                            tmem_ld<C::kChunk>(tcol + c + C::kChunk, hv[(ci + 1) & 1]);
+                            tmem_ld<C::kChunk>(tcol + N + c + C::kChunk, lv[(ci + 1) & 1]);
+                        }
+                        accumulate(hv[ci & 1], lv[ci & 1], c, C::kChunk, j0, ev[0]);
+                    }
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[gb % C::kSlots]);
+                    release_stage(j0);
+                }
+                gb += ng;
             }
             gs += (nb + 1) >> 1;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&uempty[eb]);   // unit entry and exponent tile consumed
             if (bad) break;
             if (row_ok) {
-                float* y = d->y;
+                float* y = info.y;
 #pragma unroll
-                for (int i = 0; i < C::kCols; i++) {
-                    const int b = nt * N + chalf * C::kCols + i;
-                    if (b < B) y[(size_t)b * M + m] = acc[i];
+                for (int k = 0; k < C::kCols; k += 2) {
+                    const int b = nt * N + col0 + k;
+                    if (b < B) y[(size_t)b * M + m] = acc[k / 2].x;
+                    if (b + 1 < B) y[(size_t)(b + 1) * M + m] = acc[k / 2].y;
                 }
             }
         }
@@ -346,7 +560,10 @@ __global__ void __launch_bounds__(256) quant_planes_kernel(const float* x, int B
             q0 = __float2int_rn(__fmul_rn(v.x, q));
             q1 = __float2int_rn(__fmul_rn(v.y, q));
         }
-        const uint32_t hi = ((uint32_t)(q0 >> 8) & 0xFFu) | (((uint32_t)(q1 >> 8) & 0xFFu) << 8);
+        // xq = 256*hi + lo with lo the low byte read as a signed int8 and
+        // hi = (xq - lo) / 256 in [-64, 64]: both planes are signed int8
+        const int l0 = (int)(int8_t)(q0 & 0xFF), l1 = (int)(int8_t)(q1 & 0xFF);
+        const uint32_t hi = ((uint32_t)((q0 - l0) >> 8) & 0xFFu) | (((uint32_t)((q1 - l1) >> 8) & 0xFFu) << 8);
         const uint32_t lo = ((uint32_t)q0 & 0xFFu) | (((uint32_t)q1 & 0xFFu) << 8);
         *reinterpret_cast<uint16_t*>(planes + off) = (uint16_t)hi;
         *reinterpret_cast<uint16_t*>(planes + (size_t)B * K + off) = (uint16_t)lo;
@@ -450,6 +667,7 @@ static cudaError_t launch_b(const TcDesc* dev_descs, const TcDesc* one, int n, i
 cudaError_t launch_gemm_tc(const TcDesc* dev_descs, const TcDesc* one, int n, int total_units, int B, bool dots,
                            unsigned int* err, cudaStream_t stream) {
     if (total_units <= 0) return cudaSuccess;
+    if (n < 1 || n > kTcMaxDescs || (!dev_descs && !one)) return cudaErrorInvalidValue;
     return dots ? launch_b<true>(dev_descs, one, n, total_units, B, err, stream)
                 : launch_b<false>(dev_descs, one, n, total_units, B, err, stream);
 }

@@ -3,11 +3,12 @@
 // Batched decode runs B sequences through the same weights, so each weight
 // row meets B activation rows: a dense int8 contraction.  The int16 block-64
 // activations (xq in [-16384, 16384], one f32 scale per 64-block) are stored
-// as two int8 planes, xq = 256*hi + lo with hi = xq >> 8 (signed, -64..64)
-// and lo = xq & 255 (unsigned), so the tensor cores compute both halves of
-// every block dot exactly in int32 (tcgen05.mma kind::i8, signed x signed and
-// signed x unsigned) and the epilogue recombines D = 256*Dhi + Dlo -- the same
-// integer the batch-1 kernel forms with dp2a.  Per block the epilogue adds
+// as two signed int8 planes, xq = 256*hi + lo with lo the low byte of xq read
+// as a signed int8 (-128..127) and hi = (xq - lo) / 256 (-64..64), so the
+// tensor cores compute both halves of every block dot exactly in int32
+// (tcgen05.mma kind::i8, one signed x signed MMA over both planes) and the
+// epilogue recombines D = 256*Dhi + Dlo -- the same integer the batch-1
+// kernel forms with dp2a.  Per block the epilogue adds
 // float(D) * 2^(e-134) * xs to an f32 accumulator (order: blocks ascending,
 // one fused multiply-add each), which agrees with the reference's NEON
 // combine to a few ulp of the sum of |terms|.
@@ -46,6 +47,9 @@ bool tc_make_desc(TcDesc* d, float* y, const void* planes, const float* xs_t, in
 
 // Units (tiles) of one descriptor after tc_make_desc.
 int tc_units(const TcDesc& d);
+
+// GEMMs one launch takes (a grouped plan of more is split into launches).
+constexpr int kTcMaxDescs = 160;
 
 // Launch: `dev_descs` (device array of n descriptors with unit_begin set,
 // largest K first) or, when it is null, the single descriptor `one`.  With

@@ -165,10 +165,15 @@ struct StackPlan {
 };
 std::vector<StackPlan> g_plans;
 
-// Grouped batched tensor-core plans.
+// Grouped batched tensor-core plans: launches of at most qb::kTcMaxDescs
+// GEMMs each (deepest first), their descriptors in one device array.
+struct TcLaunchPart {
+    int first, n, total_units;
+};
 struct TcPlan {
     qb::TcDesc* dev_descs = nullptr;
-    int n = 0, total_units = 0, B = 0;
+    std::vector<TcLaunchPart> parts;
+    int B = 0;
     bool live = false;
 };
 std::vector<TcPlan> g_tc_plans;
@@ -693,11 +698,14 @@ int qwen_b200_tc_stack_create(int n, const int8_t* const* mant, const uint8_t* c
     // deepest matrices first, so the round-robin tail is made of short units
     std::stable_sort(v.begin(), v.end(), [](const qb::TcDesc& a, const qb::TcDesc& b) { return a.K > b.K; });
     TcPlan tp;
-    for (auto& d : v) {
-        d.unit_begin = tp.total_units;
-        tp.total_units += qb::tc_units(d);
+    for (int first = 0; first < (int)v.size(); first += qb::kTcMaxDescs) {
+        TcLaunchPart part{first, std::min(qb::kTcMaxDescs, (int)v.size() - first), 0};
+        for (int k = first; k < first + part.n; k++) {
+            v[k].unit_begin = part.total_units;
+            part.total_units += qb::tc_units(v[k]);
+        }
+        tp.parts.push_back(part);
     }
-    tp.n = (int)v.size();
     tp.B = B;
     cudaError_t e = cudaMalloc(&tp.dev_descs, sizeof(qb::TcDesc) * (v.empty() ? 1 : v.size()));
     if (e != cudaSuccess) return fail(QB_ENOMEM, "tc_stack alloc", e);
@@ -715,9 +723,12 @@ int qwen_b200_tc_stack_run(int plan, void* stream) {
     const TcPlan& tp = g_tc_plans[plan - 1];
     DevState* st = nullptr;
     if (int rc = dev_state(&st)) return rc;
-    cudaError_t e = qb::launch_gemm_tc(tp.dev_descs, nullptr, tp.n, tp.total_units, tp.B, false, st->err,
-                                       static_cast<cudaStream_t>(stream));
-    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_tc_stack_run", e);
+    for (const TcLaunchPart& part : tp.parts) {
+        cudaError_t e = qb::launch_gemm_tc(tp.dev_descs + part.first, nullptr, part.n, part.total_units, tp.B, false,
+                                           st->err, static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return fail(QB_ECUDA, "qwen_b200_tc_stack_run", e);
+    }
+    return QB_OK;
 }
 
 int qwen_b200_tc_stack_destroy(int plan) {

@@ -183,3 +183,63 @@ class DeviceStack:
             exps = buf[off + t.mant_bytes: off + t.mant_bytes + t.exp_bytes].view(t.M, t.K // 64)
             out.append((self.x[i], mant, exps, self.y[i]))
         return out
+
+
+def batched_bytes(stack, B: int) -> dict:
+    """Algorithmic bytes and work of one batched step (B sequences through
+    every GEMM): weights once, planar int16 activations (2 B per element)
+    and their block scales in, fp32 outputs out."""
+    w = sum(t.mant_bytes + t.exp_bytes for t in stack)
+    io = sum(B * (2 * t.K + 4 * (t.K // 64) + 4 * t.M) for t in stack)
+    macs = sum(t.M * t.K for t in stack)
+    return {"weights": w, "io": io, "total": w + io, "macs": macs, "int_ops": 2 * macs * B,
+            "tensor_ops": 4 * macs * B}
+
+
+class DeviceBatch:
+    """Activations of B sequences for every GEMM of a stack, as planar int16
+    (ops.Planes), plus the outputs, in three flat device buffers per set (so a
+    step's inputs or outputs move in one copy).  Each set holds fresh fp32
+    N(0, 1) rows quantized on the device; benchmarks pair set c with weight
+    copy c."""
+
+    def __init__(self, stack, B, sets=1, device="cuda", seed=0):
+        import torch
+
+        from . import ops
+
+        self.stack = list(stack)
+        self.B = B
+        self.device = torch.device(device)
+        ldxs = (B + 3) // 4 * 4
+        self.ldxs = ldxs
+        po, so, yo = [], [], []
+        npl = nsc = ny = 0
+        for t in self.stack:
+            po.append(npl)
+            so.append(nsc)
+            yo.append(ny)
+            npl += 2 * B * t.K
+            nsc += (t.K // 64) * ldxs
+            ny += (B * t.M + 3) & ~3
+        self.sets = []
+        g = torch.Generator(device=self.device)
+        for s in range(sets):
+            g.manual_seed(seed * 1000 + s)
+            planes = torch.empty(npl, dtype=torch.int8, device=self.device)
+            scales = torch.zeros(nsc, dtype=torch.float32, device=self.device)
+            ys = torch.zeros(ny, dtype=torch.float32, device=self.device)
+            items = []
+            for i, t in enumerate(self.stack):
+                nb = t.K // 64
+                p = ops.Planes(planes[po[i]:po[i] + 2 * B * t.K].view(2, B, t.K),
+                               scales[so[i]:so[i] + nb * ldxs].view(nb, ldxs), B, t.K)
+                x = torch.randn((B, t.K), generator=g, device=self.device, dtype=torch.float32)
+                ops.quant_planes(x, out=p)
+                items.append((p, ys[yo[i]:yo[i] + B * t.M].view(B, t.M)))
+            self.sets.append({"planes": planes, "scales": scales, "y": ys, "items": items})
+
+    def items(self, weights, s=0):
+        """[(Planes, mant, exps, y)] for ops.BatchedStack: set s against the
+        (x, mant, exps, y) views of a DeviceStack copy."""
+        return [(p, m, e, y) for (p, y), (_, m, e, _) in zip(self.sets[s]["items"], weights)]

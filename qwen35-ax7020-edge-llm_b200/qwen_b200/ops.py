@@ -99,8 +99,9 @@ def bfp8_gemv_q(xq: torch.Tensor, xs: torch.Tensor, mant: torch.Tensor, exps: to
 
 @dataclass
 class Planes:
-    """Batched int16 block-64 activations as two int8 planes (xq = 256*hi + lo):
-    ``planes`` int8 [2, B, K] (plane 0 = hi, plane 1 = lo as raw bytes) and
+    """Batched int16 block-64 activations as two signed int8 planes
+    (xq = 256*hi + lo, lo the low byte of xq as a signed int8):
+    ``planes`` int8 [2, B, K] (plane 0 = hi, plane 1 = lo) and
     block scales ``xs_t`` fp32 [K/64, ldxs] (block-major, first B columns used)."""
     planes: torch.Tensor
     xs_t: torch.Tensor
@@ -114,7 +115,7 @@ class Planes:
     def xq(self) -> torch.Tensor:
         """The int16 activations [B, K] these planes encode."""
         hi = self.planes[0].to(torch.int32)
-        lo = self.planes[1].view(torch.uint8).to(torch.int32)
+        lo = self.planes[1].to(torch.int32)
         return (hi * 256 + lo).to(torch.int16)
 
     def xs(self) -> torch.Tensor:

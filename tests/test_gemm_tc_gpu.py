@@ -165,3 +165,28 @@ def test_batched_stack_matches_single_launches(cuda):
     from qwen_b200 import _lib
 
     assert _lib.load().qwen_b200_device_error(1) == 0
+
+
+def test_batched_stack_split_over_launches(cuda):
+    """More GEMMs than one launch takes (160): the plan runs as several
+    launches and still matches single launches bit for bit."""
+    import torch
+
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(23)
+    B = 8
+    items, singles = [], []
+    for i in range(170):
+        M, K = (128, 128) if i % 3 else (256, 192)
+        mant, exps = rand_weights(rng, M, K)
+        dm, de = torch.from_numpy(mant).cuda(), torch.from_numpy(exps).cuda()
+        p = ops.quant_planes(torch.from_numpy(rng.normal(0, 1, (B, K)).astype(np.float32)).cuda())
+        items.append((p, dm, de, torch.full((B, M), float("nan"), device="cuda")))
+        singles.append(ops.bfp8_gemm_tc(p, dm, de))
+    st = ops.BatchedStack(items)
+    st.run()
+    torch.cuda.synchronize()
+    for (_, _, _, y), ys in zip(items, singles):
+        assert np.array_equal(bits(y.cpu().numpy()), bits(ys.cpu().numpy()))
+    st.close()
