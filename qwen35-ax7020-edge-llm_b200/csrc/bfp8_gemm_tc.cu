@@ -37,7 +37,12 @@ namespace {
 constexpr int kTcThreads = 320;
 constexpr int kEpiWarps = 8;
 constexpr int kTileRows = 128;
-constexpr int kStageK = 128;   // K bytes per pipeline stage (two 64-blocks)
+constexpr int kBoxK = 128;     // K bytes of one TMA box (one 128-byte swizzled row per matrix row)
+
+// 64-blocks per pipeline stage: four for narrow tiles (so the single TMA and
+// MMA threads pay their per-stage barrier work once per 32 KB of weights),
+// two for wide ones (shared memory holds fewer, larger stages).
+__host__ __device__ constexpr int tc_blocks_per_stage(int N) { return N <= 32 ? 4 : 2; }
 
 constexpr int kExpsMax = 56;   // block exponents per row staged in shared memory (K <= 3584)
 constexpr int kMaxTable = kTcMaxDescs;   // GEMMs per launch (their scalar fields are kept in shared memory)
@@ -74,13 +79,16 @@ struct UnitInfo {
 
 template <int N>
 struct TcCfg {
-    static constexpr int kStages = N >= 128 ? 4 : (N >= 64 ? 6 : 8);
+    static constexpr int kBPS = tc_blocks_per_stage(N);
+    static constexpr int kStageK = 64 * kBPS;                        // K bytes per stage
+    static constexpr int kBoxes = kStageK / kBoxK;                   // TMA boxes per operand per stage
+    static constexpr int kStages = N >= 128 ? 4 : (N >= 64 ? 6 : (N >= 32 ? 4 : 5));
     static constexpr int kSlots = (256 / N) < 8 ? (256 / N) : 8;
     static constexpr int kTmemCols = kSlots * 2 * N;   // 128..512, a power of two
     static constexpr int kWBytes = kTileRows * kStageK;
     static constexpr int kXBytes = 2 * N * kStageK;
     static constexpr int kStageBytes = kWBytes + kXBytes;
-    static constexpr int kSBox = 2 * N * 4;                          // scale bytes per stage
+    static constexpr int kSBox = kBPS * N * 4;                       // scale bytes per stage
     static constexpr int kSBytes = kSBox < 128 ? 128 : kSBox;        // 128-byte aligned slots
     static constexpr int kTxBytes = kStageBytes + kSBox;
     static constexpr int kCols = N / 2;                              // columns per epilogue thread
@@ -310,7 +318,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                     tma_prefetch_desc(&dn->tm_s);
                 }
                 const int local = u - r.unit_begin, rt = local / r.n_nt, nt = local - rt * r.n_nt;
-                const int nb = r.nb, nst = (nb + 1) >> 1;
+                const int nb = r.nb, nst = (nb + C::kBPS - 1) / C::kBPS;
                 const int eb = i & 1;
                 const int rows = min(kTileRows, r.M - rt * kTileRows);
                 const uint32_t ebytes = (uint32_t)rows * (uint32_t)nb;
@@ -342,9 +350,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                     }
                     unsigned char* sm = stages + (size_t)s * C::kStageBytes;
                     mbar_arrive_expect_tx(&full[s], C::kTxBytes);
-                    tma_load_2d(sm, &d->tm_w, st * kStageK, rt * kTileRows, &full[s]);
-                    tma_load_3d(sm + C::kWBytes, &d->tm_x, st * kStageK, nt * N, 0, &full[s]);
-                    tma_load_2d(sxs + (size_t)s * C::kSBytes, &d->tm_s, nt * N, st * 2, &full[s]);
+#pragma unroll
+                    for (int bx = 0; bx < C::kBoxes; bx++) {
+                        const int x = st * C::kStageK + bx * kBoxK;
+                        tma_load_2d(sm + bx * (kTileRows * kBoxK), &d->tm_w, x, rt * kTileRows, &full[s]);
+                        tma_load_3d(sm + C::kWBytes + bx * (2 * N * kBoxK), &d->tm_x, x, nt * N, 0, &full[s]);
+                    }
+                    tma_load_2d(sxs + (size_t)s * C::kSBytes, &d->tm_s, nt * N, st * C::kBPS, &full[s]);
                 }
             }
             // the last loads of every slot have landed unless a consumer quit early
@@ -360,7 +372,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
             bool bad = false;
             for (int u = blockIdx.x, i = 0; u < p.total_units && !bad; u += gridDim.x, i++) {
                 if (!mbar_wait(&ufull[i & 1], (i >> 1) & 1, p.err)) break;
-                const int nb = uring[i & 1].nb, nst = (nb + 1) >> 1;
+                const int nb = uring[i & 1].nb, nst = (nb + C::kBPS - 1) / C::kBPS;
                 for (int st = 0; st < nst && !bad; st++, gs++) {
                     const int s = gs % C::kStages;
                     if (!mbar_wait(&full[s], (gs / C::kStages) & 1, p.err)) {
@@ -369,17 +381,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                     }
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(stages + (size_t)s * C::kStageBytes);
-                    const uint64_t da = desc_sw128(a0), dx = desc_sw128(a0 + C::kWBytes);
-                    for (int h = 0; h < 2 && 2 * st + h < nb; h++, gb++) {
-                        const int t = gb % C::kSlots, j = 2 * st + h;
-                        if (!mbar_wait(&tempty[t], ((gb / C::kSlots) & 1) ^ 1, p.err)) {
-                            bad = true;
-                            break;
+                    for (int h = 0; h < C::kBPS && st * C::kBPS + h < nb; h++, gb++) {
+                        const int t = gb % C::kSlots, j = st * C::kBPS + h;
+                        if (j % G == 0) {   // the epilogue frees a group's slots together: wait for its last
+                            const uint32_t gl = gb + (uint32_t)(min(G, nb - j) - 1);
+                            if (!mbar_wait(&tempty[gl % C::kSlots], ((gl / C::kSlots) & 1) ^ 1, p.err)) {
+                                bad = true;
+                                break;
+                            }
+                            tc_fence_after();
                         }
-                        tc_fence_after();
+                        const int bx = h >> 1;   // which 128-byte box of the stage holds block j
+                        const uint64_t da = desc_sw128(a0 + bx * (kTileRows * kBoxK)),
+                                       dx = desc_sw128(a0 + C::kWBytes + bx * (2 * N * kBoxK));
 #pragma unroll
                         for (int kk = 0; kk < 2; kk++) {   // every step accumulates onto the preset
-                            const uint64_t off = (uint64_t)((h * 64 + kk * 32) >> 4);
+                            const uint64_t off = (uint64_t)(((h & 1) * 64 + kk * 32) >> 4);
                             mma_i8(tmem + (uint32_t)(t * 2 * N), da + off, dx + off, kId, 1u);
                         }
                         if (j % G == G - 1 || j == nb - 1) {   // a group of blocks is complete
@@ -415,11 +432,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
             // acc += float(256*Dhi + Dlo) * 2^(e-134) * xs over kCh columns
             // starting at column c of block j; hv/lv are the raw accumulators.
             auto accumulate = [&](const uint32_t* hv, const uint32_t* lv, int c, int kCh, int j, uint32_t e) {
-                const int s = (gs + (j >> 1)) % C::kStages;
+                const int s = (gs + j / C::kBPS) % C::kStages;
                 const float sm = exp_scale_ieee(e);
                 const float2 sm2 = make_float2(sm, sm);
                 const float2* xsv =
-                    reinterpret_cast<const float2*>(sxs + (size_t)s * C::kSBytes) + ((j & 1) * N + col0 + c) / 2;
+                    reinterpret_cast<const float2*>(sxs + (size_t)s * C::kSBytes) + ((j % C::kBPS) * N + col0 + c) / 2;
 #pragma unroll
                 for (int k = 0; k < kCh; k += 2) {
                     const float2 th = make_float2(__uint_as_float(hv[k]), __uint_as_float(hv[k + 1]));
@@ -438,9 +455,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
             };
             // this warp is done with a stage's scales after the stage's last block
             auto release_stage = [&](int j) {
-                if ((j & 1) || j == nb - 1) {
+                if (j % C::kBPS == C::kBPS - 1 || j == nb - 1) {
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&empty[(gs + (j >> 1)) % C::kStages]);
+                    if (lane == 0) mbar_arrive(&empty[(gs + j / C::kBPS) % C::kStages]);
                 }
             };
 
@@ -512,7 +529,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 }
                 gb += ng;
             }
-            gs += (nb + 1) >> 1;
+            gs += (nb + C::kBPS - 1) / C::kBPS;
             __syncwarp();
             if (lane == 0) mbar_arrive(&uempty[eb]);   // unit entry and exponent tile consumed
             if (bad) break;
@@ -575,6 +592,7 @@ template <int N, bool DOTS>
 cudaError_t launch_n(const TcDesc* dev_descs, const TcDesc* one, int n, int total_units, unsigned int* err,
                      cudaStream_t stream) {
     using C = TcCfg<N>;
+    static_assert(C::kSmem <= 232448, "shared memory plan exceeds 227 KB");
     static unsigned long long attr_set = 0;   // one bit per device
     int dev = 0;
     cudaGetDevice(&dev);
@@ -618,22 +636,22 @@ bool tc_make_desc(TcDesc* d, float* y, const void* planes, const float* xs_t, in
     {   // weights: [M][K] bytes, box 128 B x 128 rows
         const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
         const uint64_t str[1] = {(uint64_t)K};
-        const uint32_t box[2] = {(uint32_t)kStageK, (uint32_t)kTileRows};
+        const uint32_t box[2] = {(uint32_t)kBoxK, (uint32_t)kTileRows};
         if (!encode_tmap(&d->tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, mant, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
             return false;
     }
     {   // activation planes: [2][B][K] bytes, box 128 B x N rows x 2 planes
         const uint64_t dims[3] = {(uint64_t)K, (uint64_t)B, 2};
         const uint64_t str[2] = {(uint64_t)K, (uint64_t)B * (uint64_t)K};
-        const uint32_t box[3] = {(uint32_t)kStageK, (uint32_t)N, 2};
+        const uint32_t box[3] = {(uint32_t)kBoxK, (uint32_t)N, 2};
         if (!encode_tmap(&d->tm_x, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, planes, dims, str, box,
                          CU_TENSOR_MAP_SWIZZLE_128B))
             return false;
     }
-    {   // scales: [nb][ldxs] f32, box N columns x 2 blocks
+    {   // scales: [nb][ldxs] f32, box N columns x (blocks per stage)
         const uint64_t dims[2] = {(uint64_t)B, (uint64_t)(K / 64)};
         const uint64_t str[1] = {(uint64_t)ldxs * 4};
-        const uint32_t box[2] = {(uint32_t)N, 2};
+        const uint32_t box[2] = {(uint32_t)N, (uint32_t)tc_blocks_per_stage(N)};
         if (!encode_tmap(&d->tm_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, xs_t, dims, str, box,
                          CU_TENSOR_MAP_SWIZZLE_NONE))
             return false;
