@@ -34,8 +34,6 @@
 namespace qb {
 namespace {
 
-constexpr int kTcThreads = 320;
-constexpr int kEpiWarps = 8;
 constexpr int kTileRows = 128;
 constexpr int kBoxK = 128;     // K bytes of one TMA box (one 128-byte swizzled row per matrix row)
 
@@ -91,7 +89,12 @@ struct TcCfg {
     static constexpr int kSBox = kBPS * N * 4;                       // scale bytes per stage
     static constexpr int kSBytes = kSBox < 128 ? 128 : kSBox;        // 128-byte aligned slots
     static constexpr int kTxBytes = kStageBytes + kSBox;
-    static constexpr int kCols = N / 2;                              // columns per epilogue thread
+    // Epilogue warps: four per 32-lane TMEM quarter for wide tiles (each warp
+    // a quarter of the columns), two for narrow ones.
+    static constexpr int kEpiWarps = N >= 64 ? 16 : 8;
+    static constexpr int kColSplit = kEpiWarps / 4;
+    static constexpr int kThreads = 64 + 32 * kEpiWarps;
+    static constexpr int kCols = N / kColSplit;                      // columns per epilogue thread
     // Small tiles: the epilogue takes kGroup blocks per round (one barrier
     // wait, one TMEM load wait and one store wait for all of them).  Large
     // tiles: one block per round, its columns in kChunk pieces whose TMEM
@@ -99,7 +102,15 @@ struct TcCfg {
     static constexpr int kGroup = N <= 16 ? 4 : (N <= 32 ? 2 : 1);
     static constexpr int kChunk = kGroup > 1 ? kCols : 8;
     static constexpr int kPreset = kCols < 16 ? kCols : 16;
+    // true: the epilogue re-arms each drained slot with the bias patterns
+    // (tcgen05.st) and every MMA step accumulates; false: a block's first MMA
+    // step overwrites the slot and the epilogue adds the bias patterns to the
+    // loaded integers (two integer adds per dot, no TMEM stores).
+    static constexpr bool kPresets = false;
     static constexpr int kGroupsInFlight = kSlots / kGroup;
+    // blocks whose TMEM slots the MMA thread claims with one wait (whole
+    // epilogue groups, at most half of the slots)
+    static constexpr int kWaitSpan = kGroup > kSlots / 2 ? kGroup : kSlots / 2 < 4 ? kSlots / 2 : 4;
     static constexpr size_t kSmem = 1024 + (size_t)kStages * (kStageBytes + kSBytes) + 2 * (size_t)kEBytes +
                                     2 * sizeof(UnitInfo) + (size_t)kMaxTable * sizeof(DescRow) +
                                     (size_t)(2 * kStages + kGroupsInFlight + kSlots + 5) * 8 + 16;
@@ -179,6 +190,18 @@ __device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, uint32_t (&v)[16]) {
         : "r"(taddr));
 }
 
+template <>
+__device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+}
+
 // Store one 32-bit value into C consecutive columns of the warp's 32 lanes.
 template <int C>
 __device__ __forceinline__ void tmem_st_rep(uint32_t taddr, uint32_t v);
@@ -199,6 +222,11 @@ __device__ __forceinline__ void tmem_st_rep<16>(uint32_t taddr, uint32_t v) {
         "%1};" ::"r"(taddr),
         "r"(v)
         : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_st_rep<32>(uint32_t taddr, uint32_t v) {
+    tmem_st_rep<16>(taddr, v);
+    tmem_st_rep<16>(taddr + 16, v);
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -229,7 +257,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, unsign
 }
 
 template <int N, bool DOTS>
-__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ TcLaunch p) {
+__global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __grid_constant__ TcLaunch p) {
     using C = TcCfg<N>;
     extern __shared__ unsigned char tc_smem_raw[];
     unsigned char* base =
@@ -267,13 +295,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kStages; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kEpiWarps);   // every epilogue warp, after the stage's MMAs completed
+            mbar_init(&empty[s], C::kEpiWarps);   // every epilogue warp, after the stage's MMAs completed
         }
         for (int g = 0; g < C::kGroupsInFlight; g++) mbar_init(&tfull[g], 1);
-        for (int t = 0; t < C::kSlots; t++) mbar_init(&tempty[t], kEpiWarps);
+        for (int t = 0; t < C::kSlots; t++) mbar_init(&tempty[t], C::kEpiWarps);
         for (int b = 0; b < 2; b++) {
             mbar_init(&ufull[b], 1);
-            mbar_init(&uempty[b], kEpiWarps);
+            mbar_init(&uempty[b], C::kEpiWarps);
         }
         mbar_init(done, 1);
         fence_barrier_init();
@@ -283,9 +311,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int q = warp & 3, chalf = (warp - 2) >> 2;
+    const int q = warp & 3, chalf = (warp - 2) >> 2;   // TMEM lane quarter, column slice
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    if (warp >= 2) {   // preset every accumulator slot before the first MMA
+    if (C::kPresets && warp >= 2) {   // preset every accumulator slot before the first MMA
         for (int t = 0; t < C::kSlots; t++) {
             const uint32_t tcol = tmem + lane_base + (uint32_t)(t * 2 * N + chalf * C::kCols);
 #pragma unroll
@@ -383,8 +411,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                     const uint32_t a0 = smem_u32(stages + (size_t)s * C::kStageBytes);
                     for (int h = 0; h < C::kBPS && st * C::kBPS + h < nb; h++, gb++) {
                         const int t = gb % C::kSlots, j = st * C::kBPS + h;
-                        if (j % G == 0) {   // the epilogue frees a group's slots together: wait for its last
-                            const uint32_t gl = gb + (uint32_t)(min(G, nb - j) - 1);
+                        if (j % C::kWaitSpan == 0) {   // slots free in order: wait for the span's last one
+                            const uint32_t gl = gb + (uint32_t)(min(C::kWaitSpan, nb - j) - 1);
                             if (!mbar_wait(&tempty[gl % C::kSlots], ((gl / C::kSlots) & 1) ^ 1, p.err)) {
                                 bad = true;
                                 break;
@@ -395,9 +423,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                         const uint64_t da = desc_sw128(a0 + bx * (kTileRows * kBoxK)),
                                        dx = desc_sw128(a0 + C::kWBytes + bx * (2 * N * kBoxK));
 #pragma unroll
-                        for (int kk = 0; kk < 2; kk++) {   // every step accumulates onto the preset
+                        for (int kk = 0; kk < 2; kk++) {
                             const uint64_t off = (uint64_t)(((h & 1) * 64 + kk * 32) >> 4);
-                            mma_i8(tmem + (uint32_t)(t * 2 * N), da + off, dx + off, kId, 1u);
+                            mma_i8(tmem + (uint32_t)(t * 2 * N), da + off, dx + off, kId,
+                                   C::kPresets ? 1u : (uint32_t)kk);
                         }
                         if (j % G == G - 1 || j == nb - 1) {   // a group of blocks is complete
                             mma_commit(&tfull[gg % C::kGroupsInFlight]);
@@ -486,10 +515,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
 #pragma unroll
                     for (int g = 0; g < G; g++)
 #pragma unroll
-                        for (int k = 0; k < C::kCols; k++) asm volatile("" : "+r"(hv[g][k]), "+r"(lv[g][k]));
+                        for (int k = 0; k < C::kCols; k++) {
+                            asm volatile("" : "+r"(hv[g][k]), "+r"(lv[g][k]));
+                            if constexpr (!C::kPresets) {
+                                hv[g][k] += kMagicHi;
+                                lv[g][k] += kMagicLo;
+                            }
+                        }
 #pragma unroll
                     for (int g = 0; g < G; g++)
-                        if (g < ng) {   // preset the slots for their next blocks
+                        if (C::kPresets && g < ng) {   // preset the slots for their next blocks
                             const uint32_t tcol = tmem + lane_base + (uint32_t)(((gb + g) % C::kSlots) * 2 * N + col0);
                             tmem_st_rep<C::kCols>(tcol, kMagicHi);
                             tmem_st_rep<C::kCols>(tcol + N, kMagicLo);
@@ -500,7 +535,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                             accumulate(hv[g], lv[g], 0, C::kCols, j0 + g, ev[g]);
                             release_stage(j0 + g);
                         }
-                    tmem_wait_st();
+                    if constexpr (C::kPresets) tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0)
@@ -513,15 +548,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
 #pragma unroll
                     for (int c = 0, ci = 0; c < C::kCols; c += C::kChunk, ci++) {
                         tmem_wait_ld_dep<C::kChunk>(hv[ci & 1], lv[ci & 1]);
-                        tmem_st_rep<C::kChunk>(tcol + c, kMagicHi);   // preset for the slot's next block
-                        tmem_st_rep<C::kChunk>(tcol + N + c, kMagicLo);
+                        if constexpr (C::kPresets) {   // preset for the slot's next block
+                            tmem_st_rep<C::kChunk>(tcol + c, kMagicHi);
+                            tmem_st_rep<C::kChunk>(tcol + N + c, kMagicLo);
+                        } else {
+#pragma unroll
+                            for (int k = 0; k < C::kChunk; k++) {
+                                hv[ci & 1][k] += kMagicHi;
+                                lv[ci & 1][k] += kMagicLo;
+                            }
+                        }
                         if (c + C::kChunk < C::kCols) {   // next piece loads while this one is summed
                             tmem_ld<C::kChunk>(tcol + c + C::kChunk, hv[(ci + 1) & 1]);
                             tmem_ld<C::kChunk>(tcol + N + c + C::kChunk, lv[(ci + 1) & 1]);
                         }
                         accumulate(hv[ci & 1], lv[ci & 1], c, C::kChunk, j0, ev[0]);
                     }
-                    tmem_wait_st();
+                    if constexpr (C::kPresets) tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tempty[gb % C::kSlots]);
@@ -610,7 +653,7 @@ cudaError_t launch_n(const TcDesc* dev_descs, const TcDesc* one, int n, int tota
     p.err = err;
     if (one) p.one = *one;
     const int grid = std::max(1, std::min(total_units, num_sms()));
-    gemm_tc_kernel<N, DOTS><<<grid, kTcThreads, C::kSmem, stream>>>(p);
+    gemm_tc_kernel<N, DOTS><<<grid, C::kThreads, C::kSmem, stream>>>(p);
     return cudaGetLastError();
 }
 
