@@ -549,6 +549,10 @@ def run_reference(args):
 
 def main():
     args = parse()
+    # the driver reads one JSON line from rank 0's stdout: keep NCCL's version
+    # banner and informational lines off it unless the caller asked for them
+    if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+        os.environ["NCCL_DEBUG"] = "WARN"
     if args.impl == "reference":
         os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count()))
         run_reference(args)
