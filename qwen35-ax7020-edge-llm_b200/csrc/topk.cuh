@@ -74,6 +74,98 @@ __device__ inline void cand_compact(unsigned long long* cand, int* count, int ke
     __syncthreads();
 }
 
+// ---- warp-level top-64: a warp holds 64 keys, element i = r*32 + lane in
+// register a_r.  Bitonic networks on shuffles, no block barrier.
+__device__ __forceinline__ void cx_desc(unsigned long long& a, unsigned long long o, bool keep_max) {
+    a = keep_max ? (a > o ? a : o) : (a < o ? a : o);
+}
+// Merge stages j = 32..1 of a 64-element bitonic sequence into descending order.
+__device__ __forceinline__ void warp_merge64_desc(unsigned long long& a0, unsigned long long& a1) {
+    const int lane = threadIdx.x & 31;
+    {   // j = 32: the partner is the other register of the same lane
+        const unsigned long long hi = a0 > a1 ? a0 : a1, lo = a0 > a1 ? a1 : a0;
+        a0 = hi;
+        a1 = lo;
+    }
+#pragma unroll
+    for (int j = 16; j > 0; j >>= 1) {
+        const unsigned long long o0 = __shfl_xor_sync(0xffffffffu, a0, j);
+        const unsigned long long o1 = __shfl_xor_sync(0xffffffffu, a1, j);
+        const bool low = (lane & j) == 0;   // lower index of the pair keeps the larger key
+        cx_desc(a0, o0, low);
+        cx_desc(a1, o1, low);
+    }
+}
+// Sort 64 keys descending.
+__device__ __forceinline__ void warp_sort64_desc(unsigned long long& a0, unsigned long long& a1) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const unsigned long long o0 = __shfl_xor_sync(0xffffffffu, a0, j);
+            const unsigned long long o1 = __shfl_xor_sync(0xffffffffu, a1, j);
+            const int i0 = lane, i1 = 32 + lane;
+            cx_desc(a0, o0, ((i0 & j) == 0) == ((i0 & k) == 0));
+            cx_desc(a1, o1, ((i1 & j) == 0) == ((i1 & k) == 0));
+        }
+    }
+    // two sorted 32-halves in opposite directions form a bitonic 64-sequence
+    warp_merge64_desc(a0, a1);
+}
+// Number of keys greater than `key` in a descending list a[0..64).
+__device__ __forceinline__ int count_greater64(const unsigned long long* a, unsigned long long key) {
+    int lo = 0, hi = 64;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (a[mid] > key) lo = mid + 1;
+        else hi = mid;
+    }
+    return lo;
+}
+
+// Keep the best `keep` (<= 64) of the n candidate keys, sorted descending at
+// cand[0..min(n, keep)): every warp folds 64-key chunks into its own sorted
+// top-64, then the warps' lists are merged by rank.  Needs kCandCap >=
+// 64 * warps + keep.  Called by the whole block.
+__device__ inline void cand_topk64(unsigned long long* cand, int* count, int keep) {
+    __syncthreads();
+    const int n = *count;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    unsigned long long r0 = 0ull, r1 = 0ull;   // running top-64, descending
+    for (int base = w * 64; base < n; base += nw * 64) {
+        unsigned long long c0 = base + lane < n ? cand[base + lane] : 0ull;
+        unsigned long long c1 = base + 32 + lane < n ? cand[base + 32 + lane] : 0ull;
+        warp_sort64_desc(c0, c1);
+        // max(running[i], chunk[63 - i]) holds the top 64 as a bitonic sequence
+        const unsigned long long x0 = __shfl_sync(0xffffffffu, c1, 31 - lane);
+        const unsigned long long x1 = __shfl_sync(0xffffffffu, c0, 31 - lane);
+        r0 = r0 > x0 ? r0 : x0;
+        r1 = r1 > x1 ? r1 : x1;
+        warp_merge64_desc(r0, r1);
+    }
+    __syncthreads();   // every chunk read
+    unsigned long long* lists = cand;                 // nw sorted lists of 64
+    unsigned long long* out = cand + 64 * nw;
+    lists[w * 64 + lane] = r0;
+    lists[w * 64 + 32 + lane] = r1;
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < nw * keep; idx += blockDim.x) {
+        const int l = idx / keep, i = idx - l * keep;
+        const unsigned long long key = lists[l * 64 + i];
+        if (key == 0ull) continue;
+        int rank = i;
+        for (int o = 0; o < nw; o++)
+            if (o != l) rank += count_greater64(lists + o * 64, key);
+        if (rank < keep) out[rank] = key;
+    }
+    __syncthreads();
+    const int m = n < keep ? n : keep;
+    for (int i = threadIdx.x; i < m; i += blockDim.x) cand[i] = out[i];
+    if (threadIdx.x == 0) *count = m;
+    __syncthreads();
+}
+
 // Block-wide max of a 64-bit key; result valid in every thread.
 __device__ inline unsigned long long block_max_u64(unsigned long long v, unsigned long long* red) {
     for (int o = 16; o > 0; o >>= 1) {
@@ -124,7 +216,10 @@ __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int* c
     if (tid == 0 && bm) atomicMax(&sc->argmax_key, bm);
 
     if (kk > 0) {
-        cand_compact(cand, cand_count, kk);
+        if (kk <= 64 && 64 * (int)(blockDim.x >> 5) + kk <= kCandCap)
+            cand_topk64(cand, cand_count, kk);
+        else
+            cand_compact(cand, cand_count, kk);
         int n = *cand_count;
         unsigned long long* dst = sc->lists + (size_t)blockIdx.x * kk;
         for (int i = tid; i < n; i += blockDim.x) dst[i] = cand[i];
@@ -142,6 +237,96 @@ __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int* c
     if (tid == 0) {
         unsigned long long k = *((volatile unsigned long long*)&sc->argmax_key);
         *out_id = k ? key_id(k) : 0;
+    }
+    if (kk > 0 && (long long)gridDim.x * kk + (gridDim.x + 1) / 2 <= work_cap) {
+        // Fast path: one parallel sweep copies every list into shared memory
+        // (list c at work[c*kk], zero keys past its count), so the selection
+        // below never waits on a chain of global loads.
+        __shared__ int s_m2;
+        __shared__ int s_total2;
+        const int G = gridDim.x;
+        int* s_counts = reinterpret_cast<int*>(work + (size_t)G * kk);   // after the lists
+        if (tid == 0) {
+            s_m2 = 0;
+            s_total2 = 0;
+        }
+        // the other CTAs' lists are complete (their fence precedes their
+        // ticket); read them from L2 with independent loads
+        for (int c = tid; c < G; c += blockDim.x) s_counts[c] = __ldcg(sc->counts + c);
+        __syncthreads();
+        // sixteen independent loads in flight per thread (a load-then-store
+        // loop would wait one L2 round trip per key)
+        const int total_keys = G * kk;
+        for (int base = tid; base < total_keys; base += 16 * blockDim.x) {
+            unsigned long long v[16];
+#pragma unroll
+            for (int u = 0; u < 16; u++) {
+                const int idx = base + u * blockDim.x;
+                v[u] = 0ull;
+                if (idx < total_keys) {
+                    const int c = idx / kk;
+                    if (idx - c * kk < s_counts[c]) v[u] = __ldcg(sc->lists + idx);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 16; u++) {
+                const int idx = base + u * blockDim.x;
+                if (idx < total_keys) work[idx] = v[u];
+            }
+        }
+        __syncthreads();
+        // thresholds: T1 = best kk-th key of a full list, T2 = kk-th best head
+        const int gp = next_pow2(G);
+        unsigned long long t1 = 0ull;
+        int tot = 0;
+        for (int c = tid; c < gp; c += blockDim.x) {
+            cand[c] = c < G ? work[(size_t)c * kk] : 0ull;
+            if (c < G) {
+                const unsigned long long last = work[(size_t)c * kk + kk - 1];
+                t1 = last > t1 ? last : t1;
+                tot += s_counts[c];
+            }
+        }
+        for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+        if (lane == 0) atomicAdd(&s_total2, tot);
+        t1 = block_max_u64(t1, red);   // contains barriers
+        // T2 = the kk-th largest head, by counting (heads are distinct or zero)
+        __shared__ unsigned long long s_t2;
+        if (tid == 0) s_t2 = 0ull;
+        __syncthreads();
+        for (int c = tid; c < G; c += blockDim.x) {
+            const unsigned long long hd = cand[c];
+            if (hd == 0ull) continue;
+            int r = 0;
+            for (int o = 0; o < G; o++) r += cand[o] > hd;
+            if (r == kk - 1) s_t2 = hd;
+        }
+        __syncthreads();
+        const unsigned long long t2 = s_t2;
+        const unsigned long long T = t1 > t2 ? t1 : t2;
+        const int total = s_total2;
+        const int want = total < kk ? total : kk;
+        __syncthreads();
+        // every key >= T (at least `want` of them) into cand
+        for (int idx = tid; idx < G * kk; idx += blockDim.x) {
+            const unsigned long long key = work[idx];
+            if (key != 0ull && key >= T) {
+                const int p = atomicAdd(&s_m2, 1);
+                if (p < kCandCap) cand[p] = key;
+            }
+        }
+        __syncthreads();
+        const int m = s_m2;
+        if (m <= kCandCap) {
+            rank_place(cand, m, want, work);   // work is free again
+            for (int i = tid; i < want; i += blockDim.x) {
+                out_ids[i] = key_id(work[i]);
+                out_scores[i] = key_score(work[i]);
+            }
+            if (tid == 0) *out_n = want;
+            kk = 0;   // done: skip the general path below
+        }
+        __syncthreads();
     }
     if (kk > 0) {
         __shared__ int s_m;
