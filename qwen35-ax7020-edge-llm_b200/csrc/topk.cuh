@@ -238,62 +238,64 @@ __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int* c
         unsigned long long k = *((volatile unsigned long long*)&sc->argmax_key);
         *out_id = k ? key_id(k) : 0;
     }
-    if (kk > 0 && (long long)gridDim.x * kk + (gridDim.x + 1) / 2 <= work_cap) {
-        // Fast path: one parallel sweep copies every list into shared memory
-        // (list c at work[c*kk], zero keys past its count), so the selection
-        // below never waits on a chain of global loads.
+    constexpr int kPre = 8;   // keys per list read by the fast path
+    if (kk > 0 && (long long)gridDim.x * (kPre + 2) <= work_cap && (int)gridDim.x <= kCandCap) {
+        // Fast path: one round of independent L2 loads brings every list's
+        // count, first kPre keys and kk-th key.  Every key >= T lies in a
+        // list prefix unless some list's kPre-th key is itself >= T; only
+        // then does the general path below run.
         __shared__ int s_m2;
         __shared__ int s_total2;
+        __shared__ int s_spill;
+        __shared__ unsigned long long s_t2;
         const int G = gridDim.x;
-        int* s_counts = reinterpret_cast<int*>(work + (size_t)G * kk);   // after the lists
+        constexpr int E = kPre + 1;   // entries per list: prefix, then the kk-th key
+        int* s_counts = reinterpret_cast<int*>(work + (size_t)G * E);
         if (tid == 0) {
             s_m2 = 0;
             s_total2 = 0;
+            s_spill = 0;
+            s_t2 = 0ull;
         }
-        // the other CTAs' lists are complete (their fence precedes their
-        // ticket); read them from L2 with independent loads
-        for (int c = tid; c < G; c += blockDim.x) s_counts[c] = __ldcg(sc->counts + c);
-        __syncthreads();
-        // sixteen independent loads in flight per thread (a load-then-store
-        // loop would wait one L2 round trip per key)
-        const int total_keys = G * kk;
-        for (int base = tid; base < total_keys; base += 16 * blockDim.x) {
-            unsigned long long v[16];
+        const int total_ent = G * E;
+        for (int base = tid; base < total_ent; base += 8 * blockDim.x) {
+            unsigned long long v[8];
 #pragma unroll
-            for (int u = 0; u < 16; u++) {
+            for (int u = 0; u < 8; u++) {
                 const int idx = base + u * blockDim.x;
                 v[u] = 0ull;
-                if (idx < total_keys) {
-                    const int c = idx / kk;
-                    if (idx - c * kk < s_counts[c]) v[u] = __ldcg(sc->lists + idx);
+                if (idx < total_ent) {
+                    const int c = idx / E, e = idx - c * E;
+                    const int pos = e < kPre ? e : kk - 1;
+                    if (pos < kk) v[u] = __ldcg(sc->lists + (size_t)c * kk + pos);
                 }
             }
 #pragma unroll
-            for (int u = 0; u < 16; u++) {
+            for (int u = 0; u < 8; u++) {
                 const int idx = base + u * blockDim.x;
-                if (idx < total_keys) work[idx] = v[u];
+                if (idx < total_ent) work[idx] = v[u];
             }
         }
+        for (int c = tid; c < G; c += blockDim.x) s_counts[c] = __ldcg(sc->counts + c);
         __syncthreads();
-        // thresholds: T1 = best kk-th key of a full list, T2 = kk-th best head
-        const int gp = next_pow2(G);
+        for (int idx = tid; idx < total_ent; idx += blockDim.x) {   // drop entries past each list's count
+            const int c = idx / E, e = idx - c * E;
+            const int pos = e < kPre ? e : kk - 1;
+            if (pos >= s_counts[c]) work[idx] = 0ull;
+        }
+        __syncthreads();
+        // T1 = best kk-th key of a full list, T2 = kk-th largest head
         unsigned long long t1 = 0ull;
         int tot = 0;
-        for (int c = tid; c < gp; c += blockDim.x) {
-            cand[c] = c < G ? work[(size_t)c * kk] : 0ull;
-            if (c < G) {
-                const unsigned long long last = work[(size_t)c * kk + kk - 1];
-                t1 = last > t1 ? last : t1;
-                tot += s_counts[c];
-            }
+        for (int c = tid; c < G; c += blockDim.x) {
+            cand[c] = work[(size_t)c * E];
+            const unsigned long long last = work[(size_t)c * E + kPre];
+            t1 = last > t1 ? last : t1;
+            tot += s_counts[c];
         }
         for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
         if (lane == 0) atomicAdd(&s_total2, tot);
-        t1 = block_max_u64(t1, red);   // contains barriers
-        // T2 = the kk-th largest head, by counting (heads are distinct or zero)
-        __shared__ unsigned long long s_t2;
-        if (tid == 0) s_t2 = 0ull;
-        __syncthreads();
+        t1 = block_max_u64(t1, red);   // contains barriers (cand heads visible after it)
         for (int c = tid; c < G; c += blockDim.x) {
             const unsigned long long hd = cand[c];
             if (hd == 0ull) continue;
@@ -302,22 +304,23 @@ __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int* c
             if (r == kk - 1) s_t2 = hd;
         }
         __syncthreads();
-        const unsigned long long t2 = s_t2;
-        const unsigned long long T = t1 > t2 ? t1 : t2;
+        const unsigned long long T = t1 > s_t2 ? t1 : s_t2;
         const int total = s_total2;
         const int want = total < kk ? total : kk;
         __syncthreads();
-        // every key >= T (at least `want` of them) into cand
-        for (int idx = tid; idx < G * kk; idx += blockDim.x) {
-            const unsigned long long key = work[idx];
+        // gather the prefix keys >= T; flag lists whose prefix may not hold all of theirs
+        for (int idx = tid; idx < G * kPre; idx += blockDim.x) {
+            const int c = idx / kPre, e = idx - c * kPre;
+            const unsigned long long key = work[(size_t)c * E + e];
             if (key != 0ull && key >= T) {
                 const int p = atomicAdd(&s_m2, 1);
                 if (p < kCandCap) cand[p] = key;
+                if (e == kPre - 1 && s_counts[c] > kPre) s_spill = 1;
             }
         }
         __syncthreads();
         const int m = s_m2;
-        if (m <= kCandCap) {
+        if (!s_spill && m <= kCandCap && m <= work_cap) {
             rank_place(cand, m, want, work);   // work is free again
             for (int i = tid; i < want; i += blockDim.x) {
                 out_ids[i] = key_id(work[i]);
