@@ -181,6 +181,10 @@ struct LmState {
     unsigned long long best;
     unsigned long long* cand;
     int* cand_count;
+    // k <= 64: every warp keeps its best 64 keys in registers (element
+    // i = r*32 + lane in r_r, descending); thr is the 64th of them
+    bool wl;
+    unsigned long long r0, r1, thr;
 };
 
 template <bool LM>
@@ -207,19 +211,28 @@ __device__ __forceinline__ void unit_result(const WArgs& A, const SDesc* T, cons
         if (lane == 0) D.tickets[U.g] = 0u;
         return;
     }
-    if (row >= U.M) return;
     if (LM) {
-        if (yv > -1e30f) {
+        const bool ok = row < U.M;
+        if (ok && yv > -1e30f) {
             const unsigned long long k = cand_key(yv, row);
             lm.best = k > lm.best ? k : lm.best;
         }
-        if (A.kk > 0 && yv > -3.402823466e38f) {
-            const int p = atomicAdd(lm.cand_count, 1);
-            if (p < kCandCap) lm.cand[p] = cand_key(yv, row);
+        if (A.kk > 0) {
+            if (lm.wl) {   // whole warp: fold the unit's 32 scores into the warp's top-64
+                const unsigned long long key = (ok && yv > -3.402823466e38f) ? cand_key(yv, row) : 0ull;
+                if (__any_sync(0xffffffffu, key > lm.thr)) {
+                    warp_fold64(lm.r0, lm.r1, key, 0ull);
+                    lm.thr = __shfl_sync(0xffffffffu, lm.r1, 31);
+                }
+            } else if (ok && yv > -3.402823466e38f) {
+                const int p = atomicAdd(lm.cand_count, 1);
+                if (p < kCandCap) lm.cand[p] = cand_key(yv, row);
+            }
         }
-    } else {
-        T[U.d].y[row] = yv;
+        return;
     }
+    if (row >= U.M) return;
+    T[U.d].y[row] = yv;
 }
 
 // The 4 blocks of one stage for this lane's row: lane-class sums with
@@ -317,10 +330,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_con
     lm.best = 0ull;
     lm.cand = cand;
     lm.cand_count = &s_cand_count;
+    lm.wl = A.kk > 0 && A.kk <= 64;
+    lm.r0 = lm.r1 = lm.thr = 0ull;
 
     const int W = gridDim.x * kWarps;
-    const int gw = blockIdx.x * kWarps + warp;
-    int rr_next = gw;   // round-robin schedule
+    // static schedule: CTA c owns the contiguous units [U*c/G, U*(c+1)/G)
+    // (13 or 14 of 2048 on 148 SMs rather than 8 or 16), its warps take
+    // them in turn
+    const int cta_end = (int)(((long long)nu_total * (blockIdx.x + 1)) / gridDim.x);
+    int rr_next = (int)(((long long)nu_total * blockIdx.x) / gridDim.x) + warp;
     bool exhausted = false;
     auto claim = [&]() -> int {
         if (exhausted) return nu_total;
@@ -339,8 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_con
                 }
             }
         } else {
-            u = rr_next;
-            rr_next += W;
+            u = rr_next < cta_end ? rr_next : nu_total;
+            rr_next += kWarps;
             if (u >= nu_total) exhausted = true;
         }
         return u < nu_total ? u : nu_total;
@@ -460,9 +478,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_con
     cp_async_wait<0>();
     if (LM) {
         __syncthreads();
+        if (lm.wl) {
+            cand[warp * 64 + lane] = lm.r0;
+            cand[warp * 64 + 32 + lane] = lm.r1;
+            merge_warp_lists64(cand, &s_cand_count, A.kk);
+        }
         unsigned long long* work = reinterpret_cast<unsigned long long*>(rings);
         lm_finish(A.sc, cand, &s_cand_count, work, (kWarps * kRing * kStage) / 8, lm.best, A.kk, A.out_id,
-                  A.out_ids, A.out_scores, A.out_n, s_red);
+                  A.out_ids, A.out_scores, A.out_n, s_red, lm.wl);
     }
 }
 
@@ -750,8 +773,8 @@ cudaError_t launch_gemv(const GemvDesc& d0, uint32_t* act, unsigned int* err, cu
 }
 
 cudaError_t launch_bfp8_lm_head(const float* h, const int8_t* mant, const uint8_t* exps, int vocab,
-                                int hidden, int k, LmScratch* scratch, uint32_t* act, unsigned int* err,
-                                int* out_id, int* out_ids, float* out_scores, int* out_n,
+                                int hidden, int k, LmScratch* scratch, uint32_t* act, unsigned int* ctr,
+                                unsigned int* err, int* out_id, int* out_ids, float* out_scores, int* out_n,
                                 cudaStream_t stream) {
     GemvDesc d{};
     d.mant = mant;
@@ -763,10 +786,15 @@ cudaError_t launch_bfp8_lm_head(const float* h, const int8_t* mant, const uint8_
     GemvPlan plan;
     if (!fast_shape_ok(d) || !gemv_plan(&d, 1, act, &plan)) return cudaErrorInvalidValue;
     const int grid = std::min(std::min(num_sms(), (plan.total_units + kWarps - 1) / kWarps), kMaxGrid);
-    // round-robin units: every CTA scores at most this many rows
-    const long long rows_per_cta =
-        (long long)((plan.total_units + grid * kWarps - 1) / (grid * kWarps)) * kWarps * kRows;
-    if (rows_per_cta > kCandCap) return cudaErrorInvalidValue;
+    const int kk = std::min(k, vocab);
+    // k <= 64 keeps candidates in registers; a larger k appends every row to
+    // the CTA's buffer, which bounds the rows per CTA
+    const bool warp_lists = kk <= 64;
+    if (!warp_lists) {
+        const long long rows_per_cta =
+            (long long)((plan.total_units + grid * kWarps - 1) / (grid * kWarps)) * kWarps * kRows;
+        if (rows_per_cta > kCandCap) return cudaErrorInvalidValue;
+    }
     PrepArgs P{};
     P.single = d;
     P.n = 1;
@@ -776,10 +804,11 @@ cudaError_t launch_bfp8_lm_head(const float* h, const int8_t* mant, const uint8_
     A.single = d;
     A.n = 1;
     A.total_units = plan.total_units;
-    A.ctr = nullptr;
+    A.ctr = nullptr;   // round-robin: with ~2 units per warp a claim round trip costs more than it balances
+    (void)ctr;
     A.err = err;
     A.sc = scratch;
-    A.kk = std::min(k, vocab);
+    A.kk = kk;
     A.out_id = out_id;
     A.out_ids = out_ids;
     A.out_scores = out_scores;

@@ -88,9 +88,11 @@ cudaError_t launch_gemv_fast(const GemvDesc& d, uint32_t* act, size_t act_cap_wo
 // BFP8 lm_head: scores = bfp8_gemv(h), fused argmax (ties -> lowest id, best
 // must beat -1e30) and top-k (k <= 1024; score desc, ties ascending id).
 // Results land in device memory: out_id[0], out_ids/out_scores[0..n), *out_n.
+// `ctr` is a zeroed pair of counters the launch may use for dynamic unit
+// claims (k <= 64); the kernel leaves it zero.
 cudaError_t launch_bfp8_lm_head(const float* h, const int8_t* mant, const uint8_t* exps, int vocab,
-                                int hidden, int k, LmScratch* scratch, uint32_t* act, unsigned int* err,
-                                int* out_id, int* out_ids, float* out_scores, int* out_n,
+                                int hidden, int k, LmScratch* scratch, uint32_t* act, unsigned int* ctr,
+                                unsigned int* err, int* out_id, int* out_ids, float* out_scores, int* out_n,
                                 cudaStream_t stream);
 
 // Standalone block-64 quantizer: x [B][K] -> xq [B][K] (natural order), xs [B][K/64].

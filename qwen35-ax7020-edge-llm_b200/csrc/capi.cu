@@ -209,6 +209,7 @@ struct DevState {
     unsigned int* err = nullptr;
     uint32_t* act = nullptr;       // paired-activation scratch of single-GEMV launches
     unsigned int* tickets = nullptr;   // zeroed split-K counters of fast single-GEMV launches
+    unsigned int* lm_ctr = nullptr;    // zeroed unit-claim counters of the BFP8 lm_head
 };
 constexpr size_t kTicketWords = 16384;
 constexpr size_t kActScratchWords = 128 * 1024;   // serves K <= 253952
@@ -235,10 +236,14 @@ int dev_state(DevState** out) {
         unsigned int* tk = nullptr;
         if ((e = cudaMalloc(&tk, kTicketWords * 4)) != cudaSuccess) return fail(QB_ENOMEM, "ticket alloc", e);
         if ((e = cudaMemset(tk, 0, kTicketWords * 4)) != cudaSuccess) return fail(QB_ECUDA, "ticket clear", e);
+        unsigned int* lc = nullptr;
+        if ((e = cudaMalloc(&lc, 2 * sizeof(unsigned int))) != cudaSuccess) return fail(QB_ENOMEM, "lm counter alloc", e);
+        if ((e = cudaMemset(lc, 0, 2 * sizeof(unsigned int))) != cudaSuccess) return fail(QB_ECUDA, "lm counter clear", e);
         st.scratch = p;
         st.err = w;
         st.act = a;
         st.tickets = tk;
+        st.lm_ctr = lc;
     }
     *out = &st;
     return QB_OK;
@@ -648,7 +653,8 @@ int qwen_b200_lm_head_bfp8_dev(const float* h, const int8_t* mant, const uint8_t
     DevState* st = nullptr;
     if (int rc = dev_state(&st)) return rc;
     if (qb::gemv_act_words(hidden) > kActScratchWords) return fail(QB_EINVAL, "lm_head_bfp8: hidden too large");
-    cudaError_t e = qb::launch_bfp8_lm_head(h, mant, exps, vocab, hidden, k, st->scratch, st->act, st->err, out_id,
+    cudaError_t e = qb::launch_bfp8_lm_head(h, mant, exps, vocab, hidden, k, st->scratch, st->act, st->lm_ctr, st->err,
+                                            out_id,
                                             out_ids, out_scores, out_n, static_cast<cudaStream_t>(stream));
     if (e == cudaErrorInvalidValue)
         return fail(QB_EINVAL, "lm_head_bfp8: hidden must be a multiple of 512, mant/exps/h 16/4/8-byte aligned, "

@@ -124,46 +124,67 @@ __device__ __forceinline__ int count_greater64(const unsigned long long* a, unsi
     return lo;
 }
 
-// Keep the best `keep` (<= 64) of the n candidate keys, sorted descending at
-// cand[0..min(n, keep)): every warp folds 64-key chunks into its own sorted
-// top-64, then the warps' lists are merged by rank.  Needs kCandCap >=
-// 64 * warps + keep.  Called by the whole block.
+// Fold 64 more keys (c0, c1: element i = r*32 + lane) into a warp's running
+// top-64 (r0, r1), both descending.
+__device__ __forceinline__ void warp_fold64(unsigned long long& r0, unsigned long long& r1, unsigned long long c0,
+                                            unsigned long long c1) {
+    const int lane = threadIdx.x & 31;
+    warp_sort64_desc(c0, c1);
+    // max(running[i], chunk[63 - i]) holds the top 64 as a bitonic sequence
+    const unsigned long long x0 = __shfl_sync(0xffffffffu, c1, 31 - lane);
+    const unsigned long long x1 = __shfl_sync(0xffffffffu, c0, 31 - lane);
+    r0 = r0 > x0 ? r0 : x0;
+    r1 = r1 > x1 ? r1 : x1;
+    warp_merge64_desc(r0, r1);
+}
+
+// cand[w*64 .. w*64+64) hold every warp's descending top-64 (zero keys
+// empty).  Writes the best `keep` (<= 64) keys of their union, descending,
+// to cand[0..m) and m = min(nonzero keys, keep) to *count.  Needs kCandCap
+// >= 64 * warps + keep.  Called by the whole block.
+__device__ inline void merge_warp_lists64(unsigned long long* cand, int* count, int keep) {
+    const int nw = blockDim.x >> 5;
+    unsigned long long* out = cand + 64 * nw;
+    __shared__ int s_nz;
+    if (threadIdx.x == 0) s_nz = 0;
+    __syncthreads();
+    int nz = 0;
+    for (int idx = threadIdx.x; idx < nw * keep; idx += blockDim.x) {
+        const int l = idx / keep, i = idx - l * keep;
+        const unsigned long long key = cand[l * 64 + i];
+        if (key == 0ull) continue;
+        nz++;
+        int rank = i;
+        for (int o = 0; o < nw; o++)
+            if (o != l) rank += count_greater64(cand + o * 64, key);
+        if (rank < keep) out[rank] = key;
+    }
+    if (nz) atomicAdd(&s_nz, nz);
+    __syncthreads();
+    const int m = s_nz < keep ? s_nz : keep;
+    for (int i = threadIdx.x; i < m; i += blockDim.x) cand[i] = out[i];
+    if (threadIdx.x == 0) *count = m;
+    __syncthreads();
+}
+
+// Keep the best `keep` (<= 64) of the n candidate keys in cand[0..n),
+// sorted descending at cand[0..min(n, keep)): every warp folds 64-key
+// chunks into its own sorted top-64, then the warps' lists are merged by
+// rank.  Called by the whole block.
 __device__ inline void cand_topk64(unsigned long long* cand, int* count, int keep) {
     __syncthreads();
     const int n = *count;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
     unsigned long long r0 = 0ull, r1 = 0ull;   // running top-64, descending
     for (int base = w * 64; base < n; base += nw * 64) {
-        unsigned long long c0 = base + lane < n ? cand[base + lane] : 0ull;
-        unsigned long long c1 = base + 32 + lane < n ? cand[base + 32 + lane] : 0ull;
-        warp_sort64_desc(c0, c1);
-        // max(running[i], chunk[63 - i]) holds the top 64 as a bitonic sequence
-        const unsigned long long x0 = __shfl_sync(0xffffffffu, c1, 31 - lane);
-        const unsigned long long x1 = __shfl_sync(0xffffffffu, c0, 31 - lane);
-        r0 = r0 > x0 ? r0 : x0;
-        r1 = r1 > x1 ? r1 : x1;
-        warp_merge64_desc(r0, r1);
+        const unsigned long long c0 = base + lane < n ? cand[base + lane] : 0ull;
+        const unsigned long long c1 = base + 32 + lane < n ? cand[base + 32 + lane] : 0ull;
+        warp_fold64(r0, r1, c0, c1);
     }
     __syncthreads();   // every chunk read
-    unsigned long long* lists = cand;                 // nw sorted lists of 64
-    unsigned long long* out = cand + 64 * nw;
-    lists[w * 64 + lane] = r0;
-    lists[w * 64 + 32 + lane] = r1;
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < nw * keep; idx += blockDim.x) {
-        const int l = idx / keep, i = idx - l * keep;
-        const unsigned long long key = lists[l * 64 + i];
-        if (key == 0ull) continue;
-        int rank = i;
-        for (int o = 0; o < nw; o++)
-            if (o != l) rank += count_greater64(lists + o * 64, key);
-        if (rank < keep) out[rank] = key;
-    }
-    __syncthreads();
-    const int m = n < keep ? n : keep;
-    for (int i = threadIdx.x; i < m; i += blockDim.x) cand[i] = out[i];
-    if (threadIdx.x == 0) *count = m;
-    __syncthreads();
+    cand[w * 64 + lane] = r0;
+    cand[w * 64 + 32 + lane] = r1;
+    merge_warp_lists64(cand, count, keep);
 }
 
 // Block-wide max of a 64-bit key; result valid in every thread.
@@ -196,7 +217,8 @@ __device__ inline void rank_place(const unsigned long long* work, int m, int kee
 }
 
 // End-of-CTA work for the lm_head kernels.  `cand`/`cand_count` is the CTA's
-// shared buffer (kCandCap keys), `work` a shared scratch area of `work_cap`
+// shared buffer (kCandCap keys; with `precompacted` it already holds the
+// CTA's best kk keys, descending), `work` a shared scratch area of `work_cap`
 // keys that may alias the CTA's stage buffers.  `best` is this thread's
 // argmax key.  Writes out_id[0] (argmax) and, for kk > 0,
 // out_ids/out_scores[0..n) and *out_n.
@@ -209,14 +231,16 @@ __device__ inline void rank_place(const unsigned long long* work, int m, int kee
 __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int* cand_count,
                                  unsigned long long* work, int work_cap, unsigned long long best,
                                  int kk, int* out_id, int* out_ids, float* out_scores, int* out_n,
-                                 unsigned long long* red) {
+                                 unsigned long long* red, bool precompacted = false) {
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
     unsigned long long bm = block_max_u64(best, red);
     if (tid == 0 && bm) atomicMax(&sc->argmax_key, bm);
 
     if (kk > 0) {
-        if (kk <= 64 && 64 * (int)(blockDim.x >> 5) + kk <= kCandCap)
+        if (precompacted)
+            __syncthreads();   // cand[0..*cand_count) already holds the CTA's best kk, descending
+        else if (kk <= 64 && 64 * (int)(blockDim.x >> 5) + kk <= kCandCap)
             cand_topk64(cand, cand_count, kk);
         else
             cand_compact(cand, cand_count, kk);
