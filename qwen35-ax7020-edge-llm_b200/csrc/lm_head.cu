@@ -168,6 +168,135 @@ __global__ void __launch_bounds__(kThreads, 1) lm_bf16_kernel(const __grid_const
               A.out_ids, A.out_scores, A.out_n, s_red);
 }
 
+// ---------------------------------------------------------------- warp-autonomous scan
+// hidden % 128 == 0 and k <= 64.  A unit is 32 table rows and a warp owns it
+// from first byte to score: lane = row, the lane keeps all eight chains of
+// its row in registers, so there is no CTA barrier while streaming.  Each
+// warp has a private ring of kWRing 8 KB stages (two TMA boxes of 32 rows x
+// 64 elements, SWIZZLE_128B), refilled by its lane 0.  Candidates: each warp
+// keeps its best 64 keys in registers; the CTA merges the eight lists at
+// the end.  CTA c scores the contiguous units [U*c/G, U*(c+1)/G).
+constexpr int kWRows = 32;
+constexpr int kWRing = 3;
+constexpr int kWStage = kWRows * 256;   // 128 elements of 32 rows
+constexpr int kWWarps = kThreads / 32;
+
+__device__ __forceinline__ void wissue(const LmArgs& A, int u, int s, unsigned char* st, uint64_t* bar) {
+    mbar_arrive_expect_tx(bar, kWStage);
+    tma_load_2d(st, &A.tmap, s * 128, u * kWRows, bar);
+    tma_load_2d(st + kWRows * 128, &A.tmap, s * 128 + 64, u * kWRows, bar);
+}
+
+template <bool TOPK>
+__global__ void __launch_bounds__(kThreads, 1) lm_bf16_warp_kernel(const __grid_constant__ LmArgs A) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                           ~uintptr_t(1023));
+    unsigned char* rings = smem;                                                  // [warp][slot] 8 KB
+    uint64_t* bars = reinterpret_cast<uint64_t*>(rings + kWWarps * kWRing * kWStage);   // [warp][slot]
+    float* hs = reinterpret_cast<float*>(bars + kWWarps * kWRing);
+    unsigned long long* cand = reinterpret_cast<unsigned long long*>(hs + A.hidden);   // 64 * warps + 64
+    __shared__ int s_cand_count;
+    __shared__ unsigned long long s_red[kThreads / 32];
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    unsigned char* ring = rings + warp * kWRing * kWStage;
+    uint64_t* bar = bars + warp * kWRing;
+    if (lane == 0) {
+        for (int k = 0; k < kWRing; k++) mbar_init(&bar[k], 1);
+        fence_barrier_init();
+        tma_prefetch_desc(&A.tmap);
+    }
+    if (tid == 0) s_cand_count = 0;
+    __syncwarp();
+
+    const int U = (A.vocab + kWRows - 1) / kWRows;
+    const int u_begin = (int)(((long long)U * blockIdx.x) / gridDim.x);
+    const int u_end = (int)(((long long)U * (blockIdx.x + 1)) / gridDim.x);
+    const int nst = A.hidden / 128;
+    const int my_units = u_end - u_begin > warp ? (u_end - u_begin - warp + kWWarps - 1) / kWWarps : 0;
+    const int total = my_units * nst;   // stages this warp streams
+
+    // prologue: the first kWRing-1 stages, then h (overlaps the copies)
+    int iu = 0, is = 0, issued = 0;
+    if (lane == 0)
+        for (int k = 0; k < kWRing - 1 && issued < total; k++, issued++) {
+            wissue(A, u_begin + warp + iu * kWWarps, is, ring + k * kWStage, &bar[k]);
+            if (++is == nst) { is = 0; iu++; }
+        }
+    for (int i = tid; i < A.hidden; i += kThreads) hs[i] = A.h[i];
+    __syncthreads();
+
+    unsigned long long best = 0ull, r0 = 0ull, r1 = 0ull, thr = 0ull;
+    float c[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) c[q] = 0.0f;
+    const int sw = lane & 7;
+    int cu = 0, cs = 0;
+#pragma unroll 1
+    for (int it = 0; it < total; it++) {
+        const int slot = it % kWRing;
+        mbar_wait(&bar[slot], (uint32_t)(it / kWRing) & 1u, A.err);
+        __syncwarp();
+        if (lane == 0 && issued < total) {   // refill the slot consumed last iteration
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            const int ns = (it + kWRing - 1) % kWRing;
+            wissue(A, u_begin + warp + iu * kWWarps, is, ring + ns * kWStage, &bar[ns]);
+            if (++is == nst) { is = 0; iu++; }
+            issued++;
+        }
+        const unsigned char* rowp = ring + slot * kWStage + lane * 128;
+        const float4* hp = reinterpret_cast<const float4*>(hs + cs * 128);
+#pragma unroll
+        for (int b = 0; b < 2; b++) {
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const uint4 w = *reinterpret_cast<const uint4*>(rowp + b * (kWRows * 128) + ((j ^ sw) << 4));
+                const float4 ha = hp[(b * 64 + j * 8) / 4];
+                const float4 hb = hp[(b * 64 + j * 8) / 4 + 1];
+                c[0] = add_ftz(c[0], mul_ftz(__uint_as_float(w.x << 16), ha.x));
+                c[1] = add_ftz(c[1], mul_ftz(__uint_as_float(w.x & 0xFFFF0000u), ha.y));
+                c[2] = add_ftz(c[2], mul_ftz(__uint_as_float(w.y << 16), ha.z));
+                c[3] = add_ftz(c[3], mul_ftz(__uint_as_float(w.y & 0xFFFF0000u), ha.w));
+                c[4] = add_ftz(c[4], mul_ftz(__uint_as_float(w.z << 16), hb.x));
+                c[5] = add_ftz(c[5], mul_ftz(__uint_as_float(w.z & 0xFFFF0000u), hb.y));
+                c[6] = add_ftz(c[6], mul_ftz(__uint_as_float(w.w << 16), hb.z));
+                c[7] = add_ftz(c[7], mul_ftz(__uint_as_float(w.w & 0xFFFF0000u), hb.w));
+            }
+        }
+        if (++cs == nst) {   // the row is complete: the reference's chain combine
+            const float s = add_ftz(add_ftz(add_ftz(c[0], c[4]), add_ftz(c[2], c[6])),
+                                    add_ftz(add_ftz(c[1], c[5]), add_ftz(c[3], c[7])));
+            const int row = (u_begin + warp + cu * kWWarps) * kWRows + lane;
+            const bool ok = row < A.vocab;
+            if (ok && s > -1e30f) {
+                const unsigned long long key = cand_key(s, row);
+                best = key > best ? key : best;
+            }
+            if (TOPK) {
+                const unsigned long long key = (ok && s > -3.402823466e38f) ? cand_key(s, row) : 0ull;
+                if (__any_sync(0xffffffffu, key > thr)) {
+                    warp_fold64(r0, r1, key, 0ull);
+                    thr = __shfl_sync(0xffffffffu, r1, 31);
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < 8; q++) c[q] = 0.0f;
+            cs = 0;
+            cu++;
+        }
+    }
+    __syncthreads();
+    if (TOPK) {
+        cand[warp * 64 + lane] = r0;
+        cand[warp * 64 + 32 + lane] = r1;
+        merge_warp_lists64(cand, &s_cand_count, A.kk);
+    }
+    unsigned long long* work = reinterpret_cast<unsigned long long*>(rings);
+    lm_finish(A.sc, cand, &s_cand_count, work, (kWWarps * kWRing * kWStage) / 8, best, TOPK ? A.kk : 0,
+              A.out_id, A.out_ids, A.out_scores, A.out_n, s_red, TOPK);
+}
+
 // Any hidden size / alignment: one thread per row, same score order; the
 // with_tail flag adds the elements past the last multiple of 8 on IEEE
 // scalar arithmetic (lm_head_topk) or drops them (lm_head_argmax).
@@ -241,9 +370,31 @@ cudaError_t launch_lm_head_bf16(const float* h, const uint16_t* E, int vocab, in
     A.out_scores = out_scores;
     A.out_n = out_n;
     A.err = err_word;
+    const bool warp_path = hidden % 128 == 0 && A.kk <= 64;
     const bool fast = hidden % 8 == 0 && reinterpret_cast<uintptr_t>(E) % 16 == 0 &&
                       reinterpret_cast<uintptr_t>(h) % 8 == 0 &&
-                      encode_tmap_2d(&A.tmap, E, 2, (uint64_t)vocab, (uint64_t)hidden, (uint32_t)kRows);
+                      encode_tmap_2d(&A.tmap, E, 2, (uint64_t)vocab, (uint64_t)hidden,
+                                     (uint32_t)(warp_path ? kWRows : kRows));
+    if (fast && warp_path) {
+        const int units = (vocab + kWRows - 1) / kWRows;
+        const int grid = std::min(std::min(num_sms(), units), kMaxGrid);
+        const size_t smem = 1024 + (size_t)kWWarps * kWRing * kWStage + (size_t)kWWarps * kWRing * 8 +
+                            4 * (size_t)hidden + (size_t)(64 * kWWarps + 64) * 8;
+        if (smem > 232448) return cudaErrorInvalidValue;
+        cudaError_t err;
+        if (A.kk > 0) {
+            err = cudaFuncSetAttribute(lm_bf16_warp_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+            if (err != cudaSuccess) return err;
+            lm_bf16_warp_kernel<true><<<grid, kThreads, smem, stream>>>(A);
+        } else {
+            err = cudaFuncSetAttribute(lm_bf16_warp_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+            if (err != cudaSuccess) return err;
+            lm_bf16_warp_kernel<false><<<grid, kThreads, smem, stream>>>(A);
+        }
+        return cudaGetLastError();
+    }
     if (fast) {
         A.units = (vocab + kRows - 1) / kRows;
         A.slices = ((hidden >> 3) + kChunks - 1) / kChunks;

@@ -95,3 +95,13 @@ def test_bfp8_lm_head(cuda, V, H, k):
     if k > 0:
         assert ids == rids.tolist()
         assert np.array_equal(bits(np.array(sc, np.float32)), bits(rsc))
+
+
+@pytest.mark.parametrize("V,H,k", [(4099, 384, 40), (33, 128, 64), (70000, 256, 0), (70000, 256, 7)])
+def test_bf16_ragged_vocab(cuda, V, H, k):
+    """Vocab sizes that are not a multiple of the row tile, and more rows
+    than one row per lane per CTA."""
+    rng = np.random.default_rng(V + H + k)
+    tab = (rng.normal(0, 1, (V, H)).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    h = rng.normal(0, 1, H).astype(np.float32)
+    check_bf16(tab, h, k)
