@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--workload", choices=["stack", "gemv", "lm_bf16", "lm_bfp8", "sharded", "batched"],
                     default="stack")
     ap.add_argument("--batch", type=int, default=256, help="sequences per step of --workload batched")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="--workload sharded: rows stored into every GPU by the GEMV kernel, or NCCL all-gathers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--copies", type=int, default=0,
@@ -360,14 +362,17 @@ def run_batched(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kin
 
 def run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, peak_kind):
     """8 layers x (gate, up 28672x8192; down 8192x28672),
-    batch 1, output rows sharded over the ranks with an NCCL all-gather
-    after every projection.  Total work is fixed as N grows (strong scaling)."""
+    batch 1, output rows sharded over the ranks; the rows reach every GPU
+    through the GEMV kernel's own peer stores (--exchange peer) or an NCCL
+    all-gather after every projection.  Total work is fixed as N grows
+    (strong scaling)."""
     from qwen_b200 import sharded
 
     layers = sharded.scaled_layers()
     full_w = sum(t.M * t.K + t.M * t.K // 64 for L in layers for t in (L.gate, L.up, L.down))
     copies = args.copies or max(1, math.ceil(L2_DEFEAT_BYTES / (full_w / world)))
-    st = sharded.ShardedDeviceStack(layers, world, rank, dev, copies=copies, seed=11, fast=True)
+    st = sharded.ShardedDeviceStack(layers, world, rank, dev, copies=copies, seed=11, fast=True,
+                                    exchange=args.exchange)
     clk = ClockSampler(gpu_uuid(torch, dev), local)
     secs = timed(torch, lambda i: st.step(i % copies), args.steps, args.warmup, barrier)
     clocks = clk.stop()
@@ -376,18 +381,23 @@ def run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, p
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     per_step = float(t.item()) / args.steps
     nbytes = st.bytes_per_step()
+    if args.exchange == "peer" and st.device_error():
+        raise RuntimeError("sharded: a peer flag wait timed out")
     st.close()
     per_rank_gbs = nbytes / world / per_step / 1e9
     return {"value": round(nbytes / per_step / 1e9, 2), "ms_per_step": round(per_step * 1e3, 4), "scaling": "strong",
             "config": {"workload": "scaled BFP8 stack: 8 x (gate/up 28672x8192, down 8192x28672), batch 1",
                        "arithmetic": "fast (split-K, fma per block; within 1e-5 of the exact order)",
                        "algorithmic_bytes_per_step": nbytes, "weight_bytes": full_w,
-                       "parallelism": f"output rows sharded x{world}, NCCL all-gather after each projection",
+                       "parallelism": f"output rows sharded x{world}, " + (
+                           "GEMV epilogue stores rows into every GPU over NVLink, epoch flags between launches"
+                           if args.exchange == "peer" else "NCCL all-gather after each projection"),
                        "l2": f"rotates {copies} copies of this rank's {full_w / world / 1e9:.2f} GB"},
             "roofline": {"bound": "hbm", "achieved": round(per_rank_gbs, 2), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(per_rank_gbs / hbm_peak, 4), "peak_kind": peak_kind, "traffic": None,
                          "kernel": "gemv_warp_kernel per rank (per-rank GB/s incl. all-gathers)"},
             "gpu_launches": args.steps * len(layers) * 4,   # 2 grouped launches x (act_prep + gemv_warp); NCCL not counted
+            "exchange": args.exchange,
             "clocks": clocks}
 
 

@@ -171,6 +171,38 @@ QB_API int qwen_b200_stack_create_ex(int n, const int8_t* const* mant, const uin
 QB_API int qwen_b200_stack_run(int plan, void* stream);
 QB_API int qwen_b200_stack_destroy(int plan);
 
+/* ---- Row-sharded stacks over several GPUs of one node (one process per GPU).
+ * Each rank owns rows [row_base[i], row_base[i] + M[i]) of GEMV i; y[i] points
+ * at that row range inside this rank's full-length output vector, and
+ * peer_y[i * (world - 1) + r] at the FULL output vector (row 0) of GEMV i on
+ * the r-th other rank, mapped into this process (qwen_b200_ipc_open).  Every
+ * row the kernel finishes is stored locally and into each peer vector, so no
+ * separate all-gather runs.  Replaces the per-layer all-gather of the
+ * distributed decode loop (layer outputs gathered across ranks before the
+ * next layer's GEMVs read them). */
+QB_API int qwen_b200_stack_create_sharded(int n, const int8_t* const* mant, const uint8_t* const* exps,
+                                          const float* const* x, float* const* y, const int* M, const int* K,
+                                          int flags, int world, const float* const* peer_y, const int* row_base);
+/* One launch of a (sharded) plan with cross-GPU ordering.  With wait_epoch
+ * != 0 the launch first spins (bounded; QB_ERR peer timeout in the error word)
+ * until wait_flags[r] >= wait_epoch for every rank r < world (wrap-safe
+ * compare), i.e. until every rank finished the launch its inputs come from.
+ * With sig_epoch != 0 the last CTA of the launch stores sig_epoch into
+ * sig_flags[r][rank] for every r < world (release, system scope) after all
+ * rows reached every GPU.  sig_flags[r] is rank r's flag array (world uints),
+ * wait_flags is this rank's own; epochs grow by one per launch on all ranks. */
+QB_API int qwen_b200_stack_run_sync(int plan, void* stream, const unsigned int* wait_flags, unsigned int wait_epoch,
+                                    unsigned int* const* sig_flags, unsigned int sig_epoch, int world, int rank);
+/* Zeroed device memory that can be shared with qwen_b200_ipc_handle (plain
+ * cudaMalloc: IPC needs the allocation's own base pointer). */
+QB_API int qwen_b200_dev_alloc(size_t bytes, void** out);
+QB_API int qwen_b200_dev_free(void* p);
+/* 64-byte CUDA IPC handle of a qwen_b200_dev_alloc base; open it in another
+ * process on the same node (peer access enabled lazily), close when done. */
+QB_API int qwen_b200_ipc_handle(const void* base, void* handle_out);
+QB_API int qwen_b200_ipc_open(const void* handle, void** out);
+QB_API int qwen_b200_ipc_close(void* p);
+
 /* ---- Batched decode on the tensor cores (B sequences share the weights).
  * Activations are int16 block-64 values stored as two signed int8 planes,
  * xq = 256*hi + lo (lo = low byte of xq as a signed int8, hi = (xq - lo)/256):
@@ -226,7 +258,8 @@ QB_API int qwen_b200_lm_head_bfp8_dev(const float* h, const int8_t* mant, const 
 QB_API int qwen_b200_pack_bfp8_dev(const float* w, int M, int K, int8_t* mant, uint8_t* exps, void* stream);
 
 /* Error bits the kernels of the current device recorded (bounded waits that
- * timed out: 1); 0 if none.  clear != 0 resets them.  No reference
+ * timed out: 1 for a copy or pipeline barrier, 2 for a peer flag of
+ * qwen_b200_stack_run_sync); 0 if none.  clear != 0 resets them.  No reference
  * counterpart. */
 QB_API int qwen_b200_device_error(int clear);
 

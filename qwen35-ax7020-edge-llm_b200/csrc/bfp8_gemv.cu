@@ -59,7 +59,43 @@ struct PrepArgs {
     GemvDesc single;
     const GemvDesc* list;
     int n;
+    const unsigned int* wait_flags;   // row-sharded stacks: inputs complete once every rank's flag
+    unsigned int wait_epoch;          // reaches wait_epoch (0: no wait)
+    int world;
+    unsigned int* err;
 };
+
+// ---------------------------------------------------------------- cross-GPU flags
+constexpr uint32_t kFlagPolls = 1u << 22;   // bounded wait on peer flags (each poll may sleep)
+constexpr uint32_t kErrPeerTimeout = 2u;
+
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Thread 0 waits until flags[r] >= epoch for every rank r (wrap-safe compare),
+// giving up after kFlagPolls polls with kErrPeerTimeout in *err; then the
+// whole CTA proceeds.
+__device__ __forceinline__ void wait_peer_flags(const unsigned int* flags, int world, unsigned int epoch,
+                                                unsigned int* err) {
+    if (threadIdx.x == 0) {
+        for (int r = 0; r < world; r++) {
+            uint32_t i = 0;
+            while ((int)(ld_acquire_sys(flags + r) - epoch) < 0) {
+                if (++i == kFlagPolls) {
+                    if (err) atomicOr(err, kErrPeerTimeout);
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+    }
+    __syncthreads();
+}
 
 __device__ __forceinline__ const GemvDesc& prep_desc(const PrepArgs& A, int d) {
     return A.list ? A.list[d] : A.single;
@@ -68,6 +104,7 @@ __device__ __forceinline__ const GemvDesc& prep_desc(const PrepArgs& A, int d) {
 // grid (n, chunks): CTA (d, c) prepares blocks [64c, 64c + 64) of GEMV d.
 __global__ void __launch_bounds__(kThreads) act_prep_kernel(const __grid_constant__ PrepArgs A) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (A.wait_epoch) wait_peer_flags(A.wait_flags, A.world, A.wait_epoch, A.err);
     const GemvDesc& D = prep_desc(A, blockIdx.x);
     const int nb = D.K >> 6;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -122,6 +159,7 @@ struct WArgs {
     int* out_ids;
     float* out_scores;
     int* out_n;
+    SyncArgs sync;          // row-sharded stacks: completion signal (sig_epoch 0: none)
 };
 
 __device__ __forceinline__ const GemvDesc& wdesc(const WArgs& A, int d) {
@@ -140,6 +178,7 @@ struct SDesc {
     float* y;
     float* partial;
     unsigned int* tickets;
+    const PeerOut* peer;
 };
 
 struct Unit {
@@ -187,6 +226,12 @@ struct LmState {
     unsigned long long r0, r1, thr;
 };
 
+// A row-sharded GEMV's output row into every rank's full vector.
+__device__ __forceinline__ void store_peers(const PeerOut* P, int row, float v) {
+    const int n = P->n, g = P->row_base + row;
+    for (int r = 0; r < n; r++) P->y[r][g] = v;
+}
+
 template <bool LM>
 __device__ __forceinline__ void unit_result(const WArgs& A, const SDesc* T, const Unit& U, int lane, float yv,
                                             LmState& lm) {
@@ -207,6 +252,7 @@ __device__ __forceinline__ void unit_result(const WArgs& A, const SDesc* T, cons
             float sum = 0.0f;
             for (int s = 0; s < D.nseg; s++) sum = __fadd_rn(sum, __ldcg(D.partial + (size_t)s * U.M + row));
             D.y[row] = sum;
+            if (D.peer) store_peers(D.peer, row, sum);
         }
         if (lane == 0) D.tickets[U.g] = 0u;
         return;
@@ -233,6 +279,7 @@ __device__ __forceinline__ void unit_result(const WArgs& A, const SDesc* T, cons
     }
     if (row >= U.M) return;
     T[U.d].y[row] = yv;
+    if (T[U.d].peer) store_peers(T[U.d].peer, row, yv);
 }
 
 // The 4 blocks of one stage for this lane's row: lane-class sums with
@@ -321,6 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_con
         t.xs = D.xscale;
         t.tmap = &D.tmap;
         t.y = D.y;
+        t.peer = D.peer;
         sdesc[d] = t;
     }
     __syncthreads();
@@ -476,6 +524,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_con
         i++;
     }
     cp_async_wait<0>();
+    if (!LM && A.sync.sig_epoch) {
+        // the last CTA to finish publishes the epoch to every rank: all of
+        // this launch's rows (local and peer stores) are visible before it
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence_system();
+            const unsigned int t = atomicAdd(A.sync.sig_ticket, 1u);
+            if (t == gridDim.x - 1) {
+                __threadfence_system();
+                for (int r = 0; r < A.sync.world; r++) st_release_sys(A.sync.sig_flags[r] + A.sync.rank, A.sync.sig_epoch);
+                *A.sync.sig_ticket = 0u;   // the plan's next launch is stream-ordered after this one
+            }
+        }
+    }
     if (LM) {
         __syncthreads();
         if (lm.wl) {
@@ -704,11 +766,20 @@ static cudaError_t launch_warp(const WArgs& A, int grid, cudaStream_t stream) {
 }
 
 cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, unsigned int* ctr,
-                             unsigned int* err, cudaStream_t stream) {
+                             unsigned int* err, cudaStream_t stream, const SyncArgs* sync) {
     if (plan.n <= 0 || plan.total_units <= 0) return cudaSuccess;
+    if (sync && (sync->world < 1 || sync->world > kMaxRanks || sync->rank < 0 || sync->rank >= sync->world ||
+                 (sync->wait_epoch && !sync->wait_flags) || (sync->sig_epoch && !sync->sig_ticket)))
+        return cudaErrorInvalidValue;
     PrepArgs P{};
     P.list = dev_descs;
     P.n = plan.n;
+    P.err = err;
+    if (sync) {
+        P.wait_flags = sync->wait_flags;
+        P.wait_epoch = sync->wait_epoch;
+        P.world = sync->world;
+    }
     cudaError_t e = launch_prep(P, (plan.kmax / 64 + 63) / 64, stream);
     if (e != cudaSuccess) return e;
     WArgs A{};
@@ -717,6 +788,7 @@ cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, un
     A.total_units = plan.total_units;
     A.ctr = ctr;
     A.err = err;
+    if (sync) A.sync = *sync;
     const int grid = std::min(num_sms(), (plan.total_units + kWarps - 1) / kWarps);
     return plan.fast ? launch_warp<false, true>(A, grid, stream) : launch_warp<false, false>(A, grid, stream);
 }

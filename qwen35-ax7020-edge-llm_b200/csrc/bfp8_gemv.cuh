@@ -11,6 +11,29 @@ namespace qb {
 // (05-主机侧源码/bfp8_packer.py:53-86).  The activation is either fp32 `x`
 // (quantized by the reference block-64 rule) or, when x == nullptr, an
 // already quantized int16 `xq` [K] with scales `xs` [K/64].
+// Row-sharded GEMVs: every output row is also stored into each rank's copy
+// of the full output vector (peer pointers from IPC handles), in place of an
+// all-gather.
+constexpr int kMaxRanks = 8;
+struct PeerOut {
+    float* y[kMaxRanks];   // the other ranks' full output vectors (peer pointers)
+    int n;                 // how many
+    int row_base;          // global index of this rank's row 0 in a full vector
+};
+
+// Cross-GPU ordering of a grouped launch on row-sharded stacks.  Before the
+// launch reads its inputs, act_prep waits (bounded) until every rank has
+// published `wait_epoch` in this GPU's `wait_flags`; when the launch's last
+// CTA is done it publishes `sig_epoch` into every rank's flag array.
+struct SyncArgs {
+    const unsigned int* wait_flags;          // this GPU's flags, one per rank
+    unsigned int wait_epoch;                 // 0: no wait
+    unsigned int* sig_flags[kMaxRanks];      // every rank's flag array (peer pointers)
+    unsigned int* sig_ticket;                // zeroed grid ticket of this plan
+    unsigned int sig_epoch;                  // 0: no signal
+    int world, rank;
+};
+
 struct alignas(64) GemvDesc {
     CUtensorMap tmap;       // planner: 2D map of `mant` (M rows x K bytes, 32 x 128-byte boxes)
     const int8_t* mant;
@@ -29,6 +52,7 @@ struct alignas(64) GemvDesc {
     int nseg;               // planner: K segments per row group (1 = whole rows)
     int seg_stages;         // planner: 256-byte columns per segment
     int pad_;
+    const PeerOut* peer;    // optional (device memory): also store rows into every rank's vector
 };
 
 struct LmScratch;
@@ -73,7 +97,8 @@ bool gemv_plan(GemvDesc* descs, int n, uint32_t* act, GemvPlan* plan, int mode =
 // first launch; every launch leaves it zero).  `err` (device word, may be
 // null) collects kernel error bits.
 cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, unsigned int* ctr,
-                             unsigned int* err, cudaStream_t stream);
+                             unsigned int* err, cudaStream_t stream,
+                             const SyncArgs* sync = nullptr);
 
 // One exact GEMV (any M >= 1, K a positive multiple of 64, any alignment).
 // `act` is device scratch of gemv_act_words(K) words.

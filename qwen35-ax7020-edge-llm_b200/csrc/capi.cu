@@ -161,6 +161,8 @@ struct StackPlan {
     qb::GemvDesc* dev_descs = nullptr;
     uint32_t* act = nullptr;          // paired activations of every GEMV
     unsigned int* ctr = nullptr;      // unit counter pair of the dynamic scheduler
+    qb::PeerOut* peers = nullptr;     // row-sharded plans: where each GEMV's rows also go
+    unsigned int* sig_ticket = nullptr;   // row-sharded plans: grid ticket of the completion signal
     bool live = false;
 };
 std::vector<StackPlan> g_plans;
@@ -556,14 +558,46 @@ int qwen_b200_quant_dev(const float* x, int B, int K, int16_t* xq, float* xs, vo
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_quant_dev", e);
 }
 
-int qwen_b200_stack_create_ex(int n, const int8_t* const* mant, const uint8_t* const* exps, const float* const* x,
-                              float* const* y, const int* M, const int* K, int flags) {
+}  // extern "C"
+
+namespace {
+
+struct PeerSpec {
+    int world;
+    const float* const* peer_y;   // n x (world - 1): the other ranks' full vectors per GEMV
+    const int* row_base;          // n: global row of this rank's row 0
+};
+
+int stack_create_impl(int n, const int8_t* const* mant, const uint8_t* const* exps, const float* const* x,
+                      float* const* y, const int* M, const int* K, int flags, const PeerSpec* ps) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (n <= 0 || !mant || !exps || !x || !y || !M || !K) return fail(QB_EINVAL, "stack: bad arguments");
+    if (ps && (ps->world < 1 || ps->world > qb::kMaxRanks || (ps->world > 1 && !ps->peer_y) || !ps->row_base))
+        return fail(QB_EINVAL, "stack: bad peer description");
     std::vector<qb::GemvDesc> v;
+    std::vector<qb::PeerOut> peers;
+    StackPlan sp;
+    if (ps) {
+        cudaError_t e = cudaMalloc(&sp.peers, sizeof(qb::PeerOut) * n);
+        if (e != cudaSuccess) return fail(QB_ENOMEM, "stack peer alloc", e);
+        if ((e = cudaMalloc(&sp.sig_ticket, sizeof(unsigned int))) != cudaSuccess)
+            return fail(QB_ENOMEM, "stack ticket alloc", e);
+        if ((e = cudaMemset(sp.sig_ticket, 0, sizeof(unsigned int))) != cudaSuccess)
+            return fail(QB_ECUDA, "stack ticket clear", e);
+    }
     for (int i = 0; i < n; i++) {
         if (M[i] < 0 || K[i] <= 0 || K[i] % 64 || !mant[i] || !exps[i] || !x[i] || !y[i])
             return fail(QB_EINVAL, "stack: bad descriptor");
+        qb::PeerOut po{};
+        if (ps) {
+            po.n = ps->world - 1;
+            po.row_base = ps->row_base[i];
+            for (int r = 0; r + 1 < ps->world; r++) {
+                po.y[r] = const_cast<float*>(ps->peer_y[(size_t)i * (ps->world - 1) + r]);
+                if (!po.y[r]) return fail(QB_EINVAL, "stack: null peer vector");
+            }
+        }
+        peers.push_back(po);
         if (M[i] == 0) continue;
         qb::GemvDesc d{};
         d.mant = mant[i];
@@ -572,9 +606,9 @@ int qwen_b200_stack_create_ex(int n, const int8_t* const* mant, const uint8_t* c
         d.y = y[i];
         d.M = M[i];
         d.K = K[i];
+        d.peer = ps ? sp.peers + i : nullptr;
         v.push_back(d);
     }
-    StackPlan sp;
     const int mode = (flags & QB_STACK_FAST) ? qb::kFast : qb::kExact;
     if (!qb::gemv_plan(v.data(), (int)v.size(), nullptr, &sp.plan, mode))
         return fail(QB_EINVAL, "stack: 1..160 GEMVs, every K a multiple of 512, mant/exps/x 16/4/8-byte aligned");
@@ -586,6 +620,8 @@ int qwen_b200_stack_create_ex(int n, const int8_t* const* mant, const uint8_t* c
     if ((e = cudaMemset(sp.act, 0, sp.plan.act_words * 4 + 16)) != cudaSuccess)
         return fail(QB_ECUDA, "stack act clear", e);
     qb::gemv_plan(v.data(), (int)v.size(), sp.act, &sp.plan, mode);
+    if (ps && (e = cudaMemcpy(sp.peers, peers.data(), sizeof(qb::PeerOut) * n, cudaMemcpyHostToDevice)) != cudaSuccess)
+        return fail(QB_ECUDA, "stack peer upload", e);
     e = cudaMalloc(&sp.dev_descs, sizeof(qb::GemvDesc) * (v.size() ? v.size() : 1));
     if (e != cudaSuccess) return fail(QB_ENOMEM, "stack alloc", e);
     e = cudaMemcpy(sp.dev_descs, v.data(), sizeof(qb::GemvDesc) * v.size(), cudaMemcpyHostToDevice);
@@ -593,6 +629,80 @@ int qwen_b200_stack_create_ex(int n, const int8_t* const* mant, const uint8_t* c
     sp.live = true;
     g_plans.push_back(sp);
     return (int)g_plans.size();
+}
+
+}  // namespace
+
+extern "C" {
+
+int qwen_b200_stack_create_ex(int n, const int8_t* const* mant, const uint8_t* const* exps, const float* const* x,
+                              float* const* y, const int* M, const int* K, int flags) {
+    return stack_create_impl(n, mant, exps, x, y, M, K, flags, nullptr);
+}
+
+int qwen_b200_stack_create_sharded(int n, const int8_t* const* mant, const uint8_t* const* exps,
+                                   const float* const* x, float* const* y, const int* M, const int* K, int flags,
+                                   int world, const float* const* peer_y, const int* row_base) {
+    PeerSpec ps{world, peer_y, row_base};
+    return stack_create_impl(n, mant, exps, x, y, M, K, flags, &ps);
+}
+
+int qwen_b200_stack_run_sync(int plan, void* stream, const unsigned int* wait_flags, unsigned int wait_epoch,
+                             unsigned int* const* sig_flags, unsigned int sig_epoch, int world, int rank) {
+    if (plan < 1 || plan > (int)g_plans.size() || !g_plans[plan - 1].live) return fail(QB_EINVAL, "stack: bad handle");
+    const StackPlan& sp = g_plans[plan - 1];
+    if (world < 1 || world > qb::kMaxRanks || rank < 0 || rank >= world || (sig_epoch && (!sig_flags || !sp.sig_ticket)) ||
+        (wait_epoch && !wait_flags))
+        return fail(QB_EINVAL, "stack_run_sync: bad arguments (a plan from qwen_b200_stack_create_sharded, "
+                               "1 <= world <= 8)");
+    qb::SyncArgs sy{};
+    sy.wait_flags = wait_flags;
+    sy.wait_epoch = wait_epoch;
+    sy.sig_ticket = sp.sig_ticket;
+    sy.sig_epoch = sig_epoch;
+    sy.world = world;
+    sy.rank = rank;
+    for (int r = 0; r < world && sig_flags; r++) sy.sig_flags[r] = sig_flags[r];
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    cudaError_t e =
+        qb::launch_gemv_list(sp.dev_descs, sp.plan, sp.ctr, st->err, static_cast<cudaStream_t>(stream), &sy);
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_stack_run_sync", e);
+}
+
+int qwen_b200_dev_alloc(size_t bytes, void** out) {
+    if (!out || !bytes) return fail(QB_EINVAL, "qwen_b200_dev_alloc: bad arguments");
+    cudaError_t e = cudaMalloc(out, bytes);
+    if (e != cudaSuccess) return fail(QB_ENOMEM, "qwen_b200_dev_alloc", e);
+    if ((e = cudaMemset(*out, 0, bytes)) != cudaSuccess) return fail(QB_ECUDA, "qwen_b200_dev_alloc clear", e);
+    return QB_OK;
+}
+
+int qwen_b200_dev_free(void* p) {
+    cudaError_t e = cudaFree(p);
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_dev_free", e);
+}
+
+int qwen_b200_ipc_handle(const void* base, void* handle_out) {
+    if (!base || !handle_out) return fail(QB_EINVAL, "qwen_b200_ipc_handle: bad arguments");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(base));
+    if (e != cudaSuccess) return fail(QB_ECUDA, "cudaIpcGetMemHandle", e);
+    std::memcpy(handle_out, &h, sizeof h);
+    return QB_OK;
+}
+
+int qwen_b200_ipc_open(const void* handle, void** out) {
+    if (!handle || !out) return fail(QB_EINVAL, "qwen_b200_ipc_open: bad arguments");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof h);
+    cudaError_t e = cudaIpcOpenMemHandle(out, h, cudaIpcMemLazyEnablePeerAccess);
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "cudaIpcOpenMemHandle", e);
+}
+
+int qwen_b200_ipc_close(void* p) {
+    cudaError_t e = cudaIpcCloseMemHandle(p);
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "cudaIpcCloseMemHandle", e);
 }
 
 int qwen_b200_stack_create(int n, const int8_t* const* mant, const uint8_t* const* exps, const float* const* x,
@@ -615,6 +725,8 @@ int qwen_b200_stack_destroy(int plan) {
     cudaFree(g_plans[plan - 1].dev_descs);
     cudaFree(g_plans[plan - 1].act);
     cudaFree(g_plans[plan - 1].ctr);
+    cudaFree(g_plans[plan - 1].peers);
+    cudaFree(g_plans[plan - 1].sig_ticket);
     g_plans[plan - 1].live = false;
     g_plans[plan - 1].dev_descs = nullptr;
     return QB_OK;

@@ -24,6 +24,7 @@ from ._lib import KernelError, check, load
 __all__ = [
     "KernelError", "quant_block64", "bfp8_gemv", "bfp8_gemv_fast", "bfp8_gemv_q", "lm_head_bf16", "lm_head_bfp8",
     "pack_bfp8", "LinearStack", "LmResult", "Planes", "quant_planes", "bfp8_gemm_tc", "BatchedStack",
+    "PeerRegion", "ShardedLinearStack",
 ]
 
 
@@ -280,6 +281,113 @@ class LinearStack:
 
     def run(self, stream: int | None = None) -> None:
         check(load().qwen_b200_stack_run(self.handle, _stream() if stream is None else stream), "LinearStack.run")
+
+    def close(self) -> None:
+        if getattr(self, "handle", 0) > 0:
+            load().qwen_b200_stack_destroy(self.handle)
+            self.handle = 0
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class _DevArray:
+    """A raw device range seen as a 1-D tensor (no ownership)."""
+
+    def __init__(self, ptr: int, n: int, typestr: str):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+class PeerRegion:
+    """Zeroed device memory shared with the other processes of one node over
+    CUDA IPC: ``handle()`` gives 64 bytes to send to them, ``PeerRegion.open``
+    maps another process's region into this one.  Tensors made by ``floats``
+    and ``uints`` alias the memory and must not outlive ``close()``."""
+
+    def __init__(self, nbytes: int = 0, _ptr: int = 0, _owned: bool = True):
+        if _ptr:
+            self.ptr = _ptr
+        else:
+            p = ctypes.c_void_p()
+            check(load().qwen_b200_dev_alloc(max(nbytes, 256), ctypes.byref(p)), "PeerRegion")
+            self.ptr = p.value
+        self.nbytes = nbytes
+        self._owned = _owned
+
+    def handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(64)
+        check(load().qwen_b200_ipc_handle(self.ptr, buf), "PeerRegion.handle")
+        return buf.raw
+
+    @classmethod
+    def open(cls, handle: bytes, nbytes: int) -> "PeerRegion":
+        p = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(bytes(handle), 64)
+        check(load().qwen_b200_ipc_open(buf, ctypes.byref(p)), "PeerRegion.open")
+        return cls(nbytes, _ptr=p.value, _owned=False)
+
+    def floats(self, offset: int, n: int) -> torch.Tensor:
+        return torch.as_tensor(_DevArray(self.ptr + offset, n, "<f4"))
+
+    def uints(self, offset: int, n: int) -> torch.Tensor:
+        return torch.as_tensor(_DevArray(self.ptr + offset, n, "<i4"))
+
+    def close(self) -> None:
+        if self.ptr:
+            if self._owned:
+                load().qwen_b200_dev_free(self.ptr)
+            else:
+                load().qwen_b200_ipc_close(self.ptr)
+            self.ptr = 0
+
+
+class ShardedLinearStack:
+    """A grouped launch of the row slices one rank owns of several GEMVs,
+    storing every finished row into this rank's full output vector AND into
+    the other ranks' (mapped) full vectors, then raising the ranks'
+    completion flags.
+
+    ``items``: (x fp32 [K], mant int8 [m, K], exps uint8 [m, K/64], y fp32 [m])
+    where y is this rank's row range [r0, r0 + m) of its full vector;
+    ``peer_ptrs[i]``: device addresses of GEMV i's full vector on every other
+    rank (world - 1 of them); ``row_base[i]`` = r0.  ``run(wait, sig, ...)``
+    waits for epoch ``wait`` on this rank's flags (0: no wait) and publishes
+    epoch ``sig`` into every rank's flags.  Epochs are baked into the launch,
+    so a captured graph would replay stale epochs: launch it directly.
+    """
+
+    def __init__(self, items, peer_ptrs, row_base, world: int, fast: bool = False):
+        n = len(items)
+        P = ctypes.c_void_p * n
+        I = ctypes.c_int * n
+        self._keep = items
+        self.world = world
+        mant = P(*[_ptr(m) for (_, m, _, _) in items])
+        exps = P(*[_ptr(e) for (_, _, e, _) in items])
+        xs = P(*[_ptr(x) for (x, _, _, _) in items])
+        ys = P(*[_ptr(y) for (_, _, _, y) in items])
+        Ms = I(*[m.shape[0] for (_, m, _, _) in items])
+        Ks = I(*[m.shape[1] for (_, m, _, _) in items])
+        flat = [p for ps in peer_ptrs for p in ps]
+        if len(flat) != n * (world - 1):
+            raise ValueError("ShardedLinearStack: need world - 1 peer vectors per GEMV")
+        peers = (ctypes.c_void_p * max(1, len(flat)))(*flat)
+        rb = I(*row_base)
+        h = load().qwen_b200_stack_create_sharded(n, mant, exps, xs, ys, Ms, Ks, 1 if fast else 0, world, peers, rb)
+        if h <= 0:
+            check(h, "ShardedLinearStack")
+        self.handle = h
+
+    def run(self, wait_flags: int, wait_epoch: int, sig_flags, sig_epoch: int, rank: int,
+            stream: int | None = None) -> None:
+        sf = (ctypes.c_void_p * self.world)(*sig_flags)
+        check(load().qwen_b200_stack_run_sync(self.handle, _stream() if stream is None else stream, wait_flags,
+                                              wait_epoch, sf, sig_epoch, self.world, rank),
+              "ShardedLinearStack.run")
 
     def close(self) -> None:
         if getattr(self, "handle", 0) > 0:

@@ -2,9 +2,16 @@
 
 Every GEMV's rows are split into contiguous slices, one per rank, with slice
 boundaries on multiples of 64 rows.  Each rank streams only its slice of the
-weights (the exact kernel, so its rows are bit-identical to an unsharded
-run) and an all-gather over NCCL rebuilds the full output vector in every
-rank's own memory before the next GEMV reads it.  The data flow of one
+weights (rows bit-identical to an unsharded run of the same arithmetic) and
+the full output vector is rebuilt in every rank's own memory before the next
+GEMV reads it, in one of two ways:
+
+* ``exchange="nccl"``: an NCCL all-gather after every grouped launch;
+* ``exchange="peer"``: the GEMV kernel itself stores each finished row into
+  every rank's full vector over NVLink (CUDA IPC mappings), and the last CTA
+  of each launch raises a per-rank epoch flag on every GPU; the next launch
+  waits (bounded) for all ranks' flags before it reads its input.  No
+  collective runs, and the weight stream of a launch starts while it waits.  The data flow of one
 scaled MLP layer (gate / up ffn x hidden, down hidden x ffn): gate and up
 read the layer input; down reads the gathered gate output (the element-wise
 SwiGLU between them is glue outside this path); the next layer reads the
@@ -69,14 +76,19 @@ class ShardedDeviceStack:
     across steps so that timing never finds them in L2.
     """
 
-    def __init__(self, layers, world, rank, device, copies=1, seed=0, group=None, fast=False):
+    def __init__(self, layers, world, rank, device, copies=1, seed=0, group=None, fast=False, exchange="nccl"):
         import torch
 
         from . import ops
 
+        if exchange not in ("nccl", "peer"):
+            raise ValueError("exchange must be 'nccl' or 'peer'")
         self.layers = list(layers)
         self.world, self.rank, self.group = world, rank, group
         self.fast = fast
+        self.exchange = exchange
+        self.region, self.peer_regions = None, []
+        self.epoch = 0
         self.device = torch.device(device)
         self.shards = {}   # name -> (r0, r1)
         slices = []        # (name, r0, r1, K)
@@ -112,13 +124,51 @@ class ShardedDeviceStack:
         L0 = self.layers[0]
         self.x0 = torch.randn(L0.gate.K, generator=gx, device=self.device, dtype=torch.float32)
         # gathered outputs (full vectors, every rank) and this rank's slices
-        self.full = {t.name: torch.zeros(t.M, dtype=torch.float32, device=self.device)
-                     for L in self.layers for t in (L.gate, L.up, L.down)}
+        if exchange == "peer":
+            self._map_regions()
+        else:
+            self.full = {t.name: torch.zeros(t.M, dtype=torch.float32, device=self.device)
+                         for L in self.layers for t in (L.gate, L.up, L.down)}
         self.part = {t.name: torch.zeros(self.padded_rows(t.M), dtype=torch.float32, device=self.device)
                      for L in self.layers for t in (L.gate, L.up, L.down)}
         self.gath = {t.name: torch.zeros(self.padded_rows(t.M) * world, dtype=torch.float32, device=self.device)
                      for L in self.layers for t in (L.gate, L.up, L.down)}
         self.plans = [self._plans(c) for c in range(copies)]
+
+    FLAGS_BYTES = 256   # epoch flags at the head of every region: one uint per rank
+
+    def _map_regions(self):
+        """One IPC-shared region per rank: the epoch flags, then every GEMV's
+        full output vector (256-byte aligned).  Handles are exchanged with an
+        all_gather_object; the other ranks' regions are mapped here."""
+        import torch.distributed as dist
+
+        from . import ops
+
+        for L in self.layers:
+            for t in (L.gate, L.up, L.down):
+                r0, r1 = self.shards[t.name]
+                if r1 <= r0:
+                    raise ValueError(f"exchange='peer' needs rows on every rank ({t.name}: M={t.M})")
+        self.voff, off = {}, self.FLAGS_BYTES
+        for L in self.layers:
+            for t in (L.gate, L.up, L.down):
+                self.voff[t.name] = off
+                off += (4 * t.M + 255) // 256 * 256
+        self.region = ops.PeerRegion(off)
+        self.full = {name: self.region.floats(o, t.M) for name, o, t in
+                     ((t.name, self.voff[t.name], t) for L in self.layers for t in (L.gate, L.up, L.down))}
+        self.flags = self.region.uints(0, self.world)
+        self.peer_base = [0] * self.world   # every rank's region base, mapped into this process
+        self.peer_base[self.rank] = self.region.ptr
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, self.region.handle(), group=self.group)
+            for r in range(self.world):
+                if r != self.rank:
+                    reg = ops.PeerRegion.open(handles[r], off)
+                    self.peer_regions.append(reg)
+                    self.peer_base[r] = reg.ptr
 
     def padded_rows(self, M):
         """Every rank contributes the same count to the all-gather: the
@@ -144,8 +194,13 @@ class ShardedDeviceStack:
         x = self.x0
 
         def out(t, rows):   # a single rank writes straight into the full vector
+            if self.exchange == "peer":
+                r0, r1 = self.shards[t.name]
+                return self.full[t.name][r0:r1]
             return self.full[t.name] if self.world == 1 else self.part[t.name][:rows]
 
+        if self.exchange == "peer":
+            return self._peer_plans(copy)
         for L in self.layers:
             gu = []
             for t in (L.gate, L.up):
@@ -160,6 +215,39 @@ class ShardedDeviceStack:
                           ops.LinearStack(dn, fast=self.fast) if dn else None))
             x = self.full[L.down.name]
         return plans
+
+    def _peer_plans(self, copy):
+        from . import ops
+
+        others = [r for r in range(self.world) if r != self.rank]
+        plans = []
+        x = self.x0
+
+        def stack(ts, xin):
+            items, peers, bases = [], [], []
+            for t in ts:
+                mant, exps = self.weight(copy, t)
+                r0, r1 = self.shards[t.name]
+                items.append((xin, mant, exps, self.full[t.name][r0:r1]))
+                peers.append([self.peer_base[r] + self.voff[t.name] for r in others])
+                bases.append(r0)
+            return ops.ShardedLinearStack(items, peers, bases, self.world, fast=self.fast)
+
+        for L in self.layers:
+            plans.append((stack((L.gate, L.up), x), stack((L.down,), self.full[L.gate.name])))
+            x = self.full[L.down.name]
+        return plans
+
+    def _launch_peer(self, plan):
+        """Launch n waits for every rank's launch n - 1 and publishes n (one
+        rank: stream order is enough, no flags)."""
+        if self.world == 1:
+            plan.run(self.peer_base[0], 0, self.peer_base, 0, 0)
+            return
+        wait = self.epoch & 0xFFFFFFFF
+        self.epoch += 1
+        sig = self.epoch & 0xFFFFFFFF
+        plan.run(self.peer_base[self.rank], wait, [b for b in self.peer_base], sig, self.rank)
 
     def _gather(self, t):
         import torch.distributed as dist
@@ -179,6 +267,11 @@ class ShardedDeviceStack:
 
     def step(self, copy=0):
         """One token through every layer (grouped GEMV launches + gathers)."""
+        if self.exchange == "peer":
+            for gu, dn in self.plans[copy]:
+                self._launch_peer(gu)
+                self._launch_peer(dn)
+            return
         for L, (gu, dn) in zip(self.layers, self.plans[copy]):
             if gu is not None:
                 gu.run()
@@ -197,8 +290,31 @@ class ShardedDeviceStack:
                 tot += t.M * t.K + t.M * t.K // 64 + 4 * t.K + 4 * t.M
         return tot
 
+    def device_error(self) -> int:
+        """The kernels' error word (2: a peer flag wait timed out), cleared."""
+        from ._lib import load
+
+        return load().qwen_b200_device_error(1)
+
     def close(self):
+        """Release plans and mappings.  In peer mode every rank must call it
+        (it synchronises the device and barriers before freeing its region,
+        which the others map)."""
+        import torch
+        import torch.distributed as dist
+
         for gu, dn in (p for plans in self.plans for p in plans):
             for s in (gu, dn):
                 if s is not None:
                     s.close()
+        if self.region is not None:
+            torch.cuda.synchronize(self.device)
+            for reg in self.peer_regions:
+                reg.close()
+            self.peer_regions = []
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            self.full = {}
+            self.flags = None
+            self.region.close()
+            self.region = None

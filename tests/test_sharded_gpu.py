@@ -1,5 +1,7 @@
-"""Row-sharded stack on two GPUs (NCCL): every gathered output equals the
-single-GPU run bit for bit.  Needs two GPUs; skipped otherwise."""
+"""Row-sharded stack on two GPUs: every gathered output equals the single-GPU
+run bit for bit, with the NCCL all-gather and with the in-kernel peer stores
+(exchange="peer"); the fast arithmetic gives the same bits both ways.  The
+two-GPU cases are skipped with fewer GPUs; the bounded flag wait runs on one."""
 import os
 import socket
 
@@ -30,12 +32,18 @@ def _worker(rank, world, port, path):
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
-    st = sharded.ShardedDeviceStack(_layers(), world, rank, f"cuda:{rank}", copies=1, seed=4)
-    for _ in range(2):
-        st.step()
-    torch.cuda.synchronize()
-    np.save(path + f".{rank}.npy", _outputs(st))
-    st.close()
+    for exchange in ("nccl", "peer"):
+        for fast in (False, True):
+            st = sharded.ShardedDeviceStack(_layers(), world, rank, f"cuda:{rank}", copies=2, seed=4, fast=fast,
+                                            exchange=exchange)
+            for i in range(3):
+                st.step(i % 2)
+            torch.cuda.synchronize()
+            np.save(path + f".{exchange}.{int(fast)}.{rank}.npy", _outputs(st))
+            if exchange == "peer":
+                assert st.device_error() == 0
+                assert st.flags.cpu().tolist() == [6 * len(st.layers)] * world   # 2 launches x 3 steps
+            st.close()
     dist.barrier()
     dist.destroy_process_group()
 
@@ -59,6 +67,50 @@ def test_two_gpu_sharded_stack_matches_single_gpu(cuda, tmp_path):
     s.close()
     path = str(tmp_path / "out")
     mp.start_processes(_worker, args=(2, port, path), nprocs=2, join=True, start_method="spawn")
+    fast_ref = np.load(path + ".nccl.1.0.npy")
     for r in range(2):
-        got = np.load(path + f".{r}.npy")
-        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), r
+        for exchange in ("nccl", "peer"):
+            got = np.load(path + f".{exchange}.0.{r}.npy")
+            assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (exchange, r)
+            got = np.load(path + f".{exchange}.1.{r}.npy")
+            assert np.array_equal(got.view(np.uint32), fast_ref.view(np.uint32)), (exchange, r)
+    np.testing.assert_allclose(fast_ref, ref, rtol=1e-4, atol=1e-4)
+
+
+def test_peer_mode_single_rank_matches_plain(cuda):
+    """exchange="peer" on one rank (no mappings, no flags needed): the same
+    bits as the plain stack."""
+    import torch
+
+    from qwen_b200 import sharded
+
+    a = sharded.ShardedDeviceStack(_layers(), 1, 0, "cuda:0", copies=1, seed=4)
+    b = sharded.ShardedDeviceStack(_layers(), 1, 0, "cuda:0", copies=1, seed=4, exchange="peer")
+    a.step()
+    b.step()
+    b.step()
+    torch.cuda.synchronize()
+    assert np.array_equal(_outputs(a).view(np.uint32), _outputs(b).view(np.uint32))
+    assert b.flags.cpu().tolist() == [0]
+    assert b.device_error() == 0
+    a.close()
+    b.close()
+
+
+def test_peer_flag_wait_times_out_with_status(cuda):
+    """A flag that nothing raises: the bounded wait gives up, the error word
+    reports it (bit 2), the launch still completes and the context stays
+    usable."""
+    import torch
+
+    from qwen_b200 import sharded
+
+    st = sharded.ShardedDeviceStack(_layers(), 1, 0, "cuda:0", copies=1, seed=4, exchange="peer")
+    st.device_error()
+    gu, _ = st.plans[0][0]
+    base = st.peer_base[0]
+    gu.run(base, 1000, [base], 7, 0)     # waits for epoch 1000, which never comes
+    torch.cuda.synchronize()
+    assert st.device_error() & 2
+    assert st.flags.cpu().tolist() == [7]
+    st.close()
