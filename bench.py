@@ -53,7 +53,8 @@ def parse():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=["stack", "gemv", "lm_bf16", "lm_bfp8", "sharded", "batched"],
                     default="stack")
-    ap.add_argument("--batch", type=int, default=256, help="sequences per step of --workload batched")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences per step: --workload batched (default 256) or sharded (default 1)")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="--workload sharded: rows stored into every GPU by the GEMV kernel, or NCCL all-gathers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -61,7 +62,10 @@ def parse():
     ap.add_argument("--copies", type=int, default=0,
                     help="weight copies to rotate (default: enough for > 4 GB; fewer only for profiling)")
     ap.add_argument("--cpu-sample", action="store_true", help=argparse.SUPPRESS)
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.batch is None:
+        args.batch = 256 if args.workload == "batched" else 1
+    return args
 
 
 def peaks():
@@ -371,8 +375,9 @@ def run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, p
     layers = sharded.scaled_layers()
     full_w = sum(t.M * t.K + t.M * t.K // 64 for L in layers for t in (L.gate, L.up, L.down))
     copies = args.copies or max(1, math.ceil(L2_DEFEAT_BYTES / (full_w / world)))
+    B = args.batch
     st = sharded.ShardedDeviceStack(layers, world, rank, dev, copies=copies, seed=11, fast=True,
-                                    exchange=args.exchange)
+                                    exchange=args.exchange, batch=B)
     clk = ClockSampler(gpu_uuid(torch, dev), local)
     secs = timed(torch, lambda i: st.step(i % copies), args.steps, args.warmup, barrier)
     clocks = clk.stop()
@@ -386,8 +391,9 @@ def run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, p
     st.close()
     per_rank_gbs = nbytes / world / per_step / 1e9
     return {"value": round(nbytes / per_step / 1e9, 2), "ms_per_step": round(per_step * 1e3, 4), "scaling": "strong",
-            "config": {"workload": "scaled BFP8 stack: 8 x (gate/up 28672x8192, down 8192x28672), batch 1",
-                       "arithmetic": "fast (split-K, fma per block; within 1e-5 of the exact order)",
+            "config": {"workload": f"scaled BFP8 stack: 8 x (gate/up 28672x8192, down 8192x28672), batch {B}",
+                       "arithmetic": "fast (split-K, fma per block; within 1e-5 of the exact order)" if B == 1 else
+                                     "tcgen05 kind::i8 over hi/lo int8 planes, exact int32 block dots",
                        "algorithmic_bytes_per_step": nbytes, "weight_bytes": full_w,
                        "parallelism": f"output rows sharded x{world}, " + (
                            "GEMV epilogue stores rows into every GPU over NVLink, epoch flags between launches"
@@ -395,8 +401,10 @@ def run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, p
                        "l2": f"rotates {copies} copies of this rank's {full_w / world / 1e9:.2f} GB"},
             "roofline": {"bound": "hbm", "achieved": round(per_rank_gbs, 2), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(per_rank_gbs / hbm_peak, 4), "peak_kind": peak_kind, "traffic": None,
-                         "kernel": "gemv_warp_kernel per rank (per-rank GB/s incl. all-gathers)"},
-            "gpu_launches": args.steps * len(layers) * 4,   # 2 grouped launches x (act_prep + gemv_warp); NCCL not counted
+                         "kernel": ("gemv_warp_kernel" if B == 1 else "gemm_tc_kernel") +
+                                   " per rank (per-rank GB/s incl. the exchange)"},
+            # 2 grouped launches per layer x (act_prep + gemv_warp, or quant_planes + gemm_tc); NCCL not counted
+            "gpu_launches": args.steps * len(layers) * 4,
             "exchange": args.exchange,
             "clocks": clocks}
 

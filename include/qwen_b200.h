@@ -236,6 +236,28 @@ QB_API int qwen_b200_tc_stack_create(int n, const int8_t* const* mant, const uin
 QB_API int qwen_b200_tc_stack_run(int plan, void* stream);
 QB_API int qwen_b200_tc_stack_destroy(int plan);
 
+/* Row-sharded batched stacks (one process per GPU, same protocol as
+ * qwen_b200_stack_create_sharded): GEMM i writes rows [row_base[i],
+ * row_base[i] + M[i]) of every batch row, y[i] + b * ldy[i] + r (y[i] already
+ * offset to this rank's first row inside its full [B][ldy[i]] output), and
+ * stores the same values at peer_y[i * (world - 1) + r] + b * ldy[i] +
+ * row_base[i] + r on every other rank.  world 1 with peer_y NULL gives a
+ * plain stack with strided outputs. */
+QB_API int qwen_b200_tc_stack_create_sharded(int n, const int8_t* const* mant, const uint8_t* const* exps,
+                                             const int8_t* const* planes, const float* const* xs_t,
+                                             float* const* y, const int* M, const int* K, const int* ldy, int B,
+                                             int ldxs, int world, const float* const* peer_y, const int* row_base);
+/* One run of a sharded batched plan; with sig_epoch != 0 its last CTA
+ * publishes sig_epoch into sig_flags[r][rank] for every rank r. */
+QB_API int qwen_b200_tc_stack_run_sync(int plan, void* stream, unsigned int* const* sig_flags,
+                                       unsigned int sig_epoch, int world, int rank);
+/* qwen_b200_quant_planes_dev() that first waits (bounded; error bit 2) until
+ * wait_flags[r] >= wait_epoch for every rank r < world: the quantizer of a
+ * sharded batched layer reads the full outputs all ranks wrote. */
+QB_API int qwen_b200_quant_planes_wait_dev(const float* x, int B, int K, int8_t* planes, float* xs_t, int ldxs,
+                                           const unsigned int* wait_flags, unsigned int wait_epoch, int world,
+                                           void* stream);
+
 /* bf16 lm_head over E [vocab][hidden] (tied embedding).  Always writes the
  * greedy id to out_id[0]; for k > 0 also the top-k into out_ids/out_scores
  * and its length into out_n[0].  k <= 1024.  Device form of

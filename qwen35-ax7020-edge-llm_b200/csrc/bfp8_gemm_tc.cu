@@ -61,10 +61,11 @@ constexpr float kMagicSum = 3233808384.0f;   // 1.5*2^31 + 1.5*2^23 = 771 * 2^22
 // Scalar fields of one GEMM, copied to shared memory at kernel start so that
 // unit lookups never wait on global loads.
 struct DescRow {
-    int unit_begin, n_nt, nb, M, B, pad_;
+    int unit_begin, n_nt, nb, M, B, ldy;
     const uint8_t* exps;
     float* y;
     int32_t* dots;
+    const PeerOut* peer;
 };
 
 // One unit as the producer publishes it to the MMA and epilogue warps.
@@ -72,7 +73,8 @@ struct UnitInfo {
     const uint8_t* exps;   // exponent rows of the tile (shared-memory copy when ebulk)
     float* y;
     int32_t* dots;
-    int M, nb, B, rt, nt, ebulk;
+    const PeerOut* peer;
+    int M, nb, B, rt, nt, ebulk, ldy, pad_;
 };
 
 template <int N>
@@ -120,6 +122,7 @@ struct TcLaunch {
     const TcDesc* descs;   // device array, or null: use `one`
     int n, total_units;
     unsigned int* err;
+    SyncArgs sync;         // row-sharded plans: completion signal (sig_epoch 0: none)
     TcDesc one;
 };
 
@@ -286,10 +289,11 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
         r.nb = d->nb;
         r.M = d->M;
         r.B = d->B;
-        r.pad_ = 0;
+        r.ldy = d->ldy;
         r.exps = d->exps;
         r.y = d->y;
         r.dots = d->dots;
+        r.peer = d->peer;
         tab[k] = r;
     }
     if (threadIdx.x == 0) {
@@ -356,6 +360,8 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
                 info.exps = ebulk ? ebuf + eb * kEBytes : esrc;
                 info.y = r.y;
                 info.dots = r.dots;
+                info.peer = r.peer;
+                info.ldy = r.ldy;
                 info.M = r.M;
                 info.nb = nb;
                 info.B = r.B;
@@ -573,16 +579,26 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
                 gb += ng;
             }
             gs += (nb + C::kBPS - 1) / C::kBPS;
+            // output stride and peer list, read from the ring entry after the
+            // block loop (not held in registers through it)
+            const int ldy = uring[eb].ldy;
+            const PeerOut* peer = uring[eb].peer;
             __syncwarp();
             if (lane == 0) mbar_arrive(&uempty[eb]);   // unit entry and exponent tile consumed
             if (bad) break;
             if (row_ok) {
-                float* y = info.y;
+                // destination 0: this GPU's output; then every other rank's
+                // copy of the full output (row-sharded plans)
+                const int np = peer ? peer->n : 0;
+                const int b0 = nt * N + col0;
+                for (int q2 = -1; q2 < np; q2++) {
+                    float* dst = q2 < 0 ? info.y + m : peer->y[q2] + peer->row_base + m;
+                    dst += (size_t)b0 * ldy;
 #pragma unroll
-                for (int k = 0; k < C::kCols; k += 2) {
-                    const int b = nt * N + col0 + k;
-                    if (b < B) y[(size_t)b * M + m] = acc[k / 2].x;
-                    if (b + 1 < B) y[(size_t)(b + 1) * M + m] = acc[k / 2].y;
+                    for (int k = 0; k < C::kCols; k += 2) {
+                        if (b0 + k < B) dst[k * ldy] = acc[k / 2].x;
+                        if (b0 + k + 1 < B) dst[(k + 1) * ldy] = acc[k / 2].y;
+                    }
                 }
             }
         }
@@ -595,6 +611,7 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
         tc_fence_after();
         tmem_dealloc(tmem, C::kTmemCols);
     }
+    signal_peers(p.sync);   // row-sharded plans: the last CTA publishes the epoch
 }
 
 // ------------------------------------------------------------ quantizer
@@ -602,7 +619,9 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
 // the reference's arithmetic: amax, q = 16384/amax (IEEE division), xq =
 // rint(x*q) half-even, xs = amax/16384; zero block when amax <= 1e-20.
 __global__ void __launch_bounds__(256) quant_planes_kernel(const float* x, int B, int K, uint8_t* planes,
-                                                           float* xs_t, int ldxs) {
+                                                           float* xs_t, int ldxs, const unsigned int* wait_flags,
+                                                           unsigned int wait_epoch, int world, unsigned int* err) {
+    if (wait_epoch) wait_peer_flags(wait_flags, world, wait_epoch, err);   // row-sharded: inputs from all ranks
     const int nb = K >> 6;
     const long long total = (long long)B * nb;
     const int lane = threadIdx.x & 31;
@@ -633,7 +652,7 @@ __global__ void __launch_bounds__(256) quant_planes_kernel(const float* x, int B
 
 template <int N, bool DOTS>
 cudaError_t launch_n(const TcDesc* dev_descs, const TcDesc* one, int n, int total_units, unsigned int* err,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, const SyncArgs* sync) {
     using C = TcCfg<N>;
     static_assert(C::kSmem <= 232448, "shared memory plan exceeds 227 KB");
     static unsigned long long attr_set = 0;   // one bit per device
@@ -651,6 +670,7 @@ cudaError_t launch_n(const TcDesc* dev_descs, const TcDesc* one, int n, int tota
     p.n = n;
     p.total_units = total_units;
     p.err = err;
+    if (sync) p.sync = *sync;
     if (one) p.one = *one;
     const int grid = std::max(1, std::min(total_units, num_sms()));
     gemm_tc_kernel<N, DOTS><<<grid, C::kThreads, C::kSmem, stream>>>(p);
@@ -668,8 +688,10 @@ int tc_tile_n(int B) {
 }
 
 bool tc_make_desc(TcDesc* d, float* y, const void* planes, const float* xs_t, int ldxs, const int8_t* mant,
-                  const uint8_t* exps, int M, int K, int B, int32_t* dots) {
+                  const uint8_t* exps, int M, int K, int B, int32_t* dots, int ldy) {
     if (!d || !y || !planes || !xs_t || !mant || !exps || M <= 0 || K <= 0 || K % 64 || B <= 0) return false;
+    if (ldy == 0) ldy = M;
+    if (ldy < M) return false;
     if (ldxs < B || ldxs % 4) return false;
     if ((reinterpret_cast<uintptr_t>(planes) | reinterpret_cast<uintptr_t>(xs_t) |
          reinterpret_cast<uintptr_t>(mant)) & 15)
@@ -708,6 +730,7 @@ bool tc_make_desc(TcDesc* d, float* y, const void* planes, const float* xs_t, in
     d->nb = K / 64;
     d->unit_begin = 0;
     d->n_nt = (B + N - 1) / N;
+    d->ldy = ldy;
     return true;
 }
 
@@ -715,30 +738,34 @@ int tc_units(const TcDesc& d) { return ((d.M + kTileRows - 1) / kTileRows) * d.n
 
 template <bool DOTS>
 static cudaError_t launch_b(const TcDesc* dev_descs, const TcDesc* one, int n, int total_units, int B, unsigned int* err,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, const SyncArgs* sync) {
     switch (tc_tile_n(B)) {
-        case 8: return launch_n<8, DOTS>(dev_descs, one, n, total_units, err, stream);
-        case 16: return launch_n<16, DOTS>(dev_descs, one, n, total_units, err, stream);
-        case 32: return launch_n<32, DOTS>(dev_descs, one, n, total_units, err, stream);
-        case 64: return launch_n<64, DOTS>(dev_descs, one, n, total_units, err, stream);
-        default: return launch_n<128, DOTS>(dev_descs, one, n, total_units, err, stream);
+        case 8: return launch_n<8, DOTS>(dev_descs, one, n, total_units, err, stream, sync);
+        case 16: return launch_n<16, DOTS>(dev_descs, one, n, total_units, err, stream, sync);
+        case 32: return launch_n<32, DOTS>(dev_descs, one, n, total_units, err, stream, sync);
+        case 64: return launch_n<64, DOTS>(dev_descs, one, n, total_units, err, stream, sync);
+        default: return launch_n<128, DOTS>(dev_descs, one, n, total_units, err, stream, sync);
     }
 }
 
 cudaError_t launch_gemm_tc(const TcDesc* dev_descs, const TcDesc* one, int n, int total_units, int B, bool dots,
-                           unsigned int* err, cudaStream_t stream) {
+                           unsigned int* err, cudaStream_t stream, const SyncArgs* sync) {
+    if (sync && !sync_args_ok(*sync)) return cudaErrorInvalidValue;
     if (total_units <= 0) return cudaSuccess;
     if (n < 1 || n > kTcMaxDescs || (!dev_descs && !one)) return cudaErrorInvalidValue;
-    return dots ? launch_b<true>(dev_descs, one, n, total_units, B, err, stream)
-                : launch_b<false>(dev_descs, one, n, total_units, B, err, stream);
+    return dots ? launch_b<true>(dev_descs, one, n, total_units, B, err, stream, sync)
+                : launch_b<false>(dev_descs, one, n, total_units, B, err, stream, sync);
 }
 
 cudaError_t launch_quant_planes(const float* x, int B, int K, void* planes, float* xs_t, int ldxs,
-                                cudaStream_t stream) {
+                                cudaStream_t stream, const SyncArgs* sync, unsigned int* err) {
+    if (sync && !sync_args_ok(*sync)) return cudaErrorInvalidValue;
     const long long total = (long long)B * (K / 64);
     if (total <= 0) return cudaSuccess;
     const int grid = (int)std::min<long long>((total + 7) / 8, (long long)num_sms() * 16);
-    quant_planes_kernel<<<grid, 256, 0, stream>>>(x, B, K, static_cast<uint8_t*>(planes), xs_t, ldxs);
+    quant_planes_kernel<<<grid, 256, 0, stream>>>(x, B, K, static_cast<uint8_t*>(planes), xs_t, ldxs,
+                                                  sync ? sync->wait_flags : nullptr, sync ? sync->wait_epoch : 0u,
+                                                  sync ? sync->world : 1, err);
     return cudaGetLastError();
 }
 

@@ -21,6 +21,8 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 
+#include "peer.cuh"
+
 namespace qb {
 
 // One GEMM of a (grouped) launch: y[B][M] = W[M][K] (BFP8) x X[B][K] (planar int16).
@@ -29,12 +31,14 @@ struct alignas(128) TcDesc {
     CUtensorMap tm_x;       // planes [2][B][K] u8, box 128 B x N rows x 2 planes, SWIZZLE_128B
     CUtensorMap tm_s;       // scales [nb][ldxs] f32, box N columns x 2 blocks
     const uint8_t* exps;    // [M][nb]
-    float* y;               // [B][M]
+    float* y;               // [B][ldy]: row b of the output at y + b * ldy
     int32_t* dots;          // optional [B][M][nb]: exact block dots (verification)
     int M, K, B, nb;
     int unit_begin;         // first unit (row tile x column tile) of this GEMM
     int n_nt;               // column tiles per row tile
-    int pad_[2];
+    int ldy;                // output row stride (>= M)
+    int pad_;
+    const PeerOut* peer;    // optional (device memory): row-sharded GEMMs also store into every rank's output
 };
 
 // Column-tile width used for a batch of B rows (8, 16, 32, 64 or 128).
@@ -43,7 +47,7 @@ int tc_tile_n(int B);
 // Fill `d` (host memory); false if a pointer, stride or size breaks the
 // kernel's alignment rules.
 bool tc_make_desc(TcDesc* d, float* y, const void* planes, const float* xs_t, int ldxs, const int8_t* mant,
-                  const uint8_t* exps, int M, int K, int B, int32_t* dots);
+                  const uint8_t* exps, int M, int K, int B, int32_t* dots, int ldy = 0);   // ldy 0: M
 
 // Units (tiles) of one descriptor after tc_make_desc.
 int tc_units(const TcDesc& d);
@@ -54,12 +58,15 @@ constexpr int kTcMaxDescs = 160;
 // Launch: `dev_descs` (device array of n descriptors with unit_begin set,
 // largest K first) or, when it is null, the single descriptor `one`.  With
 // `dots` the kernel also writes every exact block dot to desc.dots.
+// `sync` (row-sharded plans): the last CTA publishes sig_epoch (its wait
+// fields are unused: the quantizer that feeds the launch waits).
 cudaError_t launch_gemm_tc(const TcDesc* dev_descs, const TcDesc* one, int n, int total_units, int B, bool dots,
-                           unsigned int* err, cudaStream_t stream);
+                           unsigned int* err, cudaStream_t stream, const SyncArgs* sync = nullptr);
 
-// fp32 [B][K] -> planes [2][B][K] + xs_t [K/64][ldxs], the reference
-// quantizer's arithmetic (bit-exact xq and scales).
+// fp32 [B][K] -> planes [2][B][K] + xs_t [K/64][ldxs],
+// the reference quantizer's arithmetic (bit-exact xq and scales).  With
+// `sync`, every CTA first waits (bounded) for sync->wait_epoch from all ranks.
 cudaError_t launch_quant_planes(const float* x, int B, int K, void* planes, float* xs_t, int ldxs,
-                                cudaStream_t stream);
+                                cudaStream_t stream, const SyncArgs* sync = nullptr, unsigned int* err = nullptr);
 
 }  // namespace qb

@@ -65,38 +65,6 @@ struct PrepArgs {
     unsigned int* err;
 };
 
-// ---------------------------------------------------------------- cross-GPU flags
-constexpr uint32_t kFlagPolls = 1u << 22;   // bounded wait on peer flags (each poll may sleep)
-constexpr uint32_t kErrPeerTimeout = 2u;
-
-__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
-    unsigned int v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-// Thread 0 waits until flags[r] >= epoch for every rank r (wrap-safe compare),
-// giving up after kFlagPolls polls with kErrPeerTimeout in *err; then the
-// whole CTA proceeds.
-__device__ __forceinline__ void wait_peer_flags(const unsigned int* flags, int world, unsigned int epoch,
-                                                unsigned int* err) {
-    if (threadIdx.x == 0) {
-        for (int r = 0; r < world; r++) {
-            uint32_t i = 0;
-            while ((int)(ld_acquire_sys(flags + r) - epoch) < 0) {
-                if (++i == kFlagPolls) {
-                    if (err) atomicOr(err, kErrPeerTimeout);
-                    break;
-                }
-                __nanosleep(64);
-            }
-        }
-    }
-    __syncthreads();
-}
-
 __device__ __forceinline__ const GemvDesc& prep_desc(const PrepArgs& A, int d) {
     return A.list ? A.list[d] : A.single;
 }
@@ -524,20 +492,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_con
         i++;
     }
     cp_async_wait<0>();
-    if (!LM && A.sync.sig_epoch) {
-        // the last CTA to finish publishes the epoch to every rank: all of
-        // this launch's rows (local and peer stores) are visible before it
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            __threadfence_system();
-            const unsigned int t = atomicAdd(A.sync.sig_ticket, 1u);
-            if (t == gridDim.x - 1) {
-                __threadfence_system();
-                for (int r = 0; r < A.sync.world; r++) st_release_sys(A.sync.sig_flags[r] + A.sync.rank, A.sync.sig_epoch);
-                *A.sync.sig_ticket = 0u;   // the plan's next launch is stream-ordered after this one
-            }
-        }
-    }
+    // row-sharded stacks: the last CTA publishes the epoch to every rank
+    if (!LM) signal_peers(A.sync);
     if (LM) {
         __syncthreads();
         if (lm.wl) {
@@ -768,9 +724,7 @@ static cudaError_t launch_warp(const WArgs& A, int grid, cudaStream_t stream) {
 cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, unsigned int* ctr,
                              unsigned int* err, cudaStream_t stream, const SyncArgs* sync) {
     if (plan.n <= 0 || plan.total_units <= 0) return cudaSuccess;
-    if (sync && (sync->world < 1 || sync->world > kMaxRanks || sync->rank < 0 || sync->rank >= sync->world ||
-                 (sync->wait_epoch && !sync->wait_flags) || (sync->sig_epoch && !sync->sig_ticket)))
-        return cudaErrorInvalidValue;
+    if (sync && !sync_args_ok(*sync)) return cudaErrorInvalidValue;
     PrepArgs P{};
     P.list = dev_descs;
     P.n = plan.n;

@@ -4,6 +4,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "peer.cuh"
+
 namespace qb {
 
 // One BFP8 GEMV.  Weights use the reference's SoA layout: mantissas int8
@@ -11,29 +13,6 @@ namespace qb {
 // (05-主机侧源码/bfp8_packer.py:53-86).  The activation is either fp32 `x`
 // (quantized by the reference block-64 rule) or, when x == nullptr, an
 // already quantized int16 `xq` [K] with scales `xs` [K/64].
-// Row-sharded GEMVs: every output row is also stored into each rank's copy
-// of the full output vector (peer pointers from IPC handles), in place of an
-// all-gather.
-constexpr int kMaxRanks = 8;
-struct PeerOut {
-    float* y[kMaxRanks];   // the other ranks' full output vectors (peer pointers)
-    int n;                 // how many
-    int row_base;          // global index of this rank's row 0 in a full vector
-};
-
-// Cross-GPU ordering of a grouped launch on row-sharded stacks.  Before the
-// launch reads its inputs, act_prep waits (bounded) until every rank has
-// published `wait_epoch` in this GPU's `wait_flags`; when the launch's last
-// CTA is done it publishes `sig_epoch` into every rank's flag array.
-struct SyncArgs {
-    const unsigned int* wait_flags;          // this GPU's flags, one per rank
-    unsigned int wait_epoch;                 // 0: no wait
-    unsigned int* sig_flags[kMaxRanks];      // every rank's flag array (peer pointers)
-    unsigned int* sig_ticket;                // zeroed grid ticket of this plan
-    unsigned int sig_epoch;                  // 0: no signal
-    int world, rank;
-};
-
 struct alignas(64) GemvDesc {
     CUtensorMap tmap;       // planner: 2D map of `mant` (M rows x K bytes, 32 x 128-byte boxes)
     const int8_t* mant;

@@ -176,6 +176,8 @@ struct TcPlan {
     qb::TcDesc* dev_descs = nullptr;
     std::vector<TcLaunchPart> parts;
     int B = 0;
+    qb::PeerOut* peers = nullptr;         // row-sharded plans: where each GEMM's rows also go
+    unsigned int* sig_ticket = nullptr;   // row-sharded plans: grid ticket of the completion signal
     bool live = false;
 };
 std::vector<TcPlan> g_tc_plans;
@@ -797,25 +799,54 @@ int qwen_b200_gemm_tc_dev(float* y, const int8_t* planes, const float* xs_t, int
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_gemm_tc_dev", e);
 }
 
-int qwen_b200_tc_stack_create(int n, const int8_t* const* mant, const uint8_t* const* exps,
-                              const int8_t* const* planes, const float* const* xs_t, float* const* y, const int* M,
-                              const int* K, int B, int ldxs) {
+}  // extern "C"
+
+namespace {
+
+int tc_stack_create_impl(int n, const int8_t* const* mant, const uint8_t* const* exps, const int8_t* const* planes,
+                         const float* const* xs_t, float* const* y, const int* M, const int* K, const int* ldy, int B,
+                         int ldxs, const PeerSpec* ps) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (n <= 0 || n > 4096 || !mant || !exps || !planes || !xs_t || !y || !M || !K || B <= 0)
         return fail(QB_EINVAL, "tc_stack: bad arguments");
+    if (ps && (ps->world < 1 || ps->world > qb::kMaxRanks || (ps->world > 1 && !ps->peer_y) || !ps->row_base))
+        return fail(QB_EINVAL, "tc_stack: bad peer description");
+    TcPlan tp;
+    std::vector<qb::PeerOut> peers(ps ? n : 0);
+    if (ps) {
+        cudaError_t e = cudaMalloc(&tp.peers, sizeof(qb::PeerOut) * n);
+        if (e != cudaSuccess) return fail(QB_ENOMEM, "tc_stack peer alloc", e);
+        if ((e = cudaMalloc(&tp.sig_ticket, sizeof(unsigned int))) != cudaSuccess)
+            return fail(QB_ENOMEM, "tc_stack ticket alloc", e);
+        if ((e = cudaMemset(tp.sig_ticket, 0, sizeof(unsigned int))) != cudaSuccess)
+            return fail(QB_ECUDA, "tc_stack ticket clear", e);
+    }
     std::vector<qb::TcDesc> v;
     for (int i = 0; i < n; i++) {
+        if (ps) {
+            qb::PeerOut& po = peers[i];
+            po = qb::PeerOut{};
+            po.n = ps->world - 1;
+            po.row_base = ps->row_base[i];
+            for (int r = 0; r + 1 < ps->world; r++) {
+                po.y[r] = const_cast<float*>(ps->peer_y[(size_t)i * (ps->world - 1) + r]);
+                if (!po.y[r]) return fail(QB_EINVAL, "tc_stack: null peer output");
+            }
+        }
         if (M[i] == 0) continue;
         qb::TcDesc d;
-        if (M[i] < 0 || !qb::tc_make_desc(&d, y[i], planes[i], xs_t[i], ldxs, mant[i], exps[i], M[i], K[i], B,
-                                          nullptr))
+        if (M[i] < 0 || (ldy && ldy[i] < M[i]) ||
+            !qb::tc_make_desc(&d, y[i], planes[i], xs_t[i], ldxs, mant[i], exps[i], M[i], K[i], B, nullptr,
+                              ldy ? ldy[i] : 0))
             return fail(QB_EINVAL, "tc_stack: bad descriptor (K a multiple of 64, 16-byte aligned planes/xs_t/"
-                                   "mant, ldxs >= B and a multiple of 4)");
+                                   "mant, ldxs >= B and a multiple of 4, ldy >= M)");
+        d.peer = ps ? tp.peers + i : nullptr;
         v.push_back(d);
     }
+    if (ps && (cudaMemcpy(tp.peers, peers.data(), sizeof(qb::PeerOut) * n, cudaMemcpyHostToDevice) != cudaSuccess))
+        return fail(QB_ECUDA, "tc_stack peer upload");
     // deepest matrices first, so the round-robin tail is made of short units
     std::stable_sort(v.begin(), v.end(), [](const qb::TcDesc& a, const qb::TcDesc& b) { return a.K > b.K; });
-    TcPlan tp;
     for (int first = 0; first < (int)v.size(); first += qb::kTcMaxDescs) {
         TcLaunchPart part{first, std::min(qb::kTcMaxDescs, (int)v.size() - first), 0};
         for (int k = first; k < first + part.n; k++) {
@@ -835,26 +866,91 @@ int qwen_b200_tc_stack_create(int n, const int8_t* const* mant, const uint8_t* c
     return (int)g_tc_plans.size();
 }
 
-int qwen_b200_tc_stack_run(int plan, void* stream) {
+int tc_stack_launch(int plan, void* stream, const qb::SyncArgs* sync) {
     if (plan < 1 || plan > (int)g_tc_plans.size() || !g_tc_plans[plan - 1].live)
         return fail(QB_EINVAL, "tc_stack: bad handle");
     const TcPlan& tp = g_tc_plans[plan - 1];
     DevState* st = nullptr;
     if (int rc = dev_state(&st)) return rc;
-    for (const TcLaunchPart& part : tp.parts) {
+    for (size_t k = 0; k < tp.parts.size(); k++) {
+        const TcLaunchPart& part = tp.parts[k];
+        // the completion signal rides on the last launch (the others finish before it starts)
+        const qb::SyncArgs* s = k + 1 == tp.parts.size() ? sync : nullptr;
         cudaError_t e = qb::launch_gemm_tc(tp.dev_descs + part.first, nullptr, part.n, part.total_units, tp.B, false,
-                                           st->err, static_cast<cudaStream_t>(stream));
+                                           st->err, static_cast<cudaStream_t>(stream), s);
         if (e != cudaSuccess) return fail(QB_ECUDA, "qwen_b200_tc_stack_run", e);
     }
     return QB_OK;
 }
+
+}  // namespace
+
+extern "C" {
+
+int qwen_b200_tc_stack_create(int n, const int8_t* const* mant, const uint8_t* const* exps,
+                              const int8_t* const* planes, const float* const* xs_t, float* const* y, const int* M,
+                              const int* K, int B, int ldxs) {
+    return tc_stack_create_impl(n, mant, exps, planes, xs_t, y, M, K, nullptr, B, ldxs, nullptr);
+}
+
+int qwen_b200_tc_stack_create_sharded(int n, const int8_t* const* mant, const uint8_t* const* exps,
+                                      const int8_t* const* planes, const float* const* xs_t, float* const* y,
+                                      const int* M, const int* K, const int* ldy, int B, int ldxs, int world,
+                                      const float* const* peer_y, const int* row_base) {
+    if (!ldy) return fail(QB_EINVAL, "tc_stack_create_sharded: ldy is required");
+    PeerSpec ps{world, peer_y, row_base};
+    return tc_stack_create_impl(n, mant, exps, planes, xs_t, y, M, K, ldy, B, ldxs, &ps);
+}
+
+int qwen_b200_tc_stack_run_sync(int plan, void* stream, unsigned int* const* sig_flags, unsigned int sig_epoch,
+                                int world, int rank) {
+    if (plan < 1 || plan > (int)g_tc_plans.size() || !g_tc_plans[plan - 1].live)
+        return fail(QB_EINVAL, "tc_stack: bad handle");
+    const TcPlan& tp = g_tc_plans[plan - 1];
+    if (world < 1 || world > qb::kMaxRanks || rank < 0 || rank >= world ||
+        (sig_epoch && (!sig_flags || !tp.sig_ticket)))
+        return fail(QB_EINVAL, "tc_stack_run_sync: bad arguments (a plan from qwen_b200_tc_stack_create_sharded, "
+                               "1 <= world <= 8)");
+    qb::SyncArgs sy{};
+    sy.sig_ticket = tp.sig_ticket;
+    sy.sig_epoch = sig_epoch;
+    sy.world = world;
+    sy.rank = rank;
+    for (int r = 0; r < world && sig_flags; r++) sy.sig_flags[r] = sig_flags[r];
+    return tc_stack_launch(plan, stream, &sy);
+}
+
+int qwen_b200_quant_planes_wait_dev(const float* x, int B, int K, int8_t* planes, float* xs_t, int ldxs,
+                                    const unsigned int* wait_flags, unsigned int wait_epoch, int world,
+                                    void* stream) {
+    if (!x || !planes || !xs_t || B <= 0 || K <= 0 || K % 64 || ldxs < B || world < 1 || world > qb::kMaxRanks ||
+        (wait_epoch && !wait_flags))
+        return fail(QB_EINVAL, "qwen_b200_quant_planes_wait_dev: bad arguments");
+    if ((reinterpret_cast<uintptr_t>(x) & 7) || (reinterpret_cast<uintptr_t>(planes) & 1))
+        return fail(QB_EINVAL, "qwen_b200_quant_planes_wait_dev: x must be 8-byte and planes 2-byte aligned");
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    qb::SyncArgs sy{};
+    sy.wait_flags = wait_flags;
+    sy.wait_epoch = wait_epoch;
+    sy.world = world;
+    cudaError_t e = qb::launch_quant_planes(x, B, K, planes, xs_t, ldxs, static_cast<cudaStream_t>(stream), &sy,
+                                            st->err);
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_quant_planes_wait_dev", e);
+}
+
+int qwen_b200_tc_stack_run(int plan, void* stream) { return tc_stack_launch(plan, stream, nullptr); }
 
 int qwen_b200_tc_stack_destroy(int plan) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (plan < 1 || plan > (int)g_tc_plans.size() || !g_tc_plans[plan - 1].live)
         return fail(QB_EINVAL, "tc_stack: bad handle");
     cudaFree(g_tc_plans[plan - 1].dev_descs);
+    cudaFree(g_tc_plans[plan - 1].peers);
+    cudaFree(g_tc_plans[plan - 1].sig_ticket);
     g_tc_plans[plan - 1].dev_descs = nullptr;
+    g_tc_plans[plan - 1].peers = nullptr;
+    g_tc_plans[plan - 1].sig_ticket = nullptr;
     g_tc_plans[plan - 1].live = false;
     return QB_OK;
 }

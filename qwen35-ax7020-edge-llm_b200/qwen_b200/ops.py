@@ -24,7 +24,7 @@ from ._lib import KernelError, check, load
 __all__ = [
     "KernelError", "quant_block64", "bfp8_gemv", "bfp8_gemv_fast", "bfp8_gemv_q", "lm_head_bf16", "lm_head_bfp8",
     "pack_bfp8", "LinearStack", "LmResult", "Planes", "quant_planes", "bfp8_gemm_tc", "BatchedStack",
-    "PeerRegion", "ShardedLinearStack",
+    "PeerRegion", "ShardedLinearStack", "quant_planes_wait", "ShardedBatchedStack",
 ]
 
 
@@ -392,6 +392,63 @@ class ShardedLinearStack:
     def close(self) -> None:
         if getattr(self, "handle", 0) > 0:
             load().qwen_b200_stack_destroy(self.handle)
+            self.handle = 0
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def quant_planes_wait(x: torch.Tensor, out: Planes, wait_flags: int, wait_epoch: int, world: int) -> Planes:
+    """quant_planes() that first waits (bounded) until every rank published
+    ``wait_epoch`` into this GPU's flag array at ``wait_flags``."""
+    x = _need(x, torch.float32, "x")
+    B, K = x.shape
+    check(load().qwen_b200_quant_planes_wait_dev(_ptr(x), B, K, _ptr(out.planes), _ptr(out.xs_t), out.ldxs,
+                                                 wait_flags, wait_epoch, world, _stream()), "quant_planes_wait")
+    return out
+
+
+class ShardedBatchedStack:
+    """A grouped tcgen05 launch over the row slices one rank owns of several
+    batched GEMMs.  ``items``: (Planes, mant int8 [m, K], exps, y) where ``y``
+    is the device address of this rank's first column inside its full
+    [B][ldy] output; ``ldy[i]`` the full row length; ``peer_ptrs[i]`` the
+    full outputs of GEMM i on the other ranks (world - 1, may be empty for
+    world 1); ``row_base[i]`` this rank's first row.  ``run(sig_flags,
+    sig_epoch, rank)`` publishes the epoch when every row reached every GPU."""
+
+    def __init__(self, items, ldy, peer_ptrs, row_base, world: int):
+        n = len(items)
+        P = ctypes.c_void_p * n
+        I = ctypes.c_int * n
+        self._keep = items
+        self.world = world
+        B = items[0][0].B
+        ldxs = items[0][0].ldxs
+        flat = [p for ps in peer_ptrs for p in ps]
+        if len(flat) != n * (world - 1):
+            raise ValueError("ShardedBatchedStack: need world - 1 peer outputs per GEMM")
+        peers = (ctypes.c_void_p * max(1, len(flat)))(*flat) if flat else None
+        h = load().qwen_b200_tc_stack_create_sharded(
+            n, P(*[_ptr(m) for (_, m, _, _) in items]), P(*[_ptr(e) for (_, _, e, _) in items]),
+            P(*[_ptr(p.planes) for (p, _, _, _) in items]), P(*[_ptr(p.xs_t) for (p, _, _, _) in items]),
+            P(*[int(y) for (_, _, _, y) in items]), I(*[m.shape[0] for (_, m, _, _) in items]),
+            I(*[m.shape[1] for (_, m, _, _) in items]), I(*ldy), B, ldxs, world, peers, I(*row_base))
+        if h <= 0:
+            check(h, "ShardedBatchedStack")
+        self.handle = h
+
+    def run(self, sig_flags=None, sig_epoch: int = 0, rank: int = 0, stream: int | None = None) -> None:
+        sf = (ctypes.c_void_p * self.world)(*sig_flags) if sig_flags else None
+        check(load().qwen_b200_tc_stack_run_sync(self.handle, _stream() if stream is None else stream, sf, sig_epoch,
+                                                 self.world, rank), "ShardedBatchedStack.run")
+
+    def close(self) -> None:
+        if getattr(self, "handle", 0) > 0:
+            load().qwen_b200_tc_stack_destroy(self.handle)
             self.handle = 0
 
     def __del__(self):

@@ -67,7 +67,11 @@ def run_layers(layers, x0, gemv, all_gather, world, rank):
 
 class ShardedDeviceStack:
     """This rank's weight slices of a scaled stack on its GPU, plus the
-    gather buffers, driven by grouped launches and NCCL all-gathers.
+    full outputs, driven by grouped launches and the chosen exchange.
+
+    ``batch`` 1 runs the batch-1 GEMV kernels (one activation vector per
+    token); ``batch`` B > 1 runs B sequences per step through the tcgen05
+    kernels (each layer input quantized to planar int16, outputs [B][M]).
 
     `fast` selects the split-K arithmetic (see ops.bfp8_gemv_fast), which
     keeps every GPU busy when each holds few rows.  Weights are fp32 N(0, 0.02) drawn per tensor from a seeded generator on
@@ -76,13 +80,17 @@ class ShardedDeviceStack:
     across steps so that timing never finds them in L2.
     """
 
-    def __init__(self, layers, world, rank, device, copies=1, seed=0, group=None, fast=False, exchange="nccl"):
+    def __init__(self, layers, world, rank, device, copies=1, seed=0, group=None, fast=False, exchange="nccl",
+                 batch=1):
         import torch
 
         from . import ops
 
         if exchange not in ("nccl", "peer"):
             raise ValueError("exchange must be 'nccl' or 'peer'")
+        if batch < 1:
+            raise ValueError("batch must be >= 1")
+        self.B = batch
         self.layers = list(layers)
         self.world, self.rank, self.group = world, rank, group
         self.fast = fast
@@ -122,18 +130,30 @@ class ShardedDeviceStack:
         gx = torch.Generator(device=self.device)
         gx.manual_seed(seed + 7)
         L0 = self.layers[0]
-        self.x0 = torch.randn(L0.gate.K, generator=gx, device=self.device, dtype=torch.float32)
-        # gathered outputs (full vectors, every rank) and this rank's slices
+        B = self.B
+        xshape = (L0.gate.K,) if B == 1 else (B, L0.gate.K)
+        self.x0 = torch.randn(xshape, generator=gx, device=self.device, dtype=torch.float32)
+        # gathered outputs (full [M] vectors or [B][M] matrices, every rank)
+        # and this rank's slices
         if exchange == "peer":
             self._map_regions()
         else:
-            self.full = {t.name: torch.zeros(t.M, dtype=torch.float32, device=self.device)
+            self.full = {t.name: torch.zeros(self._oshape(t.M), dtype=torch.float32, device=self.device)
                          for L in self.layers for t in (L.gate, L.up, L.down)}
-        self.part = {t.name: torch.zeros(self.padded_rows(t.M), dtype=torch.float32, device=self.device)
+        self.part = {t.name: torch.zeros(B * self.padded_rows(t.M), dtype=torch.float32, device=self.device)
                      for L in self.layers for t in (L.gate, L.up, L.down)}
-        self.gath = {t.name: torch.zeros(self.padded_rows(t.M) * world, dtype=torch.float32, device=self.device)
+        self.gath = {t.name: torch.zeros(B * self.padded_rows(t.M) * world, dtype=torch.float32, device=self.device)
                      for L in self.layers for t in (L.gate, L.up, L.down)}
+        if B > 1:   # planar int16 activations, one set per input width (local only)
+            self.planes = {}
+            for L in self.layers:
+                for K in (L.gate.K, L.down.K):
+                    if K not in self.planes:
+                        self.planes[K] = ops.planes_empty(B, K, self.device)
         self.plans = [self._plans(c) for c in range(copies)]
+
+    def _oshape(self, M):
+        return (M,) if self.B == 1 else (self.B, M)
 
     FLAGS_BYTES = 256   # epoch flags at the head of every region: one uint per rank
 
@@ -154,9 +174,9 @@ class ShardedDeviceStack:
         for L in self.layers:
             for t in (L.gate, L.up, L.down):
                 self.voff[t.name] = off
-                off += (4 * t.M + 255) // 256 * 256
+                off += (4 * self.B * t.M + 255) // 256 * 256
         self.region = ops.PeerRegion(off)
-        self.full = {name: self.region.floats(o, t.M) for name, o, t in
+        self.full = {name: self.region.floats(o, self.B * t.M).view(self._oshape(t.M)) for name, o, t in
                      ((t.name, self.voff[t.name], t) for L in self.layers for t in (L.gate, L.up, L.down))}
         self.flags = self.region.uints(0, self.world)
         self.peer_base = [0] * self.world   # every rank's region base, mapped into this process
@@ -199,6 +219,8 @@ class ShardedDeviceStack:
                 return self.full[t.name][r0:r1]
             return self.full[t.name] if self.world == 1 else self.part[t.name][:rows]
 
+        if self.B > 1:
+            return self._batched_plans(copy)
         if self.exchange == "peer":
             return self._peer_plans(copy)
         for L in self.layers:
@@ -238,6 +260,58 @@ class ShardedDeviceStack:
             x = self.full[L.down.name]
         return plans
 
+    def _batched_plans(self, copy):
+        """Per layer one grouped tcgen05 launch for gate+up and one for down.
+        Outputs go straight into the full [B][M] matrices (one rank, or
+        exchange="peer", which also stores into every other rank's), or into
+        this rank's contiguous [B][slice] part for the NCCL all-gather."""
+        from . import ops
+
+        others = [r for r in range(self.world) if r != self.rank]
+        peer = self.exchange == "peer" and self.world > 1
+        plans = []
+
+        def stack(ts, planes):
+            items, ldy, peers, bases = [], [], [], []
+            for t in ts:
+                mant, exps = self.weight(copy, t)
+                r0, r1 = self.shards[t.name]
+                if self.world == 1 or peer:
+                    y = self.full[t.name].data_ptr() + 4 * r0
+                    ldy.append(t.M)
+                else:
+                    y = self.part[t.name].data_ptr()
+                    ldy.append(self.padded_rows(t.M))
+                items.append((planes, mant, exps, y))
+                peers.append([self.peer_base[r] + self.voff[t.name] for r in others] if peer else [])
+                bases.append(r0 if peer else 0)
+            return ops.ShardedBatchedStack(items, ldy, peers, bases, self.world if peer else 1)
+
+        for L in self.layers:
+            plans.append((stack((L.gate, L.up), self.planes[L.gate.K]), stack((L.down,), self.planes[L.down.K])))
+        return plans
+
+    def _step_batched(self, copy):
+        from . import ops
+
+        peer = self.exchange == "peer" and self.world > 1
+        x = self.x0
+        for L, (gu, dn) in zip(self.layers, self.plans[copy]):
+            for plan, xin, outs, K in ((gu, x, (L.gate, L.up), L.gate.K),
+                                       (dn, self.full[L.gate.name], (L.down,), L.down.K)):
+                if peer:
+                    wait = self.epoch & 0xFFFFFFFF
+                    self.epoch += 1
+                    ops.quant_planes_wait(xin, self.planes[K], self.peer_base[self.rank], wait, self.world)
+                    plan.run(self.peer_base, self.epoch & 0xFFFFFFFF, self.rank)
+                else:
+                    ops.quant_planes(xin, self.planes[K])
+                    plan.run()
+                    if self.world > 1:
+                        for t in outs:
+                            self._gather(t)
+            x = self.full[L.down.name]
+
     def _launch_peer(self, plan):
         """Launch n waits for every rank's launch n - 1 and publishes n (one
         rank: stream order is enough, no flags)."""
@@ -255,18 +329,24 @@ class ShardedDeviceStack:
         part, gath, full = self.part[t.name], self.gath[t.name], self.full[t.name]
         if self.world == 1:
             return
-        if part.numel() * self.world == t.M:   # equal slices: gather straight into place
+        B = self.B
+        if B == 1 and part.numel() * self.world == t.M:   # equal slices: gather straight into place
             dist.all_gather_into_tensor(full, part, group=self.group)
             return
         dist.all_gather_into_tensor(gath, part, group=self.group)
-        P = part.numel()
+        P = part.numel() // B
+        g = gath.view(self.world, B, P)
+        f = full.view(B, t.M)
         for r in range(self.world):
             r0, r1 = shard_rows(t.M, self.world, r)
             if r1 > r0:
-                full[r0:r1].copy_(gath[r * P: r * P + (r1 - r0)])
+                f[:, r0:r1].copy_(g[r, :, :r1 - r0])
 
     def step(self, copy=0):
         """One token through every layer (grouped GEMV launches + gathers)."""
+        if self.B > 1:
+            self._step_batched(copy)
+            return
         if self.exchange == "peer":
             for gu, dn in self.plans[copy]:
                 self._launch_peer(gu)
@@ -287,7 +367,10 @@ class ShardedDeviceStack:
         tot = 0
         for L in self.layers:
             for t in (L.gate, L.up, L.down):
-                tot += t.M * t.K + t.M * t.K // 64 + 4 * t.K + 4 * t.M
+                if self.B == 1:
+                    tot += t.M * t.K + t.M * t.K // 64 + 4 * t.K + 4 * t.M
+                else:   # planar int16 activations + block scales in, fp32 out
+                    tot += t.M * t.K + t.M * t.K // 64 + self.B * (2 * t.K + 4 * (t.K // 64) + 4 * t.M)
         return tot
 
     def device_error(self) -> int:

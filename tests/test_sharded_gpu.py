@@ -17,8 +17,11 @@ def _layers():
     return sharded.scaled_layers(layers=2, hidden=1024, ffn=3584)
 
 
+BATCH = 64   # the batched row of the multi-GPU configuration
+
+
 def _outputs(st):
-    return np.concatenate([st.full[t.name].cpu().numpy() for L in st.layers for t in (L.gate, L.up, L.down)])
+    return np.concatenate([st.full[t.name].cpu().numpy().ravel() for L in st.layers for t in (L.gate, L.up, L.down)])
 
 
 def _worker(rank, world, port, path):
@@ -44,6 +47,16 @@ def _worker(rank, world, port, path):
                 assert st.device_error() == 0
                 assert st.flags.cpu().tolist() == [6 * len(st.layers)] * world   # 2 launches x 3 steps
             st.close()
+        st = sharded.ShardedDeviceStack(_layers(), world, rank, f"cuda:{rank}", copies=2, seed=4, exchange=exchange,
+                                        batch=BATCH)
+        for i in range(3):
+            st.step(i % 2)
+        torch.cuda.synchronize()
+        np.save(path + f".{exchange}.b.{rank}.npy", _outputs(st))
+        if exchange == "peer":
+            assert st.device_error() == 0
+            assert st.flags.cpu().tolist() == [6 * len(st.layers)] * world
+        st.close()
     dist.barrier()
     dist.destroy_process_group()
 
@@ -61,6 +74,11 @@ def test_two_gpu_sharded_stack_matches_single_gpu(cuda, tmp_path):
     torch.cuda.synchronize()
     ref = _outputs(single)
     single.close()
+    single = sharded.ShardedDeviceStack(_layers(), 1, 0, "cuda:0", copies=1, seed=4, batch=BATCH)
+    single.step()
+    torch.cuda.synchronize()
+    ref_b = _outputs(single)
+    single.close()
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
@@ -74,6 +92,8 @@ def test_two_gpu_sharded_stack_matches_single_gpu(cuda, tmp_path):
             assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (exchange, r)
             got = np.load(path + f".{exchange}.1.{r}.npy")
             assert np.array_equal(got.view(np.uint32), fast_ref.view(np.uint32)), (exchange, r)
+            got = np.load(path + f".{exchange}.b.{r}.npy")
+            assert np.array_equal(got.view(np.uint32), ref_b.view(np.uint32)), (exchange, "batched", r)
     np.testing.assert_allclose(fast_ref, ref, rtol=1e-4, atol=1e-4)
 
 
@@ -95,6 +115,30 @@ def test_peer_mode_single_rank_matches_plain(cuda):
     assert b.device_error() == 0
     a.close()
     b.close()
+
+
+def test_batched_single_rank_chains_layers(cuda):
+    """batch > 1 on one rank: every layer's outputs equal the tcgen05 GEMM of
+    the previous output, computed GEMM by GEMM through ops (same kernels,
+    checks the layer chaining and the strided outputs); exchange="peer" on
+    one rank gives the same bits."""
+    import torch
+
+    from qwen_b200 import ops, sharded
+
+    for exchange in ("nccl", "peer"):
+        st = sharded.ShardedDeviceStack(_layers(), 1, 0, "cuda:0", copies=1, seed=4, batch=12, exchange=exchange)
+        st.step()
+        torch.cuda.synchronize()
+        x = st.x0
+        for L in st.layers:
+            for t, xin in ((L.gate, x), (L.up, x), (L.down, None)):
+                xin = xin if xin is not None else st.full[L.gate.name]
+                mant, exps = st.weight(0, t)
+                y = ops.bfp8_gemm_tc(ops.quant_planes(xin.contiguous()), mant, exps)
+                assert torch.equal(y.view(torch.int32), st.full[t.name].view(torch.int32)), (exchange, t.name)
+            x = st.full[L.down.name]
+        st.close()
 
 
 def test_peer_flag_wait_times_out_with_status(cuda):
