@@ -69,35 +69,54 @@ __device__ __forceinline__ const GemvDesc& prep_desc(const PrepArgs& A, int d) {
     return A.list ? A.list[d] : A.single;
 }
 
-// grid (n, chunks): CTA (d, c) prepares blocks [64c, 64c + 64) of GEMV d.
-__global__ void __launch_bounds__(kThreads) act_prep_kernel(const __grid_constant__ PrepArgs A) {
+// grid (n, chunks), kPrepThreads threads: CTA (d, c) prepares blocks
+// [kPrepChunk*c, kPrepChunk*(c+1)) of GEMV d, each warp kPrepPerWarp blocks
+// with all their loads in flight at once.  Small CTAs (64 threads, <= 32
+// registers) fit beside a resident gemv_warp CTA, so the PDL-launched GEMV
+// starts streaming weights while the activations are still being prepared.
+constexpr int kPrepThreads = 64;
+constexpr int kPrepPerWarp = 4;
+constexpr int kPrepChunk = kPrepThreads / 32 * kPrepPerWarp;
+
+__global__ void __launch_bounds__(kPrepThreads) act_prep_kernel(const __grid_constant__ PrepArgs A) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (A.wait_epoch) wait_peer_flags(A.wait_flags, A.world, A.wait_epoch, A.err);
     const GemvDesc& D = prep_desc(A, blockIdx.x);
     const int nb = D.K >> 6;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int b_end = min(nb, (int)(blockIdx.y + 1) * 64);
-    for (int b = blockIdx.y * 64 + warp; b < b_end; b += kWarps) {
+    const int b0 = blockIdx.y * kPrepChunk + warp * kPrepPerWarp;
+    if (b0 >= nb) return;
+    const float* x = D.x;
+    float2 v[kPrepPerWarp];
+    if (x) {
+#pragma unroll
+        for (int j = 0; j < kPrepPerWarp; j++)
+            if (b0 + j < nb) v[j] = reinterpret_cast<const float2*>(x + 64 * (b0 + j))[lane];
+    }
+#pragma unroll
+    for (int j = 0; j < kPrepPerWarp; j++) {
+        const int b = b0 + j;
+        if (b >= nb) break;
         int q0, q1;
         float xs;
-        if (D.x) {
-            float2 v = reinterpret_cast<const float2*>(D.x + 64 * b)[lane];
-            float a = fmaxf(fabsf(v.x), fabsf(v.y));
+        if (x) {
+            const float2 vv = v[j];
+            float a = fmaxf(fabsf(vv.x), fabsf(vv.y));
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
             if (a > 1e-20f) {
                 float q = __fdiv_rn(16384.0f, a);
                 xs = __fdiv_rn(a, 16384.0f);
-                q0 = __float2int_rn(__fmul_rn(v.x, q));
-                q1 = __float2int_rn(__fmul_rn(v.y, q));
+                q0 = __float2int_rn(__fmul_rn(vv.x, q));
+                q1 = __float2int_rn(__fmul_rn(vv.y, q));
             } else {
                 xs = 0.0f;
                 q0 = q1 = 0;
             }
         } else {
-            short2 v = reinterpret_cast<const short2*>(D.xq + 64 * b)[lane];
-            q0 = v.x;
-            q1 = v.y;
+            short2 w = reinterpret_cast<const short2*>(D.xq + 64 * b)[lane];
+            q0 = w.x;
+            q1 = w.y;
             xs = D.xs[b];
         }
         uint32_t mine = ((uint32_t)q0 & 0xFFFFu) | ((uint32_t)q1 << 16);
@@ -297,7 +316,8 @@ __device__ __forceinline__ void stage_blocks(const unsigned char* st, const uint
 }
 
 template <bool LM, bool FAST>
-__global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_constant__ WArgs A) {
+// <= 248 registers: 2048 of the SM's 65536 stay free for a 64-thread act_prep CTA
+__global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs A) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                            ~uintptr_t(1023));
@@ -360,8 +380,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_con
         if (exhausted) return nu_total;
         int u;
         if (A.ctr) {
+            // units [0, W) go to the warps statically (warp gw starts on unit
+            // gw), the counter hands out the rest
             unsigned int v = 0;
-            if (lane == 0) v = atomicAdd(&A.ctr[0], 1u);
+            if (lane == 0) v = atomicAdd(&A.ctr[0], 1u) + (unsigned int)W;
             u = (int)__shfl_sync(0xffffffffu, v, 0);
             if (u >= nu_total) {
                 exhausted = true;
@@ -386,9 +408,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_con
     // overlaps the unit's streaming
     int claimed0, claimed1;          // claim sequence entries 2j and 2j+1
     int kp = 0;                      // index of the producer's unit in the claim sequence
-    claimed0 = claim();
+    const int gw = blockIdx.x * kWarps + warp;
+    claimed0 = A.ctr ? (gw < nu_total ? gw : nu_total) : claim();
     claimed1 = nu_total;
-    int ahead = claim();
+    int ahead = nu_total;            // claimed once the activations are ready (its round trip overlaps their copies)
     Unit pu = load_unit(sdesc, nd, nu_total, claimed0);
     int ps = pu.valid ? pu.st0 : 0;
     if (lane == 0 && pu.valid) tma_prefetch_desc(sdesc[pu.d].tmap);
@@ -439,8 +462,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_con
         cp_async_commit();
     };
 
+    // a unit has >= 2 stages, so the first issue never needs the next claim;
+    // the second goes out now unless it could finish the unit
     issue(0, false);
-    issue(1, false);
+    bool issued1 = false;
+    if (!pu.valid || pu.st1 - ps >= 2) {
+        issue(1, false);
+        issued1 = true;
+    }
 
     // the activations come from act_prep (programmatic dependent launch)
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -454,6 +483,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_warp_kernel(const __grid_con
             bulk_load(xring + kXp + 512, pend_xs1, 16, &bar[1]);
         }
     }
+    ahead = claim();
+    if (!issued1) issue(1, true);
 
     int kc = 0;
     Unit cu = load_unit(sdesc, nd, nu_total, claimed0);
@@ -643,6 +674,12 @@ bool gemv_plan(GemvDesc* descs, int n, uint32_t* act, GemvPlan* plan, int mode, 
         }
         d.seg_stages = (nst + nseg - 1) / nseg;
         d.nseg = (nst + d.seg_stages - 1) / d.seg_stages;
+        // every segment, the last one included, has >= 2 stages: the kernel
+        // issues a unit's first stage before it claims the next unit
+        while (d.nseg > 1 && nst - (d.nseg - 1) * d.seg_stages < 2) {
+            d.seg_stages++;
+            d.nseg = (nst + d.seg_stages - 1) / d.seg_stages;
+        }
         pair_words += (gemv_act_words(d.K) + 3) & ~size_t(3);
         if (d.nseg > 1) {
             part_words += (size_t)d.nseg * d.M;
@@ -692,9 +729,9 @@ bool gemv_plan(GemvDesc* descs, int n, uint32_t* act, GemvPlan* plan, int mode, 
     return true;
 }
 
-static cudaError_t launch_prep(const PrepArgs& P, int nchunks, cudaStream_t stream) {
-    dim3 grid(P.n, nchunks);
-    act_prep_kernel<<<grid, kThreads, 0, stream>>>(P);
+static cudaError_t launch_prep(const PrepArgs& P, int kmax, cudaStream_t stream) {
+    dim3 grid(P.n, (kmax / 64 + kPrepChunk - 1) / kPrepChunk);
+    act_prep_kernel<<<grid, kPrepThreads, 0, stream>>>(P);
     return cudaGetLastError();
 }
 
@@ -734,7 +771,7 @@ cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, un
         P.wait_epoch = sync->wait_epoch;
         P.world = sync->world;
     }
-    cudaError_t e = launch_prep(P, (plan.kmax / 64 + 63) / 64, stream);
+    cudaError_t e = launch_prep(P, plan.kmax, stream);
     if (e != cudaSuccess) return e;
     WArgs A{};
     A.list = dev_descs;
@@ -757,7 +794,7 @@ cudaError_t launch_gemv_fast(const GemvDesc& d0, uint32_t* act, size_t act_cap_w
     PrepArgs P{};
     P.single = d;
     P.n = 1;
-    cudaError_t e = launch_prep(P, (d.K / 64 + 63) / 64, stream);
+    cudaError_t e = launch_prep(P, d.K, stream);
     if (e != cudaSuccess) return e;
     WArgs A{};
     A.single = d;
@@ -786,7 +823,7 @@ cudaError_t launch_gemv(const GemvDesc& d0, uint32_t* act, unsigned int* err, cu
     PrepArgs P{};
     P.single = d;
     P.n = 1;
-    cudaError_t e = launch_prep(P, (d.K / 64 + 63) / 64, stream);
+    cudaError_t e = launch_prep(P, d.K, stream);
     if (e != cudaSuccess) return e;
     WArgs A{};
     A.single = d;
@@ -824,7 +861,7 @@ cudaError_t launch_bfp8_lm_head(const float* h, const int8_t* mant, const uint8_
     PrepArgs P{};
     P.single = d;
     P.n = 1;
-    cudaError_t e = launch_prep(P, (d.K / 64 + 63) / 64, stream);
+    cudaError_t e = launch_prep(P, d.K, stream);
     if (e != cudaSuccess) return e;
     WArgs A{};
     A.single = d;
