@@ -533,7 +533,7 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
             merge_warp_lists64(cand, &s_cand_count, A.kk);
         }
         unsigned long long* work = reinterpret_cast<unsigned long long*>(rings);
-        lm_finish(A.sc, cand, &s_cand_count, work, (kWarps * kRing * kStage) / 8, lm.best, A.kk, A.out_id,
+        lm_finish(A.sc, cand, kCandCap, &s_cand_count, work, (kWarps * kRing * kStage) / 8, lm.best, A.kk, A.out_id,
                   A.out_ids, A.out_scores, A.out_n, s_red, lm.wl);
     }
 }

@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1) lm_bf16_kernel(const __grid_const
     }
     __syncthreads();
     unsigned long long* work = reinterpret_cast<unsigned long long*>(stages);
-    lm_finish(A.sc, cand, &s_cand_count, work, (kP * kStage) / 8, best, TOPK ? A.kk : 0, A.out_id,
+    lm_finish(A.sc, cand, kCandCap, &s_cand_count, work, (kP * kStage) / 8, best, TOPK ? A.kk : 0, A.out_id,
               A.out_ids, A.out_scores, A.out_n, s_red);
 }
 
@@ -293,7 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1) lm_bf16_warp_kernel(const __grid_
         merge_warp_lists64(cand, &s_cand_count, A.kk);
     }
     unsigned long long* work = reinterpret_cast<unsigned long long*>(rings);
-    lm_finish(A.sc, cand, &s_cand_count, work, (kWWarps * kWRing * kWStage) / 8, best, TOPK ? A.kk : 0,
+    lm_finish(A.sc, cand, 64 * kWWarps + 64, &s_cand_count, work, (kWWarps * kWRing * kWStage) / 8, best, TOPK ? A.kk : 0,
               A.out_id, A.out_ids, A.out_scores, A.out_n, s_red, TOPK);
 }
 
@@ -348,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(const float* scores
         }
         __syncthreads();
     }
-    lm_finish(A.sc, cand, &s_cand_count, work, kCandCap * 4, best, A.kk, A.out_id, A.out_ids,
+    lm_finish(A.sc, cand, kCandCap, &s_cand_count, work, kCandCap * 4, best, A.kk, A.out_id, A.out_ids,
               A.out_scores, A.out_n, s_red);
 }
 

@@ -217,7 +217,8 @@ __device__ inline void rank_place(const unsigned long long* work, int m, int kee
 }
 
 // End-of-CTA work for the lm_head kernels.  `cand`/`cand_count` is the CTA's
-// shared buffer (kCandCap keys; with `precompacted` it already holds the
+// shared buffer (cand_cap keys, >= 64 * warps + 64 and >= the next power of
+// two of the grid size; with `precompacted` it already holds the
 // CTA's best kk keys, descending), `work` a shared scratch area of `work_cap`
 // keys that may alias the CTA's stage buffers.  `best` is this thread's
 // argmax key.  Writes out_id[0] (argmax) and, for kk > 0,
@@ -228,7 +229,7 @@ __device__ inline void rank_place(const unsigned long long* work, int m, int kee
 // least T2 = the kk-th largest head L_c[0]; every key >= T = max(T1, T2)
 // is gathered (typically ~2kk of them) and ranked.  If too many qualify
 // the CTA falls back to a radix select of K* over the lists.
-__device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int* cand_count,
+__device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int cand_cap, int* cand_count,
                                  unsigned long long* work, int work_cap, unsigned long long best,
                                  int kk, int* out_id, int* out_ids, float* out_scores, int* out_n,
                                  unsigned long long* red, bool precompacted = false) {
@@ -240,7 +241,7 @@ __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int* c
     if (kk > 0) {
         if (precompacted)
             __syncthreads();   // cand[0..*cand_count) already holds the CTA's best kk, descending
-        else if (kk <= 64 && 64 * (int)(blockDim.x >> 5) + kk <= kCandCap)
+        else if (kk <= 64 && 64 * (int)(blockDim.x >> 5) + kk <= cand_cap)
             cand_topk64(cand, cand_count, kk);
         else
             cand_compact(cand, cand_count, kk);
@@ -263,7 +264,7 @@ __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int* c
         *out_id = k ? key_id(k) : 0;
     }
     constexpr int kPre = 8;   // keys per list read by the fast path
-    if (kk > 0 && (long long)gridDim.x * (kPre + 2) <= work_cap && (int)gridDim.x <= kCandCap) {
+    if (kk > 0 && (long long)gridDim.x * (kPre + 2) <= work_cap && (int)gridDim.x <= cand_cap) {
         // Fast path: one round of independent L2 loads brings every list's
         // count, first kPre keys and kk-th key.  Every key >= T lies in a
         // list prefix unless some list's kPre-th key is itself >= T; only
@@ -338,13 +339,13 @@ __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int* c
             const unsigned long long key = work[(size_t)c * E + e];
             if (key != 0ull && key >= T) {
                 const int p = atomicAdd(&s_m2, 1);
-                if (p < kCandCap) cand[p] = key;
+                if (p < cand_cap) cand[p] = key;
                 if (e == kPre - 1 && s_counts[c] > kPre) s_spill = 1;
             }
         }
         __syncthreads();
         const int m = s_m2;
-        if (!s_spill && m <= kCandCap && m <= work_cap) {
+        if (!s_spill && m <= cand_cap && m <= work_cap) {
             rank_place(cand, m, want, work);   // work is free again
             for (int i = tid; i < want; i += blockDim.x) {
                 out_ids[i] = key_id(work[i]);
@@ -465,7 +466,7 @@ __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int* c
                     const unsigned long long key = lists[(size_t)c * kk + i];
                     if (key >= kstar) {
                         int p = atomicAdd(&s_m, 1);
-                        if (p < kTopkMax) cand[p] = key;
+                        if (p < cand_cap) cand[p] = key;
                     }
                 }
             }
