@@ -146,6 +146,7 @@ struct WArgs {
     int* out_ids;
     float* out_scores;
     int* out_n;
+    int lm_warp_lists;      // top-k in per-warp register lists (k <= 64 and too many rows per CTA to buffer)
     SyncArgs sync;          // row-sharded stacks: completion signal (sig_epoch 0: none)
 };
 
@@ -257,9 +258,14 @@ __device__ __forceinline__ void unit_result(const WArgs& A, const SDesc* T, cons
                     warp_fold64(lm.r0, lm.r1, key, 0ull);
                     lm.thr = __shfl_sync(0xffffffffu, lm.r1, 31);
                 }
-            } else if (ok && yv > -3.402823466e38f) {
-                const int p = atomicAdd(lm.cand_count, 1);
-                if (p < kCandCap) lm.cand[p] = cand_key(yv, row);
+            } else {   // append the unit's keys to the CTA's buffer (one atomic per warp)
+                const bool take = ok && yv > -3.402823466e38f;
+                const unsigned int bal = __ballot_sync(0xffffffffu, take);
+                int base = 0;
+                if (lane == 0 && bal) base = atomicAdd(lm.cand_count, __popc(bal));
+                base = __shfl_sync(0xffffffffu, base, 0);
+                const int p = base + __popc(bal & ((1u << lane) - 1u));
+                if (take && p < kCandCap) lm.cand[p] = cand_key(yv, row);
             }
         }
         return;
@@ -366,7 +372,7 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
     lm.best = 0ull;
     lm.cand = cand;
     lm.cand_count = &s_cand_count;
-    lm.wl = A.kk > 0 && A.kk <= 64;
+    lm.wl = A.kk > 0 && A.lm_warp_lists;
     lm.r0 = lm.r1 = lm.thr = 0ull;
 
     const int W = gridDim.x * kWarps;
@@ -850,14 +856,14 @@ cudaError_t launch_bfp8_lm_head(const float* h, const int8_t* mant, const uint8_
     if (!fast_shape_ok(d) || !gemv_plan(&d, 1, act, &plan)) return cudaErrorInvalidValue;
     const int grid = std::min(std::min(num_sms(), (plan.total_units + kWarps - 1) / kWarps), kMaxGrid);
     const int kk = std::min(k, vocab);
-    // k <= 64 keeps candidates in registers; a larger k appends every row to
-    // the CTA's buffer, which bounds the rows per CTA
-    const bool warp_lists = kk <= 64;
-    if (!warp_lists) {
-        const long long rows_per_cta =
-            (long long)((plan.total_units + grid * kWarps - 1) / (grid * kWarps)) * kWarps * kRows;
-        if (rows_per_cta > kCandCap) return cudaErrorInvalidValue;
-    }
+    // Every scored row is appended to the CTA's shared buffer and the CTA
+    // selects its top-k once at its end; when its rows do not fit the buffer,
+    // k <= 64 keeps running per-warp top-64 lists in registers instead (a
+    // bitonic fold per unit, which stalls that warp's weight stream).
+    const long long rows_per_cta =
+        (long long)((plan.total_units + grid * kWarps - 1) / (grid * kWarps)) * kWarps * kRows;
+    const bool warp_lists = rows_per_cta > kCandCap;
+    if (warp_lists && kk > 64) return cudaErrorInvalidValue;
     PrepArgs P{};
     P.single = d;
     P.n = 1;
@@ -876,6 +882,7 @@ cudaError_t launch_bfp8_lm_head(const float* h, const int8_t* mant, const uint8_
     A.out_ids = out_ids;
     A.out_scores = out_scores;
     A.out_n = out_n;
+    A.lm_warp_lists = warp_lists ? 1 : 0;
     return launch_warp<true, false>(A, grid, stream);
 }
 
