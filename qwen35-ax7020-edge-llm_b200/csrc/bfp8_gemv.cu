@@ -69,6 +69,39 @@ __device__ __forceinline__ const GemvDesc& prep_desc(const PrepArgs& A, int d) {
     return A.list ? A.list[d] : A.single;
 }
 
+// The reference block-64 quantizer on one block, lane l holding elements 2l
+// and 2l+1 in `v`: q = 16384/amax, xq = rint(x*q) half-even, xs = amax/16384;
+// a zero block when amax <= 1e-20 (quant_x_blocks, qwen_kernels_opt.c:182-205).
+__device__ __forceinline__ void block_quant(float2 v, int& q0, int& q1, float& xs) {
+    float a = fmaxf(fabsf(v.x), fabsf(v.y));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    if (a > 1e-20f) {
+        const float q = __fdiv_rn(16384.0f, a);
+        xs = __fdiv_rn(a, 16384.0f);
+        q0 = __float2int_rn(__fmul_rn(v.x, q));
+        q1 = __float2int_rn(__fmul_rn(v.y, q));
+    } else {
+        xs = 0.0f;
+        q0 = q1 = 0;
+    }
+}
+
+// Block b of the paired activation layout the GEMV consumes (global or
+// shared memory) from lane l's int16 elements 2l, 2l+1 and the block scale.
+__device__ __forceinline__ void block_store(uint32_t* xpairs, float* xscale, int b, int lane, int q0, int q1,
+                                            float xs) {
+    const uint32_t mine = ((uint32_t)q0 & 0xFFFFu) | ((uint32_t)q1 << 16);
+    const uint32_t part = __shfl_down_sync(0xffffffffu, mine, 2);
+    if ((lane & 3) < 2) {
+        const int g = lane >> 2, p = 2 * (lane & 3);
+        const uint32_t w0 = (mine & 0xFFFFu) | (part << 16);
+        const uint32_t w1 = (mine >> 16) | (part & 0xFFFF0000u);
+        *reinterpret_cast<uint2*>(xpairs + b * 32 + g * 4 + p) = make_uint2(w0, w1);
+    }
+    if (lane == 0) xscale[b] = xs;
+}
+
 // grid (n, chunks), kPrepThreads threads: CTA (d, c) prepares blocks
 // [kPrepChunk*c, kPrepChunk*(c+1)) of GEMV d, each warp kPrepPerWarp blocks
 // with all their loads in flight at once.  Small CTAs (64 threads, <= 32
@@ -100,34 +133,14 @@ __global__ void __launch_bounds__(kPrepThreads) act_prep_kernel(const __grid_con
         int q0, q1;
         float xs;
         if (x) {
-            const float2 vv = v[j];
-            float a = fmaxf(fabsf(vv.x), fabsf(vv.y));
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-            if (a > 1e-20f) {
-                float q = __fdiv_rn(16384.0f, a);
-                xs = __fdiv_rn(a, 16384.0f);
-                q0 = __float2int_rn(__fmul_rn(vv.x, q));
-                q1 = __float2int_rn(__fmul_rn(vv.y, q));
-            } else {
-                xs = 0.0f;
-                q0 = q1 = 0;
-            }
+            block_quant(v[j], q0, q1, xs);
         } else {
-            short2 w = reinterpret_cast<const short2*>(D.xq + 64 * b)[lane];
+            const short2 w = reinterpret_cast<const short2*>(D.xq + 64 * b)[lane];
             q0 = w.x;
             q1 = w.y;
             xs = D.xs[b];
         }
-        uint32_t mine = ((uint32_t)q0 & 0xFFFFu) | ((uint32_t)q1 << 16);
-        uint32_t part = __shfl_down_sync(0xffffffffu, mine, 2);
-        if ((lane & 3) < 2) {
-            int g = lane >> 2, p = 2 * (lane & 3);
-            uint32_t w0 = (mine & 0xFFFFu) | (part << 16);
-            uint32_t w1 = (mine >> 16) | (part & 0xFFFF0000u);
-            *reinterpret_cast<uint2*>(D.xpairs + b * 32 + g * 4 + p) = make_uint2(w0, w1);
-        }
-        if (lane == 0) D.xscale[b] = xs;
+        block_store(D.xpairs, D.xscale, b, lane, q0, q1, xs);
     }
 }
 
@@ -147,6 +160,8 @@ struct WArgs {
     float* out_scores;
     int* out_n;
     int lm_warp_lists;      // top-k in per-warp register lists (k <= 64 and too many rows per CTA to buffer)
+    int res_act;            // single GEMV, small K: every CTA quantizes the whole activation into its own
+                            // shared memory (no act_prep kernel, no activation copies per stage)
     SyncArgs sync;          // row-sharded stacks: completion signal (sig_epoch 0: none)
 };
 
@@ -431,20 +446,21 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
     const uint32_t* pend_xp1 = nullptr;
     const float* pend_xs0 = nullptr;
     const float* pend_xs1 = nullptr;
+    const bool res = A.res_act != 0;
     auto issue = [&](int slot, bool xp_ready) {
         if (pu.valid) {
             if (lane == 0) {
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                mbar_arrive_expect_tx(&bar[slot], kStage + kXp);
+                mbar_arrive_expect_tx(&bar[slot], res ? kStage : kStage + kXp);
                 const void* tm = sdesc[pu.d].tmap;
                 tma_load_2d(ring + slot * kStage, tm, ps * 256, pu.r0, &bar[slot]);
                 tma_load_2d(ring + slot * kStage + kBox, tm, ps * 256 + 128, pu.r0, &bar[slot]);
-                if (xp_ready) {
+                if (xp_ready && !res) {
                     bulk_load(xring + slot * kXp, pu.xp + ps * 128, 512, &bar[slot]);
                     bulk_load(xring + slot * kXp + 512, pu.xs + ps * 4, 16, &bar[slot]);
                 }
             }
-            if (!xp_ready) {
+            if (!xp_ready && !res) {
                 if (slot == 0) {
                     pend_xp0 = pu.xp + ps * 128;
                     pend_xs0 = pu.xs + ps * 4;
@@ -477,9 +493,43 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
         issued1 = true;
     }
 
-    // the activations come from act_prep (programmatic dependent launch)
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (lane == 0) {
+    if (res) {
+        // resident activation: this CTA quantizes all nb blocks of the single
+        // GEMV's activation into the (otherwise unused) activation-ring space
+        const GemvDesc& D = wdesc(A, 0);
+        const int nb = D.K >> 6;
+        uint32_t* xp = reinterpret_cast<uint32_t*>(xrings);
+        float* xsc = reinterpret_cast<float*>(xrings + (size_t)D.K * 2);
+        for (int b0 = warp; b0 < nb; b0 += 4 * kWarps) {
+            float2 v[4];
+            if (D.x) {
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    if (b0 + j * kWarps < nb) v[j] = reinterpret_cast<const float2*>(D.x + 64 * (b0 + j * kWarps))[lane];
+            }
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int b = b0 + j * kWarps;
+                if (b >= nb) break;
+                int q0, q1;
+                float xs;
+                if (D.x) {
+                    block_quant(v[j], q0, q1, xs);
+                } else {
+                    short2 w = reinterpret_cast<const short2*>(D.xq + 64 * b)[lane];
+                    q0 = w.x;
+                    q1 = w.y;
+                    xs = D.xs[b];
+                }
+                block_store(xp, xsc, b, lane, q0, q1, xs);
+            }
+        }
+        __syncthreads();
+    } else {
+        // the activations come from act_prep (programmatic dependent launch)
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+    }
+    if (lane == 0 && !res) {
         if (pend_xp0) {
             bulk_load(xring, pend_xp0, 512, &bar[0]);
             bulk_load(xring + 512, pend_xs0, 16, &bar[0]);
@@ -510,8 +560,10 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
         const bool odd = odd_unit && (cu.r0 + lane == cu.M - 1);
         const uint32_t ew = *reinterpret_cast<const uint32_t*>(ering + slot * 128 + lane * 4);
         const unsigned char* st = ring + slot * kStage + lane * 128;
-        const uint4* xst = reinterpret_cast<const uint4*>(xring + slot * kXp);
-        const float* xsst = reinterpret_cast<const float*>(xring + slot * kXp + 512);
+        const uint4* xst = res ? reinterpret_cast<const uint4*>(xrings + cs * 512)
+                               : reinterpret_cast<const uint4*>(xring + slot * kXp);
+        const float* xsst = res ? reinterpret_cast<const float*>(xrings + (size_t)cu.K * 2) + cs * 4
+                                : reinterpret_cast<const float*>(xring + slot * kXp + 512);
         if (FAST)
             stage_blocks<false, true>(st, xst, xsst, ew, sw, false, f0, f1, f2, f3, fo);
         else if (!odd_unit)
@@ -735,6 +787,10 @@ bool gemv_plan(GemvDesc* descs, int n, uint32_t* act, GemvPlan* plan, int mode, 
     return true;
 }
 
+// A single GEMV whose whole paired activation (2K bytes + K/16 scale bytes)
+// fits the activation-ring space quantizes it in every CTA (res_act).
+static bool res_fits(int K) { return 2 * (size_t)K + (size_t)K / 16 <= (size_t)kWarps * kRing * kXp; }
+
 static cudaError_t launch_prep(const PrepArgs& P, int kmax, cudaStream_t stream) {
     dim3 grid(P.n, (kmax / 64 + kPrepChunk - 1) / kPrepChunk);
     act_prep_kernel<<<grid, kPrepThreads, 0, stream>>>(P);
@@ -760,7 +816,7 @@ static cudaError_t launch_warp(const WArgs& A, int grid, cudaStream_t stream) {
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = A.res_act ? 0 : 1;   // a programmatic dependent of act_prep unless it quantizes itself
     return cudaLaunchKernelEx(&cfg, gemv_warp_kernel<LM, FAST>, A);
 }
 
@@ -797,12 +853,16 @@ cudaError_t launch_gemv_fast(const GemvDesc& d0, uint32_t* act, size_t act_cap_w
     GemvPlan plan;
     if (!act || !tickets || !gemv_plan(&d, 1, act, &plan, kFast, act_cap_words, tickets, tickets_cap))
         return cudaErrorInvalidValue;
-    PrepArgs P{};
-    P.single = d;
-    P.n = 1;
-    cudaError_t e = launch_prep(P, d.K, stream);
-    if (e != cudaSuccess) return e;
+    const bool res = res_fits(d.K);
+    if (!res) {
+        PrepArgs P{};
+        P.single = d;
+        P.n = 1;
+        cudaError_t e = launch_prep(P, d.K, stream);
+        if (e != cudaSuccess) return e;
+    }
     WArgs A{};
+    A.res_act = res ? 1 : 0;
     A.single = d;
     A.n = 1;
     A.total_units = plan.total_units;
@@ -826,12 +886,16 @@ cudaError_t launch_gemv(const GemvDesc& d0, uint32_t* act, unsigned int* err, cu
         gemv_generic_kernel<<<(d.M + kThreads - 1) / kThreads, kThreads, smem, stream>>>(d);
         return cudaGetLastError();
     }
-    PrepArgs P{};
-    P.single = d;
-    P.n = 1;
-    cudaError_t e = launch_prep(P, d.K, stream);
-    if (e != cudaSuccess) return e;
+    const bool res = res_fits(d.K);
+    if (!res) {
+        PrepArgs P{};
+        P.single = d;
+        P.n = 1;
+        cudaError_t e = launch_prep(P, d.K, stream);
+        if (e != cudaSuccess) return e;
+    }
     WArgs A{};
+    A.res_act = res ? 1 : 0;
     A.single = d;
     A.n = 1;
     A.total_units = plan.total_units;
@@ -864,12 +928,16 @@ cudaError_t launch_bfp8_lm_head(const float* h, const int8_t* mant, const uint8_
         (long long)((plan.total_units + grid * kWarps - 1) / (grid * kWarps)) * kWarps * kRows;
     const bool warp_lists = rows_per_cta > kCandCap;
     if (warp_lists && kk > 64) return cudaErrorInvalidValue;
-    PrepArgs P{};
-    P.single = d;
-    P.n = 1;
-    cudaError_t e = launch_prep(P, d.K, stream);
-    if (e != cudaSuccess) return e;
+    const bool res = res_fits(d.K);
+    if (!res) {
+        PrepArgs P{};
+        P.single = d;
+        P.n = 1;
+        cudaError_t e = launch_prep(P, d.K, stream);
+        if (e != cudaSuccess) return e;
+    }
     WArgs A{};
+    A.res_act = res ? 1 : 0;
     A.single = d;
     A.n = 1;
     A.total_units = plan.total_units;
