@@ -35,6 +35,7 @@ namespace qb {
 namespace {
 
 constexpr int kTileRows = 128;
+static_assert(kTileRows == kTcTileRowsPublic, "partial slots are laid out for 128-row tiles");
 constexpr int kBoxK = 128;     // K bytes of one TMA box (one 128-byte swizzled row per matrix row)
 
 // 64-blocks per pipeline stage: four for narrow tiles (so the single TMA and
@@ -61,7 +62,7 @@ constexpr float kMagicSum = 3233808384.0f;   // 1.5*2^31 + 1.5*2^23 = 771 * 2^22
 // Scalar fields of one GEMM, copied to shared memory at kernel start so that
 // unit lookups never wait on global loads.
 struct DescRow {
-    int unit_begin, n_nt, nb, M, B, ldy;
+    int unit_begin, n_nt, nb, M, B, ldy, tile_begin, pad_;
     const uint8_t* exps;
     float* y;
     int32_t* dots;
@@ -74,7 +75,10 @@ struct UnitInfo {
     float* y;
     int32_t* dots;
     const PeerOut* peer;
-    int M, nb, B, rt, nt, ebulk, ldy, pad_;
+    unsigned int* tickets;  // pieces of a cut tile: the tile's counters
+    int M, nb, B, rt, nt, ebulk, ldy;
+    int j0, nbs;            // the unit covers blocks [j0, j0 + nbs) of the tile; nbs == 0 ends the sequence
+    int npieces, cfirst, pslot;   // a tile cut between CTAs: its piece count, first CTA, this piece's slot
 };
 
 template <int N>
@@ -123,6 +127,9 @@ struct TcLaunch {
     int n, total_units;
     unsigned int* err;
     SyncArgs sync;         // row-sharded plans: completion signal (sig_epoch 0: none)
+    float* partial;        // stream-K (nullptr: one whole tile per unit, CTA c takes units c, c + G, ...)
+    unsigned int* tickets;
+    long long total_stages;
     TcDesc one;
 };
 
@@ -290,6 +297,8 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
         r.M = d->M;
         r.B = d->B;
         r.ldy = d->ldy;
+        r.tile_begin = d->tile_begin;
+        r.pad_ = 0;
         r.exps = d->exps;
         r.y = d->y;
         r.dots = d->dots;
@@ -336,21 +345,22 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
         // ---------------------------------------------------- TMA producer
         if (lane == 0) {
             uint32_t gs = 0;
-            int di = 0;
+            int di = 0, i = 0, prefetched = -1;   // prefetched: last GEMM whose successor's maps were warmed
             bool bad = false;
-            for (int u = blockIdx.x, i = 0; u < p.total_units && !bad; u += gridDim.x, i++) {
-                di = desc_index(tab, n, u, di);
+            // Publish unit i (tile `tile` of GEMM di, stages [st0, st1) of its
+            // K) to the MMA and epilogue warps, then stream its stages.
+            auto unit = [&](int tile, int st0, int st1, int npieces, int cfirst) {
                 const DescRow& r = tab[di];
                 const TcDesc* d = p.descs ? p.descs + di : &p.one;
-                if (u + (int)gridDim.x < p.total_units) {   // warm the TMA descriptor cache for the next unit
-                    const int dj = desc_index(tab, n, u + gridDim.x, di);
-                    const TcDesc* dn = p.descs ? p.descs + dj : &p.one;
-                    tma_prefetch_desc(&dn->tm_w);
-                    tma_prefetch_desc(&dn->tm_x);
-                    tma_prefetch_desc(&dn->tm_s);
+                if (p.partial && di != prefetched && p.descs && di + 1 < n) {
+                    // stream-K walks the GEMMs in order: warm the next one's TMA maps
+                    tma_prefetch_desc(&p.descs[di + 1].tm_w);
+                    tma_prefetch_desc(&p.descs[di + 1].tm_x);
+                    tma_prefetch_desc(&p.descs[di + 1].tm_s);
+                    prefetched = di;
                 }
-                const int local = u - r.unit_begin, rt = local / r.n_nt, nt = local - rt * r.n_nt;
-                const int nb = r.nb, nst = (nb + C::kBPS - 1) / C::kBPS;
+                const int rt = tile / r.n_nt, nt = tile - rt * r.n_nt;
+                const int nb = r.nb, j0 = st0 * C::kBPS, nbs = min(nb, st1 * C::kBPS) - j0;
                 const int eb = i & 1;
                 const int rows = min(kTileRows, r.M - rt * kTileRows);
                 const uint32_t ebytes = (uint32_t)rows * (uint32_t)nb;
@@ -368,7 +378,16 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
                 info.rt = rt;
                 info.nt = nt;
                 info.ebulk = ebulk;
-                if (!mbar_wait(&uempty[eb], ((i >> 1) & 1) ^ 1, p.err)) break;
+                info.j0 = j0;
+                info.nbs = nbs;
+                info.npieces = npieces;
+                info.cfirst = cfirst;
+                info.pslot = 2 * (int)blockIdx.x + ((int)blockIdx.x == cfirst ? 1 : 0);
+                info.tickets = npieces > 1 ? p.tickets + (size_t)(r.tile_begin + tile) * kTcTicketsPerTile : nullptr;
+                if (!mbar_wait(&uempty[eb], ((i >> 1) & 1) ^ 1, p.err)) {
+                    bad = true;
+                    return;
+                }
                 uring[eb] = info;   // published by the arrive below (release)
                 if (ebulk) {
                     mbar_arrive_expect_tx(&ufull[eb], ebytes);
@@ -376,26 +395,70 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
                 } else {
                     mbar_arrive_expect_tx(&ufull[eb], 0);
                 }
-                for (int st = 0; st < nst; st++, gs++) {
+                i++;
+                for (int sg = st0; sg < st1; sg++, gs++) {   // sg: stage index along the tile's K
                     const int s = gs % C::kStages;
                     if (!mbar_wait(&empty[s], ((gs / C::kStages) & 1) ^ 1, p.err)) {
                         bad = true;
-                        break;
+                        return;
                     }
                     unsigned char* sm = stages + (size_t)s * C::kStageBytes;
                     mbar_arrive_expect_tx(&full[s], C::kTxBytes);
 #pragma unroll
                     for (int bx = 0; bx < C::kBoxes; bx++) {
-                        const int x = st * C::kStageK + bx * kBoxK;
+                        const int x = sg * C::kStageK + bx * kBoxK;
                         tma_load_2d(sm + bx * (kTileRows * kBoxK), &d->tm_w, x, rt * kTileRows, &full[s]);
                         tma_load_3d(sm + C::kWBytes + bx * (2 * N * kBoxK), &d->tm_x, x, nt * N, 0, &full[s]);
                     }
-                    tma_load_2d(sxs + (size_t)s * C::kSBytes, &d->tm_s, nt * N, st * C::kBPS, &full[s]);
+                    tma_load_2d(sxs + (size_t)s * C::kSBytes, &d->tm_s, nt * N, sg * C::kBPS, &full[s]);
+                }
+            };
+            if (p.partial) {
+                // stream-K: this CTA's share [sa, sb) of the launch's stages
+                const long long S = p.total_stages, G = gridDim.x;
+                const long long sa = S * blockIdx.x / G, sb = S * (blockIdx.x + 1) / G;
+                auto cta_of = [&](long long x) -> int {   // the CTA whose share holds stage x
+                    long long c = x * G / S;
+                    while (c + 1 < G && S * (c + 1) / G <= x) c++;
+                    while (c > 0 && S * c / G > x) c--;
+                    return (int)c;
+                };
+                long long pos = sa;
+                while (pos < sb && !bad) {
+                    di = desc_index(tab, n, (int)pos, di);
+                    const DescRow& r = tab[di];
+                    const int nstt = (r.nb + C::kBPS - 1) / C::kBPS;
+                    const int local = (int)(pos - r.unit_begin), tile = local / nstt, st0 = local - tile * nstt;
+                    const int st1 = (int)min((long long)nstt, (long long)st0 + (sb - pos));
+                    const long long tb = (long long)r.unit_begin + (long long)tile * nstt;
+                    const int cf = cta_of(tb), cl = cta_of(tb + nstt - 1);
+                    unit(tile, st0, st1, cl - cf + 1, cf);
+                    pos += st1 - st0;
+                }
+            } else {
+                for (int u = blockIdx.x; u < p.total_units && !bad; u += gridDim.x) {
+                    di = desc_index(tab, n, u, di);
+                    const DescRow& r = tab[di];
+                    if (u + (int)gridDim.x < p.total_units) {   // warm the TMA maps of this CTA's next unit
+                        const int dj = desc_index(tab, n, u + gridDim.x, di);
+                        const TcDesc* dn = p.descs ? p.descs + dj : &p.one;
+                        tma_prefetch_desc(&dn->tm_w);
+                        tma_prefetch_desc(&dn->tm_x);
+                        tma_prefetch_desc(&dn->tm_s);
+                    }
+                    unit(u - r.unit_begin, 0, (r.nb + C::kBPS - 1) / C::kBPS, 1, (int)blockIdx.x);
+                }
+            }
+            if (!bad) {   // end of the sequence: an entry with no blocks
+                const int eb = i & 1;
+                if (mbar_wait(&uempty[eb], ((i >> 1) & 1) ^ 1, p.err)) {
+                    uring[eb].nbs = 0;
+                    mbar_arrive_expect_tx(&ufull[eb], 0);
                 }
             }
             // the last loads of every slot have landed unless a consumer quit early
-            for (uint32_t i = gs > (uint32_t)C::kStages ? gs - C::kStages : 0; i < gs; i++)
-                mbar_wait(&full[i % C::kStages], (i / C::kStages) & 1, nullptr);
+            for (uint32_t k = gs > (uint32_t)C::kStages ? gs - C::kStages : 0; k < gs; k++)
+                mbar_wait(&full[k % C::kStages], (k / C::kStages) & 1, nullptr);
         }
     } else if (warp == 1) {
         // ---------------------------------------------------- MMA issuer
@@ -404,9 +467,10 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
             constexpr int G = C::kGroup;
             uint32_t gs = 0, gb = 0, gg = 0;
             bool bad = false;
-            for (int u = blockIdx.x, i = 0; u < p.total_units && !bad; u += gridDim.x, i++) {
+            for (int i = 0; !bad; i++) {
                 if (!mbar_wait(&ufull[i & 1], (i >> 1) & 1, p.err)) break;
-                const int nb = uring[i & 1].nb, nst = (nb + C::kBPS - 1) / C::kBPS;
+                const int nb = uring[i & 1].nbs, nst = (nb + C::kBPS - 1) / C::kBPS;   // this unit's blocks
+                if (nb == 0) break;   // end of the sequence
                 for (int st = 0; st < nst && !bad; st++, gs++) {
                     const int s = gs % C::kStages;
                     if (!mbar_wait(&full[s], (gs / C::kStages) & 1, p.err)) {
@@ -451,14 +515,15 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
         uint32_t gs = 0, gb = 0, gg = 0;
         bool bad = false;
         const float2 neg_magic = make_float2(-kMagicSum, -kMagicSum);
-        for (int u = blockIdx.x, i = 0; u < p.total_units && !bad; u += gridDim.x, i++) {
+        for (int i = 0; !bad; i++) {
             const int eb = i & 1;
             if (!warp_wait(&ufull[eb], (i >> 1) & 1, p.err)) break;
+            if (uring[eb].nbs == 0) break;   // end of the sequence
             const UnitInfo info = uring[eb];
-            const int M = info.M, nb = info.nb, B = info.B, nt = info.nt;
+            const int M = info.M, nb = info.nbs, B = info.B, nt = info.nt;   // nb: this unit's blocks
             const int r = q * 32 + lane, m = info.rt * kTileRows + r;
             const bool row_ok = m < M;
-            const uint8_t* erow = info.exps + (size_t)(row_ok ? r : 0) * nb;
+            const uint8_t* erow = info.exps + (size_t)(row_ok ? r : 0) * info.nb + info.j0;
             const int col0 = chalf * C::kCols;
             float2 acc[C::kCols / 2];
 #pragma unroll
@@ -483,7 +548,7 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
                         for (int w = 0; w < 2; w++) {
                             const int D = (int)(hv[k + w] - kMagicHi) * 256 + (int)(lv[k + w] - kMagicLo);
                             const int b = nt * N + col0 + c + k + w;
-                            if (row_ok && b < B) info.dots[((size_t)b * M + m) * nb + j] = D;
+                            if (row_ok && b < B) info.dots[((size_t)b * M + m) * info.nb + info.j0 + j] = D;
                         }
                     }
                 }
@@ -579,13 +644,54 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
                 gb += ng;
             }
             gs += (nb + C::kBPS - 1) / C::kBPS;
-            // output stride and peer list, read from the ring entry after the
-            // block loop (not held in registers through it)
+            // output stride, peer list and K split, read from the ring entry
+            // after the block loop (not held in registers through it)
             const int ldy = uring[eb].ldy;
             const PeerOut* peer = uring[eb].peer;
+            const int npieces = uring[eb].npieces, cfirst = uring[eb].cfirst, pslot = uring[eb].pslot;
+            unsigned int* tick = uring[eb].tickets;
             __syncwarp();
             if (lane == 0) mbar_arrive(&uempty[eb]);   // unit entry and exponent tile consumed
             if (bad) break;
+            if (npieces > 1) {
+                // a tile cut between CTAs: publish this piece's sums ([slot][b][row]);
+                // the warp that completes the tile's column slice adds the
+                // pieces in K order (CTA order)
+                const int b0 = nt * N + col0;
+                if (row_ok) {
+                    float* dst = p.partial + ((size_t)pslot * B + b0) * kTileRows + r;
+#pragma unroll
+                    for (int k = 0; k < C::kCols; k += 2) {
+                        if (b0 + k < B) dst[(size_t)k * kTileRows] = acc[k / 2].x;
+                        if (b0 + k + 1 < B) dst[(size_t)(k + 1) * kTileRows] = acc[k / 2].y;
+                    }
+                }
+                __threadfence();
+                __syncwarp();
+                unsigned int t = 0;
+                if (lane == 0) t = atomicAdd(tick + (warp - 2), 1u);
+                t = __shfl_sync(0xffffffffu, t, 0);
+                if (t != (unsigned int)npieces - 1u) continue;
+                __threadfence();
+                if (row_ok) {
+#pragma unroll
+                    for (int k = 0; k < C::kCols; k += 2) {
+                        float2 sum = make_float2(0.0f, 0.0f);
+                        for (int c2 = 0; c2 < npieces; c2++) {
+                            const int slot = 2 * (cfirst + c2) + (c2 == 0 ? 1 : 0);
+                            float2 v = acc[k / 2];
+                            if (slot != pslot) {
+                                const float* src = p.partial + ((size_t)slot * B + b0 + k) * kTileRows + r;
+                                v.x = b0 + k < B ? __ldcg(src) : 0.0f;
+                                v.y = b0 + k + 1 < B ? __ldcg(src + kTileRows) : 0.0f;
+                            }
+                            sum = c2 == 0 ? v : __fadd2_rn(sum, v);
+                        }
+                        acc[k / 2] = sum;
+                    }
+                }
+                if (lane == 0) tick[warp - 2] = 0u;   // the next launch is stream-ordered after this one
+            }
             if (row_ok) {
                 // destination 0: this GPU's output; then every other rank's
                 // copy of the full output (row-sharded plans)
@@ -652,7 +758,7 @@ __global__ void __launch_bounds__(256) quant_planes_kernel(const float* x, int B
 
 template <int N, bool DOTS>
 cudaError_t launch_n(const TcDesc* dev_descs, const TcDesc* one, int n, int total_units, unsigned int* err,
-                     cudaStream_t stream, const SyncArgs* sync) {
+                     cudaStream_t stream, const SyncArgs* sync, const TcStreamK* sk) {
     using C = TcCfg<N>;
     static_assert(C::kSmem <= 232448, "shared memory plan exceeds 227 KB");
     static unsigned long long attr_set = 0;   // one bit per device
@@ -672,7 +778,13 @@ cudaError_t launch_n(const TcDesc* dev_descs, const TcDesc* one, int n, int tota
     p.err = err;
     if (sync) p.sync = *sync;
     if (one) p.one = *one;
-    const int grid = std::max(1, std::min(total_units, num_sms()));
+    int grid = std::max(1, std::min(total_units, num_sms()));
+    if (sk) {
+        p.partial = sk->partial;
+        p.tickets = sk->tickets;
+        p.total_stages = sk->total_stages;
+        grid = tc_streamk_grid(sk->total_stages);
+    }
     gemm_tc_kernel<N, DOTS><<<grid, C::kThreads, C::kSmem, stream>>>(p);
     return cudaGetLastError();
 }
@@ -736,25 +848,35 @@ bool tc_make_desc(TcDesc* d, float* y, const void* planes, const float* xs_t, in
 
 int tc_units(const TcDesc& d) { return ((d.M + kTileRows - 1) / kTileRows) * d.n_nt; }
 
+int tc_stages(const TcDesc& d) {
+    const int bps = tc_blocks_per_stage(tc_tile_n(d.B));
+    return tc_units(d) * ((d.nb + bps - 1) / bps);
+}
+
+int tc_streamk_grid(int total_stages) { return std::max(1, std::min(total_stages, num_sms())); }
+
+bool tc_prefer_streamk(int tiles) { return tiles < 8 * num_sms(); }
+
 template <bool DOTS>
 static cudaError_t launch_b(const TcDesc* dev_descs, const TcDesc* one, int n, int total_units, int B, unsigned int* err,
-                     cudaStream_t stream, const SyncArgs* sync) {
+                     cudaStream_t stream, const SyncArgs* sync, const TcStreamK* sk) {
     switch (tc_tile_n(B)) {
-        case 8: return launch_n<8, DOTS>(dev_descs, one, n, total_units, err, stream, sync);
-        case 16: return launch_n<16, DOTS>(dev_descs, one, n, total_units, err, stream, sync);
-        case 32: return launch_n<32, DOTS>(dev_descs, one, n, total_units, err, stream, sync);
-        case 64: return launch_n<64, DOTS>(dev_descs, one, n, total_units, err, stream, sync);
-        default: return launch_n<128, DOTS>(dev_descs, one, n, total_units, err, stream, sync);
+        case 8: return launch_n<8, DOTS>(dev_descs, one, n, total_units, err, stream, sync, sk);
+        case 16: return launch_n<16, DOTS>(dev_descs, one, n, total_units, err, stream, sync, sk);
+        case 32: return launch_n<32, DOTS>(dev_descs, one, n, total_units, err, stream, sync, sk);
+        case 64: return launch_n<64, DOTS>(dev_descs, one, n, total_units, err, stream, sync, sk);
+        default: return launch_n<128, DOTS>(dev_descs, one, n, total_units, err, stream, sync, sk);
     }
 }
 
 cudaError_t launch_gemm_tc(const TcDesc* dev_descs, const TcDesc* one, int n, int total_units, int B, bool dots,
-                           unsigned int* err, cudaStream_t stream, const SyncArgs* sync) {
+                           unsigned int* err, cudaStream_t stream, const SyncArgs* sync, const TcStreamK* sk) {
     if (sync && !sync_args_ok(*sync)) return cudaErrorInvalidValue;
     if (total_units <= 0) return cudaSuccess;
     if (n < 1 || n > kTcMaxDescs || (!dev_descs && !one)) return cudaErrorInvalidValue;
-    return dots ? launch_b<true>(dev_descs, one, n, total_units, B, err, stream, sync)
-                : launch_b<false>(dev_descs, one, n, total_units, B, err, stream, sync);
+    if (sk && (!sk->partial || !sk->tickets || sk->total_stages <= 0)) return cudaErrorInvalidValue;
+    return dots ? launch_b<true>(dev_descs, one, n, total_units, B, err, stream, sync, sk)
+                : launch_b<false>(dev_descs, one, n, total_units, B, err, stream, sync, sk);
 }
 
 cudaError_t launch_quant_planes(const float* x, int B, int K, void* planes, float* xs_t, int ldxs,

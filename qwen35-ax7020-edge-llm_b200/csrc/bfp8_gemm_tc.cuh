@@ -34,10 +34,10 @@ struct alignas(128) TcDesc {
     float* y;               // [B][ldy]: row b of the output at y + b * ldy
     int32_t* dots;          // optional [B][M][nb]: exact block dots (verification)
     int M, K, B, nb;
-    int unit_begin;         // first unit (row tile x column tile) of this GEMM
+    int unit_begin;         // first unit (row tile x column tile) of this GEMM; stream-K: first stage
     int n_nt;               // column tiles per row tile
     int ldy;                // output row stride (>= M)
-    int pad_;
+    int tile_begin;         // stream-K launches: index of this GEMM's first tile among the launch's tiles
     const PeerOut* peer;    // optional (device memory): row-sharded GEMMs also store into every rank's output
 };
 
@@ -49,8 +49,27 @@ int tc_tile_n(int B);
 bool tc_make_desc(TcDesc* d, float* y, const void* planes, const float* xs_t, int ldxs, const int8_t* mant,
                   const uint8_t* exps, int M, int K, int B, int32_t* dots, int ldy = 0);   // ldy 0: M
 
-// Units (tiles) of one descriptor after tc_make_desc.
+// Units (tiles: row tile x column tile) of one descriptor after tc_make_desc.
 int tc_units(const TcDesc& d);
+
+// Stream-K launches: every CTA takes an equal, contiguous share of the
+// launch's K stages (tile after tile, each tile's stages in K order), so the
+// work is balanced whatever the tile count.  A tile cut between CTAs is
+// finished by the last of its pieces to complete, which adds the pieces'
+// partial sums in K order.
+constexpr int kTcTicketsPerTile = 16;   // one counter per epilogue warp of a tile
+constexpr int kTcTileRowsPublic = 128;  // weight rows per tile (a partial slot holds B x 128 fp32)
+int tc_stages(const TcDesc& d);          // K stages of one descriptor: tiles x ceil(nb / blocks per stage)
+int tc_streamk_grid(int total_stages);   // CTAs of a stream-K launch
+// Stream-K pays off when a launch has too few tiles to spread evenly over the
+// SMs (whole-tile units, CTA c taking units c, c + G, ..., keep the tiles of
+// neighbouring CTAs adjacent, which the L2 rewards when there are plenty).
+bool tc_prefer_streamk(int tiles);
+struct TcStreamK {
+    float* partial;          // 2 x grid slots of B x 128 fp32 (pieces cut at CTA boundaries)
+    unsigned int* tickets;   // kTcTicketsPerTile zeroed counters per tile of the launch (left zero)
+    int total_stages;        // sum of tc_stages over the launch's descriptors (their unit_begin = first stage)
+};
 
 // GEMMs one launch takes (a grouped plan of more is split into launches).
 constexpr int kTcMaxDescs = 160;
@@ -61,7 +80,8 @@ constexpr int kTcMaxDescs = 160;
 // `sync` (row-sharded plans): the last CTA publishes sig_epoch (its wait
 // fields are unused: the quantizer that feeds the launch waits).
 cudaError_t launch_gemm_tc(const TcDesc* dev_descs, const TcDesc* one, int n, int total_units, int B, bool dots,
-                           unsigned int* err, cudaStream_t stream, const SyncArgs* sync = nullptr);
+                           unsigned int* err, cudaStream_t stream, const SyncArgs* sync = nullptr,
+                           const TcStreamK* sk = nullptr);
 
 // fp32 [B][K] -> planes [2][B][K] + xs_t [K/64][ldxs],
 // the reference quantizer's arithmetic (bit-exact xq and scales).  With

@@ -171,11 +171,14 @@ std::vector<StackPlan> g_plans;
 // GEMMs each (deepest first), their descriptors in one device array.
 struct TcLaunchPart {
     int first, n, total_units;
+    int total_stages;   // stream-K launches (0: whole-tile units): unit_begin of their descriptors = first stage
 };
 struct TcPlan {
     qb::TcDesc* dev_descs = nullptr;
     std::vector<TcLaunchPart> parts;
     int B = 0;
+    float* partial = nullptr;           // stream-K piece sums (2 slots per CTA)
+    unsigned int* sk_tickets = nullptr; // stream-K counters (kTcTicketsPerTile per tile, left zero)
     qb::PeerOut* peers = nullptr;         // row-sharded plans: where each GEMM's rows also go
     unsigned int* sig_ticket = nullptr;   // row-sharded plans: grid ticket of the completion signal
     bool live = false;
@@ -847,15 +850,38 @@ int tc_stack_create_impl(int n, const int8_t* const* mant, const uint8_t* const*
         return fail(QB_ECUDA, "tc_stack peer upload");
     // deepest matrices first, so the round-robin tail is made of short units
     std::stable_sort(v.begin(), v.end(), [](const qb::TcDesc& a, const qb::TcDesc& b) { return a.K > b.K; });
+    // stream-K launches: every CTA an equal share of the K stages
+    int max_tiles = 0, max_grid = 0;
     for (int first = 0; first < (int)v.size(); first += qb::kTcMaxDescs) {
-        TcLaunchPart part{first, std::min(qb::kTcMaxDescs, (int)v.size() - first), 0};
+        TcLaunchPart part{first, std::min(qb::kTcMaxDescs, (int)v.size() - first), 0, 0};
+        long long stages = 0;
         for (int k = first; k < first + part.n; k++) {
             v[k].unit_begin = part.total_units;
+            v[k].tile_begin = part.total_units;
+            stages += qb::tc_stages(v[k]);
             part.total_units += qb::tc_units(v[k]);
+        }
+        if (stages > (1ll << 30)) return fail(QB_EINVAL, "tc_stack: too much work for one launch");
+        if (qb::tc_prefer_streamk(part.total_units)) {
+            long long st = 0;
+            for (int k = first; k < first + part.n; k++) {
+                v[k].unit_begin = (int)st;
+                st += qb::tc_stages(v[k]);
+            }
+            part.total_stages = (int)stages;
+            max_tiles = std::max(max_tiles, part.total_units);
+            max_grid = std::max(max_grid, qb::tc_streamk_grid(part.total_stages));
         }
         tp.parts.push_back(part);
     }
     tp.B = B;
+    if (max_grid > 0) {
+        cudaError_t e2 = cudaMalloc(&tp.partial, (size_t)2 * max_grid * B * qb::kTcTileRowsPublic * sizeof(float));
+        if (e2 != cudaSuccess) return fail(QB_ENOMEM, "tc_stack partial alloc", e2);
+        const size_t tb = (size_t)max_tiles * qb::kTcTicketsPerTile * sizeof(unsigned int);
+        if ((e2 = cudaMalloc(&tp.sk_tickets, tb)) != cudaSuccess) return fail(QB_ENOMEM, "tc_stack ticket alloc", e2);
+        if ((e2 = cudaMemset(tp.sk_tickets, 0, tb)) != cudaSuccess) return fail(QB_ECUDA, "tc_stack ticket clear", e2);
+    }
     cudaError_t e = cudaMalloc(&tp.dev_descs, sizeof(qb::TcDesc) * (v.empty() ? 1 : v.size()));
     if (e != cudaSuccess) return fail(QB_ENOMEM, "tc_stack alloc", e);
     if (!v.empty() &&
@@ -876,8 +902,10 @@ int tc_stack_launch(int plan, void* stream, const qb::SyncArgs* sync) {
         const TcLaunchPart& part = tp.parts[k];
         // the completion signal rides on the last launch (the others finish before it starts)
         const qb::SyncArgs* s = k + 1 == tp.parts.size() ? sync : nullptr;
+        const qb::TcStreamK sk{tp.partial, tp.sk_tickets, part.total_stages};
         cudaError_t e = qb::launch_gemm_tc(tp.dev_descs + part.first, nullptr, part.n, part.total_units, tp.B, false,
-                                           st->err, static_cast<cudaStream_t>(stream), s);
+                                           st->err, static_cast<cudaStream_t>(stream), s,
+                                           part.total_stages ? &sk : nullptr);
         if (e != cudaSuccess) return fail(QB_ECUDA, "qwen_b200_tc_stack_run", e);
     }
     return QB_OK;
@@ -948,6 +976,10 @@ int qwen_b200_tc_stack_destroy(int plan) {
     cudaFree(g_tc_plans[plan - 1].dev_descs);
     cudaFree(g_tc_plans[plan - 1].peers);
     cudaFree(g_tc_plans[plan - 1].sig_ticket);
+    cudaFree(g_tc_plans[plan - 1].partial);
+    cudaFree(g_tc_plans[plan - 1].sk_tickets);
+    g_tc_plans[plan - 1].partial = nullptr;
+    g_tc_plans[plan - 1].sk_tickets = nullptr;
     g_tc_plans[plan - 1].dev_descs = nullptr;
     g_tc_plans[plan - 1].peers = nullptr;
     g_tc_plans[plan - 1].sig_ticket = nullptr;

@@ -1,6 +1,9 @@
-"""Row-sharded stack on two GPUs: every gathered output equals the single-GPU
-run bit for bit, with the NCCL all-gather and with the in-kernel peer stores
-(exchange="peer"); the fast arithmetic gives the same bits both ways.  The
+"""Row-sharded stack on two GPUs: at batch 1 every gathered output equals the
+single-GPU run bit for bit, with the NCCL all-gather and with the in-kernel
+peer stores (exchange="peer"); the fast arithmetic gives the same bits both
+ways.  At batch 64 (tcgen05, stream-K: where a tile is cut between CTAs
+depends on the total work, so the fp32 sums group differently) both exchanges
+give the same bits and agree with one GPU to 1e-4 of the output scale.  The
 two-GPU cases are skipped with fewer GPUs; the bounded flag wait runs on one."""
 import os
 import socket
@@ -93,7 +96,9 @@ def test_two_gpu_sharded_stack_matches_single_gpu(cuda, tmp_path):
             got = np.load(path + f".{exchange}.1.{r}.npy")
             assert np.array_equal(got.view(np.uint32), fast_ref.view(np.uint32)), (exchange, r)
             got = np.load(path + f".{exchange}.b.{r}.npy")
-            assert np.array_equal(got.view(np.uint32), ref_b.view(np.uint32)), (exchange, "batched", r)
+            assert np.array_equal(got.view(np.uint32), np.load(path + ".nccl.b.0.npy").view(np.uint32)), \
+                (exchange, "batched", r)
+            assert np.max(np.abs(got - ref_b)) <= 1e-4 * np.max(np.abs(ref_b)), (exchange, "batched", r)
     np.testing.assert_allclose(fast_ref, ref, rtol=1e-4, atol=1e-4)
 
 
@@ -118,10 +123,10 @@ def test_peer_mode_single_rank_matches_plain(cuda):
 
 
 def test_batched_single_rank_chains_layers(cuda):
-    """batch > 1 on one rank: every layer's outputs equal the tcgen05 GEMM of
-    the previous output, computed GEMM by GEMM through ops (same kernels,
-    checks the layer chaining and the strided outputs); exchange="peer" on
-    one rank gives the same bits."""
+    """batch > 1 on one rank: every layer's outputs match the tcgen05 GEMM of
+    the previous output computed GEMM by GEMM through ops (checks the layer
+    chaining, the strided outputs and the stream-K piece sums: the same exact
+    block dots, fp32 sums grouped differently), for both exchanges."""
     import torch
 
     from qwen_b200 import ops, sharded
@@ -136,7 +141,8 @@ def test_batched_single_rank_chains_layers(cuda):
                 xin = xin if xin is not None else st.full[L.gate.name]
                 mant, exps = st.weight(0, t)
                 y = ops.bfp8_gemm_tc(ops.quant_planes(xin.contiguous()), mant, exps)
-                assert torch.equal(y.view(torch.int32), st.full[t.name].view(torch.int32)), (exchange, t.name)
+                err = (y - st.full[t.name]).abs().max().item()
+                assert err <= 1e-5 * y.abs().max().item(), (exchange, t.name, err)
             x = st.full[L.down.name]
         st.close()
 
