@@ -102,17 +102,11 @@ struct TcCfg {
     static constexpr int kThreads = 64 + 32 * kEpiWarps;
     static constexpr int kCols = N / kColSplit;                      // columns per epilogue thread
     // Small tiles: the epilogue takes kGroup blocks per round (one barrier
-    // wait, one TMEM load wait and one store wait for all of them).  Large
+    // wait and one TMEM load wait for all of them).  Large
     // tiles: one block per round, its columns in kChunk pieces whose TMEM
     // loads overlap the previous piece's arithmetic.
     static constexpr int kGroup = N <= 16 ? 4 : (N <= 32 ? 2 : 1);
     static constexpr int kChunk = kGroup > 1 ? kCols : 8;
-    static constexpr int kPreset = kCols < 16 ? kCols : 16;
-    // true: the epilogue re-arms each drained slot with the bias patterns
-    // (tcgen05.st) and every MMA step accumulates; false: a block's first MMA
-    // step overwrites the slot and the epilogue adds the bias patterns to the
-    // loaded integers (two integer adds per dot, no TMEM stores).
-    static constexpr bool kPresets = false;
     static constexpr int kGroupsInFlight = kSlots / kGroup;
     // blocks whose TMEM slots the MMA thread claims with one wait (whole
     // epilogue groups, at most half of the slots)
@@ -212,33 +206,6 @@ __device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, uint32_t (&v)[32]) {
         : "r"(taddr));
 }
 
-// Store one 32-bit value into C consecutive columns of the warp's 32 lanes.
-template <int C>
-__device__ __forceinline__ void tmem_st_rep(uint32_t taddr, uint32_t v);
-template <>
-__device__ __forceinline__ void tmem_st_rep<4>(uint32_t taddr, uint32_t v) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %1, %1, %1};" ::"r"(taddr), "r"(v) : "memory");
-}
-template <>
-__device__ __forceinline__ void tmem_st_rep<8>(uint32_t taddr, uint32_t v) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
-                 "r"(v)
-                 : "memory");
-}
-template <>
-__device__ __forceinline__ void tmem_st_rep<16>(uint32_t taddr, uint32_t v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
-        "%1};" ::"r"(taddr),
-        "r"(v)
-        : "memory");
-}
-template <>
-__device__ __forceinline__ void tmem_st_rep<32>(uint32_t taddr, uint32_t v) {
-    tmem_st_rep<16>(taddr, v);
-    tmem_st_rep<16>(taddr + 16, v);
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // tcgen05.wait::ld, then tie the loaded registers to it so that no use of
 // them can be scheduled before the wait.
@@ -326,17 +293,6 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
     const uint32_t tmem = *tmem_slot;
     const int q = warp & 3, chalf = (warp - 2) >> 2;   // TMEM lane quarter, column slice
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    if (C::kPresets && warp >= 2) {   // preset every accumulator slot before the first MMA
-        for (int t = 0; t < C::kSlots; t++) {
-            const uint32_t tcol = tmem + lane_base + (uint32_t)(t * 2 * N + chalf * C::kCols);
-#pragma unroll
-            for (int c = 0; c < C::kCols; c += C::kPreset) {
-                tmem_st_rep<C::kPreset>(tcol + c, kMagicHi);
-                tmem_st_rep<C::kPreset>(tcol + N + c, kMagicLo);
-            }
-        }
-        tmem_wait_st();
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -496,7 +452,7 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
                         for (int kk = 0; kk < 2; kk++) {
                             const uint64_t off = (uint64_t)(((h & 1) * 64 + kk * 32) >> 4);
                             mma_i8(tmem + (uint32_t)(t * 2 * N), da + off, dx + off, kId,
-                                   C::kPresets ? 1u : (uint32_t)kk);
+                                   (uint32_t)kk);   // a block's first step overwrites its slot
                         }
                         if (j % G == G - 1 || j == nb - 1) {   // a group of blocks is complete
                             mma_commit(&tfull[gg % C::kGroupsInFlight]);
@@ -588,17 +544,8 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
 #pragma unroll
                         for (int k = 0; k < C::kCols; k++) {
                             asm volatile("" : "+r"(hv[g][k]), "+r"(lv[g][k]));
-                            if constexpr (!C::kPresets) {
-                                hv[g][k] += kMagicHi;
-                                lv[g][k] += kMagicLo;
-                            }
-                        }
-#pragma unroll
-                    for (int g = 0; g < G; g++)
-                        if (C::kPresets && g < ng) {   // preset the slots for their next blocks
-                            const uint32_t tcol = tmem + lane_base + (uint32_t)(((gb + g) % C::kSlots) * 2 * N + col0);
-                            tmem_st_rep<C::kCols>(tcol, kMagicHi);
-                            tmem_st_rep<C::kCols>(tcol + N, kMagicLo);
+                            hv[g][k] += kMagicHi;   // bias patterns: exact int -> float (see accumulate)
+                            lv[g][k] += kMagicLo;
                         }
 #pragma unroll
                     for (int g = 0; g < G; g++)
@@ -606,7 +553,6 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
                             accumulate(hv[g], lv[g], 0, C::kCols, j0 + g, ev[g]);
                             release_stage(j0 + g);
                         }
-                    if constexpr (C::kPresets) tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0)
@@ -619,15 +565,10 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
 #pragma unroll
                     for (int c = 0, ci = 0; c < C::kCols; c += C::kChunk, ci++) {
                         tmem_wait_ld_dep<C::kChunk>(hv[ci & 1], lv[ci & 1]);
-                        if constexpr (C::kPresets) {   // preset for the slot's next block
-                            tmem_st_rep<C::kChunk>(tcol + c, kMagicHi);
-                            tmem_st_rep<C::kChunk>(tcol + N + c, kMagicLo);
-                        } else {
 #pragma unroll
-                            for (int k = 0; k < C::kChunk; k++) {
-                                hv[ci & 1][k] += kMagicHi;
-                                lv[ci & 1][k] += kMagicLo;
-                            }
+                        for (int k = 0; k < C::kChunk; k++) {   // bias patterns
+                            hv[ci & 1][k] += kMagicHi;
+                            lv[ci & 1][k] += kMagicLo;
                         }
                         if (c + C::kChunk < C::kCols) {   // next piece loads while this one is summed
                             tmem_ld<C::kChunk>(tcol + c + C::kChunk, hv[(ci + 1) & 1]);
@@ -635,7 +576,6 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
                         }
                         accumulate(hv[ci & 1], lv[ci & 1], c, C::kChunk, j0, ev[0]);
                     }
-                    if constexpr (C::kPresets) tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tempty[gb % C::kSlots]);
