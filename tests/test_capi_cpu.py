@@ -112,3 +112,29 @@ def test_invalid_arguments_are_rejected_without_a_device():
     assert lib.qwen_b200_gemv_dev(None, None, None, None, 4, 64, None) == -1
     assert lib.qwen_b200_stack_run(12345, None) == -1
     assert b"bad handle" in lib.qwen_b200_last_error()
+
+
+def test_sharded_entry_points_reject_bad_arguments_without_a_gpu():
+    """The row-sharded and IPC entry points validate before touching a device:
+    unknown plans, world sizes outside 1..8, missing flag arrays and null
+    buffers return QB_EINVAL (-1) with a message."""
+    from qwen_b200 import _lib
+
+    lib = _lib.load()
+    flags = (ctypes.c_void_p * 8)()
+    assert lib.qwen_b200_stack_run_sync(0, None, None, 0, flags, 0, 1, 0) == -1
+    assert lib.qwen_b200_stack_run_sync(12345, None, None, 0, flags, 0, 1, 0) == -1
+    assert lib.qwen_b200_tc_stack_run_sync(0, None, flags, 1, 2, 0) == -1
+    assert lib.qwen_b200_quant_planes_wait_dev(None, 1, 64, None, None, 4, None, 0, 1, None) == -1
+    assert lib.qwen_b200_quant_planes_wait_dev(None, 1, 64, None, None, 4, None, 1, 9, None) == -1
+    out = ctypes.c_void_p()
+    assert lib.qwen_b200_dev_alloc(0, ctypes.byref(out)) == -1
+    assert lib.qwen_b200_ipc_handle(None, None) == -1
+    assert lib.qwen_b200_ipc_open(None, ctypes.byref(out)) == -1
+    assert b"bad" in lib.qwen_b200_last_error() or b"qwen_b200" in lib.qwen_b200_last_error()
+    one = (ctypes.c_void_p * 1)()
+    ints = (ctypes.c_int * 1)(64)
+    # world 9 is out of range
+    assert lib.qwen_b200_stack_create_sharded(1, one, one, one, one, ints, ints, 0, 9, one, ints) == -1
+    assert lib.qwen_b200_tc_stack_create_sharded(1, one, one, one, one, one, ints, ints, None, 8, 8, 1, None,
+                                                 ints) == -1
