@@ -258,11 +258,10 @@ __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int ca
     if (s_ticket != gridDim.x - 1) return;
     __threadfence();
 
-    // ---- last CTA: final results
-    if (tid == 0) {
-        unsigned long long k = *((volatile unsigned long long*)&sc->argmax_key);
-        *out_id = k ? key_id(k) : 0;
-    }
+    // ---- last CTA: final results.  The argmax word is loaded now and stored
+    // at the end, so its round trip overlaps the top-k work.
+    unsigned long long amax = 0ull;
+    if (tid == 0) amax = *((volatile unsigned long long*)&sc->argmax_key);
     constexpr int kPre = 8;   // keys per list read by the fast path
     if (kk > 0 && (long long)gridDim.x * (kPre + 2) <= work_cap && (int)gridDim.x <= cand_cap) {
         // Fast path: one round of independent L2 loads brings every list's
@@ -283,6 +282,9 @@ __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int ca
             s_t2 = 0ull;
         }
         const int total_ent = G * E;
+        // the counts ride in the same round of loads as the list entries
+        int cnt = 0;
+        if (tid < G) cnt = __ldcg(sc->counts + tid);
         for (int base = tid; base < total_ent; base += 8 * blockDim.x) {
             unsigned long long v[8];
 #pragma unroll
@@ -301,7 +303,8 @@ __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int ca
                 if (idx < total_ent) work[idx] = v[u];
             }
         }
-        for (int c = tid; c < G; c += blockDim.x) s_counts[c] = __ldcg(sc->counts + c);
+        if (tid < G) s_counts[tid] = cnt;
+        for (int c = tid + blockDim.x; c < G; c += blockDim.x) s_counts[c] = __ldcg(sc->counts + c);
         __syncthreads();
         for (int idx = tid; idx < total_ent; idx += blockDim.x) {   // drop entries past each list's count
             const int c = idx / E, e = idx - c * E;
@@ -483,6 +486,7 @@ __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int ca
         if (tid == 0) *out_n = want;
     }
     if (tid == 0) {
+        *out_id = amax ? key_id(amax) : 0;
         sc->argmax_key = 0ull;
         sc->ticket = 0u;
     }
