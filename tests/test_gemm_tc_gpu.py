@@ -199,3 +199,40 @@ def test_batched_stack_split_over_launches(cuda):
     for (_, _, _, y), ys in zip(items, singles):
         assert np.array_equal(bits(y.cpu().numpy()), bits(ys.cpu().numpy()))
     st.close()
+
+
+@pytest.mark.parametrize("M,K,B", [(256, 16384, 64), (130, 8192, 20), (128, 4096, 3)])
+def test_batched_stack_stream_k_many_pieces(cuda, M, K, B):
+    """A launch with far fewer tiles than SMs and a deep K: stream-K cuts every
+    tile into dozens of pieces (one per CTA share), the last piece of each tile
+    adds the others' sums in K order.  Outputs stay within the rounding bound
+    (one extra rounding per piece, at most one per block), are the same bits on
+    a second run, and the per-tile counters are left at zero (a third run with
+    new activations is checked too)."""
+    import torch
+
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(M + K + B)
+    mant, exps = rand_weights(rng, M, K)
+    dm, de = torch.from_numpy(mant).cuda(), torch.from_numpy(exps).cuda()
+    x = rng.normal(0, 1, (B, K)).astype(np.float32)
+    p = ops.quant_planes(torch.from_numpy(x).cuda())
+    y = torch.full((B, M), float("nan"), device="cuda")
+    st = ops.BatchedStack([(p, dm, de, y)])
+    st.run()
+    torch.cuda.synchronize()
+    y1 = y.cpu().numpy().copy()
+    Rows(x, mant, exps).check(y1, ("stream-K", M, K, B), extra_roundings=K // 64)
+    st.run()
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(y.cpu().numpy()), bits(y1))
+    x2 = rng.normal(0, 1, (B, K)).astype(np.float32)
+    ops.quant_planes(torch.from_numpy(x2).cuda(), out=p)
+    st.run()
+    torch.cuda.synchronize()
+    Rows(x2, mant, exps).check(y.cpu().numpy(), ("stream-K second input", M, K, B), extra_roundings=K // 64)
+    st.close()
+    from qwen_b200 import _lib
+
+    assert _lib.load().qwen_b200_device_error(1) == 0
