@@ -113,24 +113,12 @@ __device__ __forceinline__ void warp_sort64_desc(unsigned long long& a0, unsigne
     // two sorted 32-halves in opposite directions form a bitonic 64-sequence
     warp_merge64_desc(a0, a1);
 }
-// Number of keys greater than `key` in a descending list a[0..64).
-__device__ __forceinline__ int count_greater64(const unsigned long long* a, unsigned long long key) {
-    int lo = 0, hi = 64;
-    while (lo < hi) {
-        const int mid = (lo + hi) >> 1;
-        if (a[mid] > key) lo = mid + 1;
-        else hi = mid;
-    }
-    return lo;
-}
-
-// Fold 64 more keys (c0, c1: element i = r*32 + lane) into a warp's running
-// top-64 (r0, r1), both descending.
-__device__ __forceinline__ void warp_fold64(unsigned long long& r0, unsigned long long& r1, unsigned long long c0,
-                                            unsigned long long c1) {
+// Top 64 of two descending 64-key lists held by a warp (element i = r*32 +
+// lane in register r), into (r0, r1), descending.
+__device__ __forceinline__ void warp_merge_sorted64(unsigned long long& r0, unsigned long long& r1,
+                                                    unsigned long long c0, unsigned long long c1) {
     const int lane = threadIdx.x & 31;
-    warp_sort64_desc(c0, c1);
-    // max(running[i], chunk[63 - i]) holds the top 64 as a bitonic sequence
+    // max(r[i], c[63 - i]) holds the top 64 as a bitonic sequence
     const unsigned long long x0 = __shfl_sync(0xffffffffu, c1, 31 - lane);
     const unsigned long long x1 = __shfl_sync(0xffffffffu, c0, 31 - lane);
     r0 = r0 > x0 ? r0 : x0;
@@ -138,32 +126,41 @@ __device__ __forceinline__ void warp_fold64(unsigned long long& r0, unsigned lon
     warp_merge64_desc(r0, r1);
 }
 
+// Fold 64 more keys (c0, c1: element i = r*32 + lane) into a warp's running
+// top-64 (r0, r1), both descending.
+__device__ __forceinline__ void warp_fold64(unsigned long long& r0, unsigned long long& r1, unsigned long long c0,
+                                            unsigned long long c1) {
+    warp_sort64_desc(c0, c1);
+    warp_merge_sorted64(r0, r1, c0, c1);
+}
+
 // cand[w*64 .. w*64+64) hold every warp's descending top-64 (zero keys
 // empty).  Writes the best `keep` (<= 64) keys of their union, descending,
-// to cand[0..m) and m = min(nonzero keys, keep) to *count.  Needs kCandCap
-// >= 64 * warps + keep.  Called by the whole block.
+// to cand[0..m) and m = min(nonzero keys, keep) to *count.  A merge tree in
+// registers: at level s, warp w (a multiple of 2s) absorbs warp w + s's list
+// with one bitonic merge; log2(warps) levels, one barrier each.  Needs
+// kCandCap >= 64 * warps.  Called by the whole block.
 __device__ inline void merge_warp_lists64(unsigned long long* cand, int* count, int keep) {
-    const int nw = blockDim.x >> 5;
-    unsigned long long* out = cand + 64 * nw;
-    __shared__ int s_nz;
-    if (threadIdx.x == 0) s_nz = 0;
-    __syncthreads();
-    int nz = 0;
-    for (int idx = threadIdx.x; idx < nw * keep; idx += blockDim.x) {
-        const int l = idx / keep, i = idx - l * keep;
-        const unsigned long long key = cand[l * 64 + i];
-        if (key == 0ull) continue;
-        nz++;
-        int rank = i;
-        for (int o = 0; o < nw; o++)
-            if (o != l) rank += count_greater64(cand + o * 64, key);
-        if (rank < keep) out[rank] = key;
+    const int nw = blockDim.x >> 5, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();   // every warp's list is in place
+    unsigned long long r0 = cand[w * 64 + lane], r1 = cand[w * 64 + 32 + lane];
+    for (int step = 1; step < nw; step <<= 1) {
+        // slot w is read at this level only by a warp that does not absorb,
+        // so an absorbing warp may rewrite its own slot at once
+        if ((w & (2 * step - 1)) == 0 && w + step < nw) {
+            warp_merge_sorted64(r0, r1, cand[(w + step) * 64 + lane], cand[(w + step) * 64 + 32 + lane]);
+            cand[w * 64 + lane] = r0;
+            cand[w * 64 + 32 + lane] = r1;
+        }
+        __syncthreads();
     }
-    if (nz) atomicAdd(&s_nz, nz);
-    __syncthreads();
-    const int m = s_nz < keep ? s_nz : keep;
-    for (int i = threadIdx.x; i < m; i += blockDim.x) cand[i] = out[i];
-    if (threadIdx.x == 0) *count = m;
+    if (w == 0) {
+        const int nz = __popc(__ballot_sync(0xffffffffu, r0 != 0ull)) + __popc(__ballot_sync(0xffffffffu, r1 != 0ull));
+        const int m = nz < keep ? nz : keep;
+        if (lane < m) cand[lane] = r0;
+        if (32 + lane < m) cand[32 + lane] = r1;
+        if (lane == 0) *count = m;
+    }
     __syncthreads();
 }
 
