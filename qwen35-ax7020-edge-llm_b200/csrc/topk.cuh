@@ -207,6 +207,7 @@ __device__ inline void rank_place(const unsigned long long* work, int m, int kee
     for (int i = threadIdx.x; i < m; i += blockDim.x) {
         const unsigned long long k = work[i];
         int r = 0;
+#pragma unroll 8
         for (int j = 0; j < m; j++) r += work[j] > k;
         if (r < keep) out[r] = k;
     }
@@ -325,7 +326,8 @@ __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int ca
             const unsigned long long hd = cand[c];
             if (hd == 0ull) continue;
             int r = 0;
-            for (int o = 0; o < G; o++) r += cand[o] > hd;
+#pragma unroll 8
+            for (int o = 0; o < G; o++) r += cand[o] > hd;   // independent loads, 8 in flight
             if (r == kk - 1) s_t2 = hd;
         }
         __syncthreads();
