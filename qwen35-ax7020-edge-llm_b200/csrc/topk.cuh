@@ -261,7 +261,7 @@ __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int ca
     unsigned long long amax = 0ull;
     if (tid == 0) amax = *((volatile unsigned long long*)&sc->argmax_key);
     constexpr int kPre = 8;   // keys per list read by the fast path
-    if (kk > 0 && (long long)gridDim.x * (kPre + 2) <= work_cap && (int)gridDim.x <= cand_cap) {
+    if (kk > 0 && (long long)gridDim.x * (kPre + 2) <= work_cap && (((int)gridDim.x + 7) & ~7) <= cand_cap) {
         // Fast path: one round of independent L2 loads brings every list's
         // count, first kPre keys and kk-th key.  Every key >= T lies in a
         // list prefix unless some list's kPre-th key is itself >= T; only
@@ -322,12 +322,19 @@ __device__ inline void lm_finish(LmScratch* sc, unsigned long long* cand, int ca
         for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
         if (lane == 0) atomicAdd(&s_total2, tot);
         t1 = block_max_u64(t1, red);   // contains barriers (cand heads visible after it)
+        for (int i = G + tid; i < ((G + 7) & ~7); i += blockDim.x) cand[i] = 0ull;   // pad to 8 heads
+        __syncthreads();
         for (int c = tid; c < G; c += blockDim.x) {
             const unsigned long long hd = cand[c];
             if (hd == 0ull) continue;
             int r = 0;
-#pragma unroll 8
-            for (int o = 0; o < G; o++) r += cand[o] > hd;   // independent loads, 8 in flight
+            for (int o0 = 0; o0 < G; o0 += 8) {   // 8 heads per round, loads issued together
+                unsigned long long v[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) v[u] = cand[o0 + u];
+#pragma unroll
+                for (int u = 0; u < 8; u++) r += v[u] > hd;
+            }
             if (r == kk - 1) s_t2 = hd;
         }
         __syncthreads();
