@@ -119,6 +119,16 @@ QB_API void qwen_b200_reset_weights(void);
 QB_API int qwen_b200_gemv_dev(float* y, const float* x, const int8_t* mant, const uint8_t* exps, int M, int K,
                        void* stream);
 
+/* y[M] = exact BFP8 GEMV of rmsnorm(x, norm_w, eps) in one launch: the
+ * reference's rmsnorm (qwen_kernels_opt.c:140-172, NEON build order: four
+ * flushed lane sums of x*x, r = 1/sqrtf(sum/K + eps), x * (r * (1 + w))),
+ * then its quantizer and GEMV, bit for bit -- the rmsnorm -> bfp8_gemv pair
+ * forward_token_c runs before the attention and MLP projections
+ * (qwen_kernels_opt.c:946-1001), without the normalized vector leaving the
+ * SM.  K a multiple of 512 and <= 6144; x and norm_w 8-byte aligned. */
+QB_API int qwen_b200_rmsnorm_gemv_dev(float* y, const float* x, const float* norm_w, float eps, const int8_t* mant,
+                                      const uint8_t* exps, int M, int K, void* stream);
+
 /* Same from an already quantized activation: xq int16 [K], xs fp32 [K/64]. */
 QB_API int qwen_b200_gemv_q_dev(float* y, const int16_t* xq, const float* xs, const int8_t* mant,
                          const uint8_t* exps, int M, int K, void* stream);

@@ -17,6 +17,7 @@
  *     (and its scalar build     :489-505)
  *   - lm_head_topk selection    04-板载脚本与工具/qwen_sampling.c:110-155,160-353
  *   - gemv_core dequant mode    02-RTL与仿真/gemv_core.v:40-69,299-534
+ *   - rmsnorm, NEON and scalar  04-板载脚本与工具/qwen_kernels_opt.c:140-172
  *
  * Floating point model.  The reference board runs the vector parts on ARMv7
  * Advanced SIMD, which always flushes subnormal inputs and results to a zero
@@ -47,6 +48,32 @@ static float bf16_bits_to_f32(uint16_t u) {
     float f;
     memcpy(&f, &w, 4);
     return f;
+}
+
+/* ---------------------------------------------------------------- rmsnorm */
+/* rmsnorm (qwen_kernels_opt.c:140-172), NEON build: four lane sums of x*x
+ * over i = 4j + l (VMLA, not fused, flushed), combined as (s0 + s2) + (s1 + s3);
+ * any n % 4 tail added on VFP; r = 1 / sqrtf(sum / n + eps) on VFP; then
+ * y = x * (r * (1 + w)) on the vector unit (tail: (x * r) * (1 + w) on VFP). */
+ORC_API void orc_rmsnorm_neon(float* y, const float* x, const float* w, int n, float eps) {
+    float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    int i = 0;
+    for (; i + 4 <= n; i += 4)
+        for (int l = 0; l < 4; l++) s4[l] = neon_add(s4[l], neon_mul(x[i + l], x[i + l]));
+    float sum = neon_add(neon_add(s4[0], s4[2]), neon_add(s4[1], s4[3]));
+    for (; i < n; i++) sum += x[i] * x[i];
+    const float r = 1.0f / sqrtf((sum / (float)n) + eps);
+    for (i = 0; i + 4 <= n; i += 4)
+        for (int l = 0; l < 4; l++) y[i + l] = neon_mul(x[i + l], neon_mul(r, neon_add(1.0f, w[i + l])));
+    for (; i < n; i++) y[i] = x[i] * r * (1.0f + w[i]);
+}
+
+/* The same routine's portable build: one running sum, y = (x * r) * (1 + w). */
+ORC_API void orc_rmsnorm_scalar(float* y, const float* x, const float* w, int n, float eps) {
+    float sum = 0.0f;
+    for (int i = 0; i < n; i++) sum += x[i] * x[i];
+    const float r = 1.0f / sqrtf((sum / (float)n) + eps);
+    for (int i = 0; i < n; i++) y[i] = x[i] * r * (1.0f + w[i]);
 }
 
 /* EXP_SCALE[e] = 2^(e-134); subnormal for e < 8 (qwen_kernels_opt.c:131). */

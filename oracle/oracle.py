@@ -60,6 +60,8 @@ def lib():
             "orc_bfp8_lm_head": [_P, _P, _P, _I, _I, _I, _P, _P, _P],
             "orc_xorshift32": [_P, _P, ctypes.c_size_t],
             "orc_selftest_fill": [_P, _P, ctypes.c_size_t, _P, ctypes.c_size_t],
+            "orc_rmsnorm_neon": [_P, _P, _P, _I, ctypes.c_float],
+            "orc_rmsnorm_scalar": [_P, _P, _P, _I, ctypes.c_float],
         }
         for name, args in sigs.items():
             fn = getattr(L, name)
@@ -166,6 +168,17 @@ def bfp8_gemv(x, mant, exps):
     x, px = _c(x, np.float32)
     y = np.zeros(M, np.float32)
     lib().orc_bfp8_gemv_neon(y.ctypes.data, px, pm, pe, M, K)
+    return y
+
+
+def rmsnorm(x, w, eps, neon=True):
+    """rmsnorm (qwen_kernels_opt.c:140-172): the NEON build's order (what the
+    board runs) or the portable build's."""
+    x, px = _c(x, np.float32)
+    w, pw = _c(w, np.float32)
+    y = np.empty_like(x)
+    fn = lib().orc_rmsnorm_neon if neon else lib().orc_rmsnorm_scalar
+    fn(y.ctypes.data, px, pw, x.size, float(eps))
     return y
 
 

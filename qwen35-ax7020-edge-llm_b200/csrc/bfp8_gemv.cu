@@ -162,6 +162,8 @@ struct WArgs {
     int lm_warp_lists;      // top-k in per-warp register lists (k <= 64 and too many rows per CTA to buffer)
     int res_act;            // single GEMV, small K: every CTA quantizes the whole activation into its own
                             // shared memory (no act_prep kernel, no activation copies per stage)
+    const float* norm_w;    // res_act only: x is first rmsnorm-ed with these weights (nullptr: not)
+    float norm_eps;
     SyncArgs sync;          // row-sharded stacks: completion signal (sig_epoch 0: none)
 };
 
@@ -500,12 +502,43 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
         const int nb = D.K >> 6;
         uint32_t* xp = reinterpret_cast<uint32_t*>(xrings);
         float* xsc = reinterpret_cast<float*>(xrings + (size_t)D.K * 2);
+        float nr = 0.0f;   // rmsnorm scale
+        if (A.norm_w) {
+            // rmsnorm, the reference's NEON build (qwen_kernels_opt.c:140-172):
+            // four lane sums of x*x over i = 4j + l (multiply, then add, both
+            // flushed), combined as (s0 + s2) + (s1 + s3); then, in IEEE
+            // single precision, r = 1 / sqrt(sum / K + eps)
+            __shared__ float s_nr;
+            if (warp == 0) {
+                float acc = 0.0f;
+                if (lane < 4)
+                    for (int i = lane; i < D.K; i += 4) acc = add_ftz(acc, mul_ftz(D.x[i], D.x[i]));
+                const float pair = add_ftz(acc, __shfl_down_sync(0xffffffffu, acc, 2));   // s0+s2, s1+s3
+                const float other = __shfl_down_sync(0xffffffffu, pair, 1);
+                if (lane == 0) {
+                    const float sum = add_ftz(pair, other);
+                    s_nr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)D.K), A.norm_eps)));
+                }
+            }
+            __syncthreads();
+            nr = s_nr;
+        }
         for (int b0 = warp; b0 < nb; b0 += 4 * kWarps) {
             float2 v[4];
             if (D.x) {
 #pragma unroll
                 for (int j = 0; j < 4; j++)
                     if (b0 + j * kWarps < nb) v[j] = reinterpret_cast<const float2*>(D.x + 64 * (b0 + j * kWarps))[lane];
+                if (A.norm_w) {   // y = x * (r * (1 + w)), flushed like the vector unit
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        if (b0 + j * kWarps < nb) {
+                            const float2 w =
+                                reinterpret_cast<const float2*>(A.norm_w + 64 * (b0 + j * kWarps))[lane];
+                            v[j].x = mul_ftz(v[j].x, mul_ftz(nr, add_ftz(1.0f, w.x)));
+                            v[j].y = mul_ftz(v[j].y, mul_ftz(nr, add_ftz(1.0f, w.y)));
+                        }
+                }
             }
 #pragma unroll
             for (int j = 0; j < 4; j++) {
@@ -896,6 +929,27 @@ cudaError_t launch_gemv(const GemvDesc& d0, uint32_t* act, unsigned int* err, cu
     }
     WArgs A{};
     A.res_act = res ? 1 : 0;
+    A.single = d;
+    A.n = 1;
+    A.total_units = plan.total_units;
+    A.ctr = nullptr;
+    A.err = err;
+    const int grid = std::min(num_sms(), (plan.total_units + kWarps - 1) / kWarps);
+    return launch_warp<false, false>(A, grid, stream);
+}
+
+cudaError_t launch_rmsnorm_gemv(const GemvDesc& d0, const float* norm_w, float eps, uint32_t* act, unsigned int* err,
+                               cudaStream_t stream) {
+    if (d0.M <= 0) return cudaSuccess;
+    GemvDesc d = d0;
+    GemvPlan plan;
+    if (!d.x || !norm_w || (reinterpret_cast<uintptr_t>(norm_w) & 7) || !res_fits(d.K) || !fast_shape_ok(d) ||
+        !act || !gemv_plan(&d, 1, act, &plan))
+        return cudaErrorInvalidValue;
+    WArgs A{};
+    A.res_act = 1;
+    A.norm_w = norm_w;
+    A.norm_eps = eps;
     A.single = d;
     A.n = 1;
     A.total_units = plan.total_units;

@@ -83,6 +83,12 @@ cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, un
 // `act` is device scratch of gemv_act_words(K) words.
 cudaError_t launch_gemv(const GemvDesc& d, uint32_t* act, unsigned int* err, cudaStream_t stream);
 
+// One exact GEMV of rmsnorm(x, norm_w, eps) (the reference's NEON-order
+// rmsnorm, then its quantizer and GEMV), in one launch: every CTA normalizes
+// and quantizes x itself.  K <= 6144, a multiple of 512; aligned pointers.
+cudaError_t launch_rmsnorm_gemv(const GemvDesc& d, const float* norm_w, float eps, uint32_t* act, unsigned int* err,
+                               cudaStream_t stream);
+
 // Fast-mode single GEMV (K % 512 == 0, aligned pointers); `act` holds
 // act_cap_words words of scratch, `tickets` tickets_cap zeroed counters
 // (every launch leaves them zero).

@@ -23,7 +23,7 @@ from ._lib import KernelError, check, load
 
 __all__ = [
     "KernelError", "quant_block64", "bfp8_gemv", "bfp8_gemv_fast", "bfp8_gemv_q", "lm_head_bf16", "lm_head_bfp8",
-    "pack_bfp8", "LinearStack", "LmResult", "Planes", "quant_planes", "bfp8_gemm_tc", "BatchedStack",
+    "pack_bfp8", "LinearStack", "rmsnorm_bfp8_gemv", "LmResult", "Planes", "quant_planes", "bfp8_gemm_tc", "BatchedStack",
     "PeerRegion", "ShardedLinearStack", "quant_planes_wait", "ShardedBatchedStack",
 ]
 
@@ -82,6 +82,24 @@ def bfp8_gemv_fast(x: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor, out:
     M, K = mant.shape
     y = out if out is not None else torch.empty(M, dtype=torch.float32, device=x.device)
     check(load().qwen_b200_gemv_fast_dev(_ptr(y), _ptr(x), _ptr(mant), _ptr(exps), M, K, _stream()), "bfp8_gemv_fast")
+    return y
+
+
+def rmsnorm_bfp8_gemv(x: torch.Tensor, norm_w: torch.Tensor, eps: float, mant: torch.Tensor, exps: torch.Tensor,
+                      out: torch.Tensor | None = None):
+    """y [M] = bfp8_gemv(rmsnorm(x, norm_w, eps)) in one launch, bit for bit
+    the reference's rmsnorm (NEON order) followed by its quantizer and GEMV.
+    K a multiple of 512 and <= 6144."""
+    x = _need(x, torch.float32, "x")
+    norm_w = _need(norm_w, torch.float32, "norm_w")
+    mant = _need(mant, torch.int8, "mant")
+    exps = _need(exps, torch.uint8, "exps")
+    M, K = mant.shape
+    if x.numel() != K or norm_w.numel() != K:
+        raise ValueError("shape mismatch")
+    y = out if out is not None else torch.empty(M, dtype=torch.float32, device=mant.device)
+    check(load().qwen_b200_rmsnorm_gemv_dev(_ptr(y), _ptr(x), _ptr(norm_w), float(eps), _ptr(mant), _ptr(exps), M, K,
+                                            _stream()), "rmsnorm_bfp8_gemv")
     return y
 
 

@@ -212,10 +212,28 @@ def make_tb():
     np.savez_compressed(os.path.join(HERE, "tb_gemv.npz"), **out)
 
 
+def make_ref_rmsnorm(k):
+    """rmsnorm of the reference compiled for x86 (its portable build,
+    qwen_kernels_opt.c:140-172), on a few sizes, scales and eps values."""
+    k.rmsnorm.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int, ctypes.c_float]
+    rng = np.random.default_rng(11)
+    out = {}
+    for tag, (n, sx, eps) in {"a": (1024, 1.0, 1e-6), "b": (3584, 20.0, 1e-5), "c": (1000, 1e-3, 1e-6),
+                              "d": (4096, 1e-19, 1e-6)}.items():
+        x = rng.normal(0, sx, n).astype(np.float32)
+        w = rng.normal(0, 0.1, n).astype(np.float32)
+        y = np.zeros(n, np.float32)
+        k.rmsnorm(y.ctypes.data, x.ctypes.data, w.ctypes.data, n, eps)
+        out[f"{tag}_x"], out[f"{tag}_w"], out[f"{tag}_y"] = x, w, y
+        out[f"{tag}_eps"] = np.float32(eps)
+    np.savez_compressed(os.path.join(HERE, "ref_rmsnorm.npz"), **out)
+
+
 def main():
     k, s = ref_libs()
     make_packer()
     make_ref_gemv(k)
+    make_ref_rmsnorm(k)
     make_ref_lm(k, s)
     make_sampler(s)
     make_tb()

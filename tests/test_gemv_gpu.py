@@ -246,3 +246,44 @@ def test_linear_stack_fast_within_tolerance(cuda):
         tol = 1e-5 * term_magnitude(xn, mn, en) + 1e-30
         assert (np.abs(y.cpu().numpy() - ref) <= tol).all()
     stack.close()
+
+
+# ---------------------------------------------------- rmsnorm -> GEMV, fused
+@pytest.mark.parametrize("M,K,sx,eps", [(3584, 1024, 1.0, 1e-6), (33, 2048, 25.0, 1e-5), (257, 6144, 0.5, 1e-6),
+                                        (1, 512, 1e-20, 1e-6), (1024, 3584, 3.0, 1e-6)])
+def test_rmsnorm_gemv_bit_exact(cuda, M, K, sx, eps):
+    """One launch = the reference's rmsnorm (NEON build order) followed by its
+    quantizer and GEMV: every output bit-identical to the oracle chaining
+    rmsnorm and bfp8_gemv, including an odd row count (the scalar last row)
+    and an input whose squares are subnormal (flushed; eps sets the scale)."""
+    import torch
+
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(M + K)
+    mant, exps = rand_weights(rng, M, K)
+    x = rng.normal(0, sx, K).astype(np.float32)
+    w = rng.normal(0, 0.1, K).astype(np.float32)
+    ref = O.bfp8_gemv(O.rmsnorm(x, w, eps, neon=True), mant, exps)
+    dx, dw, dm, de = to_dev(x, w, mant, exps)
+    y = ops.rmsnorm_bfp8_gemv(dx, dw, eps, dm, de)
+    y2 = ops.rmsnorm_bfp8_gemv(dx, dw, eps, dm, de)
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(y.cpu().numpy()), bits(ref))
+    assert np.array_equal(bits(y2.cpu().numpy()), bits(ref))
+
+
+def test_rmsnorm_gemv_rejects_large_k(cuda):
+    """The fused prologue keeps the whole activation in each CTA's shared
+    memory: K above 6144 (or not a multiple of 512) is refused with QB_EINVAL."""
+    import torch
+
+    from qwen_b200 import ops
+    from qwen_b200._lib import KernelError
+
+    for K in (6656, 1088):
+        mant = torch.zeros((8, K), dtype=torch.int8, device="cuda")
+        exps = torch.zeros((8, K // 64), dtype=torch.uint8, device="cuda")
+        x = torch.ones(K, device="cuda")
+        with pytest.raises(KernelError):
+            ops.rmsnorm_bfp8_gemv(x, x, 1e-6, mant, exps)

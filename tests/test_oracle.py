@@ -193,3 +193,28 @@ def test_oracle_topk_rules():
     assert O.argmax(s) == 1
     assert O.argmax(np.full(5, -1e31, np.float32)) == 0
     assert O.topk(s, 0)[0].size == 0
+
+
+def test_scalar_rmsnorm_matches_fixture(golden):
+    """Oracle's portable-build rmsnorm == the reference's rmsnorm compiled for
+    x86 (qwen_kernels_opt.c:140-172), bit for bit, including a vector whose
+    squares are subnormal (the eps term then decides the scale)."""
+    g = golden("ref_rmsnorm.npz")
+    for t in "abcd":
+        y = O.rmsnorm(g[f"{t}_x"], g[f"{t}_w"], float(g[f"{t}_eps"]), neon=False)
+        assert np.array_equal(y.view(np.uint32), g[f"{t}_y"].view(np.uint32)), t
+
+
+def test_neon_rmsnorm_close_to_scalar_reference(golden):
+    """The NEON-order restatement (four flushed lane sums, x * (r * (1 + w)))
+    differs from the portable build only by rounding order.  A float sum of n
+    positive squares carries at most n * 2^-24 relative error, which the
+    square root halves; plus a few roundings in the scale: every output within
+    (n / 2 + 4) * 2^-24 of the reference, relatively."""
+    g = golden("ref_rmsnorm.npz")
+    for t in "abcd":
+        x = g[f"{t}_x"]
+        y = O.rmsnorm(x, g[f"{t}_w"], float(g[f"{t}_eps"]), neon=True)
+        ref = g[f"{t}_y"]
+        tol = (x.size / 2 + 4) * 2.0 ** -24
+        assert np.all(np.abs(y - ref) <= tol * np.abs(ref)), t
