@@ -129,6 +129,16 @@ QB_API int qwen_b200_gemv_dev(float* y, const float* x, const int8_t* mant, cons
 QB_API int qwen_b200_rmsnorm_gemv_dev(float* y, const float* x, const float* norm_w, float eps, const int8_t* mant,
                                       const uint8_t* exps, int M, int K, void* stream);
 
+/* The residual step in front of it as well: x_out = x + res (the reference's
+ * add_residual, qwen_kernels_opt.c:388-396, flushed vector adds -- the
+ * residual-stream update forward_token_c makes after each attention and MLP
+ * block), then y = qwen_b200_rmsnorm_gemv_dev of x_out, in one launch.
+ * x_out must not overlap x or res (the reference updates x in place; here
+ * every CTA reads x while one writes x_out). */
+QB_API int qwen_b200_residual_rmsnorm_gemv_dev(float* y, float* x_out, const float* x, const float* res,
+                                               const float* norm_w, float eps, const int8_t* mant,
+                                               const uint8_t* exps, int M, int K, void* stream);
+
 /* Same from an already quantized activation: xq int16 [K], xs fp32 [K/64]. */
 QB_API int qwen_b200_gemv_q_dev(float* y, const int16_t* xq, const float* xs, const int8_t* mant,
                          const uint8_t* exps, int M, int K, void* stream);

@@ -18,6 +18,7 @@
  *   - lm_head_topk selection    04-板载脚本与工具/qwen_sampling.c:110-155,160-353
  *   - gemv_core dequant mode    02-RTL与仿真/gemv_core.v:40-69,299-534
  *   - rmsnorm, NEON and scalar  04-板载脚本与工具/qwen_kernels_opt.c:140-172
+ *   - add_residual              04-板载脚本与工具/qwen_kernels_opt.c:388-396
  *
  * Floating point model.  The reference board runs the vector parts on ARMv7
  * Advanced SIMD, which always flushes subnormal inputs and results to a zero
@@ -66,6 +67,17 @@ ORC_API void orc_rmsnorm_neon(float* y, const float* x, const float* w, int n, f
     for (i = 0; i + 4 <= n; i += 4)
         for (int l = 0; l < 4; l++) y[i + l] = neon_mul(x[i + l], neon_mul(r, neon_add(1.0f, w[i + l])));
     for (; i < n; i++) y[i] = x[i] * r * (1.0f + w[i]);
+}
+
+/* add_residual (qwen_kernels_opt.c:388-396): x += res, four lanes at a time on
+ * the vector unit (flushed), any n % 4 tail on VFP.  neon = 0: the portable
+ * build (every element on VFP). */
+ORC_API void orc_add_residual(float* x, const float* res, int n, int neon) {
+    int i = 0;
+    if (neon)
+        for (; i + 4 <= n; i += 4)
+            for (int l = 0; l < 4; l++) x[i + l] = neon_add(x[i + l], res[i + l]);
+    for (; i < n; i++) x[i] += res[i];
 }
 
 /* The same routine's portable build: one running sum, y = (x * r) * (1 + w). */

@@ -62,6 +62,7 @@ def lib():
             "orc_selftest_fill": [_P, _P, ctypes.c_size_t, _P, ctypes.c_size_t],
             "orc_rmsnorm_neon": [_P, _P, _P, _I, ctypes.c_float],
             "orc_rmsnorm_scalar": [_P, _P, _P, _I, ctypes.c_float],
+            "orc_add_residual": [_P, _P, _I, _I],
         }
         for name, args in sigs.items():
             fn = getattr(L, name)
@@ -179,6 +180,15 @@ def rmsnorm(x, w, eps, neon=True):
     y = np.empty_like(x)
     fn = lib().orc_rmsnorm_neon if neon else lib().orc_rmsnorm_scalar
     fn(y.ctypes.data, px, pw, x.size, float(eps))
+    return y
+
+
+def add_residual(x, res, neon=True):
+    """x + res as add_residual (qwen_kernels_opt.c:388-396) computes it in
+    place: the NEON build's flushed lanes or the portable build."""
+    y = np.array(x, dtype=np.float32, copy=True)
+    r, pr = _c(res, np.float32)
+    lib().orc_add_residual(y.ctypes.data, pr, y.size, 1 if neon else 0)
     return y
 
 

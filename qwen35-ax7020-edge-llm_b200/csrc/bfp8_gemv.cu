@@ -164,6 +164,8 @@ struct WArgs {
                             // shared memory (no act_prep kernel, no activation copies per stage)
     const float* norm_w;    // res_act only: x is first rmsnorm-ed with these weights (nullptr: not)
     float norm_eps;
+    const float* norm_res;  // with norm_w: x + norm_res is normalized (nullptr: x) ...
+    float* norm_xout;       // ... and CTA 0 stores x + norm_res there (the updated residual stream)
     SyncArgs sync;          // row-sharded stacks: completion signal (sig_epoch 0: none)
 };
 
@@ -512,7 +514,11 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
             if (warp == 0) {
                 float acc = 0.0f;
                 if (lane < 4)
-                    for (int i = lane; i < D.K; i += 4) acc = add_ftz(acc, mul_ftz(D.x[i], D.x[i]));
+                    for (int i = lane; i < D.K; i += 4) {
+                        // add_residual (qwen_kernels_opt.c:388-396): flushed lane adds
+                        const float v = A.norm_res ? add_ftz(D.x[i], A.norm_res[i]) : D.x[i];
+                        acc = add_ftz(acc, mul_ftz(v, v));
+                    }
                 const float pair = add_ftz(acc, __shfl_down_sync(0xffffffffu, acc, 2));   // s0+s2, s1+s3
                 const float other = __shfl_down_sync(0xffffffffu, pair, 1);
                 if (lane == 0) {
@@ -533,6 +539,14 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
 #pragma unroll
                     for (int j = 0; j < 4; j++)
                         if (b0 + j * kWarps < nb) {
+                            if (A.norm_res) {
+                                const float2 rr =
+                                    reinterpret_cast<const float2*>(A.norm_res + 64 * (b0 + j * kWarps))[lane];
+                                v[j].x = add_ftz(v[j].x, rr.x);
+                                v[j].y = add_ftz(v[j].y, rr.y);
+                                if (blockIdx.x == 0)
+                                    reinterpret_cast<float2*>(A.norm_xout + 64 * (b0 + j * kWarps))[lane] = v[j];
+                            }
                             const float2 w =
                                 reinterpret_cast<const float2*>(A.norm_w + 64 * (b0 + j * kWarps))[lane];
                             v[j].x = mul_ftz(v[j].x, mul_ftz(nr, add_ftz(1.0f, w.x)));
@@ -939,17 +953,30 @@ cudaError_t launch_gemv(const GemvDesc& d0, uint32_t* act, unsigned int* err, cu
 }
 
 cudaError_t launch_rmsnorm_gemv(const GemvDesc& d0, const float* norm_w, float eps, uint32_t* act, unsigned int* err,
-                               cudaStream_t stream) {
+                               cudaStream_t stream, const float* res, float* x_out) {
     if (d0.M <= 0) return cudaSuccess;
     GemvDesc d = d0;
     GemvPlan plan;
     if (!d.x || !norm_w || (reinterpret_cast<uintptr_t>(norm_w) & 7) || !res_fits(d.K) || !fast_shape_ok(d) ||
         !act || !gemv_plan(&d, 1, act, &plan))
         return cudaErrorInvalidValue;
+    if ((res == nullptr) != (x_out == nullptr)) return cudaErrorInvalidValue;
+    if (res) {
+        // x_out is written while every CTA still reads x and res: no overlap
+        const uintptr_t o0 = reinterpret_cast<uintptr_t>(x_out), o1 = o0 + 4 * (size_t)d.K;
+        auto overlaps = [&](const float* p) {
+            const uintptr_t p0 = reinterpret_cast<uintptr_t>(p), p1 = p0 + 4 * (size_t)d.K;
+            return p0 < o1 && o0 < p1;
+        };
+        if (((reinterpret_cast<uintptr_t>(res) | o0) & 7) || overlaps(d.x) || overlaps(res))
+            return cudaErrorInvalidValue;
+    }
     WArgs A{};
     A.res_act = 1;
     A.norm_w = norm_w;
     A.norm_eps = eps;
+    A.norm_res = res;
+    A.norm_xout = x_out;
     A.single = d;
     A.n = 1;
     A.total_units = plan.total_units;

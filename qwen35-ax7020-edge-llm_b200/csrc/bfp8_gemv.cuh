@@ -86,8 +86,10 @@ cudaError_t launch_gemv(const GemvDesc& d, uint32_t* act, unsigned int* err, cud
 // One exact GEMV of rmsnorm(x, norm_w, eps) (the reference's NEON-order
 // rmsnorm, then its quantizer and GEMV), in one launch: every CTA normalizes
 // and quantizes x itself.  K <= 6144, a multiple of 512; aligned pointers.
+// With `res`, x + res (the reference's add_residual) is normalized instead
+// and also stored to x_out, which must not overlap x or res.
 cudaError_t launch_rmsnorm_gemv(const GemvDesc& d, const float* norm_w, float eps, uint32_t* act, unsigned int* err,
-                               cudaStream_t stream);
+                               cudaStream_t stream, const float* res = nullptr, float* x_out = nullptr);
 
 // Fast-mode single GEMV (K % 512 == 0, aligned pointers); `act` holds
 // act_cap_words words of scratch, `tickets` tickets_cap zeroed counters

@@ -538,6 +538,28 @@ int qwen_b200_rmsnorm_gemv_dev(float* y, const float* x, const float* norm_w, fl
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_rmsnorm_gemv_dev", e);
 }
 
+int qwen_b200_residual_rmsnorm_gemv_dev(float* y, float* x_out, const float* x, const float* res,
+                                        const float* norm_w, float eps, const int8_t* mant, const uint8_t* exps,
+                                        int M, int K, void* stream) {
+    if (int rc = check_gemv_args(y, x, mant, exps, M, K)) return rc;
+    if (!norm_w || !res || !x_out) return fail(QB_EINVAL, "qwen_b200_residual_rmsnorm_gemv_dev: null pointer");
+    qb::GemvDesc d{};
+    d.mant = mant;
+    d.exps = exps;
+    d.x = x;
+    d.y = y;
+    d.M = M;
+    d.K = K;
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    cudaError_t e = qb::launch_rmsnorm_gemv(d, norm_w, eps, st->act, st->err, static_cast<cudaStream_t>(stream),
+                                            res, x_out);
+    if (e == cudaErrorInvalidValue)
+        return fail(QB_EINVAL, "qwen_b200_residual_rmsnorm_gemv_dev: K a multiple of 512 and <= 6144, 8-byte aligned "
+                               "vectors, x_out overlapping neither x nor res");
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_residual_rmsnorm_gemv_dev", e);
+}
+
 int qwen_b200_gemv_q_dev(float* y, const int16_t* xq, const float* xs, const int8_t* mant,
                          const uint8_t* exps, int M, int K, void* stream) {
     if (int rc = check_gemv_args(y, xq, mant, exps, M, K)) return rc;

@@ -23,7 +23,7 @@ from ._lib import KernelError, check, load
 
 __all__ = [
     "KernelError", "quant_block64", "bfp8_gemv", "bfp8_gemv_fast", "bfp8_gemv_q", "lm_head_bf16", "lm_head_bfp8",
-    "pack_bfp8", "LinearStack", "rmsnorm_bfp8_gemv", "LmResult", "Planes", "quant_planes", "bfp8_gemm_tc", "BatchedStack",
+    "pack_bfp8", "LinearStack", "rmsnorm_bfp8_gemv", "residual_rmsnorm_bfp8_gemv", "LmResult", "Planes", "quant_planes", "bfp8_gemm_tc", "BatchedStack",
     "PeerRegion", "ShardedLinearStack", "quant_planes_wait", "ShardedBatchedStack",
 ]
 
@@ -101,6 +101,27 @@ def rmsnorm_bfp8_gemv(x: torch.Tensor, norm_w: torch.Tensor, eps: float, mant: t
     check(load().qwen_b200_rmsnorm_gemv_dev(_ptr(y), _ptr(x), _ptr(norm_w), float(eps), _ptr(mant), _ptr(exps), M, K,
                                             _stream()), "rmsnorm_bfp8_gemv")
     return y
+
+
+def residual_rmsnorm_bfp8_gemv(x: torch.Tensor, res: torch.Tensor, norm_w: torch.Tensor, eps: float,
+                               mant: torch.Tensor, exps: torch.Tensor):
+    """(x + res, bfp8_gemv(rmsnorm(x + res, norm_w, eps))) in one launch, bit
+    for bit the reference's add_residual, rmsnorm, quantizer and GEMV.
+    K a multiple of 512 and <= 6144.  Returns (y [M], x_out [K])."""
+    x = _need(x, torch.float32, "x")
+    res = _need(res, torch.float32, "res")
+    norm_w = _need(norm_w, torch.float32, "norm_w")
+    mant = _need(mant, torch.int8, "mant")
+    exps = _need(exps, torch.uint8, "exps")
+    M, K = mant.shape
+    if x.numel() != K or res.numel() != K or norm_w.numel() != K:
+        raise ValueError("shape mismatch")
+    y = torch.empty(M, dtype=torch.float32, device=mant.device)
+    x_out = torch.empty(K, dtype=torch.float32, device=mant.device)
+    check(load().qwen_b200_residual_rmsnorm_gemv_dev(_ptr(y), _ptr(x_out), _ptr(x), _ptr(res), _ptr(norm_w),
+                                                     float(eps), _ptr(mant), _ptr(exps), M, K, _stream()),
+          "residual_rmsnorm_bfp8_gemv")
+    return y, x_out
 
 
 def bfp8_gemv_q(xq: torch.Tensor, xs: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor):

@@ -229,11 +229,25 @@ def make_ref_rmsnorm(k):
     np.savez_compressed(os.path.join(HERE, "ref_rmsnorm.npz"), **out)
 
 
+def make_ref_residual(k):
+    """add_residual of the reference compiled for x86 (its portable build,
+    qwen_kernels_opt.c:388-396), incl. subnormal operands."""
+    k.add_residual.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+    rng = np.random.default_rng(12)
+    x = rng.normal(0, 1, 1003).astype(np.float32)
+    r = rng.normal(0, 1, 1003).astype(np.float32)
+    x[5], r[5], x[9], r[17] = 1e-39, 1e-39, -3e-40, 2e-41
+    y = x.copy()
+    k.add_residual(y.ctypes.data, r.ctypes.data, y.size)
+    np.savez_compressed(os.path.join(HERE, "ref_residual.npz"), x=x, r=r, y=y)
+
+
 def main():
     k, s = ref_libs()
     make_packer()
     make_ref_gemv(k)
     make_ref_rmsnorm(k)
+    make_ref_residual(k)
     make_ref_lm(k, s)
     make_sampler(s)
     make_tb()

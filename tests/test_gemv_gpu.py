@@ -287,3 +287,44 @@ def test_rmsnorm_gemv_rejects_large_k(cuda):
         x = torch.ones(K, device="cuda")
         with pytest.raises(KernelError):
             ops.rmsnorm_bfp8_gemv(x, x, 1e-6, mant, exps)
+
+
+@pytest.mark.parametrize("M,K,sx", [(3584, 1024, 1.0), (33, 2048, 40.0), (257, 6144, 1e-20)])
+def test_residual_rmsnorm_gemv_bit_exact(cuda, M, K, sx):
+    """x_out = x + res (the reference's flushed add_residual) and y = GEMV of
+    rmsnorm(x_out) from one launch, both bit-identical to the oracle chain,
+    including subnormal residual sums (flushed)."""
+    import torch
+
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(M * 3 + K)
+    mant, exps = rand_weights(rng, M, K)
+    x = rng.normal(0, sx, K).astype(np.float32)
+    res = rng.normal(0, sx, K).astype(np.float32)
+    w = rng.normal(0, 0.1, K).astype(np.float32)
+    xo = O.add_residual(x, res, neon=True)
+    ref = O.bfp8_gemv(O.rmsnorm(xo, w, 1e-6, neon=True), mant, exps)
+    dx, dr, dw, dm, de = to_dev(x, res, w, mant, exps)
+    for _ in range(2):
+        y, x_out = ops.residual_rmsnorm_bfp8_gemv(dx, dr, dw, 1e-6, dm, de)
+        torch.cuda.synchronize()
+        assert np.array_equal(bits(x_out.cpu().numpy()), bits(xo))
+        assert np.array_equal(bits(y.cpu().numpy()), bits(ref))
+
+
+def test_residual_rmsnorm_gemv_rejects_aliasing(cuda):
+    """x_out may not overlap x or res (every CTA reads them while one writes it)."""
+    import torch
+
+    from qwen_b200._lib import load
+
+    K, M = 1024, 64
+    mant = torch.zeros((M, K), dtype=torch.int8, device="cuda")
+    exps = torch.zeros((M, K // 64), dtype=torch.uint8, device="cuda")
+    x = torch.ones(K, device="cuda")
+    r = torch.ones(K, device="cuda")
+    y = torch.empty(M, device="cuda")
+    rc = load().qwen_b200_residual_rmsnorm_gemv_dev(y.data_ptr(), x.data_ptr(), x.data_ptr(), r.data_ptr(),
+                                                    r.data_ptr(), 1e-6, mant.data_ptr(), exps.data_ptr(), M, K, None)
+    assert rc == -1

@@ -218,3 +218,16 @@ def test_neon_rmsnorm_close_to_scalar_reference(golden):
         ref = g[f"{t}_y"]
         tol = (x.size / 2 + 4) * 2.0 ** -24
         assert np.all(np.abs(y - ref) <= tol * np.abs(ref)), t
+
+
+def test_add_residual_matches_fixture(golden):
+    """Oracle's portable-build add_residual == the compiled reference, bit for
+    bit; the NEON form flushes subnormal operands and sums (the vector unit),
+    and equals it elsewhere."""
+    g = golden("ref_residual.npz")
+    y = O.add_residual(g["x"], g["r"], neon=False)
+    assert np.array_equal(y.view(np.uint32), g["y"].view(np.uint32))
+    yn = O.add_residual(g["x"], g["r"], neon=True)
+    sub = (np.abs(g["x"]) < 1.18e-38) | (np.abs(g["r"]) < 1.18e-38) | (np.abs(g["y"]) < 1.18e-38)
+    assert np.array_equal(yn[~sub].view(np.uint32), g["y"][~sub].view(np.uint32))
+    assert yn[5] == 0.0
