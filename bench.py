@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["stack", "gemv", "lm_bf16", "lm_bfp8", "sharded", "batched"],
+    ap.add_argument("--workload", choices=["stack", "gemv", "lm_bf16", "lm_bfp8", "sharded", "batched", "rtl20"],
                     default="stack")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per step: --workload batched (default 256) or sharded (default 1)")
@@ -255,6 +255,8 @@ def run_b200(args):
         line.update(run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, peak_kind))
     elif args.workload == "batched":
         line.update(run_batched(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kind))
+    elif args.workload == "rtl20":
+        line.update(run_rtl20(args, torch, dev, barrier, world, hbm_peak, peak_kind))
     else:
         line.update(run_lm_head(args, torch, ops, dev, barrier, world, hbm_peak, peak_kind))
 
@@ -538,6 +540,79 @@ def run_lm_head(args, torch, ops, dev, barrier, world, hbm_peak, peak_kind):
             "gpu_launches": args.steps * copies * (1 if args.workload == "lm_bf16" else 2)}
 
 
+def run_rtl20(args, torch, dev, barrier, world, hbm_peak, peak_kind):
+    """Secondary line: the RTL dequant mode (gemv_core's floor(y * 2^20)
+    words) of the cfg-0 GEMV, 3584 x 1024, from fp32 x.  `value` times the
+    kernel alone (a CUDA graph of one call per weight copy); `exact_ms`
+    times the exact-mode single GEMV entry the same way; `e2e` copies x in
+    and the words out around each call."""
+    import numpy as np
+
+    from qwen_b200 import _lib, model, ops
+
+    L = _lib.load()
+    M, K = 3584, 1024
+    wbytes = M * K + M * K // 64
+    nbytes = wbytes + 4 * K + 4 * M
+    copies = args.copies or max(2, math.ceil(L2_DEFEAT_BYTES / wbytes))
+    ds = model.DeviceStack([model.Linear("mlp.up_proj", M, K)], copies=copies, device=dev, seed=1234)
+    views = [ds.views(c)[0] for c in range(copies)]
+    words = torch.empty(M, dtype=torch.int32, device=dev)
+    flags = torch.zeros(1, dtype=torch.int32, device=dev)
+    y = torch.empty(M, dtype=torch.float32, device=dev)
+
+    def rtl(i, x=None):
+        xx, m, e, _ = views[i % copies]
+        xx = xx if x is None else x
+        _lib.check(L.qwen_b200_gemv_rtl20_dev(words.data_ptr(), xx.data_ptr(), None, None, m.data_ptr(),
+                                              e.data_ptr(), M, K, flags.data_ptr(), ops._stream()), "rtl20")
+
+    def exact(i):
+        xx, m, e, _ = views[i % copies]
+        _lib.check(L.qwen_b200_gemv_dev(y.data_ptr(), xx.data_ptr(), m.data_ptr(), e.data_ptr(), M, K,
+                                        ops._stream()), "gemv")
+
+    per = {}
+    for name, fn in (("rtl20", rtl), ("exact", exact)):
+        graph = graph_of(torch, fn, copies)
+        per[name] = timed(torch, lambda i: graph.replay(), args.steps, args.warmup, barrier) / args.steps / copies
+        del graph
+    gbs = nbytes / per["rtl20"] / 1e9
+
+    hx = torch.empty(K, dtype=torch.float32, pin_memory=True)
+    hx.copy_(views[0][0].cpu())
+    hw = torch.empty(M, dtype=torch.int32, pin_memory=True)
+    dx = torch.empty(K, dtype=torch.float32, device=dev)
+
+    def e2e_call(i):
+        dx.copy_(hx, non_blocking=True)
+        rtl(i, dx)
+        hw.copy_(words, non_blocking=True)
+    for i in range(args.warmup):
+        e2e_call(i)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        e2e_call(i)
+    torch.cuda.synchronize()
+    e2e_step = (time.perf_counter() - t0) / args.steps
+    if int(flags.item()) != 0:
+        raise RuntimeError("rtl20 bench: unexpected saturation flags on N(0, 0.02) weights")
+    return {"value": round(world * gbs, 2), "ms_per_step": round(per["rtl20"] * 1e3, 5),
+            "dtype": "int16xint8->int64 fixed point",
+            "config": {"workload": "RTL dequant mode (floor(y*2^20) words), single BFP8 GEMV 3584x1024",
+                       "algorithmic_bytes_per_step": nbytes, "exact_ms": round(per["exact"] * 1e3, 5),
+                       "l2": f"rotates {copies} weight copies ({copies * wbytes / 1e9:.2f} GB) > 126 MB L2",
+                       "launch": "CUDA graph of one call per copy (one launch each: the CTAs quantize x)"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind, "traffic": None,
+                         "kernel": "gemv_warp_kernel<RTL>"},
+            "e2e": {"value": round(world * nbytes / e2e_step / 1e9, 2), "unit": "GB/s",
+                    "ms_per_step": round(e2e_step * 1e3, 4), "h2d_bytes_per_step": 4 * K,
+                    "d2h_bytes_per_step": 4 * M},
+            "gpu_launches": args.steps * copies}
+
+
 # ------------------------------------------------------------------ reference arm
 def reference_stack_runner(workload, seed=7):
     """The reference's own bfp8_gemv (oracle/_ref/libref_kernels.so, built
@@ -584,6 +659,10 @@ def cpu_baseline(workload, batch=1):
 
 def run_reference(args):
     if int(os.environ.get("RANK", "0")) != 0:
+        return
+    if args.workload == "rtl20":
+        print(json.dumps({"impl": "reference", "unavailable": "the RTL dequant mode exists only as FPGA fabric "
+                          "(gemv_core.v); the reference has no CPU implementation of it"}))
         return
     from qwen_b200 import model
 

@@ -154,6 +154,24 @@ QB_API int qwen_b200_gemv_q_dev(float* y, const int16_t* xq, const float* xs, co
 QB_API int qwen_b200_gemv_fast_dev(float* y, const float* x, const int8_t* mant, const uint8_t* exps, int M,
                                    int K, void* stream);
 
+/* RTL dequant mode: the GEMV the FPGA gemv_core computes with dequant_en = 1
+ * (02-RTL与仿真/gemv_core.v:299-534; the host side reads each word as
+ * y * 2^-20).  Per row one int32 word floor(y * 2^20): every block's exact
+ * int32 dot D times the 17-bit truncated mantissa of xs, shifted by
+ * Ex + e - 110 (clamped to [-63, 63]) into a saturating 64-bit accumulator
+ * with 40 fraction bits, clamped to the int32 range on output.  As in the
+ * RTL's two-stage shifter, a shift below -63 moves right by
+ * 7 + 8*((-sh >> 3) & 7) (its high stage reads the unclamped amount).  The
+ * activation is fp32 x (quantized by quant_x_blocks) or, with x == NULL, an
+ * already quantized xq int16 [K] / xs fp32 [K/64]; exactly one of the two.
+ * `flags` (device word, may be NULL; the caller zeroes it) gets bit 0 when a
+ * term or a row sum saturated and bit 1 when an output word was clamped
+ * (the RTL's sticky saturation bit).  Integer arithmetic, bit-exact; any M,
+ * K a positive multiple of 64. */
+QB_API int qwen_b200_gemv_rtl20_dev(int32_t* y_words, const float* x, const int16_t* xq, const float* xs,
+                                    const int8_t* mant, const uint8_t* exps, int M, int K, unsigned int* flags,
+                                    void* stream);
+
 /* Block-64 activation quantizer (quant_x_blocks, qwen_kernels_opt.c:182-205)
  * over B rows: x [B][K] -> xq int16 [B][K], xs [B][K/64]. */
 QB_API int qwen_b200_quant_dev(const float* x, int B, int K, int16_t* xq, float* xs, void* stream);

@@ -166,6 +166,7 @@ struct WArgs {
     float norm_eps;
     const float* norm_res;  // with norm_w: x + norm_res is normalized (nullptr: x) ...
     float* norm_xout;       // ... and CTA 0 stores x + norm_res there (the updated residual stream)
+    unsigned int* rtl_flags;   // RTL mode: sticky flags word (may be null)
     SyncArgs sync;          // row-sharded stacks: completion signal (sig_epoch 0: none)
 };
 
@@ -294,35 +295,105 @@ __device__ __forceinline__ void unit_result(const WArgs& A, const SDesc* T, cons
     if (T[U.d].peer) store_peers(T[U.d].peer, row, yv);
 }
 
-// The 4 blocks of one stage for this lane's row: lane-class sums with
-// __dp2a, then the reference float steps into the four chains (or, for the
-// odd last row, the scalar form into fo).
+// ---------------------------------------------------------- RTL dequant mode
+// The FPGA dequant datapath (02-RTL与仿真/gemv_core.v:299-534), integer only:
+// the block scale xs decodes to a 17-bit mantissa 1.f[22:7] (truncated) and
+// exponent Ex (zero / subnormal / inf / NaN xs -> mantissa 0, Ex 0); with
+// sh = Ex + e - 110 the block adds D * mant * 2^sh to a 64-bit accumulator
+// carrying 40 fraction bits.  sh is clamped to [-63, 63]; a clamped positive
+// shift, or a left shift that loses bits of |D * mant|, saturates the term to
+// +-(2^63 - 1) by the sign of the product; the row sum saturates the same way.
+// The shifter works in two stages (:374-428): the low three bits of the
+// amount come from the clamped shift, the high three from the unclamped one,
+// so a shift below -63 moves right by 7 + 8 * ((-sh >> 3) & 7), as the
+// hardware does.
+// The row's word is clamp(acc, -2^31 << 20, (2^31 - 1) << 20) bits [51:20],
+// i.e. floor(y * 2^20).  Flags: bit 0 a term or the sum saturated, bit 1 the
+// output was clamped (the RTL's sticky saturation bit).
+constexpr long long kRtlAccMax = 0x7FFFFFFFFFFFFFFFll;
+constexpr long long kRtlAccMin = -0x7FFFFFFFFFFFFFFFll;
+constexpr long long kRtlOutMax = 2251799812636672ll;    // (2^31 - 1) << 20
+constexpr long long kRtlOutMin = -2251799813685248ll;   // -2^31 << 20
+
+__device__ __forceinline__ void rtl_block(long long& acc, unsigned int& flags, int D, uint32_t xsb, uint32_t e) {
+    const uint32_t eb = (xsb >> 23) & 0xFFu;
+    const bool norm = eb != 0u && eb != 255u;
+    const unsigned long long mant = norm ? (unsigned long long)((1u << 16) | ((xsb >> 7) & 0xFFFFu)) : 0ull;
+    const int sh = (norm ? (int)eb - 127 : 0) + (int)e - 110;
+    const int shc = sh > 63 ? 63 : (sh < -63 ? -63 : sh);
+    const long long prod = (long long)D * (long long)mant;                   // |prod| < 2^45
+    const unsigned long long pabs = (unsigned long long)(D < 0 ? -(long long)D : (long long)D) * mant;
+    const int ovf_sh = shc >= 16 ? 63 - shc : 63;
+    long long term;
+    if (sh > 63 || (pabs >> ovf_sh) != 0ull) {
+        term = prod < 0 ? kRtlAccMin : kRtlAccMax;
+        flags |= 1u;
+    } else if (shc >= 0) {
+        term = (long long)((unsigned long long)prod << shc);
+    } else {
+        term = (prod >> ((-shc) & 7)) >> (8 * (((-sh) >> 3) & 7));   // arithmetic: floors
+    }
+    const long long sum = (long long)((unsigned long long)acc + (unsigned long long)term);
+    if (((acc ^ sum) & (term ^ sum)) < 0) {   // signed overflow: acc and term share the sign sum lost
+        acc = acc < 0 ? kRtlAccMin : kRtlAccMax;
+        flags |= 1u;
+    } else {
+        acc = sum;
+    }
+}
+
+__device__ __forceinline__ int rtl_word(long long acc, unsigned int& flags) {
+    if (acc > kRtlOutMax) {
+        acc = kRtlOutMax;
+        flags |= 2u;
+    } else if (acc < kRtlOutMin) {
+        acc = kRtlOutMin;
+        flags |= 2u;
+    }
+    return (int)(acc >> 20);
+}
+
+// Lane-class sums L_j = sum over i = j mod 4 of m*xq for block jb of a
+// stage (four 16-byte chunks of this lane's swizzled row, the paired int16
+// activation of the block), with __dp2a.
+__device__ __forceinline__ void lane_sums(const unsigned char* st, const uint4* xst, int sw, int jb, int& L0,
+                                          int& L1, int& L2, int& L3) {
+    const unsigned char* rowp = st + (jb >> 1) * kBox;
+    const int cb = (jb & 1) * 4;
+    const uint4* xb = xst + jb * 8;
+    int A0 = 0, A1 = 0, A2 = 0, A3 = 0, B0 = 0, B1 = 0, B2 = 0, B3 = 0;
+#pragma unroll
+    for (int cc = 0; cc < 4; cc++) {
+        const uint4 w = *reinterpret_cast<const uint4*>(rowp + (((cb + cc) ^ sw) << 4));
+        const uint4 xa = xb[2 * cc], xc = xb[2 * cc + 1];
+        const int p01 = (int)__byte_perm(w.x, w.y, 0x5140), p23 = (int)__byte_perm(w.x, w.y, 0x7362);
+        A0 = __dp2a_lo((int)xa.x, p01, A0);
+        A1 = __dp2a_hi((int)xa.y, p01, A1);
+        A2 = __dp2a_lo((int)xa.z, p23, A2);
+        A3 = __dp2a_hi((int)xa.w, p23, A3);
+        const int q01 = (int)__byte_perm(w.z, w.w, 0x5140), q23 = (int)__byte_perm(w.z, w.w, 0x7362);
+        B0 = __dp2a_lo((int)xc.x, q01, B0);
+        B1 = __dp2a_hi((int)xc.y, q01, B1);
+        B2 = __dp2a_lo((int)xc.z, q23, B2);
+        B3 = __dp2a_hi((int)xc.w, q23, B3);
+    }
+    L0 = A0 + B0;
+    L1 = A1 + B1;
+    L2 = A2 + B2;
+    L3 = A3 + B3;
+}
+
+// The 4 blocks of one stage for this lane's row: lane-class sums, then the
+// reference float steps into the four chains (or, for the odd last row, the
+// scalar form into fo).
 template <bool ODD, bool FAST>
 __device__ __forceinline__ void stage_blocks(const unsigned char* st, const uint4* xst, const float* xsst,
                                              uint32_t ew, int sw, bool odd, float& f0, float& f1, float& f2,
                                              float& f3, float& fo) {
 #pragma unroll
     for (int jb = 0; jb < 4; jb++) {
-        const unsigned char* rowp = st + (jb >> 1) * kBox;
-        const int cb = (jb & 1) * 4;
-        const uint4* xb = xst + jb * 8;
-        int A0 = 0, A1 = 0, A2 = 0, A3 = 0, B0 = 0, B1 = 0, B2 = 0, B3 = 0;
-#pragma unroll
-        for (int cc = 0; cc < 4; cc++) {
-            const uint4 w = *reinterpret_cast<const uint4*>(rowp + (((cb + cc) ^ sw) << 4));
-            const uint4 xa = xb[2 * cc], xc = xb[2 * cc + 1];
-            const int p01 = (int)__byte_perm(w.x, w.y, 0x5140), p23 = (int)__byte_perm(w.x, w.y, 0x7362);
-            A0 = __dp2a_lo((int)xa.x, p01, A0);
-            A1 = __dp2a_hi((int)xa.y, p01, A1);
-            A2 = __dp2a_lo((int)xa.z, p23, A2);
-            A3 = __dp2a_hi((int)xa.w, p23, A3);
-            const int q01 = (int)__byte_perm(w.z, w.w, 0x5140), q23 = (int)__byte_perm(w.z, w.w, 0x7362);
-            B0 = __dp2a_lo((int)xc.x, q01, B0);
-            B1 = __dp2a_hi((int)xc.y, q01, B1);
-            B2 = __dp2a_lo((int)xc.z, q23, B2);
-            B3 = __dp2a_hi((int)xc.w, q23, B3);
-        }
-        const int L0 = A0 + B0, L1 = A1 + B1, L2 = A2 + B2, L3 = A3 + B3;
+        int L0, L1, L2, L3;
+        lane_sums(st, xst, sw, jb, L0, L1, L2, L3);
         const uint32_t e = (ew >> (8 * jb)) & 0xFFu;
         const float xsb = xsst[jb];
         if (FAST) {
@@ -340,7 +411,22 @@ __device__ __forceinline__ void stage_blocks(const unsigned char* st, const uint
     }
 }
 
-template <bool LM, bool FAST>
+// The 4 blocks of one stage in the RTL dequant mode: one int32 dot per block
+// into the row's 64-bit fixed-point accumulator.
+__device__ __forceinline__ void stage_blocks_rtl(const unsigned char* st, const uint4* xst, const float* xsst,
+                                                 uint32_t ew, int sw, long long& acc, unsigned int& flags) {
+#pragma unroll
+    for (int jb = 0; jb < 4; jb++) {
+        int L0, L1, L2, L3;
+        lane_sums(st, xst, sw, jb, L0, L1, L2, L3);
+        rtl_block(acc, flags, (L0 + L1) + (L2 + L3), __float_as_uint(xsst[jb]), (ew >> (8 * jb)) & 0xFFu);
+    }
+}
+
+// LM: lm_head epilogue (argmax / top-k instead of stores).  FAST: fast-mode
+// arithmetic.  RTL: the RTL dequant mode (one int32 word per row, stored in
+// y's bits, sticky flags ORed into A.rtl_flags).
+template <bool LM, bool FAST, bool RTL>
 // <= 248 registers: 2048 of the SM's 65536 stay free for a 64-thread act_prep CTA
 __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs A) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -593,6 +679,9 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
     Unit cu = load_unit(sdesc, nd, nu_total, claimed0);
     int cs = cu.valid ? cu.st0 : 0;
     float f0 = 0.f, f1 = 0.f, f2 = 0.f, f3 = 0.f, fo = 0.f;
+    long long racc = 0;          // RTL: the row's fixed-point accumulator
+    unsigned int rfl = 0u;       // RTL: flags of the current unit
+    unsigned int rflags = 0u;    // RTL: sticky flags of this lane's rows
     const int sw = lane & 7;
     int i = 0;
 #pragma unroll 1
@@ -603,7 +692,7 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
         __syncwarp();
         issue((i + kRing - 1) % kRing, true);
 
-        const bool odd_unit = !FAST && (cu.M & 1) && (cu.r0 + kRows > cu.M - 1);   // holds the odd last row
+        const bool odd_unit = !FAST && !RTL && (cu.M & 1) && (cu.r0 + kRows > cu.M - 1);   // holds the odd last row
         const bool odd = odd_unit && (cu.r0 + lane == cu.M - 1);
         const uint32_t ew = *reinterpret_cast<const uint32_t*>(ering + slot * 128 + lane * 4);
         const unsigned char* st = ring + slot * kStage + lane * 128;
@@ -611,14 +700,24 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
                                : reinterpret_cast<const uint4*>(xring + slot * kXp);
         const float* xsst = res ? reinterpret_cast<const float*>(xrings + (size_t)cu.K * 2) + cs * 4
                                 : reinterpret_cast<const float*>(xring + slot * kXp + 512);
-        if (FAST)
+        if (RTL)
+            stage_blocks_rtl(st, xst, xsst, ew, sw, racc, rfl);
+        else if (FAST)
             stage_blocks<false, true>(st, xst, xsst, ew, sw, false, f0, f1, f2, f3, fo);
         else if (!odd_unit)
             stage_blocks<false, false>(st, xst, xsst, ew, sw, false, f0, f1, f2, f3, fo);
         else
             stage_blocks<true, false>(st, xst, xsst, ew, sw, odd, f0, f1, f2, f3, fo);
         if (++cs == cu.st1) {
-            const float yv = FAST ? f0 : (odd ? fo : add_ftz(add_ftz(f0, f2), add_ftz(f1, f3)));
+            float yv;
+            if (RTL) {
+                yv = __int_as_float(rtl_word(racc, rfl));
+                if (cu.r0 + lane < cu.M) rflags |= rfl;   // lanes past M hold no row
+                racc = 0;
+                rfl = 0u;
+            } else {
+                yv = FAST ? f0 : (odd ? fo : add_ftz(add_ftz(f0, f2), add_ftz(f1, f3)));
+            }
             unit_result<LM>(A, sdesc, cu, lane, yv, lm);
             f0 = f1 = f2 = f3 = fo = 0.f;
             kc++;
@@ -628,6 +727,10 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
         i++;
     }
     cp_async_wait<0>();
+    if (RTL && A.rtl_flags) {
+        const unsigned int f = __reduce_or_sync(0xffffffffu, rflags);
+        if (lane == 0 && f) atomicOr(A.rtl_flags, f);
+    }
     // row-sharded stacks: the last CTA publishes the epoch to every rank
     if (!LM) signal_peers(A.sync);
     if (LM) {
@@ -644,8 +747,11 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
 }
 
 // ---------------------------------------------------------------- generic
-// Any K multiple of 64, any alignment: one thread per row, same arithmetic.
-__global__ void __launch_bounds__(kThreads) gemv_generic_kernel(const __grid_constant__ GemvDesc D) {
+// Any K multiple of 64, any alignment: one thread per row, same arithmetic
+// (RTL: the dequant datapath's words, sticky flags ORed into *rtl_flags).
+template <bool RTL>
+__global__ void __launch_bounds__(kThreads) gemv_generic_kernel(const __grid_constant__ GemvDesc D,
+                                                                unsigned int* rtl_flags) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int nb = D.K >> 6;
     int16_t* xq = reinterpret_cast<int16_t*>(smem);
@@ -683,11 +789,15 @@ __global__ void __launch_bounds__(kThreads) gemv_generic_kernel(const __grid_con
     const uint8_t* e = D.exps + (size_t)m * nb;
     const bool odd = (D.M & 1) && m == D.M - 1;
     float f0 = 0.f, f1 = 0.f, f2 = 0.f, f3 = 0.f, sum = 0.f;
+    long long racc = 0;
+    unsigned int rfl = 0u;
     for (int b = 0; b < nb; b++) {
         int L[4] = {0, 0, 0, 0};
         for (int i2 = 0; i2 < 64; i2++) L[i2 & 3] += (int)w[64 * b + i2] * (int)xq[64 * b + i2];
         const uint32_t eb = e[b];
-        if (odd) {
+        if (RTL) {
+            rtl_block(racc, rfl, (L[0] + L[1]) + (L[2] + L[3]), __float_as_uint(xs[b]), eb);
+        } else if (odd) {
             float t = mul_rn(mul_rn(i2f_rn(L[0] + L[1] + L[2] + L[3]), exp_scale_ieee(eb)), xs[b]);
             sum = add_rn(sum, t);
         } else {
@@ -697,6 +807,11 @@ __global__ void __launch_bounds__(kThreads) gemv_generic_kernel(const __grid_con
             f2 = add_ftz(f2, mul_ftz(mul_ftz(i2f_rn(L[2]), S), xs[b]));
             f3 = add_ftz(f3, mul_ftz(mul_ftz(i2f_rn(L[3]), S), xs[b]));
         }
+    }
+    if (RTL) {
+        D.y[m] = __int_as_float(rtl_word(racc, rfl));
+        if (rfl && rtl_flags) atomicOr(rtl_flags, rfl);
+        return;
     }
     D.y[m] = odd ? sum : add_ftz(add_ftz(f0, f2), add_ftz(f1, f3));
 }
@@ -844,12 +959,12 @@ static cudaError_t launch_prep(const PrepArgs& P, int kmax, cudaStream_t stream)
     return cudaGetLastError();
 }
 
-template <bool LM, bool FAST>
+template <bool LM, bool FAST, bool RTL = false>
 static cudaError_t launch_warp(const WArgs& A, int grid, cudaStream_t stream) {
     const size_t smem = warp_smem_bytes(LM, A.n);
     static size_t configured = 0;   // largest dynamic smem size set so far
     if (smem > configured) {
-        cudaError_t err = cudaFuncSetAttribute(gemv_warp_kernel<LM, FAST>,
+        cudaError_t err = cudaFuncSetAttribute(gemv_warp_kernel<LM, FAST, RTL>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (err != cudaSuccess) return err;
         configured = smem;
@@ -864,7 +979,7 @@ static cudaError_t launch_warp(const WArgs& A, int grid, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = A.res_act ? 0 : 1;   // a programmatic dependent of act_prep unless it quantizes itself
-    return cudaLaunchKernelEx(&cfg, gemv_warp_kernel<LM, FAST>, A);
+    return cudaLaunchKernelEx(&cfg, gemv_warp_kernel<LM, FAST, RTL>, A);
 }
 
 cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, unsigned int* ctr,
@@ -919,20 +1034,26 @@ cudaError_t launch_gemv_fast(const GemvDesc& d0, uint32_t* act, size_t act_cap_w
     return launch_warp<false, true>(A, grid, stream);
 }
 
-cudaError_t launch_gemv(const GemvDesc& d0, uint32_t* act, unsigned int* err, cudaStream_t stream) {
+template <bool RTL>
+static cudaError_t launch_generic(const GemvDesc& d, unsigned int* rtl_flags, cudaStream_t stream) {
+    const size_t smem = (((size_t)2 * d.K + 15) & ~size_t(15)) + 4 * (size_t)(d.K / 64);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(gemv_generic_kernel<RTL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    gemv_generic_kernel<RTL><<<(d.M + kThreads - 1) / kThreads, kThreads, smem, stream>>>(d, rtl_flags);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gemv(const GemvDesc& d0, uint32_t* act, unsigned int* err, cudaStream_t stream, int mode,
+                        unsigned int* rtl_flags) {
     if (d0.M <= 0) return cudaSuccess;
-    if (d0.K <= 0 || d0.K % 64) return cudaErrorInvalidValue;
+    if (d0.K <= 0 || d0.K % 64 || (mode != kExact && mode != kRtl20)) return cudaErrorInvalidValue;
+    const bool rtl = mode == kRtl20;
     GemvDesc d = d0;
     GemvPlan plan;
-    if (!fast_shape_ok(d) || !act || !gemv_plan(&d, 1, act, &plan)) {
-        const size_t smem = (((size_t)2 * d.K + 15) & ~size_t(15)) + 4 * (size_t)(d.K / 64);
-        if (smem > 200 * 1024) return cudaErrorInvalidValue;
-        cudaError_t e = cudaFuncSetAttribute(gemv_generic_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess) return e;
-        gemv_generic_kernel<<<(d.M + kThreads - 1) / kThreads, kThreads, smem, stream>>>(d);
-        return cudaGetLastError();
-    }
+    if (!fast_shape_ok(d) || !act || !gemv_plan(&d, 1, act, &plan))
+        return rtl ? launch_generic<true>(d, rtl_flags, stream) : launch_generic<false>(d, nullptr, stream);
     const bool res = res_fits(d.K);
     if (!res) {
         PrepArgs P{};
@@ -948,8 +1069,9 @@ cudaError_t launch_gemv(const GemvDesc& d0, uint32_t* act, unsigned int* err, cu
     A.total_units = plan.total_units;
     A.ctr = nullptr;
     A.err = err;
+    A.rtl_flags = rtl_flags;
     const int grid = std::min(num_sms(), (plan.total_units + kWarps - 1) / kWarps);
-    return launch_warp<false, false>(A, grid, stream);
+    return rtl ? launch_warp<false, false, true>(A, grid, stream) : launch_warp<false, false>(A, grid, stream);
 }
 
 cudaError_t launch_rmsnorm_gemv(const GemvDesc& d0, const float* norm_w, float eps, uint32_t* act, unsigned int* err,

@@ -52,7 +52,12 @@ struct GemvPlan {
 //          within a K segment, segments summed in order; rows may be split
 //          into K segments so that short, deep matrices fill the GPU.
 //          Deterministic; |y - exact| <= 1e-5 * sum_b |term_b|.
-enum GemvMode { kExact = 0, kFast = 1 };
+//   rtl20: the FPGA dequant datapath (02-RTL与仿真/gemv_core.v:299-534):
+//          per row one int32 word floor(y * 2^20) from a saturating 64-bit
+//          fixed-point sum (stored in y's 32 bits), sticky flags (bit 0 a
+//          term or sum saturated, bit 1 the output clamped) ORed into a
+//          device word.  Integer only, bit-exact.
+enum GemvMode { kExact = 0, kFast = 1, kRtl20 = 2 };
 
 // Activation scratch (32-bit words) one GEMV of depth K needs.
 size_t gemv_act_words(int K);
@@ -79,9 +84,12 @@ cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, un
                              unsigned int* err, cudaStream_t stream,
                              const SyncArgs* sync = nullptr);
 
-// One exact GEMV (any M >= 1, K a positive multiple of 64, any alignment).
-// `act` is device scratch of gemv_act_words(K) words.
-cudaError_t launch_gemv(const GemvDesc& d, uint32_t* act, unsigned int* err, cudaStream_t stream);
+// One exact (or, mode kRtl20, RTL dequant) GEMV: any M >= 1, K a positive
+// multiple of 64, any alignment.  `act` is device scratch of
+// gemv_act_words(K) words; `rtl_flags` (device word, may be null) collects
+// the kRtl20 flags.
+cudaError_t launch_gemv(const GemvDesc& d, uint32_t* act, unsigned int* err, cudaStream_t stream,
+                        int mode = kExact, unsigned int* rtl_flags = nullptr);
 
 // One exact GEMV of rmsnorm(x, norm_w, eps) (the reference's NEON-order
 // rmsnorm, then its quantizer and GEMV), in one launch: every CTA normalizes

@@ -579,6 +579,28 @@ int qwen_b200_gemv_q_dev(float* y, const int16_t* xq, const float* xs, const int
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_gemv_q_dev", e);
 }
 
+int qwen_b200_gemv_rtl20_dev(int32_t* y_words, const float* x, const int16_t* xq, const float* xs,
+                             const int8_t* mant, const uint8_t* exps, int M, int K, unsigned int* flags,
+                             void* stream) {
+    if ((x != nullptr) == (xq != nullptr) || (xq && !xs))
+        return fail(QB_EINVAL, "qwen_b200_gemv_rtl20_dev: give x, or xq and xs");
+    if (int rc = check_gemv_args(y_words, x ? (const void*)x : (const void*)xq, mant, exps, M, K)) return rc;
+    qb::GemvDesc d{};
+    d.mant = mant;
+    d.exps = exps;
+    d.x = x;
+    d.xq = xq;
+    d.xs = x ? nullptr : xs;
+    d.y = reinterpret_cast<float*>(y_words);   // the kernels store each row's int32 word in these bits
+    d.M = M;
+    d.K = K;
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    if (qb::gemv_act_words(K) > kActScratchWords) return fail(QB_EINVAL, "K too large");
+    cudaError_t e = qb::launch_gemv(d, st->act, st->err, static_cast<cudaStream_t>(stream), qb::kRtl20, flags);
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_gemv_rtl20_dev", e);
+}
+
 int qwen_b200_gemv_fast_dev(float* y, const float* x, const int8_t* mant, const uint8_t* exps, int M, int K,
                             void* stream) {
     if (int rc = check_gemv_args(y, x, mant, exps, M, K)) return rc;

@@ -137,6 +137,32 @@ def bfp8_gemv_q(xq: torch.Tensor, xs: torch.Tensor, mant: torch.Tensor, exps: to
     return y
 
 
+def bfp8_gemv_rtl20(mant: torch.Tensor, exps: torch.Tensor, x: torch.Tensor | None = None,
+                    xq: torch.Tensor | None = None, xs: torch.Tensor | None = None):
+    """The FPGA gemv_core dequant mode (02-RTL与仿真/gemv_core.v:299-534):
+    returns (words int32 [M], flags) with words = floor(y * 2^20) from the
+    RTL's saturating 64-bit fixed-point sum and flags bit 0 = a term or row
+    sum saturated, bit 1 = an output word clamped.  The activation is fp32
+    ``x`` (quantized by the reference rule) or ``xq`` int16 / ``xs`` fp32."""
+    mant = _need(mant, torch.int8, "mant")
+    exps = _need(exps, torch.uint8, "exps")
+    if (x is None) == (xq is None) or (xq is not None and xs is None):
+        raise ValueError("bfp8_gemv_rtl20: give x, or xq and xs")
+    M, K = mant.shape
+    words = torch.empty(M, dtype=torch.int32, device=mant.device)
+    flags = torch.zeros(1, dtype=torch.int32, device=mant.device)
+    if x is not None:
+        x = _need(x, torch.float32, "x")
+        args = (_ptr(x), None, None)
+    else:
+        xq = _need(xq, torch.int16, "xq")
+        xs = _need(xs, torch.float32, "xs")
+        args = (None, _ptr(xq), _ptr(xs))
+    check(load().qwen_b200_gemv_rtl20_dev(_ptr(words), *args, _ptr(mant), _ptr(exps), M, K, _ptr(flags),
+                                          _stream()), "bfp8_gemv_rtl20")
+    return words, int(flags.item())
+
+
 @dataclass
 class Planes:
     """Batched int16 block-64 activations as two signed int8 planes

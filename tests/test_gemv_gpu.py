@@ -126,6 +126,74 @@ def test_gemv_q_tb_vectors(cuda, golden):
         assert np.array_equal(bits(y), bits(O.bfp8_gemv_q(xq, xs, w, e))), i
 
 
+# ------------------------------------------------------------------ RTL dequant mode
+def test_gemv_rtl20_tb_vectors(cuda, golden):
+    """tb_gemv_core.v stimulus (:401-419) in the RTL dequant mode: words and
+    sticky flags equal the oracle's (rails with the clamp flag on the
+    saturation case, ~0 on the flush case)."""
+    from qwen_b200 import ops
+
+    g = golden("tb_gemv.npz")
+    for i, (K, M, sd, dq, elo, ehi, xo, au, sat) in enumerate(g["cases"]):
+        xq, xs, w, e = g[f"{i}_xq"], g[f"{i}_xs"], g[f"{i}_w"], g[f"{i}_e"]
+        mant, exps, dq_, ds_ = to_dev(w, e, xq, xs)
+        words, flags = ops.bfp8_gemv_rtl20(mant, exps, xq=dq_, xs=ds_)
+        ref_w, ref_f = O.bfp8_gemv_rtl20(xq, xs, w, e)
+        assert np.array_equal(words.cpu().numpy(), ref_w), i
+        assert flags == ref_f, i
+
+
+RTL_SHAPES = [(3584, 1024), (64, 8192), (33, 2048), (1, 512), (257, 6144), (5, 192), (40, 64 * 23)]
+
+
+@pytest.mark.parametrize("M,K", RTL_SHAPES)
+@pytest.mark.parametrize("sh_lo,sh_hi", [(-120, -50), (-30, 12), (20, 70)])
+def test_gemv_rtl20_bit_exact(cuda, rtl_case, M, K, sh_lo, sh_hi):
+    """Pre-quantized activations over flushing, normal and saturating shifts
+    (and zero / subnormal / inf / NaN / negative block scales): words and
+    flags bit-exact; warp kernel (K % 512 == 0, both activation paths) and
+    generic kernel (other K)."""
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(M * 31 + K + sh_lo)
+    mant, exps, xq, xs = rtl_case(rng, M, K, sh_lo, sh_hi, specials=True)
+    dm, de, dq, ds = to_dev(mant, exps, xq, xs)
+    words, flags = ops.bfp8_gemv_rtl20(dm, de, xq=dq, xs=ds)
+    ref_w, ref_f = O.bfp8_gemv_rtl20(xq, xs, mant, exps)
+    assert np.array_equal(words.cpu().numpy(), ref_w)
+    assert flags == ref_f
+
+
+@pytest.mark.parametrize("M,K", [(3584, 1024), (1024, 3584), (64, 8192), (17, 192)])
+def test_gemv_rtl20_from_fp32(cuda, M, K):
+    """fp32 activations quantized in the launch by the reference rule, then
+    the dequant datapath: equal to the oracle's quantizer + dequant mode, and
+    close to the float GEMV: the 17-bit truncated xs mantissa loses < 2^-16
+    of each block term, the floors < 2^-19 in all."""
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(K + 3 * M)
+    mant, exps = rand_weights(rng, M, K)
+    x = rng.normal(0, 1, K).astype(np.float32)
+    dx, dm, de = to_dev(x, mant, exps)
+    words, flags = ops.bfp8_gemv_rtl20(dm, de, x=dx)
+    xq, xs = O.quant_x(x)
+    ref_w, ref_f = O.bfp8_gemv_rtl20(xq, xs, mant, exps)
+    words = words.cpu().numpy()
+    assert np.array_equal(words, ref_w) and flags == ref_f == 0
+    y = O.bfp8_gemv(x, mant, exps).astype(np.float64)
+    terms = np.abs(O.block_dots(mant, xq).astype(np.float64) * np.exp2(exps.astype(np.float64) - 134) * xs)
+    assert (np.abs(words / 2.0**20 - y) <= 3e-5 * terms.sum(1) + 2.0**-19).all()
+
+
+def test_gemv_rtl20_rejects_bad_activation_args(cuda):
+    from qwen_b200 import ops
+
+    mant, exps = to_dev(np.zeros((4, 64), np.int8), np.zeros((4, 1), np.uint8))
+    with pytest.raises(ValueError):
+        ops.bfp8_gemv_rtl20(mant, exps)
+
+
 # ------------------------------------------------------------------ grouped stack
 def test_linear_stack_full_token_bit_exact(cuda):
     """The 150 GEMVs of one Qwen3.5-0.8B token in one grouped launch."""

@@ -102,6 +102,92 @@ def test_tb_gemv_core_rtl20_tolerance(golden):
             assert flags == 0
 
 
+def rtl_stage_model(xq, xs, mant, exps):
+    """gemv_core.v dequant datapath (02-RTL与仿真/gemv_core.v:299-495) stage
+    by stage with the RTL's register widths: S7 xs decode and the 10-bit
+    shift sh_q, S8 clamp / overflow-test operand / 49-bit product, S9 the
+    low three shift bits from the clamped amount, S10 the high three from
+    the unclamped sh_q2, S11 the 65-bit saturating row sum, S12 the output
+    clamp and bits [51:20].  Returns (words, flags) like the oracle."""
+    M64 = (1 << 64) - 1
+    AMAX, OMAX, OMIN = (1 << 63) - 1, (2**31 - 1) << 20, -(2**31) << 20
+
+    def s64(v):
+        v &= M64
+        return v - (1 << 64) if v >> 63 else v
+
+    def s10(v):
+        v &= 1023
+        return v - 1024 if v >> 9 else v
+
+    M, K = mant.shape
+    nb = K // 64
+    xb = np.ascontiguousarray(xs, np.float32).view(np.uint32)
+    dots = (mant.astype(np.int64).reshape(M, nb, 64) * xq.astype(np.int64).reshape(nb, 64)).sum(-1)
+    words, flags = np.zeros(M, np.int32), 0
+    for m in range(M):
+        acc = 0
+        for b in range(nb):
+            bd, x = int(dots[m, b]), int(xb[b])
+            eb = (x >> 23) & 0xFF
+            norm = eb not in (0, 255)
+            mant17 = ((1 << 16) | ((x >> 7) & 0xFFFF)) if norm else 0
+            sh_q = s10((eb - 127 if norm else 0) + (int(exps[m, b]) - 134) + 24)
+            sh_c = max(-63, min(63, sh_q))
+            ovf_sh = 63 - (sh_c & 63) if sh_c >= 16 else 63
+            prod = bd * mant17
+            ovf = ((abs(bd) * mant17) >> ovf_sh) != 0 or sh_q > 63
+            lo = (prod >> ((-sh_c) & 7)) if sh_c < 0 else s64(prod << (sh_c & 7))
+            if sh_q < 0:
+                shifted = lo >> (8 * ((((-sh_q) & 1023) >> 3) & 7))
+            else:
+                shifted = s64(lo << (8 * ((sh_q >> 3) & 7)))
+            contrib = (-AMAX if prod < 0 else AMAX) if ovf else shifted
+            flags |= int(ovf)
+            total = acc + contrib
+            if total > AMAX or total < -(1 << 63):
+                acc = -AMAX if acc < 0 else AMAX
+                flags |= 1
+            else:
+                acc = total
+        if acc > OMAX or acc < OMIN:
+            flags |= 2
+        words[m] = max(OMIN, min(OMAX, acc)) >> 20
+    return words, flags
+
+
+@pytest.mark.parametrize("sh_lo,sh_hi", [(-120, -50), (-70, 10), (-20, 20), (0, 40), (30, 80)])
+@pytest.mark.parametrize("K,specials", [(64, False), (384, True), (640, True)])
+def test_rtl20_oracle_matches_stage_model(rtl_case, sh_lo, sh_hi, K, specials):
+    """The C oracle's dequant mode == the stage-by-stage Verilog model, words
+    and flags, over shifts from deep flushes (incl. the -103..-64 band the
+    two-stage shifter does not flush) to saturation."""
+    rng = np.random.default_rng(K * 1009 + sh_lo + 500)
+    for _ in range(4):
+        mant, exps, xq, xs = rtl_case(rng, 6, K, sh_lo, sh_hi, specials)
+        words, flags = O.bfp8_gemv_rtl20(xq, xs, mant, exps)
+        mw, mf = rtl_stage_model(xq, xs, mant, exps)
+        assert np.array_equal(words, mw)
+        assert flags == mf
+
+
+def test_rtl20_short_right_shift_below_minus_63():
+    """A shift of -64 moves right by 7 (low bits of the clamped -63, high
+    bits of the unclamped -64), so one block of dot 2^20 with xs = 1.0
+    adds floor(2^20 * 2^16 / 2^7) to the 40-fraction-bit accumulator:
+    word = 2^29 >> 20 = 512.  A lossless clamp would give 0."""
+    mant = np.zeros((1, 64), np.int8)
+    xq = np.zeros(64, np.int16)
+    mant[0, :64] = 64
+    xq[:64] = 256                      # D = 64 * 64 * 256 = 2^20
+    xs = np.array([1.0], np.float32)   # Ex 0, mantissa 2^16
+    exps = np.array([[46]], np.uint8)  # sh = 0 + 46 - 110 = -64
+    words, flags = O.bfp8_gemv_rtl20(xq, xs, mant, exps)
+    assert words[0] == (((1 << 20) << 16) >> 7) >> 20 == 512
+    assert flags == 0
+    assert rtl_stage_model(xq, xs, mant, exps)[0][0] == 512
+
+
 def test_neon_order_close_to_double_model(golden):
     """The NEON-order float result tracks the exact double sum of its terms."""
     g = golden("tb_gemv.npz")
