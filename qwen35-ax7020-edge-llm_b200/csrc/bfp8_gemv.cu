@@ -119,6 +119,11 @@ __global__ void __launch_bounds__(kPrepThreads) act_prep_kernel(const __grid_con
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b0 = blockIdx.y * kPrepChunk + warp * kPrepPerWarp;
     if (b0 >= nb) return;
+    // launched as a programmatic dependent of the previous step's GEMV: x
+    // (possibly its output) and this plan's scratch (which it may still
+    // read) are touched only once that grid has completed (a no-op for a
+    // plain launch)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const float* x = D.x;
     float2 v[kPrepPerWarp];
     if (x) {
@@ -441,6 +446,11 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
     __shared__ int s_cand_count;
     __shared__ unsigned long long s_red[kWarps];
 
+    // a following act_prep launched as this grid's programmatic dependent
+    // may start now (it waits for this grid's completion before it touches
+    // memory), and so may the next GEMV behind it: its CTAs take the SMs of
+    // this grid's finished CTAs and prefetch their first weight stages
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     unsigned char* ring = rings + warp * kRing * kStage;
     unsigned char* xring = xrings + warp * kRing * kXp;
@@ -953,10 +963,19 @@ bool gemv_plan(GemvDesc* descs, int n, uint32_t* act, GemvPlan* plan, int mode, 
 // fits the activation-ring space quantizes it in every CTA (res_act).
 static bool res_fits(int K) { return 2 * (size_t)K + (size_t)K / 16 <= (size_t)kWarps * kRing * kXp; }
 
-static cudaError_t launch_prep(const PrepArgs& P, int kmax, cudaStream_t stream) {
-    dim3 grid(P.n, (kmax / 64 + kPrepChunk - 1) / kPrepChunk);
-    act_prep_kernel<<<grid, kPrepThreads, 0, stream>>>(P);
-    return cudaGetLastError();
+// pdl: launch as a programmatic dependent of the stream's previous kernel
+// (the kernel waits for that grid before it reads or writes memory).
+static cudaError_t launch_prep(const PrepArgs& P, int kmax, cudaStream_t stream, bool pdl = false) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(P.n, (kmax / 64 + kPrepChunk - 1) / kPrepChunk);
+    cfg.blockDim = dim3(kPrepThreads);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, act_prep_kernel, P);
 }
 
 template <bool LM, bool FAST, bool RTL = false>
@@ -995,7 +1014,13 @@ cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, un
         P.wait_epoch = sync->wait_epoch;
         P.world = sync->world;
     }
-    cudaError_t e = launch_prep(P, plan.kmax, stream);
+    // back-to-back steps overlap: this step's GEMV CTAs start (descriptor
+    // table, first weight stages) while the previous kernel's last CTAs
+    // finish.  Not for row-sharded plans (their act_prep waits on peer
+    // flags) nor inside stream capture.
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) return cudaGetLastError();
+    cudaError_t e = launch_prep(P, plan.kmax, stream, !sync && cap == cudaStreamCaptureStatusNone);
     if (e != cudaSuccess) return e;
     WArgs A{};
     A.list = dev_descs;
