@@ -304,6 +304,21 @@ QB_API int qwen_b200_quant_planes_wait_dev(const float* x, int B, int K, int8_t*
 QB_API int qwen_b200_lm_head_bf16_dev(const float* h, const uint16_t* E, int vocab, int hidden, int k,
                                int* out_id, int* out_ids, float* out_scores, int* out_n, void* stream);
 
+/* Device form of sample_from_topk() (qwen_sampling.c:411-529): one warp on
+ * `stream` samples from a DEVICE candidate list -- typically the ids /
+ * scores / out_n a qwen_b200_lm_head_*_dev call just wrote -- and writes the
+ * chosen id to out_id[0] (device), so the token never crosses to the host.
+ * The list length is n, or min(n, *n_dev) when n_dev (device) is given;
+ * n <= 1024.  rng_state is a DEVICE xorshift32 word updated in place (NULL:
+ * ids[0], as the reference); an empty list writes -1.  Same procedure and
+ * IEEE float / double operation order as the reference, with CUDA's expf in
+ * place of the C library's: the token is the reference's except when a
+ * draw lands within a few ulps of a bucket boundary; the rng state advances
+ * identically. */
+QB_API int qwen_b200_sample_topk_dev(const int* ids, const float* scores, const int* n_dev, int n,
+                                     float temperature, int top_k, float top_p, unsigned int* rng_state,
+                                     int* out_id, void* stream);
+
 /* BFP8 lm_head (vocab x hidden BFP8 matrix): exact bfp8_gemv scores fused
  * with the same argmax / top-k rules; the scores never reach global memory.
  * No reference routine (the reference lm_head is bf16); same scratch rule. */

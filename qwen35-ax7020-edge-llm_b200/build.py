@@ -22,7 +22,8 @@ INCLUDE = os.path.join(REPO, "include")
 LIB_NAME = "libqwen_kernels_b200.so"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CU_SOURCES = ["bfp8_gemv.cu", "bfp8_gemm_tc.cu", "lm_head.cu", "pack.cu", "tma.cu", "capi.cu", "noalloc.cu"]
+CU_SOURCES = ["bfp8_gemv.cu", "bfp8_gemm_tc.cu", "lm_head.cu", "pack.cu", "sample.cu", "tma.cu", "capi.cu",
+              "noalloc.cu"]
 
 
 def _nvcc() -> str:

@@ -8,6 +8,7 @@
 #include "bfp8_gemv.cuh"
 #include "common.cuh"
 #include "lm_head.cuh"
+#include "sample.cuh"
 #include "topk.cuh"
 
 #include "qwen_b200.h"
@@ -823,6 +824,17 @@ int qwen_b200_lm_head_bf16_dev(const float* h, const uint16_t* E, int vocab, int
     cudaError_t e = qb::launch_lm_head_bf16(h, E, vocab, hidden, k, 1, st->scratch, st->err, nullptr, out_id,
                                             out_ids, out_scores, out_n, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_lm_head_bf16_dev", e);
+}
+
+int qwen_b200_sample_topk_dev(const int* ids, const float* scores, const int* n_dev, int n, float temperature,
+                              int top_k, float top_p, unsigned int* rng_state, int* out_id, void* stream) {
+    if (!ids || !scores || !out_id || n < 0 || n > qb::kSampleMax)
+        return fail(QB_EINVAL, "qwen_b200_sample_topk_dev: null list or output, or n outside 0..1024");
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    qb::SampleArgs a{ids, scores, n_dev, n, temperature, top_k, top_p, rng_state, out_id};
+    cudaError_t e = qb::launch_sample_topk(a, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_sample_topk_dev", e);
 }
 
 int qwen_b200_lm_head_bfp8_dev(const float* h, const int8_t* mant, const uint8_t* exps, int vocab, int hidden,

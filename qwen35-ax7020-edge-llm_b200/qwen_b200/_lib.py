@@ -60,6 +60,7 @@ SIGNATURES = {
     "qwen_b200_quant_planes_wait_dev": (_I, [_P, _I, _I, _P, _P, _I, _P, ctypes.c_uint, _I, _P]),
     "qwen_b200_lm_head_bf16_dev": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P, _P]),
     "qwen_b200_lm_head_bfp8_dev": (_I, [_P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P]),
+    "qwen_b200_sample_topk_dev": (_I, [_P, _P, _P, _I, _F, _I, _F, _P, _P, _P]),
     "qwen_b200_pack_bfp8_dev": (_I, [_P, _I, _I, _P, _P, _P]),
     "qwen_b200_device_error": (_I, [_I]),
     "qwen_b200_last_error": (ctypes.c_char_p, []),

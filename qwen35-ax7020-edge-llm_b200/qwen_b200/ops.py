@@ -308,6 +308,25 @@ def lm_head_bfp8(h: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor, k: int
     return r
 
 
+def sample_topk(ids: torch.Tensor, scores: torch.Tensor, temperature: float, top_k: int, top_p: float,
+                rng_state: torch.Tensor | None, n: torch.Tensor | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """sample_from_topk on the device (qwen_sampling.c:411-529) over a device
+    candidate list, e.g. ``r = lm_head_bfp8(...); sample_topk(r.ids, r.scores,
+    T, top_k, top_p, state, n=r.n)``.  ``rng_state`` is an int32 [1] device
+    tensor holding the xorshift32 state, updated in place (None: the first
+    id).  Returns the chosen id as an int32 [1] device tensor (no sync)."""
+    ids = _need(ids, torch.int32, "ids")
+    scores = _need(scores, torch.float32, "scores")
+    if out is None:
+        out = torch.empty(1, dtype=torch.int32, device=ids.device)
+    st = None if rng_state is None else _ptr(_need(rng_state, torch.int32, "rng_state"))
+    nd = None if n is None else _ptr(_need(n, torch.int32, "n"))
+    check(load().qwen_b200_sample_topk_dev(_ptr(ids), _ptr(scores), nd, ids.numel(), float(temperature),
+                                           int(top_k), float(top_p), st, _ptr(out), _stream()), "sample_topk")
+    return out
+
+
 def pack_bfp8(w: torch.Tensor, out_mant: torch.Tensor | None = None, out_exps: torch.Tensor | None = None):
     """Pack fp32 [M, K] weights into (mant int8 [M, K], exps uint8 [M, K/64]) on the device."""
     w = _need(w, torch.float32, "w")
