@@ -138,3 +138,22 @@ def test_sharded_entry_points_reject_bad_arguments_without_a_gpu():
     assert lib.qwen_b200_stack_create_sharded(1, one, one, one, one, ints, ints, 0, 9, one, ints) == -1
     assert lib.qwen_b200_tc_stack_create_sharded(1, one, one, one, one, one, ints, ints, None, 8, 8, 1, None,
                                                  ints) == -1
+
+
+def test_rtl20_and_device_sampler_reject_bad_arguments_without_a_gpu():
+    """The RTL dequant GEMV wants exactly one activation form (fp32 x, or xq
+    with xs) and K a positive multiple of 64; the device sampler wants a list,
+    an output and 0 <= n <= 1024.  Both reject before touching a device."""
+    from qwen_b200 import _lib
+
+    lib = _lib.load()
+    p = ctypes.c_void_p(64)   # never dereferenced: validation fails first
+    assert lib.qwen_b200_gemv_rtl20_dev(p, None, None, None, p, p, 4, 64, None, None) == -1
+    assert b"give x, or xq and xs" in lib.qwen_b200_last_error()
+    assert lib.qwen_b200_gemv_rtl20_dev(p, p, p, p, p, p, 4, 64, None, None) == -1
+    assert lib.qwen_b200_gemv_rtl20_dev(p, None, p, None, p, p, 4, 64, None, None) == -1
+    assert lib.qwen_b200_gemv_rtl20_dev(p, p, None, None, p, p, 4, 96, None, None) == -1
+    assert lib.qwen_b200_sample_topk_dev(p, p, None, 1025, 1.0, 0, 1.0, None, p, None) == -1
+    assert lib.qwen_b200_sample_topk_dev(p, p, None, -1, 1.0, 0, 1.0, None, p, None) == -1
+    assert lib.qwen_b200_sample_topk_dev(None, p, None, 4, 1.0, 0, 1.0, None, p, None) == -1
+    assert b"outside 0..1024" in lib.qwen_b200_last_error()
