@@ -139,6 +139,16 @@ QB_API int qwen_b200_residual_rmsnorm_gemv_dev(float* y, float* x_out, const flo
                                                const float* norm_w, float eps, const int8_t* mant,
                                                const uint8_t* exps, int M, int K, void* stream);
 
+/* The MLP's down projection with its SwiGLU in front, in one launch:
+ * y = qwen_b200_gemv_dev of swiglu(gate, up), swiglu as the reference's NEON
+ * build computes it (qwen_kernels_opt.c:332-386: exp_neon's clamp, range
+ * reduction and degree-6 polynomial, flushed lanes, the division on VFP) --
+ * the pair forward_linear_layer / forward_mlp run between the gate / up and
+ * down GEMVs (:983-984, :1000-1001).  K a multiple of 512 and <= 6144;
+ * mant 16-, exps 4-, gate / up 8-byte aligned. */
+QB_API int qwen_b200_swiglu_gemv_dev(float* y, const float* gate, const float* up, const int8_t* mant,
+                                     const uint8_t* exps, int M, int K, void* stream);
+
 /* Same from an already quantized activation: xq int16 [K], xs fp32 [K/64]. */
 QB_API int qwen_b200_gemv_q_dev(float* y, const int16_t* xq, const float* xs, const int8_t* mant,
                          const uint8_t* exps, int M, int K, void* stream);

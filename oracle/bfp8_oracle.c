@@ -80,6 +80,59 @@ ORC_API void orc_add_residual(float* x, const float* res, int n, int neon) {
     for (; i < n; i++) x[i] += res[i];
 }
 
+/* ------------------------------------------------------------------ swiglu */
+static float neon_sub(float a, float b) { return ftz(ftz(a) - ftz(b)); }
+
+/* VMAX / VMIN against a constant (ARMv7 Advanced SIMD, flush-to-zero): a NaN
+ * operand gives NaN, else the larger / smaller of the flushed operands. */
+static float neon_max_c(float a, float c) { a = ftz(a); return (a != a) ? a : (a > c ? a : c); }
+static float neon_min_c(float a, float c) { a = ftz(a); return (a != a) ? a : (a < c ? a : c); }
+
+/* exp_neon (qwen_kernels_opt.c:332-351), one lane: x clamped to [-87, 88];
+ * fx = x * RN(1/ln 2); n = fx rounded to an integer by adding and
+ * subtracting 1.5 * 2^23; f = fx - n; p = the degree-6 Taylor polynomial of
+ * 2^f, coefficients RN((ln 2)^k / k!), by Horner steps that round the product
+ * before the add (VMLA); times 2^n built from exponent bits (VCVT rounds
+ * toward zero, a NaN converts to 0).  Every step flushed like the vector
+ * unit. */
+static const float kLog2e = 0x1.715476p+0f;                  /* RN(1/ln 2) */
+static const float kRoundMagic = 0x1.8p+23f;                 /* 1.5 * 2^23 */
+static const float kExp2Taylor[7] = {                        /* RN((ln 2)^k / k!), k = 0..6 */
+    0x1p+0f, 0x1.62e430p-1f, 0x1.ebfbe0p-3f, 0x1.c6b08ep-5f, 0x1.3b2ab6p-7f, 0x1.5d87fep-10f, 0x1.430912p-13f};
+
+static float exp_neon_lane(float x) {
+    x = neon_min_c(neon_max_c(x, -87.0f), 88.0f);
+    const float fx = neon_mul(x, kLog2e);
+    const float n = neon_sub(neon_add(fx, kRoundMagic), kRoundMagic);
+    const float f = neon_sub(fx, n);
+    float p = kExp2Taylor[6];
+    for (int k = 5; k >= 0; k--) p = neon_add(kExp2Taylor[k], neon_mul(p, f));
+    const int e = ((n != n) ? 0 : (int)n) + 127;
+    const uint32_t bits = (uint32_t)e << 23;
+    float sc;
+    memcpy(&sc, &bits, 4);
+    return neon_mul(p, sc);
+}
+
+/* swiglu (qwen_kernels_opt.c:365-386), NEON build: per lane
+ * y = (g / (1 + exp_neon(-g))) * up, the add and the final product on the
+ * vector unit (flushed), the division on VFP (IEEE, unflushed g); elements
+ * past the last multiple of 4 on VFP with the C library's expf.  neon = 0:
+ * the portable build, every element (g / (1 + expf(-g))) * up on VFP. */
+ORC_API void orc_swiglu(float* y, const float* gate, const float* up, int n, int neon) {
+    int i = 0;
+    if (neon)
+        for (; i < (n & ~3); i++) {
+            const float g = gate[i];
+            const float d = neon_add(1.0f, exp_neon_lane(-g));
+            y[i] = neon_mul(g / d, up[i]);
+        }
+    for (; i < n; i++) {
+        const float g = gate[i];
+        y[i] = (g / (1.0f + expf(-g))) * up[i];
+    }
+}
+
 /* The same routine's portable build: one running sum, y = (x * r) * (1 + w). */
 ORC_API void orc_rmsnorm_scalar(float* y, const float* x, const float* w, int n, float eps) {
     float sum = 0.0f;

@@ -63,6 +63,7 @@ def lib():
             "orc_rmsnorm_neon": [_P, _P, _P, _I, ctypes.c_float],
             "orc_rmsnorm_scalar": [_P, _P, _P, _I, ctypes.c_float],
             "orc_add_residual": [_P, _P, _I, _I],
+            "orc_swiglu": [_P, _P, _P, _I, _I],
         }
         for name, args in sigs.items():
             fn = getattr(L, name)
@@ -189,6 +190,17 @@ def add_residual(x, res, neon=True):
     y = np.array(x, dtype=np.float32, copy=True)
     r, pr = _c(res, np.float32)
     lib().orc_add_residual(y.ctypes.data, pr, y.size, 1 if neon else 0)
+    return y
+
+
+def swiglu(gate, up, neon=True):
+    """(g / (1 + exp(-g))) * up as swiglu (qwen_kernels_opt.c:365-386)
+    computes it: the NEON build (exp_neon, flushed lanes) or the portable
+    build (expf on every element)."""
+    g, pg = _c(gate, np.float32)
+    u, pu = _c(up, np.float32)
+    y = np.zeros(g.size, np.float32)
+    lib().orc_swiglu(y.ctypes.data, pg, pu, g.size, 1 if neon else 0)
     return y
 
 

@@ -87,6 +87,40 @@ __device__ __forceinline__ void block_quant(float2 v, int& q0, int& q1, float& x
     }
 }
 
+// exp_neon (qwen_kernels_opt.c:332-351), one lane, with the vector unit's
+// flush-to-zero on every step: x clamped to [-87, 88] (a NaN stays NaN);
+// fx = x * RN(1/ln 2); n = fx rounded to an integer by adding and
+// subtracting 1.5 * 2^23; f = fx - n; p = the degree-6 Taylor polynomial of
+// 2^f (coefficients RN((ln 2)^k / k!)) by Horner steps that round the product
+// before the add (VMLA is not fused); the result p * 2^n with 2^n built from
+// exponent bits (the conversion rounds toward zero and takes a NaN to 0).
+__device__ __forceinline__ float exp_neon_lane(float x) {
+    constexpr float kLog2e = 0x1.715476p+0f;       // RN(1/ln 2)
+    constexpr float kRoundMagic = 0x1.8p+23f;      // 1.5 * 2^23
+    x = mul_ftz(x, 1.0f);                          // VMAX flushes a subnormal operand
+    x = (x != x) ? x : (x > -87.0f ? x : -87.0f);
+    x = (x != x) ? x : (x < 88.0f ? x : 88.0f);
+    const float fx = mul_ftz(x, kLog2e);
+    const float n = sub_ftz(add_ftz(fx, kRoundMagic), kRoundMagic);
+    const float f = sub_ftz(fx, n);
+    float p = 0x1.430912p-13f;                     // k = 6
+    p = add_ftz(0x1.5d87fep-10f, mul_ftz(p, f));   // k = 5
+    p = add_ftz(0x1.3b2ab6p-7f, mul_ftz(p, f));    // k = 4
+    p = add_ftz(0x1.c6b08ep-5f, mul_ftz(p, f));    // k = 3
+    p = add_ftz(0x1.ebfbe0p-3f, mul_ftz(p, f));    // k = 2
+    p = add_ftz(0x1.62e430p-1f, mul_ftz(p, f));    // k = 1
+    p = add_ftz(1.0f, mul_ftz(p, f));              // k = 0
+    return mul_ftz(p, __int_as_float((__float2int_rz(n) + 127) << 23));
+}
+
+// swiglu (qwen_kernels_opt.c:365-386), NEON build, one lane:
+// (g / (1 + exp_neon(-g))) * up, the add and the product flushed, the
+// division on VFP (IEEE, g unflushed).
+__device__ __forceinline__ float swiglu_lane(float g, float up) {
+    const float d = add_ftz(1.0f, exp_neon_lane(-g));
+    return mul_ftz(__fdiv_rn(g, d), up);
+}
+
 // Block b of the paired activation layout the GEMV consumes (global or
 // shared memory) from lane l's int16 elements 2l, 2l+1 and the block scale.
 __device__ __forceinline__ void block_store(uint32_t* xpairs, float* xscale, int b, int lane, int q0, int q1,
@@ -172,6 +206,7 @@ struct WArgs {
     const float* norm_res;  // with norm_w: x + norm_res is normalized (nullptr: x) ...
     float* norm_xout;       // ... and CTA 0 stores x + norm_res there (the updated residual stream)
     unsigned int* rtl_flags;   // RTL mode: sticky flags word (may be null)
+    const float* glu_up;    // res_act only: the activation is swiglu(x, glu_up) (nullptr: x)
     SyncArgs sync;          // row-sharded stacks: completion signal (sig_epoch 0: none)
 };
 
@@ -631,6 +666,15 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
 #pragma unroll
                 for (int j = 0; j < 4; j++)
                     if (b0 + j * kWarps < nb) v[j] = reinterpret_cast<const float2*>(D.x + 64 * (b0 + j * kWarps))[lane];
+                if (A.glu_up) {   // x holds the gate projection: swiglu(gate, up)
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        if (b0 + j * kWarps < nb) {
+                            const float2 u = reinterpret_cast<const float2*>(A.glu_up + 64 * (b0 + j * kWarps))[lane];
+                            v[j].x = swiglu_lane(v[j].x, u.x);
+                            v[j].y = swiglu_lane(v[j].y, u.y);
+                        }
+                }
                 if (A.norm_w) {   // y = x * (r * (1 + w)), flushed like the vector unit
 #pragma unroll
                     for (int j = 0; j < 4; j++)
@@ -1124,6 +1168,26 @@ cudaError_t launch_rmsnorm_gemv(const GemvDesc& d0, const float* norm_w, float e
     A.norm_eps = eps;
     A.norm_res = res;
     A.norm_xout = x_out;
+    A.single = d;
+    A.n = 1;
+    A.total_units = plan.total_units;
+    A.ctr = nullptr;
+    A.err = err;
+    const int grid = std::min(num_sms(), (plan.total_units + kWarps - 1) / kWarps);
+    return launch_warp<false, false>(A, grid, stream);
+}
+
+cudaError_t launch_swiglu_gemv(const GemvDesc& d0, const float* up, uint32_t* act, unsigned int* err,
+                               cudaStream_t stream) {
+    if (d0.M <= 0) return cudaSuccess;
+    GemvDesc d = d0;
+    GemvPlan plan;
+    if (!d.x || !up || (reinterpret_cast<uintptr_t>(up) & 7) || !res_fits(d.K) || !fast_shape_ok(d) || !act ||
+        !gemv_plan(&d, 1, act, &plan))
+        return cudaErrorInvalidValue;
+    WArgs A{};
+    A.res_act = 1;
+    A.glu_up = up;
     A.single = d;
     A.n = 1;
     A.total_units = plan.total_units;

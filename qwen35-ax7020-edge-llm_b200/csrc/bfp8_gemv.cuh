@@ -99,6 +99,13 @@ cudaError_t launch_gemv(const GemvDesc& d, uint32_t* act, unsigned int* err, cud
 cudaError_t launch_rmsnorm_gemv(const GemvDesc& d, const float* norm_w, float eps, uint32_t* act, unsigned int* err,
                                cudaStream_t stream, const float* res = nullptr, float* x_out = nullptr);
 
+// One exact GEMV of swiglu(gate, up) (the reference's NEON swiglu, then its
+// quantizer and GEMV; d.x holds the gate projection) in one launch: every
+// CTA applies swiglu and quantizes itself.  K <= 6144, a multiple of 512;
+// aligned pointers (up 8-byte).
+cudaError_t launch_swiglu_gemv(const GemvDesc& d, const float* up, uint32_t* act, unsigned int* err,
+                               cudaStream_t stream);
+
 // Fast-mode single GEMV (K % 512 == 0, aligned pointers); `act` holds
 // act_cap_words words of scratch, `tickets` tickets_cap zeroed counters
 // (every launch leaves them zero).

@@ -561,6 +561,26 @@ int qwen_b200_residual_rmsnorm_gemv_dev(float* y, float* x_out, const float* x, 
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_residual_rmsnorm_gemv_dev", e);
 }
 
+int qwen_b200_swiglu_gemv_dev(float* y, const float* gate, const float* up, const int8_t* mant,
+                              const uint8_t* exps, int M, int K, void* stream) {
+    if (int rc = check_gemv_args(y, gate, mant, exps, M, K)) return rc;
+    if (!up) return fail(QB_EINVAL, "qwen_b200_swiglu_gemv_dev: null up projection");
+    qb::GemvDesc d{};
+    d.mant = mant;
+    d.exps = exps;
+    d.x = gate;
+    d.y = y;
+    d.M = M;
+    d.K = K;
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    cudaError_t e = qb::launch_swiglu_gemv(d, up, st->act, st->err, static_cast<cudaStream_t>(stream));
+    if (e == cudaErrorInvalidValue)
+        return fail(QB_EINVAL, "qwen_b200_swiglu_gemv_dev: K a multiple of 512 and <= 6144, mant/exps 16/4-byte, "
+                               "gate/up 8-byte aligned");
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_swiglu_gemv_dev", e);
+}
+
 int qwen_b200_gemv_q_dev(float* y, const int16_t* xq, const float* xs, const int8_t* mant,
                          const uint8_t* exps, int M, int K, void* stream) {
     if (int rc = check_gemv_args(y, xq, mant, exps, M, K)) return rc;

@@ -25,6 +25,11 @@ __device__ __forceinline__ float add_ftz(float a, float b) {
     asm("add.rn.ftz.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
     return d;
 }
+__device__ __forceinline__ float sub_ftz(float a, float b) {
+    float d;
+    asm("sub.rn.ftz.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
 __device__ __forceinline__ float mul_rn(float a, float b) {
     float d;
     asm("mul.rn.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));

@@ -35,6 +35,7 @@ SIGNATURES = {
     "qwen_b200_gemv_noalloc_dev": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "qwen_b200_gemv_fast_dev": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "qwen_b200_gemv_q_dev": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
+    "qwen_b200_swiglu_gemv_dev": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
     "qwen_b200_gemv_rtl20_dev": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _P, _P]),
     "qwen_b200_rmsnorm_gemv_dev": (_I, [_P, _P, _P, _F, _P, _P, _I, _I, _P]),
     "qwen_b200_residual_rmsnorm_gemv_dev": (_I, [_P, _P, _P, _P, _P, _F, _P, _P, _I, _I, _P]),

@@ -137,6 +137,21 @@ def bfp8_gemv_q(xq: torch.Tensor, xs: torch.Tensor, mant: torch.Tensor, exps: to
     return y
 
 
+def swiglu_bfp8_gemv(gate: torch.Tensor, up: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor):
+    """y = BFP8 GEMV of swiglu(gate, up) in one launch, swiglu as the
+    reference's NEON build computes it (qwen_kernels_opt.c:332-386): the MLP's
+    down projection with its activation fused in front.  K <= 6144."""
+    gate = _need(gate, torch.float32, "gate")
+    up = _need(up, torch.float32, "up")
+    mant = _need(mant, torch.int8, "mant")
+    exps = _need(exps, torch.uint8, "exps")
+    M, K = mant.shape
+    y = torch.empty(M, dtype=torch.float32, device=mant.device)
+    check(load().qwen_b200_swiglu_gemv_dev(_ptr(y), _ptr(gate), _ptr(up), _ptr(mant), _ptr(exps), M, K,
+                                           _stream()), "swiglu_bfp8_gemv")
+    return y
+
+
 def bfp8_gemv_rtl20(mant: torch.Tensor, exps: torch.Tensor, x: torch.Tensor | None = None,
                     xq: torch.Tensor | None = None, xs: torch.Tensor | None = None):
     """The FPGA gemv_core dequant mode (02-RTL与仿真/gemv_core.v:299-534):

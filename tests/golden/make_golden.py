@@ -242,12 +242,32 @@ def make_ref_residual(k):
     np.savez_compressed(os.path.join(HERE, "ref_residual.npz"), x=x, r=r, y=y)
 
 
+def make_ref_swiglu(k):
+    """swiglu of the reference compiled for x86 (its portable build,
+    qwen_kernels_opt.c:365-386): g / (1 + expf(-g)) * up, over N(0, 3) gates
+    plus zeros, subnormals, values past exp_neon's clamps (+-87, +-88) and
+    large magnitudes; n = 3587 leaves a tail after the last multiple of 4."""
+    k.swiglu.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+    rng = np.random.default_rng(13)
+    n = 3587
+    g = rng.normal(0, 3, n).astype(np.float32)
+    u = rng.normal(0, 1, n).astype(np.float32)
+    special = [0.0, -0.0, 1e-39, -1e-39, 3e-41, 87.0, -87.0, 87.5, -87.5, 88.0, -88.0, 88.5, -88.5, 100.0,
+               -100.0, 1e4, -1e4, 20.0, -20.0, 1e-6]
+    g[:len(special)] = np.array(special, np.float32)
+    u[40:44] = np.array([1e-39, -2e-40, 0.0, 1e30], np.float32)
+    y = np.zeros(n, np.float32)
+    k.swiglu(y.ctypes.data, g.ctypes.data, u.ctypes.data, n)
+    np.savez_compressed(os.path.join(HERE, "ref_swiglu.npz"), gate=g, up=u, y=y)
+
+
 def main():
     k, s = ref_libs()
     make_packer()
     make_ref_gemv(k)
     make_ref_rmsnorm(k)
     make_ref_residual(k)
+    make_ref_swiglu(k)
     make_ref_lm(k, s)
     make_sampler(s)
     make_tb()

@@ -316,6 +316,35 @@ def test_linear_stack_fast_within_tolerance(cuda):
     stack.close()
 
 
+# ---------------------------------------------------- swiglu -> GEMV, fused
+@pytest.mark.parametrize("M,K", [(1024, 3584), (33, 2048), (257, 6144), (1024, 512)])
+def test_swiglu_gemv_bit_exact(cuda, M, K):
+    """y = GEMV(swiglu(gate, up)) in one launch == the oracle chaining the
+    NEON-build swiglu and the GEMV, bit for bit; the gates include zeros,
+    subnormals and values past exp_neon's clamps."""
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(M + 7 * K)
+    mant, exps = rand_weights(rng, M, K)
+    gate = rng.normal(0, 3, K).astype(np.float32)
+    up = rng.normal(0, 1, K).astype(np.float32)
+    gate[:10] = np.array([0.0, -0.0, 1e-39, -1e-39, 87.5, -87.5, 88.5, -88.5, 100.0, -100.0], np.float32)
+    up[20:23] = np.array([1e-39, 0.0, -3e-40], np.float32)
+    y = ops.swiglu_bfp8_gemv(*to_dev(gate, up, mant, exps)).cpu().numpy()
+    ref = O.bfp8_gemv(O.swiglu(gate, up, neon=True), mant, exps)
+    assert np.array_equal(bits(y), bits(ref))
+
+
+def test_swiglu_gemv_rejects_large_k(cuda):
+    from qwen_b200 import ops
+    from qwen_b200._lib import KernelError
+
+    mant, exps = rand_weights(np.random.default_rng(1), 8, 8192)
+    g = np.ones(8192, np.float32)
+    with pytest.raises(KernelError):
+        ops.swiglu_bfp8_gemv(*to_dev(g, g, mant, exps))
+
+
 # ---------------------------------------------------- rmsnorm -> GEMV, fused
 @pytest.mark.parametrize("M,K,sx,eps", [(3584, 1024, 1.0, 1e-6), (33, 2048, 25.0, 1e-5), (257, 6144, 0.5, 1e-6),
                                         (1, 512, 1e-20, 1e-6), (1024, 3584, 3.0, 1e-6)])

@@ -306,6 +306,41 @@ def test_neon_rmsnorm_close_to_scalar_reference(golden):
         assert np.all(np.abs(y - ref) <= tol * np.abs(ref)), t
 
 
+def test_swiglu_matches_fixture(golden):
+    """Oracle's portable-build swiglu == the compiled reference
+    (qwen_kernels_opt.c:365-386 built for x86), bit for bit, incl. zeros,
+    subnormals, values past exp_neon's clamps and a tail of 3 elements."""
+    g = golden("ref_swiglu.npz")
+    y = O.swiglu(g["gate"], g["up"], neon=False)
+    same = (y.view(np.uint32) == g["y"].view(np.uint32)) | (np.isnan(y) & np.isnan(g["y"]))
+    assert same.all()
+
+
+def test_swiglu_neon_restatement_bound(golden):
+    """The NEON build's swiglu stays within 2^-24 * (16 + 2|g|) relative of
+    the portable build while exp_neon's argument is inside its [-87, 88]
+    clamp and the result is normal.  exp_neon rounds fx = x * log2(e) to
+    float before splitting off n (an absolute error up to |fx| * 2^-24, i.e.
+    ~|x| * 2^-24 relative in 2^fx), then evaluates the degree-6 Taylor
+    polynomial of 2^f (|f| <= 1/2, truncation (ln2/2)^7/7! < 2^-23) with
+    seven roundings; the add, the division and the product add three more.
+    The tail (n % 4) is computed alike by both builds."""
+    g = golden("ref_swiglu.npz")
+    yn = O.swiglu(g["gate"], g["up"], neon=True).astype(np.float64)
+    ref = g["y"].astype(np.float64)
+    ag = np.abs(g["gate"].astype(np.float64))
+    inside = (ag <= 87.0) & (np.abs(ref) >= 2.0**-126)
+    assert inside.sum() > 3500
+    bound = 2.0**-24 * (16 + 2 * ag[inside]) * np.abs(ref[inside])
+    assert (np.abs(yn - ref)[inside] <= bound).all()
+    n = g["gate"].size
+    assert np.array_equal(yn[n - n % 4:], ref[n - n % 4:])
+    # exp_neon clamps -g at 88: g = -100 gives a tiny nonzero value where
+    # expf overflows to inf and the portable build returns -0
+    i = int(np.where(g["gate"] == -100.0)[0][0])
+    assert ref[i] == 0.0 and yn[i] != 0.0
+
+
 def test_add_residual_matches_fixture(golden):
     """Oracle's portable-build add_residual == the compiled reference, bit for
     bit; the NEON form flushes subnormal operands and sums (the vector unit),
