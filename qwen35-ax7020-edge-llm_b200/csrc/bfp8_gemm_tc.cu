@@ -253,6 +253,9 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
     uint64_t* done = uempty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
+    // the next launch on the stream (a programmatic dependent) may start its
+    // CTAs' prologues on the SMs this grid's finished CTAs leave
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = p.descs ? p.n : 1;
     for (int k = threadIdx.x; k < n; k += blockDim.x) {
@@ -296,6 +299,10 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // Up to here only the (immutable) descriptor table was read; activation
+    // planes, outputs and stream-K scratch are touched only once the
+    // previous grid on the stream has completed (a no-op for a plain launch).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     if (warp == 0) {
         // ---------------------------------------------------- TMA producer
@@ -725,8 +732,21 @@ cudaError_t launch_n(const TcDesc* dev_descs, const TcDesc* one, int n, int tota
         p.total_stages = sk->total_stages;
         grid = tc_streamk_grid(sk->total_stages);
     }
-    gemm_tc_kernel<N, DOTS><<<grid, C::kThreads, C::kSmem, stream>>>(p);
-    return cudaGetLastError();
+    // a programmatic dependent of the previous kernel (its prologue overlaps
+    // that grid's tail), except under stream capture
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(C::kThreads);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = cap == cudaStreamCaptureStatusNone ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<N, DOTS>, p);
 }
 
 }  // namespace
