@@ -335,7 +335,12 @@ def sample_topk(ids: torch.Tensor, scores: torch.Tensor, temperature: float, top
     scores = _need(scores, torch.float32, "scores")
     if out is None:
         out = torch.empty(1, dtype=torch.int32, device=ids.device)
+    for t, name in ((rng_state, "rng_state"), (out, "out")):
+        # updated in place: a contiguous copy would take the update instead
+        if t is not None and not t.is_contiguous():
+            raise ValueError(f"sample_topk: {name} must be contiguous")
     st = None if rng_state is None else _ptr(_need(rng_state, torch.int32, "rng_state"))
+    _need(out, torch.int32, "out")
     nd = None if n is None else _ptr(_need(n, torch.int32, "n"))
     check(load().qwen_b200_sample_topk_dev(_ptr(ids), _ptr(scores), nd, ids.numel(), float(temperature),
                                            int(top_k), float(top_p), st, _ptr(out), _stream()), "sample_topk")
