@@ -474,22 +474,26 @@ def run_lm_head(args, torch, ops, dev, barrier, world, hbm_peak, peak_kind):
         per = V * H * 2
         copies = max(2, math.ceil(L2_DEFEAT_BYTES / per))
         tabs = [tab] + [tab.clone() for _ in range(copies - 1)]
+        res = ops.lm_outputs(dev, k)   # preallocated: the timed graph holds only the lm_head kernels
 
         def call(i):
-            ops.lm_head_bf16(h, tabs[i % copies], k)
+            ops.lm_head_bf16(h, tabs[i % copies], k, out=res)
         desc = "bf16 lm_head 65536x1024 + argmax + top-40"
     else:
         mant, exps = ops.pack_bfp8(w)
         per = V * H + V * H // 64
         copies = max(2, math.ceil(L2_DEFEAT_BYTES / per))
         mats = [(mant, exps)] + [(mant.clone(), exps.clone()) for _ in range(copies - 1)]
+        res = ops.lm_outputs(dev, k)   # preallocated: the timed graph holds only the lm_head kernels
 
         def call(i):
             m, e = mats[i % copies]
-            ops.lm_head_bfp8(h, m, e, k)
+            ops.lm_head_bfp8(h, m, e, k, out=res)
         desc = "BFP8 lm_head 65536x1024 + argmax + top-40"
     graph = graph_of(torch, call, copies)
+    clk = ClockSampler(gpu_uuid(torch, dev), dev.index or 0)
     secs = timed(torch, lambda i: graph.replay(), args.steps, args.warmup, barrier)
+    clocks = clk.stop()
     per_step = secs / args.steps / copies   # one lm_head per table copy in each replay
     nbytes = per + 4 * H
     gbs = nbytes / per_step / 1e9
@@ -515,7 +519,7 @@ def run_lm_head(args, torch, ops, dev, barrier, world, hbm_peak, peak_kind):
         def e2e_call(i):
             dh.copy_(hx, non_blocking=True)
             m, e = mats[i % copies]
-            r = ops.lm_head_bfp8(dh, m, e, k)
+            r = ops.lm_head_bfp8(dh, m, e, k, out=res)
             hi[:k].copy_(r.ids[:k], non_blocking=True)
             hs.copy_(r.scores[:k], non_blocking=True)
             hi[k:k + 1].copy_(r.argmax, non_blocking=True)
@@ -537,7 +541,7 @@ def run_lm_head(args, torch, ops, dev, barrier, world, hbm_peak, peak_kind):
             "e2e": {"value": round(world * nbytes / e2e_step / 1e9, 2), "unit": "GB/s",
                     "ms_per_step": round(e2e_step * 1e3, 4), "h2d_bytes_per_step": 4 * H,
                     "d2h_bytes_per_step": 8 * k + 4},
-            "gpu_launches": args.steps * copies * (1 if args.workload == "lm_bf16" else 2)}
+            "gpu_launches": args.steps * copies, "clocks": clocks}
 
 
 def run_rtl20(args, torch, dev, barrier, world, hbm_peak, peak_kind):
@@ -573,9 +577,14 @@ def run_rtl20(args, torch, dev, barrier, world, hbm_peak, peak_kind):
                                         ops._stream()), "gemv")
 
     per = {}
+    clocks = None
     for name, fn in (("rtl20", rtl), ("exact", exact)):
         graph = graph_of(torch, fn, copies)
+        clk = ClockSampler(gpu_uuid(torch, dev), dev.index or 0)
         per[name] = timed(torch, lambda i: graph.replay(), args.steps, args.warmup, barrier) / args.steps / copies
+        sampled = clk.stop()
+        if name == "rtl20":
+            clocks = sampled
         del graph
     gbs = nbytes / per["rtl20"] / 1e9
 
@@ -610,7 +619,7 @@ def run_rtl20(args, torch, dev, barrier, world, hbm_peak, peak_kind):
             "e2e": {"value": round(world * nbytes / e2e_step / 1e9, 2), "unit": "GB/s",
                     "ms_per_step": round(e2e_step * 1e3, 4), "h2d_bytes_per_step": 4 * K,
                     "d2h_bytes_per_step": 4 * M},
-            "gpu_launches": args.steps * copies}
+            "gpu_launches": args.steps * copies, "clocks": clocks}
 
 
 # ------------------------------------------------------------------ reference arm

@@ -295,8 +295,24 @@ def _lm_outputs(device, k: int) -> LmResult:
                     torch.zeros(1, dtype=torch.int32, device=device))
 
 
-def lm_head_bf16(h: torch.Tensor, E: torch.Tensor, k: int = 0) -> LmResult:
-    """Tied-embedding lm_head over E bf16 bits [vocab, hidden] (uint16 or bfloat16)."""
+def lm_outputs(device, k: int) -> LmResult:
+    """Preallocated outputs for repeated lm_head calls (``out=``): the kernels
+    overwrite them with plain stores, so one set serves every call."""
+    return _lm_outputs(torch.device(device), k)
+
+
+def _lm_check_out(out: LmResult, device, k: int) -> LmResult:
+    kk = max(k, 1)
+    for t, dt, n, name in ((out.argmax, torch.int32, 1, "argmax"), (out.ids, torch.int32, kk, "ids"),
+                           (out.scores, torch.float32, kk, "scores"), (out.n, torch.int32, 1, "n")):
+        if t.device != device or t.dtype != dt or not t.is_contiguous() or t.numel() < n:
+            raise ValueError(f"lm_head out.{name}: {dt} contiguous on {device} with >= {n} elements")
+    return out
+
+
+def lm_head_bf16(h: torch.Tensor, E: torch.Tensor, k: int = 0, out: LmResult | None = None) -> LmResult:
+    """Tied-embedding lm_head over E bf16 bits [vocab, hidden] (uint16 or bfloat16);
+    ``out`` (from lm_outputs) is written instead of fresh outputs."""
     h = _need(h, torch.float32, "h")
     if E.dtype == torch.bfloat16:
         E = E.view(torch.int16)
@@ -304,19 +320,21 @@ def lm_head_bf16(h: torch.Tensor, E: torch.Tensor, k: int = 0) -> LmResult:
         raise TypeError("E must hold bf16 bit patterns (bfloat16/int16/uint16)")
     E = E.contiguous()
     V, H = E.shape
-    r = _lm_outputs(h.device, min(k, V))
+    r = _lm_check_out(out, h.device, min(k, V)) if out is not None else _lm_outputs(h.device, min(k, V))
     check(load().qwen_b200_lm_head_bf16_dev(_ptr(h), _ptr(E), V, H, k, _ptr(r.argmax), _ptr(r.ids),
                                             _ptr(r.scores), _ptr(r.n), _stream()), "lm_head_bf16")
     return r
 
 
-def lm_head_bfp8(h: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor, k: int = 40) -> LmResult:
-    """BFP8 lm_head [vocab, hidden] with fused argmax and top-k."""
+def lm_head_bfp8(h: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor, k: int = 40,
+                 out: LmResult | None = None) -> LmResult:
+    """BFP8 lm_head [vocab, hidden] with fused argmax and top-k; ``out`` (from
+    lm_outputs) is written instead of fresh outputs."""
     h = _need(h, torch.float32, "h")
     mant = _need(mant, torch.int8, "mant")
     exps = _need(exps, torch.uint8, "exps")
     V, H = mant.shape
-    r = _lm_outputs(h.device, min(k, V))
+    r = _lm_check_out(out, h.device, min(k, V)) if out is not None else _lm_outputs(h.device, min(k, V))
     check(load().qwen_b200_lm_head_bfp8_dev(_ptr(h), _ptr(mant), _ptr(exps), V, H, k, _ptr(r.argmax),
                                             _ptr(r.ids), _ptr(r.scores), _ptr(r.n), _stream()),
           "lm_head_bfp8")

@@ -105,3 +105,28 @@ def test_bf16_ragged_vocab(cuda, V, H, k):
     tab = (rng.normal(0, 1, (V, H)).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
     h = rng.normal(0, 1, H).astype(np.float32)
     check_bf16(tab, h, k)
+
+
+def test_lm_heads_write_preallocated_outputs(cuda):
+    """``out=`` outputs (one set reused across calls, the way a decode loop or
+    a CUDA graph uses them) give the same results as fresh outputs, for the
+    BFP8 and the bf16 lm_head; the kernels need no zeroing between calls."""
+    import torch
+
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(21)
+    V, H, k = 8192, 1024, 40
+    w = rng.normal(0, 0.02, (V, H)).astype(np.float32)
+    mant, exps = O.pack_bfp8(w)
+    E = torch.from_numpy(w).cuda().to(torch.bfloat16)
+    out_q = ops.lm_outputs("cuda", k)
+    out_b = ops.lm_outputs("cuda", k)
+    for _ in range(3):
+        h = dev(rng.normal(0, 1, H).astype(np.float32))
+        ref_q = ops.lm_head_bfp8(h, dev(mant), dev(exps), k).host()
+        assert ops.lm_head_bfp8(h, dev(mant), dev(exps), k, out=out_q).host() == ref_q
+        ref_b = ops.lm_head_bf16(h, E, k).host()
+        assert ops.lm_head_bf16(h, E, k, out=out_b).host() == ref_b
+    with pytest.raises(ValueError):
+        ops.lm_head_bfp8(h, dev(mant), dev(exps), k, out=ops.lm_outputs("cuda", 8))
