@@ -152,6 +152,19 @@ def swiglu_bfp8_gemv(gate: torch.Tensor, up: torch.Tensor, mant: torch.Tensor, e
     return y
 
 
+def mlp_block(h: torch.Tensor, res: torch.Tensor, post_ln_w: torch.Tensor, gate, up, down, eps: float = 1e-6):
+    """forward_mlp (qwen_kernels_opt.c:994-1003) on the device in three
+    launches, with the residual add of the block before it folded in front:
+    h1 = h + res (add_residual), g / u = the gate / up GEMVs of rmsnorm(h1),
+    d = the down GEMV of swiglu(g, u); returns (h1, d), and the next block
+    adds d (the reference's closing add_residual(h, down_buf)).  ``gate``,
+    ``up``, ``down`` are (mant, exps) pairs.  Every step is the reference's
+    NEON-build arithmetic, so h1 and d equal its values bit for bit."""
+    g, h1 = residual_rmsnorm_bfp8_gemv(h, res, post_ln_w, eps, *gate)
+    u = rmsnorm_bfp8_gemv(h1, post_ln_w, eps, *up)
+    return h1, swiglu_bfp8_gemv(g, u, *down)
+
+
 def bfp8_gemv_rtl20(mant: torch.Tensor, exps: torch.Tensor, x: torch.Tensor | None = None,
                     xq: torch.Tensor | None = None, xs: torch.Tensor | None = None):
     """The FPGA gemv_core dequant mode (02-RTL与仿真/gemv_core.v:299-534):

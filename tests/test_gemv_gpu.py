@@ -335,6 +335,35 @@ def test_swiglu_gemv_bit_exact(cuda, M, K):
     assert np.array_equal(bits(y), bits(ref))
 
 
+def test_mlp_block_chain_bit_exact(cuda):
+    """Two chained MLP blocks of the 0.8B shapes (gate / up 3584x1024, down
+    1024x3584) through ops.mlp_block == the oracle chaining the NEON-build
+    add_residual, rmsnorm, GEMVs and swiglu, bit for bit (the residual
+    stream h and each block's down output)."""
+    import torch
+
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(77)
+    h = rng.normal(0, 1, 1024).astype(np.float32)
+    res = rng.normal(0, 1, 1024).astype(np.float32)
+    dh, dres = to_dev(h, res)
+    for blk in range(2):
+        w = rng.normal(0, 0.1, 1024).astype(np.float32)
+        mg, eg = rand_weights(rng, 3584, 1024)
+        mu, eu = rand_weights(rng, 3584, 1024)
+        md, ed = rand_weights(rng, 1024, 3584)
+        dw, dmg, deg, dmu, deu, dmd, ded = to_dev(w, mg, eg, mu, eu, md, ed)
+        dh, dres = ops.mlp_block(dh, dres, dw, (dmg, deg), (dmu, deu), (dmd, ded))
+        torch.cuda.synchronize()
+        h = O.add_residual(h, res, neon=True)
+        nrm = O.rmsnorm(h, w, 1e-6, neon=True)
+        inter = O.swiglu(O.bfp8_gemv(nrm, mg, eg), O.bfp8_gemv(nrm, mu, eu), neon=True)
+        res = O.bfp8_gemv(inter, md, ed)
+        assert np.array_equal(bits(dh.cpu().numpy()), bits(h)), blk
+        assert np.array_equal(bits(dres.cpu().numpy()), bits(res)), blk
+
+
 def test_swiglu_gemv_rejects_large_k(cuda):
     from qwen_b200 import ops
     from qwen_b200._lib import KernelError
