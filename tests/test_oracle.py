@@ -341,6 +341,62 @@ def test_swiglu_neon_restatement_bound(golden):
     assert ref[i] == 0.0 and yn[i] != 0.0
 
 
+def neon_swiglu_model(gate, up):
+    """The NEON build's swiglu (qwen_kernels_opt.c:332-386) as numpy float32
+    arithmetic, independent of the C oracle: every vector-unit step is one
+    IEEE float32 operation with subnormal operands and results flushed to a
+    signed zero; the division is IEEE (VFP)."""
+    f32 = np.float32
+    tiny = f32(2.0**-126)
+
+    def ftz(a):
+        a = np.asarray(a, f32)
+        return np.where(np.abs(a) < tiny, np.copysign(f32(0), a), a).astype(f32)
+
+    def mul(a, b):
+        return ftz(ftz(a) * ftz(b))
+
+    def add(a, b):
+        return ftz(ftz(a) + ftz(b))
+
+    def sub(a, b):
+        return ftz(ftz(a) - ftz(b))
+
+    g = np.asarray(gate, f32)
+    x = ftz(-g)
+    with np.errstate(invalid="ignore"):
+        x = np.where(np.isnan(x), x, np.maximum(x, f32(-87)))
+        x = np.where(np.isnan(x), x, np.minimum(x, f32(88)))
+    fx = mul(x, f32(1 / np.log(2)))
+    n = sub(add(fx, f32(1.5 * 2**23)), f32(1.5 * 2**23))
+    f = sub(fx, n)
+    coef = [f32(np.log(2) ** k / np.prod(range(1, k + 1))) for k in range(7)]
+    p = coef[6]
+    for k in range(5, -1, -1):
+        p = add(coef[k], mul(p, f))
+    e = np.where(np.isnan(n), 0, np.trunc(np.nan_to_num(n))).astype(np.int64) + 127
+    sc = (e.astype(np.uint32) << np.uint32(23)).view(f32)
+    d = add(f32(1), mul(p, sc))
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        return mul((g / d).astype(f32), np.asarray(up, f32))
+
+
+def test_swiglu_neon_oracle_matches_numpy_model(golden):
+    """The C oracle's NEON-build swiglu == the independent numpy model, bit
+    for bit, over the fixture and 10^6 gates spanning the clamps, zeros and
+    subnormals (NaN payloads aside)."""
+    g = golden("ref_swiglu.npz")
+    rng = np.random.default_rng(8)
+    gates = [g["gate"][: g["gate"].size & ~3], rng.uniform(-100, 100, 1 << 20).astype(np.float32),
+             (rng.normal(0, 1, 4096) * 1e-38).astype(np.float32)]
+    for gate in gates:
+        up = rng.normal(0, 1, gate.size).astype(np.float32)
+        a = O.swiglu(gate, up, neon=True)
+        b = neon_swiglu_model(gate, up)
+        same = (a.view(np.uint32) == b.view(np.uint32)) | (np.isnan(a) & np.isnan(b))
+        assert same.all(), np.where(~same)[0][:5]
+
+
 def test_add_residual_matches_fixture(golden):
     """Oracle's portable-build add_residual == the compiled reference, bit for
     bit; the NEON form flushes subnormal operands and sums (the vector unit),
