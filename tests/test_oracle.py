@@ -397,6 +397,61 @@ def test_swiglu_neon_oracle_matches_numpy_model(golden):
         assert same.all(), np.where(~same)[0][:5]
 
 
+def neon_gemv_model(xq, xs, mant, exps):
+    """bfp8_gemv's NEON int16 path (qwen_kernels_opt.c:213-308) as numpy
+    arithmetic, independent of the C oracle: lane-class sums L_j over
+    i = j mod 4 in integers; per block f_j = f_j + ((float(L_j) * S) * xs)
+    with every float32 step flushed like the vector unit (S = 2^(e-134) is a
+    subnormal, hence flushed, for e < 8); y = (f0 + f2) + (f1 + f3).  An odd
+    last row runs on VFP: sum = sum + (float(sum_j L_j) * S) * xs in IEEE."""
+    f32 = np.float32
+    tiny = f32(2.0**-126)
+
+    def ftz(a):
+        a = np.asarray(a, f32)
+        return np.where(np.abs(a) < tiny, np.copysign(f32(0), a), a).astype(f32)
+
+    def mul(a, b):
+        return ftz(ftz(a) * ftz(b))
+
+    def add(a, b):
+        return ftz(ftz(a) + ftz(b))
+
+    M, K = mant.shape
+    nb = K // 64
+    L = (mant.astype(np.int64).reshape(M, nb, 16, 4) * xq.astype(np.int64).reshape(nb, 16, 4)).sum(axis=2)
+    S = np.ldexp(f32(1), exps.astype(np.int32) - 134).astype(f32)
+    xs = np.asarray(xs, f32)
+    Mv = M & ~1
+    f = np.zeros((Mv, 4), f32)
+    with np.errstate(over="ignore", invalid="ignore"):   # huge exponents overflow to inf / NaN
+        for b in range(nb):
+            f = add(f, mul(mul(L[:Mv, b, :].astype(f32), S[:Mv, b:b + 1]), xs[b]))
+        y = np.zeros(M, f32)
+        y[:Mv] = add(add(f[:, 0], f[:, 2]), add(f[:, 1], f[:, 3]))
+        if M & 1:
+            acc = f32(0)
+            for b in range(nb):
+                acc = f32(acc + f32(f32(f32(L[M - 1, b].sum()) * S[M - 1, b]) * xs[b]))
+            y[M - 1] = acc
+    return y
+
+
+@pytest.mark.parametrize("M,K,elo,ehi", [(64, 1024, 100, 140), (33, 512, 0, 20), (17, 2048, 0, 255),
+                                         (5, 192, 120, 134)])
+def test_neon_gemv_oracle_matches_numpy_model(M, K, elo, ehi):
+    """The C oracle's NEON-order GEMV == the independent numpy model, bit for
+    bit, incl. odd row counts and exponents that make S or the terms
+    subnormal (flushed on the vector unit, kept on VFP)."""
+    rng = np.random.default_rng(M * K + elo)
+    mant = rng.integers(-128, 128, (M, K)).astype(np.int8)
+    exps = rng.integers(elo, ehi + 1, (M, K // 64)).astype(np.uint8)
+    xq, xs = O.quant_x(rng.normal(0, 1, K).astype(np.float32) * np.float32(rng.choice([1e-3, 1.0, 1e3])))
+    a = O.bfp8_gemv_q(xq, xs, mant, exps)
+    b = neon_gemv_model(xq, xs, mant, exps)
+    assert ((a.view(np.uint32) == b.view(np.uint32)) | (np.isnan(a) & np.isnan(b))).all()
+
+
 def test_add_residual_matches_fixture(golden):
     """Oracle's portable-build add_residual == the compiled reference, bit for
     bit; the NEON form flushes subnormal operands and sums (the vector unit),
