@@ -452,6 +452,52 @@ def test_neon_gemv_oracle_matches_numpy_model(M, K, elo, ehi):
     assert ((a.view(np.uint32) == b.view(np.uint32)) | (np.isnan(a) & np.isnan(b))).all()
 
 
+def _ftz32(a):
+    a = np.asarray(a, np.float32)
+    return np.where(np.abs(a) < np.float32(2.0**-126), np.copysign(np.float32(0), a), a).astype(np.float32)
+
+
+def _nmul(a, b):
+    return _ftz32(_ftz32(a) * _ftz32(b))
+
+
+def _nadd(a, b):
+    return _ftz32(_ftz32(a) + _ftz32(b))
+
+
+def test_neon_rmsnorm_and_lm_scores_match_numpy_models():
+    """Two more NEON-order restatements against independent numpy models,
+    bit for bit: rmsnorm (qwen_kernels_opt.c:140-172: four flushed lane sums
+    of x*x over i = 4j + l, (s0 + s2) + (s1 + s3), r = 1/sqrt(sum/n + eps) in
+    IEEE, y = x * (r * (1 + w)) flushed) and the bf16 lm_head scores
+    (:427-456: eight flushed chains c = i mod 8, then
+    ((c0 + c4) + (c2 + c6)) + ((c1 + c5) + (c3 + c7)))."""
+    f32 = np.float32
+    rng = np.random.default_rng(31)
+    for n, sx in ((1024, 1.0), (3584, 30.0), (512, 1e-20)):
+        x = (rng.normal(0, 1, n) * sx).astype(f32)
+        w = rng.normal(0, 0.1, n).astype(f32)
+        s4 = np.zeros(4, f32)
+        for i in range(0, n, 4):
+            s4 = _nadd(s4, _nmul(x[i:i + 4], x[i:i + 4]))
+        total = _nadd(_nadd(s4[0], s4[2]), _nadd(s4[1], s4[3]))
+        r = f32(f32(1) / np.sqrt(f32(f32(total / f32(n)) + f32(1e-6)), dtype=f32))
+        model = _nmul(x, _nmul(r, _nadd(f32(1), w)))
+        got = O.rmsnorm(x, w, 1e-6, neon=True)
+        assert np.array_equal(got.view(np.uint32), model.view(np.uint32)), n
+    V, H = 257, 1024
+    E = (rng.normal(0, 0.05, (V, H)).astype(f32).view(np.uint32) >> 16).astype(np.uint16)
+    h = rng.normal(0, 1, H).astype(f32)
+    Ef = (E.astype(np.uint32) << 16).view(f32)
+    c = np.zeros((V, 8), f32)
+    for i in range(0, H, 8):
+        c = _nadd(c, _nmul(Ef[:, i:i + 8], h[i:i + 8]))
+    model = _nadd(_nadd(_nadd(c[:, 0], c[:, 4]), _nadd(c[:, 2], c[:, 6])),
+                  _nadd(_nadd(c[:, 1], c[:, 5]), _nadd(c[:, 3], c[:, 7])))
+    got = O.lm_scores(h, E, with_tail=False)
+    assert np.array_equal(got.view(np.uint32), model.view(np.uint32))
+
+
 def test_add_residual_matches_fixture(golden):
     """Oracle's portable-build add_residual == the compiled reference, bit for
     bit; the NEON form flushes subnormal operands and sums (the vector unit),
