@@ -80,7 +80,8 @@ QB_API int lm_head_argmax(const float* h, const uint16_t* embed_table, int vocab
 /* Replaces lm_head_topk() (04-板载脚本与工具/qwen_sampling.c:283-353; caller
  * chat_v3.py:151-155,180-181).  Writes the min(k, vocab) best (id, score)
  * pairs sorted by score descending, ties by ascending id, and returns their
- * number; 0 on invalid arguments.  This build serves k <= 1024. */
+ * number; 0 on invalid arguments.  Any k: k <= 1024 runs the fused scan,
+ * larger k scores every row on the device and sorts (score, id) keys there. */
 QB_API int lm_head_topk(const float* h, const uint16_t* embed_table, int vocab_size, int hidden_dim, int k,
                  int* out_ids, float* out_scores);
 

@@ -708,16 +708,8 @@ cudaError_t launch_n(const TcDesc* dev_descs, const TcDesc* one, int n, int tota
                      cudaStream_t stream, const SyncArgs* sync, const TcStreamK* sk) {
     using C = TcCfg<N>;
     static_assert(C::kSmem <= 232448, "shared memory plan exceeds 227 KB");
-    static unsigned long long attr_set = 0;   // one bit per device
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!(attr_set >> dev & 1ull)) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<N, DOTS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)C::kSmem);
-        if (e != cudaSuccess) return e;
-        attr_set |= 1ull << dev;
-    }
+    if (cudaError_t e = raise_smem_limit(reinterpret_cast<const void*>(gemm_tc_kernel<N, DOTS>), C::kSmem))
+        return e;
     TcLaunch p{};
     p.descs = dev_descs;
     p.n = n;

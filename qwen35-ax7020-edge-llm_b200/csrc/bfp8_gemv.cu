@@ -1025,13 +1025,8 @@ static cudaError_t launch_prep(const PrepArgs& P, int kmax, cudaStream_t stream,
 template <bool LM, bool FAST, bool RTL = false>
 static cudaError_t launch_warp(const WArgs& A, int grid, cudaStream_t stream) {
     const size_t smem = warp_smem_bytes(LM, A.n);
-    static size_t configured = 0;   // largest dynamic smem size set so far
-    if (smem > configured) {
-        cudaError_t err = cudaFuncSetAttribute(gemv_warp_kernel<LM, FAST, RTL>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (err != cudaSuccess) return err;
-        configured = smem;
-    }
+    cudaError_t err = raise_smem_limit(reinterpret_cast<const void*>(gemv_warp_kernel<LM, FAST, RTL>), smem);
+    if (err != cudaSuccess) return err;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);

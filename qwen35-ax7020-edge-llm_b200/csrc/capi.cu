@@ -4,6 +4,7 @@
 // conventions (04-板载脚本与工具/qwen_kernels_opt.c, qwen_sampling.c) and run
 // the work on the device; the _dev entry points take device pointers and a
 // stream and are what the PyTorch operators and the benchmarks call.
+#include "api_error.cuh"
 #include "bfp8_gemm_tc.cuh"
 #include "bfp8_gemv.cuh"
 #include "common.cuh"
@@ -24,10 +25,11 @@
 #include <vector>
 
 namespace {
-
 thread_local std::string g_err;
+}  // namespace
 
-int fail(int code, const char* what, cudaError_t e = cudaSuccess) {
+namespace qb {
+int api_fail(int code, const char* what, cudaError_t e) {
     char buf[256];
     if (e != cudaSuccess)
         snprintf(buf, sizeof buf, "%s: %s", what, cudaGetErrorString(e));
@@ -36,6 +38,11 @@ int fail(int code, const char* what, cudaError_t e = cudaSuccess) {
     g_err = buf;
     return code;
 }
+}  // namespace qb
+
+namespace {
+
+int fail(int code, const char* what, cudaError_t e = cudaSuccess) { return qb::api_fail(code, what, e); }
 
 // ---------------------------------------------------------------- profiler
 enum { PF_GEMV = 0, PF_ARGMAX, PF_TOPK, PF_SAMPLE, PF_UPLOAD, PF_N };
@@ -405,6 +412,50 @@ static int lm_bf16_host(const float* h, const uint16_t* E, int vocab, int hidden
     return 0;
 }
 
+// lm_head_topk for k above the fused kernels' 1024: the scores of every row
+// in the lm_head_topk order, then one device radix sort of (score, ~id) keys.
+static int lm_bf16_host_large(const float* h, const uint16_t* E, int vocab, int hidden, int k, int* out_ids,
+                              float* out_scores) {
+    if (ensure_ctx()) return QB_ENODEV;
+    int rc = QB_OK;
+    const void* dE = device_of(E, (size_t)vocab * hidden * 2, &rc);
+    if (!dE) return rc;
+    const int kk = k < vocab ? k : vocab;
+    const size_t in_b = 4 * (size_t)hidden, out_b = (size_t)kk * 8 + 16;
+    const size_t temp_b = qb::topk_large_temp_bytes(vocab);
+    // device: scores, two key buffers, sort temp storage (one growable block)
+    const size_t sc_b = (4 * (size_t)vocab + 255) & ~size_t(255), key_b = (8 * (size_t)vocab + 255) & ~size_t(255);
+    if ((rc = grow_pinned(&g_ctx.h_in, &g_ctx.h_in_cap, in_b)) ||
+        (rc = grow_pinned(&g_ctx.h_out, &g_ctx.h_out_cap, out_b)) ||
+        (rc = grow_dev(&g_ctx.d_in, &g_ctx.d_in_cap, in_b + 16)) ||
+        (rc = grow_dev(&g_ctx.d_out, &g_ctx.d_out_cap, out_b)) ||
+        (rc = grow_dev(reinterpret_cast<void**>(&g_ctx.d_scores), &g_ctx.d_scores_cap, sc_b + 2 * key_b + temp_b)))
+        return rc;
+    unsigned char* blk = reinterpret_cast<unsigned char*>(g_ctx.d_scores);
+    float* d_sc_all = reinterpret_cast<float*>(blk);
+    unsigned long long* keys = reinterpret_cast<unsigned long long*>(blk + sc_b);
+    unsigned long long* keys_alt = reinterpret_cast<unsigned long long*>(blk + sc_b + key_b);
+    void* temp = blk + sc_b + 2 * key_b;
+    cudaStream_t s = g_ctx.stream;
+    memcpy(g_ctx.h_in, h, in_b);
+    cudaMemcpyAsync(g_ctx.d_in, g_ctx.h_in, in_b, cudaMemcpyHostToDevice, s);
+    int* d_ids = static_cast<int*>(g_ctx.d_out);
+    float* d_sc = reinterpret_cast<float*>(d_ids + kk);
+    cudaError_t e = qb::launch_lm_scores_bf16(static_cast<const float*>(g_ctx.d_in), static_cast<const uint16_t*>(dE),
+                                              vocab, hidden, 1, d_sc_all, s);
+    if (e == cudaSuccess)
+        e = qb::launch_topk_large(d_sc_all, vocab, kk, keys, keys_alt, temp, temp_b, d_ids, d_sc, g_ctx.d_res + 1,
+                                  s);
+    if (e != cudaSuccess) return fail(QB_ECUDA, "lm_head_topk launch", e);
+    int n = 0;
+    cudaMemcpyAsync(g_ctx.h_out, d_ids, (size_t)kk * 8, cudaMemcpyDeviceToHost, s);
+    cudaMemcpyAsync(&n, g_ctx.d_res + 1, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return fail(QB_ECUDA, "lm_head_topk", e);
+    memcpy(out_ids, g_ctx.h_out, (size_t)n * 4);
+    memcpy(out_scores, static_cast<char*>(g_ctx.h_out) + (size_t)kk * 4, (size_t)n * 4);
+    return n;
+}
+
 int lm_head_argmax(const float* h, const uint16_t* embed_table, int vocab_size, int hidden_dim) {
     ProfScope ps(PF_ARGMAX);
     std::lock_guard<std::mutex> lk(g_mu);
@@ -424,8 +475,8 @@ int lm_head_topk(const float* h, const uint16_t* embed_table, int vocab_size, in
     if (!h || !embed_table || !out_ids || !out_scores) return 0;
     if (vocab_size <= 0 || hidden_dim <= 0 || k <= 0) return 0;
     if ((k < vocab_size ? k : vocab_size) > qb::kTopkMax) {
-        fail(QB_EINVAL, "lm_head_topk: k above 1024 is not served by this build");
-        return 0;
+        const int n = lm_bf16_host_large(h, embed_table, vocab_size, hidden_dim, k, out_ids, out_scores);
+        return n < 0 ? 0 : n;
     }
     int id = 0;
     int n = lm_bf16_host(h, embed_table, vocab_size, hidden_dim, k, 1, out_ids, out_scores, &id);

@@ -11,6 +11,10 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
 namespace qb {
 
 constexpr int kWarp = 32;
@@ -93,5 +97,26 @@ __device__ __forceinline__ void cp_async8(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+// ------------------------------------------------------------ host helpers
+// Raise the dynamic shared-memory limit of kernel `fn` on the current device
+// to at least `bytes`.  cudaFuncSetAttribute acts per device context, so the
+// largest size set so far is remembered per (kernel, device); a mutex keeps
+// concurrent host threads from lowering a limit another thread just raised.
+inline cudaError_t raise_smem_limit(const void* fn, size_t bytes) {
+    static std::mutex mu;
+    static std::unordered_map<const void*, std::vector<size_t>> limits;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(mu);
+    std::vector<size_t>& per_dev = limits[fn];
+    if ((int)per_dev.size() <= dev) per_dev.resize(dev + 1, 0);
+    if (bytes <= per_dev[dev]) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) per_dev[dev] = bytes;
+    return e;
+}
 
 }  // namespace qb

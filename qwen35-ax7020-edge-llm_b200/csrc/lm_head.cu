@@ -22,6 +22,8 @@
 #include "tma.cuh"
 #include "topk.cuh"
 
+#include <cub/device/device_radix_sort.cuh>
+
 #include <algorithm>
 
 namespace qb {
@@ -424,6 +426,68 @@ cudaError_t launch_lm_head_bf16(const float* h, const uint16_t* E, int vocab, in
     if (err != cudaSuccess) return err;
     const int grid = std::max(1, std::min(std::min(num_sms(), (vocab + 1023) / 1024), kMaxGrid));
     select_kernel<<<grid, kThreads, smem, stream>>>(score_buf, vocab, A);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ k > 1024
+// Top-k with any k (the reference's lm_head_topk serves every k): every
+// score becomes a 64-bit key (ordered score, ~id), so one descending radix
+// sort of the keys is the reference order -- score descending, ties by
+// ascending id -- and scores not above -FLT_MAX (which the reference never
+// offers to its table) get key 0 and sort last.
+__global__ void topk_keys_kernel(const float* scores, int vocab, unsigned long long* keys) {
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < vocab; t += gridDim.x * blockDim.x) {
+        const float s = scores[t];
+        keys[t] = s > -3.402823466e38f ? cand_key(s, t) : 0ull;
+    }
+}
+
+__global__ void topk_emit_kernel(const unsigned long long* sorted, int kk, int* out_ids, float* out_scores,
+                                 int* out_n) {
+    __shared__ int s_n;
+    if (threadIdx.x == 0) s_n = 0;
+    __syncthreads();
+    int valid = 0;
+    for (int i = threadIdx.x; i < kk; i += blockDim.x) {
+        const unsigned long long key = sorted[i];
+        if (key) {
+            out_ids[i] = key_id(key);
+            out_scores[i] = key_score(key);
+            valid++;
+        }
+    }
+    atomicAdd(&s_n, valid);
+    __syncthreads();
+    if (threadIdx.x == 0) *out_n = s_n;   // the valid keys are a prefix of the sorted list
+}
+
+size_t topk_large_temp_bytes(int vocab) {
+    size_t temp = 0;
+    cub::DoubleBuffer<unsigned long long> db(nullptr, nullptr);
+    cub::DeviceRadixSort::SortKeysDescending(nullptr, temp, db, vocab);
+    return temp;
+}
+
+cudaError_t launch_topk_large(const float* scores, int vocab, int kk, unsigned long long* keys,
+                              unsigned long long* keys_alt, void* temp, size_t temp_bytes, int* out_ids,
+                              float* out_scores, int* out_n, cudaStream_t stream) {
+    if (vocab <= 0 || kk <= 0 || kk > vocab || !keys || !keys_alt || !temp) return cudaErrorInvalidValue;
+    const int grid = std::max(1, std::min((vocab + kThreads - 1) / kThreads, num_sms() * 8));
+    topk_keys_kernel<<<grid, kThreads, 0, stream>>>(scores, vocab, keys);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    cub::DoubleBuffer<unsigned long long> db(keys, keys_alt);
+    e = cub::DeviceRadixSort::SortKeysDescending(temp, temp_bytes, db, vocab, 0, 64, stream);
+    if (e != cudaSuccess) return e;
+    topk_emit_kernel<<<1, 1024, 0, stream>>>(db.Current(), kk, out_ids, out_scores, out_n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_lm_scores_bf16(const float* h, const uint16_t* E, int vocab, int hidden, int with_tail,
+                                  float* scores, cudaStream_t stream) {
+    if (vocab <= 0 || hidden <= 0 || !scores) return cudaErrorInvalidValue;
+    lm_bf16_generic_kernel<<<(vocab + kThreads - 1) / kThreads, kThreads, 0, stream>>>(h, E, vocab, hidden,
+                                                                                     with_tail, scores);
     return cudaGetLastError();
 }
 

@@ -10,6 +10,7 @@
 // point whose scratch is a fixed array in the library's own device image:
 // it exists on every GPU that loads the library, from load until the
 // process exits, and costs kNoAllocScratchWords * 4 bytes (33 KB) each.
+#include "api_error.cuh"
 #include "bfp8_gemv.cuh"
 
 #include "qwen_b200.h"
@@ -34,11 +35,15 @@ uint32_t* g_scratch_addr[kMaxDevices] = {};
 // per device (with that device current).  No allocation happens here.
 int scratch_address(uint32_t** out) {
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return QB_ENODEV;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return qb::api_fail(QB_ENODEV, "qwen_b200_gemv_noalloc_dev: no current device", e);
+    if (dev < 0 || dev >= kMaxDevices)
+        return qb::api_fail(QB_ENODEV, "qwen_b200_gemv_noalloc_dev: device index beyond 63");
     std::lock_guard<std::mutex> lk(g_setup_mu);
     if (!g_scratch_addr[dev]) {
         void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return QB_ECUDA;
+        if ((e = cudaGetSymbolAddress(&p, g_noalloc_scratch)) != cudaSuccess || !p)
+            return qb::api_fail(QB_ECUDA, "qwen_b200_gemv_noalloc_dev: scratch address lookup", e);
         g_scratch_addr[dev] = static_cast<uint32_t*>(p);
     }
     *out = g_scratch_addr[dev];
@@ -49,8 +54,11 @@ int scratch_address(uint32_t** out) {
 
 extern "C" int qwen_b200_gemv_noalloc_dev(float* y, const float* x, const int8_t* mant, const uint8_t* exps, int M,
                                           int K, void* stream) {
-    if (!y || !x || !mant || !exps || M < 0 || K <= 0 || K % 64) return QB_EINVAL;
-    if (K > kNoAllocMaxK) return QB_EINVAL;   // the fixed scratch holds one activation of K <= 16384
+    if (!y || !x || !mant || !exps) return qb::api_fail(QB_EINVAL, "qwen_b200_gemv_noalloc_dev: null pointer");
+    if (M < 0 || K <= 0 || K % 64)
+        return qb::api_fail(QB_EINVAL, "qwen_b200_gemv_noalloc_dev: M must be >= 0 and K a positive multiple of 64");
+    if (K > kNoAllocMaxK)   // the fixed scratch holds one activation of K <= 16384
+        return qb::api_fail(QB_EINVAL, "qwen_b200_gemv_noalloc_dev: K above 16384 exceeds the fixed scratch");
     if (M == 0) return QB_OK;
     uint32_t* scratch = nullptr;
     if (int rc = scratch_address(&scratch)) return rc;
@@ -64,5 +72,5 @@ extern "C" int qwen_b200_gemv_noalloc_dev(float* y, const float* x, const int8_t
     // every word the kernels read is written by this call's activation pass
     // first, so the previous call's contents need no clearing
     cudaError_t e = qb::launch_gemv(d, scratch, nullptr, static_cast<cudaStream_t>(stream));
-    return e == cudaSuccess ? QB_OK : QB_ECUDA;
+    return e == cudaSuccess ? QB_OK : qb::api_fail(QB_ECUDA, "qwen_b200_gemv_noalloc_dev", e);
 }

@@ -3,7 +3,8 @@
 Run in a container that has the reference tree (read-only) and the
 reference C files compiled by ``make -C oracle ref``:
 
-    python tests/golden/make_golden.py [REFERENCE_ROOT]
+    python tests/golden/make_golden.py REFERENCE_ROOT
+    (or QWEN_REFERENCE_ROOT=... python tests/golden/make_golden.py)
 
 Every fixture is produced by the reference's OWN code or recipe:
   packer.npz      05-主机侧源码/bfp8_packer.py pack_matrix_soa, imported and run
@@ -32,7 +33,9 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 from oracle import oracle as O  # noqa: E402
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("QWEN_REFERENCE_ROOT", "")
+if __name__ == "__main__" and not os.path.isdir(REF):
+    sys.exit("make_golden.py: pass the reference checkout (or set QWEN_REFERENCE_ROOT)")
 REF_DIR = os.path.join(REPO, "oracle", "_ref")
 
 

@@ -109,3 +109,28 @@ def test_profiler_counts_dropin_calls(lib):
     lib.qwen_prof_enable(0)
     lib.qwen_b200_forget_weights(mant.ctypes.data)
     lib.qwen_b200_forget_weights(exps.ctypes.data)
+
+
+def test_lm_head_topk_dropin_serves_k_above_1024(lib):
+    """The reference returns min(k, vocab) entries for every k
+    (qwen_sampling.c:283-353); above 1024 the scores are sorted on the device.
+    Duplicate rows give tied scores (ascending id first), a NaN row and a
+    -inf row are never offered, and k past the vocabulary caps at its size."""
+    g = O.XorShift32(0x2468ACE1)
+    tab, h = g.selftest_fill(3000, 64)
+    tab[100] = tab[7]                               # ties with id 7
+    tab[2999] = tab[7]
+    tab[50] = np.uint16(0x7FC0)                     # NaN row -> NaN score
+    tab[51] = np.uint16(0)
+    tab[51][0] = np.uint16(0xFF80)                  # -inf * h[0] ... -> +-inf or NaN
+    V, H = tab.shape
+    for k in (1025, 2048, V - 1, V, V + 50):
+        kk = min(k, V)
+        ids = np.full(kk, -7, np.int32)
+        sc = np.zeros(kk, np.float32)
+        n = lib.lm_head_topk(h.ctypes.data, tab.ctypes.data, V, H, k, ids.ctypes.data, sc.ctypes.data)
+        rids, rsc = O.lm_head_topk(h, tab, k)
+        assert n == len(rids), (k, n, len(rids))
+        assert np.array_equal(ids[:n], rids), k
+        assert np.array_equal(bits(sc[:n]), bits(rsc)), k
+    lib.qwen_b200_forget_weights(tab.ctypes.data)
