@@ -2,27 +2,38 @@
 """Benchmark of the BFP8 GEMV / lm_head decode hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload stack|gemv|lm_bf16|lm_bfp8|sharded|batched] [--batch B]
+                    [--workload stack|gemv|lm_bf16|lm_bfp8|sharded|batched|rtl20] [--batch B]
+                    [--headline-only] [--no-sharded] [--no-cpu-baseline] [--no-e2e]
 
 Default workload (the BASELINE metric's configuration): the full per-token
 linear stack of Qwen3.5-0.8B at batch 1 -- 150 BFP8 GEMVs, 504,791,040 bytes
 of weights, each GEMV on its own fp32 N(0,1) activation re-quantized inside
 the kernel -- as ONE grouped kernel launch per token.  A step is one token.
-Weights are random N(0, 0.02), packed on the device, and the timed steps
-rotate through enough byte-identical copies (> 4 GB) that no step finds its
-weights in the 126 MB L2.
+The weights are the same packed bytes in both arms (``synthetic_stack``) and
+the timed steps rotate through enough byte-identical device copies (> 4 GB)
+that no step finds its weights in the 126 MB L2.
 
 One JSON line on rank 0.  `value` is algorithmic GB/s of the stack
 (weights + fp32 activations in + fp32 outputs out, summed over ranks) with
 everything resident in HBM; `e2e` is the same metric with every token's
 activations copied in from pinned host memory and its outputs copied back
-inside the timed region.  With --gpus N under torchrun every rank runs its
-own token stream on its own GPU (independent decode replicas, weak scaling,
-no collective on the data path).
+inside the timed region (copies of one token overlap the neighbouring
+tokens' kernels on two copy streams; `e2e.serial_*` has them in line).  With
+--gpus N under torchrun every rank runs its own token stream on its own GPU
+(independent decode replicas, weak scaling, no collective on the data path).
+
+Beside the headline the default line carries, on one GPU, `configs`: the
+other BASELINE configurations (the single 3584x1024 GEMV, the bf16 and BFP8
+lm_heads with top-40, batched tcgen05 decode at B = 8/32/128/256), the same
+150 GEMVs issued as a token issues them (`chain`), and the reference-facing
+host-pointer bfp8_gemv per call (`abi`); and on every N, `sharded`: the
+row-sharded multi-GPU configuration (8 x gate/up 28672x8192 + down
+8192x28672) at batch 1 and 64, strong scaling over the ranks, with a parity
+check against one GPU.  `cpu_baseline` times the reference on the host.
 
 --impl reference times the reference's own C bfp8_gemv (compiled from its
 source for this host, scalar float path since the host has no NEON) on the
-same workload with every host thread, rank 0 only.
+same packed bytes with every host thread, rank 0 only.
 """
 from __future__ import annotations
 
@@ -33,6 +44,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
@@ -43,6 +55,7 @@ for _p in (REPO, PKG):
 
 METRIC = "BFP8 GEMV HBM GB/s (% of B200 peak); 0.8B-shape linear-stack ms/token, batch 1"
 L2_DEFEAT_BYTES = 4.3e9
+STACK_SEED = 1234
 
 
 def parse():
@@ -56,12 +69,16 @@ def parse():
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per step: --workload batched (default 256) or sharded (default 1)")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
-                    help="--workload sharded: rows stored into every GPU by the GEMV kernel, or NCCL all-gathers")
+                    help="--workload sharded: stores into every GPU by the kernels, or NCCL all-gathers")
+    ap.add_argument("--headline-only", action="store_true", help="skip the per-configuration sub-records")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the row-sharded multi-GPU record")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--copies", type=int, default=0,
                     help="weight copies to rotate (default: enough for > 4 GB; fewer only for profiling)")
     ap.add_argument("--cpu-sample", action="store_true", help=argparse.SUPPRESS)
+    ap.add_argument("--cpu-kind", default="ref", help=argparse.SUPPRESS)
+    ap.add_argument("--cpu-data", default="", help=argparse.SUPPRESS)
     args = ap.parse_args()
     if args.batch is None:
         args.batch = 256 if args.workload == "batched" else 1
@@ -97,6 +114,80 @@ def stack_shapes(workload):
     if workload == "gemv":
         return [model.Linear("mlp.up_proj", 3584, 1024)], "single BFP8 GEMV 3584x1024, batch 1"
     raise ValueError(workload)
+
+
+def pack_rows(w):
+    """Block-64 BFP8 SoA packing of fp32 rows [M, K] by the reference
+    packer's rule (05-主机侧源码/bfp8_packer.py:53-86): e = ceil(log2(peak))
+    + 127 per 64-block (127 and zero mantissas below 1e-12), m =
+    clip(rint(w * 2^(134 - e)), -128, 127); ceil(log2) is taken exactly from
+    the float's bits, as the device packer does."""
+    import numpy as np
+
+    M, K = w.shape
+    blk = w.reshape(M, K // 64, 64)
+    peak = np.abs(blk).max(axis=2)
+    u = peak.view(np.uint32)
+    lg = ((u >> 23) & 0xFF).astype(np.int32) - 127 + ((u & 0x7FFFFF) != 0)
+    e = np.clip(lg + 127, 0, 255)
+    zero = ~(peak >= np.float32(1e-12))
+    e[zero] = 127
+    scale = ((261 - e).astype(np.uint32) << 23).view(np.float32)
+    m = np.clip(np.rint(blk * scale[:, :, None]), -128, 127).astype(np.int8)
+    m[zero] = 0
+    return m.reshape(M, K), e.astype(np.uint8)
+
+
+def synthetic_stack(shapes, seed=STACK_SEED):
+    """The packed weights (the weight-file image at model.layout offsets) and
+    the fp32 activations (one per GEMV, concatenated in stack order) of a
+    stack -- the SAME bytes in the B200 arm and the reference arm.  One
+    N(0, 0.02) matrix per distinct shape is drawn (numpy, seeded) and packed;
+    the i-th tensor of that shape is it with its rows rotated by 997 * i
+    (packed rows are independent: every tensor is a packed N(0, 0.02) matrix
+    and no two are equal).  Activations are N(0, 1)."""
+    import numpy as np
+
+    from qwen_b200 import model
+
+    table, total = model.layout(shapes)
+    buf = np.zeros(total, np.uint8)
+    bases, seen = {}, {}
+    for name, (off, t) in table.items():
+        key = (t.M, t.K)
+        if key not in bases:
+            rng = np.random.default_rng([seed, t.M, t.K])
+            w = rng.standard_normal((t.M, t.K), dtype=np.float32)
+            w *= np.float32(0.02)
+            bases[key] = pack_rows(w)
+        i = seen.get(key, 0)
+        seen[key] = i + 1
+        mant, exps = bases[key]
+        sh = (997 * i) % t.M
+        buf[off:off + t.mant_bytes] = np.roll(mant, sh, axis=0).view(np.uint8).reshape(-1)
+        buf[off + t.mant_bytes:off + t.mant_bytes + t.exp_bytes] = np.roll(exps, sh, axis=0).reshape(-1)
+        buf[off + t.mant_bytes + t.exp_bytes:off + t.soa_bytes] = 127   # exponent padding of the file format
+    x = np.random.default_rng([seed, 1]).standard_normal(sum(t.K for t in shapes), dtype=np.float32)
+    return buf, x
+
+
+def stack_views(buf, x, shapes):
+    """(y, x, mant, exps, M, K) host arrays of every GEMV of a synthetic
+    stack, sliced from the weight image as the engine slices its mmap
+    (04-板载脚本与工具/qwen_real_engine.py:834-846)."""
+    import numpy as np
+
+    from qwen_b200 import model
+
+    table, _ = model.layout(shapes)
+    out, pos = [], 0
+    for t in shapes:
+        off, _ = table[t.name]
+        mant = buf[off:off + t.mant_bytes].view(np.int8).reshape(t.M, t.K)
+        exps = buf[off + t.mant_bytes:off + t.mant_bytes + t.exp_bytes].reshape(t.M, t.K // 64)
+        out.append((np.empty(t.M, np.float32), x[pos:pos + t.K], mant, exps, t.M, t.K))
+        pos += t.K
+    return out
 
 
 class ClockSampler:
@@ -181,11 +272,24 @@ def timed(torch, fn, steps, warmup, barrier):
     return s.elapsed_time(e) / 1e3
 
 
+def max_over_ranks(torch, dist, secs, dev, world):
+    t = torch.tensor([secs], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def guarded(fn, *a, **kw):
+    """A sub-record must never take the headline down with it."""
+    try:
+        return fn(*a, **kw)
+    except Exception as e:
+        return {"error": f"{type(e).__name__}: {str(e)[:300]}"}
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
-
-    from qwen_b200 import model, ops
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -205,67 +309,392 @@ def run_b200(args):
     hbm_peak, peak_kind = peaks()
     line = {"metric": METRIC, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int16xint8->fp32",
-            "data": "synthetic: weights N(0,0.02) packed BFP8 on device (seeded), activations N(0,1)"}
-
+            "data": "synthetic: weights N(0,0.02) packed BFP8 (seeded), activations N(0,1)"}
+    cpu_data = None
     if args.workload in ("stack", "gemv"):
-        shapes, desc = stack_shapes(args.workload)
-        nb = model.stack_bytes(shapes)
-        wbytes = nb["weights"]
-        copies = args.copies or max(2, math.ceil(L2_DEFEAT_BYTES / wbytes))
-        ds = model.DeviceStack(shapes, copies=copies, device=dev, seed=1234 + rank)
-        plans = [ops.LinearStack(ds.views(c)) for c in range(copies)]
-        launches_per_step = 2   # act_prep + gemv_warp
-
-        def step(i):
-            plans[i % copies].run()
-
-        # ------------------------------------------------ device-resident timing
-        clk = ClockSampler(gpu_uuid(torch, dev), dev.index or 0)
-        secs = timed(torch, step, args.steps, args.warmup, barrier)
-        clocks = clk.stop()
-        t = torch.tensor([secs], device=dev)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        secs = float(t.item())
-        per_step = secs / args.steps
-        value = world * nb["total"] / per_step / 1e9
-        kernel_gbs = nb["total"] / per_step / 1e9
-
-        # ------------------------------------------------ end to end, host buffers
-        e2e = None
-        if not args.no_e2e:
-            e2e = end_to_end(torch, dist, ds, plans, copies, nb, args, barrier, world, dev)
-        line.update({
-            "value": round(value, 2), "ms_per_step": round(per_step * 1e3, 4),
-            "config": {"workload": desc, "gemvs_per_step": len(shapes), "weight_bytes": wbytes,
-                       "algorithmic_bytes_per_step": nb["total"], "macs_per_step": nb["macs"],
-                       "l2": f"rotates {copies} weight copies ({copies * wbytes / 1e9:.2f} GB) > 126 MB L2",
-                       "launch": "act_prep + one grouped warp-autonomous kernel (PDL) per step", "parallelism": f"replicas x{world}"},
-            "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 2), "peak": hbm_peak, "unit": "GB/s",
-                         "frac": round(kernel_gbs / hbm_peak, 4), "peak_kind": peak_kind,
-                         "traffic": committed_traffic(args.workload),
-                         "kernel": "gemv_warp_kernel (grouped)"},
-            "e2e": e2e,
-            "gpu_launches": launches_per_step * args.steps,
-            "clocks": clocks,
-        })
-        for p in plans:
-            p.close()
+        rec, cpu_data = run_stack(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kind)
+        line.update(rec)
+        if args.workload == "stack" and world == 1 and not args.headline_only:
+            line["configs"] = run_configs(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kind)
+        if args.workload == "stack" and not args.headline_only and not args.no_sharded:
+            line["sharded"] = run_sharded_records(args, torch, dist, dev, barrier, world, rank, local, hbm_peak,
+                                                  peak_kind)
     elif args.workload == "sharded":
-        line.update(run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, peak_kind))
+        line.update(run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, peak_kind,
+                                args.batch, args.exchange, args.steps, args.warmup))
     elif args.workload == "batched":
-        line.update(run_batched(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kind))
+        line.update(run_batched(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kind, args.batch,
+                                args.steps, args.warmup))
     elif args.workload == "rtl20":
         line.update(run_rtl20(args, torch, dev, barrier, world, hbm_peak, peak_kind))
     else:
-        line.update(run_lm_head(args, torch, ops, dev, barrier, world, hbm_peak, peak_kind))
+        line.update(run_lm_head(args, torch, dev, barrier, world, hbm_peak, peak_kind, args.workload, args.steps,
+                                args.warmup))
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args.workload, args.batch)
+        line["cpu_baseline"] = cpu_baseline(args.workload, args.batch, cpu_data)
+    if cpu_data:
+        try:
+            os.unlink(cpu_data)
+        except OSError:
+            pass
     if world > 1:
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ headline
+def run_stack(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kind):
+    """The 0.8B linear stack (or the single cfg-0 GEMV) as one grouped launch
+    per token."""
+    import numpy as np
+
+    from qwen_b200 import model, ops
+
+    shapes, desc = stack_shapes(args.workload)
+    nb = model.stack_bytes(shapes)
+    wbytes = nb["weights"]
+    copies = args.copies or max(2, math.ceil(L2_DEFEAT_BYTES / wbytes))
+    hbuf, hx = synthetic_stack(shapes)
+    cpu_data = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # the reference-arm children read the same bytes
+        fd, cpu_data = tempfile.mkstemp(suffix=".npz", prefix="qwen_b200_bench_")
+        os.close(fd)
+        np.savez(cpu_data, buf=hbuf, x=hx)
+    ds = model.DeviceStack(shapes, copies=copies, device=dev, host_bytes=hbuf, host_x=hx)
+    del hbuf
+    plans = [ops.LinearStack(ds.views(c)) for c in range(copies)]
+    launches_per_step = 2   # act_prep + gemv_warp
+
+    def step(i):
+        plans[i % copies].run()
+
+    clk = ClockSampler(gpu_uuid(torch, dev), dev.index or 0)
+    secs = timed(torch, step, args.steps, args.warmup, barrier)
+    clocks = clk.stop()
+    per_step = max_over_ranks(torch, dist, secs, dev, world) / args.steps
+    value = world * nb["total"] / per_step / 1e9
+    kernel_gbs = nb["total"] / per_step / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = end_to_end(torch, dist, ds, plans, copies, nb, args, barrier, world, dev)
+    for p in plans:
+        p.close()
+    del ds, plans
+    torch.cuda.empty_cache()
+    return {
+        "value": round(value, 2), "ms_per_step": round(per_step * 1e3, 4),
+        "config": {"workload": desc, "gemvs_per_step": len(shapes), "weight_bytes": wbytes,
+                   "algorithmic_bytes_per_step": nb["total"], "macs_per_step": nb["macs"],
+                   "weights": "bench.synthetic_stack (the reference arm streams the same bytes)",
+                   "l2": f"rotates {copies} weight copies ({copies * wbytes / 1e9:.2f} GB) > 126 MB L2",
+                   "launch": "act_prep + one grouped warp-autonomous kernel (PDL) per step",
+                   "parallelism": f"replicas x{world}"},
+        "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 2), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(kernel_gbs / hbm_peak, 4), "peak_kind": peak_kind,
+                     "traffic": committed_traffic(args.workload), "kernel": "gemv_warp_kernel (grouped)"},
+        "e2e": e2e,
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+    }, cpu_data
+
+
+def end_to_end(torch, dist, ds, plans, copies, nb, args, barrier, world, dev):
+    """The same tokens through the public API with host buffers: every
+    token's activations copied in from pinned host memory, the stack run, its
+    outputs copied back.  Pipelined: two activation / output buffer sets, the
+    input copies on one copy stream and the output copies on another, so a
+    token's copies overlap the neighbouring tokens' kernels; the timed region
+    runs from an event every stream waits on to the last output copy.  The
+    serial figure has every copy in line with the kernels on one stream."""
+    from qwen_b200 import ops
+
+    hx = torch.empty(ds.x_flat.numel(), dtype=torch.float32, pin_memory=True)
+    hx.copy_(ds.x_flat.cpu())
+    hy = [torch.empty(ds.y_flat.numel(), dtype=torch.float32, pin_memory=True) for _ in range(2)]
+    xb = [ds.x_flat, torch.empty_like(ds.x_flat)]
+    yb = [ds.y_flat, torch.empty_like(ds.y_flat)]
+    pl = [plans, [ops.LinearStack(ds.views(c, xb[1], yb[1])) for c in range(copies)]]
+    cur = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    in_done = [torch.cuda.Event() for _ in range(2)]
+    run_done = [torch.cuda.Event() for _ in range(2)]
+    out_done = [torch.cuda.Event() for _ in range(2)]
+    for k in range(2):
+        for ev in (in_done[k], run_done[k], out_done[k]):
+            ev.record(cur)
+
+    def token(i):
+        k = i % 2
+        s_in.wait_event(run_done[k])            # the kernels two tokens back are done reading xb[k]
+        with torch.cuda.stream(s_in):
+            xb[k].copy_(hx, non_blocking=True)
+            in_done[k].record(s_in)
+        cur.wait_event(in_done[k])
+        cur.wait_event(out_done[k])             # yb[k] was copied out
+        pl[k][i % copies].run()
+        run_done[k].record(cur)
+        s_out.wait_event(run_done[k])
+        with torch.cuda.stream(s_out):
+            hy[k].copy_(yb[k], non_blocking=True)
+            out_done[k].record(s_out)
+
+    def run(n, base):
+        for i in range(n):
+            token(base + i)
+
+    def barrier_():
+        if world > 1:
+            dist.barrier()
+
+    run(args.warmup, 0)
+    torch.cuda.synchronize()
+    barrier_()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(cur)
+    s_in.wait_event(start)
+    s_out.wait_event(start)
+    run(args.steps, args.warmup)
+    cur.wait_event(out_done[0])
+    cur.wait_event(out_done[1])
+    end.record(cur)
+    torch.cuda.synchronize()
+    barrier_()
+    per = max_over_ranks(torch, dist, start.elapsed_time(end) / 1e3, dev, world) / args.steps
+
+    def serial_step(i):
+        ds.x_flat.copy_(hx, non_blocking=True)
+        plans[i % copies].run()
+        hy[0].copy_(ds.y_flat, non_blocking=True)
+
+    ser = max_over_ranks(torch, dist, timed(torch, serial_step, args.steps, args.warmup, barrier), dev, world)
+    ser /= args.steps
+    for p in pl[1]:
+        p.close()
+    return {"value": round(world * nb["total"] / per / 1e9, 2), "unit": "GB/s", "ms_per_step": round(per * 1e3, 4),
+            "h2d_bytes_per_step": hx.numel() * 4, "d2h_bytes_per_step": hy[0].numel() * 4,
+            "serial_value": round(world * nb["total"] / ser / 1e9, 2), "serial_ms_per_step": round(ser * 1e3, 4),
+            "path": "ops.LinearStack.run on the timed stream; torch pinned-memory copies on two copy streams"}
+
+
+# ------------------------------------------------------------------ sub-records (one GPU)
+def run_configs(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kind):
+    """The other BASELINE configurations, each a bounded run with its own
+    roofline (steps are kept short: these are reported beside the headline)."""
+    steps, warm = 20, 3
+    out = {}
+    out["cfg0_gemv_3584x1024"] = guarded(run_single_gemv, torch, dev, barrier, hbm_peak, peak_kind, steps, warm)
+    torch.cuda.empty_cache()
+    for w in ("lm_bf16", "lm_bfp8"):
+        out[f"cfg2_{w}"] = guarded(run_lm_head, args, torch, dev, barrier, world, hbm_peak, peak_kind, w, steps, warm)
+        torch.cuda.empty_cache()
+    for B in (8, 32, 128, 256):
+        out[f"cfg3_b{B}"] = guarded(run_batched, args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kind, B,
+                                    steps, warm, e2e=False)
+        torch.cuda.empty_cache()
+    out["chain"] = guarded(run_chain, torch, dev, barrier, hbm_peak, peak_kind, steps, warm)
+    torch.cuda.empty_cache()
+    out["abi"] = guarded(run_abi, torch, dev)
+    torch.cuda.empty_cache()
+    return out
+
+
+def graph_of(torch, fn, n):
+    """CUDA graph of n calls fn(0..n-1) (warmed up on a side stream first)."""
+    fn(0)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn(0)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(n):
+            fn(i)
+    return g
+
+
+def run_single_gemv(torch, dev, barrier, hbm_peak, peak_kind, steps, warm):
+    """one 3584 x 1024 GEMV per call through the device
+    entry point (one launch: every CTA quantizes x), timed as a CUDA graph of
+    one call per weight copy; `e2e` is the reference-facing bfp8_gemv with
+    host pointers (registered weights), per call."""
+    import numpy as np
+
+    from qwen_b200 import _lib, model, ops
+
+    L = _lib.load()
+    M, K = 3584, 1024
+    shapes = [model.Linear("mlp.up_proj", M, K)]
+    wbytes = M * K + M * K // 64
+    nbytes = wbytes + 4 * K + 4 * M
+    copies = max(2, math.ceil(L2_DEFEAT_BYTES / wbytes))
+    hbuf, hx = synthetic_stack(shapes)
+    ds = model.DeviceStack(shapes, copies=copies, device=dev, host_bytes=hbuf, host_x=hx)
+    views = [ds.views(c)[0] for c in range(copies)]
+    y = torch.empty(M, dtype=torch.float32, device=dev)
+
+    def call(i):
+        xx, m, e, _ = views[i % copies]
+        _lib.check(L.qwen_b200_gemv_dev(y.data_ptr(), xx.data_ptr(), m.data_ptr(), e.data_ptr(), M, K,
+                                        ops._stream()), "gemv")
+
+    graph = graph_of(torch, call, copies)
+    clk = ClockSampler(gpu_uuid(torch, dev), dev.index or 0)
+    per = timed(torch, lambda i: graph.replay(), steps, warm, barrier) / steps / copies
+    clocks = clk.stop()
+    del graph
+    gbs = nbytes / per / 1e9
+    # the drop-in: host x, host weights (registered once, like the engine's mmap), host y
+    (yh, xh, mh, eh, _, _), = stack_views(hbuf, hx, shapes)
+    L.qwen_b200_register_weights(hbuf.ctypes.data, hbuf.nbytes)
+    for _ in range(20):
+        L.bfp8_gemv(yh.ctypes.data, xh.ctypes.data, mh.ctypes.data, eh.ctypes.data, M, K)
+    n, t0 = 0, time.perf_counter()
+    while n < 200 or time.perf_counter() - t0 < 0.5:
+        L.bfp8_gemv(yh.ctypes.data, xh.ctypes.data, mh.ctypes.data, eh.ctypes.data, M, K)
+        n += 1
+    call_s = (time.perf_counter() - t0) / n
+    L.qwen_b200_forget_weights(hbuf.ctypes.data)
+    ok = bool(np.array_equal(yh.view(np.uint32), y.cpu().numpy().view(np.uint32)))
+    return {"value": round(gbs, 2), "unit": "GB/s", "us_per_call": round(per * 1e6, 3),
+            "config": {"workload": "single BFP8 GEMV 3584x1024, batch 1 (BASELINE config 0)",
+                       "algorithmic_bytes_per_step": nbytes, "launch": "CUDA graph of one call per copy",
+                       "l2": f"rotates {copies} weight copies ({copies * wbytes / 1e9:.2f} GB)"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind,
+                         "traffic": committed_traffic("gemv"), "kernel": "gemv_warp_kernel (res_act)"},
+            "e2e": {"value": round(nbytes / call_s / 1e9, 2), "unit": "GB/s", "us_per_call": round(call_s * 1e6, 2),
+                    "h2d_bytes_per_step": 4 * K, "d2h_bytes_per_step": 4 * M,
+                    "path": "bfp8_gemv drop-in, host pointers, weights registered", "same_bits_as_device": ok},
+            "clocks": clocks}
+
+
+def run_chain(torch, dev, barrier, hbm_peak, peak_kind, steps, warm):
+    """The 150 GEMVs of a token issued the way a decoder issues them, each a
+    dependent launch: per layer the rmsnorm -> projection pairs of the
+    attention / DeltaNet block (the first with the residual add in front),
+    its output projection (its input, the attention / DeltaNet output, is a
+    fixed vector: that glue is outside this path), then the MLP as residual
+    add + rmsnorm -> gate, rmsnorm -> up, swiglu -> down.  The token is one
+    CUDA graph per weight copy."""
+    from qwen_b200 import _lib, model, ops
+
+    L = _lib.load()
+    shapes = model.qwen35_08b_stack()
+    nb = model.stack_bytes(shapes)
+    copies = max(2, math.ceil(L2_DEFEAT_BYTES / nb["weights"]))
+    hbuf, hx = synthetic_stack(shapes)
+    ds = model.DeviceStack(shapes, copies=copies, device=dev, host_bytes=hbuf, host_x=hx)
+    del hbuf
+    H = model.HIDDEN
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    h0 = torch.randn(H, generator=g, device=dev)
+    ln = torch.randn(H, generator=g, device=dev) * 0.1
+    glue = torch.randn(2048, generator=g, device=dev)
+    hs = [torch.empty(H, device=dev) for _ in range(2)]
+    ys = [torch.empty(t.M, device=dev) for t in shapes]
+    st = lambda: ops._stream()   # noqa: E731
+    eps = 1e-6
+
+    def token(c):
+        views = ds.views(c)
+        h, nxt = h0, 0
+        res = None
+        i = 0
+        for l in range(model.LAYERS):
+            n_attn = 4 if l in model.FULL_ATTN else 3
+            proj = list(range(i, i + n_attn - 1))        # q/k/v or qkv/z: from rmsnorm(h)
+            o = i + n_attn - 1
+            gate, up, down = o + 1, o + 2, o + 3
+            for j, k in enumerate(proj):
+                _, m, e, _ = views[k]
+                t = shapes[k]
+                if j == 0 and res is not None:          # h = h + previous down, then its rmsnorm
+                    out = hs[nxt]
+                    _lib.check(L.qwen_b200_residual_rmsnorm_gemv_dev(
+                        ys[k].data_ptr(), out.data_ptr(), h.data_ptr(), res.data_ptr(), ln.data_ptr(), eps,
+                        m.data_ptr(), e.data_ptr(), t.M, t.K, st()), "chain")
+                    h, nxt = out, 1 - nxt
+                else:
+                    _lib.check(L.qwen_b200_rmsnorm_gemv_dev(ys[k].data_ptr(), h.data_ptr(), ln.data_ptr(), eps,
+                                                            m.data_ptr(), e.data_ptr(), t.M, t.K, st()), "chain")
+            _, m, e, _ = views[o]
+            t = shapes[o]
+            _lib.check(L.qwen_b200_gemv_dev(ys[o].data_ptr(), glue.data_ptr(), m.data_ptr(), e.data_ptr(), t.M, t.K,
+                                            st()), "chain")
+            out = hs[nxt]                                 # h = h + o, rmsnorm -> gate
+            _, m, e, _ = views[gate]
+            t = shapes[gate]
+            _lib.check(L.qwen_b200_residual_rmsnorm_gemv_dev(
+                ys[gate].data_ptr(), out.data_ptr(), h.data_ptr(), ys[o].data_ptr(), ln.data_ptr(), eps,
+                m.data_ptr(), e.data_ptr(), t.M, t.K, st()), "chain")
+            h, nxt = out, 1 - nxt
+            _, m, e, _ = views[up]
+            t = shapes[up]
+            _lib.check(L.qwen_b200_rmsnorm_gemv_dev(ys[up].data_ptr(), h.data_ptr(), ln.data_ptr(), eps,
+                                                    m.data_ptr(), e.data_ptr(), t.M, t.K, st()), "chain")
+            _, m, e, _ = views[down]
+            t = shapes[down]
+            _lib.check(L.qwen_b200_swiglu_gemv_dev(ys[down].data_ptr(), ys[gate].data_ptr(), ys[up].data_ptr(),
+                                                   m.data_ptr(), e.data_ptr(), t.M, t.K, st()), "chain")
+            res = ys[down]
+            i = down + 1
+        assert i == len(shapes)
+
+    graphs = [graph_of(torch, lambda _i, c=c: token(c), 1) for c in range(copies)]
+    clk = ClockSampler(gpu_uuid(torch, dev), dev.index or 0)
+    per = timed(torch, lambda i: graphs[i % copies].replay(), steps, warm, barrier) / steps
+    clocks = clk.stop()
+    del graphs
+    gbs = nb["total"] / per / 1e9
+    return {"value": round(gbs, 2), "unit": "GB/s", "ms_per_token": round(per * 1e3, 4),
+            "config": {"workload": "qwen35-0.8b linear stack as a token issues it: 150 dependent GEMV launches "
+                                   "(rmsnorm / residual / swiglu fused in front), one CUDA graph per token",
+                       "algorithmic_bytes_per_step": nb["total"],
+                       "l2": f"rotates {copies} weight copies"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind,
+                         "kernel": "gemv_warp_kernel (res_act, 150 launches)"},
+            "gpu_launches_per_token": len(shapes), "clocks": clocks}
+
+
+def run_abi(torch, dev):
+    """The reference-facing drop-in as the engine calls it: 150 synchronous
+    bfp8_gemv calls per token with host pointers into the (registered)
+    weight image and host activations / outputs."""
+    from qwen_b200 import _lib, model
+
+    L = _lib.load()
+    shapes = model.qwen35_08b_stack()
+    nb = model.stack_bytes(shapes)
+    hbuf, hx = synthetic_stack(shapes)
+    ents = stack_views(hbuf, hx, shapes)
+    L.qwen_b200_register_weights(hbuf.ctypes.data, hbuf.nbytes)
+
+    def token():
+        for y, x, m, e, M, K in ents:
+            L.bfp8_gemv(y.ctypes.data, x.ctypes.data, m.ctypes.data, e.ctypes.data, M, K)
+
+    token()
+    n, t0 = 0, time.perf_counter()
+    while n < 3 or (time.perf_counter() - t0 < 2.0 and n < 50):
+        token()
+        n += 1
+    per = (time.perf_counter() - t0) / n
+    L.qwen_b200_forget_weights(hbuf.ctypes.data)
+    return {"value": round(nb["total"] / per / 1e9, 2), "unit": "GB/s", "ms_per_token": round(per * 1e3, 3),
+            "us_per_call": round(per / len(shapes) * 1e6, 2), "tokens_timed": n,
+            "config": {"workload": "150 bfp8_gemv drop-in calls per token, host pointers (the engine's ctypes "
+                                   "loop, qwen_real_engine.py:1073-1087), weights registered once",
+                       "algorithmic_bytes_per_step": nb["total"]},
+            "h2d_bytes_per_step": 4 * sum(t.K for t in shapes), "d2h_bytes_per_step": 4 * sum(t.M for t in shapes)}
 
 
 def int8_peak_tops(torch, dev):
@@ -288,7 +717,10 @@ def int8_peak_tops(torch, dev):
     return 2 * n ** 3 / best / 1e12
 
 
-def run_batched(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kind):
+_INT8_PEAK = {}
+
+
+def run_batched(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kind, B, steps, warmup, e2e=True):
     """B sequences x the 0.8B linear stack, one grouped
     tcgen05 kind::i8 launch per step (150 GEMMs).  Activations enter as
     planar int16 (hi/lo int8 planes + block scales, the quantizer's output);
@@ -296,22 +728,20 @@ def run_batched(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kin
     together (> 4 GB), so no step finds its inputs in L2."""
     from qwen_b200 import model, ops
 
-    B = args.batch
     shapes = model.qwen35_08b_stack()
     nb = model.batched_bytes(shapes, B)
     copies = args.copies or max(2, math.ceil(L2_DEFEAT_BYTES / nb["weights"]))
     ds = model.DeviceStack(shapes, copies=copies, device=dev, seed=1234 + rank)
     db = model.DeviceBatch(shapes, B, sets=copies, device=dev, seed=77 + rank)
     plans = [ops.BatchedStack(db.items(ds.views(c), c)) for c in range(copies)]
-    p_int8 = int8_peak_tops(torch, dev)
+    if dev.index not in _INT8_PEAK:
+        _INT8_PEAK[dev.index] = int8_peak_tops(torch, dev)
+    p_int8 = _INT8_PEAK[dev.index]
 
     clk = ClockSampler(gpu_uuid(torch, dev), dev.index or 0)
-    secs = timed(torch, lambda i: plans[i % copies].run(), args.steps, args.warmup, barrier)
+    secs = timed(torch, lambda i: plans[i % copies].run(), steps, warmup, barrier)
     clocks = clk.stop()
-    t = torch.tensor([secs], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    per_step = float(t.item()) / args.steps
+    per_step = max_over_ranks(torch, dist, secs, dev, world) / steps
     gbs = nb["total"] / per_step / 1e9
     tops = nb["tensor_ops"] / per_step / 1e12
     t_hbm = nb["total"] / (hbm_peak * 1e9)
@@ -328,8 +758,8 @@ def run_batched(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kin
                  "hbm_frac": round(gbs / hbm_peak, 4), "tensor_frac": round(tops / p_int8, 4),
                  "int8_peak_tops": round(p_int8, 1)})
 
-    e2e = None
-    if not args.no_e2e:
+    e2e_rec = None
+    if e2e and not args.no_e2e:
         s0 = db.sets[0]
         hp = torch.empty(s0["planes"].numel(), dtype=torch.int8, pin_memory=True)
         hs = torch.empty(s0["scales"].numel(), dtype=torch.float32, pin_memory=True)
@@ -344,17 +774,14 @@ def run_batched(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kin
             plans[i % copies].run()
             hy.copy_(st["y"], non_blocking=True)
 
-        esecs = timed(torch, e2e_step, args.steps, args.warmup, barrier)
-        te = torch.tensor([esecs], device=dev)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        eper = float(te.item()) / args.steps
-        e2e = {"value": round(world * nb["total"] / eper / 1e9, 2), "unit": "GB/s",
-               "ms_per_step": round(eper * 1e3, 4), "tokens_per_s": round(world * B / eper, 1),
-               "h2d_bytes_per_step": hp.numel() + hs.numel() * 4, "d2h_bytes_per_step": hy.numel() * 4}
+        eper = max_over_ranks(torch, dist, timed(torch, e2e_step, steps, warmup, barrier), dev, world) / steps
+        e2e_rec = {"value": round(world * nb["total"] / eper / 1e9, 2), "unit": "GB/s",
+                   "ms_per_step": round(eper * 1e3, 4), "tokens_per_s": round(world * B / eper, 1),
+                   "h2d_bytes_per_step": hp.numel() + hs.numel() * 4, "d2h_bytes_per_step": hy.numel() * 4}
     for p in plans:
         p.close()
-    return {"value": round(world * gbs, 2), "ms_per_step": round(per_step * 1e3, 4), "dtype": "int8xint8->int32 (hi/lo planes)->fp32",
+    return {"value": round(world * gbs, 2), "ms_per_step": round(per_step * 1e3, 4),
+            "dtype": "int8xint8->int32 (hi/lo planes)->fp32",
             "config": {"workload": f"batched decode: B={B} sequences x qwen35-0.8b linear stack (150 BFP8 GEMMs)",
                        "batch": B, "gemms_per_step": len(shapes), "weight_bytes": nb["weights"],
                        "algorithmic_bytes_per_step": nb["total"], "macs_per_step": nb["macs"] * B,
@@ -363,113 +790,116 @@ def run_batched(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kin
                        "l2": f"rotates {copies} weight copies + activation sets "
                              f"({copies * nb['weights'] / 1e9:.2f} GB weights) > 126 MB L2",
                        "launch": "one grouped tcgen05 kernel per step", "parallelism": f"replicas x{world}"},
-            "roofline": roof, "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks}
+            "roofline": roof, "e2e": e2e_rec, "gpu_launches": steps, "clocks": clocks}
 
 
-def run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, peak_kind):
+# ------------------------------------------------------------------ multi-GPU (config 4)
+def run_sharded_records(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, peak_kind):
+    """Config 4 beside the headline, on every N: batch 1 with the kernels'
+    peer stores and with NCCL all-gathers, batch 64 with peer stores."""
+    out = {}
+    for key, B, ex in (("b1_peer", 1, "peer"), ("b1_nccl", 1, "nccl"), ("b64_peer", 64, "peer")):
+        out[key] = run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, peak_kind, B, ex,
+                               10, 3, check_parity=True)
+        torch.cuda.empty_cache()
+    return out
+
+
+def run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, peak_kind, B, exchange, steps, warmup,
+                check_parity=True):
     """8 layers x (gate, up 28672x8192; down 8192x28672),
-    batch 1, output rows sharded over the ranks; the rows reach every GPU
-    through the GEMV kernel's own peer stores (--exchange peer) or an NCCL
-    all-gather after every projection.  Total work is fixed as N grows
-    (strong scaling)."""
+    output rows sharded over the ranks; per layer the shard-local swiglu +
+    quantizer's int16 activation and the down rows reach every GPU through
+    the kernels' own peer stores (peer) or NCCL all-gathers.  Total work is
+    fixed as N grows (strong scaling).  Parity: rank 0 runs the same steps
+    on its own GPU alone and compares every layer's gathered activation and
+    down output bit for bit (batch 1; the fast arithmetic cuts K at fixed
+    steps, so the bits do not depend on N) or within 1e-4 of the output scale
+    (batch 64: stream-K groups the fp32 sums by the total work)."""
+    import numpy as np
+
     from qwen_b200 import sharded
 
     layers = sharded.scaled_layers()
     full_w = sum(t.M * t.K + t.M * t.K // 64 for L in layers for t in (L.gate, L.up, L.down))
     copies = args.copies or max(1, math.ceil(L2_DEFEAT_BYTES / (full_w / world)))
-    B = args.batch
-    st = sharded.ShardedDeviceStack(layers, world, rank, dev, copies=copies, seed=11, fast=True,
-                                    exchange=args.exchange, batch=B)
+    st = sharded.ShardedDeviceStack(layers, world, rank, dev, copies=copies, seed=11, fast=True, exchange=exchange,
+                                    batch=B)
     clk = ClockSampler(gpu_uuid(torch, dev), local)
-    secs = timed(torch, lambda i: st.step(i % copies), args.steps, args.warmup, barrier)
+    secs = timed(torch, lambda i: st.step(i % copies), steps, warmup, barrier)
     clocks = clk.stop()
-    t = torch.tensor([secs], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    per_step = float(t.item()) / args.steps
+    per_step = max_over_ranks(torch, dist, secs, dev, world) / steps
     nbytes = st.bytes_per_step()
-    if args.exchange == "peer" and st.device_error():
-        raise RuntimeError("sharded: a peer flag wait timed out")
+    xbytes = st.exchange_bytes_per_step()
+    err = st.device_error() if exchange == "peer" else 0
+    parity = None
+    if check_parity:
+        torch.cuda.synchronize()
+        mine = st.outputs() if B == 1 else st.final_output().cpu().numpy()
+        if world == 1:
+            parity = {"ok": True, "how": "one GPU: the run is its own reference"}
+        elif rank == 0:
+            ref = sharded.ShardedDeviceStack(layers, 1, 0, dev, copies=1, seed=11, fast=True, exchange="nccl",
+                                             batch=B)
+            ref.step()
+            torch.cuda.synchronize()
+            if B == 1:
+                same = bool(np.array_equal(mine, ref.outputs()))
+                parity = {"ok": same, "how": "every layer's gathered int16 activation + scales and down output "
+                                             "vs one GPU, bit for bit"}
+            else:
+                r = ref.final_output().cpu().numpy()
+                rel = float(np.max(np.abs(mine - r)) / max(np.max(np.abs(r)), 1e-30))
+                parity = {"ok": rel <= 1e-4, "max_abs_diff_over_scale": rel,
+                          "how": "last layer's down output vs one GPU, within 1e-4 of its scale (stream-K)"}
+            ref.close()
+            del ref
+        barrier()
     st.close()
+    del st
     per_rank_gbs = nbytes / world / per_step / 1e9
-    return {"value": round(nbytes / per_step / 1e9, 2), "ms_per_step": round(per_step * 1e3, 4), "scaling": "strong",
-            "config": {"workload": f"scaled BFP8 stack: 8 x (gate/up 28672x8192, down 8192x28672), batch {B}",
-                       "arithmetic": "fast (split-K, fma per block; within 1e-5 of the exact order)" if B == 1 else
-                                     "tcgen05 kind::i8 over hi/lo int8 planes, exact int32 block dots",
-                       "algorithmic_bytes_per_step": nbytes, "weight_bytes": full_w,
-                       "parallelism": f"output rows sharded x{world}, " + (
-                           "GEMV epilogue stores rows into every GPU over NVLink, epoch flags between launches"
-                           if args.exchange == "peer" else "NCCL all-gather after each projection"),
-                       "l2": f"rotates {copies} copies of this rank's {full_w / world / 1e9:.2f} GB"},
-            "roofline": {"bound": "hbm", "achieved": round(per_rank_gbs, 2), "peak": hbm_peak, "unit": "GB/s",
-                         "frac": round(per_rank_gbs / hbm_peak, 4), "peak_kind": peak_kind, "traffic": None,
-                         "kernel": ("gemv_warp_kernel" if B == 1 else "gemm_tc_kernel") +
-                                   " per rank (per-rank GB/s incl. the exchange)"},
-            # 2 grouped launches per layer x (act_prep + gemv_warp, or quant_planes + gemm_tc); NCCL not counted
-            "gpu_launches": args.steps * len(layers) * 4,
-            "exchange": args.exchange,
-            "clocks": clocks}
+    rec = {"value": round(nbytes / per_step / 1e9, 2), "unit": "GB/s", "ms_per_step": round(per_step * 1e3, 4),
+           "scaling": "strong",
+           "config": {"workload": f"scaled BFP8 stack: 8 x (gate/up 28672x8192, down 8192x28672), batch {B}",
+                      "arithmetic": "fast (K cut at fixed 1 KB steps, fma per block; within 1e-5 of the exact order)"
+                                    if B == 1 else "tcgen05 kind::i8 over hi/lo int8 planes, exact int32 block dots",
+                      "algorithmic_bytes_per_step": nbytes, "weight_bytes": full_w,
+                      "exchange_bytes_per_rank_per_step": xbytes,
+                      "parallelism": f"output rows sharded x{world}; per layer gate/up local, swiglu + quantizer "
+                                     "shard-local, int16 activation and fp32 down rows to every GPU by " + (
+                                         "the kernels' NVLink stores, epoch flags between launches"
+                                         if exchange == "peer" else "NCCL all-gathers"),
+                      "l2": f"rotates {copies} copies of this rank's {full_w / world / 1e9:.2f} GB"},
+           "roofline": {"bound": "hbm", "achieved": round(per_rank_gbs, 2), "peak": hbm_peak, "unit": "GB/s",
+                        "frac": round(per_rank_gbs / hbm_peak, 4), "peak_kind": peak_kind, "traffic": None,
+                        "kernel": ("gemv_warp_kernel" if B == 1 else "gemm_tc_kernel") +
+                                  " per rank (per-rank GB/s incl. the exchange)"},
+           # per layer: gate/up (quantizer + GEMV), activation, down (quantizer + GEMV / GEMM); NCCL not counted
+           "gpu_launches": steps * len(layers) * (5 if B == 1 else 4),
+           "exchange": exchange, "parity": parity, "clocks": clocks}
+    if err:
+        rec["device_error"] = err
+    return rec
 
 
-def end_to_end(torch, dist, ds, plans, copies, nb, args, barrier, world, dev):
-    """The same token through the public API with host buffers: the step's
-    activations copied in from pinned host memory, the stack run, its
-    outputs copied back, all on the timed stream."""
-    hx = torch.empty(ds.x_flat.numel(), dtype=torch.float32, pin_memory=True)
-    hx.copy_(ds.x_flat.cpu())
-    hy = torch.empty(ds.y_flat.numel(), dtype=torch.float32, pin_memory=True)
-
-    def e2e_step(i):
-        ds.x_flat.copy_(hx, non_blocking=True)
-        plans[i % copies].run()
-        hy.copy_(ds.y_flat, non_blocking=True)
-
-    esecs = timed(torch, e2e_step, args.steps, args.warmup, barrier)
-    te = torch.tensor([esecs], device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    esecs = float(te.item())
-    return {"value": round(world * nb["total"] / (esecs / args.steps) / 1e9, 2), "unit": "GB/s",
-            "ms_per_step": round(esecs / args.steps * 1e3, 4),
-            "h2d_bytes_per_step": hx.numel() * 4, "d2h_bytes_per_step": hy.numel() * 4}
-
-
-def graph_of(torch, fn, n):
-    """CUDA graph of n calls fn(0..n-1) (warmed up on a side stream first)."""
-    fn(0)
-    torch.cuda.synchronize()
-    side = torch.cuda.Stream()
-    side.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(side):
-        fn(0)
-    torch.cuda.current_stream().wait_stream(side)
-    torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        for i in range(n):
-            fn(i)
-    return g
-
-
-def run_lm_head(args, torch, ops, dev, barrier, world, hbm_peak, peak_kind):
-    """Secondary lines: the 65536 x 1024 lm_head (bf16 table or BFP8 matrix)
-    fused with argmax and top-40.  `value` times the kernels alone: each
-    step replays a CUDA graph of one call per table copy (no per-call host
-    work); `e2e` calls the reference-facing host API (lm_head_topk with a
-    host h and a registered host table for bf16; the BFP8 device call with
-    h copied in and the ids and scores copied out otherwise)."""
-    import ctypes
-
+# ------------------------------------------------------------------ lm_head / rtl20
+def run_lm_head(args, torch, dev, barrier, world, hbm_peak, peak_kind, workload, steps, warmup):
+    """The 65536 x 1024 lm_head (bf16 table or BFP8 matrix) fused with
+    argmax and top-40.  `value` times the kernels alone: each step replays a
+    CUDA graph of one call per table copy (no per-call host work); `e2e`
+    calls the reference-facing host API (lm_head_topk with a host h and a
+    registered host table for bf16; the BFP8 device call with h copied in and
+    the ids and scores copied out otherwise)."""
     import numpy as np
 
-    from qwen_b200 import _lib
+    from qwen_b200 import _lib, ops
 
     V, H, k = 65536, 1024, 40
     g = torch.Generator(device=dev)
     g.manual_seed(7)
     w = torch.randn((V, H), generator=g, device=dev) * 0.02
     h = torch.randn(H, generator=g, device=dev)
-    if args.workload == "lm_bf16":
+    if workload == "lm_bf16":
         tab = w.to(torch.bfloat16).view(torch.int16)
         per = V * H * 2
         copies = max(2, math.ceil(L2_DEFEAT_BYTES / per))
@@ -484,7 +914,7 @@ def run_lm_head(args, torch, ops, dev, barrier, world, hbm_peak, peak_kind):
         per = V * H + V * H // 64
         copies = max(2, math.ceil(L2_DEFEAT_BYTES / per))
         mats = [(mant, exps)] + [(mant.clone(), exps.clone()) for _ in range(copies - 1)]
-        res = ops.lm_outputs(dev, k)   # preallocated: the timed graph holds only the lm_head kernels
+        res = ops.lm_outputs(dev, k)
 
         def call(i):
             m, e = mats[i % copies]
@@ -492,18 +922,18 @@ def run_lm_head(args, torch, ops, dev, barrier, world, hbm_peak, peak_kind):
         desc = "BFP8 lm_head 65536x1024 + argmax + top-40"
     graph = graph_of(torch, call, copies)
     clk = ClockSampler(gpu_uuid(torch, dev), dev.index or 0)
-    secs = timed(torch, lambda i: graph.replay(), args.steps, args.warmup, barrier)
+    secs = timed(torch, lambda i: graph.replay(), steps, warmup, barrier)
     clocks = clk.stop()
-    per_step = secs / args.steps / copies   # one lm_head per table copy in each replay
+    del graph
+    per_step = secs / steps / copies   # one lm_head per table copy in each replay
     nbytes = per + 4 * H
     gbs = nbytes / per_step / 1e9
 
-    # end to end through the host API
     L = _lib.load()
     hh = h.cpu().numpy().astype(np.float32)
     ids = np.zeros(k, np.int32)
     scs = np.zeros(k, np.float32)
-    if args.workload == "lm_bf16":
+    if workload == "lm_bf16":
         host_tab = w[:].to(torch.bfloat16).view(torch.int16).cpu().numpy()
         L.qwen_b200_register_weights(host_tab.ctypes.data, host_tab.nbytes)
 
@@ -523,25 +953,27 @@ def run_lm_head(args, torch, ops, dev, barrier, world, hbm_peak, peak_kind):
             hi[:k].copy_(r.ids[:k], non_blocking=True)
             hs.copy_(r.scores[:k], non_blocking=True)
             hi[k:k + 1].copy_(r.argmax, non_blocking=True)
-    for i in range(args.warmup):
+    for i in range(warmup):
         e2e_call(i)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    for i in range(args.steps):
+    for i in range(steps):
         e2e_call(i)
     torch.cuda.synchronize()
-    e2e_step = (time.perf_counter() - t0) / args.steps
+    e2e_step = (time.perf_counter() - t0) / steps
+    if workload == "lm_bf16":
+        L.qwen_b200_forget_weights(host_tab.ctypes.data)
     del w
-    return {"value": round(world * gbs, 2), "ms_per_step": round(per_step * 1e3, 4),
+    return {"value": round(world * gbs, 2), "unit": "GB/s", "ms_per_step": round(per_step * 1e3, 4),
             "config": {"workload": desc, "algorithmic_bytes_per_step": nbytes,
                        "l2": f"rotates {copies} copies", "launch": "CUDA graph of one call per copy"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind,
-                         "traffic": committed_traffic(args.workload)},
+                         "traffic": committed_traffic(workload)},
             "e2e": {"value": round(world * nbytes / e2e_step / 1e9, 2), "unit": "GB/s",
                     "ms_per_step": round(e2e_step * 1e3, 4), "h2d_bytes_per_step": 4 * H,
                     "d2h_bytes_per_step": 8 * k + 4},
-            "gpu_launches": args.steps * copies, "clocks": clocks}
+            "gpu_launches": steps * copies, "clocks": clocks}
 
 
 def run_rtl20(args, torch, dev, barrier, world, hbm_peak, peak_kind):
@@ -550,8 +982,6 @@ def run_rtl20(args, torch, dev, barrier, world, hbm_peak, peak_kind):
     kernel alone (a CUDA graph of one call per weight copy); `exact_ms`
     times the exact-mode single GEMV entry the same way; `e2e` copies x in
     and the words out around each call."""
-    import numpy as np
-
     from qwen_b200 import _lib, model, ops
 
     L = _lib.load()
@@ -622,48 +1052,102 @@ def run_rtl20(args, torch, dev, barrier, world, hbm_peak, peak_kind):
             "gpu_launches": args.steps * copies, "clocks": clocks}
 
 
-# ------------------------------------------------------------------ reference arm
-def reference_stack_runner(workload, seed=7):
-    """The reference's own bfp8_gemv (oracle/_ref/libref_kernels.so, built
-    from 04-板载脚本与工具/qwen_kernels_opt.c) over the workload's GEMVs."""
+# ------------------------------------------------------------------ reference arm / CPU baseline
+def _omp_threads(n):
+    """Set the OpenMP team size of the reference library (libgomp reads
+    OMP_NUM_THREADS once, when it loads; torchrun exports 1), and return the
+    size OpenMP reports."""
+    import ctypes
+
+    try:
+        gomp = ctypes.CDLL("libgomp.so.1")
+        gomp.omp_set_num_threads(int(n))
+        return int(gomp.omp_get_max_threads())
+    except OSError:
+        return int(n)
+
+
+def cpu_runner(kind, workload, data_path=""):
+    """(token function, shapes, description, cores) of one CPU row over the
+    workload's GEMVs on the synthetic stack's bytes:
+      ref       the reference's own C bfp8_gemv (oracle/_ref, built from
+                04-板载脚本与工具/qwen_kernels_opt.c; x86 has no NEON, so its
+                scalar float path), OpenMP with every host thread
+      ref2      the same with 2 threads (the board's core count)
+      numpy     the reference engine's numpy fallback (qwen_real_engine.py:
+                1233-1239), restated in oracle/oracle.py and pinned to it
+      oracle    the NEON-order int16 restatement (oracle/bfp8_oracle.c), one thread"""
     import ctypes
 
     import numpy as np
 
-    lib = ctypes.CDLL(os.path.join(REPO, "oracle", "_ref", "libref_kernels.so"))
-    P, I = ctypes.c_void_p, ctypes.c_int
-    lib.bfp8_gemv.argtypes = [P, P, P, P, I, I]
-    lib.bfp8_gemv.restype = None
-    lib.init_kernels()
-    shapes, desc = stack_shapes("stack" if workload == "batched" else workload)
-    rng = np.random.default_rng(seed)
-    ents = []
-    for t in shapes:
-        mant = rng.integers(-128, 128, (t.M, t.K), dtype=np.int8)
-        exps = rng.integers(118, 131, (t.M, t.K // 64), dtype=np.uint8)
-        x = rng.standard_normal(t.K, dtype=np.float32)
-        y = np.empty(t.M, np.float32)
-        ents.append((y, x, mant, exps, t.M, t.K))
+    shapes, desc = stack_shapes("stack" if workload in ("batched",) else workload)
+    if data_path:
+        d = np.load(data_path)
+        buf, x = d["buf"], d["x"]
+    else:
+        buf, x = synthetic_stack(shapes)
+    ents = stack_views(buf, x, shapes)
+    if kind in ("ref", "ref2"):
+        cores = _omp_threads(os.cpu_count() if kind == "ref" else 2)
+        lib = ctypes.CDLL(os.path.join(REPO, "oracle", "_ref", "libref_kernels.so"))
+        P, I = ctypes.c_void_p, ctypes.c_int
+        lib.bfp8_gemv.argtypes = [P, P, P, P, I, I]
+        lib.bfp8_gemv.restype = None
+        lib.init_kernels()
+        cores = _omp_threads(cores)
+
+        def token():
+            for y, xx, m, e, M, K in ents:
+                lib.bfp8_gemv(y.ctypes.data, xx.ctypes.data, m.ctypes.data, e.ctypes.data, M, K)
+        label = (f"reference C bfp8_gemv (scalar build, OpenMP {cores} threads)")
+        return token, shapes, desc, cores, label, buf
+    from oracle import oracle as O
+
+    if kind == "numpy":
+        def token():
+            for y, xx, m, e, M, K in ents:
+                y[:] = O.bfp8_gemv_numpy(xx, m, e)
+        return token, shapes, desc, 1, "reference engine numpy fallback (restated in oracle/)", buf
 
     def token():
-        for y, x, m, e, M, K in ents:
-            lib.bfp8_gemv(y.ctypes.data, x.ctypes.data, m.ctypes.data, e.ctypes.data, M, K)
-    return token, shapes, desc
+        for y, xx, m, e, M, K in ents:
+            y[:] = O.bfp8_gemv(xx, m, e)
+    return token, shapes, desc, 1, "oracle: NEON-order int16 restatement, one thread", buf
 
 
-def cpu_baseline(workload, batch=1):
-    """Bounded sample of the reference C on this host's cores, in a child
-    process so OpenMP starts with every host thread."""
+def cpu_baseline(workload, batch=1, data_path=None):
+    """Bounded samples of the CPU rows on this host, each in a child
+    process (OpenMP starts with the thread count the row asks for)."""
     if workload not in ("stack", "gemv", "batched"):
         return None
-    env = dict(os.environ, OMP_NUM_THREADS=str(os.cpu_count()))
+    rows = []
+    for kind in ("ref", "ref2", "numpy", "oracle"):
+        env = dict(os.environ, OMP_NUM_THREADS=str(os.cpu_count() if kind == "ref" else 2 if kind == "ref2" else 1))
+        cmd = [sys.executable, os.path.abspath(__file__), "--impl", "reference", "--cpu-sample", "--cpu-kind", kind,
+               "--workload", workload, "--batch", str(batch)]
+        if data_path:
+            cmd += ["--cpu-data", data_path]
+        try:
+            out = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+            rows.append(json.loads(out.stdout.strip().splitlines()[-1]))
+        except Exception as e:  # a baseline failure must not hide the GPU number
+            rows.append({"kind": kind, "error": str(e)[:200]})
+    main = dict(rows[0]) if rows and "value" in rows[0] else {"error": "reference row failed"}
+    main["rows"] = rows
+    main["host_cpu"] = _cpu_model()
+    return main
+
+
+def _cpu_model():
     try:
-        out = subprocess.run([sys.executable, os.path.abspath(__file__), "--impl", "reference", "--cpu-sample",
-                              "--workload", workload, "--batch", str(batch)], env=env, capture_output=True, text=True,
-                             timeout=300)
-        return json.loads(out.stdout.strip().splitlines()[-1])
-    except Exception as e:  # a baseline failure must not hide the GPU number
-        return {"error": str(e)[:200]}
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
 
 
 def run_reference(args):
@@ -675,27 +1159,28 @@ def run_reference(args):
         return
     from qwen_b200 import model
 
-    token, shapes, desc = reference_stack_runner(args.workload)
+    kind = args.cpu_kind if args.cpu_sample else "ref"
+    token, shapes, desc, cores, label, _buf = cpu_runner(kind, args.workload, args.cpu_data)
     nb = model.stack_bytes(shapes)
     # the reference has no batched path: B sequences cost B one-sequence passes
     seqs = args.batch if args.workload == "batched" else 1
     if seqs > 1:
         nb = model.batched_bytes(shapes, seqs)
         desc = f"batched decode: B={seqs} sequences x {desc}, one sequence at a time"
-    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count()))
+    ref_kind = "reference" if kind in ("ref", "ref2") else "port"
     if args.cpu_sample:
-        # bounded sample: whole tokens for ~10 s (at least 2)
+        # bounded sample: whole passes of the stack for ~6 s (at least 1)
+        budget = 6.0
         token()
         n, t0 = 0, time.perf_counter()
-        while n < 2 or (time.perf_counter() - t0 < 10.0 and n < 1000):
+        while n < 1 or (time.perf_counter() - t0 < budget and n < 1000):
             token()
             n += 1
         dt = (time.perf_counter() - t0) / n * seqs
         print(json.dumps({"value": round(nb["total"] / dt / 1e9, 4), "unit": "GB/s", "ms_per_step": round(dt * 1e3, 3),
-                          "cores": cores, "kind": "reference",
+                          "cores": cores, "kind": ref_kind, "row": kind,
                           "sample": f"{n} whole one-sequence passes of the stack after 1 warm-up pass, scaled by "
-                                    f"{seqs} sequences per step ({desc}); reference C bfp8_gemv scalar build, "
-                                    "OpenMP"}))
+                                    f"{seqs} sequences per step ({desc}); {label}; the B200 arm's packed bytes"}))
         return
     for _ in range(args.warmup):
         token()
@@ -709,10 +1194,11 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (reference scalar path)",
-        "data": "synthetic: random int8 mantissas, exponents 118..130, activations N(0,1)",
+        "data": "synthetic: the B200 arm's packed bytes (bench.synthetic_stack: N(0,0.02) weights, N(0,1) "
+                "activations)",
         "config": {"workload": desc, "algorithmic_bytes_per_step": nb["total"]},
         "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "reference",
-                         "sample": f"{args.steps} whole tokens after {args.warmup} warm-up tokens"},
+                         "sample": f"{args.steps} whole tokens after {args.warmup} warm-up tokens; {label}"},
         "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -724,7 +1210,9 @@ def main():
     if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
         os.environ["NCCL_DEBUG"] = "WARN"
     if args.impl == "reference":
-        os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count()))
+        if not args.cpu_sample:
+            # every host thread, also under torchrun (which exports OMP_NUM_THREADS=1)
+            os.environ["OMP_NUM_THREADS"] = str(os.cpu_count())
         run_reference(args)
     else:
         run_b200(args)

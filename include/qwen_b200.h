@@ -215,6 +215,14 @@ QB_API int qwen_b200_stack_create(int n, const int8_t* const* mant, const uint8_
  * qwen_b200_gemv_fast_dev() and lets rows of deep matrices be split into K
  * segments (for stacks with few rows per GPU, e.g. row-sharded ones). */
 #define QB_STACK_FAST 1
+/* With QB_STACK_FAST: cut every row's K into fixed 1 KB segments, so where a
+ * row is split depends on K alone -- a row-sharded plan then gives every row
+ * the same bits as the unsharded plan, on any number of GPUs. */
+#define QB_STACK_FIXED_SPLIT 2
+/* x[i] is an already quantized activation record: int16 xq [K] followed by
+ * fp32 block scales xs [K/64] (16-byte aligned), as
+ * qwen_b200_swiglu_quant_sharded_dev writes it. */
+#define QB_STACK_Q_INPUT 4
 QB_API int qwen_b200_stack_create_ex(int n, const int8_t* const* mant, const uint8_t* const* exps,
                               const float* const* x, float* const* y, const int* M, const int* K, int flags);
 QB_API int qwen_b200_stack_run(int plan, void* stream);
@@ -242,6 +250,29 @@ QB_API int qwen_b200_stack_create_sharded(int n, const int8_t* const* mant, cons
  * wait_flags is this rank's own; epochs grow by one per launch on all ranks. */
 QB_API int qwen_b200_stack_run_sync(int plan, void* stream, const unsigned int* wait_flags, unsigned int wait_epoch,
                                     unsigned int* const* sig_flags, unsigned int sig_epoch, int world, int rank);
+/* The MLP activation of a row-sharded layer, computed shard-locally: this
+ * rank holds elements [col0, col0 + n) of the gate and up projections of
+ * each of B batch rows (row stride ld_in floats); every element gets the
+ * reference's swiglu (NEON build, qwen_kernels_opt.c:332-386) and every
+ * 64-block the reference quantizer (quant_x_blocks, :182-205) -- slices are
+ * whole blocks, so the bits equal the unsharded activation's -- and the
+ * quantized slice is stored into each of the ndst buffers (this GPU's input
+ * of the down projection, then the other ranks' copies mapped with
+ * qwen_b200_ipc_open): planar == 0 (B == 1) the record of QB_STACK_Q_INPUT
+ * (xq int16 [K], xs fp32 [K/64]); planar == 1 the tcgen05 input, planes
+ * int8 [2][B][K] then xs_t fp32 [K/64][ldxs].  Only int16 values and block
+ * scales cross NVLink (2.06 bytes per element, not 2 x 4 for gate and up).
+ * With sig_epoch != 0 the last CTA publishes sig_epoch into sig_flags[r][rank]
+ * of every rank r (sig_ticket: a zeroed device word of this rank) and then
+ * waits (bounded; error bit 2) until wait_flags[r] >= sig_epoch for every
+ * rank, so a down projection launched after it on the stream reads a
+ * complete input.  Replaces the reference's swiglu between the gate / up and
+ * down GEMVs (qwen_kernels_opt.c:983-986) for a row-sharded layer. */
+QB_API int qwen_b200_swiglu_quant_sharded_dev(const float* gate, const float* up, int B, int n, int ld_in, int col0,
+                                              int K, int planar, int ldxs, void* const* dst, int ndst,
+                                              unsigned int* const* sig_flags, unsigned int* sig_ticket,
+                                              unsigned int sig_epoch, const unsigned int* wait_flags, int world,
+                                              int rank, void* stream);
 /* Zeroed device memory that can be shared with qwen_b200_ipc_handle (plain
  * cudaMalloc: IPC needs the allocation's own base pointer). */
 QB_API int qwen_b200_dev_alloc(size_t bytes, void** out);

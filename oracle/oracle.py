@@ -225,6 +225,22 @@ def bfp8_gemv_scalar(x, mant, exps):
     return y
 
 
+def bfp8_gemv_numpy(x, mant, exps):
+    """The reference engine's numpy fallback GEMV, used when no C kernel
+    library is loaded (04-板载脚本与工具/qwen_real_engine.py:1233-1239): no
+    activation quantization; per row and 64-block the float32 sum of m * x
+    (numpy's pairwise reduction over the block), times 2^(e - 134) computed
+    in float32, then the float32 sum over the row's blocks."""
+    mant = np.asarray(mant, np.int8)
+    exps = np.asarray(exps, np.uint8)
+    x = np.asarray(x, np.float32)
+    M, K = mant.shape
+    nb = K // 64
+    scales = (2.0 ** (exps.astype(np.float32) - 134.0)).reshape(M, nb)
+    dots = np.sum(mant.reshape(M, nb, 64).astype(np.float32) * x.reshape(nb, 64), axis=-1)
+    return np.sum(dots * scales, axis=-1)
+
+
 def bfp8_gemv_rtl20(xq, xs, mant, exps):
     """gemv_core dequant mode: (int32 words floor(y*2^20) [M], flags)."""
     mant, pm = _c(mant, np.int8)

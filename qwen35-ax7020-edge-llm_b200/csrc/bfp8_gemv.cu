@@ -896,7 +896,109 @@ __global__ void __launch_bounds__(kThreads) quant_block64_kernel(const float* x,
     }
 }
 
+// ------------------------------------------------------- shard-local SwiGLU
+// The MLP activation of a row-sharded layer: this rank holds elements
+// [col0, col0 + n) of the gate and up projections of every batch row; it
+// applies swiglu (the reference's NEON build, as in the fused down
+// projection), quantizes each 64-block by the reference rule -- blocks lie
+// wholly inside one rank's slice, so the bits are those of the unsharded
+// activation -- and stores the quantized slice into its own copy of the
+// down projection's input and into every other rank's, so only int16 values
+// and block scales cross NVLink.  With a signal epoch, the last CTA then
+// publishes it to every rank and waits (bounded) until every rank has
+// published it: the down projection launched after this kernel reads a
+// complete input.
+struct SqArgs {
+    const float* gate;
+    const float* up;
+    int B, n, ld_in, col0, K, ldxs, planar, ndst;
+    unsigned char* dst[kMaxRanks];   // dst[0] this GPU's input, then the other ranks'
+    SyncArgs sync;
+    unsigned int* err;
+};
+
+__global__ void __launch_bounds__(256) swiglu_quant_kernel(const __grid_constant__ SqArgs A) {
+    const int lane = threadIdx.x & 31;
+    const int nbl = A.n >> 6;
+    const long long total = (long long)A.B * nbl;
+    for (long long t = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); t < total; t += (long long)gridDim.x * 8) {
+        const int b = (int)(t / nbl), j = (int)(t - (long long)b * nbl);
+        const size_t src = (size_t)b * A.ld_in + (size_t)j * 64;
+        const float2 g = reinterpret_cast<const float2*>(A.gate + src)[lane];
+        const float2 u = reinterpret_cast<const float2*>(A.up + src)[lane];
+        const float2 v = make_float2(swiglu_lane(g.x, u.x), swiglu_lane(g.y, u.y));
+        int q0, q1;
+        float xs;
+        block_quant(v, q0, q1, xs);
+        const int col = A.col0 + 64 * j + 2 * lane, kb = (A.col0 >> 6) + j;
+        if (!A.planar) {   // quantized record: xq int16 [K], then xs fp32 [K/64]
+            const uint32_t w = ((uint32_t)q0 & 0xFFFFu) | ((uint32_t)q1 << 16);
+            for (int d = 0; d < A.ndst; d++) {
+                reinterpret_cast<uint32_t*>(A.dst[d])[col >> 1] = w;
+                if (lane == 0) reinterpret_cast<float*>(A.dst[d] + 2 * (size_t)A.K)[kb] = xs;
+            }
+        } else {           // planes [2][B][K] (xq = 256 * hi + lo), then xs_t [K/64][ldxs]
+            const int l0 = (int)(int8_t)(q0 & 0xFF), l1 = (int)(int8_t)(q1 & 0xFF);
+            const uint16_t hi =
+                (uint16_t)(((uint32_t)((q0 - l0) >> 8) & 0xFFu) | (((uint32_t)((q1 - l1) >> 8) & 0xFFu) << 8));
+            const uint16_t lo = (uint16_t)(((uint32_t)q0 & 0xFFu) | (((uint32_t)q1 & 0xFFu) << 8));
+            const size_t off = (size_t)b * A.K + col, plane = (size_t)A.B * A.K;
+            for (int d = 0; d < A.ndst; d++) {
+                *reinterpret_cast<uint16_t*>(A.dst[d] + off) = hi;
+                *reinterpret_cast<uint16_t*>(A.dst[d] + plane + off) = lo;
+                if (lane == 0) reinterpret_cast<float*>(A.dst[d] + 2 * plane)[(size_t)kb * A.ldxs + b] = xs;
+            }
+        }
+    }
+    if (!A.sync.sig_epoch) return;
+    __shared__ int s_last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        const unsigned int tk = atomicAdd(A.sync.sig_ticket, 1u);
+        s_last = tk == gridDim.x - 1;
+        if (s_last) {
+            __threadfence_system();
+            for (int r = 0; r < A.sync.world; r++) st_release_sys(A.sync.sig_flags[r] + A.sync.rank, A.sync.sig_epoch);
+            *A.sync.sig_ticket = 0u;   // the next launch using this ticket is stream-ordered after this one
+        }
+    }
+    __syncthreads();
+    if (s_last) wait_peer_flags(A.sync.wait_flags, A.sync.world, A.sync.sig_epoch, A.err);
+}
+
 // ---------------------------------------------------------------- host side
+cudaError_t launch_swiglu_quant(const float* gate, const float* up, int B, int n, int ld_in, int col0, int K,
+                                int planar, int ldxs, void* const* dst, int ndst, const SyncArgs* sync,
+                                unsigned int* err, cudaStream_t stream) {
+    if (!gate || !up || !dst || B < 1 || n < 0 || n % 64 || col0 < 0 || col0 % 64 || K % 64 || col0 + n > K ||
+        ndst < 1 || ndst > kMaxRanks || (B > 1 && !planar) || ld_in < n || (ld_in & 1) ||
+        (planar && ldxs < B) || (reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up)) & 7)
+        return cudaErrorInvalidValue;
+    if (sync && (!sync_args_ok(*sync) || (sync->sig_epoch && !sync->wait_flags))) return cudaErrorInvalidValue;
+    SqArgs A{};
+    A.gate = gate;
+    A.up = up;
+    A.B = B;
+    A.n = n;
+    A.ld_in = ld_in;
+    A.col0 = col0;
+    A.K = K;
+    A.ldxs = ldxs;
+    A.planar = planar;
+    A.ndst = ndst;
+    for (int d = 0; d < ndst; d++) {
+        if (!dst[d] || reinterpret_cast<uintptr_t>(dst[d]) & 15) return cudaErrorInvalidValue;
+        A.dst[d] = static_cast<unsigned char*>(dst[d]);
+    }
+    if (sync) A.sync = *sync;
+    A.err = err;
+    const long long total = (long long)B * (n / 64);
+    const int grid = (int)std::max<long long>(1, std::min<long long>((total + 7) / 8, (long long)num_sms() * 8));
+    swiglu_quant_kernel<<<grid, 256, 0, stream>>>(A);
+    return cudaGetLastError();
+}
+
 int num_sms() {
     static int n = 0;
     if (!n) {
@@ -921,7 +1023,7 @@ static bool fast_shape_ok(const GemvDesc& d) {
 }
 
 bool gemv_plan(GemvDesc* descs, int n, uint32_t* act, GemvPlan* plan, int mode, size_t act_cap_words,
-               unsigned int* tickets, size_t tickets_cap) {
+               unsigned int* tickets, size_t tickets_cap, int fixed_seg_stages) {
     if (n <= 0 || n > kMaxSDesc) return false;
     const bool fast = mode == kFast;
     // largest K first: the counter then hands out the biggest units first
@@ -940,7 +1042,12 @@ bool gemv_plan(GemvDesc* descs, int n, uint32_t* act, GemvPlan* plan, int mode, 
     for (GemvDesc& d : sorted) {
         const int groups = (d.M + kRows - 1) / kRows, nst = d.K >> 8;
         int nseg = 1;
-        if (fast) {
+        if (fast && fixed_seg_stages > 0) {
+            // segments of a fixed length: where a row's K is cut depends on K
+            // alone, not on how many rows this GPU holds, so a row-sharded
+            // plan gives every row the bits of the unsharded plan
+            nseg = std::max(1, (nst + fixed_seg_stages - 1) / fixed_seg_stages);
+        } else if (fast) {
             // segments of >= 2 stages: the per-warp claim ring assumes its
             // producer never runs more than one unit ahead
             nseg = (int)std::ceil(slots * ((double)d.M * d.K / total_bytes) / groups);

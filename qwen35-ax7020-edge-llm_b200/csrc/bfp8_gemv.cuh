@@ -73,8 +73,11 @@ size_t gemv_act_words(int K);
 // Fast mode keeps one counter per split row group: in `act` after the
 // segment sums, or, when `tickets` is given, in that separate zeroed buffer
 // of tickets_cap words (for scratch that other launches also write).
+// fixed_seg_stages > 0 (fast mode): cut every row's K into segments of that
+// many 256-byte stages, independent of the rows this GPU holds.
 bool gemv_plan(GemvDesc* descs, int n, uint32_t* act, GemvPlan* plan, int mode = kExact,
-               size_t act_cap_words = 0, unsigned int* tickets = nullptr, size_t tickets_cap = 0);
+               size_t act_cap_words = 0, unsigned int* tickets = nullptr, size_t tickets_cap = 0,
+               int fixed_seg_stages = 0);
 
 // Grouped exact GEMV over a planned, device-resident descriptor array.
 // `ctr` is a 2-word device counter pair owned by the plan (zero before the
@@ -125,6 +128,17 @@ cudaError_t launch_bfp8_lm_head(const float* h, const int8_t* mant, const uint8_
 // Standalone block-64 quantizer: x [B][K] -> xq [B][K] (natural order), xs [B][K/64].
 cudaError_t launch_quant_block64(const float* x, int B, int K, int16_t* xq, float* xs,
                                  cudaStream_t stream);
+
+// Shard-local SwiGLU + quantizer of a row-sharded MLP layer: elements
+// [col0, col0 + n) of every batch row b of gate / up (row stride ld_in) ->
+// swiglu (the reference's NEON build) -> block-64 quantization, stored into
+// each dst: planar == 0 (B == 1): the quantized record xq int16 [K] followed
+// by xs fp32 [K/64]; planar == 1: planes int8 [2][B][K] (hi, lo) followed by
+// xs_t fp32 [K/64][ldxs].  With sync->sig_epoch the last CTA publishes it to
+// every rank and waits for every rank's (sync->wait_flags, bounded).
+cudaError_t launch_swiglu_quant(const float* gate, const float* up, int B, int n, int ld_in, int col0, int K,
+                                int planar, int ldxs, void* const* dst, int ndst, const SyncArgs* sync,
+                                unsigned int* err, cudaStream_t stream);
 
 int num_sms();
 

@@ -703,6 +703,10 @@ int qwen_b200_quant_dev(const float* x, int B, int K, int16_t* xq, float* xs, vo
 
 namespace {
 
+// QB_STACK_FIXED_SPLIT: K segments of 4 stages (1 KB of every row) -- short
+// enough that the 1/8 shard of a deep matrix still fills the GPU.
+constexpr int kFixedSegStages = 4;
+
 struct PeerSpec {
     int world;
     const float* const* peer_y;   // n x (world - 1): the other ranks' full vectors per GEMV
@@ -743,7 +747,12 @@ int stack_create_impl(int n, const int8_t* const* mant, const uint8_t* const* ex
         qb::GemvDesc d{};
         d.mant = mant[i];
         d.exps = exps[i];
-        d.x = x[i];
+        if (flags & QB_STACK_Q_INPUT) {   // x[i]: int16 xq [K], then fp32 xs [K/64]
+            d.xq = reinterpret_cast<const int16_t*>(x[i]);
+            d.xs = reinterpret_cast<const float*>(reinterpret_cast<const char*>(x[i]) + 2 * (size_t)K[i]);
+        } else {
+            d.x = x[i];
+        }
         d.y = y[i];
         d.M = M[i];
         d.K = K[i];
@@ -751,7 +760,8 @@ int stack_create_impl(int n, const int8_t* const* mant, const uint8_t* const* ex
         v.push_back(d);
     }
     const int mode = (flags & QB_STACK_FAST) ? qb::kFast : qb::kExact;
-    if (!qb::gemv_plan(v.data(), (int)v.size(), nullptr, &sp.plan, mode))
+    const int fixed = (flags & QB_STACK_FIXED_SPLIT) ? kFixedSegStages : 0;
+    if (!qb::gemv_plan(v.data(), (int)v.size(), nullptr, &sp.plan, mode, 0, nullptr, 0, fixed))
         return fail(QB_EINVAL, "stack: 1..160 GEMVs, every K a multiple of 512, mant/exps/x 16/4/8-byte aligned");
     cudaError_t e = cudaMalloc(&sp.act, sp.plan.act_words * 4 + 16);
     if (e != cudaSuccess) return fail(QB_ENOMEM, "stack act alloc", e);
@@ -760,7 +770,7 @@ int stack_create_impl(int n, const int8_t* const* mant, const uint8_t* const* ex
         return fail(QB_ECUDA, "stack ctr clear", e);
     if ((e = cudaMemset(sp.act, 0, sp.plan.act_words * 4 + 16)) != cudaSuccess)
         return fail(QB_ECUDA, "stack act clear", e);
-    qb::gemv_plan(v.data(), (int)v.size(), sp.act, &sp.plan, mode);
+    qb::gemv_plan(v.data(), (int)v.size(), sp.act, &sp.plan, mode, 0, nullptr, 0, fixed);
     if (ps && (e = cudaMemcpy(sp.peers, peers.data(), sizeof(qb::PeerOut) * n, cudaMemcpyHostToDevice)) != cudaSuccess)
         return fail(QB_ECUDA, "stack peer upload", e);
     e = cudaMalloc(&sp.dev_descs, sizeof(qb::GemvDesc) * (v.size() ? v.size() : 1));
@@ -809,6 +819,33 @@ int qwen_b200_stack_run_sync(int plan, void* stream, const unsigned int* wait_fl
     cudaError_t e =
         qb::launch_gemv_list(sp.dev_descs, sp.plan, sp.ctr, st->err, static_cast<cudaStream_t>(stream), &sy);
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_stack_run_sync", e);
+}
+
+int qwen_b200_swiglu_quant_sharded_dev(const float* gate, const float* up, int B, int n, int ld_in, int col0, int K,
+                                       int planar, int ldxs, void* const* dst, int ndst, unsigned int* const* sig_flags,
+                                       unsigned int* sig_ticket, unsigned int sig_epoch, const unsigned int* wait_flags,
+                                       int world, int rank, void* stream) {
+    if (sig_epoch && (!sig_flags || !sig_ticket || !wait_flags || world < 1 || world > qb::kMaxRanks || rank < 0 ||
+                      rank >= world))
+        return fail(QB_EINVAL, "swiglu_quant_sharded: a signal needs every rank's flags, a ticket and this GPU's "
+                               "flags (1 <= world <= 8)");
+    qb::SyncArgs sy{};
+    if (sig_epoch) {
+        sy.wait_flags = wait_flags;
+        sy.sig_ticket = sig_ticket;
+        sy.sig_epoch = sig_epoch;
+        sy.world = world;
+        sy.rank = rank;
+        for (int r = 0; r < world; r++) sy.sig_flags[r] = sig_flags[r];
+    }
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    cudaError_t e = qb::launch_swiglu_quant(gate, up, B, n, ld_in, col0, K, planar, ldxs, dst, ndst,
+                                            sig_epoch ? &sy : nullptr, st->err, static_cast<cudaStream_t>(stream));
+    if (e == cudaErrorInvalidValue)
+        return fail(QB_EINVAL, "swiglu_quant_sharded: n, col0 and K multiples of 64 with col0 + n <= K, B == 1 unless "
+                               "planar, ldxs >= B, gate/up 8-byte and every dst 16-byte aligned, 1..8 destinations");
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_swiglu_quant_sharded_dev", e);
 }
 
 int qwen_b200_dev_alloc(size_t bytes, void** out) {

@@ -46,6 +46,8 @@ SIGNATURES = {
     "qwen_b200_stack_destroy": (_I, [_I]),
     "qwen_b200_stack_create_sharded": (_I, [_I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P]),
     "qwen_b200_stack_run_sync": (_I, [_I, _P, _P, ctypes.c_uint, _P, ctypes.c_uint, _I, _I]),
+    "qwen_b200_swiglu_quant_sharded_dev": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _I, _P, _P, ctypes.c_uint,
+                                                 _P, _I, _I, _P]),
     "qwen_b200_dev_alloc": (_I, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
     "qwen_b200_dev_free": (_I, [_P]),
     "qwen_b200_ipc_handle": (_I, [_P, _P]),

@@ -137,7 +137,7 @@ class DeviceStack:
     N(0, 1), one per GEMV, outputs one fp32 vector per GEMV.
     """
 
-    def __init__(self, stack, copies=1, device="cuda", seed=0, std=0.02):
+    def __init__(self, stack, copies=1, device="cuda", seed=0, std=0.02, host_bytes=None, host_x=None):
         import torch
 
         from . import ops
@@ -145,15 +145,21 @@ class DeviceStack:
         self.stack = list(stack)
         self.table, self.nbytes = layout(self.stack)
         self.device = torch.device(device)
-        g = torch.Generator(device=self.device)
-        g.manual_seed(seed)
-        base = torch.empty(self.nbytes, dtype=torch.uint8, device=self.device)
-        for name, (off, t) in self.table.items():
-            w = torch.randn((t.M, t.K), generator=g, device=self.device, dtype=torch.float32) * std
-            mant = base[off:off + t.mant_bytes].view(torch.int8).view(t.M, t.K)
-            exps = base[off + t.mant_bytes: off + t.mant_bytes + t.exp_bytes].view(t.M, t.K // 64)
-            ops.pack_bfp8(w, mant, exps)
-            del w
+        if host_bytes is not None:
+            # the packed weight file image (layout() offsets), e.g. an mmap
+            if host_bytes.nbytes < self.nbytes:
+                raise ValueError("host_bytes is shorter than the stack layout")
+            base = torch.from_numpy(host_bytes[:self.nbytes]).to(self.device)
+        else:
+            g = torch.Generator(device=self.device)
+            g.manual_seed(seed)
+            base = torch.empty(self.nbytes, dtype=torch.uint8, device=self.device)
+            for name, (off, t) in self.table.items():
+                w = torch.randn((t.M, t.K), generator=g, device=self.device, dtype=torch.float32) * std
+                mant = base[off:off + t.mant_bytes].view(torch.int8).view(t.M, t.K)
+                exps = base[off + t.mant_bytes: off + t.mant_bytes + t.exp_bytes].view(t.M, t.K // 64)
+                ops.pack_bfp8(w, mant, exps)
+                del w
         self.buffers = [base] + [base.clone() for _ in range(copies - 1)]
         # activations and outputs live in two flat buffers (one copy each way
         # moves a whole token); each GEMV's slice starts on a 16-byte boundary
@@ -164,15 +170,26 @@ class DeviceStack:
             yo.append(ny)
             nx += (t.K + 3) & ~3
             ny += (t.M + 3) & ~3
-        gx = torch.Generator(device=self.device)
-        gx.manual_seed(seed + 1)
-        self.x_flat = torch.randn(nx, generator=gx, device=self.device, dtype=torch.float32)
+        if host_x is not None:   # one fp32 activation per GEMV, concatenated in stack order
+            xs = torch.zeros(nx, dtype=torch.float32)
+            pos = 0
+            for o, t in zip(xo, self.stack):
+                xs[o:o + t.K] = torch.from_numpy(host_x[pos:pos + t.K])
+                pos += t.K
+            self.x_flat = xs.to(self.device)
+        else:
+            gx = torch.Generator(device=self.device)
+            gx.manual_seed(seed + 1)
+            self.x_flat = torch.randn(nx, generator=gx, device=self.device, dtype=torch.float32)
         self.y_flat = torch.zeros(ny, dtype=torch.float32, device=self.device)
+        self.x_off, self.y_off = xo, yo   # each GEMV's slice of x_flat / y_flat
         self.x = [self.x_flat[o:o + t.K] for o, t in zip(xo, self.stack)]
         self.y = [self.y_flat[o:o + t.M] for o, t in zip(yo, self.stack)]
 
-    def views(self, copy=0):
-        """[(x, mant, exps, y)] of one copy, in stack order."""
+    def views(self, copy=0, x_flat=None, y_flat=None):
+        """[(x, mant, exps, y)] of one copy, in stack order; x_flat / y_flat
+        (same sizes as this stack's) substitute other activation / output
+        buffers."""
         import torch
 
         buf = self.buffers[copy]
@@ -181,7 +198,9 @@ class DeviceStack:
             off, _ = self.table[t.name]
             mant = buf[off:off + t.mant_bytes].view(torch.int8).view(t.M, t.K)
             exps = buf[off + t.mant_bytes: off + t.mant_bytes + t.exp_bytes].view(t.M, t.K // 64)
-            out.append((self.x[i], mant, exps, self.y[i]))
+            x = self.x[i] if x_flat is None else x_flat[self.x_off[i]:self.x_off[i] + t.K]
+            y = self.y[i] if y_flat is None else y_flat[self.y_off[i]:self.y_off[i] + t.M]
+            out.append((x, mant, exps, y))
         return out
 
 

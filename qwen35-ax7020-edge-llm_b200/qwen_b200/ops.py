@@ -24,7 +24,8 @@ from ._lib import KernelError, check, load
 __all__ = [
     "KernelError", "quant_block64", "bfp8_gemv", "bfp8_gemv_fast", "bfp8_gemv_q", "lm_head_bf16", "lm_head_bfp8",
     "pack_bfp8", "LinearStack", "rmsnorm_bfp8_gemv", "residual_rmsnorm_bfp8_gemv", "LmResult", "Planes", "quant_planes", "bfp8_gemm_tc", "BatchedStack",
-    "PeerRegion", "ShardedLinearStack", "quant_planes_wait", "ShardedBatchedStack",
+    "PeerRegion", "ShardedLinearStack", "quant_planes_wait", "ShardedBatchedStack", "swiglu_quant_sharded",
+    "quant_record_bytes", "planes_record_bytes", "planes_view", "STACK_FAST", "STACK_FIXED_SPLIT", "STACK_Q_INPUT",
 ]
 
 
@@ -389,16 +390,23 @@ def pack_bfp8(w: torch.Tensor, out_mant: torch.Tensor | None = None, out_exps: t
     return mant, exps
 
 
+# Plan flags of the grouped launches (include/qwen_b200.h QB_STACK_*).
+STACK_FAST = 1          # split-K arithmetic (fused multiply-add per block)
+STACK_FIXED_SPLIT = 2   # with STACK_FAST: K cut at fixed 1 KB steps (same bits on any number of GPUs)
+STACK_Q_INPUT = 4       # x is a quantized record: int16 xq [K], then fp32 xs [K/64]
+
+
 class LinearStack:
     """A reusable grouped launch of independent BFP8 GEMVs (one kernel).
 
     ``items`` is a list of (x fp32 [K], mant int8 [M, K], exps uint8 [M, K/64],
     y fp32 [M]) device tensors; the tensors must stay alive and in place while
     the stack is used.  ``run()`` enqueues every GEMV on the current stream and
-    is safe inside CUDA graph capture.
+    is safe inside CUDA graph capture.  ``flags`` (STACK_*) overrides ``fast``;
+    with STACK_Q_INPUT every x is a quantized record (``quant_record``).
     """
 
-    def __init__(self, items, fast: bool = False):
+    def __init__(self, items, fast: bool = False, flags: int | None = None):
         n = len(items)
         P = ctypes.c_void_p * n
         I = ctypes.c_int * n
@@ -409,13 +417,21 @@ class LinearStack:
         ys = P(*[_ptr(y) for (_, _, _, y) in items])
         Ms = I(*[m.shape[0] for (_, m, _, _) in items])
         Ks = I(*[m.shape[1] for (_, m, _, _) in items])
-        h = load().qwen_b200_stack_create_ex(n, mant, exps, xs, ys, Ms, Ks, 1 if fast else 0)
+        fl = flags if flags is not None else (STACK_FAST if fast else 0)
+        h = load().qwen_b200_stack_create_ex(n, mant, exps, xs, ys, Ms, Ks, fl)
         if h <= 0:
             check(h, "LinearStack")
         self.handle = h
 
     def run(self, stream: int | None = None) -> None:
         check(load().qwen_b200_stack_run(self.handle, _stream() if stream is None else stream), "LinearStack.run")
+
+    def run_wait(self, wait_flags: int, wait_epoch: int, world: int, stream: int | None = None) -> None:
+        """run() whose input quantizer first waits (bounded) until every one
+        of `world` ranks published ``wait_epoch`` into the flag array at
+        ``wait_flags`` (row-sharded layers whose input other GPUs write)."""
+        check(load().qwen_b200_stack_run_sync(self.handle, _stream() if stream is None else stream, wait_flags,
+                                              wait_epoch, None, 0, world, 0), "LinearStack.run_wait")
 
     def close(self) -> None:
         if getattr(self, "handle", 0) > 0:
@@ -471,6 +487,9 @@ class PeerRegion:
     def uints(self, offset: int, n: int) -> torch.Tensor:
         return torch.as_tensor(_DevArray(self.ptr + offset, n, "<i4"))
 
+    def bytes(self, offset: int, n: int) -> torch.Tensor:
+        return torch.as_tensor(_DevArray(self.ptr + offset, n, "|u1"))
+
     def close(self) -> None:
         if self.ptr:
             if self._owned:
@@ -495,7 +514,7 @@ class ShardedLinearStack:
     so a captured graph would replay stale epochs: launch it directly.
     """
 
-    def __init__(self, items, peer_ptrs, row_base, world: int, fast: bool = False):
+    def __init__(self, items, peer_ptrs, row_base, world: int, fast: bool = False, flags: int | None = None):
         n = len(items)
         P = ctypes.c_void_p * n
         I = ctypes.c_int * n
@@ -512,7 +531,8 @@ class ShardedLinearStack:
             raise ValueError("ShardedLinearStack: need world - 1 peer vectors per GEMV")
         peers = (ctypes.c_void_p * max(1, len(flat)))(*flat)
         rb = I(*row_base)
-        h = load().qwen_b200_stack_create_sharded(n, mant, exps, xs, ys, Ms, Ks, 1 if fast else 0, world, peers, rb)
+        fl = flags if flags is not None else (STACK_FAST if fast else 0)
+        h = load().qwen_b200_stack_create_sharded(n, mant, exps, xs, ys, Ms, Ks, fl, world, peers, rb)
         if h <= 0:
             check(h, "ShardedLinearStack")
         self.handle = h
@@ -534,6 +554,39 @@ class ShardedLinearStack:
             self.close()
         except Exception:
             pass
+
+
+def quant_record_bytes(K: int) -> int:
+    """Bytes of a quantized activation record: int16 xq [K], fp32 xs [K/64]."""
+    return 2 * K + 4 * (K // 64)
+
+
+def planes_record_bytes(B: int, K: int, ldxs: int) -> int:
+    """Bytes of a planar record: int8 planes [2, B, K], then fp32 xs_t [K/64, ldxs]."""
+    return 2 * B * K + 4 * (K // 64) * ldxs
+
+
+def planes_view(buf: torch.Tensor, B: int, K: int, ldxs: int) -> Planes:
+    """The Planes stored in a planar record (a uint8 or int8 device tensor)."""
+    b = buf.view(torch.int8)
+    return Planes(b[:2 * B * K].view(2, B, K), b[2 * B * K:planes_record_bytes(B, K, ldxs)].view(torch.float32)
+                  .view(K // 64, ldxs), B, K)
+
+
+def swiglu_quant_sharded(gate_ptr: int, up_ptr: int, B: int, n: int, ld_in: int, col0: int, K: int, planar: bool,
+                         ldxs: int, dst_ptrs, sig_flags=None, sig_ticket: int = 0, sig_epoch: int = 0,
+                         wait_flags: int = 0, world: int = 1, rank: int = 0) -> None:
+    """The shard-local MLP activation of a row-sharded layer
+    (qwen_b200_swiglu_quant_sharded_dev): elements [col0, col0 + n) of every
+    batch row of gate / up -> swiglu -> block-64 quantization -> each
+    destination record (a quantized record, or a planar record when
+    ``planar``).  With ``sig_epoch`` the last CTA publishes the epoch and
+    waits for every rank's."""
+    dst = (ctypes.c_void_p * len(dst_ptrs))(*dst_ptrs)
+    sf = (ctypes.c_void_p * world)(*sig_flags) if sig_flags else None
+    check(load().qwen_b200_swiglu_quant_sharded_dev(gate_ptr, up_ptr, B, n, ld_in, col0, K, 1 if planar else 0, ldxs,
+                                                    dst, len(dst_ptrs), sf, sig_ticket, sig_epoch, wait_flags, world,
+                                                    rank, _stream()), "swiglu_quant_sharded")
 
 
 def quant_planes_wait(x: torch.Tensor, out: Planes, wait_flags: int, wait_epoch: int, world: int) -> Planes:

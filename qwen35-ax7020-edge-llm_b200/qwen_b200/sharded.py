@@ -1,21 +1,34 @@
-"""Output-row-sharded BFP8 linear stack over several GPUs (one process per GPU).
+"""Output-row-sharded BFP8 MLP stack over several GPUs (one process per GPU).
 
-Every GEMV's rows are split into contiguous slices, one per rank, with slice
-boundaries on multiples of 64 rows.  Each rank streams only its slice of the
-weights (rows bit-identical to an unsharded run of the same arithmetic) and
-the full output vector is rebuilt in every rank's own memory before the next
-GEMV reads it, in one of two ways:
+The multi-GPU configuration is `layers` x (gate, up: ffn x hidden; down:
+hidden x ffn).  Every GEMV's rows are split into contiguous slices, one per
+rank, with slice boundaries on multiples of 64 rows, and gate and up share
+their boundaries.  Per layer, on every rank:
 
-* ``exchange="nccl"``: an NCCL all-gather after every grouped launch;
-* ``exchange="peer"``: the GEMV kernel itself stores each finished row into
-  every rank's full vector over NVLink (CUDA IPC mappings), and the last CTA
-  of each launch raises a per-rank epoch flag on every GPU; the next launch
-  waits (bounded) for all ranks' flags before it reads its input.  No
-  collective runs, and the weight stream of a launch starts while it waits.  The data flow of one
-scaled MLP layer (gate / up ffn x hidden, down hidden x ffn): gate and up
-read the layer input; down reads the gathered gate output (the element-wise
-SwiGLU between them is glue outside this path); the next layer reads the
-gathered down output.
+1. gate / up: this rank's rows of both, from the full layer input; the
+   results stay on this GPU;
+2. the MLP activation of those rows, shard-locally: swiglu (the reference's
+   NEON build) and the block-64 quantizer -- slices are whole blocks, so the
+   bits are the unsharded activation's -- and only the quantized slice (int16
+   values + block scales, 2.06 bytes per element) is exchanged, once;
+3. down: this rank's rows, from the complete quantized activation; its fp32
+   rows reach every rank (the next layer's input -- in a real decoder the
+   residual stream, which stays fp32).
+
+Two exchanges:
+
+* ``exchange="nccl"``: NCCL all-gathers of the quantized activation and of
+  the down rows;
+* ``exchange="peer"``: the kernels store into every rank's buffers over
+  NVLink (CUDA IPC mappings of one region per rank): the activation kernel
+  stores the quantized slice, publishes an epoch flag to every rank and
+  waits (bounded) for everyone's; the down GEMV stores its rows into every
+  rank's output and publishes the next epoch, which the next layer's input
+  quantizer waits for.  No collective runs.
+
+Batch 1 runs the GEMV kernels, batch > 1 the tcgen05 GEMM (planar int16
+activations).  With ``fast`` (batch 1) every row's K is cut into segments at
+fixed 1 KB steps, so the outputs are the same bits on any number of GPUs.
 """
 from __future__ import annotations
 
@@ -46,39 +59,38 @@ def scaled_layers(layers=8, hidden=8192, ffn=28672) -> list[LayerPlan]:
     return [LayerPlan(s[3 * i], s[3 * i + 1], s[3 * i + 2]) for i in range(layers)]
 
 
-def run_layers(layers, x0, gemv, all_gather, world, rank):
-    """Reference data flow, independent of the device: `gemv(name, x_full,
-    r0, r1) -> y_shard` computes rows [r0, r1) of a GEMV, `all_gather(y_shard,
-    M) -> y_full` concatenates the rank slices.  Returns every gathered
-    output in order (gate, up, down per layer)."""
+def run_layers(layers, x0, gemv, act_quant, gemv_q, all_gather, world, rank):
+    """The data flow, independent of the device: ``gemv(name, x, r0, r1)``
+    computes rows [r0, r1) of a GEMV from an fp32 input, ``act_quant(g, u)``
+    the quantized swiglu (xq, xs) of a slice, ``gemv_q(name, xq, xs, r0, r1)``
+    rows of a GEMV from a quantized input, ``all_gather(part)`` concatenates
+    the ranks' parts.  Returns, per layer, the gathered activation (xq, xs)
+    and the gathered down output."""
     outs = []
     x = x0
     for L in layers:
         g0, g1 = shard_rows(L.gate.M, world, rank)
-        u0, u1 = shard_rows(L.up.M, world, rank)
         d0, d1 = shard_rows(L.down.M, world, rank)
-        gate = all_gather(gemv(L.gate.name, x, g0, g1), L.gate.M)
-        up = all_gather(gemv(L.up.name, x, u0, u1), L.up.M)
-        down = all_gather(gemv(L.down.name, gate, d0, d1), L.down.M)
-        outs += [gate, up, down]
+        xq_s, xs_s = act_quant(gemv(L.gate.name, x, g0, g1), gemv(L.up.name, x, g0, g1))
+        xq, xs = all_gather(xq_s), all_gather(xs_s)
+        down = all_gather(gemv_q(L.down.name, xq, xs, d0, d1))
+        outs += [xq, xs, down]
         x = down
     return outs
 
 
 class ShardedDeviceStack:
-    """This rank's weight slices of a scaled stack on its GPU, plus the
-    full outputs, driven by grouped launches and the chosen exchange.
+    """This rank's weight slices of a scaled stack on its GPU, its buffers,
+    and the launches of one step (one token, or ``batch`` sequences).
 
-    ``batch`` 1 runs the batch-1 GEMV kernels (one activation vector per
-    token); ``batch`` B > 1 runs B sequences per step through the tcgen05
-    kernels (each layer input quantized to planar int16, outputs [B][M]).
-
-    `fast` selects the split-K arithmetic (see ops.bfp8_gemv_fast), which
-    keeps every GPU busy when each holds few rows.  Weights are fp32 N(0, 0.02) drawn per tensor from a seeded generator on
+    Weights are fp32 N(0, 0.02) drawn per tensor from a seeded generator on
     the device (the same full matrix on every rank), packed, and sliced; only
     the slice is kept.  `copies` byte-identical copies of the slices rotate
     across steps so that timing never finds them in L2.
     """
+
+    FLAGS_BYTES = 256   # region head: epoch flags (one uint per rank), then the activation kernel's ticket
+    TICKET_OFFSET = 128
 
     def __init__(self, layers, world, rank, device, copies=1, seed=0, group=None, fast=False, exchange="nccl",
                  batch=1):
@@ -98,13 +110,19 @@ class ShardedDeviceStack:
         self.region, self.peer_regions = None, []
         self.epoch = 0
         self.device = torch.device(device)
+        self.ldxs = (batch + 3) // 4 * 4
+        for L in self.layers:
+            if L.gate.M != L.up.M or L.gate.K != L.up.K or L.down.K != L.gate.M:
+                raise ValueError("a layer needs gate and up of one shape and down reading their activation")
         self.shards = {}   # name -> (r0, r1)
-        slices = []        # (name, r0, r1, K)
+        slices = []        # (Linear, r0, r1)
         for L in self.layers:
             for t in (L.gate, L.up, L.down):
                 r0, r1 = shard_rows(t.M, world, rank)
                 self.shards[t.name] = (r0, r1)
                 slices.append((t, r0, r1))
+        if exchange == "peer" and world > 1 and any(r1 <= r0 for _, r0, r1 in slices):
+            raise ValueError("exchange='peer' needs rows on every rank")
         # one buffer per copy holding every slice (SoA, 64-byte aligned)
         offs, off = {}, 0
         for t, r0, r1 in slices:
@@ -133,51 +151,54 @@ class ShardedDeviceStack:
         B = self.B
         xshape = (L0.gate.K,) if B == 1 else (B, L0.gate.K)
         self.x0 = torch.randn(xshape, generator=gx, device=self.device, dtype=torch.float32)
-        # gathered outputs (full [M] vectors or [B][M] matrices, every rank)
-        # and this rank's slices
+        # gate / up outputs: full-length, only this rank's slice is written
+        self.gu = {t.name: torch.zeros(self._oshape(t.M), dtype=torch.float32, device=self.device)
+                   for L in self.layers for t in (L.gate, L.up)}
+        # the down projections' quantized inputs (records) and full outputs:
+        # in the shared region (peer) or local (nccl)
         if exchange == "peer":
             self._map_regions()
         else:
-            self.full = {t.name: torch.zeros(self._oshape(t.M), dtype=torch.float32, device=self.device)
-                         for L in self.layers for t in (L.gate, L.up, L.down)}
-        self.part = {t.name: torch.zeros(B * self.padded_rows(t.M), dtype=torch.float32, device=self.device)
-                     for L in self.layers for t in (L.gate, L.up, L.down)}
-        self.gath = {t.name: torch.zeros(B * self.padded_rows(t.M) * world, dtype=torch.float32, device=self.device)
-                     for L in self.layers for t in (L.gate, L.up, L.down)}
-        if B > 1:   # planar int16 activations, one set per input width (local only)
-            self.planes = {}
-            for L in self.layers:
-                for K in (L.gate.K, L.down.K):
-                    if K not in self.planes:
-                        self.planes[K] = ops.planes_empty(B, K, self.device)
+            self.dq = [torch.zeros(self._rec_bytes(L.down.K), dtype=torch.uint8, device=self.device)
+                       for L in self.layers]
+            self.full = {L.down.name: torch.zeros(self._oshape(L.down.M), dtype=torch.float32, device=self.device)
+                         for L in self.layers}
+        if B > 1:   # planar activations of the layer inputs (local)
+            self.planes_in = ops.planes_empty(B, L0.gate.K, self.device)
+        if exchange == "nccl" and world > 1:
+            self._gather_buffers()
         self.plans = [self._plans(c) for c in range(copies)]
 
+    # ------------------------------------------------------------ buffers
     def _oshape(self, M):
         return (M,) if self.B == 1 else (self.B, M)
 
-    FLAGS_BYTES = 256   # epoch flags at the head of every region: one uint per rank
+    def _rec_bytes(self, K):
+        from . import ops
+
+        if self.B == 1:
+            return ops.quant_record_bytes(K)
+        return ops.planes_record_bytes(self.B, K, self.ldxs)
 
     def _map_regions(self):
-        """One IPC-shared region per rank: the epoch flags, then every GEMV's
-        full output vector (256-byte aligned).  Handles are exchanged with an
-        all_gather_object; the other ranks' regions are mapped here."""
+        """One IPC-shared region per rank: the flags and ticket, then per
+        layer the down projection's quantized input and its full output
+        (256-byte aligned).  Handles are exchanged with an all_gather_object;
+        the other ranks' regions are mapped here."""
         import torch.distributed as dist
 
         from . import ops
 
+        self.qoff, self.voff, off = [], {}, self.FLAGS_BYTES
         for L in self.layers:
-            for t in (L.gate, L.up, L.down):
-                r0, r1 = self.shards[t.name]
-                if r1 <= r0:
-                    raise ValueError(f"exchange='peer' needs rows on every rank ({t.name}: M={t.M})")
-        self.voff, off = {}, self.FLAGS_BYTES
-        for L in self.layers:
-            for t in (L.gate, L.up, L.down):
-                self.voff[t.name] = off
-                off += (4 * self.B * t.M + 255) // 256 * 256
+            self.qoff.append(off)
+            off += (self._rec_bytes(L.down.K) + 255) // 256 * 256
+            self.voff[L.down.name] = off
+            off += (4 * self.B * L.down.M + 255) // 256 * 256
         self.region = ops.PeerRegion(off)
-        self.full = {name: self.region.floats(o, self.B * t.M).view(self._oshape(t.M)) for name, o, t in
-                     ((t.name, self.voff[t.name], t) for L in self.layers for t in (L.gate, L.up, L.down))}
+        self.dq = [self.region.bytes(o, self._rec_bytes(L.down.K)) for o, L in zip(self.qoff, self.layers)]
+        self.full = {L.down.name: self.region.floats(self.voff[L.down.name], self.B * L.down.M)
+                     .view(self._oshape(L.down.M)) for L in self.layers}
         self.flags = self.region.uints(0, self.world)
         self.peer_base = [0] * self.world   # every rank's region base, mapped into this process
         self.peer_base[self.rank] = self.region.ptr
@@ -191,9 +212,31 @@ class ShardedDeviceStack:
                     self.peer_base[r] = reg.ptr
 
     def padded_rows(self, M):
-        """Every rank contributes the same count to the all-gather: the
-        largest slice, rounded up to 64."""
+        """Every rank contributes the same count to an all-gather: the
+        largest slice."""
         return max(r1 - r0 for r0, r1 in (shard_rows(M, self.world, r) for r in range(self.world)))
+
+    def _gather_buffers(self):
+        import torch
+
+        B, W = self.B, self.world
+        self.part, self.gath = {}, {}
+        for L in self.layers:
+            P = self.padded_rows(L.down.M)
+            self.part[L.down.name] = torch.zeros(B * P, dtype=torch.float32, device=self.device)
+            self.gath[L.down.name] = torch.zeros(W * B * P, dtype=torch.float32, device=self.device)
+            Q = self.padded_rows(L.gate.M)
+            if B == 1:   # xq (int16) and xs (fp32) slices of the quantized record
+                self.part[("q", L.down.name)] = torch.zeros(Q, dtype=torch.int16, device=self.device)
+                self.gath[("q", L.down.name)] = torch.zeros(W * Q, dtype=torch.int16, device=self.device)
+            else:        # the planes' columns of every (plane, row)
+                self.part[("q", L.down.name)] = torch.zeros(2 * B * Q, dtype=torch.int8, device=self.device)
+                self.gath[("q", L.down.name)] = torch.zeros(W * 2 * B * Q, dtype=torch.int8, device=self.device)
+            nbq = Q // 64
+            self.part[("s", L.down.name)] = torch.zeros(nbq * (1 if B == 1 else self.ldxs), dtype=torch.float32,
+                                                        device=self.device)
+            self.gath[("s", L.down.name)] = torch.zeros(W * nbq * (1 if B == 1 else self.ldxs),
+                                                        dtype=torch.float32, device=self.device)
 
     def weight(self, copy, t):
         import torch
@@ -206,135 +249,188 @@ class ShardedDeviceStack:
         exps = buf[o + rows * t.K:o + rows * t.K + rows * t.K // 64].view(rows, t.K // 64)
         return mant, exps
 
-    def _plans(self, copy):
-        """Per layer: one grouped launch for gate+up (same input), one for down."""
+    # ------------------------------------------------------------ plans
+    def _flags(self):
         from . import ops
 
-        plans = []
-        x = self.x0
+        return (ops.STACK_FAST | ops.STACK_FIXED_SPLIT) if self.fast else 0
 
-        def out(t, rows):   # a single rank writes straight into the full vector
-            if self.exchange == "peer":
-                r0, r1 = self.shards[t.name]
-                return self.full[t.name][r0:r1]
-            return self.full[t.name] if self.world == 1 else self.part[t.name][:rows]
-
+    def _plans(self, copy):
+        """Per layer: one grouped launch for gate + up (same input, local
+        outputs) and one for down (quantized input; rows to every rank)."""
         if self.B > 1:
             return self._batched_plans(copy)
-        if self.exchange == "peer":
-            return self._peer_plans(copy)
-        for L in self.layers:
-            gu = []
-            for t in (L.gate, L.up):
-                mant, exps = self.weight(copy, t)
-                r0, r1 = self.shards[t.name]
-                if r1 > r0:
-                    gu.append((x, mant, exps, out(t, r1 - r0)))
-            mant, exps = self.weight(copy, L.down)
-            r0, r1 = self.shards[L.down.name]
-            dn = [(self.full[L.gate.name], mant, exps, out(L.down, r1 - r0))] if r1 > r0 else []
-            plans.append((ops.LinearStack(gu, fast=self.fast) if gu else None,
-                          ops.LinearStack(dn, fast=self.fast) if dn else None))
-            x = self.full[L.down.name]
-        return plans
-
-    def _peer_plans(self, copy):
         from . import ops
 
         others = [r for r in range(self.world) if r != self.rank]
+        peer = self.exchange == "peer" and self.world > 1
         plans = []
         x = self.x0
-
-        def stack(ts, xin):
-            items, peers, bases = [], [], []
-            for t in ts:
-                mant, exps = self.weight(copy, t)
-                r0, r1 = self.shards[t.name]
-                items.append((xin, mant, exps, self.full[t.name][r0:r1]))
-                peers.append([self.peer_base[r] + self.voff[t.name] for r in others])
-                bases.append(r0)
-            return ops.ShardedLinearStack(items, peers, bases, self.world, fast=self.fast)
-
-        for L in self.layers:
-            plans.append((stack((L.gate, L.up), x), stack((L.down,), self.full[L.gate.name])))
+        for i, L in enumerate(self.layers):
+            g0, g1 = self.shards[L.gate.name]
+            items = [(x, *self.weight(copy, t), self.gu[t.name][g0:g1]) for t in (L.gate, L.up) if g1 > g0]
+            gu = ops.LinearStack(items, flags=self._flags()) if items else None
+            d0, d1 = self.shards[L.down.name]
+            fl = self._flags() | ops.STACK_Q_INPUT
+            if d1 <= d0:
+                dn = None
+            elif peer:
+                dn = ops.ShardedLinearStack([(self.dq[i], *self.weight(copy, L.down), self.full[L.down.name][d0:d1])],
+                                            [[self.peer_base[r] + self.voff[L.down.name] for r in others]], [d0],
+                                            self.world, flags=fl)
+            else:
+                y = self.full[L.down.name] if self.world == 1 else self.part[L.down.name][:d1 - d0]
+                dn = ops.LinearStack([(self.dq[i], *self.weight(copy, L.down), y)], flags=fl)
+            plans.append((gu, dn))
             x = self.full[L.down.name]
         return plans
 
     def _batched_plans(self, copy):
-        """Per layer one grouped tcgen05 launch for gate+up and one for down.
-        Outputs go straight into the full [B][M] matrices (one rank, or
-        exchange="peer", which also stores into every other rank's), or into
-        this rank's contiguous [B][slice] part for the NCCL all-gather."""
+        """Per layer one grouped tcgen05 launch for gate + up (strided into
+        the local [B][M] outputs) and one for down (into the full [B][M]
+        outputs of every rank, or this rank's contiguous part for NCCL)."""
         from . import ops
 
         others = [r for r in range(self.world) if r != self.rank]
         peer = self.exchange == "peer" and self.world > 1
         plans = []
-
-        def stack(ts, planes):
-            items, ldy, peers, bases = [], [], [], []
-            for t in ts:
-                mant, exps = self.weight(copy, t)
-                r0, r1 = self.shards[t.name]
-                if self.world == 1 or peer:
-                    y = self.full[t.name].data_ptr() + 4 * r0
+        for i, L in enumerate(self.layers):
+            g0, g1 = self.shards[L.gate.name]
+            items, ldy = [], []
+            for t in (L.gate, L.up):
+                if g1 > g0:
+                    items.append((self.planes_in, *self.weight(copy, t), self.gu[t.name].data_ptr() + 4 * g0))
                     ldy.append(t.M)
-                else:
-                    y = self.part[t.name].data_ptr()
-                    ldy.append(self.padded_rows(t.M))
-                items.append((planes, mant, exps, y))
-                peers.append([self.peer_base[r] + self.voff[t.name] for r in others] if peer else [])
-                bases.append(r0 if peer else 0)
-            return ops.ShardedBatchedStack(items, ldy, peers, bases, self.world if peer else 1)
-
-        for L in self.layers:
-            plans.append((stack((L.gate, L.up), self.planes[L.gate.K]), stack((L.down,), self.planes[L.down.K])))
+            gu = ops.ShardedBatchedStack(items, ldy, [[] for _ in items], [0] * len(items), 1) if items else None
+            d0, d1 = self.shards[L.down.name]
+            planes = ops.planes_view(self.dq[i], self.B, L.down.K, self.ldxs)
+            if d1 <= d0:
+                dn = None
+            elif peer:
+                dn = ops.ShardedBatchedStack([(planes, *self.weight(copy, L.down),
+                                               self.full[L.down.name].data_ptr() + 4 * d0)], [L.down.M],
+                                             [[self.peer_base[r] + self.voff[L.down.name] for r in others]], [d0],
+                                             self.world)
+            elif self.world == 1:
+                dn = ops.ShardedBatchedStack([(planes, *self.weight(copy, L.down), self.full[L.down.name].data_ptr())],
+                                             [L.down.M], [[]], [0], 1)
+            else:
+                dn = ops.ShardedBatchedStack([(planes, *self.weight(copy, L.down), self.part[L.down.name].data_ptr())],
+                                             [self.padded_rows(L.down.M)], [[]], [0], 1)
+            plans.append((gu, dn))
         return plans
 
-    def _step_batched(self, copy):
+    # ------------------------------------------------------------ one step
+    def _activation(self, i, L, sig=0):
+        """The shard-local swiglu + quantizer of layer i into this rank's
+        down input (and, peer exchange, every other rank's), with an optional
+        epoch signal + wait."""
+        from . import ops
+
+        g0, g1 = self.shards[L.gate.name]
+        if g1 <= g0:
+            return
+        gp, up = self.gu[L.gate.name].data_ptr() + 4 * g0, self.gu[L.up.name].data_ptr() + 4 * g0
+        dst = [self.dq[i].data_ptr()]
+        if self.exchange == "peer" and self.world > 1:
+            dst += [self.peer_base[r] + self.qoff[i] for r in range(self.world) if r != self.rank]
+        if sig:
+            ops.swiglu_quant_sharded(gp, up, self.B, g1 - g0, L.gate.M, g0, L.down.K, self.B > 1, self.ldxs, dst,
+                                     sig_flags=self.peer_base, sig_ticket=self.peer_base[self.rank] + self.TICKET_OFFSET,
+                                     sig_epoch=sig, wait_flags=self.peer_base[self.rank], world=self.world,
+                                     rank=self.rank)
+        else:
+            ops.swiglu_quant_sharded(gp, up, self.B, g1 - g0, L.gate.M, g0, L.down.K, self.B > 1, self.ldxs, dst)
+
+    def _next_epoch(self):
+        self.epoch += 1
+        return self.epoch & 0xFFFFFFFF or 1
+
+    def step(self, copy=0):
+        """One token (or batch) through every layer."""
         from . import ops
 
         peer = self.exchange == "peer" and self.world > 1
         x = self.x0
-        for L, (gu, dn) in zip(self.layers, self.plans[copy]):
-            for plan, xin, outs, K in ((gu, x, (L.gate, L.up), L.gate.K),
-                                       (dn, self.full[L.gate.name], (L.down,), L.down.K)):
+        for i, (L, (gu, dn)) in enumerate(zip(self.layers, self.plans[copy])):
+            wait = self.epoch & 0xFFFFFFFF
+            if self.B > 1:
                 if peer:
-                    wait = self.epoch & 0xFFFFFFFF
-                    self.epoch += 1
-                    ops.quant_planes_wait(xin, self.planes[K], self.peer_base[self.rank], wait, self.world)
-                    plan.run(self.peer_base, self.epoch & 0xFFFFFFFF, self.rank)
+                    ops.quant_planes_wait(x, self.planes_in, self.peer_base[self.rank], wait, self.world)
                 else:
-                    ops.quant_planes(xin, self.planes[K])
-                    plan.run()
-                    if self.world > 1:
-                        for t in outs:
-                            self._gather(t)
+                    ops.quant_planes(x, self.planes_in)
+                if gu is not None:
+                    gu.run()
+            elif gu is not None:
+                if peer:
+                    gu.run_wait(self.peer_base[self.rank], wait, self.world)
+                else:
+                    gu.run()
+            if peer:
+                self._activation(i, L, self._next_epoch())
+                sig = self._next_epoch()
+                if dn is not None:
+                    if self.B > 1:
+                        dn.run(self.peer_base, sig, self.rank)
+                    else:
+                        dn.run(self.peer_base[self.rank], 0, self.peer_base, sig, self.rank)
+            else:
+                self._activation(i, L)
+                if self.world > 1:
+                    self._gather_activation(i, L)
+                if dn is not None:
+                    dn.run()
+                if self.world > 1:
+                    self._gather_down(L.down)
             x = self.full[L.down.name]
 
-    def _launch_peer(self, plan):
-        """Launch n waits for every rank's launch n - 1 and publishes n (one
-        rank: stream order is enough, no flags)."""
-        if self.world == 1:
-            plan.run(self.peer_base[0], 0, self.peer_base, 0, 0)
-            return
-        wait = self.epoch & 0xFFFFFFFF
-        self.epoch += 1
-        sig = self.epoch & 0xFFFFFFFF
-        plan.run(self.peer_base[self.rank], wait, [b for b in self.peer_base], sig, self.rank)
+    # ------------------------------------------------------------ NCCL gathers
+    def _gather_activation(self, i, L):
+        import torch.distributed as dist
 
-    def _gather(self, t):
+        B, W, K = self.B, self.world, L.down.K
+        g0, g1 = self.shards[L.gate.name]
+        Q = self.padded_rows(L.gate.M)
+        nbq = Q // 64
+        rec = self.dq[i]
+        qp, qg = self.part[("q", L.down.name)], self.gath[("q", L.down.name)]
+        sp, sg = self.part[("s", L.down.name)], self.gath[("s", L.down.name)]
+        if B == 1:
+            xq = rec[:2 * K].view(self._i16()).view(K)
+            xs = rec[2 * K:].view(self._f32()).view(K // 64)
+            qp[:g1 - g0].copy_(xq[g0:g1])
+            sp[:(g1 - g0) // 64].copy_(xs[g0 // 64:g1 // 64])
+            dist.all_gather_into_tensor(qg, qp, group=self.group)
+            dist.all_gather_into_tensor(sg, sp, group=self.group)
+            for r in range(W):
+                r0, r1 = shard_rows(L.gate.M, W, r)
+                if r1 > r0:
+                    xq[r0:r1].copy_(qg[r * Q:r * Q + r1 - r0])
+                    xs[r0 // 64:r1 // 64].copy_(sg[r * nbq:r * nbq + (r1 - r0) // 64])
+            return
+        planes = rec[:2 * B * K].view(self._i8()).view(2, B, K)
+        xs_t = rec[2 * B * K:].view(self._f32()).view(K // 64, self.ldxs)
+        qp.view(2, B, Q)[:, :, :g1 - g0].copy_(planes[:, :, g0:g1])
+        sp.view(nbq, self.ldxs)[:(g1 - g0) // 64].copy_(xs_t[g0 // 64:g1 // 64])
+        dist.all_gather_into_tensor(qg, qp, group=self.group)
+        dist.all_gather_into_tensor(sg, sp, group=self.group)
+        qv, sv = qg.view(W, 2, B, Q), sg.view(W, nbq, self.ldxs)
+        for r in range(W):
+            r0, r1 = shard_rows(L.gate.M, W, r)
+            if r1 > r0:
+                planes[:, :, r0:r1].copy_(qv[r, :, :, :r1 - r0])
+                xs_t[r0 // 64:r1 // 64].copy_(sv[r, :(r1 - r0) // 64])
+
+    def _gather_down(self, t):
         import torch.distributed as dist
 
         part, gath, full = self.part[t.name], self.gath[t.name], self.full[t.name]
-        if self.world == 1:
-            return
         B = self.B
-        if B == 1 and part.numel() * self.world == t.M:   # equal slices: gather straight into place
+        P = part.numel() // B
+        if B == 1 and P * self.world == t.M:   # equal slices: gather straight into place
             dist.all_gather_into_tensor(full, part, group=self.group)
             return
         dist.all_gather_into_tensor(gath, part, group=self.group)
-        P = part.numel() // B
         g = gath.view(self.world, B, P)
         f = full.view(B, t.M)
         for r in range(self.world):
@@ -342,35 +438,69 @@ class ShardedDeviceStack:
             if r1 > r0:
                 f[:, r0:r1].copy_(g[r, :, :r1 - r0])
 
-    def step(self, copy=0):
-        """One token through every layer (grouped GEMV launches + gathers)."""
-        if self.B > 1:
-            self._step_batched(copy)
-            return
-        if self.exchange == "peer":
-            for gu, dn in self.plans[copy]:
-                self._launch_peer(gu)
-                self._launch_peer(dn)
-            return
-        for L, (gu, dn) in zip(self.layers, self.plans[copy]):
-            if gu is not None:
-                gu.run()
-            self._gather(L.gate)
-            self._gather(L.up)
-            if dn is not None:
-                dn.run()
-            self._gather(L.down)
+    @staticmethod
+    def _i16():
+        import torch
+
+        return torch.int16
+
+    @staticmethod
+    def _i8():
+        import torch
+
+        return torch.int8
+
+    @staticmethod
+    def _f32():
+        import torch
+
+        return torch.float32
+
+    # ------------------------------------------------------------ results
+    def outputs(self):
+        """Every layer's complete quantized activation (as bytes) and down
+        output, concatenated as uint32 words (the values to compare across
+        runs bit for bit)."""
+        import numpy as np
+
+        parts = []
+        for i, L in enumerate(self.layers):
+            rec = self.dq[i].cpu().numpy()
+            parts.append(np.frombuffer(rec.tobytes() + b"\0" * ((-len(rec)) % 4), np.uint32))
+            parts.append(self.full[L.down.name].cpu().numpy().ravel().view(np.uint32))
+        return np.concatenate(parts)
+
+    def final_output(self):
+        """The last layer's down output (full, every rank)."""
+        return self.full[self.layers[-1].down.name]
 
     def bytes_per_step(self):
-        """Algorithmic bytes of one token over ALL ranks: the full weights
-        once, plus the fp32 activation in and output out of every GEMV."""
+        """Algorithmic bytes of one step over ALL ranks: the full weights
+        once; gate / up read the fp32 (batch 1) or planar (batch > 1) layer
+        input and write fp32; down reads the quantized activation and writes
+        fp32."""
+        from . import ops
+
         tot = 0
+        B = self.B
         for L in self.layers:
             for t in (L.gate, L.up, L.down):
-                if self.B == 1:
-                    tot += t.M * t.K + t.M * t.K // 64 + 4 * t.K + 4 * t.M
-                else:   # planar int16 activations + block scales in, fp32 out
-                    tot += t.M * t.K + t.M * t.K // 64 + self.B * (2 * t.K + 4 * (t.K // 64) + 4 * t.M)
+                tot += t.M * t.K + t.M * t.K // 64 + 4 * B * t.M
+            if B == 1:
+                tot += 2 * 4 * L.gate.K + ops.quant_record_bytes(L.down.K)
+            else:
+                tot += 2 * B * (2 * L.gate.K + 4 * (L.gate.K // 64)) + B * (2 * L.down.K + 4 * (L.down.K // 64))
+        return tot
+
+    def exchange_bytes_per_step(self):
+        """Bytes one rank sends to the others per step: its slice of every
+        quantized activation and of every down output, to each other rank."""
+        tot = 0
+        B = self.B
+        for L in self.layers:
+            g0, g1 = self.shards[L.gate.name]
+            d0, d1 = self.shards[L.down.name]
+            tot += (self.world - 1) * (B * (2 * (g1 - g0) + 4 * ((g1 - g0) // 64)) + 4 * B * (d1 - d0))
         return tot
 
     def device_error(self) -> int:
@@ -398,6 +528,7 @@ class ShardedDeviceStack:
             if self.world > 1:
                 dist.barrier(group=self.group)
             self.full = {}
+            self.dq = []
             self.flags = None
             self.region.close()
             self.region = None

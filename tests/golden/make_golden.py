@@ -8,6 +8,8 @@ reference C files compiled by ``make -C oracle ref``:
 
 Every fixture is produced by the reference's OWN code or recipe:
   packer.npz      05-主机侧源码/bfp8_packer.py pack_matrix_soa, imported and run
+  ref_numpy_gemv.npz  04-板载脚本与工具/qwen_real_engine.py gemv_bfp8 (its numpy
+                  fallback, :1233-1239), imported and run with no kernels
   ref_gemv.npz    04-板载脚本与工具/qwen_kernels_opt.c bfp8_gemv, compiled from
                   source for x86 (its scalar float path, :311-325)
   ref_lm.npz      qwen_kernels_opt.c lm_head_argmax and qwen_sampling.c
@@ -95,6 +97,38 @@ def make_ref_gemv(k):
         k.bfp8_gemv(y.ctypes.data, x.ctypes.data, mant.ctypes.data, exps.ctypes.data, M, K)
         out[f"{tag}_mant"], out[f"{tag}_exps"], out[f"{tag}_x"], out[f"{tag}_y"] = mant, exps, x, y
     np.savez_compressed(os.path.join(HERE, "ref_gemv.npz"), **out)
+
+
+def make_ref_numpy_gemv():
+    """The reference engine's numpy fallback (qwen_real_engine.py:1233-1239),
+    run as the reference's own method with no kernel library attached."""
+    sys.path.insert(0, os.path.join(REF, "04-板载脚本与工具"))
+    import qwen_real_engine as E  # the reference engine module itself
+
+    class NoKernels:
+        kernels = None
+
+        def __init__(self, views):
+            self.views = views
+
+        def _tensor_views(self, name):
+            return self.views[name]
+
+        def _y_buf(self, name, M):
+            return np.empty(M, np.float32)
+
+    rng = np.random.default_rng(1233)
+    out, views = {}, {}
+    for tag, (M, K) in {"a": (40, 1024), "b": (16, 4096), "c": (3, 192)}.items():
+        mant, exps = O.pack_bfp8(rng.normal(0, 0.02, (M, K)).astype(np.float32))
+        if tag == "c":
+            exps[0, 0] = 3      # a subnormal block scale 2^-131
+            exps[1, 2] = 200    # a large one
+        views[tag] = (mant.reshape(-1), exps.reshape(-1), M, K)
+        x = rng.normal(0, 1, K).astype(np.float32)
+        y = E.QwenRealEngine.gemv_bfp8(NoKernels(views), x, tag)
+        out[f"{tag}_mant"], out[f"{tag}_exps"], out[f"{tag}_x"], out[f"{tag}_y"] = mant, exps, x, y
+    np.savez_compressed(os.path.join(HERE, "ref_numpy_gemv.npz"), **out)
 
 
 # ------------------------------------------------------------------ lm_head
@@ -268,6 +302,7 @@ def main():
     k, s = ref_libs()
     make_packer()
     make_ref_gemv(k)
+    make_ref_numpy_gemv()
     make_ref_rmsnorm(k)
     make_ref_residual(k)
     make_ref_swiglu(k)

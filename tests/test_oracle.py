@@ -509,3 +509,13 @@ def test_add_residual_matches_fixture(golden):
     sub = (np.abs(g["x"]) < 1.18e-38) | (np.abs(g["r"]) < 1.18e-38) | (np.abs(g["y"]) < 1.18e-38)
     assert np.array_equal(yn[~sub].view(np.uint32), g["y"][~sub].view(np.uint32))
     assert yn[5] == 0.0
+
+
+def test_numpy_fallback_gemv_matches_reference_engine(golden):
+    """oracle.bfp8_gemv_numpy equals the reference engine's own numpy
+    fallback (qwen_real_engine.py:1233-1239, run as the reference's method in
+    make_golden.py) bit for bit, incl. a subnormal and a large block scale."""
+    g = golden("ref_numpy_gemv.npz")
+    for tag in ("a", "b", "c"):
+        y = O.bfp8_gemv_numpy(g[f"{tag}_x"], g[f"{tag}_mant"], g[f"{tag}_exps"])
+        assert np.array_equal(y.view(np.uint32), g[f"{tag}_y"].view(np.uint32)), tag

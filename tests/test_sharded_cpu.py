@@ -1,6 +1,8 @@
 """Host logic of the row-sharded multi-GPU stack, on CPU: shard planning and
-the gather data flow, run as world_size-2 gloo ranks with the oracle GEMV
-standing in for the kernel; results must equal a single-rank run bit for bit."""
+the data flow (gate / up slices, shard-local swiglu + quantizer, gathered
+int16 activation, down slices, gathered down rows), run as world_size-2 gloo
+ranks with the oracle standing in for the kernels; results must equal a
+single-rank run bit for bit."""
 import os
 import socket
 
@@ -51,20 +53,27 @@ def flow(world, rank, gather):
         m, e = W[name]
         return O.bfp8_gemv(x, m[r0:r1], e[r0:r1])
 
-    return sharded.run_layers(layers, x0, gemv, gather, world, rank)
+    def act_quant(g, u):
+        return O.quant_x(O.swiglu(g, u, neon=True))
+
+    def gemv_q(name, xq, xs, r0, r1):
+        m, e = W[name]
+        return O.bfp8_gemv_q(xq, xs, m[r0:r1], e[r0:r1])
+
+    return sharded.run_layers(layers, x0, gemv, act_quant, gemv_q, gather, world, rank)
 
 
 def _worker(rank, world, port, out_path):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
 
-    def gather(y_shard, M):
+    def gather(part):
         parts = [None] * world
-        dist.all_gather_object(parts, y_shard)
+        dist.all_gather_object(parts, part)
         return np.concatenate(parts)
 
     outs = flow(world, rank, gather)
-    np.save(out_path + f".{rank}.npy", np.concatenate(outs))
+    np.save(out_path + f".{rank}.npy", np.concatenate([o.view(np.uint8) for o in outs]))
     dist.destroy_process_group()
 
 
@@ -77,9 +86,11 @@ def _free_port():
 
 
 def test_two_rank_gloo_flow_matches_single_rank(tmp_path):
-    single = np.concatenate(flow(1, 0, lambda y, M: y))
+    """The shard-local swiglu + quantizer, the gathered int16 activation and
+    the down rows: every gathered value equals the single-rank flow's."""
+    single = np.concatenate([o.view(np.uint8) for o in flow(1, 0, lambda part: part)])
     path = str(tmp_path / "out")
     mp.start_processes(_worker, args=(2, _free_port(), path), nprocs=2, join=True, start_method="spawn")
     for r in range(2):
         got = np.load(path + f".{r}.npy")
-        assert np.array_equal(got.view(np.uint32), single.view(np.uint32)), r
+        assert np.array_equal(got, single), r
