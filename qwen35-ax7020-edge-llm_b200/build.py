@@ -4,11 +4,10 @@
 
 produces, in-tree:
   qwen_b200/libqwen_kernels_b200.so   CUDA kernels + C ABI (nvcc, sm_100a)
-  qwen_b200/_C*.so                    PyTorch operator library (torch.ops.qwen_b200)
+  qwen_b200/libqwen_b200_torch.so     PyTorch operator library (torch.ops.qwen_b200)
 """
 from __future__ import annotations
 
-import glob
 import os
 import shutil
 import subprocess
@@ -20,6 +19,7 @@ CSRC = os.path.join(PKG_ROOT, "csrc")
 OUT_DIR = os.path.join(PKG_ROOT, "qwen_b200")
 INCLUDE = os.path.join(REPO, "include")
 LIB_NAME = "libqwen_kernels_b200.so"
+TORCH_LIB_NAME = "libqwen_b200_torch.so"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CU_SOURCES = ["bfp8_gemv.cu", "bfp8_gemm_tc.cu", "lm_head.cu", "pack.cu", "sample.cu", "tma.cu", "capi.cu",
@@ -55,38 +55,29 @@ def build_core(force: bool = False, verbose: bool = False) -> str:
     return target
 
 
-def build_torch_ext(force: bool = False) -> str | None:
-    """Compile the torch.ops.qwen_b200 operator library (C++ only; it calls
-    the C ABI of the core library)."""
-    src = os.path.join(CSRC, "torch_ops.cpp")
-    if not os.path.exists(src):
-        return None
-    existing = glob.glob(os.path.join(OUT_DIR, "_C*.so"))
-    core = os.path.join(OUT_DIR, LIB_NAME)
-    if existing and not force and not _stale(existing[0], [src, core, os.path.join(INCLUDE, "qwen_b200.h")]):
-        return existing[0]
+def build_torch_ext(force: bool = False) -> str:
+    """Compile the torch.ops.qwen_b200 operator library (C++ only; every
+    operator calls the C ABI of the core library) into qwen_b200/ beside the
+    core library, which it finds through an $ORIGIN rpath."""
+    import torch
     import torch.utils.cpp_extension as ce
-    from torch.utils.cpp_extension import _get_build_directory  # noqa: F401  (import check)
 
-    build_dir = os.path.join(PKG_ROOT, "_build", "torch_ext")
-    os.makedirs(build_dir, exist_ok=True)
-    ce.load(
-        name="_C",
-        sources=[src],
-        extra_include_paths=[INCLUDE, CSRC],
-        extra_cflags=["-O2", "-std=c++17"],
-        extra_ldflags=[f"-L{OUT_DIR}", "-lqwen_kernels_b200", "-Wl,-rpath,$ORIGIN"],
-        build_directory=build_dir,
-        is_python_module=False,
-        with_cuda=True,
-        verbose=False,
-    )
-    built = glob.glob(os.path.join(build_dir, "_C*.so"))
-    if not built:
-        raise RuntimeError("torch extension build produced no library")
-    dst = os.path.join(OUT_DIR, os.path.basename(built[0]))
-    shutil.copy2(built[0], dst)
-    return dst
+    src = os.path.join(CSRC, "torch_ops.cpp")
+    core = os.path.join(OUT_DIR, LIB_NAME)
+    target = os.path.join(OUT_DIR, TORCH_LIB_NAME)
+    if not force and not _stale(target, [src, core, os.path.join(INCLUDE, "qwen_b200.h")]):
+        return target
+    cuda_home = ce.CUDA_HOME or "/usr/local/cuda"
+    cmd = [shutil.which("g++") or "g++", "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden",
+           f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
+           *[f"-I{p}" for p in ce.include_paths()], f"-I{os.path.join(cuda_home, 'include')}", f"-I{INCLUDE}",
+           src, "-o", target + ".tmp",
+           *[f"-L{p}" for p in ce.library_paths()], f"-L{OUT_DIR}",
+           "-lc10", "-lc10_cuda", "-ltorch_cpu", "-ltorch_cuda", "-ltorch", "-lqwen_kernels_b200",
+           "-Wl,-rpath,$ORIGIN"]
+    subprocess.run(cmd, check=True)
+    os.replace(target + ".tmp", target)
+    return target
 
 
 def build_all(force: bool = False, verbose: bool = False) -> None:

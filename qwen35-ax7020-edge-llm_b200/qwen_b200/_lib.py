@@ -11,6 +11,7 @@ import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libqwen_kernels_b200.so")
+TORCH_LIB_PATH = os.path.join(HERE, "libqwen_b200_torch.so")
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -85,6 +86,24 @@ def load() -> ctypes.CDLL:
             fn.argtypes = args
         _lib = lib
     return _lib
+
+
+_torch_ops = None
+
+
+def torch_ops():
+    """torch.ops.qwen_b200 (the PyTorch operator library, built in-tree by
+    ``build.py``); raises if the library is absent."""
+    global _torch_ops
+    if _torch_ops is None:
+        import torch
+
+        if not os.path.exists(TORCH_LIB_PATH):
+            raise OSError(f"{TORCH_LIB_PATH} is missing: run qwen35-ax7020-edge-llm_b200/build.py")
+        load()   # the operator library resolves the kernel library through its rpath
+        torch.ops.load_library(TORCH_LIB_PATH)
+        _torch_ops = torch.ops.qwen_b200
+    return _torch_ops
 
 
 class KernelError(RuntimeError):

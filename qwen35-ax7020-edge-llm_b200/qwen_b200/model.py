@@ -127,6 +127,116 @@ def bfp8_tensors(manifest: dict) -> list[tuple[str, int, int, int]]:
     return out
 
 
+def file_layout(entries) -> tuple[dict, int]:
+    """File offsets of (name, byte_size) entries written in order with every
+    tensor starting on a 64-byte boundary -- the reference exporter's rule
+    (05-主机侧源码/export_qwen35_weights_bfp8_64k.py:31,64-80), which gives
+    every file_offset of qwen35_weights_64k_manifest.json."""
+    off, table = 0, {}
+    for name, size in entries:
+        off = align64(off)
+        table[name] = off
+        off += size
+    return table, off
+
+
+class WeightFile:
+    """A BFP8 weight file and its manifest (the reference's
+    qwen35_weights_64k.bin + qwen35_weights_64k_manifest.json), read the way
+    the reference engine reads them: the file is mapped read-only
+    (qwen_real_engine.py:741-756) -- or any host buffer holding its bytes is
+    used -- and every BFP8 tensor is a zero-copy numpy view at its
+    file_offset, mantissas int8 [M][K] then exponents uint8 [M][K/64]
+    (:1188-1206, :834-846).  ``views`` pointers are what the engine passes to
+    bfp8_gemv, so ``register()`` (the whole mapping, once) lets the drop-in
+    C ABI find every tensor on the device; ``to_device`` uploads the tensors
+    for the device API."""
+
+    def __init__(self, manifest: dict, path: str | None = None, buffer=None):
+        import mmap
+
+        import numpy as np
+
+        self.manifest = manifest
+        if (path is None) == (buffer is None):
+            raise ValueError("WeightFile: give a path or a buffer")
+        self._f = self._mm = None
+        if path is not None:
+            self._f = open(path, "rb")
+            self._mm = mmap.mmap(self._f.fileno(), 0, access=mmap.ACCESS_READ)
+            self.buf = np.frombuffer(self._mm, dtype=np.uint8)
+        else:
+            self.buf = np.frombuffer(buffer, dtype=np.uint8)
+        self.names = [n for n, _, _, _ in sorted(bfp8_tensors(manifest), key=lambda e: e[1])]
+        for n in self.names:
+            info = manifest["tensors"][n]
+            if info["file_offset"] + info["byte_size"] > self.buf.nbytes:
+                raise ValueError(f"WeightFile: {n} lies beyond the end of the file")
+
+    def stack(self) -> list[Linear]:
+        """The BFP8 tensors as GEMV shapes, in file order (the order the
+        engine issues them in a token)."""
+        return [Linear(n, *self.manifest["tensors"][n]["shape"]) for n in self.names]
+
+    def views(self, name: str):
+        """(mant int8 [M, K], exps uint8 [M, K/64]) zero-copy host views."""
+        info = self.manifest["tensors"][name]
+        M, K = info["shape"]
+        off = info["file_offset"]
+        mant = self.buf[off:off + M * K].view("int8").reshape(M, K)
+        exps = self.buf[off + M * K:off + M * K + M * K // 64].reshape(M, K // 64)
+        return mant, exps
+
+    def register(self) -> None:
+        """Upload the whole file once for the drop-in C ABI: later bfp8_gemv
+        calls whose pointers fall inside it use the device copy."""
+        from ._lib import check, load
+
+        check(load().qwen_b200_register_weights(self.buf.ctypes.data, self.buf.nbytes), "WeightFile.register")
+
+    def forget(self) -> None:
+        from ._lib import load
+
+        load().qwen_b200_forget_weights(self.buf.ctypes.data)
+
+    def to_device(self, device="cuda", names=None) -> "DeviceWeights":
+        return DeviceWeights(self, device, names)
+
+    def close(self) -> None:
+        self.buf = None
+        if self._mm is not None:
+            self._mm.close()
+            self._f.close()
+            self._mm = self._f = None
+
+
+class DeviceWeights:
+    """The BFP8 tensors of a WeightFile on one GPU: the file span from the
+    first to the last of them copied in one transfer, so every tensor keeps
+    its file_offset (relative to the span) and its SoA layout."""
+
+    def __init__(self, wf: WeightFile, device="cuda", names=None):
+        import torch
+
+        self.names = list(names) if names is not None else list(wf.names)
+        self.info = {n: wf.manifest["tensors"][n] for n in self.names}
+        lo = min(i["file_offset"] for i in self.info.values())
+        hi = max(i["file_offset"] + i["byte_size"] for i in self.info.values())
+        self.base = lo
+        self.buf = torch.from_numpy(wf.buf[lo:hi].copy()).to(device)
+
+    def views(self, name: str):
+        """(mant int8 [M, K], exps uint8 [M, K/64]) device views."""
+        import torch
+
+        info = self.info[name]
+        M, K = info["shape"]
+        o = info["file_offset"] - self.base
+        mant = self.buf[o:o + M * K].view(torch.int8).view(M, K)
+        exps = self.buf[o + M * K:o + M * K + M * K // 64].view(M, K // 64)
+        return mant, exps
+
+
 class DeviceStack:
     """One or more copies of a synthetic BFP8 stack resident on a CUDA device.
 

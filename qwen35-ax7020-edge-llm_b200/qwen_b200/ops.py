@@ -1,8 +1,12 @@
 """Device-tensor API of the hot path (PyTorch tensors in, PyTorch tensors out).
 
-Every function runs on torch's current CUDA stream and raises
-``KernelError`` on failure.  The arithmetic is the reference NEON build's,
-bit-for-bit (see include/qwen_b200.h).
+Every function runs on torch's current CUDA stream and raises on failure.
+The arithmetic is the reference NEON build's, bit-for-bit (see
+include/qwen_b200.h).  Calls that return fresh tensors go through the
+PyTorch operators ``torch.ops.qwen_b200.*`` (csrc/torch_ops.cpp, errors as
+RuntimeError); calls that write caller-provided buffers (``out=``), grouped
+plans and the sharded launches call the C ABI directly (errors as
+KernelError).  Both reach the same entry points of libqwen_kernels_b200.so.
 
 Reference routines served (ideal1128/qwen35-ax7020-edge-llm):
   quant_block64   04-板载脚本与工具/qwen_kernels_opt.c:182-205 (quant_x_blocks)
@@ -19,7 +23,9 @@ from dataclasses import dataclass
 
 import torch
 
-from ._lib import KernelError, check, load
+from ._lib import KernelError, check, load, torch_ops
+
+T = torch_ops()   # torch.ops.qwen_b200: loading fails loudly without the built libraries
 
 __all__ = [
     "KernelError", "quant_block64", "bfp8_gemv", "bfp8_gemv_fast", "bfp8_gemv_q", "lm_head_bf16", "lm_head_bfp8",
@@ -47,13 +53,7 @@ def _need(t: torch.Tensor, dtype: torch.dtype, name: str) -> torch.Tensor:
 
 def quant_block64(x: torch.Tensor):
     """x fp32 [..., K] -> (xq int16 [..., K], xs fp32 [..., K/64])."""
-    x = _need(x, torch.float32, "x")
-    K = x.shape[-1]
-    B = x.numel() // K if K else 0
-    xq = torch.empty(x.shape, dtype=torch.int16, device=x.device)
-    xs = torch.empty((*x.shape[:-1], K // 64), dtype=torch.float32, device=x.device)
-    check(load().qwen_b200_quant_dev(_ptr(x), B, K, _ptr(xq), _ptr(xs), _stream()), "quant_block64")
-    return xq, xs
+    return T.quant_block64(_need(x, torch.float32, "x"))
 
 
 def bfp8_gemv(x: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor, out: torch.Tensor | None = None):
@@ -64,8 +64,10 @@ def bfp8_gemv(x: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor, out: torc
     M, K = mant.shape
     if x.shape[-1] != K or exps.numel() < M * (K // 64):
         raise ValueError("shape mismatch")
+    if out is None:
+        return T.bfp8_gemv(x, mant, exps, "exact")
     rows = x.reshape(-1, K)
-    y = out if out is not None else torch.empty((*x.shape[:-1], M), dtype=torch.float32, device=x.device)
+    y = out
     yr = y.view(-1, M)
     L = load()
     for i in range(rows.shape[0]):
@@ -81,7 +83,9 @@ def bfp8_gemv_fast(x: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor, out:
     mant = _need(mant, torch.int8, "mant")
     exps = _need(exps, torch.uint8, "exps")
     M, K = mant.shape
-    y = out if out is not None else torch.empty(M, dtype=torch.float32, device=x.device)
+    if out is None:
+        return T.bfp8_gemv(x, mant, exps, "fast")
+    y = out
     check(load().qwen_b200_gemv_fast_dev(_ptr(y), _ptr(x), _ptr(mant), _ptr(exps), M, K, _stream()), "bfp8_gemv_fast")
     return y
 
@@ -127,15 +131,8 @@ def residual_rmsnorm_bfp8_gemv(x: torch.Tensor, res: torch.Tensor, norm_w: torch
 
 def bfp8_gemv_q(xq: torch.Tensor, xs: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor):
     """y = BFP8 GEMV of an already quantized activation (xq int16 [K], xs fp32 [K/64])."""
-    xq = _need(xq, torch.int16, "xq")
-    xs = _need(xs, torch.float32, "xs")
-    mant = _need(mant, torch.int8, "mant")
-    exps = _need(exps, torch.uint8, "exps")
-    M, K = mant.shape
-    y = torch.empty(M, dtype=torch.float32, device=mant.device)
-    check(load().qwen_b200_gemv_q_dev(_ptr(y), _ptr(xq), _ptr(xs), _ptr(mant), _ptr(exps), M, K, _stream()),
-          "bfp8_gemv_q")
-    return y
+    return T.bfp8_gemv_q(_need(xq, torch.int16, "xq"), _need(xs, torch.float32, "xs"),
+                         _need(mant, torch.int8, "mant"), _need(exps, torch.uint8, "exps"), "exact")
 
 
 def swiglu_bfp8_gemv(gate: torch.Tensor, up: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor):
@@ -229,7 +226,10 @@ def quant_planes(x: torch.Tensor, out: Planes | None = None) -> Planes:
     (256*hi + lo equals quant_block64's xq bit for bit)."""
     x = _need(x, torch.float32, "x")
     B, K = x.shape
-    p = out if out is not None else planes_empty(B, K, x.device)
+    if out is None:
+        planes, xs_t = T.quant_planes(x)
+        return Planes(planes, xs_t, B, K)
+    p = out
     check(load().qwen_b200_quant_planes_dev(_ptr(x), B, K, _ptr(p.planes), _ptr(p.xs_t), p.ldxs, _stream()),
           "quant_planes")
     return p
@@ -244,6 +244,8 @@ def bfp8_gemm_tc(p: Planes, mant: torch.Tensor, exps: torch.Tensor, out: torch.T
     M, K = mant.shape
     if K != p.K or exps.numel() < M * (K // 64):
         raise ValueError("shape mismatch")
+    if out is None and not dots:
+        return T.bfp8_gemm_tc(p.planes, p.xs_t, mant, exps)
     y = out if out is not None else torch.empty((p.B, M), dtype=torch.float32, device=mant.device)
     d = torch.empty((p.B, M, K // 64), dtype=torch.int32, device=mant.device) if dots else None
     check(load().qwen_b200_gemm_tc_dev(_ptr(y), _ptr(p.planes), _ptr(p.xs_t), p.ldxs, _ptr(mant), _ptr(exps), M, K,
@@ -334,7 +336,9 @@ def lm_head_bf16(h: torch.Tensor, E: torch.Tensor, k: int = 0, out: LmResult | N
         raise TypeError("E must hold bf16 bit patterns (bfloat16/int16/uint16)")
     E = E.contiguous()
     V, H = E.shape
-    r = _lm_check_out(out, h.device, min(k, V)) if out is not None else _lm_outputs(h.device, min(k, V))
+    if out is None:
+        return LmResult(*T.lm_head_bf16(h, E.view(torch.int16), k))
+    r = _lm_check_out(out, h.device, min(k, V))
     check(load().qwen_b200_lm_head_bf16_dev(_ptr(h), _ptr(E), V, H, k, _ptr(r.argmax), _ptr(r.ids),
                                             _ptr(r.scores), _ptr(r.n), _stream()), "lm_head_bf16")
     return r
@@ -348,7 +352,9 @@ def lm_head_bfp8(h: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor, k: int
     mant = _need(mant, torch.int8, "mant")
     exps = _need(exps, torch.uint8, "exps")
     V, H = mant.shape
-    r = _lm_check_out(out, h.device, min(k, V)) if out is not None else _lm_outputs(h.device, min(k, V))
+    if out is None:
+        return LmResult(*T.lm_head_bfp8(h, mant, exps, k))
+    r = _lm_check_out(out, h.device, min(k, V))
     check(load().qwen_b200_lm_head_bfp8_dev(_ptr(h), _ptr(mant), _ptr(exps), V, H, k, _ptr(r.argmax),
                                             _ptr(r.ids), _ptr(r.scores), _ptr(r.n), _stream()),
           "lm_head_bfp8")
@@ -365,6 +371,9 @@ def sample_topk(ids: torch.Tensor, scores: torch.Tensor, temperature: float, top
     id).  Returns the chosen id as an int32 [1] device tensor (no sync)."""
     ids = _need(ids, torch.int32, "ids")
     scores = _need(scores, torch.float32, "scores")
+    if out is None and n is not None and rng_state is not None and rng_state.is_contiguous():
+        return T.sample_topk(ids, scores, _need(n, torch.int32, "n"), float(temperature), int(top_k), float(top_p),
+                             _need(rng_state, torch.int32, "rng_state"))
     if out is None:
         out = torch.empty(1, dtype=torch.int32, device=ids.device)
     for t, name in ((rng_state, "rng_state"), (out, "out")):
@@ -383,6 +392,8 @@ def pack_bfp8(w: torch.Tensor, out_mant: torch.Tensor | None = None, out_exps: t
     """Pack fp32 [M, K] weights into (mant int8 [M, K], exps uint8 [M, K/64]) on the device."""
     w = _need(w, torch.float32, "w")
     M, K = w.shape
+    if out_mant is None and out_exps is None:
+        return T.pack_bfp8(w)
     mant = out_mant if out_mant is not None else torch.empty((M, K), dtype=torch.int8, device=w.device)
     exps = out_exps if out_exps is not None else torch.empty((M, K // 64), dtype=torch.uint8, device=w.device)
     rc = load().qwen_b200_pack_bfp8_dev(_ptr(w), M, K, _ptr(mant), _ptr(exps), _stream())

@@ -10,6 +10,8 @@ Every fixture is produced by the reference's OWN code or recipe:
   packer.npz      05-主机侧源码/bfp8_packer.py pack_matrix_soa, imported and run
   ref_numpy_gemv.npz  04-板载脚本与工具/qwen_real_engine.py gemv_bfp8 (its numpy
                   fallback, :1233-1239), imported and run with no kernels
+  manifest_64k.json   06-模型与权重/qwen35_weights_64k_manifest.json, every
+                  tensor entry (board addresses dropped)
   ref_gemv.npz    04-板载脚本与工具/qwen_kernels_opt.c bfp8_gemv, compiled from
                   source for x86 (its scalar float path, :311-325)
   ref_lm.npz      qwen_kernels_opt.c lm_head_argmax and qwen_sampling.c
@@ -129,6 +131,20 @@ def make_ref_numpy_gemv():
         y = E.QwenRealEngine.gemv_bfp8(NoKernels(views), x, tag)
         out[f"{tag}_mant"], out[f"{tag}_exps"], out[f"{tag}_x"], out[f"{tag}_y"] = mant, exps, x, y
     np.savez_compressed(os.path.join(HERE, "ref_numpy_gemv.npz"), **out)
+
+
+def make_manifest():
+    """The reference weight manifest (06-模型与权重/qwen35_weights_64k_manifest.json):
+    every tensor's dtype, shape, type, sizes and file_offset, in file order
+    (the physical DDR addresses of the board are dropped)."""
+    import json
+
+    with open(os.path.join(REF, "06-模型与权重", "qwen35_weights_64k_manifest.json"), encoding="utf-8") as f:
+        m = json.load(f)
+    out = {k: v for k, v in m.items() if k not in ("tensors", "ddr3_base_addr")}
+    out["tensors"] = {n: {k: v for k, v in t.items() if k != "phys_addr"} for n, t in m["tensors"].items()}
+    with open(os.path.join(HERE, "manifest_64k.json"), "w", encoding="utf-8") as f:
+        json.dump(out, f, indent=0, ensure_ascii=False)
 
 
 # ------------------------------------------------------------------ lm_head
@@ -303,6 +319,7 @@ def main():
     make_packer()
     make_ref_gemv(k)
     make_ref_numpy_gemv()
+    make_manifest()
     make_ref_rmsnorm(k)
     make_ref_residual(k)
     make_ref_swiglu(k)

@@ -134,3 +134,31 @@ def test_lm_head_topk_dropin_serves_k_above_1024(lib):
         assert np.array_equal(ids[:n], rids), k
         assert np.array_equal(bits(sc[:n]), bits(rsc)), k
     lib.qwen_b200_forget_weights(tab.ctypes.data)
+
+
+def test_weight_file_through_the_dropin_and_the_device_api(lib):
+    """A weight-file image laid out by the reference manifest (layer 0's six
+    BFP8 tensors filled): the engine's pointer pattern -- the whole mapping
+    registered once, bfp8_gemv on the views' addresses -- and the device API
+    on DeviceWeights both give the oracle's bits."""
+    import torch
+
+    from qwen_b200 import model, ops
+    from test_manifest_cpu import ref_manifest, synthetic_file
+
+    buf, names, sub = synthetic_file(ref_manifest())
+    wf = model.WeightFile(sub, buffer=buf)
+    wf.register()
+    dw = wf.to_device("cuda:0")
+    rng = np.random.default_rng(77)
+    for n in names:
+        mant, exps = wf.views(n)
+        M, K = mant.shape
+        x = rng.normal(0, 1, K).astype(np.float32)
+        ref = bits(O.bfp8_gemv(x, mant, exps))
+        y = np.zeros(M, np.float32)
+        lib.bfp8_gemv(y.ctypes.data, x.ctypes.data, mant.ctypes.data, exps.ctypes.data, M, K)
+        assert np.array_equal(bits(y), ref), n
+        dm, de = dw.views(n)
+        assert np.array_equal(bits(ops.bfp8_gemv(torch.from_numpy(x).cuda(), dm, de).cpu().numpy()), ref), n
+    wf.forget()

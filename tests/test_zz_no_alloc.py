@@ -95,8 +95,12 @@ _CHILD = textwrap.dedent(r"""
         cases.append((M, K, torch.from_numpy(mant).cuda(), torch.from_numpy(exps).cuda(),
                       torch.from_numpy(x).cuda(), torch.empty(M, dtype=torch.float32, device="cuda"),
                       O.bfp8_gemv(x, mant, exps)))
-    # the context's first kernel launch reserves memory of its own (2 MB was
-    # seen): take it with a torch kernel before the first reading
+    # the library carries its own CUDA runtime: cudaFree(NULL) through it
+    # initialises that runtime, which (eager loading) loads the library's
+    # device image -- code and the fixed scratch array, about 2 MB -- before
+    # the first reading; a torch kernel takes the context's first-launch
+    # reservations
+    assert lib.qwen_b200_dev_free(None) == 0
     warm = torch.ones(1024, device="cuda") * 2
     torch.cuda.synchronize()
     free0 = torch.cuda.mem_get_info()[0]
@@ -116,8 +120,8 @@ _CHILD = textwrap.dedent(r"""
 def test_noalloc_gemv_allocates_nothing_in_a_fresh_process(cuda):
     """Only the no-alloc entry point of the library runs in the child, so
     nothing else can have created the library's per-device buffers first.
-    Modules load eagerly at context creation and one torch kernel runs first
-    (a context reserves memory at its first launch), so the reading before
+    The library's runtime is initialised first (cudaFree(NULL), loading its
+    device image eagerly) and one torch kernel runs, so the reading before
     the first call already has the library image, its fixed array and the
     context's own reservations in place."""
     env = dict(os.environ, CUDA_MODULE_LOADING="EAGER")
