@@ -498,14 +498,16 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
                 const int s = (gs + j / C::kBPS) % C::kStages;
                 const float sm = exp_scale_ieee(e);
                 const float2 sm2 = make_float2(sm, sm);
-                const float2* xsv =
-                    reinterpret_cast<const float2*>(sxs + (size_t)s * C::kSBytes) + ((j % C::kBPS) * N + col0 + c) / 2;
+                const float4* xsv =
+                    reinterpret_cast<const float4*>(sxs + (size_t)s * C::kSBytes) + ((j % C::kBPS) * N + col0 + c) / 4;
 #pragma unroll
                 for (int k = 0; k < kCh; k += 2) {
+                    const float4 x4 = xsv[k / 4];   // one 16-byte load serves four columns
+                    const float2 xs2 = (k & 2) ? make_float2(x4.z, x4.w) : make_float2(x4.x, x4.y);
                     const float2 th = make_float2(__uint_as_float(hv[k]), __uint_as_float(hv[k + 1]));
                     const float2 tl = make_float2(__uint_as_float(lv[k]), __uint_as_float(lv[k + 1]));
                     const float2 fd = __fadd2_rn(__fadd2_rn(th, neg_magic), tl);
-                    acc[(c + k) / 2] = __ffma2_rn(fd, __fmul2_rn(sm2, xsv[k / 2]), acc[(c + k) / 2]);
+                    acc[(c + k) / 2] = __ffma2_rn(fd, __fmul2_rn(sm2, xs2), acc[(c + k) / 2]);
                     if constexpr (DOTS) {
 #pragma unroll
                         for (int w = 0; w < 2; w++) {

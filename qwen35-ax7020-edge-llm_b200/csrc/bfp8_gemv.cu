@@ -463,6 +463,96 @@ __device__ __forceinline__ void stage_blocks_rtl(const unsigned char* st, const 
     }
 }
 
+// Resident activation of a single GEMV: every CTA quantizes all K/64 blocks
+// of the activation into its own shared memory at `xact` (paired int16 words,
+// 2K bytes, then the K/64 fp32 scales), applying first -- as the flags of A
+// say -- the reference's swiglu (NEON build) or its add_residual + rmsnorm
+// (NEON order; CTA 0 also stores the updated residual stream).  Every thread
+// of the CTA calls it; it ends with a CTA barrier.
+__device__ __forceinline__ void quantize_resident(const WArgs& A, const GemvDesc& D, unsigned char* xact, int warp,
+                                                  int lane) {
+    const int nb = D.K >> 6;
+    uint32_t* xp = reinterpret_cast<uint32_t*>(xact);
+    float* xsc = reinterpret_cast<float*>(xact + (size_t)D.K * 2);
+    float nr = 0.0f;   // rmsnorm scale
+    if (A.norm_w) {
+        // rmsnorm, the reference's NEON build (qwen_kernels_opt.c:140-172):
+        // four lane sums of x*x over i = 4j + l (multiply, then add, both
+        // flushed), combined as (s0 + s2) + (s1 + s3); then, in IEEE
+        // single precision, r = 1 / sqrt(sum / K + eps)
+        __shared__ float s_nr;
+        if (warp == 0) {
+            float acc = 0.0f;
+            if (lane < 4)
+                for (int i = lane; i < D.K; i += 4) {
+                    // add_residual (qwen_kernels_opt.c:388-396): flushed lane adds
+                    const float v = A.norm_res ? add_ftz(D.x[i], A.norm_res[i]) : D.x[i];
+                    acc = add_ftz(acc, mul_ftz(v, v));
+                }
+            const float pair = add_ftz(acc, __shfl_down_sync(0xffffffffu, acc, 2));   // s0+s2, s1+s3
+            const float other = __shfl_down_sync(0xffffffffu, pair, 1);
+            if (lane == 0) {
+                const float sum = add_ftz(pair, other);
+                s_nr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)D.K), A.norm_eps)));
+            }
+        }
+        __syncthreads();
+        nr = s_nr;
+    }
+    for (int b0 = warp; b0 < nb; b0 += 4 * kWarps) {
+        float2 v[4];
+        if (D.x) {
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (b0 + j * kWarps < nb) v[j] = reinterpret_cast<const float2*>(D.x + 64 * (b0 + j * kWarps))[lane];
+            if (A.glu_up) {   // x holds the gate projection: swiglu(gate, up)
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    if (b0 + j * kWarps < nb) {
+                        const float2 u = reinterpret_cast<const float2*>(A.glu_up + 64 * (b0 + j * kWarps))[lane];
+                        v[j].x = swiglu_lane(v[j].x, u.x);
+                        v[j].y = swiglu_lane(v[j].y, u.y);
+                    }
+            }
+            if (A.norm_w) {   // y = x * (r * (1 + w)), flushed like the vector unit
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    if (b0 + j * kWarps < nb) {
+                        if (A.norm_res) {
+                            const float2 rr =
+                                reinterpret_cast<const float2*>(A.norm_res + 64 * (b0 + j * kWarps))[lane];
+                            v[j].x = add_ftz(v[j].x, rr.x);
+                            v[j].y = add_ftz(v[j].y, rr.y);
+                            if (blockIdx.x == 0)
+                                reinterpret_cast<float2*>(A.norm_xout + 64 * (b0 + j * kWarps))[lane] = v[j];
+                        }
+                        const float2 w =
+                            reinterpret_cast<const float2*>(A.norm_w + 64 * (b0 + j * kWarps))[lane];
+                        v[j].x = mul_ftz(v[j].x, mul_ftz(nr, add_ftz(1.0f, w.x)));
+                        v[j].y = mul_ftz(v[j].y, mul_ftz(nr, add_ftz(1.0f, w.y)));
+                    }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int b = b0 + j * kWarps;
+            if (b >= nb) break;
+            int q0, q1;
+            float xs;
+            if (D.x) {
+                block_quant(v[j], q0, q1, xs);
+            } else {
+                short2 w = reinterpret_cast<const short2*>(D.xq + 64 * b)[lane];
+                q0 = w.x;
+                q1 = w.y;
+                xs = D.xs[b];
+            }
+            block_store(xp, xsc, b, lane, q0, q1, xs);
+        }
+    }
+    __syncthreads();
+}
+
 // LM: lm_head epilogue (argmax / top-k instead of stores).  FAST: fast-mode
 // arithmetic.  RTL: the RTL dequant mode (one int32 word per row, stored in
 // y's bits, sticky flags ORed into A.rtl_flags).
@@ -629,89 +719,7 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
     }
 
     if (res) {
-        // resident activation: this CTA quantizes all nb blocks of the single
-        // GEMV's activation into the (otherwise unused) activation-ring space
-        const GemvDesc& D = wdesc(A, 0);
-        const int nb = D.K >> 6;
-        uint32_t* xp = reinterpret_cast<uint32_t*>(xrings);
-        float* xsc = reinterpret_cast<float*>(xrings + (size_t)D.K * 2);
-        float nr = 0.0f;   // rmsnorm scale
-        if (A.norm_w) {
-            // rmsnorm, the reference's NEON build (qwen_kernels_opt.c:140-172):
-            // four lane sums of x*x over i = 4j + l (multiply, then add, both
-            // flushed), combined as (s0 + s2) + (s1 + s3); then, in IEEE
-            // single precision, r = 1 / sqrt(sum / K + eps)
-            __shared__ float s_nr;
-            if (warp == 0) {
-                float acc = 0.0f;
-                if (lane < 4)
-                    for (int i = lane; i < D.K; i += 4) {
-                        // add_residual (qwen_kernels_opt.c:388-396): flushed lane adds
-                        const float v = A.norm_res ? add_ftz(D.x[i], A.norm_res[i]) : D.x[i];
-                        acc = add_ftz(acc, mul_ftz(v, v));
-                    }
-                const float pair = add_ftz(acc, __shfl_down_sync(0xffffffffu, acc, 2));   // s0+s2, s1+s3
-                const float other = __shfl_down_sync(0xffffffffu, pair, 1);
-                if (lane == 0) {
-                    const float sum = add_ftz(pair, other);
-                    s_nr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)D.K), A.norm_eps)));
-                }
-            }
-            __syncthreads();
-            nr = s_nr;
-        }
-        for (int b0 = warp; b0 < nb; b0 += 4 * kWarps) {
-            float2 v[4];
-            if (D.x) {
-#pragma unroll
-                for (int j = 0; j < 4; j++)
-                    if (b0 + j * kWarps < nb) v[j] = reinterpret_cast<const float2*>(D.x + 64 * (b0 + j * kWarps))[lane];
-                if (A.glu_up) {   // x holds the gate projection: swiglu(gate, up)
-#pragma unroll
-                    for (int j = 0; j < 4; j++)
-                        if (b0 + j * kWarps < nb) {
-                            const float2 u = reinterpret_cast<const float2*>(A.glu_up + 64 * (b0 + j * kWarps))[lane];
-                            v[j].x = swiglu_lane(v[j].x, u.x);
-                            v[j].y = swiglu_lane(v[j].y, u.y);
-                        }
-                }
-                if (A.norm_w) {   // y = x * (r * (1 + w)), flushed like the vector unit
-#pragma unroll
-                    for (int j = 0; j < 4; j++)
-                        if (b0 + j * kWarps < nb) {
-                            if (A.norm_res) {
-                                const float2 rr =
-                                    reinterpret_cast<const float2*>(A.norm_res + 64 * (b0 + j * kWarps))[lane];
-                                v[j].x = add_ftz(v[j].x, rr.x);
-                                v[j].y = add_ftz(v[j].y, rr.y);
-                                if (blockIdx.x == 0)
-                                    reinterpret_cast<float2*>(A.norm_xout + 64 * (b0 + j * kWarps))[lane] = v[j];
-                            }
-                            const float2 w =
-                                reinterpret_cast<const float2*>(A.norm_w + 64 * (b0 + j * kWarps))[lane];
-                            v[j].x = mul_ftz(v[j].x, mul_ftz(nr, add_ftz(1.0f, w.x)));
-                            v[j].y = mul_ftz(v[j].y, mul_ftz(nr, add_ftz(1.0f, w.y)));
-                        }
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int b = b0 + j * kWarps;
-                if (b >= nb) break;
-                int q0, q1;
-                float xs;
-                if (D.x) {
-                    block_quant(v[j], q0, q1, xs);
-                } else {
-                    short2 w = reinterpret_cast<const short2*>(D.xq + 64 * b)[lane];
-                    q0 = w.x;
-                    q1 = w.y;
-                    xs = D.xs[b];
-                }
-                block_store(xp, xsc, b, lane, q0, q1, xs);
-            }
-        }
-        __syncthreads();
+        quantize_resident(A, wdesc(A, 0), xrings, warp, lane);
     } else {
         // the activations come from act_prep (programmatic dependent launch)
         asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -797,6 +805,140 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
         unsigned long long* work = reinterpret_cast<unsigned long long*>(rings);
         lm_finish(A.sc, cand, kCandCap, &s_cand_count, work, (kWarps * kRing * kStage) / 8, lm.best, A.kk, A.out_id,
                   A.out_ids, A.out_scores, A.out_n, s_red, lm.wl);
+    }
+}
+
+// ---------------------------------------------------- single GEMV, split K
+// A single exact GEMV whose activation fits shared memory (K <= 6144): one
+// CTA per 32-row group, its 8 warps splitting the group's 256-byte K stages
+// (warp w takes stages w, w + 8, w + 16), so every weight byte of the group
+// is requested at once -- a short GEMV then costs about one memory round
+// trip, not one per stage.  A warp turns each block's four lane-class sums
+// into the operands of the reference's chain, (float(L_j) * 2^(e-134)) *
+// xs (flushed multiplies; for the odd last row the scalar VFP term of the
+// whole block dot), and keeps them in registers; when every warp is done they
+// meet in shared memory over the drained stage buffers and warp 0 adds them
+// lane by lane in block order -- the float order of the reference, bit for
+// bit.  Weight and exponent loads go out before griddepcontrol.wait, so as a
+// programmatic dependent launch the kernel streams its weights during the
+// previous kernel's tail; it reads the activation and writes only after it.
+constexpr int kSplitMaxStages = 3;   // stages per warp: K <= 8 * 3 * 256 = 6144
+
+static size_t split_smem_bytes(int K) {
+    const int nst = K >> 8, spw = (nst + kWarps - 1) / kWarps;
+    return 1024 + (size_t)kWarps * spw * kStage + ((2 * (size_t)K + (size_t)K / 16 + 127) & ~size_t(127)) +
+           (size_t)kWarps * spw * (128 + 8);
+}
+
+// SPW: the most stages one warp takes (K <= SPW * 2048); its terms stay in registers.
+template <int SPW>
+__global__ void __launch_bounds__(kThreads, SPW == 1 ? 2 : 1) gemv_split_kernel(const __grid_constant__ WArgs A) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                           ~uintptr_t(1023));
+    const GemvDesc& D = A.single;
+    const int K = D.K, M = D.M, nb = K >> 6, nst = K >> 8;
+    const int spw = (nst + kWarps - 1) / kWarps;
+    unsigned char* rings = smem;                                                  // [warp][spw] stages
+    unsigned char* xact = rings + (size_t)kWarps * spw * kStage;                  // resident activation
+    unsigned char* erings = xact + ((2 * (size_t)K + (size_t)K / 16 + 127) & ~size_t(127));   // [warp][spw][lane]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(erings + (size_t)kWarps * spw * 128);         // [warp][spw]
+
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    unsigned char* ring = rings + (size_t)warp * spw * kStage;
+    unsigned char* ering = erings + (size_t)warp * spw * 128;
+    uint64_t* bar = bars + warp * spw;
+    if (lane == 0) {
+        for (int k = 0; k < spw; k++) mbar_init(&bar[k], 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+    const int sw = lane & 7;
+    uint32_t phase = 0;
+    bool first = true;
+    for (int u = blockIdx.x; u < A.total_units; u += gridDim.x, phase ^= 1u) {
+        const int r0 = u * kRows;
+        const bool row_ok = r0 + lane < M;
+        // every stage of this warp's share goes out at once (weights are immutable)
+#pragma unroll
+        for (int k = 0; k < SPW; k++) {
+            const int st = warp + k * kWarps;
+            if (st >= nst) break;
+            if (lane == 0) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive_expect_tx(&bar[k], kStage);
+                tma_load_2d(ring + k * kStage, &D.tmap, st * 256, r0, &bar[k]);
+                tma_load_2d(ring + k * kStage + kBox, &D.tmap, st * 256 + 128, r0, &bar[k]);
+            }
+            if (row_ok) cp_async4(ering + k * 128 + lane * 4, D.exps + (size_t)(r0 + lane) * nb + st * 4);
+        }
+        cp_async_commit();
+        if (first) {
+            // the activation may be the previous kernel's output: read only now
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            quantize_resident(A, D, xact, warp, lane);
+            first = false;
+        }
+        cp_async_wait<0>();
+        __syncwarp();
+        const bool odd = (M & 1) && r0 + lane == M - 1;   // the odd last row: scalar VFP arithmetic
+        float t[SPW][4][4];
+#pragma unroll
+        for (int k = 0; k < SPW; k++) {
+            const int st = warp + k * kWarps;
+            if (st >= nst) break;
+            mbar_wait(&bar[k], phase, A.err);
+            const uint32_t ew = *reinterpret_cast<const uint32_t*>(ering + k * 128 + lane * 4);
+            const unsigned char* stp = ring + k * kStage + lane * 128;
+            const uint4* xst = reinterpret_cast<const uint4*>(xact + st * 512);
+            const float* xsst = reinterpret_cast<const float*>(xact + (size_t)K * 2) + st * 4;
+#pragma unroll
+            for (int jb = 0; jb < 4; jb++) {
+                int L0, L1, L2, L3;
+                lane_sums(stp, xst, sw, jb, L0, L1, L2, L3);
+                const uint32_t e = (ew >> (8 * jb)) & 0xFFu;
+                const float xsb = xsst[jb];
+                if (!odd) {
+                    const float S = exp_scale_ftz(e);
+                    t[k][jb][0] = mul_ftz(mul_ftz(i2f_rn(L0), S), xsb);
+                    t[k][jb][1] = mul_ftz(mul_ftz(i2f_rn(L1), S), xsb);
+                    t[k][jb][2] = mul_ftz(mul_ftz(i2f_rn(L2), S), xsb);
+                    t[k][jb][3] = mul_ftz(mul_ftz(i2f_rn(L3), S), xsb);
+                } else {
+                    t[k][jb][0] = mul_rn(mul_rn(i2f_rn(L0 + L1 + L2 + L3), exp_scale_ieee(e)), xsb);
+                    t[k][jb][1] = t[k][jb][2] = t[k][jb][3] = 0.0f;
+                }
+            }
+        }
+        __syncthreads();   // every warp is done with the stage buffers
+        float* T = reinterpret_cast<float*>(rings);   // [block][lane class][lane]
+#pragma unroll
+        for (int k = 0; k < SPW; k++) {
+            const int st = warp + k * kWarps;
+            if (st >= nst) break;
+#pragma unroll
+            for (int jb = 0; jb < 4; jb++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) T[((st * 4 + jb) * 4 + j) * 32 + lane] = t[k][jb][j];
+        }
+        __syncthreads();
+        if (warp == 0) {
+            float f0 = 0.f, f1 = 0.f, f2 = 0.f, f3 = 0.f, fo = 0.f;
+            if (!odd) {
+                for (int b = 0; b < nb; b++) {
+                    const float* tb = T + b * 128 + lane;
+                    f0 = add_ftz(f0, tb[0]);
+                    f1 = add_ftz(f1, tb[32]);
+                    f2 = add_ftz(f2, tb[64]);
+                    f3 = add_ftz(f3, tb[96]);
+                }
+            } else {
+                for (int b = 0; b < nb; b++) fo = add_rn(fo, T[b * 128 + lane]);
+            }
+            if (row_ok) D.y[r0 + lane] = odd ? fo : add_ftz(add_ftz(f0, f2), add_ftz(f1, f3));
+        }
+        __syncthreads();   // the next unit's stages overwrite the terms
     }
 }
 
@@ -1205,6 +1347,27 @@ cudaError_t launch_gemv_fast(const GemvDesc& d0, uint32_t* act, size_t act_cap_w
     return launch_warp<false, true>(A, grid, stream);
 }
 
+// One exact single GEMV (K <= 6144, K % 512 == 0) on the split-K kernel, a
+// programmatic dependent of the stream's previous kernel.
+static cudaError_t launch_split(const WArgs& A, cudaStream_t stream) {
+    const size_t smem = split_smem_bytes(A.single.K);
+    const int spw = ((A.single.K >> 8) + kWarps - 1) / kWarps;
+    auto kern = spw <= 1 ? gemv_split_kernel<1> : spw == 2 ? gemv_split_kernel<2> : gemv_split_kernel<3>;
+    cudaError_t err = raise_smem_limit(reinterpret_cast<const void*>(kern), smem);
+    if (err != cudaSuccess) return err;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(A.total_units);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, A);
+}
+
 template <bool RTL>
 static cudaError_t launch_generic(const GemvDesc& d, unsigned int* rtl_flags, cudaStream_t stream) {
     const size_t smem = (((size_t)2 * d.K + 15) & ~size_t(15)) + 4 * (size_t)(d.K / 64);
@@ -1241,6 +1404,7 @@ cudaError_t launch_gemv(const GemvDesc& d0, uint32_t* act, unsigned int* err, cu
     A.ctr = nullptr;
     A.err = err;
     A.rtl_flags = rtl_flags;
+    if (res && !rtl) return launch_split(A, stream);
     const int grid = std::min(num_sms(), (plan.total_units + kWarps - 1) / kWarps);
     return rtl ? launch_warp<false, false, true>(A, grid, stream) : launch_warp<false, false>(A, grid, stream);
 }
@@ -1275,8 +1439,7 @@ cudaError_t launch_rmsnorm_gemv(const GemvDesc& d0, const float* norm_w, float e
     A.total_units = plan.total_units;
     A.ctr = nullptr;
     A.err = err;
-    const int grid = std::min(num_sms(), (plan.total_units + kWarps - 1) / kWarps);
-    return launch_warp<false, false>(A, grid, stream);
+    return launch_split(A, stream);
 }
 
 cudaError_t launch_swiglu_gemv(const GemvDesc& d0, const float* up, uint32_t* act, unsigned int* err,
@@ -1295,8 +1458,7 @@ cudaError_t launch_swiglu_gemv(const GemvDesc& d0, const float* up, uint32_t* ac
     A.total_units = plan.total_units;
     A.ctr = nullptr;
     A.err = err;
-    const int grid = std::min(num_sms(), (plan.total_units + kWarps - 1) / kWarps);
-    return launch_warp<false, false>(A, grid, stream);
+    return launch_split(A, stream);
 }
 
 cudaError_t launch_bfp8_lm_head(const float* h, const int8_t* mant, const uint8_t* exps, int vocab,

@@ -400,7 +400,8 @@ class ShardedDeviceStack:
             xs = rec[2 * K:].view(self._f32()).view(K // 64)
             qp[:g1 - g0].copy_(xq[g0:g1])
             sp[:(g1 - g0) // 64].copy_(xs[g0 // 64:g1 // 64])
-            dist.all_gather_into_tensor(qg, qp, group=self.group)
+            # NCCL has no int16: the int16 slices travel as their bytes
+            dist.all_gather_into_tensor(qg.view(self._u8()), qp.view(self._u8()), group=self.group)
             dist.all_gather_into_tensor(sg, sp, group=self.group)
             for r in range(W):
                 r0, r1 = shard_rows(L.gate.M, W, r)
@@ -443,6 +444,12 @@ class ShardedDeviceStack:
         import torch
 
         return torch.int16
+
+    @staticmethod
+    def _u8():
+        import torch
+
+        return torch.uint8
 
     @staticmethod
     def _i8():
