@@ -861,7 +861,7 @@ def run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, p
     rec = {"value": round(nbytes / per_step / 1e9, 2), "unit": "GB/s", "ms_per_step": round(per_step * 1e3, 4),
            "scaling": "strong",
            "config": {"workload": f"scaled BFP8 stack: 8 x (gate/up 28672x8192, down 8192x28672), batch {B}",
-                      "arithmetic": "fast (K cut at fixed 1 KB steps, fma per block; within 1e-5 of the exact order)"
+                      "arithmetic": "fast (K cut at fixed 2 KB steps, fma per block; within 1e-5 of the exact order)"
                                     if B == 1 else "tcgen05 kind::i8 over hi/lo int8 planes, exact int32 block dots",
                       "algorithmic_bytes_per_step": nbytes, "weight_bytes": full_w,
                       "exchange_bytes_per_rank_per_step": xbytes,

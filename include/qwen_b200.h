@@ -215,7 +215,7 @@ QB_API int qwen_b200_stack_create(int n, const int8_t* const* mant, const uint8_
  * qwen_b200_gemv_fast_dev() and lets rows of deep matrices be split into K
  * segments (for stacks with few rows per GPU, e.g. row-sharded ones). */
 #define QB_STACK_FAST 1
-/* With QB_STACK_FAST: cut every row's K into fixed 1 KB segments, so where a
+/* With QB_STACK_FAST: cut every row's K into fixed 2 KB segments, so where a
  * row is split depends on K alone -- a row-sharded plan then gives every row
  * the same bits as the unsharded plan, on any number of GPUs. */
 #define QB_STACK_FIXED_SPLIT 2

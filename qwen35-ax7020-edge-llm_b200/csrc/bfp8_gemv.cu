@@ -470,7 +470,7 @@ __device__ __forceinline__ void stage_blocks_rtl(const unsigned char* st, const 
 // (NEON order; CTA 0 also stores the updated residual stream).  Every thread
 // of the CTA calls it; it ends with a CTA barrier.
 __device__ __forceinline__ void quantize_resident(const WArgs& A, const GemvDesc& D, unsigned char* xact, int warp,
-                                                  int lane) {
+                                                  int lane, float* stage = nullptr) {
     const int nb = D.K >> 6;
     uint32_t* xp = reinterpret_cast<uint32_t*>(xact);
     float* xsc = reinterpret_cast<float*>(xact + (size_t)D.K * 2);
@@ -481,14 +481,35 @@ __device__ __forceinline__ void quantize_resident(const WArgs& A, const GemvDesc
         // flushed), combined as (s0 + s2) + (s1 + s3); then, in IEEE
         // single precision, r = 1 / sqrt(sum / K + eps)
         __shared__ float s_nr;
+        if (stage) {
+            // the whole CTA first brings x (+ res: add_residual, qwen_kernels_opt.c:
+            // 388-396, flushed lane adds) into shared memory with coalesced
+            // 8-byte loads, so the four sequential chains below read shared
+            // memory and the quantizer reads the same values
+            for (int i = threadIdx.x; i < (D.K >> 1); i += blockDim.x) {
+                float2 v = reinterpret_cast<const float2*>(D.x)[i];
+                if (A.norm_res) {
+                    const float2 r = reinterpret_cast<const float2*>(A.norm_res)[i];
+                    v = make_float2(add_ftz(v.x, r.x), add_ftz(v.y, r.y));
+                }
+                reinterpret_cast<float2*>(stage)[i] = v;
+            }
+            __syncthreads();
+        }
         if (warp == 0) {
             float acc = 0.0f;
-            if (lane < 4)
-                for (int i = lane; i < D.K; i += 4) {
-                    // add_residual (qwen_kernels_opt.c:388-396): flushed lane adds
-                    const float v = A.norm_res ? add_ftz(D.x[i], A.norm_res[i]) : D.x[i];
-                    acc = add_ftz(acc, mul_ftz(v, v));
+            if (lane < 4) {
+                if (stage) {
+#pragma unroll 8
+                    for (int i = lane; i < D.K; i += 4) acc = add_ftz(acc, mul_ftz(stage[i], stage[i]));
+                } else {
+                    for (int i = lane; i < D.K; i += 4) {
+                        // add_residual (qwen_kernels_opt.c:388-396): flushed lane adds
+                        const float v = A.norm_res ? add_ftz(D.x[i], A.norm_res[i]) : D.x[i];
+                        acc = add_ftz(acc, mul_ftz(v, v));
+                    }
                 }
+            }
             const float pair = add_ftz(acc, __shfl_down_sync(0xffffffffu, acc, 2));   // s0+s2, s1+s3
             const float other = __shfl_down_sync(0xffffffffu, pair, 1);
             if (lane == 0) {
@@ -504,7 +525,8 @@ __device__ __forceinline__ void quantize_resident(const WArgs& A, const GemvDesc
         if (D.x) {
 #pragma unroll
             for (int j = 0; j < 4; j++)
-                if (b0 + j * kWarps < nb) v[j] = reinterpret_cast<const float2*>(D.x + 64 * (b0 + j * kWarps))[lane];
+                if (b0 + j * kWarps < nb)
+                    v[j] = reinterpret_cast<const float2*>((stage ? stage : D.x) + 64 * (b0 + j * kWarps))[lane];
             if (A.glu_up) {   // x holds the gate projection: swiglu(gate, up)
 #pragma unroll
                 for (int j = 0; j < 4; j++)
@@ -519,10 +541,12 @@ __device__ __forceinline__ void quantize_resident(const WArgs& A, const GemvDesc
                 for (int j = 0; j < 4; j++)
                     if (b0 + j * kWarps < nb) {
                         if (A.norm_res) {
-                            const float2 rr =
-                                reinterpret_cast<const float2*>(A.norm_res + 64 * (b0 + j * kWarps))[lane];
-                            v[j].x = add_ftz(v[j].x, rr.x);
-                            v[j].y = add_ftz(v[j].y, rr.y);
+                            if (!stage) {   // staged values already hold x + res
+                                const float2 rr =
+                                    reinterpret_cast<const float2*>(A.norm_res + 64 * (b0 + j * kWarps))[lane];
+                                v[j].x = add_ftz(v[j].x, rr.x);
+                                v[j].y = add_ftz(v[j].y, rr.y);
+                            }
                             if (blockIdx.x == 0)
                                 reinterpret_cast<float2*>(A.norm_xout + 64 * (b0 + j * kWarps))[lane] = v[j];
                         }
@@ -719,6 +743,10 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
     }
 
     if (res) {
+        // launched as a programmatic dependent of the stream's previous
+        // kernel: its weight stages are already in flight; the activation
+        // (maybe that kernel's output) is read, and anything written, only now
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         quantize_resident(A, wdesc(A, 0), xrings, warp, lane);
     } else {
         // the activations come from act_prep (programmatic dependent launch)
@@ -824,10 +852,14 @@ __global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs 
 // previous kernel's tail; it reads the activation and writes only after it.
 constexpr int kSplitMaxStages = 3;   // stages per warp: K <= 8 * 3 * 256 = 6144
 
-static size_t split_smem_bytes(int K) {
+// Split kernels with K <= kStageMaxK stage an rmsnorm's input in shared
+// memory (4K bytes more); deeper ones read it from global memory.
+constexpr int kStageMaxK = 4096;
+
+static size_t split_smem_bytes(int K, bool stage) {
     const int nst = K >> 8, spw = (nst + kWarps - 1) / kWarps;
     return 1024 + (size_t)kWarps * spw * kStage + ((2 * (size_t)K + (size_t)K / 16 + 127) & ~size_t(127)) +
-           (size_t)kWarps * spw * (128 + 8);
+           (size_t)kWarps * spw * (128 + 8) + (stage ? 4 * (size_t)K : 0);
 }
 
 // SPW: the most stages one warp takes (K <= SPW * 2048); its terms stay in registers.
@@ -843,6 +875,7 @@ __global__ void __launch_bounds__(kThreads, SPW == 1 ? 2 : 1) gemv_split_kernel(
     unsigned char* xact = rings + (size_t)kWarps * spw * kStage;                  // resident activation
     unsigned char* erings = xact + ((2 * (size_t)K + (size_t)K / 16 + 127) & ~size_t(127));   // [warp][spw][lane]
     uint64_t* bars = reinterpret_cast<uint64_t*>(erings + (size_t)kWarps * spw * 128);         // [warp][spw]
+    float* stage = (A.norm_w && K <= kStageMaxK) ? reinterpret_cast<float*>(bars + kWarps * spw) : nullptr;
 
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -877,7 +910,7 @@ __global__ void __launch_bounds__(kThreads, SPW == 1 ? 2 : 1) gemv_split_kernel(
         if (first) {
             // the activation may be the previous kernel's output: read only now
             asm volatile("griddepcontrol.wait;" ::: "memory");
-            quantize_resident(A, D, xact, warp, lane);
+            quantize_resident(A, D, xact, warp, lane, stage);
             first = false;
         }
         cp_async_wait<0>();
@@ -1285,7 +1318,7 @@ static cudaError_t launch_warp(const WArgs& A, int grid, cudaStream_t stream) {
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = A.res_act ? 0 : 1;   // a programmatic dependent of act_prep unless it quantizes itself
+    cfg.numAttrs = 1;   // a programmatic dependent of act_prep, or (resident activation) of whatever ran before
     return cudaLaunchKernelEx(&cfg, gemv_warp_kernel<LM, FAST, RTL>, A);
 }
 
@@ -1350,7 +1383,7 @@ cudaError_t launch_gemv_fast(const GemvDesc& d0, uint32_t* act, size_t act_cap_w
 // One exact single GEMV (K <= 6144, K % 512 == 0) on the split-K kernel, a
 // programmatic dependent of the stream's previous kernel.
 static cudaError_t launch_split(const WArgs& A, cudaStream_t stream) {
-    const size_t smem = split_smem_bytes(A.single.K);
+    const size_t smem = split_smem_bytes(A.single.K, A.norm_w && A.single.K <= kStageMaxK);
     const int spw = ((A.single.K >> 8) + kWarps - 1) / kWarps;
     auto kern = spw <= 1 ? gemv_split_kernel<1> : spw == 2 ? gemv_split_kernel<2> : gemv_split_kernel<3>;
     cudaError_t err = raise_smem_limit(reinterpret_cast<const void*>(kern), smem);

@@ -703,9 +703,10 @@ int qwen_b200_quant_dev(const float* x, int B, int K, int16_t* xq, float* xs, vo
 
 namespace {
 
-// QB_STACK_FIXED_SPLIT: K segments of 4 stages (1 KB of every row) -- short
-// enough that the 1/8 shard of a deep matrix still fills the GPU.
-constexpr int kFixedSegStages = 4;
+// QB_STACK_FIXED_SPLIT: K segments of 8 stages (2 KB of every row) -- short
+// enough that the 1/8 shard of a deep matrix still fills the GPU, long
+// enough that a whole matrix is not cut into needlessly many pieces.
+constexpr int kFixedSegStages = 8;
 
 struct PeerSpec {
     int world;

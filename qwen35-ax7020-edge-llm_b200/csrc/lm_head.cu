@@ -201,6 +201,8 @@ __global__ void __launch_bounds__(kThreads, 1) lm_bf16_warp_kernel(const __grid_
     __shared__ int s_cand_count;
     __shared__ unsigned long long s_red[kThreads / 32];
 
+    // the next kernel on the stream may start its prologue now
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     unsigned char* ring = rings + warp * kWRing * kWStage;
     uint64_t* bar = bars + warp * kWRing;
@@ -226,6 +228,10 @@ __global__ void __launch_bounds__(kThreads, 1) lm_bf16_warp_kernel(const __grid_
             wissue(A, u_begin + warp + iu * kWWarps, is, ring + k * kWStage, &bar[k]);
             if (++is == nst) { is = 0; iu++; }
         }
+    // a programmatic dependent of the stream's previous kernel: the table
+    // stages are in flight; h (maybe that kernel's output) is read, and the
+    // scratch and outputs written, only once that kernel has completed
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     for (int i = tid; i < A.hidden; i += kThreads) hs[i] = A.h[i];
     __syncthreads();
 
@@ -383,19 +389,20 @@ cudaError_t launch_lm_head_bf16(const float* h, const uint16_t* E, int vocab, in
         const size_t smem = 1024 + (size_t)kWWarps * kWRing * kWStage + (size_t)kWWarps * kWRing * 8 +
                             4 * (size_t)hidden + (size_t)(64 * kWWarps + 64) * 8;
         if (smem > 232448) return cudaErrorInvalidValue;
-        cudaError_t err;
-        if (A.kk > 0) {
-            err = cudaFuncSetAttribute(lm_bf16_warp_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
-            if (err != cudaSuccess) return err;
-            lm_bf16_warp_kernel<true><<<grid, kThreads, smem, stream>>>(A);
-        } else {
-            err = cudaFuncSetAttribute(lm_bf16_warp_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
-            if (err != cudaSuccess) return err;
-            lm_bf16_warp_kernel<false><<<grid, kThreads, smem, stream>>>(A);
-        }
-        return cudaGetLastError();
+        auto kern = A.kk > 0 ? lm_bf16_warp_kernel<true> : lm_bf16_warp_kernel<false>;
+        cudaError_t err = raise_smem_limit(reinterpret_cast<const void*>(kern), smem);
+        if (err != cudaSuccess) return err;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;   // a programmatic dependent of the stream's previous kernel
+        return cudaLaunchKernelEx(&cfg, kern, A);
     }
     if (fast) {
         A.units = (vocab + kRows - 1) / kRows;

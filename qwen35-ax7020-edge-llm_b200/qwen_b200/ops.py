@@ -403,7 +403,7 @@ def pack_bfp8(w: torch.Tensor, out_mant: torch.Tensor | None = None, out_exps: t
 
 # Plan flags of the grouped launches (include/qwen_b200.h QB_STACK_*).
 STACK_FAST = 1          # split-K arithmetic (fused multiply-add per block)
-STACK_FIXED_SPLIT = 2   # with STACK_FAST: K cut at fixed 1 KB steps (same bits on any number of GPUs)
+STACK_FIXED_SPLIT = 2   # with STACK_FAST: K cut at fixed 2 KB steps (same bits on any number of GPUs)
 STACK_Q_INPUT = 4       # x is a quantized record: int16 xq [K], then fp32 xs [K/64]
 
 

@@ -28,7 +28,7 @@ Two exchanges:
 
 Batch 1 runs the GEMV kernels, batch > 1 the tcgen05 GEMM (planar int16
 activations).  With ``fast`` (batch 1) every row's K is cut into segments at
-fixed 1 KB steps, so the outputs are the same bits on any number of GPUs.
+fixed 2 KB steps, so the outputs are the same bits on any number of GPUs.
 """
 from __future__ import annotations
 
@@ -211,6 +211,10 @@ class ShardedDeviceStack:
                     self.peer_regions.append(reg)
                     self.peer_base[r] = reg.ptr
 
+    def _equal(self, M):
+        """Every rank holds the same number of rows of an M-row matrix."""
+        return self.padded_rows(M) * self.world == M
+
     def padded_rows(self, M):
         """Every rank contributes the same count to an all-gather: the
         largest slice."""
@@ -279,7 +283,9 @@ class ShardedDeviceStack:
                                             [[self.peer_base[r] + self.voff[L.down.name] for r in others]], [d0],
                                             self.world, flags=fl)
             else:
-                y = self.full[L.down.name] if self.world == 1 else self.part[L.down.name][:d1 - d0]
+                # one rank, or equal slices (gathered in place): straight into the full output
+                direct = self.world == 1 or self._equal(L.down.M)
+                y = self.full[L.down.name][d0:d1] if direct else self.part[L.down.name][:d1 - d0]
                 dn = ops.LinearStack([(self.dq[i], *self.weight(copy, L.down), y)], flags=fl)
             plans.append((gu, dn))
             x = self.full[L.down.name]
@@ -395,6 +401,13 @@ class ShardedDeviceStack:
         rec = self.dq[i]
         qp, qg = self.part[("q", L.down.name)], self.gath[("q", L.down.name)]
         sp, sg = self.part[("s", L.down.name)], self.gath[("s", L.down.name)]
+        if B == 1 and self._equal(L.gate.M):
+            # equal slices: gather the int16 values and the scales in place
+            # (NCCL has no int16: they travel as their bytes)
+            dist.all_gather_into_tensor(rec[:2 * K], rec[2 * g0:2 * g1], group=self.group)
+            xs = rec[2 * K:2 * K + 4 * (K // 64)]
+            dist.all_gather_into_tensor(xs, xs[4 * (g0 // 64):4 * (g1 // 64)], group=self.group)
+            return
         if B == 1:
             xq = rec[:2 * K].view(self._i16()).view(K)
             xs = rec[2 * K:].view(self._f32()).view(K // 64)
@@ -428,8 +441,9 @@ class ShardedDeviceStack:
         part, gath, full = self.part[t.name], self.gath[t.name], self.full[t.name]
         B = self.B
         P = part.numel() // B
-        if B == 1 and P * self.world == t.M:   # equal slices: gather straight into place
-            dist.all_gather_into_tensor(full, part, group=self.group)
+        if B == 1 and P * self.world == t.M:   # equal slices: the GEMV wrote its rows in place
+            d0, d1 = self.shards[t.name]
+            dist.all_gather_into_tensor(full, full[d0:d1], group=self.group)
             return
         dist.all_gather_into_tensor(gath, part, group=self.group)
         g = gath.view(self.world, B, P)

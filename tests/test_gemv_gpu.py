@@ -55,7 +55,8 @@ def test_quant_block64_bit_exact(cuda):
 
 # ------------------------------------------------------------------ single GEMV
 SHAPES = [(3584, 1024), (1024, 3584), (6144, 1024), (2048, 1024), (1024, 2048), (4096, 1024), (512, 1024),
-          (1, 1024), (2, 512), (3, 512), (31, 1024), (33, 2048), (3583, 1024), (129, 4096), (64, 8192)]
+          (1, 1024), (2, 512), (3, 512), (31, 1024), (33, 2048), (3583, 1024), (129, 4096), (64, 8192),
+          (33, 6144), (100, 5632), (4737, 1536)]   # split kernel: 3 and 2 stages per warp; more groups than SMs
 
 
 @pytest.mark.parametrize("M,K", SHAPES)
