@@ -13,9 +13,9 @@
 //               (both signed int8), so the accumulator holds the hi dots in
 //               columns [0, N) and the lo dots in [N, 2N); then
 //               tcgen05.commit;
-//   warps 2..9  epilogue: each thread owns one weight row (its TMEM lane)
-//               and N/2 batch columns; per block it reads Dhi/Dlo from
-//               TMEM, frees the slot, and accumulates
+//   warps 2..   epilogue (8 or 16 warps): each thread owns one weight row
+//               (its TMEM lane) and a slice of the batch columns; per block
+//               it reads Dhi/Dlo from TMEM, frees the slot, and accumulates
 //               float(256*Dhi + Dlo) * 2^(e-134) * xs in f32 registers.
 // TMEM holds kSlots accumulator pairs so the tensor cores run ahead of the
 // epilogue by up to kSlots blocks; shared memory holds kStages K stages.
@@ -47,17 +47,11 @@ constexpr int kExpsMax = 56;   // block exponents per row staged in shared memor
 constexpr int kMaxTable = kTcMaxDescs;   // GEMMs per launch (their scalar fields are kept in shared memory)
 constexpr int kEBytes = kTileRows * kExpsMax;
 
-// TMEM accumulator presets.  Before the first K step of a block, the hi
-// accumulator holds the bits of 1.5*2^31 and the lo accumulator those of
-// 1.5*2^23; the MMAs add the int32 dots to those bit patterns.  Since
-// |Dhi| < 2^20 and |Dlo| < 2^21 the sums stay inside one binade, so read as
-// floats the accumulators are exactly 1.5*2^31 + 256*Dhi (ulp 256) and
-// 1.5*2^23 + Dlo (ulp 1).  Then (hi - kMagicSum) is exact and adding lo
-// gives float(256*Dhi + Dlo) = float(D) with a single rounding: two f32
-// additions per block dot instead of an int->float conversion.
-constexpr uint32_t kMagicHi = 0x4F400000u;
-constexpr uint32_t kMagicLo = 0x4B400000u;
-constexpr float kMagicSum = 3233808384.0f;   // 1.5*2^31 + 1.5*2^23 = 771 * 2^22
+// Block dot recombination: each block's hi and lo accumulators hold the
+// exact int32 dots Dhi and Dlo; 256 * Dhi + Dlo is the exact int32 block dot
+// D (|D| < 2^31), formed with one integer multiply-add and converted to fp32
+// with one rounding (the conversion runs on the integer pipe, beside the
+// fp32 scale-and-accumulate on the FMA pipe).
 
 // Scalar fields of one GEMM, copied to shared memory at kernel start so that
 // unit lookups never wait on global loads.
@@ -477,7 +471,6 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
         constexpr int G = C::kGroup;
         uint32_t gs = 0, gb = 0, gg = 0;
         bool bad = false;
-        const float2 neg_magic = make_float2(-kMagicSum, -kMagicSum);
         for (int i = 0; !bad; i++) {
             const int eb = i & 1;
             if (!warp_wait(&ufull[eb], (i >> 1) & 1, p.err)) break;
@@ -504,14 +497,14 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
                 for (int k = 0; k < kCh; k += 2) {
                     const float4 x4 = xsv[k / 4];   // one 16-byte load serves four columns
                     const float2 xs2 = (k & 2) ? make_float2(x4.z, x4.w) : make_float2(x4.x, x4.y);
-                    const float2 th = make_float2(__uint_as_float(hv[k]), __uint_as_float(hv[k + 1]));
-                    const float2 tl = make_float2(__uint_as_float(lv[k]), __uint_as_float(lv[k + 1]));
-                    const float2 fd = __fadd2_rn(__fadd2_rn(th, neg_magic), tl);
+                    // the exact int32 dot 256 * Dhi + Dlo, converted with one rounding
+                    const float2 fd = make_float2(__int2float_rn((int)hv[k] * 256 + (int)lv[k]),
+                                                  __int2float_rn((int)hv[k + 1] * 256 + (int)lv[k + 1]));
                     acc[(c + k) / 2] = __ffma2_rn(fd, __fmul2_rn(sm2, xs2), acc[(c + k) / 2]);
                     if constexpr (DOTS) {
 #pragma unroll
                         for (int w = 0; w < 2; w++) {
-                            const int D = (int)(hv[k + w] - kMagicHi) * 256 + (int)(lv[k + w] - kMagicLo);
+                            const int D = (int)hv[k + w] * 256 + (int)lv[k + w];
                             const int b = nt * N + col0 + c + k + w;
                             if (row_ok && b < B) info.dots[((size_t)b * M + m) * info.nb + info.j0 + j] = D;
                         }
@@ -551,11 +544,7 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
 #pragma unroll
                     for (int g = 0; g < G; g++)
 #pragma unroll
-                        for (int k = 0; k < C::kCols; k++) {
-                            asm volatile("" : "+r"(hv[g][k]), "+r"(lv[g][k]));
-                            hv[g][k] += kMagicHi;   // bias patterns: exact int -> float (see accumulate)
-                            lv[g][k] += kMagicLo;
-                        }
+                        for (int k = 0; k < C::kCols; k++) asm volatile("" : "+r"(hv[g][k]), "+r"(lv[g][k]));
 #pragma unroll
                     for (int g = 0; g < G; g++)
                         if (g < ng) {
@@ -574,11 +563,6 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
 #pragma unroll
                     for (int c = 0, ci = 0; c < C::kCols; c += C::kChunk, ci++) {
                         tmem_wait_ld_dep<C::kChunk>(hv[ci & 1], lv[ci & 1]);
-#pragma unroll
-                        for (int k = 0; k < C::kChunk; k++) {   // bias patterns
-                            hv[ci & 1][k] += kMagicHi;
-                            lv[ci & 1][k] += kMagicLo;
-                        }
                         if (c + C::kChunk < C::kCols) {   // next piece loads while this one is summed
                             tmem_ld<C::kChunk>(tcol + c + C::kChunk, hv[(ci + 1) & 1]);
                             tmem_ld<C::kChunk>(tcol + N + c + C::kChunk, lv[(ci + 1) & 1]);
