@@ -491,11 +491,15 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
                 const int s = (gs + j / C::kBPS) % C::kStages;
                 const float sm = exp_scale_ieee(e);
                 const float2 sm2 = make_float2(sm, sm);
-                const float4* xsv =
-                    reinterpret_cast<const float4*>(sxs + (size_t)s * C::kSBytes) + ((j % C::kBPS) * N + col0 + c) / 4;
+                // shared-state address of the scales: plain shared loads, not generic ones
+                const uint32_t xsa = smem_u32(sxs) + (uint32_t)(s * C::kSBytes + ((j % C::kBPS) * N + col0 + c) * 4);
+                float4 x4;   // one 16-byte load serves four columns (two pairs)
 #pragma unroll
                 for (int k = 0; k < kCh; k += 2) {
-                    const float4 x4 = xsv[k / 4];   // one 16-byte load serves four columns
+                    if ((k & 2) == 0)
+                        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                                     : "=f"(x4.x), "=f"(x4.y), "=f"(x4.z), "=f"(x4.w)
+                                     : "r"(xsa + 4 * k));
                     const float2 xs2 = (k & 2) ? make_float2(x4.z, x4.w) : make_float2(x4.x, x4.y);
                     // the exact int32 dot 256 * Dhi + Dlo, converted with one rounding
                     const float2 fd = make_float2(__int2float_rn((int)hv[k] * 256 + (int)lv[k]),
