@@ -92,6 +92,77 @@ QB_API int lm_head_topk(const float* h, const uint16_t* embed_table, int vocab_s
 QB_API int sample_from_topk(const int* ids, const float* scores, int n, float temperature, int top_k,
                      float top_p, unsigned int* rng_state);
 
+/* The per-layer plans the engine hands the reference's C token loop,
+ * field for field and byte for byte its ctypes layouts
+ * (04-板载脚本与工具/qwen_real_engine.py:20-57 LinearLayerPlanC, :59-74
+ * MlpPlanC; qwen_kernels_opt.c:866-917).  All pointers are host pointers:
+ * weight slices of the mapped weight file, fp32 norm vectors. */
+typedef struct {
+    const float* in_ln_w;
+    const int8_t* mant_qkv;
+    const uint8_t* exp_qkv;
+    int M_qkv;
+    int K_qkv;
+    const float* conv_w;
+    float* conv_s;
+    const float* wa;
+    const float* wb;
+    const float* nea;
+    const float* dt;
+    float* state;
+    const int8_t* mant_z;
+    const uint8_t* exp_z;
+    int M_z;
+    int K_z;
+    const float* norm_w;
+    const int8_t* mant_o;
+    const uint8_t* exp_o;
+    int M_o;
+    int K_o;
+    const float* post_ln_w;
+    const int8_t* mant_gate;
+    const uint8_t* exp_gate;
+    int M_gate;
+    int K_gate;
+    const int8_t* mant_up;
+    const uint8_t* exp_up;
+    int M_up;
+    int K_up;
+    const int8_t* mant_down;
+    const uint8_t* exp_down;
+    int M_down;
+    int K_down;
+} LinearLayerPlanC;
+
+typedef struct {
+    const float* post_ln_w;
+    const int8_t* mant_gate;
+    const uint8_t* exp_gate;
+    int M_gate;
+    int K_gate;
+    const int8_t* mant_up;
+    const uint8_t* exp_up;
+    int M_up;
+    int K_up;
+    const int8_t* mant_down;
+    const uint8_t* exp_down;
+    int M_down;
+    int K_down;
+} MlpPlanC;
+
+/* Replaces forward_mlp() (qwen_kernels_opt.c:994-1003; caller
+ * qwen_real_engine.py:1152-1153): h += down(swiglu(gate(n), up(n))) with
+ * n = rmsnorm(h, post_ln_w, 1e-6) -- the reference's NEON-build rmsnorm,
+ * GEMVs, swiglu and add_residual, bit for bit -- as four launches on the
+ * device (rmsnorm in front of gate and of up, swiglu in front of down, the
+ * residual add); h (host, K_gate floats) is copied in and back, weight and
+ * norm pointers are translated like bfp8_gemv's.  K_gate == K_up <= 6144,
+ * M_gate == M_up == K_down, M_down == K_gate.  On error h is unchanged and
+ * qwen_b200_last_error() says why.  (LinearLayerPlanC's forward_linear_layer
+ * and forward_token_c also run the Gated-DeltaNet / attention glue, which
+ * this library does not serve.) */
+QB_API void forward_mlp(const MlpPlanC* p, float* h);
+
 /* Replace the stage profiler (qwen_kernels_opt.c:71-91; read by
  * qwen_real_engine.py:1008-1047 when QWEN_PROFILE=1).  Slots accumulate
  * host wall milliseconds per entry point. */

@@ -1045,6 +1045,22 @@ __global__ void __launch_bounds__(kThreads) gemv_generic_kernel(const __grid_con
     D.y[m] = odd ? sum : add_ftz(add_ftz(f0, f2), add_ftz(f1, f3));
 }
 
+// ---------------------------------------------------------------- residual
+// add_residual (qwen_kernels_opt.c:388-396), NEON build: x += res with the
+// vector unit's flushed adds over whole groups of four, the scalar (IEEE)
+// add on the tail.
+__global__ void __launch_bounds__(kThreads) add_residual_kernel(float* x, const float* res, int n) {
+    const int body = n & ~3;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        x[i] = i < body ? add_ftz(x[i], res[i]) : add_rn(x[i], res[i]);
+}
+
+cudaError_t launch_add_residual(float* x, const float* res, int n, cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    add_residual_kernel<<<std::min((n + kThreads - 1) / kThreads, num_sms()), kThreads, 0, stream>>>(x, res, n);
+    return cudaGetLastError();
+}
+
 // ---------------------------------------------------------------- quantizer
 __global__ void __launch_bounds__(kThreads) quant_block64_kernel(const float* x, int B, int K,
                                                                  int16_t* xq, float* xs) {

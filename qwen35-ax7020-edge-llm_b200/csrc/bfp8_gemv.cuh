@@ -140,6 +140,9 @@ cudaError_t launch_swiglu_quant(const float* gate, const float* up, int B, int n
                                 int planar, int ldxs, void* const* dst, int ndst, const SyncArgs* sync,
                                 unsigned int* err, cudaStream_t stream);
 
+// add_residual (NEON build): x[i] += res[i], flushed over groups of four.
+cudaError_t launch_add_residual(float* x, const float* res, int n, cudaStream_t stream);
+
 int num_sms();
 
 }  // namespace qb

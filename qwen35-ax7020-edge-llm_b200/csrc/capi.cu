@@ -366,6 +366,89 @@ void bfp8_gemv(float* y, const float* x, const int8_t* mant, const uint8_t* exps
     memcpy(y, g_ctx.h_out, 4 * (size_t)M);
 }
 
+static float* g_mlp_buf = nullptr;   // h | down | gate | up of the forward_mlp drop-in
+static size_t g_mlp_cap = 0;
+
+void forward_mlp(const MlpPlanC* p, float* h) {
+    ProfScope ps(PF_GEMV);
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!p || !h || !p->post_ln_w) {
+        fail(QB_EINVAL, "forward_mlp: null plan, h or norm weights");
+        return;
+    }
+    const int H = p->K_gate, F = p->M_gate;
+    if (H <= 0 || H % 512 || H > 6144 || p->K_up != H || p->M_up != F || p->K_down != F || p->M_down != H ||
+        F <= 0 || F % 512 || F > 6144) {
+        fail(QB_EINVAL, "forward_mlp: K_gate == K_up == M_down <= 6144 and M_gate == M_up == K_down <= 6144, "
+                        "multiples of 512");
+        return;
+    }
+    if (ensure_ctx()) return;
+    int rc = QB_OK;
+    auto dev_weights = [&](const int8_t* m, const uint8_t* e, int M, int K, const int8_t** dm, const uint8_t** de) {
+        const size_t wb = (size_t)M * K, eb = (size_t)M * (K / 64);
+        if (e == reinterpret_cast<const uint8_t*>(m) + wb) {
+            const void* d = device_of(m, wb + eb, &rc);
+            *dm = static_cast<const int8_t*>(d);
+            *de = d ? static_cast<const uint8_t*>(d) + wb : nullptr;
+        } else {
+            *dm = static_cast<const int8_t*>(device_of(m, wb, &rc));
+            *de = *dm ? static_cast<const uint8_t*>(device_of(e, eb, &rc)) : nullptr;
+        }
+        return *dm && *de;
+    };
+    const int8_t *gm, *um, *dm;
+    const uint8_t *ge, *ue, *de;
+    if (!p->mant_gate || !p->exp_gate || !p->mant_up || !p->exp_up || !p->mant_down || !p->exp_down) {
+        fail(QB_EINVAL, "forward_mlp: null weight pointer");
+        return;
+    }
+    if (!dev_weights(p->mant_gate, p->exp_gate, F, H, &gm, &ge) || !dev_weights(p->mant_up, p->exp_up, F, H, &um, &ue) ||
+        !dev_weights(p->mant_down, p->exp_down, H, F, &dm, &de))
+        return;
+    const float* dln = static_cast<const float*>(device_of(p->post_ln_w, 4 * (size_t)H, &rc));
+    if (!dln) return;
+    // h | down | gate | up, each 256-byte aligned
+    const size_t hb = ((size_t)H * 4 + 255) & ~size_t(255), fb = ((size_t)F * 4 + 255) & ~size_t(255);
+    if (grow_dev(reinterpret_cast<void**>(&g_mlp_buf), &g_mlp_cap, 2 * hb + 2 * fb) ||
+        grow_pinned(&g_ctx.h_in, &g_ctx.h_in_cap, 4 * (size_t)H))
+        return;
+    unsigned char* base = reinterpret_cast<unsigned char*>(g_mlp_buf);
+    float* dh = reinterpret_cast<float*>(base);
+    float* ddown = reinterpret_cast<float*>(base + hb);
+    float* dgate = reinterpret_cast<float*>(base + 2 * hb);
+    float* dup = reinterpret_cast<float*>(base + 2 * hb + fb);
+    DevState* dst = nullptr;
+    if (dev_state(&dst)) return;
+    cudaStream_t s = g_ctx.stream;
+    memcpy(g_ctx.h_in, h, 4 * (size_t)H);
+    cudaError_t e = cudaMemcpyAsync(dh, g_ctx.h_in, 4 * (size_t)H, cudaMemcpyHostToDevice, s);
+    auto desc = [](const int8_t* m, const uint8_t* ex, const float* x, float* y, int M, int K) {
+        qb::GemvDesc d{};
+        d.mant = m;
+        d.exps = ex;
+        d.x = x;
+        d.y = y;
+        d.M = M;
+        d.K = K;
+        return d;
+    };
+    // rmsnorm in front of gate and of up, swiglu in front of down, then h += down
+    if (e == cudaSuccess)
+        e = qb::launch_rmsnorm_gemv(desc(gm, ge, dh, dgate, F, H), dln, 1e-6f, dst->act, dst->err, s);
+    if (e == cudaSuccess)
+        e = qb::launch_rmsnorm_gemv(desc(um, ue, dh, dup, F, H), dln, 1e-6f, dst->act, dst->err, s);
+    if (e == cudaSuccess) e = qb::launch_swiglu_gemv(desc(dm, de, dgate, ddown, H, F), dup, dst->act, dst->err, s);
+    if (e == cudaSuccess) e = qb::launch_add_residual(dh, ddown, H, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(g_ctx.h_in, dh, 4 * (size_t)H, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        fail(e == cudaErrorInvalidValue ? QB_EINVAL : QB_ECUDA, "forward_mlp", e);
+        return;
+    }
+    memcpy(h, g_ctx.h_in, 4 * (size_t)H);
+}
+
 static int lm_bf16_host(const float* h, const uint16_t* E, int vocab, int hidden, int k, int with_tail,
                         int* out_ids, float* out_scores, int* id_out) {
     if (ensure_ctx()) return QB_ENODEV;

@@ -24,6 +24,7 @@ SIGNATURES = {
     "lm_head_argmax": (_I, [_P, _P, _I, _I]),
     "lm_head_topk": (_I, [_P, _P, _I, _I, _I, _P, _P]),
     "sample_from_topk": (_I, [_P, _P, _I, _F, _I, _F, _P]),
+    "forward_mlp": (None, [_P, _P]),
     "qwen_prof_enable": (None, [_I]),
     "qwen_prof_reset": (None, []),
     "qwen_prof_count": (_I, []),

@@ -12,6 +12,8 @@ Every fixture is produced by the reference's OWN code or recipe:
                   fallback, :1233-1239), imported and run with no kernels
   manifest_64k.json   06-模型与权重/qwen35_weights_64k_manifest.json, every
                   tensor entry (board addresses dropped)
+  plan_layouts.json   qwen_real_engine.py's ctypes LinearLayerPlanC / MlpPlanC:
+                  field offsets and sizes
   ref_gemv.npz    04-板载脚本与工具/qwen_kernels_opt.c bfp8_gemv, compiled from
                   source for x86 (its scalar float path, :311-325)
   ref_lm.npz      qwen_kernels_opt.c lm_head_argmax and qwen_sampling.c
@@ -145,6 +147,22 @@ def make_manifest():
     out["tensors"] = {n: {k: v for k, v in t.items() if k != "phys_addr"} for n, t in m["tensors"].items()}
     with open(os.path.join(HERE, "manifest_64k.json"), "w", encoding="utf-8") as f:
         json.dump(out, f, indent=0, ensure_ascii=False)
+
+
+def make_plan_layouts():
+    """Field names, offsets and sizes of the reference engine's ctypes plan
+    structures (qwen_real_engine.py:20-74), imported from the engine."""
+    import json
+
+    sys.path.insert(0, os.path.join(REF, "04-板载脚本与工具"))
+    import qwen_real_engine as E
+
+    out = {}
+    for cls in (E.LinearLayerPlanC, E.MlpPlanC):
+        out[cls.__name__] = {"size": ctypes.sizeof(cls),
+                             "fields": [[n, getattr(cls, n).offset, getattr(cls, n).size] for n, _ in cls._fields_]}
+    with open(os.path.join(HERE, "plan_layouts.json"), "w") as f:
+        json.dump(out, f, indent=1)
 
 
 # ------------------------------------------------------------------ lm_head
@@ -320,6 +338,7 @@ def main():
     make_ref_gemv(k)
     make_ref_numpy_gemv()
     make_manifest()
+    make_plan_layouts()
     make_ref_rmsnorm(k)
     make_ref_residual(k)
     make_ref_swiglu(k)

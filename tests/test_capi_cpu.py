@@ -157,3 +157,34 @@ def test_rtl20_and_device_sampler_reject_bad_arguments_without_a_gpu():
     assert lib.qwen_b200_sample_topk_dev(p, p, None, -1, 1.0, 0, 1.0, None, p, None) == -1
     assert lib.qwen_b200_sample_topk_dev(None, p, None, 4, 1.0, 0, 1.0, None, p, None) == -1
     assert b"outside 0..1024" in lib.qwen_b200_last_error()
+
+
+def test_plan_structs_match_the_engine_ctypes_layouts(tmp_path):
+    """LinearLayerPlanC / MlpPlanC in include/qwen_b200.h have, field by
+    field, the offsets and sizes of the reference engine's ctypes structures
+    (qwen_real_engine.py:20-74; tests/golden/plan_layouts.json), compiled
+    here with gcc."""
+    import json
+    import shutil
+    import subprocess
+
+    if not shutil.which("gcc"):
+        pytest.skip("no gcc")
+    layouts = json.load(open(os.path.join(REPO, "tests", "golden", "plan_layouts.json")))
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "qwen_b200.h"', 'int main(void) {']
+    for name, spec in layouts.items():
+        lines.append(f'    printf("{name} size %zu\\n", sizeof({name}));')
+        for field, _, _ in spec["fields"]:
+            lines.append(f'    printf("{name} {field} %zu %zu\\n", offsetof({name}, {field}), '
+                         f'sizeof((({name}*)0)->{field}));')
+    lines.append("    return 0;\n}")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", "-I", os.path.join(REPO, "include"), str(src), "-o", str(exe)], check=True)
+    got = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split("\n")
+    want = []
+    for name, spec in layouts.items():
+        want.append(f"{name} size {spec['size']}")
+        want += [f"{name} {f} {o} {s}" for f, o, s in spec["fields"]]
+    assert [g for g in got if g] == want

@@ -162,3 +162,54 @@ def test_weight_file_through_the_dropin_and_the_device_api(lib):
         dm, de = dw.views(n)
         assert np.array_equal(bits(ops.bfp8_gemv(torch.from_numpy(x).cuda(), dm, de).cpu().numpy()), ref), n
     wf.forget()
+
+
+class MlpPlanC(ctypes.Structure):
+    """include/qwen_b200.h MlpPlanC (the engine's ctypes layout)."""
+    _fields_ = [("post_ln_w", ctypes.c_void_p), ("mant_gate", ctypes.c_void_p), ("exp_gate", ctypes.c_void_p),
+                ("M_gate", ctypes.c_int), ("K_gate", ctypes.c_int), ("mant_up", ctypes.c_void_p),
+                ("exp_up", ctypes.c_void_p), ("M_up", ctypes.c_int), ("K_up", ctypes.c_int),
+                ("mant_down", ctypes.c_void_p), ("exp_down", ctypes.c_void_p), ("M_down", ctypes.c_int),
+                ("K_down", ctypes.c_int)]
+
+
+def test_forward_mlp_dropin_matches_the_oracle_chain(lib):
+    """forward_mlp (qwen_kernels_opt.c:994-1003) on a full-attention layer's
+    MLP shapes, weights in one registered buffer as in the weight file:
+    h + down(swiglu(gate(n), up(n))), n = rmsnorm(h), equals the oracle's
+    NEON-build chain bit for bit, twice in a row (h updated in place)."""
+    H, F = 1024, 3584
+    rng = np.random.default_rng(994)
+    parts, offs, off = [], {}, 0
+    for name, (M, K) in (("gate", (F, H)), ("up", (F, H)), ("down", (H, F))):
+        mant, exps = O.pack_bfp8(rng.normal(0, 0.02, (M, K)).astype(np.float32))
+        offs[name] = (off, mant, exps)
+        parts += [mant.view(np.uint8).ravel(), exps.ravel(), np.zeros((-(mant.size + exps.size)) % 64, np.uint8)]
+        off += mant.size + exps.size + (-(mant.size + exps.size)) % 64
+    buf = np.concatenate(parts)
+    ln = (rng.normal(0, 0.1, H)).astype(np.float32)
+    lib.qwen_b200_register_weights(buf.ctypes.data, buf.nbytes)
+    p = MlpPlanC()
+    p.post_ln_w = ln.ctypes.data
+    for name in ("gate", "up", "down"):
+        o, mant, exps = offs[name]
+        setattr(p, f"mant_{name}", buf.ctypes.data + o)
+        setattr(p, f"exp_{name}", buf.ctypes.data + o + mant.size)
+        setattr(p, f"M_{name}", mant.shape[0])
+        setattr(p, f"K_{name}", mant.shape[1])
+    h = rng.normal(0, 1, H).astype(np.float32)
+    ref = h.copy()
+    for _ in range(2):
+        lib.forward_mlp(ctypes.byref(p), h.ctypes.data)
+        n = O.rmsnorm(ref, ln, 1e-6, neon=True)
+        g = O.bfp8_gemv(n, offs["gate"][1], offs["gate"][2])
+        u = O.bfp8_gemv(n, offs["up"][1], offs["up"][2])
+        d = O.bfp8_gemv(O.swiglu(g, u, neon=True), offs["down"][1], offs["down"][2])
+        ref = O.add_residual(ref, d, neon=True)
+        assert np.array_equal(bits(h), bits(ref))
+    bad = MlpPlanC()
+    lib.forward_mlp(ctypes.byref(bad), h.ctypes.data)          # refused: null pointers
+    assert b"forward_mlp" in lib.qwen_b200_last_error()
+    assert np.array_equal(bits(h), bits(ref))                    # h untouched
+    lib.qwen_b200_forget_weights(buf.ctypes.data)
+    lib.qwen_b200_forget_weights(ln.ctypes.data)                 # uploaded on first use, cached by address
