@@ -311,12 +311,14 @@ def run_b200(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int16xint8->fp32",
             "data": "synthetic: weights N(0,0.02) packed BFP8 (seeded), activations N(0,1)"}
     cpu_data = None
-    if args.workload in ("stack", "gemv"):
+    if args.workload == "gemv":
+        line.update(run_single_gemv(torch, dev, barrier, hbm_peak, peak_kind, args.steps, args.warmup))
+    elif args.workload == "stack":
         rec, cpu_data = run_stack(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kind)
         line.update(rec)
-        if args.workload == "stack" and world == 1 and not args.headline_only:
+        if world == 1 and not args.headline_only:
             line["configs"] = run_configs(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kind)
-        if args.workload == "stack" and not args.headline_only and not args.no_sharded:
+        if not args.headline_only and not args.no_sharded:
             line["sharded"] = run_sharded_records(args, torch, dist, dev, barrier, world, rank, local, hbm_peak,
                                                   peak_kind)
     elif args.workload == "sharded":
@@ -346,8 +348,7 @@ def run_b200(args):
 
 # ------------------------------------------------------------------ headline
 def run_stack(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kind):
-    """The 0.8B linear stack (or the single cfg-0 GEMV) as one grouped launch
-    per token."""
+    """The 0.8B linear stack as one grouped launch per token."""
     import numpy as np
 
     from qwen_b200 import model, ops
@@ -563,12 +564,13 @@ def run_single_gemv(torch, dev, barrier, hbm_peak, peak_kind, steps, warm):
     L.qwen_b200_forget_weights(hbuf.ctypes.data)
     ok = bool(np.array_equal(yh.view(np.uint32), y.cpu().numpy().view(np.uint32)))
     return {"value": round(gbs, 2), "unit": "GB/s", "us_per_call": round(per * 1e6, 3),
+            "ms_per_step": round(per * 1e3, 5), "gpu_launches": steps * copies,
             "config": {"workload": "single BFP8 GEMV 3584x1024, batch 1 (BASELINE config 0)",
                        "algorithmic_bytes_per_step": nbytes, "launch": "CUDA graph of one call per copy",
                        "l2": f"rotates {copies} weight copies ({copies * wbytes / 1e9:.2f} GB)"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind,
-                         "traffic": committed_traffic("gemv"), "kernel": "gemv_warp_kernel (res_act)"},
+                         "traffic": committed_traffic("gemv"), "kernel": "gemv_split_kernel"},
             "e2e": {"value": round(nbytes / call_s / 1e9, 2), "unit": "GB/s", "us_per_call": round(call_s * 1e6, 2),
                     "h2d_bytes_per_step": 4 * K, "d2h_bytes_per_step": 4 * M,
                     "path": "bfp8_gemv drop-in, host pointers, weights registered", "same_bits_as_device": ok},
@@ -661,7 +663,7 @@ def run_chain(torch, dev, barrier, hbm_peak, peak_kind, steps, warm):
                        "l2": f"rotates {copies} weight copies"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind,
-                         "kernel": "gemv_warp_kernel (res_act, 150 launches)"},
+                         "kernel": "gemv_split_kernel (150 launches)"},
             "gpu_launches_per_token": len(shapes), "clocks": clocks}
 
 

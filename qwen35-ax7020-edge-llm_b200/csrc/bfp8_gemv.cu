@@ -581,8 +581,11 @@ __device__ __forceinline__ void quantize_resident(const WArgs& A, const GemvDesc
 // arithmetic.  RTL: the RTL dequant mode (one int32 word per row, stored in
 // y's bits, sticky flags ORed into A.rtl_flags).
 template <bool LM, bool FAST, bool RTL>
-// <= 248 registers: 2048 of the SM's 65536 stay free for a 64-thread act_prep CTA
-__global__ void __maxnreg__(248) gemv_warp_kernel(const __grid_constant__ WArgs A) {
+// <= 128 registers (no spills): half of the SM's 65536 stay free, so the next
+// launch's input quantizer CTAs (64 threads, <= 32 registers) run many at a
+// time beside a resident GEMV CTA -- at a 248-register cap only one fit, and
+// the quantizer's waves between the steps of a stack cost 6% of a token
+__global__ void __maxnreg__(128) gemv_warp_kernel(const __grid_constant__ WArgs A) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                            ~uintptr_t(1023));
