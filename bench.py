@@ -70,6 +70,7 @@ def parse():
                     help="sequences per step: --workload batched (default 256) or sharded (default 1)")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="--workload sharded: stores into every GPU by the kernels, or NCCL all-gathers")
+    ap.add_argument("--topk", type=int, default=40, help="--workload lm_bf16 / lm_bfp8: k of the fused top-k")
     ap.add_argument("--headline-only", action="store_true", help="skip the per-configuration sub-records")
     ap.add_argument("--no-sharded", action="store_true", help="skip the row-sharded multi-GPU record")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -896,7 +897,7 @@ def run_lm_head(args, torch, dev, barrier, world, hbm_peak, peak_kind, workload,
 
     from qwen_b200 import _lib, ops
 
-    V, H, k = 65536, 1024, 40
+    V, H, k = 65536, 1024, getattr(args, "topk", 40)
     g = torch.Generator(device=dev)
     g.manual_seed(7)
     w = torch.randn((V, H), generator=g, device=dev) * 0.02
@@ -910,7 +911,7 @@ def run_lm_head(args, torch, dev, barrier, world, hbm_peak, peak_kind, workload,
 
         def call(i):
             ops.lm_head_bf16(h, tabs[i % copies], k, out=res)
-        desc = "bf16 lm_head 65536x1024 + argmax + top-40"
+        desc = f"bf16 lm_head 65536x1024 + argmax + top-{k}"
     else:
         mant, exps = ops.pack_bfp8(w)
         per = V * H + V * H // 64
@@ -921,7 +922,7 @@ def run_lm_head(args, torch, dev, barrier, world, hbm_peak, peak_kind, workload,
         def call(i):
             m, e = mats[i % copies]
             ops.lm_head_bfp8(h, m, e, k, out=res)
-        desc = "BFP8 lm_head 65536x1024 + argmax + top-40"
+        desc = f"BFP8 lm_head 65536x1024 + argmax + top-{k}"
     graph = graph_of(torch, call, copies)
     clk = ClockSampler(gpu_uuid(torch, dev), dev.index or 0)
     secs = timed(torch, lambda i: graph.replay(), steps, warmup, barrier)
