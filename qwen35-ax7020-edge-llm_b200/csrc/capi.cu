@@ -569,70 +569,66 @@ int lm_head_topk(const float* h, const uint16_t* embed_table, int vocab_size, in
 int sample_from_topk(const int* ids, const float* scores, int n, float temperature, int top_k, float top_p,
                      unsigned int* rng_state) {
     ProfScope ps(PF_SAMPLE);
-    // Same procedure and operation order as qwen_sampling.c:411-529.
+    // Draws equal qwen_sampling.c:411-529 bit for bit, so every rounding step below (float
+    // exponent argument, double accumulation in candidate order, the 24-bit uniform) is fixed.
     if (!ids || !scores || n <= 0) return -1;
     if (!rng_state) return ids[0];
-    std::vector<Cand> sorted_copy;
-    bool is_sorted = true;
-    for (int i = 1; i < n; i++)
-        if (scores[i] > scores[i - 1]) {
-            is_sorted = false;
-            break;
-        }
-    if (!is_sorted) {
-        sorted_copy.resize(n);
-        for (int i = 0; i < n; i++) sorted_copy[i] = {ids[i], scores[i]};
-        qsort(sorted_copy.data(), (size_t)n, sizeof(Cand), [](const void* a, const void* b) -> int {
-            const Cand* pa = static_cast<const Cand*>(a);
-            const Cand* pb = static_cast<const Cand*>(b);
-            if (pa->score > pb->score) return -1;
-            if (pa->score < pb->score) return 1;
-            if (pa->id < pb->id) return -1;
-            if (pa->id > pb->id) return 1;
-            return 0;
+
+    // The candidates in descending score order (ties: lower id first). The fused lm_head top-k
+    // already emits them that way, so the copy is only made for an unordered list.
+    std::vector<Cand> reordered;
+    bool descending = true;
+    for (int i = 1; i < n && descending; i++) descending = !(scores[i] > scores[i - 1]);
+    if (!descending) {
+        reordered.resize(n);
+        for (int i = 0; i < n; i++) reordered[i] = {ids[i], scores[i]};
+        qsort(reordered.data(), (size_t)n, sizeof(Cand), [](const void* a, const void* b) -> int {
+            const Cand& l = *static_cast<const Cand*>(a);
+            const Cand& r = *static_cast<const Cand*>(b);
+            if (l.score > r.score) return -1;  // two comparisons: unordered (NaN) scores fall
+            if (l.score < r.score) return 1;   // through to the id order
+            return l.id < r.id ? -1 : (l.id > r.id ? 1 : 0);
         });
     }
-    auto ID = [&](int i) { return is_sorted ? ids[i] : sorted_copy[i].id; };
-    auto SC = [&](int i) { return is_sorted ? scores[i] : sorted_copy[i].score; };
+    auto token = [&](int i) { return descending ? ids[i] : reordered[i].id; };
+    auto score = [&](int i) { return descending ? scores[i] : reordered[i].score; };
 
-    if (!(temperature >= 1e-6f)) return ID(0);
-    int m = n;
-    if (top_k > 0 && top_k < m) m = top_k;
-    float maxf = SC(0);
-    for (int i = 1; i < m; i++)
-        if (SC(i) > maxf) maxf = SC(i);
-    const float inv_t = 1.0f / temperature;
-    double sum_all = 0.0;
-    for (int i = 0; i < m; i++) sum_all += (double)expf((SC(i) - maxf) * inv_t);
-    if (!(sum_all > 0.0)) return ID(0);
-    float p_thresh = top_p;
-    if (!(p_thresh > 0.0f)) p_thresh = 0.0f;
-    if (p_thresh > 1.0f) p_thresh = 1.0f;
-    int keep = m;
-    double cum = 0.0;
-    for (int i = 0; i < m; i++) {
-        cum += (double)expf((SC(i) - maxf) * inv_t) / sum_all;
-        if (cum > (double)p_thresh) {
-            keep = i + 1;
+    if (!(temperature >= 1e-6f)) return token(0);  // greedy (also catches NaN)
+    const int window = (top_k > 0 && top_k < n) ? top_k : n;
+    float peak = score(0);  // first-wins scan: a NaN head stays the peak
+    for (int i = 1; i < window; i++) peak = score(i) > peak ? score(i) : peak;
+    const float inv_temp = 1.0f / temperature;
+    // Unnormalised softmax weight of candidate i, exactly as the reference rounds it.
+    auto weight = [&](int i) { return (double)expf((score(i) - peak) * inv_temp); };
+
+    double z_window = 0.0;
+    for (int i = 0; i < window; i++) z_window += weight(i);
+    if (!(z_window > 0.0)) return token(0);
+
+    // Nucleus: the shortest prefix whose probability mass passes clamp(top_p, 0, 1).
+    const float mass = top_p > 1.0f ? 1.0f : (top_p > 0.0f ? top_p : 0.0f);
+    int nucleus = window;
+    double share = 0.0;
+    for (int i = 0; i < window; i++) {
+        share += weight(i) / z_window;
+        if (share > (double)mass) {
+            nucleus = i + 1;
             break;
         }
     }
-    if (keep < 1) keep = 1;
-    double sum_keep = 0.0;
-    for (int i = 0; i < keep; i++) sum_keep += (double)expf((SC(i) - maxf) * inv_t);
-    if (!(sum_keep > 0.0)) return ID(0);
+    double z_nucleus = 0.0;
+    for (int i = 0; i < nucleus; i++) z_nucleus += weight(i);
+    if (!(z_nucleus > 0.0)) return token(0);
+
+    // Inverse-CDF draw with a 24-bit uniform from the xorshift32 stream.
     const double u = (double)((float)(xs32_next(rng_state) >> 8) * (1.0f / 16777216.0f));
-    const double r = u * sum_keep;
-    cum = 0.0;
-    int chosen = keep - 1;
-    for (int i = 0; i < keep; i++) {
-        cum += (double)expf((SC(i) - maxf) * inv_t);
-        if (r < cum) {
-            chosen = i;
-            break;
-        }
+    const double target = u * z_nucleus;
+    double below = 0.0;
+    for (int i = 0; i < nucleus; i++) {
+        below += weight(i);
+        if (target < below) return token(i);
     }
-    return ID(chosen);
+    return token(nucleus - 1);
 }
 
 // ------------------------------------------------------------ device entry points

@@ -68,6 +68,50 @@ def test_sampler_matches_reference(golden):
         assert st.value == st1, i
 
 
+REF_SAMPLING = os.path.join(REPO, "oracle", "_ref", "libref_sampling.so")
+
+
+@pytest.mark.skipif(not os.path.exists(REF_SAMPLING), reason="oracle/_ref not built (make -C oracle ref)")
+def test_sampler_matches_compiled_reference_on_random_lists():
+    """Draw for draw against the reference's own sample_from_topk compiled here
+    (qwen_sampling.c:411-529): unordered lists, tied scores, NaN scores, and the
+    temperature / top_k / top_p edges (0, negative, NaN, above 1)."""
+    from qwen_b200 import _lib
+
+    lib = _lib.load()
+    ref = ctypes.CDLL(REF_SAMPLING)
+    for f in (lib.sample_from_topk, ref.sample_from_topk):
+        f.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_int,
+                      ctypes.c_float, ctypes.c_void_p]
+        f.restype = ctypes.c_int
+    rng = np.random.default_rng(7)
+    temps = [0.0, 1e-7, 1e-6, 0.3, 0.8, 1.0, 2.5, -1.0, float("nan")]
+    top_ps = [0.0, 0.05, 0.5, 0.9, 0.95, 1.0, 1.5, -0.2, float("nan")]
+    for case in range(600):
+        n = int(rng.integers(1, 70))
+        ids = rng.permutation(200000)[:n].astype(np.int32)
+        kind = case % 4
+        if kind == 0:
+            sc = np.sort(rng.normal(0, 3, n).astype(np.float32))[::-1].copy()
+        elif kind == 1:
+            sc = rng.normal(0, 3, n).astype(np.float32)
+        elif kind == 2:
+            sc = rng.integers(-3, 3, n).astype(np.float32)  # many ties
+        else:
+            sc = rng.normal(0, 3, n).astype(np.float32)
+            sc[rng.integers(0, n, max(1, n // 8))] = np.nan
+        t = temps[case % len(temps)]
+        tp = top_ps[(case // len(temps)) % len(top_ps)]
+        tk = int(rng.integers(-2, n + 3))
+        s0 = int(rng.integers(1, 2**32))
+        a, b = ctypes.c_uint(s0), ctypes.c_uint(s0)
+        for _ in range(8):
+            da = lib.sample_from_topk(ids.ctypes.data, sc.ctypes.data, n, t, tk, tp, ctypes.byref(a))
+            db = ref.sample_from_topk(ids.ctypes.data, sc.ctypes.data, n, t, tk, tp, ctypes.byref(b))
+            assert da == db, (case, n, t, tk, tp)
+        assert a.value == b.value, case
+
+
 def test_sampler_selftest_cases():
     """The reference self-test's sampling cases (qwen_sampling.c:682-898)."""
     from qwen_b200 import _lib
