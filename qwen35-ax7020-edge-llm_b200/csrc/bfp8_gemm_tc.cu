@@ -96,11 +96,9 @@ struct TcCfg {
     static constexpr int kThreads = 64 + 32 * kEpiWarps;
     static constexpr int kCols = N / kColSplit;                      // columns per epilogue thread
     // Small tiles: the epilogue takes kGroup blocks per round (one barrier
-    // wait and one TMEM load wait for all of them).  Large
-    // tiles: one block per round, its columns in kChunk pieces whose TMEM
-    // loads overlap the previous piece's arithmetic.
+    // wait and one TMEM load wait for all of them).  Large tiles: one block
+    // per round, read whole and its slot freed before the arithmetic.
     static constexpr int kGroup = N <= 16 ? 4 : (N <= 32 ? 2 : 1);
-    static constexpr int kChunk = kGroup > 1 ? kCols : 8;
     static constexpr int kGroupsInFlight = kSlots / kGroup;
     // blocks whose TMEM slots the MMA thread claims with one wait (whole
     // epilogue groups, at most half of the slots)
@@ -223,7 +221,7 @@ __device__ __forceinline__ int desc_index(const DescRow* tab, int n, int u, int 
 
 // Warp-uniform bounded wait (every lane polls; the warp agrees on the result).
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, unsigned int* err) {
-    const bool ok = mbar_wait(bar, parity, err);
+    const bool ok = mbar_wait_sleep(bar, parity, err);
     return __all_sync(0xffffffffu, ok);
 }
 
@@ -250,7 +248,9 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
     // the next launch on the stream (a programmatic dependent) may start its
     // CTAs' prologues on the SMs this grid's finished CTAs leave
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // the warp index broadcast from lane 0: the compiler then knows it (and the
+    // TMEM addresses built from it) to be warp-uniform
+    const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0), lane = threadIdx.x & 31;
     const int n = p.descs ? p.n : 1;
     for (int k = threadIdx.x; k < n; k += blockDim.x) {
         const TcDesc* d = p.descs ? p.descs + k : &p.one;
@@ -272,10 +272,10 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kStages; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], C::kEpiWarps);   // every epilogue warp, after the stage's MMAs completed
+            mbar_init(&empty[s], C::kEpiWarps * 32);   // every epilogue thread, after the stage's MMAs completed
         }
         for (int g = 0; g < C::kGroupsInFlight; g++) mbar_init(&tfull[g], 1);
-        for (int t = 0; t < C::kSlots; t++) mbar_init(&tempty[t], C::kEpiWarps);
+        for (int t = 0; t < C::kSlots; t++) mbar_init(&tempty[t], C::kEpiWarps * 32);
         for (int b = 0; b < 2; b++) {
             mbar_init(&ufull[b], 1);
             mbar_init(&uempty[b], C::kEpiWarps);
@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
                 info.cfirst = cfirst;
                 info.pslot = 2 * (int)blockIdx.x + ((int)blockIdx.x == cfirst ? 1 : 0);
                 info.tickets = npieces > 1 ? p.tickets + (size_t)(r.tile_begin + tile) * kTcTicketsPerTile : nullptr;
-                if (!mbar_wait(&uempty[eb], ((i >> 1) & 1) ^ 1, p.err)) {
+                if (!mbar_wait_sleep(&uempty[eb], ((i >> 1) & 1) ^ 1, p.err)) {
                     bad = true;
                     return;
                 }
@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
                 i++;
                 for (int sg = st0; sg < st1; sg++, gs++) {   // sg: stage index along the tile's K
                     const int s = gs % C::kStages;
-                    if (!mbar_wait(&empty[s], ((gs / C::kStages) & 1) ^ 1, p.err)) {
+                    if (!mbar_wait_sleep(&empty[s], ((gs / C::kStages) & 1) ^ 1, p.err)) {
                         bad = true;
                         return;
                     }
@@ -408,14 +408,14 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
             }
             if (!bad) {   // end of the sequence: an entry with no blocks
                 const int eb = i & 1;
-                if (mbar_wait(&uempty[eb], ((i >> 1) & 1) ^ 1, p.err)) {
+                if (mbar_wait_sleep(&uempty[eb], ((i >> 1) & 1) ^ 1, p.err)) {
                     uring[eb].nbs = 0;
                     mbar_arrive_expect_tx(&ufull[eb], 0);
                 }
             }
             // the last loads of every slot have landed unless a consumer quit early
             for (uint32_t k = gs > (uint32_t)C::kStages ? gs - C::kStages : 0; k < gs; k++)
-                mbar_wait(&full[k % C::kStages], (k / C::kStages) & 1, nullptr);
+                mbar_wait_sleep(&full[k % C::kStages], (k / C::kStages) & 1, nullptr);
         }
     } else if (warp == 1) {
         // ---------------------------------------------------- MMA issuer
@@ -425,12 +425,12 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
             uint32_t gs = 0, gb = 0, gg = 0;
             bool bad = false;
             for (int i = 0; !bad; i++) {
-                if (!mbar_wait(&ufull[i & 1], (i >> 1) & 1, p.err)) break;
+                if (!mbar_wait_sleep(&ufull[i & 1], (i >> 1) & 1, p.err)) break;
                 const int nb = uring[i & 1].nbs, nst = (nb + C::kBPS - 1) / C::kBPS;   // this unit's blocks
                 if (nb == 0) break;   // end of the sequence
                 for (int st = 0; st < nst && !bad; st++, gs++) {
                     const int s = gs % C::kStages;
-                    if (!mbar_wait(&full[s], (gs / C::kStages) & 1, p.err)) {
+                    if (!mbar_wait_sleep(&full[s], (gs / C::kStages) & 1, p.err)) {
                         bad = true;
                         break;
                     }
@@ -440,7 +440,7 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
                         const int t = gb % C::kSlots, j = st * C::kBPS + h;
                         if (j % C::kWaitSpan == 0) {   // slots free in order: wait for the span's last one
                             const uint32_t gl = gb + (uint32_t)(min(C::kWaitSpan, nb - j) - 1);
-                            if (!mbar_wait(&tempty[gl % C::kSlots], ((gl / C::kSlots) & 1) ^ 1, p.err)) {
+                            if (!mbar_wait_sleep(&tempty[gl % C::kSlots], ((gl / C::kSlots) & 1) ^ 1, p.err)) {
                                 bad = true;
                                 break;
                             }
@@ -464,7 +464,7 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
             }
             // no MMA may still be writing TMEM when it is released
             mma_commit(done);
-            mbar_wait(done, 0, nullptr);
+            mbar_wait_sleep(done, 0, nullptr);
         }
     } else {
         // ---------------------------------------------------- epilogue
@@ -485,42 +485,42 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
 #pragma unroll
             for (int k = 0; k < C::kCols / 2; k++) acc[k] = make_float2(0.0f, 0.0f);
 
-            // acc += float(256*Dhi + Dlo) * 2^(e-134) * xs over kCh columns
-            // starting at column c of block j; hv/lv are the raw accumulators.
-            auto accumulate = [&](const uint32_t* hv, const uint32_t* lv, int c, int kCh, int j, uint32_t e) {
+            // Per block: the shared-state address of this thread's first scale
+            // (plain shared loads, not generic ones) and the weight scale pair.
+            auto scale_base = [&](int j) -> uint32_t {
                 const int s = (gs + j / C::kBPS) % C::kStages;
-                const float sm = exp_scale_ieee(e);
-                const float2 sm2 = make_float2(sm, sm);
-                // shared-state address of the scales: plain shared loads, not generic ones
-                const uint32_t xsa = smem_u32(sxs) + (uint32_t)(s * C::kSBytes + ((j % C::kBPS) * N + col0 + c) * 4);
+                return smem_u32(sxs) + (uint32_t)(s * C::kSBytes + ((j % C::kBPS) * N + col0) * 4);
+            };
+            // acc += float(D) * 2^(e-134) * xs over the kCh columns starting at
+            // column c; dv holds the exact int32 block dots of block j.
+            auto scale_add = [&](const int* dv, int c, int kCh, uint32_t xsb, float2 sm2, int j) {
                 float4 x4;   // one 16-byte load serves four columns (two pairs)
 #pragma unroll
                 for (int k = 0; k < kCh; k += 2) {
                     if ((k & 2) == 0)
                         asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
                                      : "=f"(x4.x), "=f"(x4.y), "=f"(x4.z), "=f"(x4.w)
-                                     : "r"(xsa + 4 * k));
+                                     : "r"(xsb + 4 * (c + k)));
                     const float2 xs2 = (k & 2) ? make_float2(x4.z, x4.w) : make_float2(x4.x, x4.y);
-                    // the exact int32 dot 256 * Dhi + Dlo, converted with one rounding
-                    const float2 fd = make_float2(__int2float_rn((int)hv[k] * 256 + (int)lv[k]),
-                                                  __int2float_rn((int)hv[k + 1] * 256 + (int)lv[k + 1]));
+                    const float2 fd = make_float2(__int2float_rn(dv[k]), __int2float_rn(dv[k + 1]));
                     acc[(c + k) / 2] = __ffma2_rn(fd, __fmul2_rn(sm2, xs2), acc[(c + k) / 2]);
                     if constexpr (DOTS) {
 #pragma unroll
                         for (int w = 0; w < 2; w++) {
-                            const int D = (int)hv[k + w] * 256 + (int)lv[k + w];
                             const int b = nt * N + col0 + c + k + w;
-                            if (row_ok && b < B) info.dots[((size_t)b * M + m) * info.nb + info.j0 + j] = D;
+                            if (row_ok && b < B) info.dots[((size_t)b * M + m) * info.nb + info.j0 + j] = dv[k + w];
                         }
                     }
                 }
             };
-            // this warp is done with a stage's scales after the stage's last block
+            auto accumulate = [&](const int* dv, int c, int kCh, int j, uint32_t e) {
+                const float sm = exp_scale_ieee(e);
+                scale_add(dv, c, kCh, scale_base(j), make_float2(sm, sm), j);
+            };
+            // this thread is done with a stage's scales after the stage's last
+            // block (every epilogue thread arrives: no divergent branch)
             auto release_stage = [&](int j) {
-                if (j % C::kBPS == C::kBPS - 1 || j == nb - 1) {
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&empty[(gs + j / C::kBPS) % C::kStages]);
-                }
+                if (j % C::kBPS == C::kBPS - 1 || j == nb - 1) mbar_arrive(&empty[(gs + j / C::kBPS) % C::kStages]);
             };
 
             for (int j0 = 0; j0 < nb; j0 += G) {
@@ -549,33 +549,50 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
                     for (int g = 0; g < G; g++)
 #pragma unroll
                         for (int k = 0; k < C::kCols; k++) asm volatile("" : "+r"(hv[g][k]), "+r"(lv[g][k]));
+                    int dv[G][C::kCols];
+#pragma unroll
+                    for (int g = 0; g < G; g++)
+#pragma unroll
+                        for (int k = 0; k < C::kCols; k++) dv[g][k] = (int)hv[g][k] * 256 + (int)lv[g][k];
+                    // the group's slots are free once their dots are in registers
+                    tc_fence_before();
+                    for (int g = 0; g < ng; g++) mbar_arrive(&tempty[(gb + g) % C::kSlots]);
 #pragma unroll
                     for (int g = 0; g < G; g++)
                         if (g < ng) {
-                            accumulate(hv[g], lv[g], 0, C::kCols, j0 + g, ev[g]);
+                            accumulate(dv[g], 0, C::kCols, j0 + g, ev[g]);
                             release_stage(j0 + g);
                         }
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0)
-                        for (int g = 0; g < ng; g++) mbar_arrive(&tempty[(gb + g) % C::kSlots]);
                 } else {
+                    // Wide tiles: the slot slice is read in pieces (one TMEM load
+                    // per plane, then one wait): the whole 16 columns of a thread,
+                    // or 8 at a time of 32 (the 96-register budget of an 18-warp
+                    // CTA); each piece is reduced to the exact block dots
+                    // 256 * Dhi + Dlo and scaled.  Every thread frees the slot as
+                    // soon as the last piece is in registers, so the MMAs of a
+                    // later block overlap that piece's arithmetic.
                     const uint32_t tcol = tmem + lane_base + (uint32_t)((gb % C::kSlots) * 2 * N + col0);
-                    uint32_t hv[2][C::kChunk], lv[2][C::kChunk];
-                    tmem_ld<C::kChunk>(tcol, hv[0]);
-                    tmem_ld<C::kChunk>(tcol + N, lv[0]);
+                    const float sm = exp_scale_ieee(ev[0]);
+                    const float2 sm2 = make_float2(sm, sm);
+                    const uint32_t xsb = scale_base(j0);
+                    constexpr int kPiece = C::kCols <= 16 ? C::kCols : 8;
 #pragma unroll
-                    for (int c = 0, ci = 0; c < C::kCols; c += C::kChunk, ci++) {
-                        tmem_wait_ld_dep<C::kChunk>(hv[ci & 1], lv[ci & 1]);
-                        if (c + C::kChunk < C::kCols) {   // next piece loads while this one is summed
-                            tmem_ld<C::kChunk>(tcol + c + C::kChunk, hv[(ci + 1) & 1]);
-                            tmem_ld<C::kChunk>(tcol + N + c + C::kChunk, lv[(ci + 1) & 1]);
+                    for (int c = 0; c < C::kCols; c += kPiece) {
+                        int dv[kPiece];
+                        {
+                            uint32_t hv[kPiece], lv[kPiece];
+                            tmem_ld<kPiece>(tcol + c, hv);
+                            tmem_ld<kPiece>(tcol + N + c, lv);
+                            tmem_wait_ld_dep<kPiece>(hv, lv);
+#pragma unroll
+                            for (int k = 0; k < kPiece; k++) dv[k] = (int)hv[k] * 256 + (int)lv[k];
                         }
-                        accumulate(hv[ci & 1], lv[ci & 1], c, C::kChunk, j0, ev[0]);
+                        if (c + kPiece == C::kCols) {
+                            tc_fence_before();
+                            mbar_arrive(&tempty[gb % C::kSlots]);
+                        }
+                        scale_add(dv, c, kPiece, xsb, sm2, j0);
                     }
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&tempty[gb % C::kSlots]);
                     release_stage(j0);
                 }
                 gb += ng;

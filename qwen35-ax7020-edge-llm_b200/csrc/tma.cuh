@@ -50,6 +50,31 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
     return false;
 }
 
+// try_wait with a suspend-time hint: the thread may stay suspended for up
+// to `ns` nanoseconds, and resumes when the phase completes, so a blocked
+// waiter issues one instruction per window instead of re-polling.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"((uint32_t)__cvta_generic_to_shared(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+constexpr uint32_t kSleepHintNs = 1000;
+constexpr uint32_t kSleepWaitLimit = 1u << 22;   // windows of at most kSleepHintNs: a bound of ~4 s
+// Bounded wait for kernels whose waiters share SM sub-partitions with busy
+// warps (same error contract as mbar_wait).
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, unsigned int* err) {
+    for (uint32_t i = 0; i < kSleepWaitLimit; i++)
+        if (mbar_try_wait_hint(bar, parity, kSleepHintNs)) return true;
+    if (err) atomicOr(err, kErrMbarTimeout);
+    return false;
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
