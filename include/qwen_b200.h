@@ -157,11 +157,62 @@ typedef struct {
  * device (rmsnorm in front of gate and of up, swiglu in front of down, the
  * residual add); h (host, K_gate floats) is copied in and back, weight and
  * norm pointers are translated like bfp8_gemv's.  K_gate == K_up <= 6144,
- * M_gate == M_up == K_down, M_down == K_gate.  On error h is unchanged and
- * qwen_b200_last_error() says why.  (LinearLayerPlanC's forward_linear_layer
- * and forward_token_c also run the Gated-DeltaNet / attention glue, which
- * this library does not serve.) */
+ * M_gate == M_up == K_down, M_down == K_gate, multiples of 512.  On error h
+ * is unchanged and qwen_b200_last_error() says why. */
 QB_API void forward_mlp(const MlpPlanC* p, float* h);
+
+/* Replaces forward_linear_layer() (qwen_kernels_opt.c:938-992; caller
+ * qwen_real_engine.py:1096): one Gated-DeltaNet layer on the device in
+ * eight launches -- the qkv and z projections of rmsnorm(h, in_ln_w)
+ * (fused), one kernel for conv1d + SiLU, q/k l2 norm, the gates, the
+ * recurrent step and rmsnorm_gated (one CTA per head), the out projection,
+ * then the MLP with h + o formed in front of its gate projection.  NEON-build
+ * order throughout (the GEMVs bit for bit); the gates and the gated norm's
+ * SiLU use CUDA's expf / log1pf where the reference calls the C library's.
+ * Shapes: K_qkv == K_z == M_o == K_gate <= 6144 (a multiple of 512),
+ * M_qkv == 3 * M_z, M_z == K_o a multiple of 128 (heads = M_z / 128), the
+ * MLP as forward_mlp's.  conv_s (3 x M_qkv floats) and state (heads x 128 x
+ * 128 floats, the reference's blocked layout) are the engine's host arrays
+ * and are updated in place (state mode below).  fp32 vectors and weights
+ * resolve like bfp8_gemv's pointers (uploaded on first sight and kept: a
+ * vector rewritten in place needs qwen_b200_forget_weights()).  On error h
+ * and the states are unchanged and qwen_b200_last_error() says why. */
+QB_API void forward_linear_layer(const LinearLayerPlanC* p, float* h);
+
+/* The callback forward_token_c runs for a full-attention layer
+ * (qwen_kernels_opt.c:1006; qwen_real_engine.py:982): layer index, the
+ * host h to update in place, the caller's context. */
+typedef void (*QbFullAttnCallback)(int layer_idx, float* h, void* py_context);
+
+/* Replaces forward_token_c() (qwen_kernels_opt.c:1008-1049; caller
+ * qwen_real_engine.py:1262-1272): h = the bf16 embedding row of
+ * token_id % 65536; 24 layers -- a full-attention layer (layer_is_full[l])
+ * runs full_attn_cb on the host h (copied out, the callback may call
+ * bfp8_gemv and the other drop-ins, copied back in), then forward_mlp with
+ * mlp_plans[l]; the others forward_linear_layer with the next of
+ * linear_plans; then the final rmsnorm and the lm_head argmax over the
+ * 65536 embedding rows.  h stays on the device between layers; on return it
+ * holds the last residual stream.  Returns the token id, or -1 (h and the
+ * states unchanged unless the failure came after a callback) with
+ * qwen_b200_last_error().  Hidden size 1024, as the reference's loop.  Not
+ * reentrant across threads (neither is the reference's static workspace). */
+QB_API int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linear_plans, const MlpPlanC* mlp_plans,
+                           const int* layer_is_full, const float* final_norm_w, const uint16_t* embed_table,
+                           QbFullAttnCallback full_attn_cb, void* py_context);
+
+/* Gated-DeltaNet state residency (no reference counterpart).  Mode 0 (the
+ * default, the reference's contract): every forward_linear_layer /
+ * forward_token_c call copies each layer's conv_s and state host arrays to
+ * the device before its work and back after it (19.3 MB each way per token
+ * for the 0.8B model).  Mode 1: the device copy, made on first sight after
+ * entering the mode, is the state; the host arrays are only written by
+ * qwen_b200_gdn_state_sync()
+ * (and when switching back to mode 0).  A caller that resets or rewrites its
+ * state arrays in mode 1 calls qwen_b200_gdn_state_drop() first, so the next
+ * call re-reads them.  Return 0 or a QB_E* code. */
+QB_API int qwen_b200_gdn_state_mode(int resident);
+QB_API int qwen_b200_gdn_state_sync(void);
+QB_API void qwen_b200_gdn_state_drop(void);
 
 /* Replace the stage profiler (qwen_kernels_opt.c:71-91; read by
  * qwen_real_engine.py:1008-1047 when QWEN_PROFILE=1).  Slots accumulate

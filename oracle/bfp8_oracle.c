@@ -507,3 +507,346 @@ ORC_API void orc_selftest_fill(uint32_t* state, uint16_t* tab, size_t n_tab, flo
         h[i] = (float)v * (1.0f / 16384.0f);
     }
 }
+
+/* ============================================ Gated-DeltaNet layer and token loop
+ * The glue forward_linear_layer / forward_token_c run around the GEMVs
+ * (qwen_kernels_opt.c:507-858, 938-1049).  Every routine takes `neon`: 1 is
+ * the board build (Advanced SIMD lanes, flushed, VMLA not fused; scalar VFP
+ * where the reference leaves the vector unit), 0 the portable build the
+ * reference compiles to on x86 (plain C float arithmetic, the C library's
+ * expf/log1pf). */
+
+/* causal_conv1d_update_silu (qwen_kernels_opt.c:511-545): channel c has the
+ * weights w[4c..4c+3] and the state s0/s1/s2 (three rows of C floats):
+ * d = w0*s0 + w1*s1 + w2*s2 + w3*x, y = d / (1 + exp(-d)), then the state
+ * shifts (s0 <- s1 <- s2 <- x).  NEON build, channels in groups of four:
+ * the multiply and the three multiply-adds (product rounded first), the
+ * exp_neon of -d and 1 + e on the vector unit, the division on VFP.
+ * The portable build has no scalar loop for those groups: its loop starts at
+ * C & ~3 (the vector loop that would cover channels below it is compiled
+ * out), so it computes only a C % 4 tail and leaves every other channel's
+ * output and state untouched -- restated as such for neon = 0. */
+ORC_API void orc_conv1d_silu(float* y, const float* x, float* st, const float* w, int C, int neon) {
+    float* s0 = st;
+    float* s1 = st + C;
+    float* s2 = st + 2 * C;
+    int c = neon ? 0 : (C & ~3);
+    if (neon)
+        for (; c < (C & ~3); c++) {
+            const float xc = x[c], t0 = s0[c], t1 = s1[c], t2 = s2[c];
+            float d = neon_mul(w[4 * c], t0);
+            d = neon_add(d, neon_mul(w[4 * c + 1], t1));
+            d = neon_add(d, neon_mul(w[4 * c + 2], t2));
+            d = neon_add(d, neon_mul(w[4 * c + 3], xc));
+            y[c] = d / neon_add(1.0f, exp_neon_lane(-d));
+            s0[c] = t1;
+            s1[c] = t2;
+            s2[c] = xc;
+        }
+    for (; c < C; c++) {
+        const float xc = x[c];
+        const float dot = w[4 * c] * s0[c] + w[4 * c + 1] * s1[c] + w[4 * c + 2] * s2[c] + w[4 * c + 3] * xc;
+        y[c] = dot / (1.0f + expf(-dot));
+        s0[c] = s1[c];
+        s1[c] = s2[c];
+        s2[c] = xc;
+    }
+}
+
+/* Four flushed lane sums of a[i]*b[i] over i = 4j + l, combined as
+ * (s0 + s2) + (s1 + s3) -- the VMLA accumulator, vadd(low, high), vpadd
+ * reduction the reference uses for every vector dot (returns the number of
+ * elements consumed: n rounded down to a multiple of 4). */
+static int neon_dot4(const float* a, const float* b, int n, float* out) {
+    float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    int i = 0;
+    for (; i + 4 <= n; i += 4)
+        for (int l = 0; l < 4; l++) s[l] = neon_add(s[l], neon_mul(a[i + l], b[i + l]));
+    *out = neon_add(neon_add(s[0], s[2]), neon_add(s[1], s[3]));
+    return i;
+}
+
+/* qk_l2norm (qwen_kernels_opt.c:548-591): per head, k *= 1/sqrt(|k|^2 + 1e-6),
+ * q *= (1/sqrt(D)) / sqrt(|q|^2 + 1e-6).  NEON build: the squared norms by
+ * neon_dot4 (any tail on VFP), the scales on VFP, the products on the
+ * vector unit (which leaves a D % 4 tail unscaled, as the reference does). */
+ORC_API void orc_qk_l2norm(float* q, float* k, int H, int D, int neon) {
+    const float q_scale = 1.0f / sqrtf((float)D);
+    const float eps = 1e-6f;
+    for (int h = 0; h < H; h++) {
+        float* kh = k + (size_t)h * D;
+        float* qh = q + (size_t)h * D;
+        float k_sq = 0.0f, q_sq = 0.0f;
+        int i = 0;
+        if (neon) {
+            neon_dot4(kh, kh, D, &k_sq);
+            i = neon_dot4(qh, qh, D, &q_sq);
+        }
+        for (; i < D; i++) {
+            k_sq += kh[i] * kh[i];
+            q_sq += qh[i] * qh[i];
+        }
+        const float k_r = 1.0f / sqrtf(k_sq + eps);
+        const float q_r = q_scale / sqrtf(q_sq + eps);
+        if (neon) {
+            for (i = 0; i < (D & ~3); i++) {
+                kh[i] = neon_mul(kh[i], k_r);
+                qh[i] = neon_mul(qh[i], q_r);
+            }
+        } else {
+            for (i = 0; i < D; i++) {
+                kh[i] *= k_r;
+                qh[i] *= q_r;
+            }
+        }
+    }
+}
+
+/* gdn_gates (qwen_kernels_opt.c:593-625): per head h, av = wa[h].x and
+ * bv = wb[h].x (neon_dot4 on the NEON build, any tail on VFP);
+ * beta = 1 / (1 + expf(-bv)); alpha = expf(nea[h] * log1pf(expf(av + dt[h])))
+ * on VFP with the C library's expf / log1pf. */
+ORC_API void orc_gdn_gates(float* alpha, float* beta, const float* x, const float* wa, const float* wb,
+                           const float* nea, const float* dt, int H, int K, int neon) {
+    for (int h = 0; h < H; h++) {
+        const float* ra = wa + (size_t)h * K;
+        const float* rb = wb + (size_t)h * K;
+        float av = 0.0f, bv = 0.0f;
+        int i = 0;
+        if (neon) {
+            neon_dot4(ra, x, K, &av);
+            i = neon_dot4(rb, x, K, &bv);
+        }
+        for (; i < K; i++) {
+            av += ra[i] * x[i];
+            bv += rb[i] * x[i];
+        }
+        beta[h] = 1.0f / (1.0f + expf(-bv));
+        const float z = av + dt[h];
+        alpha[h] = expf(nea[h] * log1pf(expf(z)));
+    }
+}
+
+/* gdn_recurrent_step (qwen_kernels_opt.c:664-829).  State of head h: D x D
+ * floats, blocked so that S[i][j] sits at ((j/4 * D/4 + i/4) * 4 + j%4) * 4 +
+ * i%4.  Per head: qk = q.k (neon_dot4 on the NEON build, one running sum on
+ * the portable one); per column j: kv = sum_i S[i][j] k[i] and
+ * qs = sum_i S[i][j] q[i] in ascending i (product rounded, then added);
+ * d = (v - kv*a) * b; out = qs*a + qk*d; then S[i][j] = S*a + d*k[i].  Both
+ * builds use that order; the NEON one flushes every step. */
+ORC_API void orc_gdn_step(float* out, float* state, const float* q, const float* k, const float* v,
+                          const float* alpha, const float* beta, int H, int D, int neon) {
+    for (int h = 0; h < H; h++) {
+        const float* qh = q + (size_t)h * D;
+        const float* kh = k + (size_t)h * D;
+        const float* vh = v + (size_t)h * D;
+        float* oh = out + (size_t)h * D;
+        const float a = alpha[h], b = beta[h];
+        float* S = state + (size_t)h * D * D;
+        float qk = 0.0f;
+        if (neon)
+            neon_dot4(qh, kh, D, &qk);
+        else
+            for (int i = 0; i < D; i++) qk += qh[i] * kh[i];
+        for (int j0 = 0; j0 < D; j0 += 4) {
+            float* B = S + (size_t)(j0 >> 2) * D * 4;
+            float kv[4] = {0.0f, 0.0f, 0.0f, 0.0f}, qs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int i = 0; i < D; i++) {
+                const int blk = (i >> 2) * 16 + (i & 3);
+                for (int l = 0; l < 4; l++) {
+                    const float t = B[blk + l * 4];
+                    if (neon) {
+                        kv[l] = neon_add(kv[l], neon_mul(t, kh[i]));
+                        qs[l] = neon_add(qs[l], neon_mul(t, qh[i]));
+                    } else {
+                        kv[l] += kh[i] * t;
+                        qs[l] += qh[i] * t;
+                    }
+                }
+            }
+            float dd[4];
+            for (int l = 0; l < 4; l++) {
+                if (neon) {
+                    dd[l] = neon_mul(neon_sub(vh[j0 + l], neon_mul(kv[l], a)), b);
+                    oh[j0 + l] = neon_add(neon_mul(qs[l], a), neon_mul(qk, dd[l]));
+                } else {
+                    dd[l] = b * (vh[j0 + l] - a * kv[l]);
+                    oh[j0 + l] = a * qs[l] + qk * dd[l];
+                }
+            }
+            for (int i = 0; i < D; i++) {
+                const int blk = (i >> 2) * 16 + (i & 3);
+                for (int l = 0; l < 4; l++) {
+                    float* t = &B[blk + l * 4];
+                    *t = neon ? neon_add(neon_mul(*t, a), neon_mul(dd[l], kh[i])) : a * *t + kh[i] * dd[l];
+                }
+            }
+        }
+    }
+}
+
+/* rmsnorm_gated (qwen_kernels_opt.c:832-858): per head, r = 1 / sqrtf(|x|^2 / D
+ * + eps) (the squared norm by neon_dot4 on the NEON build); then on VFP
+ * y = ((x * r) * w[i]) * (z / (1 + expf(-z))). */
+ORC_API void orc_rmsnorm_gated(float* y, const float* x, const float* z, const float* w, int H, int D, float eps,
+                               int neon) {
+    for (int h = 0; h < H; h++) {
+        const float* xh = x + (size_t)h * D;
+        const float* zh = z + (size_t)h * D;
+        float* yh = y + (size_t)h * D;
+        float ss = 0.0f;
+        int i = 0;
+        if (neon) i = neon_dot4(xh, xh, D, &ss);
+        for (; i < D; i++) ss += xh[i] * xh[i];
+        const float r = 1.0f / sqrtf((ss / (float)D) + eps);
+        for (i = 0; i < D; i++) {
+            const float zi = zh[i];
+            yh[i] = xh[i] * r * w[i] * (zi / (1.0f + expf(-zi)));
+        }
+    }
+}
+
+/* The plans of the token loop, field for field the reference's
+ * (qwen_kernels_opt.c:866-917). */
+typedef struct {
+    const float* in_ln_w;
+    const int8_t* mant_qkv;
+    const uint8_t* exp_qkv;
+    int M_qkv, K_qkv;
+    const float* conv_w;
+    float* conv_s;
+    const float* wa;
+    const float* wb;
+    const float* nea;
+    const float* dt;
+    float* state;
+    const int8_t* mant_z;
+    const uint8_t* exp_z;
+    int M_z, K_z;
+    const float* norm_w;
+    const int8_t* mant_o;
+    const uint8_t* exp_o;
+    int M_o, K_o;
+    const float* post_ln_w;
+    const int8_t* mant_gate;
+    const uint8_t* exp_gate;
+    int M_gate, K_gate;
+    const int8_t* mant_up;
+    const uint8_t* exp_up;
+    int M_up, K_up;
+    const int8_t* mant_down;
+    const uint8_t* exp_down;
+    int M_down, K_down;
+} OrcLinearPlan;
+
+typedef struct {
+    const float* post_ln_w;
+    const int8_t* mant_gate;
+    const uint8_t* exp_gate;
+    int M_gate, K_gate;
+    const int8_t* mant_up;
+    const uint8_t* exp_up;
+    int M_up, K_up;
+    const int8_t* mant_down;
+    const uint8_t* exp_down;
+    int M_down, K_down;
+} OrcMlpPlan;
+
+enum { kOrcHidden = 1024, kOrcHeads = 16, kOrcHeadDim = 128, kOrcVocab = 65536, kOrcLayers = 24 };
+
+static void orc_gemv(float* y, const float* x, const int8_t* m, const uint8_t* e, int M, int K, int neon) {
+    if (neon)
+        orc_bfp8_gemv_neon(y, x, m, e, M, K);
+    else
+        orc_bfp8_gemv_scalar(y, x, m, e, M, K);
+}
+static void orc_rmsnorm(float* y, const float* x, const float* w, int n, int neon) {
+    if (neon)
+        orc_rmsnorm_neon(y, x, w, n, 1e-6f);
+    else
+        orc_rmsnorm_scalar(y, x, w, n, 1e-6f);
+}
+
+/* forward_mlp (qwen_kernels_opt.c:994-1004): h += down(swiglu(gate(n), up(n))),
+ * n = rmsnorm(h, post_ln_w). */
+ORC_API void orc_forward_mlp(const OrcMlpPlan* p, float* h, int neon) {
+    const int H = kOrcHidden, F = p->M_gate;
+    float* n = (float*)malloc(sizeof(float) * H);
+    float* g = (float*)malloc(sizeof(float) * F);
+    float* u = (float*)malloc(sizeof(float) * F);
+    float* a = (float*)malloc(sizeof(float) * F);
+    float* d = (float*)malloc(sizeof(float) * H);
+    orc_rmsnorm(n, h, p->post_ln_w, H, neon);
+    orc_gemv(g, n, p->mant_gate, p->exp_gate, p->M_gate, p->K_gate, neon);
+    orc_gemv(u, n, p->mant_up, p->exp_up, p->M_up, p->K_up, neon);
+    orc_swiglu(a, g, u, F, neon);
+    orc_gemv(d, a, p->mant_down, p->exp_down, p->M_down, p->K_down, neon);
+    orc_add_residual(h, d, H, neon);
+    free(n); free(g); free(u); free(a); free(d);
+}
+
+/* forward_linear_layer (qwen_kernels_opt.c:938-992), the Gated-DeltaNet layer:
+ * n = rmsnorm(h, in_ln); qkv GEMV; conv1d + SiLU over the 3*heads*D channels;
+ * q, k = the first two thirds, l2-normalised; gates from n; the recurrent
+ * step; z GEMV; rmsnorm_gated; o GEMV; h += o; then forward_mlp's steps. */
+ORC_API void orc_forward_linear_layer(const OrcLinearPlan* p, float* h, int neon) {
+    const int H = kOrcHidden, NH = kOrcHeads, D = kOrcHeadDim, V = NH * D;
+    float* n = (float*)malloc(sizeof(float) * H);
+    float* qkv = (float*)malloc(sizeof(float) * p->M_qkv);
+    /* zeroed: the reference's workspace is a zero-initialised static, and its
+     * portable build's conv never writes the channels below C & ~3 */
+    float* mixed = (float*)calloc((size_t)p->M_qkv, sizeof(float));
+    float alpha[kOrcHeads], beta[kOrcHeads];
+    float* attn = (float*)malloc(sizeof(float) * V);
+    float* z = (float*)malloc(sizeof(float) * p->M_z);
+    float* gated = (float*)malloc(sizeof(float) * V);
+    float* o = (float*)malloc(sizeof(float) * p->M_o);
+    orc_rmsnorm(n, h, p->in_ln_w, H, neon);
+    orc_gemv(qkv, n, p->mant_qkv, p->exp_qkv, p->M_qkv, p->K_qkv, neon);
+    orc_conv1d_silu(mixed, qkv, p->conv_s, p->conv_w, 3 * V, neon);
+    orc_qk_l2norm(mixed, mixed + V, NH, D, neon);
+    orc_gdn_gates(alpha, beta, n, p->wa, p->wb, p->nea, p->dt, NH, H, neon);
+    orc_gdn_step(attn, p->state, mixed, mixed + V, mixed + 2 * V, alpha, beta, NH, D, neon);
+    orc_gemv(z, n, p->mant_z, p->exp_z, p->M_z, p->K_z, neon);
+    orc_rmsnorm_gated(gated, attn, z, p->norm_w, NH, D, 1e-6f, neon);
+    orc_gemv(o, gated, p->mant_o, p->exp_o, p->M_o, p->K_o, neon);
+    orc_add_residual(h, o, H, neon);
+    OrcMlpPlan m = {p->post_ln_w, p->mant_gate, p->exp_gate, p->M_gate, p->K_gate, p->mant_up, p->exp_up,
+                    p->M_up, p->K_up, p->mant_down, p->exp_down, p->M_down, p->K_down};
+    orc_forward_mlp(&m, h, neon);
+    free(n); free(qkv); free(mixed); free(attn); free(z); free(gated); free(o);
+}
+
+typedef void (*OrcFullAttnCallback)(int layer, float* h, void* ctx);
+
+/* forward_token_c (qwen_kernels_opt.c:1008-1049): h = the bf16 embedding row
+ * of token_id % 65536; 24 layers (full-attention layers: the callback, then
+ * forward_mlp; the others forward_linear_layer with the next linear plan);
+ * the final rmsnorm; the lm_head argmax over 65536 rows (h keeps the last
+ * residual stream). */
+ORC_API int orc_forward_token(int token_id, float* h, const OrcLinearPlan* lps, const OrcMlpPlan* mps,
+                              const int* is_full, const float* final_w, const uint16_t* E,
+                              OrcFullAttnCallback cb, void* ctx, int neon) {
+    const uint16_t* row = E + (size_t)(token_id % kOrcVocab) * kOrcHidden;
+    for (int i = 0; i < kOrcHidden; i++) h[i] = bf16_bits_to_f32(row[i]);
+    int li = 0;
+    for (int l = 0; l < kOrcLayers; l++) {
+        if (is_full[l]) {
+            if (cb) cb(l, h, ctx);
+            orc_forward_mlp(&mps[l], h, neon);
+        } else {
+            orc_forward_linear_layer(&lps[li++], h, neon);
+        }
+    }
+    float* n = (float*)malloc(sizeof(float) * kOrcHidden);
+    orc_rmsnorm(n, h, final_w, kOrcHidden, neon);
+    float* s = (float*)malloc(sizeof(float) * kOrcVocab);
+    if (neon)
+        orc_lm_scores_neon(s, n, E, kOrcVocab, kOrcHidden, 0);
+    else
+        orc_lm_scores_scalar(s, n, E, kOrcVocab, kOrcHidden);
+    const int id = orc_argmax(s, kOrcVocab);
+    free(n);
+    free(s);
+    return id;
+}

@@ -64,13 +64,21 @@ def lib():
             "orc_rmsnorm_scalar": [_P, _P, _P, _I, ctypes.c_float],
             "orc_add_residual": [_P, _P, _I, _I],
             "orc_swiglu": [_P, _P, _P, _I, _I],
+            "orc_conv1d_silu": [_P, _P, _P, _P, _I, _I],
+            "orc_qk_l2norm": [_P, _P, _I, _I, _I],
+            "orc_gdn_gates": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I],
+            "orc_gdn_step": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I],
+            "orc_rmsnorm_gated": [_P, _P, _P, _P, _I, _I, ctypes.c_float, _I],
+            "orc_forward_mlp": [_P, _P, _I],
+            "orc_forward_linear_layer": [_P, _P, _I],
+            "orc_forward_token": [_I, _P, _P, _P, _P, _P, _P, _P, _P, _I],
         }
         for name, args in sigs.items():
             fn = getattr(L, name)
             fn.argtypes = args
             fn.restype = _I if name in ("orc_argmax", "orc_topk", "orc_lm_head_argmax",
                                         "orc_lm_head_topk", "orc_bfp8_lm_head",
-                                        "orc_bfp8_gemv_rtl20") else None
+                                        "orc_bfp8_gemv_rtl20", "orc_forward_token") else None
         _lib = L
     return _lib
 

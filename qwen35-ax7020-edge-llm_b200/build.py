@@ -23,7 +23,7 @@ TORCH_LIB_NAME = "libqwen_b200_torch.so"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CU_SOURCES = ["bfp8_gemv.cu", "bfp8_gemm_tc.cu", "lm_head.cu", "pack.cu", "sample.cu", "tma.cu", "capi.cu",
-              "noalloc.cu"]
+              "noalloc.cu", "gdn.cu"]
 
 
 def _nvcc() -> str:

@@ -8,6 +8,7 @@
 #include "bfp8_gemm_tc.cuh"
 #include "bfp8_gemv.cuh"
 #include "common.cuh"
+#include "gdn.cuh"
 #include "lm_head.cuh"
 #include "sample.cuh"
 #include "topk.cuh"
@@ -22,6 +23,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 namespace {
@@ -45,9 +47,10 @@ namespace {
 int fail(int code, const char* what, cudaError_t e = cudaSuccess) { return qb::api_fail(code, what, e); }
 
 // ---------------------------------------------------------------- profiler
-enum { PF_GEMV = 0, PF_ARGMAX, PF_TOPK, PF_SAMPLE, PF_UPLOAD, PF_N };
-const char* kProfNames[PF_N] = {"bfp8_gemv", "lm_head_argmax", "lm_head_topk", "sample_from_topk",
-                                "weight_upload"};
+enum { PF_GEMV = 0, PF_ARGMAX, PF_TOPK, PF_SAMPLE, PF_UPLOAD, PF_MLP, PF_LINEAR, PF_TOKEN, PF_CALLBACK, PF_N };
+const char* kProfNames[PF_N] = {"bfp8_gemv",   "lm_head_argmax",       "lm_head_topk",    "sample_from_topk",
+                                "weight_upload", "forward_mlp",        "forward_linear_layer", "forward_token_c",
+                                "full_attn_callback"};
 int g_prof_on = 0;
 double g_prof_ms[PF_N];
 
@@ -264,6 +267,285 @@ int dev_state(DevState** out) {
     return QB_OK;
 }
 
+// ---------------------------------------------------------------- layer loop
+// The reference's per-token C loop (qwen_kernels_opt.c:938-1049) on the
+// device.  Plans carry host pointers; weights and fp32 vectors resolve like
+// bfp8_gemv's (a registered range, or an upload on first sight, kept), the
+// two mutable Gated-DeltaNet states through StateSlot below.
+
+constexpr int kLoopLayers = 24;      // forward_token_c's layer count (qwen_kernels_opt.c:1028)
+constexpr int kLoopVocab = 65536;    // its embedding / lm_head rows (:1020, :1046)
+constexpr int kLoopHidden = 1024;    // its hidden size (:1021, :1043)
+
+struct DevGemv {
+    const int8_t* m = nullptr;
+    const uint8_t* e = nullptr;
+    int M = 0, K = 0;
+};
+struct DevMlp {
+    const float* post_ln = nullptr;
+    DevGemv gate, up, down;
+};
+struct DevLinear {
+    const float* in_ln = nullptr;
+    DevGemv qkv, z, o;
+    const float *conv_w = nullptr, *wa = nullptr, *wb = nullptr, *nea = nullptr, *dt = nullptr, *norm_w = nullptr;
+    float* conv_s = nullptr;   // host state arrays (mutable)
+    float* state = nullptr;
+    int heads = 0;
+    DevMlp mlp;
+};
+
+// Device address of a BFP8 matrix's mantissas and exponents (contiguous SoA
+// tensors resolve as one range).
+bool resolve_gemv(const int8_t* m, const uint8_t* e, int M, int K, DevGemv* out, int* rc) {
+    if (!m || !e || M <= 0 || K <= 0 || K % 64) {
+        *rc = fail(QB_EINVAL, "layer plan: null or misshaped BFP8 matrix");
+        return false;
+    }
+    const size_t wb = (size_t)M * K, eb = (size_t)M * (K / 64);
+    if (e == reinterpret_cast<const uint8_t*>(m) + wb) {
+        const void* d = device_of(m, wb + eb, rc);
+        if (!d) return false;
+        out->m = static_cast<const int8_t*>(d);
+        out->e = static_cast<const uint8_t*>(d) + wb;
+    } else {
+        out->m = static_cast<const int8_t*>(device_of(m, wb, rc));
+        out->e = out->m ? static_cast<const uint8_t*>(device_of(e, eb, rc)) : nullptr;
+    }
+    out->M = M;
+    out->K = K;
+    return out->m && out->e;
+}
+
+const float* resolve_vec(const float* p, size_t n, int* rc) {
+    if (!p) {
+        *rc = fail(QB_EINVAL, "layer plan: null vector");
+        return nullptr;
+    }
+    return static_cast<const float*>(device_of(p, n * sizeof(float), rc));
+}
+
+// forward_mlp's shapes: hidden H = K_gate = K_up = M_down, F = M_gate = M_up =
+// K_down, both multiples of 512 and <= 6144 (the fused rmsnorm / swiglu GEMVs).
+int resolve_mlp(const float* post_ln, const int8_t* mg, const uint8_t* eg, int Mg, int Kg, const int8_t* mu,
+                const uint8_t* eu, int Mu, int Ku, const int8_t* md, const uint8_t* ed, int Md, int Kd, DevMlp* out) {
+    const int H = Kg, F = Mg;
+    if (H <= 0 || H % 512 || H > 6144 || Ku != H || Mu != F || Kd != F || Md != H || F <= 0 || F % 512 || F > 6144)
+        return fail(QB_EINVAL, "MLP plan: K_gate == K_up == M_down and M_gate == M_up == K_down, multiples of 512, "
+                               "<= 6144");
+    int rc = QB_OK;
+    if (!resolve_gemv(mg, eg, Mg, Kg, &out->gate, &rc) || !resolve_gemv(mu, eu, Mu, Ku, &out->up, &rc) ||
+        !resolve_gemv(md, ed, Md, Kd, &out->down, &rc))
+        return rc ? rc : fail(QB_EINVAL, "MLP plan: weights");
+    if (!(out->post_ln = resolve_vec(post_ln, (size_t)H, &rc))) return rc;
+    return QB_OK;
+}
+
+int resolve_mlp_plan(const MlpPlanC* p, DevMlp* out) {
+    if (!p) return fail(QB_EINVAL, "null MLP plan");
+    return resolve_mlp(p->post_ln_w, p->mant_gate, p->exp_gate, p->M_gate, p->K_gate, p->mant_up, p->exp_up, p->M_up,
+                       p->K_up, p->mant_down, p->exp_down, p->M_down, p->K_down, out);
+}
+
+// forward_linear_layer's shapes (the reference hard-codes 1024 / 6144 / 16 x
+// 128): hidden H = K_qkv = K_z = M_o; value width V = M_z = K_o = heads * 128;
+// M_qkv = 3 V (q | k | v); the MLP as above.
+int resolve_linear_plan(const LinearLayerPlanC* p, DevLinear* out) {
+    if (!p) return fail(QB_EINVAL, "null linear-layer plan");
+    const int H = p->K_qkv, V = p->M_z;
+    if (V <= 0 || V % qb::kGdnHeadDim || p->M_qkv != 3 * V || p->K_z != H || p->K_o != V || p->M_o != H ||
+        p->K_gate != H)
+        return fail(QB_EINVAL, "linear-layer plan: K_qkv == K_z == M_o == K_gate, M_qkv == 3 M_z, K_o == M_z, "
+                               "M_z a multiple of 128");
+    if (int rc = resolve_mlp(p->post_ln_w, p->mant_gate, p->exp_gate, p->M_gate, p->K_gate, p->mant_up, p->exp_up,
+                             p->M_up, p->K_up, p->mant_down, p->exp_down, p->M_down, p->K_down, &out->mlp))
+        return rc;
+    int rc = QB_OK;
+    const int heads = V / qb::kGdnHeadDim;
+    if (!resolve_gemv(p->mant_qkv, p->exp_qkv, p->M_qkv, p->K_qkv, &out->qkv, &rc) ||
+        !resolve_gemv(p->mant_z, p->exp_z, p->M_z, p->K_z, &out->z, &rc) ||
+        !resolve_gemv(p->mant_o, p->exp_o, p->M_o, p->K_o, &out->o, &rc))
+        return rc ? rc : fail(QB_EINVAL, "linear-layer plan: weights");
+    if (!(out->in_ln = resolve_vec(p->in_ln_w, (size_t)H, &rc)) ||
+        !(out->conv_w = resolve_vec(p->conv_w, 4 * (size_t)p->M_qkv, &rc)) ||
+        !(out->wa = resolve_vec(p->wa, (size_t)heads * H, &rc)) ||
+        !(out->wb = resolve_vec(p->wb, (size_t)heads * H, &rc)) ||
+        !(out->nea = resolve_vec(p->nea, (size_t)heads, &rc)) || !(out->dt = resolve_vec(p->dt, (size_t)heads, &rc)) ||
+        !(out->norm_w = resolve_vec(p->norm_w, (size_t)qb::kGdnHeadDim, &rc)))
+        return rc;
+    if (!p->conv_s || !p->state) return fail(QB_EINVAL, "linear-layer plan: null conv_s or state");
+    out->conv_s = p->conv_s;
+    out->state = p->state;
+    out->heads = heads;
+    return QB_OK;
+}
+
+// Device copies of the engine's mutable Gated-DeltaNet state arrays, keyed
+// by host address.  Mirror mode (the default, the reference's contract): the
+// host array is copied in before every layer call and back after it.
+// Resident mode: copied in once, then the device copy is the state until
+// qwen_b200_gdn_state_sync() copies it back or _drop() forgets it.
+struct StateSlot {
+    float* dev = nullptr;
+    size_t n = 0;
+};
+std::unordered_map<const float*, StateSlot> g_state_slots;
+bool g_state_resident = false;
+
+float* state_slot(float* host, size_t n, bool* fresh, int* rc) {
+    StateSlot& s = g_state_slots[host];
+    *fresh = false;
+    if (s.dev && s.n != n) {   // a different-sized array at the same address: start over
+        cudaFree(s.dev);
+        s.dev = nullptr;
+    }
+    if (!s.dev) {
+        cudaError_t e = cudaMalloc(&s.dev, n * sizeof(float));
+        if (e != cudaSuccess) {
+            s.dev = nullptr;
+            *rc = fail(QB_ENOMEM, "state alloc", e);
+            return nullptr;
+        }
+        s.n = n;
+        *fresh = true;
+    }
+    return s.dev;
+}
+
+// Bring a layer's states onto the device (per the mode); dev_conv / dev_state
+// receive the device copies.
+int states_in(const DevLinear& w, float** dev_conv, float** dev_state, cudaStream_t s) {
+    int rc = QB_OK;
+    const size_t nc = 3 * (size_t)w.qkv.M, ns = (size_t)w.heads * qb::kGdnHeadDim * qb::kGdnHeadDim;
+    bool fc = false, fs = false;
+    if (!(*dev_conv = state_slot(w.conv_s, nc, &fc, &rc)) || !(*dev_state = state_slot(w.state, ns, &fs, &rc)))
+        return rc;
+    cudaError_t e = cudaSuccess;
+    if (!g_state_resident || fc) e = cudaMemcpyAsync(*dev_conv, w.conv_s, nc * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess && (!g_state_resident || fs))
+        e = cudaMemcpyAsync(*dev_state, w.state, ns * 4, cudaMemcpyHostToDevice, s);
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "state copy in", e);
+}
+int states_out(const DevLinear& w, const float* dev_conv, const float* dev_state, cudaStream_t s) {
+    if (g_state_resident) return QB_OK;
+    const size_t nc = 3 * (size_t)w.qkv.M, ns = (size_t)w.heads * qb::kGdnHeadDim * qb::kGdnHeadDim;
+    cudaError_t e = cudaMemcpyAsync(w.conv_s, dev_conv, nc * 4, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(w.state, dev_state, ns * 4, cudaMemcpyDeviceToHost, s);
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "state copy out", e);
+}
+
+// Work buffers of the device layer loop (the entry points are serialised).
+struct LoopBufs {
+    float *h = nullptr, *h2 = nullptr, *qkv = nullptr, *z = nullptr, *gated = nullptr, *o = nullptr,
+          *gate = nullptr, *up = nullptr, *down = nullptr, *norm = nullptr;
+    int* res = nullptr;
+    void* pin = nullptr;   // pinned staging of h and the token id
+    size_t pin_cap = 0;
+    void* block = nullptr;
+    size_t cap = 0;
+};
+LoopBufs g_loop;
+
+// Sized for hidden H, value width V (3 V qkv channels) and MLP width F.
+int loop_bufs(int H, int V, int F) {
+    auto al = [](size_t n) { return (n * sizeof(float) + 255) & ~size_t(255); };
+    const size_t need = 4 * al(H) + al(3 * (size_t)V) + 2 * al(V) + al(H) + 2 * al(F) + 256;
+    if (int rc = grow_dev(&g_loop.block, &g_loop.cap, need)) return rc;
+    if (int rc = grow_pinned(&g_loop.pin, &g_loop.pin_cap, (size_t)H * 4 + 64)) return rc;
+    unsigned char* b = static_cast<unsigned char*>(g_loop.block);
+    auto take = [&](size_t n) {
+        float* p = reinterpret_cast<float*>(b);
+        b += al(n);
+        return p;
+    };
+    g_loop.h = take(H);
+    g_loop.h2 = take(H);
+    g_loop.o = take(H);
+    g_loop.down = take(H);
+    g_loop.qkv = take(3 * (size_t)V);
+    g_loop.z = take(V);
+    g_loop.gated = take(V);
+    g_loop.norm = take(H);
+    g_loop.gate = take(F);
+    g_loop.up = take(F);
+    g_loop.res = reinterpret_cast<int*>(b);
+    return QB_OK;
+}
+
+qb::GemvDesc gemv_desc(const DevGemv& g, const float* x, float* y) {
+    qb::GemvDesc d{};
+    d.mant = g.m;
+    d.exps = g.e;
+    d.x = x;
+    d.y = y;
+    d.M = g.M;
+    d.K = g.K;
+    return d;
+}
+
+// forward_mlp's steps on the device: h += down(swiglu(gate(n), up(n))),
+// n = rmsnorm(h) -- rmsnorm fused in front of gate and of up, swiglu in front
+// of down, then the residual add (four launches).  With `res`, the layer's
+// pending residual h + res is formed in front of gate (h_out = h + res) and
+// the MLP runs on h_out; h_out then holds the result.
+cudaError_t mlp_launch(const DevMlp& w, float* h, const float* res, float* h_out, DevState* st, cudaStream_t s) {
+    const int H = w.gate.K;
+    cudaError_t e = res ? qb::launch_rmsnorm_gemv(gemv_desc(w.gate, h, g_loop.gate), w.post_ln, 1e-6f, st->act,
+                                                  st->err, s, res, h_out)
+                        : qb::launch_rmsnorm_gemv(gemv_desc(w.gate, h, g_loop.gate), w.post_ln, 1e-6f, st->act,
+                                                  st->err, s);
+    float* hh = res ? h_out : h;
+    if (e == cudaSuccess)
+        e = qb::launch_rmsnorm_gemv(gemv_desc(w.up, hh, g_loop.up), w.post_ln, 1e-6f, st->act, st->err, s);
+    if (e == cudaSuccess)
+        e = qb::launch_swiglu_gemv(gemv_desc(w.down, g_loop.gate, g_loop.down), g_loop.up, st->act, st->err, s);
+    if (e == cudaSuccess) e = qb::launch_add_residual(hh, g_loop.down, H, s);
+    return e;
+}
+
+// forward_linear_layer's steps on the device (eight launches): qkv and z
+// projections of rmsnorm(h) (fused), the Gated-DeltaNet kernel, the out
+// projection, then the MLP with h + o formed in front of its gate
+// projection.  The result lands in g_loop.h2.
+cudaError_t linear_launch(const DevLinear& w, float* h, float* dev_conv, float* dev_state, DevState* st,
+                          cudaStream_t s) {
+    cudaError_t e =
+        qb::launch_rmsnorm_gemv(gemv_desc(w.qkv, h, g_loop.qkv), w.in_ln, 1e-6f, st->act, st->err, s);
+    if (e == cudaSuccess)
+        e = qb::launch_rmsnorm_gemv(gemv_desc(w.z, h, g_loop.z), w.in_ln, 1e-6f, st->act, st->err, s);
+    if (e == cudaSuccess) {
+        qb::GdnArgs a{};
+        a.qkv = g_loop.qkv;
+        a.z = g_loop.z;
+        a.h = h;
+        a.in_ln_w = w.in_ln;
+        a.conv_w = w.conv_w;
+        a.conv_s = dev_conv;
+        a.wa = w.wa;
+        a.wb = w.wb;
+        a.nea = w.nea;
+        a.dt = w.dt;
+        a.state = dev_state;
+        a.norm_w = w.norm_w;
+        a.out = g_loop.gated;
+        a.heads = w.heads;
+        a.hidden = w.qkv.K;
+        e = qb::launch_gdn_layer(a, s);
+    }
+    if (e == cudaSuccess) e = qb::launch_gemv(gemv_desc(w.o, g_loop.gated, g_loop.o), st->act, st->err, s);
+    if (e == cudaSuccess) e = mlp_launch(w.mlp, h, g_loop.o, g_loop.h2, st, s);
+    return e;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(e == cudaErrorInvalidValue ? QB_EINVAL : QB_ECUDA, what, e);
+}
+
+// Prefix the pending error message with the failing entry point's name.
+void name_error(const char* entry) {
+    if (g_err.compare(0, strlen(entry), entry) != 0) g_err = std::string(entry) + ": " + g_err;
+}
 
 }  // namespace
 
@@ -366,87 +648,174 @@ void bfp8_gemv(float* y, const float* x, const int8_t* mant, const uint8_t* exps
     memcpy(y, g_ctx.h_out, 4 * (size_t)M);
 }
 
-static float* g_mlp_buf = nullptr;   // h | down | gate | up of the forward_mlp drop-in
-static size_t g_mlp_cap = 0;
-
 void forward_mlp(const MlpPlanC* p, float* h) {
-    ProfScope ps(PF_GEMV);
+    ProfScope ps(PF_MLP);
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!p || !h || !p->post_ln_w) {
-        fail(QB_EINVAL, "forward_mlp: null plan, h or norm weights");
+    if (!h) {
+        fail(QB_EINVAL, "forward_mlp: null h");
         return;
     }
-    const int H = p->K_gate, F = p->M_gate;
-    if (H <= 0 || H % 512 || H > 6144 || p->K_up != H || p->M_up != F || p->K_down != F || p->M_down != H ||
-        F <= 0 || F % 512 || F > 6144) {
-        fail(QB_EINVAL, "forward_mlp: K_gate == K_up == M_down <= 6144 and M_gate == M_up == K_down <= 6144, "
-                        "multiples of 512");
-        return;
-    }
-    if (ensure_ctx()) return;
-    int rc = QB_OK;
-    auto dev_weights = [&](const int8_t* m, const uint8_t* e, int M, int K, const int8_t** dm, const uint8_t** de) {
-        const size_t wb = (size_t)M * K, eb = (size_t)M * (K / 64);
-        if (e == reinterpret_cast<const uint8_t*>(m) + wb) {
-            const void* d = device_of(m, wb + eb, &rc);
-            *dm = static_cast<const int8_t*>(d);
-            *de = d ? static_cast<const uint8_t*>(d) + wb : nullptr;
-        } else {
-            *dm = static_cast<const int8_t*>(device_of(m, wb, &rc));
-            *de = *dm ? static_cast<const uint8_t*>(device_of(e, eb, &rc)) : nullptr;
-        }
-        return *dm && *de;
-    };
-    const int8_t *gm, *um, *dm;
-    const uint8_t *ge, *ue, *de;
-    if (!p->mant_gate || !p->exp_gate || !p->mant_up || !p->exp_up || !p->mant_down || !p->exp_down) {
-        fail(QB_EINVAL, "forward_mlp: null weight pointer");
-        return;
-    }
-    if (!dev_weights(p->mant_gate, p->exp_gate, F, H, &gm, &ge) || !dev_weights(p->mant_up, p->exp_up, F, H, &um, &ue) ||
-        !dev_weights(p->mant_down, p->exp_down, H, F, &dm, &de))
-        return;
-    const float* dln = static_cast<const float*>(device_of(p->post_ln_w, 4 * (size_t)H, &rc));
-    if (!dln) return;
-    // h | down | gate | up, each 256-byte aligned
-    const size_t hb = ((size_t)H * 4 + 255) & ~size_t(255), fb = ((size_t)F * 4 + 255) & ~size_t(255);
-    if (grow_dev(reinterpret_cast<void**>(&g_mlp_buf), &g_mlp_cap, 2 * hb + 2 * fb) ||
-        grow_pinned(&g_ctx.h_in, &g_ctx.h_in_cap, 4 * (size_t)H))
-        return;
-    unsigned char* base = reinterpret_cast<unsigned char*>(g_mlp_buf);
-    float* dh = reinterpret_cast<float*>(base);
-    float* ddown = reinterpret_cast<float*>(base + hb);
-    float* dgate = reinterpret_cast<float*>(base + 2 * hb);
-    float* dup = reinterpret_cast<float*>(base + 2 * hb + fb);
-    DevState* dst = nullptr;
-    if (dev_state(&dst)) return;
+    DevMlp w;
+    DevState* st = nullptr;
+    if (ensure_ctx() || resolve_mlp_plan(p, &w) || dev_state(&st) || loop_bufs(w.gate.K, qb::kGdnHeadDim, w.gate.M))
+        return name_error("forward_mlp");
+    const size_t hb = 4 * (size_t)w.gate.K;
     cudaStream_t s = g_ctx.stream;
-    memcpy(g_ctx.h_in, h, 4 * (size_t)H);
-    cudaError_t e = cudaMemcpyAsync(dh, g_ctx.h_in, 4 * (size_t)H, cudaMemcpyHostToDevice, s);
-    auto desc = [](const int8_t* m, const uint8_t* ex, const float* x, float* y, int M, int K) {
-        qb::GemvDesc d{};
-        d.mant = m;
-        d.exps = ex;
-        d.x = x;
-        d.y = y;
-        d.M = M;
-        d.K = K;
-        return d;
-    };
-    // rmsnorm in front of gate and of up, swiglu in front of down, then h += down
-    if (e == cudaSuccess)
-        e = qb::launch_rmsnorm_gemv(desc(gm, ge, dh, dgate, F, H), dln, 1e-6f, dst->act, dst->err, s);
-    if (e == cudaSuccess)
-        e = qb::launch_rmsnorm_gemv(desc(um, ue, dh, dup, F, H), dln, 1e-6f, dst->act, dst->err, s);
-    if (e == cudaSuccess) e = qb::launch_swiglu_gemv(desc(dm, de, dgate, ddown, H, F), dup, dst->act, dst->err, s);
-    if (e == cudaSuccess) e = qb::launch_add_residual(dh, ddown, H, s);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(g_ctx.h_in, dh, 4 * (size_t)H, cudaMemcpyDeviceToHost, s);
+    memcpy(g_loop.pin, h, hb);
+    cudaError_t e = cudaMemcpyAsync(g_loop.h, g_loop.pin, hb, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = mlp_launch(w, g_loop.h, nullptr, nullptr, st, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(g_loop.pin, g_loop.h, hb, cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) {
-        fail(e == cudaErrorInvalidValue ? QB_EINVAL : QB_ECUDA, "forward_mlp", e);
+        cuda_fail(e, "forward_mlp");
         return;
     }
-    memcpy(h, g_ctx.h_in, 4 * (size_t)H);
+    memcpy(h, g_loop.pin, hb);
+}
+
+void forward_linear_layer(const LinearLayerPlanC* p, float* h) {
+    ProfScope ps(PF_LINEAR);
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!h) {
+        fail(QB_EINVAL, "forward_linear_layer: null h");
+        return;
+    }
+    DevLinear w;
+    DevState* st = nullptr;
+    if (ensure_ctx() || resolve_linear_plan(p, &w) || dev_state(&st) || loop_bufs(w.qkv.K, w.z.M, w.mlp.gate.M))
+        return name_error("forward_linear_layer");
+    const size_t hb = 4 * (size_t)w.qkv.K;
+    cudaStream_t s = g_ctx.stream;
+    float *dconv = nullptr, *dstate = nullptr;
+    if (states_in(w, &dconv, &dstate, s)) return name_error("forward_linear_layer");
+    memcpy(g_loop.pin, h, hb);
+    cudaError_t e = cudaMemcpyAsync(g_loop.h, g_loop.pin, hb, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = linear_launch(w, g_loop.h, dconv, dstate, st, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(g_loop.pin, g_loop.h2, hb, cudaMemcpyDeviceToHost, s);
+    if (e != cudaSuccess) {
+        cuda_fail(e, "forward_linear_layer");
+        return;
+    }
+    if (states_out(w, dconv, dstate, s)) return name_error("forward_linear_layer");
+    if ((e = cudaStreamSynchronize(s)) != cudaSuccess) {
+        cuda_fail(e, "forward_linear_layer");
+        return;
+    }
+    memcpy(h, g_loop.pin, hb);
+}
+
+int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linear_plans, const MlpPlanC* mlp_plans,
+                    const int* layer_is_full, const float* final_norm_w, const uint16_t* embed_table,
+                    QbFullAttnCallback full_attn_cb, void* py_context) {
+    ProfScope ps(PF_TOKEN);
+    std::unique_lock<std::mutex> lk(g_mu);
+    if (!h || !linear_plans || !mlp_plans || !layer_is_full || !final_norm_w || !embed_table || token_id < 0)
+        return fail(QB_EINVAL, "forward_token_c: null pointer or negative token id"), -1;
+    if (ensure_ctx()) return name_error("forward_token_c"), -1;
+    // resolve every layer first: a bad plan changes nothing
+    std::vector<DevLinear> lin;
+    std::vector<DevMlp> mlp(kLoopLayers);
+    int n_lin = 0, F = 0, V = qb::kGdnHeadDim;
+    for (int l = 0; l < kLoopLayers; l++) {
+        if (layer_is_full[l]) {
+            if (resolve_mlp_plan(&mlp_plans[l], &mlp[l])) return name_error("forward_token_c"), -1;
+            if (mlp[l].gate.K != kLoopHidden) return fail(QB_EINVAL, "forward_token_c: hidden must be 1024"), -1;
+            F = std::max(F, mlp[l].gate.M);
+        } else {
+            lin.emplace_back();
+            if (resolve_linear_plan(&linear_plans[n_lin++], &lin.back())) return name_error("forward_token_c"), -1;
+            if (lin.back().qkv.K != kLoopHidden) return fail(QB_EINVAL, "forward_token_c: hidden must be 1024"), -1;
+            F = std::max(F, lin.back().mlp.gate.M);
+            V = std::max(V, lin.back().z.M);
+        }
+    }
+    int rc = QB_OK;
+    const uint16_t* dE =
+        static_cast<const uint16_t*>(device_of(embed_table, (size_t)kLoopVocab * kLoopHidden * 2, &rc));
+    const float* dfin = resolve_vec(final_norm_w, kLoopHidden, &rc);
+    DevState* st = nullptr;
+    if (!dE || !dfin || dev_state(&st) || loop_bufs(kLoopHidden, V, F)) return name_error("forward_token_c"), -1;
+    cudaStream_t s = g_ctx.stream;
+    const size_t hb = 4 * (size_t)kLoopHidden;
+    std::vector<float*> dconv(lin.size()), dstate(lin.size());
+    for (size_t i = 0; i < lin.size(); i++)
+        if (states_in(lin[i], &dconv[i], &dstate[i], s)) return name_error("forward_token_c"), -1;
+    // 1. the bf16 embedding row of token_id % 65536
+    cudaError_t e = qb::launch_embed_row(g_loop.h, dE, token_id % kLoopVocab, kLoopHidden, s);
+    // 2. the layers: full-attention ones run the caller's callback on the host
+    // h (the lock released: it calls back into bfp8_gemv), then the MLP
+    size_t li = 0;
+    for (int l = 0; l < kLoopLayers && e == cudaSuccess; l++) {
+        if (layer_is_full[l]) {
+            if (full_attn_cb) {
+                e = cudaMemcpyAsync(g_loop.pin, g_loop.h, hb, cudaMemcpyDeviceToHost, s);
+                if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+                if (e != cudaSuccess) break;
+                memcpy(h, g_loop.pin, hb);
+                lk.unlock();
+                {
+                    ProfScope pc(PF_CALLBACK);
+                    full_attn_cb(l, h, py_context);
+                }
+                lk.lock();
+                memcpy(g_loop.pin, h, hb);
+                e = cudaMemcpyAsync(g_loop.h, g_loop.pin, hb, cudaMemcpyHostToDevice, s);
+                if (e != cudaSuccess) break;
+            }
+            e = mlp_launch(mlp[l], g_loop.h, nullptr, nullptr, st, s);
+        } else {
+            e = linear_launch(lin[li], g_loop.h, dconv[li], dstate[li], st, s);
+            std::swap(g_loop.h, g_loop.h2);   // the layer's output is the next layer's h
+            li++;
+        }
+    }
+    // 3. final rmsnorm, 4. lm_head argmax over the 65536 embedding rows
+    if (e == cudaSuccess) e = qb::launch_rmsnorm(g_loop.norm, g_loop.h, dfin, kLoopHidden, 1e-6f, s);
+    if (e == cudaSuccess)
+        e = qb::launch_lm_head_bf16(g_loop.norm, dE, kLoopVocab, kLoopHidden, 0, 0, g_ctx.scratch, st->err, nullptr,
+                                    g_loop.res, nullptr, nullptr, g_loop.res + 1, s);
+    int* pid = reinterpret_cast<int*>(static_cast<unsigned char*>(g_loop.pin) + hb);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(g_loop.pin, g_loop.h, hb, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(pid, g_loop.res, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e != cudaSuccess) return cuda_fail(e, "forward_token_c"), -1;
+    for (size_t i = 0; i < lin.size(); i++)
+        if (states_out(lin[i], dconv[i], dstate[i], s)) return name_error("forward_token_c"), -1;
+    if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return cuda_fail(e, "forward_token_c"), -1;
+    memcpy(h, g_loop.pin, hb);
+    return *pid;
+}
+
+int qwen_b200_gdn_state_mode(int resident) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_state_resident && !resident) {   // leaving resident mode: the host arrays catch up first
+        for (auto& kv : g_state_slots) {
+            cudaError_t e = cudaMemcpy(const_cast<float*>(kv.first), kv.second.dev, kv.second.n * 4,
+                                       cudaMemcpyDeviceToHost);
+            if (e != cudaSuccess) return fail(QB_ECUDA, "state sync", e);
+        }
+    }
+    if (!g_state_resident && resident) {   // entering resident mode: start from the host arrays
+        for (auto& kv : g_state_slots) cudaFree(kv.second.dev);
+        g_state_slots.clear();
+    }
+    g_state_resident = resident != 0;
+    return QB_OK;
+}
+
+int qwen_b200_gdn_state_sync(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (auto& kv : g_state_slots) {
+        cudaError_t e =
+            cudaMemcpy(const_cast<float*>(kv.first), kv.second.dev, kv.second.n * 4, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) return fail(QB_ECUDA, "state sync", e);
+    }
+    return QB_OK;
+}
+
+void qwen_b200_gdn_state_drop(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (auto& kv : g_state_slots) cudaFree(kv.second.dev);
+    g_state_slots.clear();
 }
 
 static int lm_bf16_host(const float* h, const uint16_t* E, int vocab, int hidden, int k, int with_tail,

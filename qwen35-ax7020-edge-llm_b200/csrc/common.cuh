@@ -50,6 +50,32 @@ __device__ __forceinline__ float i2f_rn(int v) {
     return d;
 }
 
+// exp_neon (qwen_kernels_opt.c:332-351), one lane, with the vector unit's
+// flush-to-zero on every step: x clamped to [-87, 88] (a NaN stays NaN);
+// fx = x * RN(1/ln 2); n = fx rounded to an integer by adding and
+// subtracting 1.5 * 2^23; f = fx - n; p = the degree-6 Taylor polynomial of
+// 2^f (coefficients RN((ln 2)^k / k!)) by Horner steps that round the product
+// before the add (VMLA is not fused); the result p * 2^n with 2^n built from
+// exponent bits (the conversion rounds toward zero and takes a NaN to 0).
+__device__ __forceinline__ float exp_neon_lane(float x) {
+    constexpr float kLog2e = 0x1.715476p+0f;       // RN(1/ln 2)
+    constexpr float kRoundMagic = 0x1.8p+23f;      // 1.5 * 2^23
+    x = mul_ftz(x, 1.0f);                          // VMAX flushes a subnormal operand
+    x = (x != x) ? x : (x > -87.0f ? x : -87.0f);
+    x = (x != x) ? x : (x < 88.0f ? x : 88.0f);
+    const float fx = mul_ftz(x, kLog2e);
+    const float n = sub_ftz(add_ftz(fx, kRoundMagic), kRoundMagic);
+    const float f = sub_ftz(fx, n);
+    float p = 0x1.430912p-13f;                     // k = 6
+    p = add_ftz(0x1.5d87fep-10f, mul_ftz(p, f));   // k = 5
+    p = add_ftz(0x1.3b2ab6p-7f, mul_ftz(p, f));    // k = 4
+    p = add_ftz(0x1.c6b08ep-5f, mul_ftz(p, f));    // k = 3
+    p = add_ftz(0x1.ebfbe0p-3f, mul_ftz(p, f));    // k = 2
+    p = add_ftz(0x1.62e430p-1f, mul_ftz(p, f));    // k = 1
+    p = add_ftz(1.0f, mul_ftz(p, f));              // k = 0
+    return mul_ftz(p, __int_as_float((__float2int_rz(n) + 127) << 23));
+}
+
 // 2^(e-134) as the vector unit sees it: exact power of two for e >= 8, a
 // flushed zero for the subnormal range e < 8.
 __device__ __forceinline__ float exp_scale_ftz(uint32_t e) {

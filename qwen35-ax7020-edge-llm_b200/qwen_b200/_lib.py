@@ -18,6 +18,10 @@ _I = ctypes.c_int
 _F = ctypes.c_float
 
 # name -> (restype, argtypes); mirrors include/qwen_b200.h
+# void(int layer_idx, float* h, void* py_context): forward_token_c's
+# full-attention callback, the engine's CALLBACK_TYPE (qwen_real_engine.py:982)
+FULL_ATTN_CALLBACK = ctypes.CFUNCTYPE(None, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p)
+
 SIGNATURES = {
     "init_kernels": (None, []),
     "bfp8_gemv": (None, [_P, _P, _P, _P, _I, _I]),
@@ -25,6 +29,11 @@ SIGNATURES = {
     "lm_head_topk": (_I, [_P, _P, _I, _I, _I, _P, _P]),
     "sample_from_topk": (_I, [_P, _P, _I, _F, _I, _F, _P]),
     "forward_mlp": (None, [_P, _P]),
+    "forward_linear_layer": (None, [_P, _P]),
+    "forward_token_c": (_I, [_I, _P, _P, _P, _P, _P, _P, FULL_ATTN_CALLBACK, _P]),
+    "qwen_b200_gdn_state_mode": (_I, [_I]),
+    "qwen_b200_gdn_state_sync": (_I, []),
+    "qwen_b200_gdn_state_drop": (None, []),
     "qwen_prof_enable": (None, [_I]),
     "qwen_prof_reset": (None, []),
     "qwen_prof_count": (_I, []),
