@@ -2,7 +2,7 @@
 """Benchmark of the BFP8 GEMV / lm_head decode hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload stack|gemv|lm_bf16|lm_bfp8|sharded|batched|rtl20] [--batch B]
+                    [--workload stack|gemv|lm_bf16|lm_bfp8|sharded|batched|rtl20|token] [--batch B]
                     [--headline-only] [--no-sharded] [--no-cpu-baseline] [--no-e2e]
 
 Default workload (the BASELINE metric's configuration): the full per-token
@@ -38,6 +38,7 @@ same packed bytes with every host thread, rank 0 only.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 import os
@@ -64,7 +65,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["stack", "gemv", "lm_bf16", "lm_bfp8", "sharded", "batched", "rtl20"],
+    ap.add_argument("--workload", choices=["stack", "gemv", "lm_bf16", "lm_bfp8", "sharded", "batched", "rtl20",
+                                           "token"],
                     default="stack")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per step: --workload batched (default 256) or sharded (default 1)")
@@ -330,6 +332,8 @@ def run_b200(args):
                                 args.steps, args.warmup))
     elif args.workload == "rtl20":
         line.update(run_rtl20(args, torch, dev, barrier, world, hbm_peak, peak_kind))
+    elif args.workload == "token":
+        line.update(run_token(args, torch, dev, world, rank))
     else:
         line.update(run_lm_head(args, torch, dev, barrier, world, hbm_peak, peak_kind, args.workload, args.steps,
                                 args.warmup))
@@ -666,6 +670,100 @@ def run_chain(torch, dev, barrier, hbm_peak, peak_kind, steps, warm):
                          "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind,
                          "kernel": "gemv_split_kernel (150 launches)"},
             "gpu_launches_per_token": len(shapes), "clocks": clocks}
+
+
+# ------------------------------------------------------------------ token loop
+TOKEN_METRIC = "forward_token_c ms/token: Qwen3.5-0.8B shape, 24 layers + lm_head argmax, drop-in C ABI"
+TOKEN_LAUNCHES = 18 * 8 + 6 * 4 + 3   # per token: linear layers, full-attention MLPs, embed / rmsnorm / lm_head
+
+
+def _token_loop(fwd, M, lps, mps, cb, h, first, n):
+    """n autoregressive tokens through a forward_token_c-shaped function
+    (each returned id is the next input); returns the last id."""
+    tok = first
+    for _ in range(n):
+        tok = fwd(tok, h.ctypes.data, ctypes.byref(lps), ctypes.byref(mps), M.is_full.ctypes.data,
+                  M.final_ln.ctypes.data, M.embed.ctypes.data, cb, None)
+        if tok < 0:
+            raise RuntimeError("forward_token_c failed")
+    return tok
+
+
+def run_token(args, torch, dev, world, rank):
+    """The reference's per-token C loop as the engine calls it
+    (qwen_real_engine.py:1262-1272): forward_token_c with host h, host plans,
+    the engine's mutable states and a full-attention callback (a stand-in:
+    attention is not on this library's path), timed by wall clock per token.
+    Both state modes: mirror (the states copied in and out every token, the
+    reference's contract) and resident (the states stay on the device)."""
+    import numpy as np
+
+    from qwen_b200 import _lib, plans
+
+    L = _lib.load()
+    M = plans.TokenModel(seed=0)
+    cb = plans.attention_stand_in()
+    out = {}
+    for mode, name in ((0, "mirror"), (1, "resident")):
+        assert L.qwen_b200_gdn_state_mode(mode) == 0
+        st = M.fresh_states()
+        lps, mps = M.plans(st)
+        h = np.zeros(plans.HIDDEN, np.float32)
+        tok = _token_loop(L.forward_token_c, M, lps, mps, cb, h, 1, max(args.warmup, 3))
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        _token_loop(L.forward_token_c, M, lps, mps, cb, h, tok, args.steps)
+        dt = (time.perf_counter() - t0) / args.steps
+        if mode == 1:
+            L.qwen_b200_gdn_state_sync()
+            L.qwen_b200_gdn_state_drop()
+        out[name] = dt
+    L.qwen_b200_gdn_state_mode(0)
+    L.qwen_b200_reset_weights()
+    state_bytes = M.n_linear * (3 * 3 * plans.V + plans.HEADS * plans.HEAD_DIM ** 2) * 4
+    return {"metric": TOKEN_METRIC, "unit": "ms/token", "higher_is_better": False, "scaling": "replicas",
+            "value": round(out["mirror"] * 1e3, 3), "ms_per_step": round(out["mirror"] * 1e3, 3),
+            "dtype": "int16xint8->fp32 GEMVs, fp32 layer glue (NEON-build order)",
+            "data": "synthetic: plans.TokenModel(seed=0) -- random BFP8 weights (one linear-layer set, one MLP set "
+                    "shared by the layers), per-layer states, random bf16 embedding table",
+            "config": {"workload": "forward_token_c, 18 Gated-DeltaNet + 6 full-attention layers (attention: a "
+                                   "host stand-in callback), final rmsnorm, lm_head argmax over 65536 rows",
+                       "state_mode": "mirror (conv and recurrent states copied in and out every token)",
+                       "resident_ms_per_token": round(out["resident"] * 1e3, 3),
+                       "launches_per_token": TOKEN_LAUNCHES,
+                       "host_round_trips_per_token": 6},
+            "e2e": {"value": round(out["mirror"] * 1e3, 3), "unit": "ms/token",
+                    "h2d_bytes_per_step": 4 * plans.HIDDEN * 6 + state_bytes,
+                    "d2h_bytes_per_step": 4 * plans.HIDDEN * 7 + 4 + state_bytes},
+            "gpu_launches": TOKEN_LAUNCHES * args.steps}
+
+
+def token_reference_sample(budget=10.0, steps=None, warmup=1):
+    """The reference's own forward_token_c (oracle/_ref, its C file compiled
+    here; portable build, OpenMP over every host thread) on the same
+    synthetic model: (ms per token, tokens timed, threads)."""
+    import numpy as np
+
+    from qwen_b200 import plans
+
+    cores = _omp_threads(os.cpu_count())
+    lib = ctypes.CDLL(os.path.join(REPO, "oracle", "_ref", "libref_kernels.so"))
+    P, I = ctypes.c_void_p, ctypes.c_int
+    lib.forward_token_c.argtypes = [I, P, P, P, P, P, P, plans.CALLBACK, P]
+    lib.forward_token_c.restype = I
+    lib.init_kernels()
+    cores = _omp_threads(cores)
+    M = plans.TokenModel(seed=0)
+    cb = plans.attention_stand_in()
+    states = M.fresh_states()
+    lps, mps = M.plans(states)
+    h = np.zeros(plans.HIDDEN, np.float32)
+    tok = _token_loop(lib.forward_token_c, M, lps, mps, cb, h, 1, warmup)
+    n, t0 = 0, time.perf_counter()
+    while (steps is None and (n < 1 or time.perf_counter() - t0 < budget)) or (steps is not None and n < steps):
+        tok = _token_loop(lib.forward_token_c, M, lps, mps, cb, h, tok, 1)
+        n += 1
+    return (time.perf_counter() - t0) / n * 1e3, n, cores
 
 
 def run_abi(torch, dev):
@@ -1122,6 +1220,16 @@ def cpu_runner(kind, workload, data_path=""):
 def cpu_baseline(workload, batch=1, data_path=None):
     """Bounded samples of the CPU rows on this host, each in a child
     process (OpenMP starts with the thread count the row asks for)."""
+    if workload == "token":
+        env = dict(os.environ, OMP_NUM_THREADS=str(os.cpu_count()))
+        cmd = [sys.executable, os.path.abspath(__file__), "--impl", "reference", "--cpu-sample", "--workload", "token"]
+        try:
+            out = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+            row = json.loads(out.stdout.strip().splitlines()[-1])
+        except Exception as e:
+            row = {"error": str(e)[:200]}
+        row["host_cpu"] = _cpu_model()
+        return row
     if workload not in ("stack", "gemv", "batched"):
         return None
     rows = []
@@ -1159,6 +1267,27 @@ def run_reference(args):
     if args.workload == "rtl20":
         print(json.dumps({"impl": "reference", "unavailable": "the RTL dequant mode exists only as FPGA fabric "
                           "(gemv_core.v); the reference has no CPU implementation of it"}))
+        return
+    if args.workload == "token":
+        if args.cpu_sample:
+            ms, n, cores = token_reference_sample(budget=10.0)
+            print(json.dumps({"value": round(ms, 3), "unit": "ms/token", "cores": cores, "kind": "reference",
+                              "sample": f"{n} autoregressive tokens after 1 warm-up token: the reference's "
+                                        "forward_token_c (portable build, OpenMP) on plans.TokenModel(seed=0)"}))
+            return
+        ms, n, cores = token_reference_sample(steps=args.steps, warmup=args.warmup)
+        print(json.dumps({
+            "impl": "reference", "metric": TOKEN_METRIC, "value": round(ms, 3), "unit": "ms/token",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": False, "scaling": "replicas", "vs_baseline": None,
+            "dtype": "fp32 (reference portable build)",
+            "data": "synthetic: plans.TokenModel(seed=0), the B200 arm's model",
+            "config": {"workload": "the reference's forward_token_c, 24 layers + lm_head argmax, stand-in "
+                                   "attention callback"},
+            "cpu_baseline": {"value": round(ms, 3), "unit": "ms/token", "cores": cores, "kind": "reference",
+                             "sample": f"{n} autoregressive tokens after {args.warmup} warm-up tokens"},
+            "e2e": {"value": round(ms, 3), "unit": "ms/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
         return
     from qwen_b200 import model
 

@@ -232,3 +232,20 @@ def test_plan_structs_match_the_engine_ctypes_layouts(tmp_path):
         want.append(f"{name} size {spec['size']}")
         want += [f"{name} {f} {o} {s}" for f, o, s in spec["fields"]]
     assert [g for g in got if g] == want
+
+
+def test_python_plan_structs_match_the_engine_layouts():
+    """qwen_b200.plans' ctypes LinearLayerPlanC / MlpPlanC (what a Python
+    host passes to forward_linear_layer / forward_token_c) have the engine's
+    offsets and sizes (qwen_real_engine.py:20-74; tests/golden/plan_layouts.json)."""
+    import ctypes
+    import json
+
+    from qwen_b200 import plans
+
+    layouts = json.load(open(os.path.join(REPO, "tests", "golden", "plan_layouts.json")))
+    for name, spec in layouts.items():
+        cls = getattr(plans, name)
+        assert ctypes.sizeof(cls) == spec["size"], name
+        got = [(f, getattr(cls, f).offset, getattr(cls, f).size) for f, _ in cls._fields_]
+        assert got == [tuple(x) for x in spec["fields"]], name
