@@ -704,7 +704,7 @@ def run_token(args, torch, dev, world, rank):
     M = plans.TokenModel(seed=0)
     cb = plans.attention_stand_in()
     out = {}
-    for mode, name in ((0, "mirror"), (1, "resident")):
+    for mode, name in ((0, "mirror"), (1, "resident"), (2, "pinned")):
         assert L.qwen_b200_gdn_state_mode(mode) == 0
         st = M.fresh_states()
         lps, mps = M.plans(st)
@@ -716,7 +716,7 @@ def run_token(args, torch, dev, world, rank):
         dt = (time.perf_counter() - t0) / args.steps
         if mode == 1:
             L.qwen_b200_gdn_state_sync()
-            L.qwen_b200_gdn_state_drop()
+        L.qwen_b200_gdn_state_drop()
         out[name] = dt
     L.qwen_b200_gdn_state_mode(0)
     L.qwen_b200_reset_weights()
@@ -730,6 +730,7 @@ def run_token(args, torch, dev, world, rank):
                                    "host stand-in callback), final rmsnorm, lm_head argmax over 65536 rows",
                        "state_mode": "mirror (conv and recurrent states copied in and out every token)",
                        "resident_ms_per_token": round(out["resident"] * 1e3, 3),
+                       "pinned_mirror_ms_per_token": round(out["pinned"] * 1e3, 3),
                        "launches_per_token": TOKEN_LAUNCHES,
                        "host_round_trips_per_token": 6},
             "e2e": {"value": round(out["mirror"] * 1e3, 3), "unit": "ms/token",

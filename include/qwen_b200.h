@@ -200,17 +200,23 @@ QB_API int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linea
                            const int* layer_is_full, const float* final_norm_w, const uint16_t* embed_table,
                            QbFullAttnCallback full_attn_cb, void* py_context);
 
-/* Gated-DeltaNet state residency (no reference counterpart).  Mode 0 (the
- * default, the reference's contract): every forward_linear_layer /
- * forward_token_c call copies each layer's conv_s and state host arrays to
- * the device before its work and back after it (19.3 MB each way per token
- * for the 0.8B model).  Mode 1: the device copy, made on first sight after
- * entering the mode, is the state; the host arrays are only written by
- * qwen_b200_gdn_state_sync()
- * (and when switching back to mode 0).  A caller that resets or rewrites its
- * state arrays in mode 1 calls qwen_b200_gdn_state_drop() first, so the next
- * call re-reads them.  Return 0 or a QB_E* code. */
-QB_API int qwen_b200_gdn_state_mode(int resident);
+/* Gated-DeltaNet state handling (no reference counterpart).
+ *   mode 0 (the default, the reference's contract): every
+ *     forward_linear_layer / forward_token_c call copies each layer's conv_s
+ *     and state host arrays to the device before its work and back after it
+ *     (19.3 MB each way per token for the 0.8B model), as plain pageable
+ *     copies interleaved with the layers;
+ *   mode 1 (resident): the device copy, made on first sight after entering
+ *     the mode, is the state; the host arrays are written only by
+ *     qwen_b200_gdn_state_sync() and when leaving the mode;
+ *   mode 2 (pinned mirror): mode 0 with the host arrays page-locked in place
+ *     on first sight, so the copies run as asynchronous DMA beside the
+ *     layers.  The arrays stay registered until qwen_b200_gdn_state_drop() or
+ *     a mode change: a caller that frees a state array calls _drop() first.
+ * A caller that resets or rewrites its state arrays in mode 1 calls
+ * qwen_b200_gdn_state_drop() first, so the next call re-reads them.  Every
+ * mode change starts from the host arrays.  Return 0 or a QB_E* code. */
+QB_API int qwen_b200_gdn_state_mode(int mode);
 QB_API int qwen_b200_gdn_state_sync(void);
 QB_API void qwen_b200_gdn_state_drop(void);
 

@@ -70,6 +70,7 @@ struct Ctx {
     bool ready = false;
     int device = 0;
     cudaStream_t stream = nullptr;
+    cudaStream_t copy = nullptr;   // state copies of the layer loop, beside the compute stream
     qb::LmScratch* scratch = nullptr;
     // pinned host staging + device buffers for the drop-in calls
     void* h_in = nullptr;
@@ -96,7 +97,8 @@ int ensure_ctx() {
     if (const char* s = getenv("QWEN_B200_DEVICE")) dev = atoi(s);
     if (dev < 0 || dev >= ndev) dev = 0;
     if ((e = cudaSetDevice(dev)) != cudaSuccess) return fail(QB_ECUDA, "cudaSetDevice", e);
-    if ((e = cudaStreamCreateWithFlags(&g_ctx.stream, cudaStreamNonBlocking)) != cudaSuccess)
+    if ((e = cudaStreamCreateWithFlags(&g_ctx.stream, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaStreamCreateWithFlags(&g_ctx.copy, cudaStreamNonBlocking)) != cudaSuccess)
         return fail(QB_ECUDA, "cudaStreamCreate", e);
     if ((e = cudaMalloc(&g_ctx.scratch, sizeof(qb::LmScratch))) != cudaSuccess)
         return fail(QB_ENOMEM, "scratch alloc", e);
@@ -382,39 +384,78 @@ int resolve_linear_plan(const LinearLayerPlanC* p, DevLinear* out) {
 }
 
 // Device copies of the engine's mutable Gated-DeltaNet state arrays, keyed
-// by host address.  Mirror mode (the default, the reference's contract): the
-// host array is copied in before every layer call and back after it.
-// Resident mode: copied in once, then the device copy is the state until
-// qwen_b200_gdn_state_sync() copies it back or _drop() forgets it.
+// by host address.  Modes (qwen_b200_gdn_state_mode):
+//   0 mirror         the host array is copied in before every layer call and
+//                    back after it (the reference's contract), pageable copies;
+//   1 resident       copied in once, then the device copy is the state until
+//                    qwen_b200_gdn_state_sync() copies it back or _drop()
+//                    forgets it;
+//   2 pinned mirror  mode 0 with the host arrays page-locked in place on first
+//                    sight (cudaHostRegister), so the copies are asynchronous
+//                    DMA -- for callers whose arrays live until _drop() (a
+//                    registration outlives a freed array and makes later
+//                    copies over an overlapping range fail).
+enum { kStateMirror = 0, kStateResident = 1, kStatePinned = 2 };
 struct StateSlot {
     float* dev = nullptr;
     size_t n = 0;
+    bool pinned = false;
 };
 std::unordered_map<const float*, StateSlot> g_state_slots;
-bool g_state_resident = false;
+int g_state_mode = kStateMirror;
+
+void slot_release(const float* host, StateSlot& s) {
+    if (s.pinned) cudaHostUnregister(const_cast<float*>(host));
+    if (s.dev) cudaFree(s.dev);
+    s = StateSlot{};
+}
+
+void slots_clear() {
+    for (auto& kv : g_state_slots) slot_release(kv.first, kv.second);
+    g_state_slots.clear();
+}
 
 float* state_slot(float* host, size_t n, bool* fresh, int* rc) {
-    StateSlot& s = g_state_slots[host];
     *fresh = false;
-    if (s.dev && s.n != n) {   // a different-sized array at the same address: start over
-        cudaFree(s.dev);
-        s.dev = nullptr;
+    auto it = g_state_slots.find(host);
+    if (it != g_state_slots.end() && it->second.n != n) {   // a different-sized array at the same address
+        slot_release(it->first, it->second);
+        g_state_slots.erase(it);
+        it = g_state_slots.end();
     }
-    if (!s.dev) {
-        cudaError_t e = cudaMalloc(&s.dev, n * sizeof(float));
+    if (it == g_state_slots.end()) {
+        // two live arrays never overlap: a slot whose range meets this one
+        // belongs to an array that is gone
+        const char* lo = reinterpret_cast<const char*>(host);
+        const char* hi = lo + n * sizeof(float);
+        for (auto o = g_state_slots.begin(); o != g_state_slots.end();) {
+            const char* olo = reinterpret_cast<const char*>(o->first);
+            if (olo < hi && lo < olo + o->second.n * sizeof(float)) {
+                slot_release(o->first, o->second);
+                o = g_state_slots.erase(o);
+            } else {
+                ++o;
+            }
+        }
+        StateSlot sl;
+        cudaError_t e = cudaMalloc(&sl.dev, n * sizeof(float));
         if (e != cudaSuccess) {
-            s.dev = nullptr;
             *rc = fail(QB_ENOMEM, "state alloc", e);
             return nullptr;
         }
-        s.n = n;
+        sl.n = n;
+        if (g_state_mode == kStatePinned) {
+            sl.pinned = cudaHostRegister(host, n * sizeof(float), cudaHostRegisterDefault) == cudaSuccess;
+            if (!sl.pinned) cudaGetLastError();   // not an error: the copies stay pageable
+        }
+        it = g_state_slots.emplace(host, sl).first;
         *fresh = true;
     }
-    return s.dev;
+    return it->second.dev;
 }
 
-// Bring a layer's states onto the device (per the mode); dev_conv / dev_state
-// receive the device copies.
+// Bring a layer's states onto the device on stream s (per the mode);
+// dev_conv / dev_state receive the device copies.
 int states_in(const DevLinear& w, float** dev_conv, float** dev_state, cudaStream_t s) {
     int rc = QB_OK;
     const size_t nc = 3 * (size_t)w.qkv.M, ns = (size_t)w.heads * qb::kGdnHeadDim * qb::kGdnHeadDim;
@@ -422,17 +463,30 @@ int states_in(const DevLinear& w, float** dev_conv, float** dev_state, cudaStrea
     if (!(*dev_conv = state_slot(w.conv_s, nc, &fc, &rc)) || !(*dev_state = state_slot(w.state, ns, &fs, &rc)))
         return rc;
     cudaError_t e = cudaSuccess;
-    if (!g_state_resident || fc) e = cudaMemcpyAsync(*dev_conv, w.conv_s, nc * 4, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess && (!g_state_resident || fs))
+    const bool resident = g_state_mode == kStateResident;
+    if (!resident || fc) e = cudaMemcpyAsync(*dev_conv, w.conv_s, nc * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess && (!resident || fs))
         e = cudaMemcpyAsync(*dev_state, w.state, ns * 4, cudaMemcpyHostToDevice, s);
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "state copy in", e);
 }
 int states_out(const DevLinear& w, const float* dev_conv, const float* dev_state, cudaStream_t s) {
-    if (g_state_resident) return QB_OK;
+    if (g_state_mode == kStateResident) return QB_OK;
     const size_t nc = 3 * (size_t)w.qkv.M, ns = (size_t)w.heads * qb::kGdnHeadDim * qb::kGdnHeadDim;
     cudaError_t e = cudaMemcpyAsync(w.conv_s, dev_conv, nc * 4, cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaMemcpyAsync(w.state, dev_state, ns * 4, cudaMemcpyDeviceToHost, s);
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "state copy out", e);
+}
+
+// Event pool of the layer loop's copy / compute ordering (two per layer).
+std::vector<cudaEvent_t> g_loop_events;
+int loop_events(size_t n) {
+    while (g_loop_events.size() < n) {
+        cudaEvent_t ev = nullptr;
+        cudaError_t e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+        if (e != cudaSuccess) return fail(QB_ECUDA, "event create", e);
+        g_loop_events.push_back(ev);
+    }
+    return QB_OK;
 }
 
 // Work buffers of the device layer loop (the entry points are serialised).
@@ -737,9 +791,19 @@ int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linear_plans
     if (!dE || !dfin || dev_state(&st) || loop_bufs(kLoopHidden, V, F)) return name_error("forward_token_c"), -1;
     cudaStream_t s = g_ctx.stream;
     const size_t hb = 4 * (size_t)kLoopHidden;
+    // States move on the copy stream, interleaved with the layers: layer i's
+    // states go in just before its work is queued and its compute waits for
+    // them; they come back once layer i + 1 is queued.  (With pageable host
+    // arrays each copy holds the host thread while the GPU runs what is
+    // already queued; with page-locked ones, mode 2, nothing waits.)
     std::vector<float*> dconv(lin.size()), dstate(lin.size());
-    for (size_t i = 0; i < lin.size(); i++)
-        if (states_in(lin[i], &dconv[i], &dstate[i], s)) return name_error("forward_token_c"), -1;
+    cudaStream_t cs = g_ctx.copy;
+    if (loop_events(2 * lin.size() + 1)) return name_error("forward_token_c"), -1;
+    cudaEvent_t* ev_in = g_loop_events.data();
+    cudaEvent_t* ev_done = ev_in + lin.size();
+    cudaEvent_t ev_start = ev_in[2 * lin.size()];
+    if (cudaEventRecord(ev_start, s) != cudaSuccess || cudaStreamWaitEvent(cs, ev_start, 0) != cudaSuccess)
+        return cuda_fail(cudaGetLastError(), "forward_token_c"), -1;   // the previous call's work is done first
     // 1. the bf16 embedding row of token_id % 65536
     cudaError_t e = qb::launch_embed_row(g_loop.h, dE, token_id % kLoopVocab, kLoopHidden, s);
     // 2. the layers: full-attention ones run the caller's callback on the host
@@ -764,7 +828,14 @@ int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linear_plans
             }
             e = mlp_launch(mlp[l], g_loop.h, nullptr, nullptr, st, s);
         } else {
-            e = linear_launch(lin[li], g_loop.h, dconv[li], dstate[li], st, s);
+            if (states_in(lin[li], &dconv[li], &dstate[li], cs)) return name_error("forward_token_c"), -1;
+            e = cudaEventRecord(ev_in[li], cs);
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ev_in[li], 0);
+            if (e == cudaSuccess) e = linear_launch(lin[li], g_loop.h, dconv[li], dstate[li], st, s);
+            if (e == cudaSuccess) e = cudaEventRecord(ev_done[li], s);
+            if (e == cudaSuccess && li > 0) e = cudaStreamWaitEvent(cs, ev_done[li - 1], 0);
+            if (e == cudaSuccess && li > 0 && states_out(lin[li - 1], dconv[li - 1], dstate[li - 1], cs))
+                return name_error("forward_token_c"), -1;
             std::swap(g_loop.h, g_loop.h2);   // the layer's output is the next layer's h
             li++;
         }
@@ -777,28 +848,29 @@ int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linear_plans
     int* pid = reinterpret_cast<int*>(static_cast<unsigned char*>(g_loop.pin) + hb);
     if (e == cudaSuccess) e = cudaMemcpyAsync(g_loop.pin, g_loop.h, hb, cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaMemcpyAsync(pid, g_loop.res, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess && li > 0) e = cudaStreamWaitEvent(cs, ev_done[li - 1], 0);
     if (e != cudaSuccess) return cuda_fail(e, "forward_token_c"), -1;
-    for (size_t i = 0; i < lin.size(); i++)
-        if (states_out(lin[i], dconv[i], dstate[i], s)) return name_error("forward_token_c"), -1;
-    if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return cuda_fail(e, "forward_token_c"), -1;
+    if (li > 0 && states_out(lin[li - 1], dconv[li - 1], dstate[li - 1], cs)) return name_error("forward_token_c"), -1;
+    if ((e = cudaStreamSynchronize(s)) != cudaSuccess || (e = cudaStreamSynchronize(cs)) != cudaSuccess)
+        return cuda_fail(e, "forward_token_c"), -1;
     memcpy(h, g_loop.pin, hb);
     return *pid;
 }
 
-int qwen_b200_gdn_state_mode(int resident) {
+int qwen_b200_gdn_state_mode(int mode) {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (g_state_resident && !resident) {   // leaving resident mode: the host arrays catch up first
+    if (mode != kStateMirror && mode != kStateResident && mode != kStatePinned)
+        return fail(QB_EINVAL, "qwen_b200_gdn_state_mode: 0 (mirror), 1 (resident) or 2 (pinned mirror)");
+    if (mode == g_state_mode) return QB_OK;
+    if (g_state_mode == kStateResident) {   // leaving resident mode: the host arrays catch up first
         for (auto& kv : g_state_slots) {
             cudaError_t e = cudaMemcpy(const_cast<float*>(kv.first), kv.second.dev, kv.second.n * 4,
                                        cudaMemcpyDeviceToHost);
             if (e != cudaSuccess) return fail(QB_ECUDA, "state sync", e);
         }
     }
-    if (!g_state_resident && resident) {   // entering resident mode: start from the host arrays
-        for (auto& kv : g_state_slots) cudaFree(kv.second.dev);
-        g_state_slots.clear();
-    }
-    g_state_resident = resident != 0;
+    slots_clear();   // every mode starts from the host arrays (and holds no registration it did not make)
+    g_state_mode = mode;
     return QB_OK;
 }
 
@@ -814,8 +886,7 @@ int qwen_b200_gdn_state_sync(void) {
 
 void qwen_b200_gdn_state_drop(void) {
     std::lock_guard<std::mutex> lk(g_mu);
-    for (auto& kv : g_state_slots) cudaFree(kv.second.dev);
-    g_state_slots.clear();
+    slots_clear();
 }
 
 static int lm_bf16_host(const float* h, const uint16_t* E, int vocab, int hidden, int k, int with_tail,

@@ -123,31 +123,35 @@ def test_token_loop_matches_neon_oracle(libs):
     assert max(_rel(x[0], y[0]) for x, y in zip(st1, st2)) <= 1e-3
 
 
-def test_resident_state_mode_equals_mirror_mode(libs):
-    """Resident states (copied in once, synced back on request) give the
-    same tokens, h and states as the per-call mirror, bit for bit."""
+def test_state_modes_agree(libs):
+    """Resident states (copied in once, synced back on request) and the
+    page-locked mirror give the same tokens, h and states as the default
+    mirror, bit for bit."""
     lib, _ = libs
     M = LF.TokenModel(seed=4)
     cb = LF.attention_stand_in()
     out = []
-    for mode in (0, 1):
+    for mode in (0, 1, 2):
         assert lib.qwen_b200_gdn_state_mode(mode) == 0
         st = M.fresh_states()
         lps, mps = M.plans(st)
         h = np.zeros(LF.HIDDEN, np.float32)
         ids = [lib.forward_token_c(t, h.ctypes.data, ctypes.byref(lps), ctypes.byref(mps), M.is_full.ctypes.data,
                                    M.final_ln.ctypes.data, M.embed.ctypes.data, cb, None) for t in (9, 99, 999)]
+        assert min(ids) >= 0, lib.qwen_b200_last_error()
         if mode == 1:
             untouched = all(np.array_equal(s[1], s0[1]) for s, s0 in zip(st, M.states0))
             assert untouched, "resident mode wrote the host states before a sync"
             assert lib.qwen_b200_gdn_state_sync() == 0
-            lib.qwen_b200_gdn_state_drop()
+        lib.qwen_b200_gdn_state_drop()
         out.append((ids, h, st))
     assert lib.qwen_b200_gdn_state_mode(0) == 0
-    (i0, h0, s0), (i1, h1, s1) = out
-    assert i0 == i1
-    assert np.array_equal(h0, h1)
-    assert all(np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1]) for a, b in zip(s0, s1))
+    assert lib.qwen_b200_gdn_state_mode(3) != 0
+    i0, h0, s0 = out[0]
+    for i1, h1, s1 in out[1:]:
+        assert i0 == i1
+        assert np.array_equal(h0, h1)
+        assert all(np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1]) for a, b in zip(s0, s1))
 
 
 def test_bad_plan_leaves_h_and_states_unchanged(libs):
