@@ -46,13 +46,20 @@ __device__ __forceinline__ float dot4_pair(const float* a0, const float* b0, con
 __device__ __forceinline__ float recip_sqrt_ieee(float x) { return __fdiv_rn(1.0f, __fsqrt_rn(x)); }
 
 __global__ void __launch_bounds__(kThreads) gdn_layer_kernel(const GdnArgs a) {
-    extern __shared__ float gdn_smem[];   // x | wa row | wb row (hidden floats each)
+    extern __shared__ float gdn_smem[];   // x | wa row | wb row | in_ln_w (hidden floats each)
     __shared__ float sq[kD], sk[kD], sv[kD], so[kD];
     __shared__ float s_kr, s_qr, s_qk, s_rg, s_alpha, s_beta;
     const int hd = blockIdx.x, t = threadIdx.x;
     const int HD = a.heads * kD, C = 3 * HD;
 
     if (t < kColThreads) {
+        // column t of the head's state, S[4g+u][t] = B[16g+u]: all 32 float4
+        // loads go out first and land while the conv and the norms run
+        float* B = a.state + (size_t)hd * kD * kD + (size_t)(t >> 2) * (kD * 4) + (t & 3) * 4;
+        float4 col[kD / 4];
+#pragma unroll
+        for (int g = 0; g < kD / 4; g++) col[g] = *reinterpret_cast<const float4*>(B + 16 * g);
+        const float zt = a.z[hd * kD + t], nw = a.norm_w[t];   // for the gated norm at the end
         // ---- causal_conv1d_update_silu (qwen_kernels_opt.c:511-545), channels
         // hd*128 + t of q, k and v: d = w0*s0 + w1*s1 + w2*s2 + w3*x (multiply,
         // then three multiply-adds), y = d / (1 + exp_neon(-d)) with the
@@ -91,11 +98,10 @@ __global__ void __launch_bounds__(kThreads) gdn_layer_kernel(const GdnArgs a) {
             const float s = dot4_pair(sq, sk, sq, sk, kD, t);
             if (t == 0) s_qk = s;
         }
-        float* B = a.state + (size_t)hd * kD * kD + (size_t)(t >> 2) * (kD * 4) + (t & 3) * 4;   // S[4g+u][t] = B[16g+u]
         float kv = 0.0f, qs = 0.0f;
-#pragma unroll 4
+#pragma unroll
         for (int g = 0; g < kD / 4; g++) {
-            const float4 s4 = *reinterpret_cast<const float4*>(B + 16 * g);
+            const float4 s4 = col[g];
             kv = add_ftz(kv, mul_ftz(s4.x, sk[4 * g]));
             qs = add_ftz(qs, mul_ftz(s4.x, sq[4 * g]));
             kv = add_ftz(kv, mul_ftz(s4.y, sk[4 * g + 1]));
@@ -110,9 +116,9 @@ __global__ void __launch_bounds__(kThreads) gdn_layer_kernel(const GdnArgs a) {
         // d = (v - kv*a) * b; out = qs*a + qk*d; S = S*a + d*k[i]
         const float d = mul_ftz(sub_ftz(sv[t], mul_ftz(kv, al)), be);
         so[t] = add_ftz(mul_ftz(qs, al), mul_ftz(s_qk, d));
-#pragma unroll 4
+#pragma unroll
         for (int g = 0; g < kD / 4; g++) {
-            float4 s4 = *reinterpret_cast<const float4*>(B + 16 * g);
+            float4 s4 = col[g];
             s4.x = add_ftz(mul_ftz(s4.x, al), mul_ftz(d, sk[4 * g]));
             s4.y = add_ftz(mul_ftz(s4.y, al), mul_ftz(d, sk[4 * g + 1]));
             s4.z = add_ftz(mul_ftz(s4.z, al), mul_ftz(d, sk[4 * g + 2]));
@@ -127,9 +133,8 @@ __global__ void __launch_bounds__(kThreads) gdn_layer_kernel(const GdnArgs a) {
             if (t == 0) s_rg = recip_sqrt_ieee(__fadd_rn(__fdiv_rn(s, (float)kD), 1e-6f));
         }
         col_sync();
-        const float zt = a.z[hd * kD + t];
         const float silu = __fdiv_rn(zt, __fadd_rn(1.0f, expf(-zt)));
-        a.out[hd * kD + t] = __fmul_rn(__fmul_rn(__fmul_rn(so[t], s_rg), a.norm_w[t]), silu);
+        a.out[hd * kD + t] = __fmul_rn(__fmul_rn(__fmul_rn(so[t], s_rg), nw), silu);
     } else {
         // ---- gate warp: n = rmsnorm(h, in_ln_w) (NEON build, the layer's own
         // step 1), then gdn_gates (qwen_kernels_opt.c:593-625) for this head:
@@ -139,19 +144,53 @@ __global__ void __launch_bounds__(kThreads) gdn_layer_kernel(const GdnArgs a) {
         float* sx = gdn_smem;
         float* swa = gdn_smem + H;
         float* swb = gdn_smem + 2 * H;
+        float* sln = gdn_smem + 3 * H;
         const float* wa = a.wa + (size_t)hd * H;
         const float* wb = a.wb + (size_t)hd * H;
-        for (int i = lane; i < H; i += 32) {
-            sx[i] = a.h[i];
-            swa[i] = wa[i];
-            swb[i] = wb[i];
+        // stage h, the head's wa / wb rows and in_ln_w; every load of a lane
+        // goes out before the first store (16-byte loads where all four
+        // sources allow them)
+        if (((reinterpret_cast<uintptr_t>(a.h) | reinterpret_cast<uintptr_t>(wa) | reinterpret_cast<uintptr_t>(wb) |
+              reinterpret_cast<uintptr_t>(a.in_ln_w)) & 15) == 0) {
+            for (int i0 = lane; i0 < H / 4; i0 += 32 * 4) {
+                float4 v[4][4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int i = i0 + 32 * u;
+                    if (i < H / 4) {
+                        v[u][0] = reinterpret_cast<const float4*>(a.h)[i];
+                        v[u][1] = reinterpret_cast<const float4*>(wa)[i];
+                        v[u][2] = reinterpret_cast<const float4*>(wb)[i];
+                        v[u][3] = reinterpret_cast<const float4*>(a.in_ln_w)[i];
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int i = i0 + 32 * u;
+                    if (i < H / 4) {
+                        reinterpret_cast<float4*>(sx)[i] = v[u][0];
+                        reinterpret_cast<float4*>(swa)[i] = v[u][1];
+                        reinterpret_cast<float4*>(swb)[i] = v[u][2];
+                        reinterpret_cast<float4*>(sln)[i] = v[u][3];
+                    }
+                }
+            }
+        } else {
+#pragma unroll 8
+            for (int i = lane; i < H; i += 32) {
+                const float x = a.h[i], ya = wa[i], yb = wb[i], l = a.in_ln_w[i];
+                sx[i] = x;
+                swa[i] = ya;
+                swb[i] = yb;
+                sln[i] = l;
+            }
         }
         __syncwarp();
         const float ss = dot4_pair(sx, sx, sx, sx, H, lane);
         float r = 0.0f;
         if (lane == 0) r = recip_sqrt_ieee(__fadd_rn(__fdiv_rn(ss, (float)H), 1e-6f));
         r = __shfl_sync(0xffffffffu, r, 0);
-        for (int i = lane; i < H; i += 32) sx[i] = mul_ftz(sx[i], mul_ftz(r, add_ftz(1.0f, a.in_ln_w[i])));
+        for (int i = lane; i < H; i += 32) sx[i] = mul_ftz(sx[i], mul_ftz(r, add_ftz(1.0f, sln[i])));
         __syncwarp();
         const float g = dot4_pair(swa, sx, swb, sx, H, lane);   // lane 0: av, lane 4: bv
         const float bv = __shfl_sync(0xffffffffu, g, 4);
@@ -189,7 +228,7 @@ cudaError_t launch_gdn_layer(const GdnArgs& a, cudaStream_t stream) {
         !a.in_ln_w || !a.conv_w || !a.conv_s || !a.wa || !a.wb || !a.nea || !a.dt || !a.state || !a.norm_w || !a.out)
         return cudaErrorInvalidValue;
     if (reinterpret_cast<uintptr_t>(a.state) % 16) return cudaErrorInvalidValue;
-    const size_t smem = 3 * (size_t)a.hidden * sizeof(float);
+    const size_t smem = 4 * (size_t)a.hidden * sizeof(float);
     if (cudaError_t e = raise_smem_limit(reinterpret_cast<const void*>(gdn_layer_kernel), smem)) return e;
     gdn_layer_kernel<<<a.heads, kThreads, smem, stream>>>(a);
     return cudaGetLastError();
