@@ -153,9 +153,9 @@ typedef struct {
 /* Replaces forward_mlp() (qwen_kernels_opt.c:994-1003; caller
  * qwen_real_engine.py:1152-1153): h += down(swiglu(gate(n), up(n))) with
  * n = rmsnorm(h, post_ln_w, 1e-6) -- the reference's NEON-build rmsnorm,
- * GEMVs, swiglu and add_residual, bit for bit -- as four launches on the
- * device (rmsnorm in front of gate and of up, swiglu in front of down, the
- * residual add); h (host, K_gate floats) is copied in and back, weight and
+ * GEMVs, swiglu and add_residual, bit for bit -- as three launches on the
+ * device (gate and up together with the rmsnorm in front, swiglu in front of
+ * down, the residual add); h (host, K_gate floats) is copied in and back, weight and
  * norm pointers are translated like bfp8_gemv's.  K_gate == K_up <= 6144,
  * M_gate == M_up == K_down, M_down == K_gate, multiples of 512.  On error h
  * is unchanged and qwen_b200_last_error() says why. */
@@ -163,10 +163,10 @@ QB_API void forward_mlp(const MlpPlanC* p, float* h);
 
 /* Replaces forward_linear_layer() (qwen_kernels_opt.c:938-992; caller
  * qwen_real_engine.py:1096): one Gated-DeltaNet layer on the device in
- * eight launches -- the qkv and z projections of rmsnorm(h, in_ln_w)
- * (fused), one kernel for conv1d + SiLU, q/k l2 norm, the gates, the
+ * six launches -- the qkv and z projections of rmsnorm(h, in_ln_w)
+ * (one launch), one kernel for conv1d + SiLU, q/k l2 norm, the gates, the
  * recurrent step and rmsnorm_gated (one CTA per head), the out projection,
- * then the MLP with h + o formed in front of its gate projection.  NEON-build
+ * then the MLP with h + o formed in front of its gate and up projections.  NEON-build
  * order throughout (the GEMVs bit for bit); the gates and the gated norm's
  * SiLU use CUDA's expf / log1pf where the reference calls the C library's.
  * Shapes: K_qkv == K_z == M_o == K_gate <= 6144 (a multiple of 512),
@@ -267,6 +267,17 @@ QB_API int qwen_b200_rmsnorm_gemv_dev(float* y, const float* x, const float* nor
 QB_API int qwen_b200_residual_rmsnorm_gemv_dev(float* y, float* x_out, const float* x, const float* res,
                                                const float* norm_w, float eps, const int8_t* mant,
                                                const uint8_t* exps, int M, int K, void* stream);
+
+/* Two projections of the same normalized vector in one launch: y0 = the
+ * M0 x K GEMV and y1 = the M1 x K GEMV of rmsnorm(x, norm_w, eps) (or, with
+ * res and x_out, of x + res, which is also stored to x_out) -- a
+ * linear-attention layer's qkv and z projections, an MLP's gate and up
+ * (qwen_kernels_opt.c:946,970,998-999); each bit for bit
+ * qwen_b200_rmsnorm_gemv_dev / qwen_b200_residual_rmsnorm_gemv_dev of it.
+ * Same conditions as those (K a multiple of 512 and <= 6144). */
+QB_API int qwen_b200_rmsnorm_gemv2_dev(float* y0, float* y1, float* x_out, const float* x, const float* res,
+                                       const float* norm_w, float eps, const int8_t* mant0, const uint8_t* exps0,
+                                       int M0, const int8_t* mant1, const uint8_t* exps1, int M1, int K, void* stream);
 
 /* The MLP's down projection with its SwiGLU in front, in one launch:
  * y = qwen_b200_gemv_dev of swiglu(gate, up), swiglu as the reference's NEON

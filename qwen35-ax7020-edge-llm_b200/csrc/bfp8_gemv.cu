@@ -182,6 +182,11 @@ struct WArgs {
     unsigned int* rtl_flags;   // RTL mode: sticky flags word (may be null)
     const float* glu_up;    // res_act only: the activation is swiglu(x, glu_up) (nullptr: x)
     SyncArgs sync;          // row-sharded stacks: completion signal (sig_epoch 0: none)
+    // split kernel only: units [second_begin, total_units) run `second`, a
+    // GEMV of the same activation (same x and K) -- two projections of one
+    // normalized vector in one launch (second_begin 0: none)
+    int second_begin;
+    GemvDesc second;
 };
 
 __device__ __forceinline__ const GemvDesc& wdesc(const WArgs& A, int d) {
@@ -844,7 +849,11 @@ __global__ void __launch_bounds__(kThreads, SPW == 1 ? 2 : 1) gemv_split_kernel(
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                            ~uintptr_t(1023));
-    const GemvDesc& D = A.single;
+    // one unit per CTA: the CTAs past second_begin serve the second GEMV
+    const bool sec = A.second_begin > 0 && (int)blockIdx.x >= A.second_begin;
+    const GemvDesc& D = sec ? A.second : A.single;
+    const int ubase = sec ? A.second_begin : 0;
+    const int uend = A.second_begin > 0 && !sec ? A.second_begin : A.total_units;
     const int K = D.K, M = D.M, nb = K >> 6, nst = K >> 8;
     const int spw = (nst + kWarps - 1) / kWarps;
     unsigned char* rings = smem;                                                  // [warp][spw] stages
@@ -866,8 +875,8 @@ __global__ void __launch_bounds__(kThreads, SPW == 1 ? 2 : 1) gemv_split_kernel(
     const int sw = lane & 7;
     uint32_t phase = 0;
     bool first = true;
-    for (int u = blockIdx.x; u < A.total_units; u += gridDim.x, phase ^= 1u) {
-        const int r0 = u * kRows;
+    for (int u = blockIdx.x; u < uend; u += gridDim.x, phase ^= 1u) {
+        const int r0 = (u - ubase) * kRows;
         const bool row_ok = r0 + lane < M;
         // every stage of this warp's share goes out at once (weights are immutable)
 #pragma unroll
@@ -1462,6 +1471,45 @@ cudaError_t launch_rmsnorm_gemv(const GemvDesc& d0, const float* norm_w, float e
     A.single = d;
     A.n = 1;
     A.total_units = plan.total_units;
+    A.ctr = nullptr;
+    A.err = err;
+    return launch_split(A, stream);
+}
+
+cudaError_t launch_rmsnorm_gemv2(const GemvDesc& d0, const GemvDesc& d1, const float* norm_w, float eps,
+                                uint32_t* act, unsigned int* err, cudaStream_t stream, const float* res,
+                                float* x_out) {
+    if (d0.M <= 0 || d1.M <= 0 || d0.K != d1.K || d0.x != d1.x) return cudaErrorInvalidValue;
+    GemvDesc e1 = d1;
+    GemvPlan p1;
+    if (!fast_shape_ok(e1) || !act || !gemv_plan(&e1, 1, act, &p1)) return cudaErrorInvalidValue;
+    // the first GEMV's checks and plan, then the second's units appended
+    GemvDesc e0 = d0;
+    GemvPlan p0;
+    if (!e0.x || !norm_w || (reinterpret_cast<uintptr_t>(norm_w) & 7) || !res_fits(e0.K) || !fast_shape_ok(e0) ||
+        !gemv_plan(&e0, 1, act, &p0))
+        return cudaErrorInvalidValue;
+    if ((res == nullptr) != (x_out == nullptr)) return cudaErrorInvalidValue;
+    if (res) {
+        const uintptr_t o0 = reinterpret_cast<uintptr_t>(x_out), o1 = o0 + 4 * (size_t)e0.K;
+        auto overlaps = [&](const float* p) {
+            const uintptr_t q0 = reinterpret_cast<uintptr_t>(p), q1 = q0 + 4 * (size_t)e0.K;
+            return q0 < o1 && o0 < q1;
+        };
+        if (((reinterpret_cast<uintptr_t>(res) | o0) & 7) || overlaps(e0.x) || overlaps(res))
+            return cudaErrorInvalidValue;
+    }
+    WArgs A{};
+    A.res_act = 1;
+    A.norm_w = norm_w;
+    A.norm_eps = eps;
+    A.norm_res = res;
+    A.norm_xout = x_out;
+    A.single = e0;
+    A.n = 1;
+    A.second = e1;
+    A.second_begin = p0.total_units;
+    A.total_units = p0.total_units + p1.total_units;
     A.ctr = nullptr;
     A.err = err;
     return launch_split(A, stream);

@@ -102,6 +102,13 @@ cudaError_t launch_gemv(const GemvDesc& d, uint32_t* act, unsigned int* err, cud
 cudaError_t launch_rmsnorm_gemv(const GemvDesc& d, const float* norm_w, float eps, uint32_t* act, unsigned int* err,
                                cudaStream_t stream, const float* res = nullptr, float* x_out = nullptr);
 
+// Two exact GEMVs of the same rmsnorm(x) (or of x + res, stored to x_out) in
+// one launch -- d0 and d1 share x and K (a layer's qkv and z projections, an
+// MLP's gate and up); the same conditions as launch_rmsnorm_gemv.
+cudaError_t launch_rmsnorm_gemv2(const GemvDesc& d0, const GemvDesc& d1, const float* norm_w, float eps,
+                                uint32_t* act, unsigned int* err, cudaStream_t stream, const float* res = nullptr,
+                                float* x_out = nullptr);
+
 // One exact GEMV of swiglu(gate, up) (the reference's NEON swiglu, then its
 // quantizer and GEMV; d.x holds the gate projection) in one launch: every
 // CTA applies swiglu and quantizes itself.  K <= 6144, a multiple of 512;

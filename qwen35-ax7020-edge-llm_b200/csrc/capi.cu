@@ -539,35 +539,31 @@ qb::GemvDesc gemv_desc(const DevGemv& g, const float* x, float* y) {
 }
 
 // forward_mlp's steps on the device: h += down(swiglu(gate(n), up(n))),
-// n = rmsnorm(h) -- rmsnorm fused in front of gate and of up, swiglu in front
-// of down, then the residual add (four launches).  With `res`, the layer's
+// n = rmsnorm(h) -- gate and up in one launch with the rmsnorm in front,
+// swiglu in front of down, then the residual add (three launches).  With `res`, the layer's
 // pending residual h + res is formed in front of gate (h_out = h + res) and
 // the MLP runs on h_out; h_out then holds the result.
 cudaError_t mlp_launch(const DevMlp& w, float* h, const float* res, float* h_out, DevState* st, cudaStream_t s) {
     const int H = w.gate.K;
-    cudaError_t e = res ? qb::launch_rmsnorm_gemv(gemv_desc(w.gate, h, g_loop.gate), w.post_ln, 1e-6f, st->act,
-                                                  st->err, s, res, h_out)
-                        : qb::launch_rmsnorm_gemv(gemv_desc(w.gate, h, g_loop.gate), w.post_ln, 1e-6f, st->act,
-                                                  st->err, s);
+    // gate and up projections of the same rmsnorm(h) (or of h + res) in one launch
+    cudaError_t e = qb::launch_rmsnorm_gemv2(gemv_desc(w.gate, h, g_loop.gate), gemv_desc(w.up, h, g_loop.up),
+                                             w.post_ln, 1e-6f, st->act, st->err, s, res, res ? h_out : nullptr);
     float* hh = res ? h_out : h;
-    if (e == cudaSuccess)
-        e = qb::launch_rmsnorm_gemv(gemv_desc(w.up, hh, g_loop.up), w.post_ln, 1e-6f, st->act, st->err, s);
     if (e == cudaSuccess)
         e = qb::launch_swiglu_gemv(gemv_desc(w.down, g_loop.gate, g_loop.down), g_loop.up, st->act, st->err, s);
     if (e == cudaSuccess) e = qb::launch_add_residual(hh, g_loop.down, H, s);
     return e;
 }
 
-// forward_linear_layer's steps on the device (eight launches): qkv and z
-// projections of rmsnorm(h) (fused), the Gated-DeltaNet kernel, the out
-// projection, then the MLP with h + o formed in front of its gate
-// projection.  The result lands in g_loop.h2.
+// forward_linear_layer's steps on the device (six launches): the qkv and z
+// projections of rmsnorm(h) (one launch), the Gated-DeltaNet kernel, the out
+// projection, then the MLP with h + o formed in front of its gate and up
+// projections.  The result lands in g_loop.h2.
 cudaError_t linear_launch(const DevLinear& w, float* h, float* dev_conv, float* dev_state, DevState* st,
                           cudaStream_t s) {
-    cudaError_t e =
-        qb::launch_rmsnorm_gemv(gemv_desc(w.qkv, h, g_loop.qkv), w.in_ln, 1e-6f, st->act, st->err, s);
-    if (e == cudaSuccess)
-        e = qb::launch_rmsnorm_gemv(gemv_desc(w.z, h, g_loop.z), w.in_ln, 1e-6f, st->act, st->err, s);
+    // qkv and z projections of the same rmsnorm(h) in one launch
+    cudaError_t e = qb::launch_rmsnorm_gemv2(gemv_desc(w.qkv, h, g_loop.qkv), gemv_desc(w.z, h, g_loop.z), w.in_ln,
+                                             1e-6f, st->act, st->err, s);
     if (e == cudaSuccess) {
         qb::GdnArgs a{};
         a.qkv = g_loop.qkv;
@@ -1129,6 +1125,35 @@ int qwen_b200_residual_rmsnorm_gemv_dev(float* y, float* x_out, const float* x, 
         return fail(QB_EINVAL, "qwen_b200_residual_rmsnorm_gemv_dev: K a multiple of 512 and <= 6144, 8-byte aligned "
                                "vectors, x_out overlapping neither x nor res");
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_residual_rmsnorm_gemv_dev", e);
+}
+
+int qwen_b200_rmsnorm_gemv2_dev(float* y0, float* y1, float* x_out, const float* x, const float* res,
+                                const float* norm_w, float eps, const int8_t* mant0, const uint8_t* exps0, int M0,
+                                const int8_t* mant1, const uint8_t* exps1, int M1, int K, void* stream) {
+    if (int rc = check_gemv_args(y0, x, mant0, exps0, M0, K)) return rc;
+    if (int rc = check_gemv_args(y1, x, mant1, exps1, M1, K)) return rc;
+    if (!norm_w || (res == nullptr) != (x_out == nullptr))
+        return fail(QB_EINVAL, "qwen_b200_rmsnorm_gemv2_dev: null norm weights, or only one of res / x_out");
+    qb::GemvDesc d0{}, d1{};
+    d0.mant = mant0;
+    d0.exps = exps0;
+    d0.x = x;
+    d0.y = y0;
+    d0.M = M0;
+    d0.K = K;
+    d1 = d0;
+    d1.mant = mant1;
+    d1.exps = exps1;
+    d1.y = y1;
+    d1.M = M1;
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    cudaError_t e = qb::launch_rmsnorm_gemv2(d0, d1, norm_w, eps, st->act, st->err, static_cast<cudaStream_t>(stream),
+                                             res, x_out);
+    if (e == cudaErrorInvalidValue)
+        return fail(QB_EINVAL, "qwen_b200_rmsnorm_gemv2_dev: M0, M1 >= 1, K a multiple of 512 and <= 6144, 8-byte "
+                               "aligned vectors, x_out overlapping neither x nor res");
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_rmsnorm_gemv2_dev", e);
 }
 
 int qwen_b200_swiglu_gemv_dev(float* y, const float* gate, const float* up, const int8_t* mant,

@@ -50,6 +50,7 @@ SIGNATURES = {
     "qwen_b200_gemv_rtl20_dev": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _P, _P]),
     "qwen_b200_rmsnorm_gemv_dev": (_I, [_P, _P, _P, _F, _P, _P, _I, _I, _P]),
     "qwen_b200_residual_rmsnorm_gemv_dev": (_I, [_P, _P, _P, _P, _P, _F, _P, _P, _I, _I, _P]),
+    "qwen_b200_rmsnorm_gemv2_dev": (_I, [_P, _P, _P, _P, _P, _P, _F, _P, _P, _I, _P, _P, _I, _I, _P]),
     "qwen_b200_quant_dev": (_I, [_P, _I, _I, _P, _P, _P]),
     "qwen_b200_stack_create": (_I, [_I, _P, _P, _P, _P, _P, _P]),
     "qwen_b200_stack_create_ex": (_I, [_I, _P, _P, _P, _P, _P, _P, _I]),

@@ -129,6 +129,35 @@ def residual_rmsnorm_bfp8_gemv(x: torch.Tensor, res: torch.Tensor, norm_w: torch
     return y, x_out
 
 
+def rmsnorm_bfp8_gemv2(x: torch.Tensor, norm_w: torch.Tensor, eps: float, w0, w1, res: torch.Tensor | None = None):
+    """Two projections of one normalized vector in one launch (a layer's qkv
+    and z, an MLP's gate and up): (y0, y1) = the GEMVs of w0 = (mant0, exps0)
+    and w1 = (mant1, exps1) of rmsnorm(x) -- or, with res, of x + res, which
+    is returned as a third element.  Bit for bit rmsnorm_bfp8_gemv /
+    residual_rmsnorm_bfp8_gemv of each.  K a multiple of 512 and <= 6144."""
+    x = _need(x, torch.float32, "x")
+    norm_w = _need(norm_w, torch.float32, "norm_w")
+    m0, e0 = _need(w0[0], torch.int8, "mant0"), _need(w0[1], torch.uint8, "exps0")
+    m1, e1 = _need(w1[0], torch.int8, "mant1"), _need(w1[1], torch.uint8, "exps1")
+    M0, K = m0.shape
+    M1, K1 = m1.shape
+    if K1 != K or x.numel() != K or norm_w.numel() != K:
+        raise ValueError("shape mismatch")
+    y0 = torch.empty(M0, dtype=torch.float32, device=m0.device)
+    y1 = torch.empty(M1, dtype=torch.float32, device=m0.device)
+    x_out = None
+    if res is not None:
+        res = _need(res, torch.float32, "res")
+        if res.numel() != K:
+            raise ValueError("shape mismatch")
+        x_out = torch.empty(K, dtype=torch.float32, device=m0.device)
+    check(load().qwen_b200_rmsnorm_gemv2_dev(_ptr(y0), _ptr(y1), _ptr(x_out) if x_out is not None else None, _ptr(x),
+                                             _ptr(res) if res is not None else None, _ptr(norm_w), float(eps),
+                                             _ptr(m0), _ptr(e0), M0, _ptr(m1), _ptr(e1), M1, K, _stream()),
+          "rmsnorm_bfp8_gemv2")
+    return (y0, y1) if res is None else (y0, y1, x_out)
+
+
 def bfp8_gemv_q(xq: torch.Tensor, xs: torch.Tensor, mant: torch.Tensor, exps: torch.Tensor):
     """y = BFP8 GEMV of an already quantized activation (xq int16 [K], xs fp32 [K/64])."""
     return T.bfp8_gemv_q(_need(xq, torch.int16, "xq"), _need(xs, torch.float32, "xs"),

@@ -440,6 +440,35 @@ def test_residual_rmsnorm_gemv_bit_exact(cuda, M, K, sx):
         assert np.array_equal(bits(y.cpu().numpy()), bits(ref))
 
 
+@pytest.mark.parametrize("M0,M1,K,residual", [(6144, 2048, 1024, False), (3584, 3584, 1024, True),
+                                               (33, 1, 2048, True), (257, 64, 6144, False)])
+def test_rmsnorm_gemv2_bit_exact(cuda, M0, M1, K, residual):
+    """Two projections of one normalized vector in one launch (qkv and z,
+    gate and up): each output, and x + res when given, bit-identical to the
+    oracle chain, twice in a row."""
+    import torch
+
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(M0 * 7 + M1 + K)
+    m0, e0 = rand_weights(rng, M0, K)
+    m1, e1 = rand_weights(rng, M1, K)
+    x = rng.normal(0, 2.0, K).astype(np.float32)
+    res = rng.normal(0, 2.0, K).astype(np.float32)
+    w = rng.normal(0, 0.1, K).astype(np.float32)
+    xo = O.add_residual(x, res, neon=True) if residual else x
+    n = O.rmsnorm(xo, w, 1e-6, neon=True)
+    ref0, ref1 = O.bfp8_gemv(n, m0, e0), O.bfp8_gemv(n, m1, e1)
+    dx, dr, dw, dm0, de0, dm1, de1 = to_dev(x, res, w, m0, e0, m1, e1)
+    for _ in range(2):
+        out = ops.rmsnorm_bfp8_gemv2(dx, dw, 1e-6, (dm0, de0), (dm1, de1), res=dr if residual else None)
+        torch.cuda.synchronize()
+        assert np.array_equal(bits(out[0].cpu().numpy()), bits(ref0))
+        assert np.array_equal(bits(out[1].cpu().numpy()), bits(ref1))
+        if residual:
+            assert np.array_equal(bits(out[2].cpu().numpy()), bits(xo))
+
+
 def test_residual_rmsnorm_gemv_rejects_aliasing(cuda):
     """x_out may not overlap x or res (every CTA reads them while one writes it)."""
     import torch
