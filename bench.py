@@ -505,6 +505,14 @@ def run_configs(args, torch, dist, dev, barrier, world, rank, hbm_peak, peak_kin
     torch.cuda.empty_cache()
     out["abi"] = guarded(run_abi, torch, dev)
     torch.cuda.empty_cache()
+    # the per-token C loop through forward_token_c, beside the reference's own loop on the host cores
+    tok_args = argparse.Namespace(**vars(args))
+    tok_args.steps, tok_args.warmup = steps, warm
+    rec = guarded(run_token, tok_args, torch, dev, world, rank)
+    if not args.no_cpu_baseline and "error" not in rec:
+        rec["cpu_baseline"] = cpu_baseline("token")
+    out["token"] = rec
+    torch.cuda.empty_cache()
     return out
 
 

@@ -249,3 +249,32 @@ def test_python_plan_structs_match_the_engine_layouts():
         assert ctypes.sizeof(cls) == spec["size"], name
         got = [(f, getattr(cls, f).offset, getattr(cls, f).size) for f, _ in cls._fields_]
         assert got == [tuple(x) for x in spec["fields"]], name
+
+
+def test_token_loop_rejects_bad_arguments_without_a_gpu():
+    """forward_token_c refuses a negative token id or a null pointer before
+    any device work (returns -1 with a message); forward_linear_layer and
+    forward_mlp refuse a null h; the state-mode call refuses unknown modes."""
+    import ctypes
+
+    import numpy as np
+
+    from qwen_b200 import _lib, plans
+
+    lib = _lib.load()
+    h = np.zeros(plans.HIDDEN, np.float32)
+    lps = (plans.LinearLayerPlanC * 18)()
+    mps = (plans.MlpPlanC * 24)()
+    full = np.zeros(24, np.int32)
+    w = np.zeros(plans.HIDDEN, np.float32)
+    emb = np.zeros(16, np.uint16)
+    args = (h.ctypes.data, ctypes.byref(lps), ctypes.byref(mps), full.ctypes.data, w.ctypes.data, emb.ctypes.data,
+            plans.CALLBACK(), None)   # CALLBACK(): a null function pointer
+    assert lib.forward_token_c(-1, *args) == -1
+    assert b"forward_token_c" in lib.qwen_b200_last_error()
+    assert lib.forward_token_c(5, None, *args[1:]) == -1
+    lib.forward_linear_layer(ctypes.byref(lps[0]), None)
+    assert b"forward_linear_layer" in lib.qwen_b200_last_error()
+    lib.forward_mlp(ctypes.byref(mps[0]), None)
+    assert b"forward_mlp" in lib.qwen_b200_last_error()
+    assert lib.qwen_b200_gdn_state_mode(7) != 0

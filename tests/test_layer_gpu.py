@@ -123,6 +123,24 @@ def test_token_loop_matches_neon_oracle(libs):
     assert max(_rel(x[0], y[0]) for x, y in zip(st1, st2)) <= 1e-3
 
 
+def test_token_loop_without_callback(libs):
+    """A null callback skips attention, as the reference's loop does
+    (qwen_kernels_opt.c:1031): still the oracle's token ids."""
+    lib, orc = libs
+    M = LF.TokenModel(seed=6)
+    st1, st2 = M.fresh_states(), M.fresh_states()
+    (l1, m1), (l2, m2) = M.plans(st1), M.plans(st2)
+    h1 = np.zeros(LF.HIDDEN, np.float32)
+    h2 = np.zeros(LF.HIDDEN, np.float32)
+    for tok in (123, 4567):
+        a = lib.forward_token_c(tok, h1.ctypes.data, ctypes.byref(l1), ctypes.byref(m1), M.is_full.ctypes.data,
+                                M.final_ln.ctypes.data, M.embed.ctypes.data, LF.CALLBACK(), None)
+        b = orc.orc_forward_token(tok, h2.ctypes.data, ctypes.byref(l2), ctypes.byref(m2), M.is_full.ctypes.data,
+                                  M.final_ln.ctypes.data, M.embed.ctypes.data, None, None, 1)
+        assert a == b and a >= 0
+        assert _rel(h1, h2) <= 1e-3
+
+
 def test_state_modes_agree(libs):
     """Resident states (copied in once, synced back on request) and the
     page-locked mirror give the same tokens, h and states as the default
