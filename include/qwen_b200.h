@@ -187,8 +187,10 @@ typedef void (*QbFullAttnCallback)(int layer_idx, float* h, void* py_context);
 /* Replaces forward_token_c() (qwen_kernels_opt.c:1008-1049; caller
  * qwen_real_engine.py:1262-1272): h = the bf16 embedding row of
  * token_id % 65536; 24 layers -- a full-attention layer (layer_is_full[l])
- * runs full_attn_cb on the host h (copied out, the callback may call
- * bfp8_gemv and the other drop-ins, copied back in), then forward_mlp with
+ * runs full_attn_cb on the host h (copied out; the callback may call
+ * bfp8_gemv, the lm_head and sampler drop-ins -- forward_mlp,
+ * forward_linear_layer and forward_token_c refuse to run inside it -- then
+ * copied back in), then forward_mlp with
  * mlp_plans[l]; the others forward_linear_layer with the next of
  * linear_plans; then the final rmsnorm and the lm_head argmax over the
  * 65536 embedding rows.  h stays on the device between layers; on return it

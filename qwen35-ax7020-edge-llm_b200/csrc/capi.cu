@@ -500,6 +500,9 @@ struct LoopBufs {
     size_t cap = 0;
 };
 LoopBufs g_loop;
+// Set while forward_token_c runs (its lock is released during the attention
+// callback): the layer entry points share g_loop and refuse to run inside it.
+bool g_token_busy = false;
 
 // Sized for hidden H, value width V (3 V qkv channels) and MLP width F.
 int loop_bufs(int H, int V, int F) {
@@ -665,8 +668,7 @@ void bfp8_gemv(float* y, const float* x, const int8_t* mant, const uint8_t* exps
     if (!dm || !de) return;
     if (grow_pinned(&g_ctx.h_in, &g_ctx.h_in_cap, 4 * (size_t)K) ||
         grow_pinned(&g_ctx.h_out, &g_ctx.h_out_cap, 4 * (size_t)M) ||
-        grow_dev(&g_ctx.d_in, &g_ctx.d_in_cap, 4 * (size_t)K) ||
-        grow_dev(&g_ctx.d_out, &g_ctx.d_out_cap, 4 * (size_t)M))
+        grow_dev(&g_ctx.d_in, &g_ctx.d_in_cap, 4 * (size_t)K))
         return;
     cudaStream_t s = g_ctx.stream;
     memcpy(g_ctx.h_in, x, 4 * (size_t)K);
@@ -675,7 +677,9 @@ void bfp8_gemv(float* y, const float* x, const int8_t* mant, const uint8_t* exps
     d.mant = static_cast<const int8_t*>(dm);
     d.exps = static_cast<const uint8_t*>(de);
     d.x = static_cast<const float*>(g_ctx.d_in);
-    d.y = static_cast<float*>(g_ctx.d_out);
+    // the kernel stores y straight into the pinned staging buffer (device-
+    // addressable host memory): one copy-engine round trip fewer per call
+    d.y = static_cast<float*>(g_ctx.h_out);
     d.M = M;
     d.K = K;
     DevState* dst = nullptr;
@@ -689,7 +693,6 @@ void bfp8_gemv(float* y, const float* x, const int8_t* mant, const uint8_t* exps
         fail(QB_ECUDA, "bfp8_gemv launch", e);
         return;
     }
-    cudaMemcpyAsync(g_ctx.h_out, g_ctx.d_out, 4 * (size_t)M, cudaMemcpyDeviceToHost, s);
     e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) {
         fail(QB_ECUDA, "bfp8_gemv", e);
@@ -703,6 +706,10 @@ void forward_mlp(const MlpPlanC* p, float* h) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!h) {
         fail(QB_EINVAL, "forward_mlp: null h");
+        return;
+    }
+    if (g_token_busy) {
+        fail(QB_EINVAL, "forward_mlp: called from inside forward_token_c's callback");
         return;
     }
     DevMlp w;
@@ -728,6 +735,10 @@ void forward_linear_layer(const LinearLayerPlanC* p, float* h) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!h) {
         fail(QB_EINVAL, "forward_linear_layer: null h");
+        return;
+    }
+    if (g_token_busy) {
+        fail(QB_EINVAL, "forward_linear_layer: called from inside forward_token_c's callback");
         return;
     }
     DevLinear w;
@@ -761,6 +772,7 @@ int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linear_plans
     std::unique_lock<std::mutex> lk(g_mu);
     if (!h || !linear_plans || !mlp_plans || !layer_is_full || !final_norm_w || !embed_table || token_id < 0)
         return fail(QB_EINVAL, "forward_token_c: null pointer or negative token id"), -1;
+    if (g_token_busy) return fail(QB_EINVAL, "forward_token_c: called from inside its own callback"), -1;
     if (ensure_ctx()) return name_error("forward_token_c"), -1;
     // resolve every layer first: a bad plan changes nothing
     std::vector<DevLinear> lin;
@@ -812,12 +824,14 @@ int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linear_plans
                 if (e == cudaSuccess) e = cudaStreamSynchronize(s);
                 if (e != cudaSuccess) break;
                 memcpy(h, g_loop.pin, hb);
+                g_token_busy = true;
                 lk.unlock();
                 {
                     ProfScope pc(PF_CALLBACK);
                     full_attn_cb(l, h, py_context);
                 }
                 lk.lock();
+                g_token_busy = false;
                 memcpy(g_loop.pin, h, hb);
                 e = cudaMemcpyAsync(g_loop.h, g_loop.pin, hb, cudaMemcpyHostToDevice, s);
                 if (e != cudaSuccess) break;

@@ -141,6 +141,35 @@ def test_token_loop_without_callback(libs):
         assert _rel(h1, h2) <= 1e-3
 
 
+def test_layer_calls_inside_the_callback_are_refused(libs):
+    """The callback runs with the library unlocked; a forward_mlp call from
+    inside it is refused (it would overwrite the loop's device buffers) and
+    the token is still the oracle's."""
+    lib, orc = libs
+    M = LF.TokenModel(seed=7)
+    st1, st2 = M.fresh_states(), M.fresh_states()
+    (l1, m1), (l2, m2) = M.plans(st1), M.plans(st2)
+    stand_in = LF.attention_stand_in()
+    mp = M.mlp_w.plan()
+    seen = []
+
+    def cb(layer, h_ptr, ctx):
+        lib.forward_mlp(ctypes.byref(mp), h_ptr)
+        seen.append(lib.qwen_b200_last_error())
+        stand_in(layer, h_ptr, ctx)
+
+    ccb = LF.CALLBACK(cb)
+    h1 = np.zeros(LF.HIDDEN, np.float32)
+    h2 = np.zeros(LF.HIDDEN, np.float32)
+    a = lib.forward_token_c(77, h1.ctypes.data, ctypes.byref(l1), ctypes.byref(m1), M.is_full.ctypes.data,
+                            M.final_ln.ctypes.data, M.embed.ctypes.data, ccb, None)
+    b = orc.orc_forward_token(77, h2.ctypes.data, ctypes.byref(l2), ctypes.byref(m2), M.is_full.ctypes.data,
+                              M.final_ln.ctypes.data, M.embed.ctypes.data, ctypes.cast(stand_in, ctypes.c_void_p),
+                              None, 1)
+    assert len(seen) == 6 and all(b"inside forward_token_c" in e for e in seen)
+    assert a == b and _rel(h1, h2) <= 1e-3
+
+
 def test_state_modes_agree(libs):
     """Resident states (copied in once, synced back on request) and the
     page-locked mirror give the same tokens, h and states as the default
