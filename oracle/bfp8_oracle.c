@@ -770,7 +770,7 @@ static void orc_rmsnorm(float* y, const float* x, const float* w, int n, int neo
 /* forward_mlp (qwen_kernels_opt.c:994-1004): h += down(swiglu(gate(n), up(n))),
  * n = rmsnorm(h, post_ln_w). */
 ORC_API void orc_forward_mlp(const OrcMlpPlan* p, float* h, int neon) {
-    const int H = kOrcHidden, F = p->M_gate;
+    const int H = p->K_gate, F = p->M_gate;   /* the reference hard-codes 1024 / 3584 */
     float* n = (float*)malloc(sizeof(float) * H);
     float* g = (float*)malloc(sizeof(float) * F);
     float* u = (float*)malloc(sizeof(float) * F);
@@ -790,13 +790,15 @@ ORC_API void orc_forward_mlp(const OrcMlpPlan* p, float* h, int neon) {
  * q, k = the first two thirds, l2-normalised; gates from n; the recurrent
  * step; z GEMV; rmsnorm_gated; o GEMV; h += o; then forward_mlp's steps. */
 ORC_API void orc_forward_linear_layer(const OrcLinearPlan* p, float* h, int neon) {
-    const int H = kOrcHidden, NH = kOrcHeads, D = kOrcHeadDim, V = NH * D;
+    /* shapes from the plan (the reference hard-codes 1024 / 16 heads x 128) */
+    const int H = p->K_qkv, D = kOrcHeadDim, V = p->M_z, NH = V / D;
     float* n = (float*)malloc(sizeof(float) * H);
     float* qkv = (float*)malloc(sizeof(float) * p->M_qkv);
     /* zeroed: the reference's workspace is a zero-initialised static, and its
      * portable build's conv never writes the channels below C & ~3 */
     float* mixed = (float*)calloc((size_t)p->M_qkv, sizeof(float));
-    float alpha[kOrcHeads], beta[kOrcHeads];
+    float* alpha = (float*)malloc(sizeof(float) * NH);
+    float* beta = (float*)malloc(sizeof(float) * NH);
     float* attn = (float*)malloc(sizeof(float) * V);
     float* z = (float*)malloc(sizeof(float) * p->M_z);
     float* gated = (float*)malloc(sizeof(float) * V);
@@ -814,7 +816,7 @@ ORC_API void orc_forward_linear_layer(const OrcLinearPlan* p, float* h, int neon
     OrcMlpPlan m = {p->post_ln_w, p->mant_gate, p->exp_gate, p->M_gate, p->K_gate, p->mant_up, p->exp_up,
                     p->M_up, p->K_up, p->mant_down, p->exp_down, p->M_down, p->K_down};
     orc_forward_mlp(&m, h, neon);
-    free(n); free(qkv); free(mixed); free(attn); free(z); free(gated); free(o);
+    free(n); free(qkv); free(mixed); free(attn); free(z); free(gated); free(o); free(alpha); free(beta);
 }
 
 typedef void (*OrcFullAttnCallback)(int layer, float* h, void* ctx);

@@ -52,17 +52,18 @@ def bfp8_matrix(rng, M, K):
 
 
 class Mlp:
-    def __init__(self, rng):
-        self.post_ln = rng.normal(0, 0.1, HIDDEN).astype(np.float32)
-        self.gate = bfp8_matrix(rng, FFN, HIDDEN)
-        self.up = bfp8_matrix(rng, FFN, HIDDEN)
-        self.down = bfp8_matrix(rng, HIDDEN, FFN)
+    def __init__(self, rng, hidden=HIDDEN, ffn=FFN):
+        self.hidden, self.ffn = hidden, ffn
+        self.post_ln = rng.normal(0, 0.1, hidden).astype(np.float32)
+        self.gate = bfp8_matrix(rng, ffn, hidden)
+        self.up = bfp8_matrix(rng, ffn, hidden)
+        self.down = bfp8_matrix(rng, hidden, ffn)
 
     def plan(self) -> MlpPlanC:
         p = MlpPlanC()
         p.post_ln_w = self.post_ln.ctypes.data
-        for name, buf, M, K in (("gate", self.gate, FFN, HIDDEN), ("up", self.up, FFN, HIDDEN),
-                                ("down", self.down, HIDDEN, FFN)):
+        H, F = self.hidden, self.ffn
+        for name, buf, M, K in (("gate", self.gate, F, H), ("up", self.up, F, H), ("down", self.down, H, F)):
             setattr(p, "mant_" + name, buf.ctypes.data)
             setattr(p, "exp_" + name, buf.ctypes.data + M * K)
             setattr(p, "M_" + name, M)
@@ -75,20 +76,22 @@ class Linear:
     mutable states; copy_states() gives an independent set for another
     implementation."""
 
-    def __init__(self, rng, mlp: Mlp | None = None):
-        self.in_ln = rng.normal(0, 0.1, HIDDEN).astype(np.float32)
-        self.qkv = bfp8_matrix(rng, 3 * V, HIDDEN)
-        self.z = bfp8_matrix(rng, V, HIDDEN)
-        self.o = bfp8_matrix(rng, HIDDEN, V)
-        self.conv_w = rng.normal(0, 0.3, (3 * V, 4)).astype(np.float32)
-        self.wa = rng.normal(0, 0.03, (HEADS, HIDDEN)).astype(np.float32)
-        self.wb = rng.normal(0, 0.03, (HEADS, HIDDEN)).astype(np.float32)
-        self.nea = (-np.exp(rng.uniform(0.0, 1.5, HEADS))).astype(np.float32)
-        self.dt = rng.uniform(-1.0, 1.0, HEADS).astype(np.float32)
+    def __init__(self, rng, mlp: Mlp | None = None, hidden=HIDDEN, heads=HEADS, ffn=FFN):
+        self.hidden, self.heads = hidden, heads
+        v = self.v = heads * HEAD_DIM
+        self.in_ln = rng.normal(0, 0.1, hidden).astype(np.float32)
+        self.qkv = bfp8_matrix(rng, 3 * v, hidden)
+        self.z = bfp8_matrix(rng, v, hidden)
+        self.o = bfp8_matrix(rng, hidden, v)
+        self.conv_w = rng.normal(0, 0.3, (3 * v, 4)).astype(np.float32)
+        self.wa = rng.normal(0, 0.03, (heads, hidden)).astype(np.float32)
+        self.wb = rng.normal(0, 0.03, (heads, hidden)).astype(np.float32)
+        self.nea = (-np.exp(rng.uniform(0.0, 1.5, heads))).astype(np.float32)
+        self.dt = rng.uniform(-1.0, 1.0, heads).astype(np.float32)
         self.norm_w = rng.normal(1.0, 0.1, HEAD_DIM).astype(np.float32)
-        self.mlp = mlp if mlp is not None else Mlp(rng)
-        self.conv_s = rng.normal(0, 0.5, (3, 3 * V)).astype(np.float32)
-        self.state = rng.normal(0, 0.05, (HEADS, HEAD_DIM * HEAD_DIM)).astype(np.float32)
+        self.mlp = mlp if mlp is not None else Mlp(rng, hidden, ffn)
+        self.conv_s = rng.normal(0, 0.5, (3, 3 * v)).astype(np.float32)
+        self.state = rng.normal(0, 0.05, (heads, HEAD_DIM * HEAD_DIM)).astype(np.float32)
 
     def copy_states(self):
         return self.conv_s.copy(), self.state.copy()
@@ -98,8 +101,8 @@ class Linear:
         state = self.state if state is None else state
         p = LinearLayerPlanC()
         p.in_ln_w = self.in_ln.ctypes.data
-        for name, buf, M, K in (("qkv", self.qkv, 3 * V, HIDDEN), ("z", self.z, V, HIDDEN),
-                                ("o", self.o, HIDDEN, V)):
+        H, v = self.hidden, self.v
+        for name, buf, M, K in (("qkv", self.qkv, 3 * v, H), ("z", self.z, v, H), ("o", self.o, H, v)):
             setattr(p, "mant_" + name, buf.ctypes.data)
             setattr(p, "exp_" + name, buf.ctypes.data + M * K)
             setattr(p, "M_" + name, M)

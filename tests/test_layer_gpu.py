@@ -100,6 +100,22 @@ def test_linear_layer_matches_neon_oracle_over_calls(libs):
     assert not np.array_equal(s1, L.state)
 
 
+def test_linear_layer_other_shape(libs):
+    """A layer shape other than the 0.8B model's (the reference hard-codes
+    1024 / 16 heads; this library takes the shape from the plan): hidden 2048,
+    8 heads, ffn 2048 -- states bit-exact with libm-free gates, h to 1e-4."""
+    lib, orc = libs
+    rng = np.random.default_rng(24)
+    L = LF.Linear(rng, hidden=2048, heads=8, ffn=2048)
+    L.nea[:] = 0.0
+    L.wb[:] = 0.0
+    h = rng.normal(0, 1, 2048).astype(np.float32)
+    (h1, c1, s1), (h2, c2, s2) = _run_layer(lib, orc, L, h, calls=1)
+    assert not np.array_equal(h1, h), lib.qwen_b200_last_error()
+    assert np.array_equal(c1, c2) and np.array_equal(s1.view(np.uint32), s2.view(np.uint32))
+    assert _rel(h1, h2) <= 1e-4
+
+
 def test_token_loop_matches_neon_oracle(libs):
     lib, orc = libs
     M = LF.TokenModel(seed=3)
