@@ -682,7 +682,7 @@ def run_chain(torch, dev, barrier, hbm_peak, peak_kind, steps, warm):
 
 # ------------------------------------------------------------------ token loop
 TOKEN_METRIC = "forward_token_c ms/token: Qwen3.5-0.8B shape, 24 layers + lm_head argmax, drop-in C ABI"
-TOKEN_LAUNCHES = 18 * 6 + 6 * 3 + 3   # per token: linear layers, full-attention MLPs, embed / rmsnorm / lm_head
+TOKEN_LAUNCHES = 18 * 5 + 6 * 2 + 3   # per token: linear layers, full-attention MLPs, embed / rmsnorm / lm_head
 
 
 def _token_loop(fwd, M, lps, mps, cb, h, first, n):

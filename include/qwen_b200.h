@@ -153,9 +153,9 @@ typedef struct {
 /* Replaces forward_mlp() (qwen_kernels_opt.c:994-1003; caller
  * qwen_real_engine.py:1152-1153): h += down(swiglu(gate(n), up(n))) with
  * n = rmsnorm(h, post_ln_w, 1e-6) -- the reference's NEON-build rmsnorm,
- * GEMVs, swiglu and add_residual, bit for bit -- as three launches on the
- * device (gate and up together with the rmsnorm in front, swiglu in front of
- * down, the residual add); h (host, K_gate floats) is copied in and back, weight and
+ * GEMVs, swiglu and add_residual, bit for bit -- as two launches on the
+ * device (gate and up together with the rmsnorm in front; down with swiglu
+ * in front and the residual add folded into its stores); h (host, K_gate floats) is copied in and back, weight and
  * norm pointers are translated like bfp8_gemv's.  K_gate == K_up <= 6144,
  * M_gate == M_up == K_down, M_down == K_gate, multiples of 512.  On error h
  * is unchanged and qwen_b200_last_error() says why. */
@@ -163,10 +163,11 @@ QB_API void forward_mlp(const MlpPlanC* p, float* h);
 
 /* Replaces forward_linear_layer() (qwen_kernels_opt.c:938-992; caller
  * qwen_real_engine.py:1096): one Gated-DeltaNet layer on the device in
- * six launches -- the qkv and z projections of rmsnorm(h, in_ln_w)
+ * five launches -- the qkv and z projections of rmsnorm(h, in_ln_w)
  * (one launch), one kernel for conv1d + SiLU, q/k l2 norm, the gates, the
  * recurrent step and rmsnorm_gated (one CTA per head), the out projection,
- * then the MLP with h + o formed in front of its gate and up projections.  NEON-build
+ * then the MLP with h + o formed in front of its gate and up projections
+ * and the down rows added into it as they are stored.  NEON-build
  * order throughout (the GEMVs bit for bit); the gates and the gated norm's
  * SiLU use CUDA's expf / log1pf where the reference calls the C library's.
  * Shapes: K_qkv == K_z == M_o == K_gate <= 6144 (a multiple of 512),

@@ -187,6 +187,10 @@ struct WArgs {
     // normalized vector in one launch (second_begin 0: none)
     int second_begin;
     GemvDesc second;
+    // split kernel only: y is the residual stream, updated in place with the
+    // reference's add_residual arithmetic (y[i] += result: flushed lane adds
+    // for i below M & ~3, IEEE adds for the tail)
+    int res_epi;
 };
 
 __device__ __forceinline__ const GemvDesc& wdesc(const WArgs& A, int d) {
@@ -954,7 +958,12 @@ __global__ void __launch_bounds__(kThreads, SPW == 1 ? 2 : 1) gemv_split_kernel(
             } else {
                 for (int b = 0; b < nb; b++) fo = add_rn(fo, T[b * 128 + lane]);
             }
-            if (row_ok) D.y[r0 + lane] = odd ? fo : add_ftz(add_ftz(f0, f2), add_ftz(f1, f3));
+            if (row_ok) {
+                const float v = odd ? fo : add_ftz(add_ftz(f0, f2), add_ftz(f1, f3));
+                const int i = r0 + lane;
+                // add_residual (qwen_kernels_opt.c:388-396) folded into the store
+                D.y[i] = !A.res_epi ? v : (i < (M & ~3) ? add_ftz(D.y[i], v) : __fadd_rn(D.y[i], v));
+            }
         }
         __syncthreads();   // the next unit's stages overwrite the terms
     }
@@ -1516,7 +1525,7 @@ cudaError_t launch_rmsnorm_gemv2(const GemvDesc& d0, const GemvDesc& d1, const f
 }
 
 cudaError_t launch_swiglu_gemv(const GemvDesc& d0, const float* up, uint32_t* act, unsigned int* err,
-                               cudaStream_t stream) {
+                               cudaStream_t stream, bool residual) {
     if (d0.M <= 0) return cudaSuccess;
     GemvDesc d = d0;
     GemvPlan plan;
@@ -1525,6 +1534,7 @@ cudaError_t launch_swiglu_gemv(const GemvDesc& d0, const float* up, uint32_t* ac
         return cudaErrorInvalidValue;
     WArgs A{};
     A.res_act = 1;
+    A.res_epi = residual ? 1 : 0;
     A.glu_up = up;
     A.single = d;
     A.n = 1;

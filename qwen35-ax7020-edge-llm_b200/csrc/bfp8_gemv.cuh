@@ -112,9 +112,11 @@ cudaError_t launch_rmsnorm_gemv2(const GemvDesc& d0, const GemvDesc& d1, const f
 // One exact GEMV of swiglu(gate, up) (the reference's NEON swiglu, then its
 // quantizer and GEMV; d.x holds the gate projection) in one launch: every
 // CTA applies swiglu and quantizes itself.  K <= 6144, a multiple of 512;
-// aligned pointers (up 8-byte).
+// aligned pointers (up 8-byte).  With `residual`, d.y is the residual stream
+// and receives y += result (the reference's add_residual after the down
+// projection), in place, instead of the result.
 cudaError_t launch_swiglu_gemv(const GemvDesc& d, const float* up, uint32_t* act, unsigned int* err,
-                               cudaStream_t stream);
+                               cudaStream_t stream, bool residual = false);
 
 // Fast-mode single GEMV (K % 512 == 0, aligned pointers); `act` holds
 // act_cap_words words of scratch, `tickets` tickets_cap zeroed counters

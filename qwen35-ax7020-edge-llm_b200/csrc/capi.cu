@@ -492,7 +492,7 @@ int loop_events(size_t n) {
 // Work buffers of the device layer loop (the entry points are serialised).
 struct LoopBufs {
     float *h = nullptr, *h2 = nullptr, *qkv = nullptr, *z = nullptr, *gated = nullptr, *o = nullptr,
-          *gate = nullptr, *up = nullptr, *down = nullptr, *norm = nullptr;
+          *gate = nullptr, *up = nullptr, *norm = nullptr;
     int* res = nullptr;
     void* pin = nullptr;   // pinned staging of h and the token id
     size_t pin_cap = 0;
@@ -507,7 +507,7 @@ bool g_token_busy = false;
 // Sized for hidden H, value width V (3 V qkv channels) and MLP width F.
 int loop_bufs(int H, int V, int F) {
     auto al = [](size_t n) { return (n * sizeof(float) + 255) & ~size_t(255); };
-    const size_t need = 4 * al(H) + al(3 * (size_t)V) + 2 * al(V) + al(H) + 2 * al(F) + 256;
+    const size_t need = 3 * al(H) + al(3 * (size_t)V) + 2 * al(V) + al(H) + 2 * al(F) + 256;
     if (int rc = grow_dev(&g_loop.block, &g_loop.cap, need)) return rc;
     if (int rc = grow_pinned(&g_loop.pin, &g_loop.pin_cap, (size_t)H * 4 + 64)) return rc;
     unsigned char* b = static_cast<unsigned char*>(g_loop.block);
@@ -519,7 +519,6 @@ int loop_bufs(int H, int V, int F) {
     g_loop.h = take(H);
     g_loop.h2 = take(H);
     g_loop.o = take(H);
-    g_loop.down = take(H);
     g_loop.qkv = take(3 * (size_t)V);
     g_loop.z = take(V);
     g_loop.gated = take(V);
@@ -543,25 +542,25 @@ qb::GemvDesc gemv_desc(const DevGemv& g, const float* x, float* y) {
 
 // forward_mlp's steps on the device: h += down(swiglu(gate(n), up(n))),
 // n = rmsnorm(h) -- gate and up in one launch with the rmsnorm in front,
-// swiglu in front of down, then the residual add (three launches).  With `res`, the layer's
+// then down with swiglu in front and the residual add folded into its
+// stores (two launches).  With `res`, the layer's
 // pending residual h + res is formed in front of gate (h_out = h + res) and
 // the MLP runs on h_out; h_out then holds the result.
 cudaError_t mlp_launch(const DevMlp& w, float* h, const float* res, float* h_out, DevState* st, cudaStream_t s) {
-    const int H = w.gate.K;
     // gate and up projections of the same rmsnorm(h) (or of h + res) in one launch
     cudaError_t e = qb::launch_rmsnorm_gemv2(gemv_desc(w.gate, h, g_loop.gate), gemv_desc(w.up, h, g_loop.up),
                                              w.post_ln, 1e-6f, st->act, st->err, s, res, res ? h_out : nullptr);
     float* hh = res ? h_out : h;
+    // down projection of swiglu(gate, up), its rows added into the residual stream as they are stored
     if (e == cudaSuccess)
-        e = qb::launch_swiglu_gemv(gemv_desc(w.down, g_loop.gate, g_loop.down), g_loop.up, st->act, st->err, s);
-    if (e == cudaSuccess) e = qb::launch_add_residual(hh, g_loop.down, H, s);
+        e = qb::launch_swiglu_gemv(gemv_desc(w.down, g_loop.gate, hh), g_loop.up, st->act, st->err, s, true);
     return e;
 }
 
-// forward_linear_layer's steps on the device (six launches): the qkv and z
+// forward_linear_layer's steps on the device (five launches): the qkv and z
 // projections of rmsnorm(h) (one launch), the Gated-DeltaNet kernel, the out
 // projection, then the MLP with h + o formed in front of its gate and up
-// projections.  The result lands in g_loop.h2.
+// projections and the down rows added into it.  The result lands in g_loop.h2.
 cudaError_t linear_launch(const DevLinear& w, float* h, float* dev_conv, float* dev_state, DevState* st,
                           cudaStream_t s) {
     // qkv and z projections of the same rmsnorm(h) in one launch
