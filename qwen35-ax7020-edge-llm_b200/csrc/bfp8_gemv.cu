@@ -179,6 +179,7 @@ struct WArgs {
     float norm_eps;
     const float* norm_res;  // with norm_w: x + norm_res is normalized (nullptr: x) ...
     float* norm_xout;       // ... and CTA 0 stores x + norm_res there (the updated residual stream)
+    float* norm_out;        // with norm_w: CTA 0 also stores the normalized vector there (nullptr: not)
     unsigned int* rtl_flags;   // RTL mode: sticky flags word (may be null)
     const float* glu_up;    // res_act only: the activation is swiglu(x, glu_up) (nullptr: x)
     SyncArgs sync;          // row-sharded stacks: completion signal (sig_epoch 0: none)
@@ -537,6 +538,8 @@ __device__ __forceinline__ void quantize_resident(const WArgs& A, const GemvDesc
                             reinterpret_cast<const float2*>(A.norm_w + 64 * (b0 + j * kWarps))[lane];
                         v[j].x = mul_ftz(v[j].x, mul_ftz(nr, add_ftz(1.0f, w.x)));
                         v[j].y = mul_ftz(v[j].y, mul_ftz(nr, add_ftz(1.0f, w.y)));
+                        if (A.norm_out && blockIdx.x == 0)
+                            reinterpret_cast<float2*>(A.norm_out + 64 * (b0 + j * kWarps))[lane] = v[j];
                     }
             }
         }
@@ -1487,7 +1490,7 @@ cudaError_t launch_rmsnorm_gemv(const GemvDesc& d0, const float* norm_w, float e
 
 cudaError_t launch_rmsnorm_gemv2(const GemvDesc& d0, const GemvDesc& d1, const float* norm_w, float eps,
                                 uint32_t* act, unsigned int* err, cudaStream_t stream, const float* res,
-                                float* x_out) {
+                                float* x_out, float* norm_out) {
     if (d0.M <= 0 || d1.M <= 0 || d0.K != d1.K || d0.x != d1.x) return cudaErrorInvalidValue;
     GemvDesc e1 = d1;
     GemvPlan p1;
@@ -1514,6 +1517,7 @@ cudaError_t launch_rmsnorm_gemv2(const GemvDesc& d0, const GemvDesc& d1, const f
     A.norm_eps = eps;
     A.norm_res = res;
     A.norm_xout = x_out;
+    A.norm_out = norm_out;
     A.single = e0;
     A.n = 1;
     A.second = e1;

@@ -104,10 +104,12 @@ cudaError_t launch_rmsnorm_gemv(const GemvDesc& d, const float* norm_w, float ep
 
 // Two exact GEMVs of the same rmsnorm(x) (or of x + res, stored to x_out) in
 // one launch -- d0 and d1 share x and K (a layer's qkv and z projections, an
-// MLP's gate and up); the same conditions as launch_rmsnorm_gemv.
+// MLP's gate and up); the same conditions as launch_rmsnorm_gemv.  With
+// norm_out, the normalized vector itself (the reference's rmsnorm output) is
+// stored there too, 8-byte aligned.
 cudaError_t launch_rmsnorm_gemv2(const GemvDesc& d0, const GemvDesc& d1, const float* norm_w, float eps,
                                 uint32_t* act, unsigned int* err, cudaStream_t stream, const float* res = nullptr,
-                                float* x_out = nullptr);
+                                float* x_out = nullptr, float* norm_out = nullptr);
 
 // One exact GEMV of swiglu(gate, up) (the reference's NEON swiglu, then its
 // quantizer and GEMV; d.x holds the gate projection) in one launch: every

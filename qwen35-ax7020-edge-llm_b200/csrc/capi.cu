@@ -563,15 +563,15 @@ cudaError_t mlp_launch(const DevMlp& w, float* h, const float* res, float* h_out
 // projections and the down rows added into it.  The result lands in g_loop.h2.
 cudaError_t linear_launch(const DevLinear& w, float* h, float* dev_conv, float* dev_state, DevState* st,
                           cudaStream_t s) {
-    // qkv and z projections of the same rmsnorm(h) in one launch
+    // qkv and z projections of the same rmsnorm(h) in one launch, which also
+    // leaves the normalized vector for the gates
     cudaError_t e = qb::launch_rmsnorm_gemv2(gemv_desc(w.qkv, h, g_loop.qkv), gemv_desc(w.z, h, g_loop.z), w.in_ln,
-                                             1e-6f, st->act, st->err, s);
+                                             1e-6f, st->act, st->err, s, nullptr, nullptr, g_loop.norm);
     if (e == cudaSuccess) {
         qb::GdnArgs a{};
         a.qkv = g_loop.qkv;
         a.z = g_loop.z;
-        a.h = h;
-        a.in_ln_w = w.in_ln;
+        a.normed = g_loop.norm;
         a.conv_w = w.conv_w;
         a.conv_s = dev_conv;
         a.wa = w.wa;

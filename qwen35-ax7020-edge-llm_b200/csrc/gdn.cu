@@ -4,8 +4,9 @@
 // gdn_layer_kernel: one CTA per head.  Four column warps -- thread j owns
 // channel j of the head's q, k and v and column j of its 128 x 128 state --
 // and one gate warp, which computes the head's alpha and beta (two
-// hidden-long dot products in the reference's four-lane order, the longest
-// dependent chains of the step) beside the column work.  Float semantics are
+// hidden-long dot products of the layer's normalized input in the
+// reference's four-lane order, the longest dependent chains of the step)
+// beside the column work.  Float semantics are
 // the reference's NEON build (qwen_kernels_opt.c:507-858): vector steps
 // flushed (mul/add/sub_ftz), multiply-accumulate not fused, every vector dot
 // product four lane chains over i = 4m + l combined as (s0 + s2) + (s1 + s3),
@@ -46,7 +47,7 @@ __device__ __forceinline__ float dot4_pair(const float* a0, const float* b0, con
 __device__ __forceinline__ float recip_sqrt_ieee(float x) { return __fdiv_rn(1.0f, __fsqrt_rn(x)); }
 
 __global__ void __launch_bounds__(kThreads) gdn_layer_kernel(const GdnArgs a) {
-    extern __shared__ float gdn_smem[];   // x | wa row | wb row | in_ln_w (hidden floats each)
+    extern __shared__ float gdn_smem[];   // normed | wa row | wb row (hidden floats each)
     __shared__ float sq[kD], sk[kD], sv[kD], so[kD];
     __shared__ float s_kr, s_qr, s_qk, s_rg, s_alpha, s_beta;
     const int hd = blockIdx.x, t = threadIdx.x;
@@ -136,32 +137,28 @@ __global__ void __launch_bounds__(kThreads) gdn_layer_kernel(const GdnArgs a) {
         const float silu = __fdiv_rn(zt, __fadd_rn(1.0f, expf(-zt)));
         a.out[hd * kD + t] = __fmul_rn(__fmul_rn(__fmul_rn(so[t], s_rg), nw), silu);
     } else {
-        // ---- gate warp: n = rmsnorm(h, in_ln_w) (NEON build, the layer's own
-        // step 1), then gdn_gates (qwen_kernels_opt.c:593-625) for this head:
-        // av = wa . n, bv = wb . n; beta = 1 / (1 + expf(-bv));
-        // alpha = expf(nea * log1pf(expf(av + dt)))
+        // ---- gate warp: gdn_gates (qwen_kernels_opt.c:593-625) for this head
+        // from n = the layer's rmsnorm(h, in_ln_w): av = wa . n, bv = wb . n;
+        // beta = 1 / (1 + expf(-bv)); alpha = expf(nea * log1pf(expf(av + dt)))
         const int lane = t - kColThreads, H = a.hidden;
         float* sx = gdn_smem;
         float* swa = gdn_smem + H;
         float* swb = gdn_smem + 2 * H;
-        float* sln = gdn_smem + 3 * H;
         const float* wa = a.wa + (size_t)hd * H;
         const float* wb = a.wb + (size_t)hd * H;
-        // stage h, the head's wa / wb rows and in_ln_w; every load of a lane
-        // goes out before the first store (16-byte loads where all four
-        // sources allow them)
-        if (((reinterpret_cast<uintptr_t>(a.h) | reinterpret_cast<uintptr_t>(wa) | reinterpret_cast<uintptr_t>(wb) |
-              reinterpret_cast<uintptr_t>(a.in_ln_w)) & 15) == 0) {
+        // stage n and the head's wa / wb rows; every load of a lane goes out
+        // before the first store (16-byte loads where all three allow them)
+        if (((reinterpret_cast<uintptr_t>(a.normed) | reinterpret_cast<uintptr_t>(wa) |
+              reinterpret_cast<uintptr_t>(wb)) & 15) == 0) {
             for (int i0 = lane; i0 < H / 4; i0 += 32 * 4) {
-                float4 v[4][4];
+                float4 v[4][3];
 #pragma unroll
                 for (int u = 0; u < 4; u++) {
                     const int i = i0 + 32 * u;
                     if (i < H / 4) {
-                        v[u][0] = reinterpret_cast<const float4*>(a.h)[i];
+                        v[u][0] = reinterpret_cast<const float4*>(a.normed)[i];
                         v[u][1] = reinterpret_cast<const float4*>(wa)[i];
                         v[u][2] = reinterpret_cast<const float4*>(wb)[i];
-                        v[u][3] = reinterpret_cast<const float4*>(a.in_ln_w)[i];
                     }
                 }
 #pragma unroll
@@ -171,26 +168,18 @@ __global__ void __launch_bounds__(kThreads) gdn_layer_kernel(const GdnArgs a) {
                         reinterpret_cast<float4*>(sx)[i] = v[u][0];
                         reinterpret_cast<float4*>(swa)[i] = v[u][1];
                         reinterpret_cast<float4*>(swb)[i] = v[u][2];
-                        reinterpret_cast<float4*>(sln)[i] = v[u][3];
                     }
                 }
             }
         } else {
 #pragma unroll 8
             for (int i = lane; i < H; i += 32) {
-                const float x = a.h[i], ya = wa[i], yb = wb[i], l = a.in_ln_w[i];
+                const float x = a.normed[i], ya = wa[i], yb = wb[i];
                 sx[i] = x;
                 swa[i] = ya;
                 swb[i] = yb;
-                sln[i] = l;
             }
         }
-        __syncwarp();
-        const float ss = dot4_pair(sx, sx, sx, sx, H, lane);
-        float r = 0.0f;
-        if (lane == 0) r = recip_sqrt_ieee(__fadd_rn(__fdiv_rn(ss, (float)H), 1e-6f));
-        r = __shfl_sync(0xffffffffu, r, 0);
-        for (int i = lane; i < H; i += 32) sx[i] = mul_ftz(sx[i], mul_ftz(r, add_ftz(1.0f, sln[i])));
         __syncwarp();
         const float g = dot4_pair(swa, sx, swb, sx, H, lane);   // lane 0: av, lane 4: bv
         const float bv = __shfl_sync(0xffffffffu, g, 4);
@@ -224,11 +213,11 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* y, const float* x, 
 }  // namespace
 
 cudaError_t launch_gdn_layer(const GdnArgs& a, cudaStream_t stream) {
-    if (a.heads <= 0 || a.hidden <= 0 || a.hidden % 4 || a.hidden > kGdnMaxHidden || !a.qkv || !a.z || !a.h ||
-        !a.in_ln_w || !a.conv_w || !a.conv_s || !a.wa || !a.wb || !a.nea || !a.dt || !a.state || !a.norm_w || !a.out)
+    if (a.heads <= 0 || a.hidden <= 0 || a.hidden % 4 || a.hidden > kGdnMaxHidden || !a.qkv || !a.z || !a.normed ||
+        !a.conv_w || !a.conv_s || !a.wa || !a.wb || !a.nea || !a.dt || !a.state || !a.norm_w || !a.out)
         return cudaErrorInvalidValue;
     if (reinterpret_cast<uintptr_t>(a.state) % 16) return cudaErrorInvalidValue;
-    const size_t smem = 4 * (size_t)a.hidden * sizeof(float);
+    const size_t smem = 3 * (size_t)a.hidden * sizeof(float);
     if (cudaError_t e = raise_smem_limit(reinterpret_cast<const void*>(gdn_layer_kernel), smem)) return e;
     gdn_layer_kernel<<<a.heads, kThreads, smem, stream>>>(a);
     return cudaGetLastError();

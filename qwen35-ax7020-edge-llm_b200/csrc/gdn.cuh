@@ -13,7 +13,8 @@ constexpr int kGdnMaxHidden = 6144;
 // the qkv / z projections and the out projection, one CTA per head:
 //   conv1d + SiLU over the head's q, k and v channels (the conv state
 //   shifts), q / k l2-normalised, the head's gates alpha / beta from
-//   rmsnorm(h, in_ln_w), the recurrent step (the state is updated in place),
+//   `normed` (the layer's rmsnorm(h, in_ln_w), stored by the qkv projection
+//   launch), the recurrent step (the state is updated in place),
 //   rmsnorm_gated with z -> out.
 // Arithmetic and order are the reference's NEON build; alpha, beta and the
 // SiLU of z use CUDA's expf / log1pf where the reference calls the C
@@ -24,8 +25,7 @@ constexpr int kGdnMaxHidden = 6144;
 struct GdnArgs {
     const float* qkv;
     const float* z;
-    const float* h;
-    const float* in_ln_w;
+    const float* normed;
     const float* conv_w;
     float* conv_s;
     const float* wa;
