@@ -910,7 +910,7 @@ def run_sharded_records(args, torch, dist, dev, barrier, world, rank, local, hbm
     out = {}
     for key, B, ex in (("b1_peer", 1, "peer"), ("b1_nccl", 1, "nccl"), ("b64_peer", 64, "peer")):
         out[key] = run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, peak_kind, B, ex,
-                               10, 3, check_parity=True)
+                               20, 3, check_parity=True)
         torch.cuda.empty_cache()
     return out
 
@@ -935,8 +935,23 @@ def run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, p
     copies = args.copies or max(1, math.ceil(L2_DEFEAT_BYTES / (full_w / world)))
     st = sharded.ShardedDeviceStack(layers, world, rank, dev, copies=copies, seed=11, fast=True, exchange=exchange,
                                     batch=B)
+    graphs = None
+    if st.capturable():
+        # every plan runs once eagerly, then every rank captures one graph
+        # per weight copy (nothing runs while capturing: the barriers keep a
+        # rank's replays from waiting on a peer that is still capturing)
+        for c in range(copies):
+            st.step(c)
+        torch.cuda.synchronize()
+        barrier()
+        graphs = [st.capture(c) for c in range(copies)]
+        torch.cuda.synchronize()
+        barrier()
+        step = lambda i: graphs[i % copies].replay()   # noqa: E731
+    else:
+        step = lambda i: st.step(i % copies)   # noqa: E731
     clk = ClockSampler(gpu_uuid(torch, dev), local)
-    secs = timed(torch, lambda i: st.step(i % copies), steps, warmup, barrier)
+    secs = timed(torch, step, steps, warmup, barrier)
     clocks = clk.stop()
     per_step = max_over_ranks(torch, dist, secs, dev, world) / steps
     nbytes = st.bytes_per_step()
@@ -965,6 +980,9 @@ def run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, p
             ref.close()
             del ref
         barrier()
+    launch_kind = ("one CUDA graph per weight copy (epochs offsets from a device counter)" if graphs is not None
+                   else "eager launches from Python, NCCL between them")
+    del graphs, step
     st.close()
     del st
     per_rank_gbs = nbytes / world / per_step / 1e9
@@ -979,13 +997,16 @@ def run_sharded(args, torch, dist, dev, barrier, world, rank, local, hbm_peak, p
                                      "shard-local, int16 activation and fp32 down rows to every GPU by " + (
                                          "the kernels' NVLink stores, epoch flags between launches"
                                          if exchange == "peer" else "NCCL all-gathers"),
-                      "l2": f"rotates {copies} copies of this rank's {full_w / world / 1e9:.2f} GB"},
+                      "l2": f"rotates {copies} copies of this rank's {full_w / world / 1e9:.2f} GB",
+                      "launch": launch_kind},
            "roofline": {"bound": "hbm", "achieved": round(per_rank_gbs, 2), "peak": hbm_peak, "unit": "GB/s",
                         "frac": round(per_rank_gbs / hbm_peak, 4), "peak_kind": peak_kind, "traffic": None,
                         "kernel": ("gemv_warp_kernel" if B == 1 else "gemm_tc_kernel") +
                                   " per rank (per-rank GB/s incl. the exchange)"},
            # per layer: gate/up (quantizer + GEMV), activation, down (quantizer + GEMV / GEMM); NCCL not counted
-           "gpu_launches": steps * len(layers) * (5 if B == 1 else 4),
+           # (+ the epoch counter's advance per step with peer stores)
+           "gpu_launches": steps * (len(layers) * (5 if B == 1 else 4) +
+                                    (1 if exchange == "peer" and world > 1 else 0)),
            "exchange": exchange, "parity": parity, "clocks": clocks}
     if err:
         rec["device_error"] = err

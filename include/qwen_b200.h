@@ -415,6 +415,22 @@ QB_API int qwen_b200_swiglu_quant_sharded_dev(const float* gate, const float* up
                                               unsigned int* const* sig_flags, unsigned int* sig_ticket,
                                               unsigned int sig_epoch, const unsigned int* wait_flags, int world,
                                               int rank, void* stream);
+/* Epochs relative to a device counter, so that a CUDA graph capturing a
+ * step of row-sharded launches can be replayed: after
+ * qwen_b200_sync_epoch_base(base) (base: a 4-byte aligned device uint32 of
+ * the current device; NULL restores absolute epochs), every nonzero wait /
+ * signal epoch given to qwen_b200_stack_run_sync,
+ * qwen_b200_swiglu_quant_sharded_dev, qwen_b200_tc_stack_run_sync and
+ * qwen_b200_quant_planes_wait_dev on this device is an offset: the launch
+ * reads *base when it runs and uses *base + offset (mod 2^32).  The setting
+ * is per device and is taken when a launch is enqueued (a captured launch
+ * keeps the counter it was captured with).  qwen_b200_sync_epoch_advance
+ * enqueues *base += n on `stream` (one single-thread kernel): a step whose
+ * launches use offsets 1..n ends with it, and the next step (or the next
+ * replay of the step's graph) uses the same offsets.  No reference
+ * counterpart (the reference runs on one device). */
+QB_API int qwen_b200_sync_epoch_base(const unsigned int* base);
+QB_API int qwen_b200_sync_epoch_advance(unsigned int* base, unsigned int n, void* stream);
 /* Zeroed device memory that can be shared with qwen_b200_ipc_handle (plain
  * cudaMalloc: IPC needs the allocation's own base pointer). */
 QB_API int qwen_b200_dev_alloc(size_t bytes, void** out);

@@ -669,8 +669,10 @@ __global__ void __launch_bounds__(TcCfg<N>::kThreads, 1) gemm_tc_kernel(const __
 // rint(x*q) half-even, xs = amax/16384; zero block when amax <= 1e-20.
 __global__ void __launch_bounds__(256) quant_planes_kernel(const float* x, int B, int K, uint8_t* planes,
                                                            float* xs_t, int ldxs, const unsigned int* wait_flags,
-                                                           unsigned int wait_epoch, int world, unsigned int* err) {
-    if (wait_epoch) wait_peer_flags(wait_flags, world, wait_epoch, err);   // row-sharded: inputs from all ranks
+                                                           unsigned int wait_epoch, const unsigned int* epoch_base,
+                                                           int world, unsigned int* err) {
+    // row-sharded: inputs from all ranks
+    if (wait_epoch) wait_peer_flags(wait_flags, world, wait_epoch, epoch_base, err);
     const int nb = K >> 6;
     const long long total = (long long)B * nb;
     const int lane = threadIdx.x & 31;
@@ -835,7 +837,7 @@ cudaError_t launch_quant_planes(const float* x, int B, int K, void* planes, floa
     const int grid = (int)std::min<long long>((total + 7) / 8, (long long)num_sms() * 16);
     quant_planes_kernel<<<grid, 256, 0, stream>>>(x, B, K, static_cast<uint8_t*>(planes), xs_t, ldxs,
                                                   sync ? sync->wait_flags : nullptr, sync ? sync->wait_epoch : 0u,
-                                                  sync ? sync->world : 1, err);
+                                                  sync ? sync->epoch_base : nullptr, sync ? sync->world : 1, err);
     return cudaGetLastError();
 }
 

@@ -61,6 +61,7 @@ struct PrepArgs {
     int n;
     const unsigned int* wait_flags;   // row-sharded stacks: inputs complete once every rank's flag
     unsigned int wait_epoch;          // reaches wait_epoch (0: no wait)
+    const unsigned int* epoch_base;   // nullptr, or the counter wait_epoch is an offset from
     int world;
     unsigned int* err;
 };
@@ -121,7 +122,7 @@ constexpr int kPrepChunk = kPrepThreads / 32 * kPrepPerWarp;
 
 __global__ void __launch_bounds__(kPrepThreads) act_prep_kernel(const __grid_constant__ PrepArgs A) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    if (A.wait_epoch) wait_peer_flags(A.wait_flags, A.world, A.wait_epoch, A.err);
+    if (A.wait_epoch) wait_peer_flags(A.wait_flags, A.world, A.wait_epoch, A.epoch_base, A.err);
     const GemvDesc& D = prep_desc(A, blockIdx.x);
     const int nb = D.K >> 6;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1147,15 +1148,24 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const __grid_constant
         s_last = tk == gridDim.x - 1;
         if (s_last) {
             __threadfence_system();
-            for (int r = 0; r < A.sync.world; r++) st_release_sys(A.sync.sig_flags[r] + A.sync.rank, A.sync.sig_epoch);
+            const unsigned int e = epoch_of(A.sync.sig_epoch, A.sync.epoch_base);
+            for (int r = 0; r < A.sync.world; r++) st_release_sys(A.sync.sig_flags[r] + A.sync.rank, e);
             *A.sync.sig_ticket = 0u;   // the next launch using this ticket is stream-ordered after this one
         }
     }
     __syncthreads();
-    if (s_last) wait_peer_flags(A.sync.wait_flags, A.sync.world, A.sync.sig_epoch, A.err);
+    if (s_last) wait_peer_flags(A.sync.wait_flags, A.sync.world, A.sync.sig_epoch, A.sync.epoch_base, A.err);
 }
 
+__global__ void epoch_advance_kernel(unsigned int* base, unsigned int n) { *base += n; }
+
 // ---------------------------------------------------------------- host side
+cudaError_t launch_epoch_advance(unsigned int* base, unsigned int n, cudaStream_t stream) {
+    if (!base || (reinterpret_cast<uintptr_t>(base) & 3)) return cudaErrorInvalidValue;
+    epoch_advance_kernel<<<1, 1, 0, stream>>>(base, n);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_swiglu_quant(const float* gate, const float* up, int B, int n, int ld_in, int col0, int K,
                                 int planar, int ldxs, void* const* dst, int ndst, const SyncArgs* sync,
                                 unsigned int* err, cudaStream_t stream) {
@@ -1346,6 +1356,7 @@ cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, un
     if (sync) {
         P.wait_flags = sync->wait_flags;
         P.wait_epoch = sync->wait_epoch;
+        P.epoch_base = sync->epoch_base;
         P.world = sync->world;
     }
     // back-to-back steps overlap: this step's GEMV CTAs start (descriptor

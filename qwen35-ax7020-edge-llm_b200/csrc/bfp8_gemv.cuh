@@ -151,6 +151,10 @@ cudaError_t launch_swiglu_quant(const float* gate, const float* up, int B, int n
                                 int planar, int ldxs, void* const* dst, int ndst, const SyncArgs* sync,
                                 unsigned int* err, cudaStream_t stream);
 
+// Enqueue *base += n (mod 2^32): moves the epoch counter of row-sharded
+// launches (SyncArgs::epoch_base) past one step's epochs.
+cudaError_t launch_epoch_advance(unsigned int* base, unsigned int n, cudaStream_t stream);
+
 // add_residual (NEON build): x[i] += res[i], flushed over groups of four.
 cudaError_t launch_add_residual(float* x, const float* res, int n, cudaStream_t stream);
 

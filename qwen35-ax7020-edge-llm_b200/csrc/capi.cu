@@ -230,18 +230,20 @@ struct DevState {
     uint32_t* act = nullptr;       // paired-activation scratch of single-GEMV launches
     unsigned int* tickets = nullptr;   // zeroed split-K counters of fast single-GEMV launches
     unsigned int* lm_ctr = nullptr;    // zeroed unit-claim counters of the BFP8 lm_head
+    const unsigned int* epoch_base = nullptr;   // row-sharded launches: epoch counter (nullptr: absolute epochs)
 };
+constexpr int kMaxDevices = 64;
 constexpr size_t kTicketWords = 16384;
 constexpr size_t kActScratchWords = 128 * 1024;   // serves K <= 253952
 
 int dev_state(DevState** out) {
     static std::mutex mu;
-    static std::vector<DevState> per_dev;
+    static DevState per_dev[kMaxDevices];   // fixed: the pointers handed out stay valid
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return fail(QB_ECUDA, "cudaGetDevice", e);
+    if (dev < 0 || dev >= kMaxDevices) return fail(QB_ENODEV, "device index beyond 63");
     std::lock_guard<std::mutex> lk(mu);
-    if ((int)per_dev.size() <= dev) per_dev.resize(dev + 1);
     DevState& st = per_dev[dev];
     if (!st.scratch) {
         qb::LmScratch* p = nullptr;
@@ -1364,6 +1366,8 @@ int qwen_b200_stack_run_sync(int plan, void* stream, const unsigned int* wait_fl
         (wait_epoch && !wait_flags))
         return fail(QB_EINVAL, "stack_run_sync: bad arguments (a plan from qwen_b200_stack_create_sharded, "
                                "1 <= world <= 8)");
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
     qb::SyncArgs sy{};
     sy.wait_flags = wait_flags;
     sy.wait_epoch = wait_epoch;
@@ -1371,9 +1375,8 @@ int qwen_b200_stack_run_sync(int plan, void* stream, const unsigned int* wait_fl
     sy.sig_epoch = sig_epoch;
     sy.world = world;
     sy.rank = rank;
+    sy.epoch_base = st->epoch_base;
     for (int r = 0; r < world && sig_flags; r++) sy.sig_flags[r] = sig_flags[r];
-    DevState* st = nullptr;
-    if (int rc = dev_state(&st)) return rc;
     cudaError_t e =
         qb::launch_gemv_list(sp.dev_descs, sp.plan, sp.ctr, st->err, static_cast<cudaStream_t>(stream), &sy);
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_stack_run_sync", e);
@@ -1387,6 +1390,8 @@ int qwen_b200_swiglu_quant_sharded_dev(const float* gate, const float* up, int B
                       rank >= world))
         return fail(QB_EINVAL, "swiglu_quant_sharded: a signal needs every rank's flags, a ticket and this GPU's "
                                "flags (1 <= world <= 8)");
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
     qb::SyncArgs sy{};
     if (sig_epoch) {
         sy.wait_flags = wait_flags;
@@ -1394,16 +1399,31 @@ int qwen_b200_swiglu_quant_sharded_dev(const float* gate, const float* up, int B
         sy.sig_epoch = sig_epoch;
         sy.world = world;
         sy.rank = rank;
+        sy.epoch_base = st->epoch_base;
         for (int r = 0; r < world; r++) sy.sig_flags[r] = sig_flags[r];
     }
-    DevState* st = nullptr;
-    if (int rc = dev_state(&st)) return rc;
     cudaError_t e = qb::launch_swiglu_quant(gate, up, B, n, ld_in, col0, K, planar, ldxs, dst, ndst,
                                             sig_epoch ? &sy : nullptr, st->err, static_cast<cudaStream_t>(stream));
     if (e == cudaErrorInvalidValue)
         return fail(QB_EINVAL, "swiglu_quant_sharded: n, col0 and K multiples of 64 with col0 + n <= K, B == 1 unless "
                                "planar, ldxs >= B, gate/up 8-byte and every dst 16-byte aligned, 1..8 destinations");
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_swiglu_quant_sharded_dev", e);
+}
+
+int qwen_b200_sync_epoch_base(const unsigned int* base) {
+    if (reinterpret_cast<uintptr_t>(base) & 3)
+        return fail(QB_EINVAL, "qwen_b200_sync_epoch_base: the counter must be 4-byte aligned");
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
+    st->epoch_base = base;
+    return QB_OK;
+}
+
+int qwen_b200_sync_epoch_advance(unsigned int* base, unsigned int n, void* stream) {
+    cudaError_t e = qb::launch_epoch_advance(base, n, static_cast<cudaStream_t>(stream));
+    if (e == cudaErrorInvalidValue)
+        return fail(QB_EINVAL, "qwen_b200_sync_epoch_advance: a 4-byte aligned device counter is required");
+    return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_sync_epoch_advance", e);
 }
 
 int qwen_b200_dev_alloc(size_t bytes, void** out) {
@@ -1681,11 +1701,14 @@ int qwen_b200_tc_stack_run_sync(int plan, void* stream, unsigned int* const* sig
         (sig_epoch && (!sig_flags || !tp.sig_ticket)))
         return fail(QB_EINVAL, "tc_stack_run_sync: bad arguments (a plan from qwen_b200_tc_stack_create_sharded, "
                                "1 <= world <= 8)");
+    DevState* st = nullptr;
+    if (int rc = dev_state(&st)) return rc;
     qb::SyncArgs sy{};
     sy.sig_ticket = tp.sig_ticket;
     sy.sig_epoch = sig_epoch;
     sy.world = world;
     sy.rank = rank;
+    sy.epoch_base = st->epoch_base;
     for (int r = 0; r < world && sig_flags; r++) sy.sig_flags[r] = sig_flags[r];
     return tc_stack_launch(plan, stream, &sy);
 }
@@ -1704,6 +1727,7 @@ int qwen_b200_quant_planes_wait_dev(const float* x, int B, int K, int8_t* planes
     sy.wait_flags = wait_flags;
     sy.wait_epoch = wait_epoch;
     sy.world = world;
+    sy.epoch_base = st->epoch_base;
     cudaError_t e = qb::launch_quant_planes(x, B, K, planes, xs_t, ldxs, static_cast<cudaStream_t>(stream), &sy,
                                             st->err);
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "qwen_b200_quant_planes_wait_dev", e);

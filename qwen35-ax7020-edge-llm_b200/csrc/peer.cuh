@@ -29,6 +29,10 @@ struct SyncArgs {
     unsigned int* sig_ticket;                // zeroed grid ticket of this plan
     unsigned int sig_epoch;                  // 0: no signal
     int world, rank;
+    // nullptr: the epochs above are absolute.  Otherwise a nonzero epoch is
+    // an offset from the device counter *epoch_base, read when the launch
+    // runs (so a captured graph replays fresh epochs once the counter moves)
+    const unsigned int* epoch_base;
 };
 
 constexpr uint32_t kFlagPolls = 1u << 22;   // bounded wait on peer flags (each poll may sleep)
@@ -49,12 +53,18 @@ __device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) 
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Thread 0 waits until flags[r] >= epoch for every rank r (wrap-safe
-// compare), giving up after kFlagPolls polls with kErrPeerTimeout in *err;
-// then the whole CTA proceeds.  Every thread of the CTA must call it.
+// The epoch a launch uses: e itself, or e + *base (mod 2^32) with a counter.
+__device__ __forceinline__ unsigned int epoch_of(unsigned int e, const unsigned int* base) {
+    return base ? e + *base : e;
+}
+
+// Thread 0 waits until flags[r] >= epoch_of(epoch, base) for every rank r
+// (wrap-safe compare), giving up after kFlagPolls polls with kErrPeerTimeout
+// in *err; then the whole CTA proceeds.  Every thread of the CTA must call it.
 __device__ __forceinline__ void wait_peer_flags(const unsigned int* flags, int world, unsigned int epoch,
-                                                unsigned int* err) {
+                                                const unsigned int* base, unsigned int* err) {
     if (threadIdx.x == 0) {
+        epoch = epoch_of(epoch, base);
         for (int r = 0; r < world; r++) {
             uint32_t i = 0;
             while ((int)(ld_acquire_sys(flags + r) - epoch) < 0) {
@@ -79,7 +89,8 @@ __device__ __forceinline__ void signal_peers(const SyncArgs& s) {
         const unsigned int t = atomicAdd(s.sig_ticket, 1u);
         if (t == gridDim.x * gridDim.y * gridDim.z - 1) {
             __threadfence_system();
-            for (int r = 0; r < s.world; r++) st_release_sys(s.sig_flags[r] + s.rank, s.sig_epoch);
+            const unsigned int e = epoch_of(s.sig_epoch, s.epoch_base);
+            for (int r = 0; r < s.world; r++) st_release_sys(s.sig_flags[r] + s.rank, e);
             *s.sig_ticket = 0u;   // the plan's next launch is stream-ordered after this one
         }
     }

@@ -73,6 +73,8 @@ SIGNATURES = {
     "qwen_b200_tc_stack_create_sharded": (_I, [_I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _P]),
     "qwen_b200_tc_stack_run_sync": (_I, [_I, _P, _P, ctypes.c_uint, _I, _I]),
     "qwen_b200_quant_planes_wait_dev": (_I, [_P, _I, _I, _P, _P, _I, _P, ctypes.c_uint, _I, _P]),
+    "qwen_b200_sync_epoch_base": (_I, [_P]),
+    "qwen_b200_sync_epoch_advance": (_I, [_P, ctypes.c_uint, _P]),
     "qwen_b200_lm_head_bf16_dev": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P, _P]),
     "qwen_b200_lm_head_bfp8_dev": (_I, [_P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P]),
     "qwen_b200_sample_topk_dev": (_I, [_P, _P, _P, _I, _F, _I, _F, _P, _P, _P]),

@@ -31,6 +31,7 @@ __all__ = [
     "KernelError", "quant_block64", "bfp8_gemv", "bfp8_gemv_fast", "bfp8_gemv_q", "lm_head_bf16", "lm_head_bfp8",
     "pack_bfp8", "LinearStack", "rmsnorm_bfp8_gemv", "residual_rmsnorm_bfp8_gemv", "LmResult", "Planes", "quant_planes", "bfp8_gemm_tc", "BatchedStack",
     "PeerRegion", "ShardedLinearStack", "quant_planes_wait", "ShardedBatchedStack", "swiglu_quant_sharded",
+    "sync_epoch_base", "sync_epoch_advance",
     "quant_record_bytes", "planes_record_bytes", "planes_view", "STACK_FAST", "STACK_FIXED_SPLIT", "STACK_Q_INPUT",
 ]
 
@@ -550,8 +551,9 @@ class ShardedLinearStack:
     ``peer_ptrs[i]``: device addresses of GEMV i's full vector on every other
     rank (world - 1 of them); ``row_base[i]`` = r0.  ``run(wait, sig, ...)``
     waits for epoch ``wait`` on this rank's flags (0: no wait) and publishes
-    epoch ``sig`` into every rank's flags.  Epochs are baked into the launch,
-    so a captured graph would replay stale epochs: launch it directly.
+    epoch ``sig`` into every rank's flags.  Absolute epochs are baked into
+    the launch; for a captured graph make them offsets from a device counter
+    (``sync_epoch_base`` / ``sync_epoch_advance``).
     """
 
     def __init__(self, items, peer_ptrs, row_base, world: int, fast: bool = False, flags: int | None = None):
@@ -627,6 +629,20 @@ def swiglu_quant_sharded(gate_ptr: int, up_ptr: int, B: int, n: int, ld_in: int,
     check(load().qwen_b200_swiglu_quant_sharded_dev(gate_ptr, up_ptr, B, n, ld_in, col0, K, 1 if planar else 0, ldxs,
                                                     dst, len(dst_ptrs), sf, sig_ticket, sig_epoch, wait_flags, world,
                                                     rank, _stream()), "swiglu_quant_sharded")
+
+
+def sync_epoch_base(base_ptr: int | None) -> None:
+    """Make the epochs of this device's row-sharded launches offsets from the
+    device uint32 at ``base_ptr`` (None: absolute epochs again); the
+    launches enqueued from now on read the counter when they run, so a CUDA
+    graph of a step replays with fresh epochs (qwen_b200_sync_epoch_base)."""
+    check(load().qwen_b200_sync_epoch_base(base_ptr or None), "sync_epoch_base")
+
+
+def sync_epoch_advance(base_ptr: int, n: int) -> None:
+    """Enqueue counter += n on the current stream (the end of a step whose
+    launches used epoch offsets 1..n)."""
+    check(load().qwen_b200_sync_epoch_advance(base_ptr, n & 0xFFFFFFFF, _stream()), "sync_epoch_advance")
 
 
 def quant_planes_wait(x: torch.Tensor, out: Planes, wait_flags: int, wait_epoch: int, world: int) -> Planes:

@@ -24,7 +24,9 @@ Two exchanges:
   stores the quantized slice, publishes an epoch flag to every rank and
   waits (bounded) for everyone's; the down GEMV stores its rows into every
   rank's output and publishes the next epoch, which the next layer's input
-  quantizer waits for.  No collective runs.
+  quantizer waits for.  No collective runs.  Epochs are offsets from a
+  per-rank device counter that the step's last launch advances, so one step
+  can be captured in a CUDA graph and replayed (``capture``).
 
 Batch 1 runs the GEMV kernels, batch > 1 the tcgen05 GEMM (planar int16
 activations).  With ``fast`` (batch 1) every row's K is cut into segments at
@@ -89,8 +91,9 @@ class ShardedDeviceStack:
     across steps so that timing never finds them in L2.
     """
 
-    FLAGS_BYTES = 256   # region head: epoch flags (one uint per rank), then the activation kernel's ticket
-    TICKET_OFFSET = 128
+    FLAGS_BYTES = 256   # region head: epoch flags (one uint per rank), the activation kernel's ticket,
+    TICKET_OFFSET = 128   # and this rank's epoch counter
+    COUNTER_OFFSET = 192
 
     def __init__(self, layers, world, rank, device, copies=1, seed=0, group=None, fast=False, exchange="nccl",
                  batch=1):
@@ -108,7 +111,6 @@ class ShardedDeviceStack:
         self.fast = fast
         self.exchange = exchange
         self.region, self.peer_regions = None, []
-        self.epoch = 0
         self.device = torch.device(device)
         self.ldxs = (batch + 3) // 4 * 4
         for L in self.layers:
@@ -200,9 +202,16 @@ class ShardedDeviceStack:
         self.full = {L.down.name: self.region.floats(self.voff[L.down.name], self.B * L.down.M)
                      .view(self._oshape(L.down.M)) for L in self.layers}
         self.flags = self.region.uints(0, self.world)
+        self.counter = self.region.uints(self.COUNTER_OFFSET, 1)
         self.peer_base = [0] * self.world   # every rank's region base, mapped into this process
         self.peer_base[self.rank] = self.region.ptr
         if self.world > 1:
+            # epoch 1 stands for "before the first step" (the first layer's
+            # wait); set before the handle exchange, so before any peer signals
+            import torch
+
+            self.flags.fill_(1)
+            torch.cuda.synchronize(self.device)
             handles = [None] * self.world
             dist.all_gather_object(handles, self.region.handle(), group=self.group)
             for r in range(self.world):
@@ -348,18 +357,51 @@ class ShardedDeviceStack:
         else:
             ops.swiglu_quant_sharded(gp, up, self.B, g1 - g0, L.gate.M, g0, L.down.K, self.B > 1, self.ldxs, dst)
 
-    def _next_epoch(self):
-        self.epoch += 1
-        return self.epoch & 0xFFFFFFFF or 1
-
     def step(self, copy=0):
-        """One token (or batch) through every layer."""
+        """One token (or batch) through every layer.  Peer exchange: layer
+        i waits for epoch 2i+1, its activation kernel publishes 2i+2 and its
+        down projection 2i+3, all offsets from this rank's device counter,
+        which the step's last launch advances by 2 * layers (so the next
+        step's first wait is this step's last signal)."""
         from . import ops
 
         peer = self.exchange == "peer" and self.world > 1
+        if peer:
+            ops.sync_epoch_base(self.region.ptr + self.COUNTER_OFFSET)
+        try:
+            self._step(copy, peer)
+            if peer:
+                ops.sync_epoch_advance(self.region.ptr + self.COUNTER_OFFSET, 2 * len(self.layers))
+        finally:
+            if peer:
+                ops.sync_epoch_base(None)
+
+    def capturable(self):
+        """Whether a step launches only this library's kernels (peer
+        exchange, or one rank), so that it can be captured in a CUDA graph."""
+        return self.exchange == "peer" or self.world == 1
+
+    def capture(self, copy=0):
+        """A CUDA graph of one step on weight copy `copy`.  Every plan must
+        have run once (step) before; every rank captures the same steps, and
+        nothing runs while capturing.  Replays advance the epoch counter as
+        step() does, so replays and steps may follow one another in any
+        order (the same on every rank)."""
+        import torch
+
+        if not self.capturable():
+            raise ValueError("a step with NCCL all-gathers is not captured")
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step(copy)
+        return g
+
+    def _step(self, copy, peer):
+        from . import ops
+
         x = self.x0
         for i, (L, (gu, dn)) in enumerate(zip(self.layers, self.plans[copy])):
-            wait = self.epoch & 0xFFFFFFFF
+            wait = 2 * i + 1
             if self.B > 1:
                 if peer:
                     ops.quant_planes_wait(x, self.planes_in, self.peer_base[self.rank], wait, self.world)
@@ -373,8 +415,8 @@ class ShardedDeviceStack:
                 else:
                     gu.run()
             if peer:
-                self._activation(i, L, self._next_epoch())
-                sig = self._next_epoch()
+                self._activation(i, L, 2 * i + 2)
+                sig = 2 * i + 3
                 if dn is not None:
                     if self.B > 1:
                         dn.run(self.peer_base, sig, self.rank)

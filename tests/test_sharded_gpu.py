@@ -51,7 +51,22 @@ def _worker(rank, world, port, path):
             np.save(path + f".{exchange}.{int(fast)}.{rank}.npy", _outputs(st))
             if exchange == "peer":
                 assert st.device_error() == 0
-                assert st.flags.cpu().tolist() == [6 * len(st.layers)] * world   # 2 signals x 3 steps per layer
+                # epochs start at 1; 2 signals per layer and step, 3 steps
+                assert st.flags.cpu().tolist() == [6 * len(st.layers) + 1] * world
+                assert st.counter.cpu().tolist() == [6 * len(st.layers)]
+                if fast:
+                    # one CUDA graph per copy, replayed after the eager steps:
+                    # the epochs come from the counter, so replays stay ordered
+                    graphs = [st.capture(c) for c in range(2)]
+                    torch.cuda.synchronize()
+                    dist.barrier()
+                    for i in range(3):
+                        graphs[i % 2].replay()
+                    torch.cuda.synchronize()
+                    np.save(path + f".graph.{rank}.npy", _outputs(st))
+                    assert st.device_error() == 0
+                    assert st.flags.cpu().tolist() == [12 * len(st.layers) + 1] * world
+                    del graphs
             st.close()
         st = sharded.ShardedDeviceStack(_layers(), world, rank, f"cuda:{rank}", copies=2, seed=4, exchange=exchange,
                                         batch=BATCH)
@@ -62,7 +77,7 @@ def _worker(rank, world, port, path):
         np.save(path + f".{exchange}.bf.{rank}.npy", st.final_output().cpu().numpy())
         if exchange == "peer":
             assert st.device_error() == 0
-            assert st.flags.cpu().tolist() == [6 * len(st.layers)] * world
+            assert st.flags.cpu().tolist() == [6 * len(st.layers) + 1] * world
         st.close()
     dist.barrier()
     dist.destroy_process_group()
@@ -103,6 +118,7 @@ def test_two_gpu_sharded_stack_matches_single_gpu(cuda, tmp_path):
             assert np.array_equal(got, np.load(path + ".nccl.b.0.npy")), (exchange, "batched", r)
             fin = np.load(path + f".{exchange}.bf.{r}.npy")
             assert np.max(np.abs(fin - ref_b)) <= 1e-4 * np.max(np.abs(ref_b)), (exchange, "batched", r)
+        assert np.array_equal(np.load(path + f".graph.{r}.npy"), ref[True]), ("graph replay", r)
 
 
 def test_peer_mode_single_rank_matches_plain(cuda):
@@ -233,3 +249,63 @@ def test_peer_flag_wait_times_out_with_status(cuda):
     torch.cuda.synchronize()
     assert st.device_error() == 0
     st.close()
+
+
+def test_epoch_counter_graph_replays(cuda):
+    """Epochs as offsets from a device counter: a captured graph of (a
+    GEMV that waits for offset 1 and publishes offset 2; counter += 1)
+    publishes a fresh epoch on every replay, its rows equal the same GEMV
+    in a plain stack, and with the counter unset the epochs are absolute
+    again."""
+    import torch
+
+    from oracle import oracle as O
+    from qwen_b200 import ops
+
+    rng = np.random.default_rng(3)
+    M, K = 256, 1024
+    mant, exps = O.pack_bfp8(rng.normal(0, 0.02, (M, K)).astype(np.float32))
+    dev = torch.device("cuda:0")
+    x = torch.from_numpy(rng.normal(0, 1, K).astype(np.float32)).to(dev)
+    m, e = torch.from_numpy(mant).to(dev), torch.from_numpy(exps).to(dev)
+    y = torch.zeros(M, dtype=torch.float32, device=dev)
+    region = ops.PeerRegion(256)
+    flags, counter = region.uints(0, 1), region.uints(192, 1)
+    flags.fill_(1)
+    stack = ops.ShardedLinearStack([(x, m, e, y)], [[]], [0], 1, fast=True)
+    base = region.ptr + 192
+
+    def step():
+        ops.sync_epoch_base(base)
+        try:
+            stack.run(region.ptr, 1, [region.ptr], 2, 0)
+            ops.sync_epoch_advance(base, 1)
+        finally:
+            ops.sync_epoch_base(None)
+
+    lib = ops.load()
+    lib.qwen_b200_device_error(1)
+    step()                                    # eager: waits for 0 + 1, publishes 0 + 2
+    torch.cuda.synchronize()
+    assert flags.cpu().tolist() == [2] and counter.cpu().tolist() == [1]
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for i in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    assert flags.cpu().tolist() == [5] and counter.cpu().tolist() == [4]
+    assert lib.qwen_b200_device_error(1) == 0
+    y2 = torch.zeros_like(y)
+    plain = ops.LinearStack([(x, m, e, y2)], fast=True)
+    plain.run()
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2)
+    plain.close()
+    stack.run(region.ptr, 5, [region.ptr], 9, 0)   # counter unset: absolute epochs
+    torch.cuda.synchronize()
+    assert flags.cpu().tolist() == [9] and counter.cpu().tolist() == [4]
+    assert lib.qwen_b200_device_error(1) == 0
+    del g
+    stack.close()
+    region.close()
