@@ -122,18 +122,29 @@ constexpr int kPrepChunk = kPrepThreads / 32 * kPrepPerWarp;
 
 __global__ void __launch_bounds__(kPrepThreads) act_prep_kernel(const __grid_constant__ PrepArgs A) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    if (A.wait_epoch) wait_peer_flags(A.wait_flags, A.world, A.wait_epoch, A.epoch_base, A.err);
+    // the descriptor is immutable: its fields are read before the wait below
     const GemvDesc& D = prep_desc(A, blockIdx.x);
     const int nb = D.K >> 6;
+    const float* x = D.x;
+    const int16_t* xq = D.xq;
+    const float* xsrc = D.xs;
+    uint32_t* xpairs = D.xpairs;
+    float* xscale = D.xscale;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b0 = blockIdx.y * kPrepChunk + warp * kPrepPerWarp;
-    if (b0 >= nb) return;
-    // launched as a programmatic dependent of the previous step's GEMV: x
-    // (possibly its output) and this plan's scratch (which it may still
-    // read) are touched only once that grid has completed (a no-op for a
-    // plain launch)
+    // warps without blocks leave at once (a CTA that waits for peers keeps
+    // them for the block-wide wait)
+    if (!A.wait_epoch && b0 >= nb) return;
+    // launched as a programmatic dependent of the stream's previous kernel:
+    // x (possibly its output) and this plan's scratch (which it may still
+    // read) are touched, and peer flags polled, only once that grid has
+    // completed -- so a row-sharded wait never spins beside the kernel on
+    // this GPU that raises this rank's own flag (a no-op for a plain launch)
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    const float* x = D.x;
+    if (A.wait_epoch) {
+        wait_peer_flags(A.wait_flags, A.world, A.wait_epoch, A.epoch_base, A.err);
+        if (b0 >= nb) return;
+    }
     float2 v[kPrepPerWarp];
     if (x) {
 #pragma unroll
@@ -149,12 +160,12 @@ __global__ void __launch_bounds__(kPrepThreads) act_prep_kernel(const __grid_con
         if (x) {
             block_quant(v[j], q0, q1, xs);
         } else {
-            const short2 w = reinterpret_cast<const short2*>(D.xq + 64 * b)[lane];
+            const short2 w = reinterpret_cast<const short2*>(xq + 64 * b)[lane];
             q0 = w.x;
             q1 = w.y;
-            xs = D.xs[b];
+            xs = xsrc[b];
         }
-        block_store(D.xpairs, D.xscale, b, lane, q0, q1, xs);
+        block_store(xpairs, xscale, b, lane, q0, q1, xs);
     }
 }
 
@@ -1107,6 +1118,10 @@ struct SqArgs {
 };
 
 __global__ void __launch_bounds__(256) swiglu_quant_kernel(const __grid_constant__ SqArgs A) {
+    // a programmatic dependent of the gate / up GEMV: its outputs are read
+    // once that grid has completed; the next launch may start its prologue
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int lane = threadIdx.x & 31;
     const int nbl = A.n >> 6;
     const long long total = (long long)A.B * nbl;
@@ -1193,8 +1208,16 @@ cudaError_t launch_swiglu_quant(const float* gate, const float* up, int B, int n
     A.err = err;
     const long long total = (long long)B * (n / 64);
     const int grid = (int)std::max<long long>(1, std::min<long long>((total + 7) / 8, (long long)num_sms() * 8));
-    swiglu_quant_kernel<<<grid, 256, 0, stream>>>(A);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, swiglu_quant_kernel, A);
 }
 
 int num_sms() {
@@ -1361,11 +1384,9 @@ cudaError_t launch_gemv_list(const GemvDesc* dev_descs, const GemvPlan& plan, un
     }
     // back-to-back steps overlap: this step's GEMV CTAs start (descriptor
     // table, first weight stages) while the previous kernel's last CTAs
-    // finish.  Not for row-sharded plans (their act_prep waits on peer
-    // flags) nor inside stream capture.
-    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) return cudaGetLastError();
-    cudaError_t e = launch_prep(P, plan.kmax, stream, !sync && cap == cudaStreamCaptureStatusNone);
+    // finish (act_prep waits for that kernel before it reads, writes or
+    // polls peer flags)
+    cudaError_t e = launch_prep(P, plan.kmax, stream, true);
     if (e != cudaSuccess) return e;
     WArgs A{};
     A.list = dev_descs;
