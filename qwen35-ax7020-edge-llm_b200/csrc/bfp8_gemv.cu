@@ -276,31 +276,11 @@ __device__ __forceinline__ void store_peers(const PeerOut* P, int row, float v) 
     for (int r = 0; r < n; r++) P->y[r][g] = v;
 }
 
+// A whole-K unit's row results (split segments are published by the caller).
 template <bool LM>
 __device__ __forceinline__ void unit_result(const WArgs& A, const SDesc* T, const Unit& U, int lane, float yv,
                                             LmState& lm) {
     const int row = U.r0 + lane;
-    const SDesc& D = T[U.d];
-    if (!LM && D.nseg > 1) {
-        // fast mode, split row group: publish this segment's sums; the warp
-        // that completes the group adds the segments in order
-        if (row < U.M) D.partial[(size_t)U.s * U.M + row] = yv;
-        __threadfence();
-        __syncwarp();
-        unsigned int t = 0;
-        if (lane == 0) t = atomicAdd(&D.tickets[U.g], 1u);
-        t = __shfl_sync(0xffffffffu, t, 0);
-        if (t != (unsigned int)D.nseg - 1u) return;
-        __threadfence();
-        if (row < U.M) {
-            float sum = 0.0f;
-            for (int s = 0; s < D.nseg; s++) sum = __fadd_rn(sum, __ldcg(D.partial + (size_t)s * U.M + row));
-            D.y[row] = sum;
-            if (D.peer) store_peers(D.peer, row, sum);
-        }
-        if (lane == 0) D.tickets[U.g] = 0u;
-        return;
-    }
     if (LM) {
         const bool ok = row < U.M;
         if (ok && yv > -1e30f) {
@@ -774,6 +754,39 @@ __global__ void __maxnreg__(128) gemv_warp_kernel(const __grid_constant__ WArgs 
     unsigned int rfl = 0u;       // RTL: flags of the current unit
     unsigned int rflags = 0u;    // RTL: sticky flags of this lane's rows
     const int sw = lane & 7;
+    // fast mode (the only one that splits row groups): a finished segment's
+    // sums are stored at once; the fence and the group ticket follow one
+    // stage later and the ticket's answer one more stage later, so neither
+    // round trip stalls the stream.  The warp holding the group's last
+    // ticket adds the segments in order.
+    int pub = 0;                     // 0: none; 1: sums stored; 2: ticket requested
+    int pub_d = 0, pub_g = 0;        // the pending segment's GEMV and row group
+    unsigned int pub_raw = 0u;       // lane 0: the ticket's answer
+    auto pub_ticket = [&]() {
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) pub_raw = atomicAdd(&sdesc[pub_d].tickets[pub_g], 1u);
+        pub = 2;
+    };
+    auto pub_finish = [&]() {
+        const SDesc& D = sdesc[pub_d];
+        const unsigned int t = __shfl_sync(0xffffffffu, pub_raw, 0);
+        pub = 0;
+        if (t != (unsigned int)D.nseg - 1u) return;
+        __threadfence();
+        const int row = pub_g * kRows + lane;
+        if (row < D.M) {
+            float sum = 0.0f;
+            for (int s = 0; s < D.nseg; s++) sum = __fadd_rn(sum, __ldcg(D.partial + (size_t)s * D.M + row));
+            D.y[row] = sum;
+            if (D.peer) store_peers(D.peer, row, sum);
+        }
+        if (lane == 0) D.tickets[pub_g] = 0u;
+    };
+    auto pub_flush = [&]() {
+        if (pub == 1) pub_ticket();
+        if (pub == 2) pub_finish();
+    };
     int i = 0;
 #pragma unroll 1
     while (cu.valid) {
@@ -799,6 +812,10 @@ __global__ void __maxnreg__(128) gemv_warp_kernel(const __grid_constant__ WArgs 
             stage_blocks<false, false>(st, xst, xsst, ew, sw, false, f0, f1, f2, f3, fo);
         else
             stage_blocks<true, false>(st, xst, xsst, ew, sw, odd, f0, f1, f2, f3, fo);
+        if (FAST && !LM && pub) {
+            if (pub == 2) pub_finish();
+            else pub_ticket();
+        }
         if (++cs == cu.st1) {
             float yv;
             if (RTL) {
@@ -809,7 +826,16 @@ __global__ void __maxnreg__(128) gemv_warp_kernel(const __grid_constant__ WArgs 
             } else {
                 yv = FAST ? f0 : (odd ? fo : add_ftz(add_ftz(f0, f2), add_ftz(f1, f3)));
             }
-            unit_result<LM>(A, sdesc, cu, lane, yv, lm);
+            if (FAST && !LM && sdesc[cu.d].nseg > 1) {
+                pub_flush();
+                const int row = cu.r0 + lane;
+                if (row < cu.M) sdesc[cu.d].partial[(size_t)cu.s * cu.M + row] = yv;
+                pub_d = cu.d;
+                pub_g = cu.g;
+                pub = 1;
+            } else {
+                unit_result<LM>(A, sdesc, cu, lane, yv, lm);
+            }
             f0 = f1 = f2 = f3 = fo = 0.f;
             kc++;
             cu = load_unit(sdesc, nd, nu_total, (kc & 1) ? claimed1 : claimed0);
@@ -817,6 +843,7 @@ __global__ void __maxnreg__(128) gemv_warp_kernel(const __grid_constant__ WArgs 
         }
         i++;
     }
+    if (FAST && !LM) pub_flush();
     cp_async_wait<0>();
     if (RTL && A.rtl_flags) {
         const unsigned int f = __reduce_or_sync(0xffffffffu, rflags);
