@@ -777,7 +777,16 @@ __global__ void __maxnreg__(128) gemv_warp_kernel(const __grid_constant__ WArgs 
         const int row = pub_g * kRows + lane;
         if (row < D.M) {
             float sum = 0.0f;
-            for (int s = 0; s < D.nseg; s++) sum = __fadd_rn(sum, __ldcg(D.partial + (size_t)s * D.M + row));
+            // eight segment loads in flight at a time, added in segment order
+            for (int s0 = 0; s0 < D.nseg; s0 += 8) {
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    v[j] = s0 + j < D.nseg ? __ldcg(D.partial + (size_t)(s0 + j) * D.M + row) : 0.0f;
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    if (s0 + j < D.nseg) sum = __fadd_rn(sum, v[j]);
+            }
             D.y[row] = sum;
             if (D.peer) store_peers(D.peer, row, sum);
         }
