@@ -207,8 +207,12 @@ QB_API int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linea
  *   mode 0 (the default, the reference's contract): every
  *     forward_linear_layer / forward_token_c call copies each layer's conv_s
  *     and state host arrays to the device before its work and back after it
- *     (19.3 MB each way per token for the 0.8B model), as plain pageable
- *     copies interleaved with the layers;
+ *     (19.3 MB each way per token for the 0.8B model).  forward_token_c
+ *     reads every layer's arrays into a page-locked staging buffer of its
+ *     own (several host threads; QWEN_B200_COPY_THREADS, default up to 4)
+ *     before the first layer, copies between that buffer and the device
+ *     beside the layers, and writes the arrays back after the last layer;
+ *     forward_linear_layer copies the arrays directly (pageable);
  *   mode 1 (resident): the device copy, made on first sight after entering
  *     the mode, is the state; the host arrays are written only by
  *     qwen_b200_gdn_state_sync() and when leaving the mode;

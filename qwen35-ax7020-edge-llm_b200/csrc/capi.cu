@@ -18,11 +18,13 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <condition_variable>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <unordered_map>
 #include <vector>
 
@@ -388,7 +390,9 @@ int resolve_linear_plan(const LinearLayerPlanC* p, DevLinear* out) {
 // Device copies of the engine's mutable Gated-DeltaNet state arrays, keyed
 // by host address.  Modes (qwen_b200_gdn_state_mode):
 //   0 mirror         the host array is copied in before every layer call and
-//                    back after it (the reference's contract), pageable copies;
+//                    back after it (the reference's contract): pageable
+//                    copies, or, in forward_token_c, through the staging
+//                    buffer below;
 //   1 resident       copied in once, then the device copy is the state until
 //                    qwen_b200_gdn_state_sync() copies it back or _drop()
 //                    forgets it;
@@ -456,27 +460,149 @@ float* state_slot(float* host, size_t n, bool* fresh, int* rc) {
     return it->second.dev;
 }
 
+// Floats of a layer's conv state and recurrent state.
+size_t conv_floats(const DevLinear& w) { return 3 * (size_t)w.qkv.M; }
+size_t state_floats(const DevLinear& w) { return (size_t)w.heads * qb::kGdnHeadDim * qb::kGdnHeadDim; }
+
 // Bring a layer's states onto the device on stream s (per the mode);
-// dev_conv / dev_state receive the device copies.
-int states_in(const DevLinear& w, float** dev_conv, float** dev_state, cudaStream_t s) {
+// dev_conv / dev_state receive the device copies.  With `stage` (mirror
+// mode in forward_token_c) the host side of the copies is the layer's
+// page-locked staging area -- conv state, then recurrent state -- instead of
+// the caller's arrays.
+int states_in(const DevLinear& w, float** dev_conv, float** dev_state, cudaStream_t s, const float* stage = nullptr) {
     int rc = QB_OK;
-    const size_t nc = 3 * (size_t)w.qkv.M, ns = (size_t)w.heads * qb::kGdnHeadDim * qb::kGdnHeadDim;
+    const size_t nc = conv_floats(w), ns = state_floats(w);
     bool fc = false, fs = false;
     if (!(*dev_conv = state_slot(w.conv_s, nc, &fc, &rc)) || !(*dev_state = state_slot(w.state, ns, &fs, &rc)))
         return rc;
     cudaError_t e = cudaSuccess;
     const bool resident = g_state_mode == kStateResident;
-    if (!resident || fc) e = cudaMemcpyAsync(*dev_conv, w.conv_s, nc * 4, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess && (!resident || fs))
-        e = cudaMemcpyAsync(*dev_state, w.state, ns * 4, cudaMemcpyHostToDevice, s);
+    const float* hc = stage ? stage : w.conv_s;
+    const float* hs = stage ? stage + nc : w.state;
+    if (!resident || fc) e = cudaMemcpyAsync(*dev_conv, hc, nc * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess && (!resident || fs)) e = cudaMemcpyAsync(*dev_state, hs, ns * 4, cudaMemcpyHostToDevice, s);
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "state copy in", e);
 }
-int states_out(const DevLinear& w, const float* dev_conv, const float* dev_state, cudaStream_t s) {
+int states_out(const DevLinear& w, const float* dev_conv, const float* dev_state, cudaStream_t s,
+               float* stage = nullptr) {
     if (g_state_mode == kStateResident) return QB_OK;
-    const size_t nc = 3 * (size_t)w.qkv.M, ns = (size_t)w.heads * qb::kGdnHeadDim * qb::kGdnHeadDim;
-    cudaError_t e = cudaMemcpyAsync(w.conv_s, dev_conv, nc * 4, cudaMemcpyDeviceToHost, s);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(w.state, dev_state, ns * 4, cudaMemcpyDeviceToHost, s);
+    const size_t nc = conv_floats(w), ns = state_floats(w);
+    float* hc = stage ? stage : w.conv_s;
+    float* hs = stage ? stage + nc : w.state;
+    cudaError_t e = cudaMemcpyAsync(hc, dev_conv, nc * 4, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(hs, dev_state, ns * 4, cudaMemcpyDeviceToHost, s);
     return e == cudaSuccess ? QB_OK : fail(QB_ECUDA, "state copy out", e);
+}
+
+// Mirror mode's staging: the caller's pageable state arrays are copied into
+// one page-locked buffer (and back) by several host threads at once, and
+// the device copies are DMA from / to that buffer.  A pageable cudaMemcpy
+// stages through the driver's own buffers on one thread (~8.6 GB/s here);
+// the threads split the bytes evenly (QWEN_B200_COPY_THREADS, default
+// min(4, hardware threads)).
+void* g_stage = nullptr;
+size_t g_stage_bytes = 0;
+
+int stage_reserve(size_t bytes) {
+    if (bytes <= g_stage_bytes) return QB_OK;
+    if (g_stage) cudaFreeHost(g_stage);
+    g_stage = nullptr;
+    g_stage_bytes = 0;
+    cudaError_t e = cudaHostAlloc(&g_stage, bytes, cudaHostAllocDefault);
+    if (e != cudaSuccess) {
+        g_stage = nullptr;
+        return fail(QB_ENOMEM, "state staging buffer", e);
+    }
+    g_stage_bytes = bytes;
+    return QB_OK;
+}
+
+struct CopyChunk {
+    char* dst;
+    const char* src;
+    size_t n;
+};
+
+// The copy threads: created on first use, they wait for jobs and live until
+// the process exits.  One job at a time (callers hold the library lock);
+// the caller's own thread copies the first part.
+class CopyPool {
+  public:
+    explicit CopyPool(int n) : n_(1) {
+        int i = 1;
+        try {
+            for (; i < n; i++) std::thread([this, i] { run(i); }).detach();
+        } catch (...) {   // fewer threads than asked for
+        }
+        n_ = i;
+    }
+    void copy(const std::vector<CopyChunk>& v) {
+        size_t total = 0;
+        for (const CopyChunk& c : v) total += c.n;
+        if (n_ == 1 || total < ((size_t)1 << 20)) {
+            part(v, 0, total);
+            return;
+        }
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            job_ = &v;
+            total_ = total;
+            pending_ = n_ - 1;
+            gen_++;
+        }
+        cv_.notify_all();
+        part(v, 0, total / n_);
+        std::unique_lock<std::mutex> lk(mu_);
+        done_.wait(lk, [this] { return pending_ == 0; });
+        job_ = nullptr;
+    }
+
+  private:
+    // the bytes [b0, b1) of the chunks' concatenation
+    static void part(const std::vector<CopyChunk>& v, size_t b0, size_t b1) {
+        size_t base = 0;
+        for (const CopyChunk& c : v) {
+            const size_t lo = std::max(b0, base), hi = std::min(b1, base + c.n);
+            if (lo < hi) memcpy(c.dst + (lo - base), c.src + (lo - base), hi - lo);
+            base += c.n;
+            if (base >= b1) break;
+        }
+    }
+    void run(int i) {
+        unsigned int seen = 0;
+        for (;;) {
+            const std::vector<CopyChunk>* job;
+            size_t total;
+            {
+                std::unique_lock<std::mutex> lk(mu_);
+                cv_.wait(lk, [&] { return gen_ != seen; });
+                seen = gen_;
+                job = job_;
+                total = total_;
+            }
+            part(*job, total * i / n_, total * (i + 1) / n_);
+            std::lock_guard<std::mutex> lk(mu_);
+            if (--pending_ == 0) done_.notify_one();
+        }
+    }
+    int n_;
+    std::mutex mu_;
+    std::condition_variable cv_, done_;
+    const std::vector<CopyChunk>* job_ = nullptr;
+    size_t total_ = 0;
+    int pending_ = 0;
+    unsigned int gen_ = 0;
+};
+
+// Every chunk copied, the concatenated bytes split evenly over the pool.
+void parallel_copy(const std::vector<CopyChunk>& v) {
+    static CopyPool* pool = [] {   // never destroyed: its threads outlive static destructors
+        const char* e = getenv("QWEN_B200_COPY_THREADS");
+        int t = e ? atoi(e) : 0;
+        if (t <= 0) t = std::min(4, (int)std::max(1u, std::thread::hardware_concurrency()));
+        return new CopyPool(std::min(t, 64));
+    }();
+    pool->copy(v);
 }
 
 // Event pool of the layer loop's copy / compute ordering (two per layer).
@@ -802,10 +928,32 @@ int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linear_plans
     const size_t hb = 4 * (size_t)kLoopHidden;
     // States move on the copy stream, interleaved with the layers: layer i's
     // states go in just before its work is queued and its compute waits for
-    // them; they come back once layer i + 1 is queued.  (With pageable host
-    // arrays each copy holds the host thread while the GPU runs what is
-    // already queued; with page-locked ones, mode 2, nothing waits.)
+    // them; they come back once layer i + 1 is queued.  The host side of
+    // these copies is page-locked, so nothing waits: the staging buffer in
+    // mirror mode, the registered arrays in mode 2.
     std::vector<float*> dconv(lin.size()), dstate(lin.size());
+    // mirror mode: every layer's states are first copied into the staging
+    // buffer by several host threads, and back into the caller's arrays
+    // after the last layer
+    std::vector<float*> stage(lin.size(), nullptr);
+    std::vector<CopyChunk> back;   // staging -> the caller's arrays, after the last copy out
+    if (g_state_mode == kStateMirror && !lin.empty()) {
+        size_t total = 0;
+        for (const DevLinear& w : lin) total += (conv_floats(w) + state_floats(w)) * 4;
+        if (stage_reserve(total)) return name_error("forward_token_c"), -1;
+        std::vector<CopyChunk> in;
+        char* p = static_cast<char*>(g_stage);
+        for (size_t i = 0; i < lin.size(); i++) {
+            const size_t bc = conv_floats(lin[i]) * 4, bs = state_floats(lin[i]) * 4;
+            stage[i] = reinterpret_cast<float*>(p);
+            in.push_back({p, reinterpret_cast<const char*>(lin[i].conv_s), bc});
+            in.push_back({p + bc, reinterpret_cast<const char*>(lin[i].state), bs});
+            back.push_back({reinterpret_cast<char*>(lin[i].conv_s), p, bc});
+            back.push_back({reinterpret_cast<char*>(lin[i].state), p + bc, bs});
+            p += bc + bs;
+        }
+        parallel_copy(in);
+    }
     cudaStream_t cs = g_ctx.copy;
     if (loop_events(2 * lin.size() + 1)) return name_error("forward_token_c"), -1;
     cudaEvent_t* ev_in = g_loop_events.data();
@@ -839,13 +987,14 @@ int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linear_plans
             }
             e = mlp_launch(mlp[l], g_loop.h, nullptr, nullptr, st, s);
         } else {
-            if (states_in(lin[li], &dconv[li], &dstate[li], cs)) return name_error("forward_token_c"), -1;
+            if (states_in(lin[li], &dconv[li], &dstate[li], cs, stage[li])) return name_error("forward_token_c"), -1;
             e = cudaEventRecord(ev_in[li], cs);
             if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ev_in[li], 0);
             if (e == cudaSuccess) e = linear_launch(lin[li], g_loop.h, dconv[li], dstate[li], st, s);
             if (e == cudaSuccess) e = cudaEventRecord(ev_done[li], s);
             if (e == cudaSuccess && li > 0) e = cudaStreamWaitEvent(cs, ev_done[li - 1], 0);
-            if (e == cudaSuccess && li > 0 && states_out(lin[li - 1], dconv[li - 1], dstate[li - 1], cs))
+            if (e == cudaSuccess && li > 0 &&
+                states_out(lin[li - 1], dconv[li - 1], dstate[li - 1], cs, stage[li - 1]))
                 return name_error("forward_token_c"), -1;
             std::swap(g_loop.h, g_loop.h2);   // the layer's output is the next layer's h
             li++;
@@ -861,9 +1010,11 @@ int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linear_plans
     if (e == cudaSuccess) e = cudaMemcpyAsync(pid, g_loop.res, sizeof(int), cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess && li > 0) e = cudaStreamWaitEvent(cs, ev_done[li - 1], 0);
     if (e != cudaSuccess) return cuda_fail(e, "forward_token_c"), -1;
-    if (li > 0 && states_out(lin[li - 1], dconv[li - 1], dstate[li - 1], cs)) return name_error("forward_token_c"), -1;
+    if (li > 0 && states_out(lin[li - 1], dconv[li - 1], dstate[li - 1], cs, stage[li - 1]))
+        return name_error("forward_token_c"), -1;
     if ((e = cudaStreamSynchronize(s)) != cudaSuccess || (e = cudaStreamSynchronize(cs)) != cudaSuccess)
         return cuda_fail(e, "forward_token_c"), -1;
+    parallel_copy(back);
     memcpy(h, g_loop.pin, hb);
     return *pid;
 }
