@@ -934,7 +934,8 @@ int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linear_plans
     std::vector<float*> dconv(lin.size()), dstate(lin.size());
     // mirror mode: every layer's states are first copied into the staging
     // buffer by several host threads, and back into the caller's arrays
-    // after the last layer
+    // once their copies out have landed (while the host waits for the GPU
+    // at a callback or at the end)
     std::vector<float*> stage(lin.size(), nullptr);
     std::vector<CopyChunk> back;   // staging -> the caller's arrays, after the last copy out
     if (g_state_mode == kStateMirror && !lin.empty()) {
@@ -955,10 +956,26 @@ int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linear_plans
         parallel_copy(in);
     }
     cudaStream_t cs = g_ctx.copy;
-    if (loop_events(2 * lin.size() + 1)) return name_error("forward_token_c"), -1;
+    if (loop_events(3 * lin.size() + 1)) return name_error("forward_token_c"), -1;
     cudaEvent_t* ev_in = g_loop_events.data();
     cudaEvent_t* ev_done = ev_in + lin.size();
-    cudaEvent_t ev_start = ev_in[2 * lin.size()];
+    cudaEvent_t* ev_out = ev_in + 2 * lin.size();   // a layer's copy out has landed in the staging buffer
+    cudaEvent_t ev_start = ev_in[3 * lin.size()];
+    size_t out_queued = 0, out_back = 0;   // mirror mode: layers whose copy out is queued / written back
+    // mirror mode: while the GPU works through what is queued on s, the
+    // layers whose states have landed are written back to the caller's arrays
+    auto write_back_while_busy = [&]() {
+        if (back.empty()) return;
+        while (cudaStreamQuery(s) == cudaErrorNotReady) {
+            if (out_back < out_queued && cudaEventQuery(ev_out[out_back]) == cudaSuccess) {
+                parallel_copy({back[2 * out_back], back[2 * out_back + 1]});
+                out_back++;
+            } else {
+                std::this_thread::yield();
+            }
+        }
+        cudaGetLastError();   // "not ready" is no failure
+    };
     if (cudaEventRecord(ev_start, s) != cudaSuccess || cudaStreamWaitEvent(cs, ev_start, 0) != cudaSuccess)
         return cuda_fail(cudaGetLastError(), "forward_token_c"), -1;   // the previous call's work is done first
     // 1. the bf16 embedding row of token_id % 65536
@@ -970,8 +987,9 @@ int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linear_plans
         if (layer_is_full[l]) {
             if (full_attn_cb) {
                 e = cudaMemcpyAsync(g_loop.pin, g_loop.h, hb, cudaMemcpyDeviceToHost, s);
-                if (e == cudaSuccess) e = cudaStreamSynchronize(s);
                 if (e != cudaSuccess) break;
+                write_back_while_busy();
+                if ((e = cudaStreamSynchronize(s)) != cudaSuccess) break;
                 memcpy(h, g_loop.pin, hb);
                 g_token_busy = true;
                 lk.unlock();
@@ -996,6 +1014,8 @@ int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linear_plans
             if (e == cudaSuccess && li > 0 &&
                 states_out(lin[li - 1], dconv[li - 1], dstate[li - 1], cs, stage[li - 1]))
                 return name_error("forward_token_c"), -1;
+            if (e == cudaSuccess && li > 0 && (e = cudaEventRecord(ev_out[li - 1], cs)) == cudaSuccess)
+                out_queued = li;
             std::swap(g_loop.h, g_loop.h2);   // the layer's output is the next layer's h
             li++;
         }
@@ -1012,9 +1032,13 @@ int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linear_plans
     if (e != cudaSuccess) return cuda_fail(e, "forward_token_c"), -1;
     if (li > 0 && states_out(lin[li - 1], dconv[li - 1], dstate[li - 1], cs, stage[li - 1]))
         return name_error("forward_token_c"), -1;
+    if (li > 0 && (e = cudaEventRecord(ev_out[li - 1], cs)) != cudaSuccess) return cuda_fail(e, "forward_token_c"), -1;
+    out_queued = li;
+    write_back_while_busy();
     if ((e = cudaStreamSynchronize(s)) != cudaSuccess || (e = cudaStreamSynchronize(cs)) != cudaSuccess)
         return cuda_fail(e, "forward_token_c"), -1;
-    parallel_copy(back);
+    if (!back.empty() && out_back < li)
+        parallel_copy(std::vector<CopyChunk>(back.begin() + 2 * out_back, back.end()));
     memcpy(h, g_loop.pin, hb);
     return *pid;
 }
