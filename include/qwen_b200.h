@@ -211,7 +211,8 @@ QB_API int forward_token_c(int token_id, float* h, const LinearLayerPlanC* linea
  *     reads every layer's arrays into a page-locked staging buffer of its
  *     own (several host threads; QWEN_B200_COPY_THREADS, default up to 4)
  *     before the first layer, copies between that buffer and the device
- *     beside the layers, and writes the arrays back after the last layer;
+ *     beside the layers, and writes each layer's arrays back once its copy
+ *     out has landed (while it waits for the GPU; all before it returns);
  *     forward_linear_layer copies the arrays directly (pageable);
  *   mode 1 (resident): the device copy, made on first sight after entering
  *     the mode, is the state; the host arrays are written only by
