@@ -392,7 +392,7 @@ QB_API int qwen_b200_stack_create_sharded(int n, const int8_t* const* mant, cons
  * until wait_flags[r] >= wait_epoch for every rank r < world (wrap-safe
  * compare), i.e. until every rank finished the launch its inputs come from.
  * With sig_epoch != 0 the last CTA of the launch stores sig_epoch into
- * sig_flags[r][rank] for every r < world (release, system scope) after all
+ * sig_flags[r][rank] for every r < world (behind a system-scope fence) after all
  * rows reached every GPU.  sig_flags[r] is rank r's flag array (world uints),
  * wait_flags is this rank's own; epochs grow by one per launch on all ranks. */
 QB_API int qwen_b200_stack_run_sync(int plan, void* stream, const unsigned int* wait_flags, unsigned int wait_epoch,

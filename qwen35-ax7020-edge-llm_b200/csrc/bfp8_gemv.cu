@@ -1200,7 +1200,7 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const __grid_constant
         if (s_last) {
             __threadfence_system();
             const unsigned int e = epoch_of(A.sync.sig_epoch, A.sync.epoch_base);
-            for (int r = 0; r < A.sync.world; r++) st_release_sys(A.sync.sig_flags[r] + A.sync.rank, e);
+            for (int r = 0; r < A.sync.world; r++) st_relaxed_sys(A.sync.sig_flags[r] + A.sync.rank, e);
             *A.sync.sig_ticket = 0u;   // the next launch using this ticket is stream-ordered after this one
         }
     }
