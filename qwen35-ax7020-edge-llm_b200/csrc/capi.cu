@@ -28,6 +28,8 @@
 #include <unordered_map>
 #include <vector>
 
+#include <unistd.h>
+
 namespace {
 thread_local std::string g_err;
 }  // namespace
@@ -528,7 +530,7 @@ struct CopyChunk {
 // the caller's own thread copies the first part.
 class CopyPool {
   public:
-    explicit CopyPool(int n) : n_(1) {
+    explicit CopyPool(int n) : n_(1), pid_(getpid()) {
         int i = 1;
         try {
             for (; i < n; i++) std::thread([this, i] { run(i); }).detach();
@@ -539,7 +541,8 @@ class CopyPool {
     void copy(const std::vector<CopyChunk>& v) {
         size_t total = 0;
         for (const CopyChunk& c : v) total += c.n;
-        if (n_ == 1 || total < ((size_t)1 << 20)) {
+        // a forked child has none of the parent's threads: it copies alone
+        if (n_ == 1 || total < ((size_t)1 << 20) || getpid() != pid_) {
             part(v, 0, total);
             return;
         }
@@ -586,6 +589,7 @@ class CopyPool {
         }
     }
     int n_;
+    pid_t pid_;   // the process whose threads these are
     std::mutex mu_;
     std::condition_variable cv_, done_;
     const std::vector<CopyChunk>* job_ = nullptr;
